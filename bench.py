@@ -1,0 +1,334 @@
+"""Benchmark of the Kernel-DeltaNet hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1)
+
+Workload: single-layer long-context prefill, B=1
+sequence per GPU, H=16 heads, T=65536, d_k=64 lifted to D=512, d_v=64, chunk 64,
+bf16 inputs, fp32 accumulation and state, zero initial state; q,k ~ N(0,1)
+then L2-normalised, v ~ N(0,1), beta = sigmoid(N(0,1)), decay = 1.
+A "step" is one prefill of that sequence.  With N GPUs every rank runs its own
+sequence (whole sequences shard with no communication): weak scaling, value =
+N * 65536 tokens / max-over-ranks step time.
+
+The line also carries the decode workload (configs[3]: 64 streams x 16 heads,
+fp32 state, one token per step) as ``decode`` and, on rank 0 at N=1, the CPU
+baseline (the numpy port of the reference path, timed on a bounded sample).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "kernel-deltanet_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "KDN layer prefill tokens/s at T=64k,D=512 (1–8 B200); decode steps/s"
+B, H, T, DK, DV, D, C = 1, 16, 65536, 64, 64, 512, 64
+FLOP_PER_TOKEN_HEAD = 360448  # 5 D-wide + 4 C-wide GEMMs per chunk / C (algorithmic count)
+DEC_STREAMS, DEC_H = 64, 16
+DEC_BYTES_PER_HEAD = 2 * DV * D * 4 + 3 * DK * 4 + 4 + DV * 4  # 263,172 B: state r+w, q,k,v, beta, y
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return {"hbm_gbs": j["hbm_gbs"], "bf16_tflops": j["bf16_tflops"],
+                "bf16_tflops_sustained": j.get("bf16_tflops_sustained", j["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = f"/tmp/kdn_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, x in enumerate(r) if x.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+def dist_init(backend):
+    import datetime
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def prefill_inputs(dev, seed, n_heads=H, seq=T):
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.nn.functional.normalize(torch.randn(n_heads, seq, DK, generator=g, device=dev), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(n_heads, seq, DK, generator=g, device=dev), dim=-1)
+    v = torch.randn(n_heads, seq, DV, generator=g, device=dev)
+    beta = torch.sigmoid(torch.randn(n_heads, seq, generator=g, device=dev))
+    return q.bfloat16(), k.bfloat16(), v.bfloat16(), beta
+
+
+def cpu_baseline(seq_sample: int):
+    """The numpy port of the reference path on the host cores (bounded sample)."""
+    import numpy as np
+
+    import oracle
+
+    c = oracle.make_projection_constants()
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((H, seq_sample, DK)).astype(np.float32)
+    k = rng.standard_normal((H, seq_sample, DK)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((H, seq_sample, DV)).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((H, seq_sample))))).astype(np.float32)
+    t0 = time.perf_counter()
+    oracle.chunked_deltanet_forward(q, k, v, beta, None, c, C, None, np.float32)
+    el = time.perf_counter() - t0
+    return {"value": B * seq_sample / el, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"B=1 H={H} T={seq_sample} (fp32 numpy port of kernels/fused_kernel_deltanet.py, "
+                      f"{os.cpu_count()} host threads), {el:.2f} s"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_init("gloo")
+    if rank != 0:
+        return
+    seq = args.ref_seq
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(seq)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.median(vals)
+    r["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * B * seq / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config1 prefill sample B=1 H={H} T={seq} of T=65536, d_k=64->D=512, d_v=64, "
+                                   f"C=64 (CPU, host cores)", "global_batch": 1, "seq_len": seq,
+                       "parallelism": "host threads"},
+            "cpu_baseline": r,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def bench_decode(dev, steps, warmup, peaks):
+    import torch
+
+    import kdn_b200
+
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    states = 0.02 * torch.randn(DEC_STREAMS, DEC_H, DV, D, generator=g, device=dev)
+    qs = torch.nn.functional.normalize(torch.randn(steps + warmup, DEC_STREAMS, DEC_H, DK, generator=g, device=dev), dim=-1)
+    ks = torch.nn.functional.normalize(torch.randn(steps + warmup, DEC_STREAMS, DEC_H, DK, generator=g, device=dev), dim=-1)
+    vs = torch.randn(steps + warmup, DEC_STREAMS, DEC_H, DV, generator=g, device=dev)
+    bs = torch.sigmoid(torch.randn(steps + warmup, DEC_STREAMS, DEC_H, generator=g, device=dev))
+    slots = torch.arange(DEC_STREAMS, device=dev, dtype=torch.int64)
+    out = torch.empty(DEC_STREAMS, DEC_H, DV, device=dev)
+    for i in range(warmup):
+        kdn_b200.hybrid_recurrent_forward(qs[i], ks[i], vs[i], bs[i], None, states, slots, out, fwht_proj=proj)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(warmup, warmup + steps):
+        kdn_b200.hybrid_recurrent_forward(qs[i], ks[i], vs[i], bs[i], None, states, slots, out, fwht_proj=proj)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    gbs = DEC_STREAMS * DEC_H * DEC_BYTES_PER_HEAD / (ms * 1e-3) / 1e9
+    return {"metric": "decode steps/s (64 streams x 16 heads, fp32 state 128 MiB)", "value": 1e3 / ms,
+            "unit": "steps/s", "ms_per_step": ms, "steps": steps,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                         "note": f"state 128 MiB ~ L2 126 MB; peak {peaks['src']}"}}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import kdn_b200
+
+    rank, world, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peaks = load_peaks()
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    q, k, v, beta = prefill_inputs(dev, 1234 + rank)
+    y = torch.empty(H, T, DV, device=dev, dtype=torch.bfloat16)
+    S = torch.empty(H, DV, D, device=dev, dtype=torch.float32)
+    lib = kdn_b200.load()
+    pstruct, _ = proj.kdn_projection(dev)
+    ws_bytes = int(lib.kdn_chunked_prefill_workspace_size(H, T, DV, C, pstruct, 1))
+    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+
+    def step(qq=q, kk=k, vv=v, bb=beta):
+        kdn_b200.fused_chunked_deltanet_forward(qq, kk, vv, bb, None, proj, C, mode="bf16", workspace=ws, out=y,
+                                                final_state=S)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # end to end through the public API: pinned host inputs -> device -> prefill -> host outputs
+    hq, hk, hv, hb = (x.cpu().pin_memory() for x in (q, k, v, beta))
+    hy = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+    hS = torch.empty(S.shape, dtype=S.dtype).pin_memory()
+    dq, dk, dv_, db = (torch.empty_like(x) for x in (q, k, v, beta))
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hb))
+    d2h = hy.numel() * hy.element_size() + hS.numel() * hS.element_size()
+
+    def e2e_step():
+        for dst, src in ((dq, hq), (dk, hk), (dv_, hv), (db, hb)):
+            dst.copy_(src, non_blocking=True)
+        step(dq, dk, dv_, db)
+        hy.copy_(y, non_blocking=True)
+        hS.copy_(S, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(3, min(args.steps, 10))
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    dec = bench_decode(dev, steps=200, warmup=5, peaks=peaks)
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        return
+    tokens = world * B * T
+    flops = FLOP_PER_TOKEN_HEAD * B * H * T
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get("prefill_step_bytes")
+    launches_per_step = int(getattr(kdn_b200, "PREFILL_LAUNCHES", {}).get("bf16", 3))
+    line = {
+        "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config1 prefill: B=1 seq per GPU, H={H}, T={T}, d_k={DK}->D={D}, d_v={DV}, C={C}, "
+                               "bf16 in, fp32 accumulate/state", "global_batch": world * B, "seq_len": T,
+                   "heads": H, "parallelism": f"dp{world} (whole sequences per rank, no communication)",
+                   "l2": "inputs 402 MB per step > 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
+                     "note": f"algorithmic {FLOP_PER_TOKEN_HEAD} FLOP/token-head over the whole prefill step "
+                             f"({launches_per_step} launches); peak {peaks['src']} burst"},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+        "decode": dec,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.ref_seq)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-seq", type=int, default=4096, help="tokens per CPU-baseline sample (16 heads)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+    try:
+        import torch.distributed as dist
+
+        if dist.is_initialized():
+            dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,152 @@
+/*
+ * kdn.h -- C ABI of libkdn, the B200 (sm_100a) implementation of the
+ * Kernel-DeltaNet hot path:
+ *
+ *   structured-FWHT feature lift (d_k = 64 -> D = 512, spherical renorm)
+ *     -> exact gated delta-rule chunked prefill
+ *     -> single-token decode state update
+ *
+ * Conventions shared by every entry point:
+ *   - all tensor arguments are DEVICE pointers to contiguous row-major arrays;
+ *     shapes are given by the int64 size arguments;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *     all work is enqueued on it, nothing synchronises the host;
+ *   - the caller owns every buffer; no entry point allocates device memory;
+ *   - the return value is a status code (KDN_OK == 0); on failure
+ *     kdn_last_error() returns a message for the calling thread; nothing aborts.
+ */
+#ifndef KDN_H_
+#define KDN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KDN_ABI_VERSION 1
+
+/* status codes */
+#define KDN_OK 0
+#define KDN_ERR_INVALID 1     /* bad argument: null pointer, shape, alignment */
+#define KDN_ERR_UNSUPPORTED 2 /* valid but not implemented (e.g. d_k != 64) */
+#define KDN_ERR_CUDA 3        /* a CUDA runtime call or launch failed */
+#define KDN_ERR_WORKSPACE 4   /* workspace too small */
+#define KDN_ERR_DEVICE 5      /* a kernel's own bounds check recorded a bad index */
+
+/* element types */
+#define KDN_DTYPE_F32 0
+#define KDN_DTYPE_BF16 1
+
+/* index types (slot_mapping) */
+#define KDN_INDEX_I32 0
+#define KDN_INDEX_I64 1
+
+/* prefill arithmetic modes */
+#define KDN_MODE_F32 0  /* exact fp32 arithmetic (CUDA cores) */
+#define KDN_MODE_BF16 1 /* bf16 tensor-core products, fp32 accumulation, fp32 state */
+
+/* decode readout order */
+#define KDN_READOUT_PRE 0  /* y = S_{t-1} phi(q_t), then update (module semantics) */
+#define KDN_READOUT_POST 1 /* update, then y = S_t phi(q_t) (decode benchmark variant) */
+
+/*
+ * Constants of one structured projection (the reference's
+ * FastWalshHadamardProjection, kernels/fwht.py:48-111).  Block m of the dense
+ * map is H diag(d3[m]) H diag(d2[m]) H diag(d1[m]) / sqrt(d_k) with H the +-1
+ * Sylvester matrix of order d_k.
+ *
+ *   sign_bits[m][s] bit i == 1  <=>  stage s (0:d1, 1:d2, 2:d3) sign of block m,
+ *                                    element i, is -1
+ *   phase: device pointer to D floats (the reference's buffer `b`)
+ *   tau_inv = 1 / d_k^(1/4); amp = sqrt(2 / D)
+ */
+typedef struct kdn_projection {
+  int32_t d_k;
+  int32_t D;
+  float tau_inv;
+  float amp;
+  uint64_t sign_bits[8][3];
+  const float* phase;
+} kdn_projection;
+
+/* ABI version (KDN_ABI_VERSION) of the loaded library. */
+int kdn_abi_version(void);
+
+/* Message describing the last failure on the calling thread ("" if none). */
+const char* kdn_last_error(void);
+
+/*
+ * Feature lift phi(x) = u / (||u|| + 1e-8), u = amp * cos(Omega x * tau_inv + phase).
+ * x: [n, d_k] (x_dtype), out: [n, D] (out_dtype).
+ * Replaces FastWalshHadamardProjection.forward, kernels/fwht.py:113-130
+ * (and the pybind fwht_forward of kernels/fwht_cuda.cpp:8-30).
+ */
+int kdn_fwht_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t n,
+                  const kdn_projection* proj, void* stream);
+
+/*
+ * Bytes of device workspace kdn_chunked_prefill needs for these sizes
+ * (0 when the selected path keeps everything on chip).
+ */
+size_t kdn_chunked_prefill_workspace_size(int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                                          const kdn_projection* proj, int mode);
+
+/*
+ * Exact gated delta-rule prefill over N independent sequences (heads
+ * flattened into N):
+ *   S_t = decay_t S_{t-1} (I - beta_t phi(k_t) phi(k_t)^T) + beta_t v_t phi(k_t)^T
+ *   y_t = S_{t-1} phi(q_t)
+ * q, k: [N, T, d_k]; v, y: [N, T, dv] (in_dtype / y_dtype); beta, decay: [N, T]
+ * (gate_dtype; decay may be NULL meaning 1); initial_state: [N, dv, D] fp32 or
+ * NULL (zeros); final_state: [N, dv, D] fp32 (may alias initial_state).
+ * chunk: 32 or 64.  mode: KDN_MODE_F32 or KDN_MODE_BF16.
+ * Replaces fused_chunked_deltanet_forward, kernels/fused_kernel_deltanet.py:31-155.
+ */
+int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtype,
+                        const void* beta, const void* decay, int gate_dtype,
+                        const float* initial_state, void* y, int y_dtype, float* final_state,
+                        int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                        const kdn_projection* proj, int mode,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * One decode token per (token, head), states addressed through slot_mapping:
+ * q, k: [num_tokens, H, d_k]; v, out: [num_tokens, H, dv] (in_dtype / out_dtype);
+ * beta, decay: [num_tokens, H] (gate_dtype, decay may be NULL);
+ * states: [num_slots, H, dv, D] (state_dtype), updated in place;
+ * slot_mapping: [num_tokens] (index_dtype); a negative slot marks a padding
+ * token: its output row is zeroed and no state is touched.  A slot >= num_slots
+ * is skipped the same way and recorded for kdn_device_error().
+ * Two tokens mapped to the same slot in one call race: map each slot once.
+ * Replaces the hybrid_recurrent_forward op, serving/vllm_kernel_deltanet_op.cpp:11-34
+ * (semantics of kernels/kernel_deltanet_fused.py:288-300).
+ */
+int kdn_decode_step(const void* q, const void* k, const void* v, int in_dtype,
+                    const void* beta, const void* decay, int gate_dtype,
+                    void* states, int state_dtype, int64_t num_slots,
+                    const void* slot_mapping, int index_dtype,
+                    void* out, int out_dtype,
+                    int64_t num_tokens, int32_t H, int32_t dv,
+                    const kdn_projection* proj, int readout, void* stream);
+
+/*
+ * Copy slot `parent` of a slot-major state pool onto slot `child` on `stream`.
+ * Replaces fork_recurrent_state, serving/vllm_kernel_deltanet_op.cpp:39-58.
+ */
+int kdn_fork_state(void* states, int64_t num_slots, int64_t bytes_per_slot,
+                   int64_t parent, int64_t child, void* stream);
+
+/*
+ * Read and clear the device-side error word of the current device (written by
+ * kernels whose bounds checks skipped a bad index).  Synchronises `stream`.
+ * *code_out = 0 when nothing was recorded.
+ */
+int kdn_device_error(void* stream, int* code_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KDN_H_ */

@@ -1,0 +1,204 @@
+// capi.cu -- the extern "C" surface of libkdn (declared in include/kdn.h).
+//
+// Every entry point validates its arguments, enqueues work on the caller's
+// stream and returns a status code; failures leave a message in a thread-local
+// buffer read by kdn_last_error().  Nothing here allocates device memory.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "kdn_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return KDN_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(KDN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+bool valid_dtype(int d) { return d == KDN_DTYPE_F32 || d == KDN_DTYPE_BF16; }
+
+int check_projection(const kdn_projection* proj) {
+  if (!proj) return fail(KDN_ERR_INVALID, "projection is NULL");
+  if (proj->d_k != 64) return fail(KDN_ERR_UNSUPPORTED, "d_k=%d: only d_k=64 is implemented", proj->d_k);
+  if (proj->D < 64 || proj->D > 512 || proj->D % 64 != 0)
+    return fail(KDN_ERR_UNSUPPORTED, "D=%d: D must be a multiple of 64 in [64, 512]", proj->D);
+  if (!proj->phase) return fail(KDN_ERR_INVALID, "projection phase pointer is NULL");
+  if (!aligned(proj->phase, 8)) return fail(KDN_ERR_INVALID, "projection phase pointer must be 8-byte aligned");
+  return KDN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kdn_abi_version(void) { return KDN_ABI_VERSION; }
+
+const char* kdn_last_error(void) { return g_last_error.c_str(); }
+
+int kdn_fwht_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t n, const kdn_projection* proj,
+                  void* stream) {
+  if (int rc = check_projection(proj)) return rc;
+  if (n < 0) return fail(KDN_ERR_INVALID, "n=%lld < 0", (long long)n);
+  if (n > 0 && (!x || !out)) return fail(KDN_ERR_INVALID, "x/out is NULL");
+  if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
+  if (!aligned(x, 8) || !aligned(out, 8)) return fail(KDN_ERR_INVALID, "x/out must be 8-byte aligned");
+  const kdn::ProjParams P = kdn::make_proj_params(*proj);
+  cudaError_t e = kdn::launch_lift(x, x_dtype, out, out_dtype, n, P, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lift launch");
+  return ok();
+}
+
+size_t kdn_chunked_prefill_workspace_size(int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                                          const kdn_projection* proj, int mode) {
+  (void)mode;
+  if (!proj || N <= 0 || T <= 0 || (chunk != 32 && chunk != 64)) return 0;
+  return kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
+}
+
+int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtype, const void* beta,
+                        const void* decay, int gate_dtype, const float* initial_state, void* y, int y_dtype,
+                        float* final_state, int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                        const kdn_projection* proj, int mode, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (int rc = check_projection(proj)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N < 1 || N > 65535) return fail(KDN_ERR_INVALID, "N=%lld outside [1, 65535]", (long long)N);
+  if (T < 0) return fail(KDN_ERR_INVALID, "T=%lld < 0", (long long)T);
+  if (dv < 16 || dv > 512 || dv % 16 != 0)
+    return fail(KDN_ERR_UNSUPPORTED, "dv=%d: dv must be a multiple of 16 in [16, 512]", dv);
+  if (chunk != 32 && chunk != 64) return fail(KDN_ERR_UNSUPPORTED, "chunk=%d: chunk must be 32 or 64", chunk);
+  if (mode != KDN_MODE_F32 && mode != KDN_MODE_BF16) return fail(KDN_ERR_INVALID, "bad mode %d", mode);
+  if (!valid_dtype(in_dtype) || !valid_dtype(gate_dtype) || !valid_dtype(y_dtype))
+    return fail(KDN_ERR_INVALID, "bad dtype");
+  if (!final_state) return fail(KDN_ERR_INVALID, "final_state is NULL");
+  const size_t state_bytes = sizeof(float) * size_t(N) * dv * proj->D;
+  if (T == 0) {  // nothing to scan: S_out = S_in
+    cudaError_t e = initial_state ? (initial_state == final_state
+                                         ? cudaSuccess
+                                         : cudaMemcpyAsync(final_state, initial_state, state_bytes,
+                                                           cudaMemcpyDeviceToDevice, st))
+                                  : cudaMemsetAsync(final_state, 0, state_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "empty prefill state copy");
+    return ok();
+  }
+  if (!q || !k || !v || !beta || !y) return fail(KDN_ERR_INVALID, "q/k/v/beta/y is NULL");
+  if (!aligned(q, 8) || !aligned(k, 8)) return fail(KDN_ERR_INVALID, "q/k must be 8-byte aligned");
+  const size_t need = kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
+  if (!workspace || workspace_bytes < need)
+    return fail(KDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(KDN_ERR_INVALID, "workspace must be 256-byte aligned");
+
+  kdn::PrefillProblem p;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.in_dtype = in_dtype;
+  p.beta = beta;
+  p.decay = decay;
+  p.gate_dtype = gate_dtype;
+  p.S0 = initial_state;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  p.S_out = final_state;
+  p.N = N;
+  p.T = T;
+  p.dv = dv;
+  p.C = chunk;
+  p.D = proj->D;
+  const kdn::ProjParams P = kdn::make_proj_params(*proj);
+  cudaError_t e = kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return ok();
+}
+
+int kdn_decode_step(const void* q, const void* k, const void* v, int in_dtype, const void* beta, const void* decay,
+                    int gate_dtype, void* states, int state_dtype, int64_t num_slots, const void* slot_mapping,
+                    int index_dtype, void* out, int out_dtype, int64_t num_tokens, int32_t H, int32_t dv,
+                    const kdn_projection* proj, int readout, void* stream) {
+  if (int rc = check_projection(proj)) return rc;
+  if (num_tokens < 0 || num_tokens > 65535)
+    return fail(KDN_ERR_INVALID, "num_tokens=%lld outside [0, 65535]", (long long)num_tokens);
+  if (num_tokens == 0) return ok();
+  if (H < 1 || H > 65535) return fail(KDN_ERR_INVALID, "H=%d outside [1, 65535]", H);
+  if (dv < 16 || dv % 16 != 0) return fail(KDN_ERR_UNSUPPORTED, "dv=%d: dv must be a positive multiple of 16", dv);
+  if (num_slots < 1) return fail(KDN_ERR_INVALID, "num_slots=%lld < 1", (long long)num_slots);
+  if (!q || !k || !v || !beta || !states || !slot_mapping || !out)
+    return fail(KDN_ERR_INVALID, "a required pointer is NULL");
+  if (!valid_dtype(in_dtype) || !valid_dtype(gate_dtype) || !valid_dtype(state_dtype) || !valid_dtype(out_dtype))
+    return fail(KDN_ERR_INVALID, "bad dtype");
+  if (index_dtype != KDN_INDEX_I32 && index_dtype != KDN_INDEX_I64) return fail(KDN_ERR_INVALID, "bad index dtype");
+  if (readout != KDN_READOUT_PRE && readout != KDN_READOUT_POST) return fail(KDN_ERR_INVALID, "bad readout");
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(states, 8)) return fail(KDN_ERR_INVALID, "misaligned q/k/states");
+  kdn::DecodeProblem p;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.in_dtype = in_dtype;
+  p.beta = beta;
+  p.decay = decay;
+  p.gate_dtype = gate_dtype;
+  p.states = states;
+  p.state_dtype = state_dtype;
+  p.num_slots = num_slots;
+  p.slot_mapping = slot_mapping;
+  p.index_dtype = index_dtype;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.num_tokens = num_tokens;
+  p.H = H;
+  p.dv = dv;
+  p.D = proj->D;
+  p.readout = readout;
+  const kdn::ProjParams P = kdn::make_proj_params(*proj);
+  cudaError_t e = kdn::launch_decode(p, P, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return ok();
+}
+
+int kdn_fork_state(void* states, int64_t num_slots, int64_t bytes_per_slot, int64_t parent, int64_t child,
+                   void* stream) {
+  if (!states) return fail(KDN_ERR_INVALID, "states is NULL");
+  if (bytes_per_slot <= 0) return fail(KDN_ERR_INVALID, "bytes_per_slot=%lld", (long long)bytes_per_slot);
+  if (parent < 0 || parent >= num_slots || child < 0 || child >= num_slots)
+    return fail(KDN_ERR_INVALID, "slot out of range: parent=%lld child=%lld num_slots=%lld", (long long)parent,
+                (long long)child, (long long)num_slots);
+  if (parent == child) return ok();
+  char* base = static_cast<char*>(states);
+  cudaError_t e = cudaMemcpyAsync(base + child * bytes_per_slot, base + parent * bytes_per_slot,
+                                  size_t(bytes_per_slot), cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fork copy");
+  return ok();
+}
+
+int kdn_device_error(void* stream, int* code_out) {
+  if (!code_out) return fail(KDN_ERR_INVALID, "code_out is NULL");
+  int code = 0;
+  cudaError_t e = kdn::decode_read_error(static_cast<cudaStream_t>(stream), &code);
+  if (e != cudaSuccess) return cuda_fail(e, "device error read");
+  *code_out = code;
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+// kdn_internal.h -- host-side declarations shared by libkdn's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "kdn.h"
+#include "kdn_common.cuh"
+
+namespace kdn {
+
+// ------------------------------------------------------------------ lift.cu
+cudaError_t launch_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t n, const ProjParams& P,
+                        cudaStream_t stream);
+
+// ------------------------------------------------------------ prefill paths
+struct PrefillProblem {
+  const void* q;
+  const void* k;
+  const void* v;
+  int in_dtype;
+  const void* beta;
+  const void* decay;  // may be null (== 1)
+  int gate_dtype;
+  const float* S0;  // may be null (zeros)
+  void* y;
+  int y_dtype;
+  float* S_out;
+  int64_t N, T;
+  int dv, C, D;
+};
+
+// prefill_simt.cu: exact fp32 arithmetic on CUDA cores, three launches over a workspace.
+size_t simt_prefill_workspace(int64_t N, int64_t T, int dv, int C, int D);
+cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
+                                cudaStream_t stream);
+
+// ---------------------------------------------------------------- decode.cu
+struct DecodeProblem {
+  const void* q;
+  const void* k;
+  const void* v;
+  int in_dtype;
+  const void* beta;
+  const void* decay;
+  int gate_dtype;
+  void* states;
+  int state_dtype;
+  int64_t num_slots;
+  const void* slot_mapping;
+  int index_dtype;
+  void* out;
+  int out_dtype;
+  int64_t num_tokens;
+  int H, dv, D;
+  int readout;
+};
+cudaError_t launch_decode(const DecodeProblem& p, const ProjParams& P, cudaStream_t stream);
+// reads and clears the decode kernels' device error word (synchronises stream)
+cudaError_t decode_read_error(cudaStream_t stream, int* code);
+
+}  // namespace kdn

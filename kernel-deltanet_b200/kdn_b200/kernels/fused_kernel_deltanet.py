@@ -1,0 +1,137 @@
+"""Exact gated delta-rule chunked prefill -- drop-in for kernels/fused_kernel_deltanet.py.
+
+``fused_chunked_deltanet_forward(q, k, v, beta, decay, fwht_proj, chunk_size,
+initial_state) -> (Y, S)`` keeps the reference signature and meaning
+(kernels/fused_kernel_deltanet.py:31-40):
+
+    S_t = decay_t S_{t-1} (I - beta_t phi(k_t) phi(k_t)^T) + beta_t v_t phi(k_t)^T
+    y_t = S_{t-1} phi(q_t)
+
+with q, k [B, T, d_k], v [B, T, d_v], beta/decay [B, T], state [B, d_v, D]
+(heads flattened into B by the caller, as in pipeline/transmute.py:75-79).
+Y is returned in q's dtype; the state is always returned in float32 (the
+reference keeps it in the input dtype -- fp32 state is this build's contract).
+
+Arithmetic modes: ``"fp32"`` (exact fp32, CUDA cores) and ``"bf16"`` (bf16
+tensor-core products with fp32 accumulation and fp32 state); default: "bf16"
+for bfloat16 inputs, "fp32" otherwise.  The work runs in libkdn on the
+tensors' CUDA device and current stream; there is no CPU path.  Backward is
+not implemented (the reference recomputes through autograd, :158-179).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from .. import _lib
+from .fwht import FastWalshHadamardProjection
+
+_MODES = {"fp32": _lib.KDN_MODE_F32, "bf16": _lib.KDN_MODE_BF16}
+
+
+def _check_cuda(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("kdn_b200 runs on CUDA tensors only (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def fused_chunked_deltanet_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    beta: torch.Tensor,
+    decay: Optional[torch.Tensor],
+    fwht_proj: FastWalshHadamardProjection,
+    chunk_size: int = 64,
+    initial_state: Optional[torch.Tensor] = None,
+    *,
+    mode: Optional[str] = None,
+    workspace: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    final_state: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    dev = _check_cuda(q, k, v, beta, decay, initial_state)
+    if q.dim() != 3 or k.shape != q.shape or v.dim() != 3 or v.shape[:2] != q.shape[:2]:
+        raise RuntimeError(f"expected q,k [B,T,d_k] and v [B,T,d_v]; got {tuple(q.shape)}, {tuple(k.shape)}, "
+                           f"{tuple(v.shape)}")
+    B, T, d_k = q.shape
+    dv = v.shape[-1]
+    D = fwht_proj.D
+    if d_k != fwht_proj.d_k:
+        raise RuntimeError(f"d_k {d_k} != projection d_k {fwht_proj.d_k}")
+    if beta.shape != (B, T) or (decay is not None and decay.shape != (B, T)):
+        raise RuntimeError("beta/decay must be [B, T]")
+    if mode is None:
+        mode = "bf16" if q.dtype == torch.bfloat16 else "fp32"
+    if mode not in _MODES:
+        raise RuntimeError(f"mode must be one of {sorted(_MODES)}")
+    in_dtype = q.dtype if q.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    q = q.to(in_dtype).contiguous()
+    k = k.to(in_dtype).contiguous()
+    v = v.to(in_dtype).contiguous()
+    gate_dtype = beta.dtype if beta.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    beta = beta.to(gate_dtype).contiguous()
+    if decay is not None:
+        decay = decay.to(gate_dtype).contiguous()
+    S0 = None
+    if initial_state is not None:
+        if initial_state.shape != (B, dv, D):
+            raise RuntimeError(f"initial_state must be [B, d_v, D] = {(B, dv, D)}")
+        S0 = initial_state.to(torch.float32).contiguous()
+
+    y = out if out is not None else torch.empty(B, T, dv, device=dev, dtype=in_dtype)
+    S = final_state if final_state is not None else torch.empty(B, dv, D, device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    proj, _phase = fwht_proj.kdn_projection(dev)
+    mcode = _MODES[mode]
+    ws_bytes = int(lib.kdn_chunked_prefill_workspace_size(B, T, dv, chunk_size, proj, mcode))
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    rc = lib.kdn_chunked_prefill(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q),
+        beta.data_ptr(), _lib.ptr(decay), _lib.dtype_code(beta),
+        _lib.ptr(S0), y.data_ptr(), _lib.dtype_code(y), S.data_ptr(),
+        B, T, dv, chunk_size, proj, mcode, workspace.data_ptr(), ws_bytes, _lib.stream_handle(dev))
+    _lib.check(rc, "kdn_chunked_prefill")
+    return y, S
+
+
+class FusedKernelDeltaNetFunction(torch.autograd.Function):
+    """Forward-only autograd wrapper (kernels/fused_kernel_deltanet.py:158-179 recomputes for backward)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, beta, decay, fwht_proj, chunk_size=64):
+        Y, _ = fused_chunked_deltanet_forward(q, k, v, beta, decay, fwht_proj, chunk_size)
+        return Y
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        raise NotImplementedError("kdn_b200: the backward pass of the chunked scan is not implemented")
+
+
+class FusedKernelDeltaNet(nn.Module):
+    """Module form (kernels/fused_kernel_deltanet.py:182-208)."""
+
+    def __init__(self, d_model: int = 64, d_kernel: int = 512, chunk_size: int = 64, mode: Optional[str] = None):
+        super().__init__()
+        self.d_model = d_model
+        self.d_kernel = d_kernel
+        self.chunk_size = chunk_size
+        self.mode = mode
+        self.fwht_proj = FastWalshHadamardProjection(d_k=d_model, D=d_kernel)
+
+    def forward(self, q, k, v, beta, decay, initial_state=None):
+        return fused_chunked_deltanet_forward(q=q, k=k, v=v, beta=beta, decay=decay, fwht_proj=self.fwht_proj,
+                                              chunk_size=self.chunk_size, initial_state=initial_state,
+                                              mode=self.mode)

@@ -1,0 +1,130 @@
+"""Pin the numpy oracle to golden vectors produced by the reference itself.
+
+The fixtures were written by tests/golden/make_golden.py, which runs the
+reference's fwht.py / fused_kernel_deltanet.py / blelloch_scan.py and its
+float64 test recurrence on CPU.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import fro_rel, rel_err
+
+
+def _load(golden_dir, name):
+    return np.load(os.path.join(golden_dir, name + ".npz"))
+
+
+@pytest.mark.parametrize("seed", [42, 7])
+def test_projection_constants_match_reference(golden_dir, seed):
+    g = _load(golden_dir, f"lift_seed{seed}")
+    c = oracle.make_projection_constants(64, 512, seed)
+    np.testing.assert_array_equal(c.d1, g["d1"])
+    np.testing.assert_array_equal(c.d2, g["d2"])
+    np.testing.assert_array_equal(c.d3, g["d3"])
+    np.testing.assert_array_equal(c.b, g["b"])
+    # dense Omega is exact integers / 8 in both
+    np.testing.assert_array_equal(oracle.build_omega(c, np.float32), g["omega"])
+
+
+@pytest.mark.parametrize("seed", [42, 7])
+def test_lift_matches_reference(golden_dir, seed):
+    g = _load(golden_dir, f"lift_seed{seed}")
+    c = oracle.make_projection_constants(64, 512, seed)
+    phi = oracle.lift(g["x"], c)
+    assert rel_err(phi, g["phi"]) < 2e-6
+    np.testing.assert_allclose(np.linalg.norm(phi, axis=-1), 1.0, atol=1e-7)
+
+
+def test_omega_blocks_are_scaled_orthogonal():
+    c = oracle.make_projection_constants()
+    om = oracle.build_omega(c)
+    for m in range(c.M):
+        blk = om[m * 64:(m + 1) * 64]
+        # H D3 H D2 H D1 / 8 with the unnormalised +-1 H: rows have norm 64
+        np.testing.assert_allclose(blk @ blk.T, 4096.0 * np.eye(64), atol=1e-9)
+
+
+NAMES = ["prefill_t130_gated_s0", "prefill_t63", "prefill_t64", "prefill_t1",
+         "prefill_c32_dv128_gated", "prefill_t256_c64"]
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_chunked_oracle_matches_reference(golden_dir, name):
+    g = _load(golden_dir, name)
+    seed, N, T, d_k, dv, C, gated, init = [int(x) for x in g["meta"]]
+    c = oracle.make_projection_constants()
+    Y, S = oracle.chunked_deltanet_forward(
+        g["q"], g["k"], g["v"], g["beta"], g["decay"], c, C, g["S0"] if init else None)
+    assert Y.shape == g["Y"].shape and S.shape == g["S"].shape
+    # oracle runs in float64, the reference in float32
+    assert rel_err(Y, g["Y"]) < 2e-5
+    assert fro_rel(S, g["S"]) < 2e-6
+
+
+@pytest.mark.parametrize("name", ["prefill_t130_gated_s0", "prefill_c32_dv128_gated"])
+def test_chunked_equals_token_recurrence(golden_dir, name):
+    g = _load(golden_dir, name)
+    seed, N, T, d_k, dv, C, gated, init = [int(x) for x in g["meta"]]
+    c = oracle.make_projection_constants()
+    S0 = g["S0"] if init else None
+    Yc, Sc = oracle.chunked_deltanet_forward(g["q"], g["k"], g["v"], g["beta"], g["decay"], c, C, S0)
+    Yr, Sr = oracle.token_recurrence(g["q"], g["k"], g["v"], g["beta"], g["decay"], c, S0)
+    assert rel_err(Yc, Yr) < 1e-10
+    assert fro_rel(Sc, Sr) < 1e-11
+
+
+def test_recurrence_matches_reference_float64(golden_dir):
+    g = _load(golden_dir, "recurrence_t40")
+    c = oracle.make_projection_constants()
+    Y, S = oracle.token_recurrence(g["q"], g["k"], g["v"], g["beta"], g["decay"], c)
+    # the reference lifts in fp32 then recurs in float64
+    assert rel_err(Y, g["Y"]) < 2e-5
+    assert fro_rel(S, g["S"]) < 2e-6
+
+
+def test_decode_post_matches_reference(golden_dir):
+    g = _load(golden_dir, "decode_post_step")
+    c = oracle.make_projection_constants()
+    y, S = oracle.decode_step_post(g["S_prev"], g["q"], g["k"], g["v"], g["beta"], g["decay"], c)
+    assert rel_err(y, g["y"]) < 2e-5
+    assert fro_rel(S, g["S"]) < 2e-6
+
+
+def test_decode_pre_is_first_recurrence_step(golden_dir):
+    g = _load(golden_dir, "recurrence_t40")
+    c = oracle.make_projection_constants()
+    Yr, _ = oracle.token_recurrence(g["q"][:, :3], g["k"][:, :3], g["v"][:, :3], g["beta"][:, :3],
+                                    g["decay"][:, :3], c)
+    S = np.zeros((2, 64, 512))
+    for t in range(3):
+        y, S = oracle.decode_step(S, g["q"][:, t], g["k"][:, t], g["v"][:, t], g["beta"][:, t],
+                                  g["decay"][:, t], c)
+        np.testing.assert_allclose(y, Yr[:, t], atol=1e-12)
+
+
+def test_compose_matches_reference(golden_dir):
+    g = _load(golden_dir, "compose")
+    A, B = oracle.compose((g["A1"], g["B1"]), (g["A2"], g["B2"]))
+    np.testing.assert_allclose(A, g["A"], atol=1e-12)
+    np.testing.assert_allclose(B, g["B"], atol=1e-12)
+
+
+def test_block_transition_composes_to_full_scan():
+    rng = np.random.default_rng(0)
+    c = oracle.make_projection_constants()
+    N, T, dv = 1, 96, 16
+    q = rng.standard_normal((N, T, 64)); q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k = rng.standard_normal((N, T, 64)); k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((N, T, dv))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((N, T))))
+    decay = 1 / (1 + np.exp(-(rng.standard_normal((N, T)) + 3)))
+    _, S_full = oracle.chunked_deltanet_forward(q, k, v, beta, decay, c, 32)
+    t1 = oracle.chunk_block_transition(q[:, :64], k[:, :64], v[:, :64], beta[:, :64], decay[:, :64], c, 32)
+    t2 = oracle.chunk_block_transition(q[:, 64:], k[:, 64:], v[:, 64:], beta[:, 64:], decay[:, 64:], c, 32)
+    A, B = oracle.compose(t1, t2)
+    S = oracle.apply_transition(np.zeros((N, dv, 512)), (A, B))
+    assert fro_rel(S, S_full) < 1e-10
