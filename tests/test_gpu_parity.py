@@ -259,11 +259,12 @@ def test_decode_bf16_state_and_inputs(kdn, consts):
     S, q, k, v, beta, decay = _decode_inputs(70, 6, 2, 6)
     slots = np.arange(6)
     Sb = to_dev(S, torch.bfloat16)
+    S_in = Sb.float().cpu().numpy()  # the kernel updates Sb in place
     out = torch.empty(6, 2, 64, device=DEV, dtype=torch.bfloat16)
     kdn.hybrid_recurrent_forward(to_dev(q, torch.bfloat16), to_dev(k, torch.bfloat16), to_dev(v, torch.bfloat16),
                                  to_dev(beta, torch.bfloat16), to_dev(decay, torch.bfloat16), Sb,
                                  to_dev(slots, torch.int64), out)
-    y_ref, S_ref = oracle.decode_step(Sb.float().cpu().numpy(), bf16_round(q), bf16_round(k), bf16_round(v),
+    y_ref, S_ref = oracle.decode_step(S_in, bf16_round(q), bf16_round(k), bf16_round(v),
                                       bf16_round(beta), bf16_round(decay), consts)
     assert rel_err(out.float().cpu().numpy(), y_ref) < BF16_Y_TOL
     assert fro_rel(Sb.float().cpu().numpy(), S_ref) < BF16_S_TOL
