@@ -284,7 +284,7 @@ def run_ours(args):
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         traffic = json.load(open(tp)).get("prefill_step_bytes")
-    launches_per_step = int(getattr(kdn_b200, "PREFILL_LAUNCHES", {}).get("bf16", 3))
+    launches_per_step = 1  # the fused tensor-core prefill is one launch per step
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,

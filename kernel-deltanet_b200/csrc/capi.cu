@@ -49,6 +49,23 @@ int check_projection(const kdn_projection* proj) {
   return KDN_OK;
 }
 
+// The bf16 tensor-core path applies when the shape matches and the dense Omega
+// is exact in bf16; the exactness check walks the butterfly on the host, so its
+// result is cached per sign pattern.
+bool use_tc_path(const kdn_projection* proj, int32_t dv, int32_t chunk, int mode) {
+  if (mode != KDN_MODE_BF16) return false;
+  static thread_local uint64_t cached_bits[8][3];
+  static thread_local int cached_D = -1;
+  static thread_local bool cached_ok = false;
+  const kdn::ProjParams P = kdn::make_proj_params(*proj);
+  if (cached_D != proj->D || memcmp(cached_bits, proj->sign_bits, sizeof(cached_bits)) != 0) {
+    cached_ok = kdn::tc_prefill_supported(proj->D, 64, 64, P);
+    cached_D = proj->D;
+    memcpy(cached_bits, proj->sign_bits, sizeof(cached_bits));
+  }
+  return cached_ok && proj->D == 512 && dv == 64 && chunk == 64;
+}
+
 }  // namespace
 
 extern "C" {
@@ -72,8 +89,8 @@ int kdn_fwht_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t 
 
 size_t kdn_chunked_prefill_workspace_size(int64_t N, int64_t T, int32_t dv, int32_t chunk,
                                           const kdn_projection* proj, int mode) {
-  (void)mode;
   if (!proj || N <= 0 || T <= 0 || (chunk != 32 && chunk != 64)) return 0;
+  if (proj->D >= 64 && proj->D <= 512 && proj->d_k == 64 && use_tc_path(proj, dv, chunk, mode)) return 0;
   return kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
 }
 
@@ -105,10 +122,13 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   }
   if (!q || !k || !v || !beta || !y) return fail(KDN_ERR_INVALID, "q/k/v/beta/y is NULL");
   if (!aligned(q, 8) || !aligned(k, 8)) return fail(KDN_ERR_INVALID, "q/k must be 8-byte aligned");
-  const size_t need = kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
-  if (!workspace || workspace_bytes < need)
+  const bool tc = use_tc_path(proj, dv, chunk, mode);
+  if (tc && (!aligned(q, 16) || !aligned(k, 16)))
+    return fail(KDN_ERR_INVALID, "q/k must be 16-byte aligned for the tensor-core path");
+  const size_t need = tc ? 0 : kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
+  if (need > 0 && (!workspace || workspace_bytes < need))
     return fail(KDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
-  if (!aligned(workspace, 256)) return fail(KDN_ERR_INVALID, "workspace must be 256-byte aligned");
+  if (need > 0 && !aligned(workspace, 256)) return fail(KDN_ERR_INVALID, "workspace must be 256-byte aligned");
 
   kdn::PrefillProblem p;
   p.q = q;
@@ -128,7 +148,7 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   p.C = chunk;
   p.D = proj->D;
   const kdn::ProjParams P = kdn::make_proj_params(*proj);
-  cudaError_t e = kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st);
+  cudaError_t e = tc ? kdn::launch_tc_prefill(p, P, st) : kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return ok();
 }
@@ -194,10 +214,12 @@ int kdn_fork_state(void* states, int64_t num_slots, int64_t bytes_per_slot, int6
 
 int kdn_device_error(void* stream, int* code_out) {
   if (!code_out) return fail(KDN_ERR_INVALID, "code_out is NULL");
-  int code = 0;
+  int code = 0, code_tc = 0;
   cudaError_t e = kdn::decode_read_error(static_cast<cudaStream_t>(stream), &code);
   if (e != cudaSuccess) return cuda_fail(e, "device error read");
-  *code_out = code;
+  e = kdn::tc_read_error(static_cast<cudaStream_t>(stream), &code_tc);
+  if (e != cudaSuccess) return cuda_fail(e, "device error read");
+  *code_out = code ? code : code_tc;
   return ok();
 }
 

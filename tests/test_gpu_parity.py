@@ -295,3 +295,85 @@ def test_fork_state(kdn):
     assert torch.equal(St[3], St[1])
     with pytest.raises(RuntimeError, match="out of range"):
         kdn.fork_recurrent_state(St, 0, 4)
+
+
+# ------------------------------------------------- tensor-core (bf16) path
+TC_CASES = [
+    # (seed, N, T, gated, init)
+    (100, 1, 1, False, False),
+    (101, 2, 63, True, True),
+    (102, 3, 64, False, True),
+    (103, 2, 65, True, False),
+    (104, 5, 130, False, False),
+    (105, 2, 1000, True, True),
+]
+
+
+def test_tc_path_selected(kdn, proj):
+    lib = kdn.load()
+    s, _ = proj.kdn_projection(DEV)
+    assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == 0  # fused, no workspace
+    assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 0) > 0   # CUDA-core path
+
+
+@pytest.mark.parametrize("case", TC_CASES)
+def test_tc_prefill_vs_oracle(kdn, proj, consts, case):
+    seed, N, T, gated, init = case
+    q, k, v, beta, decay, S0 = make_inputs(seed, N, T, 64, gated, init)
+    qb, kb, vb = (to_dev(a, torch.bfloat16) for a in (q, k, v))
+    Y, S = kdn.fused_chunked_deltanet_forward(qb, kb, vb, to_dev(beta), to_dev(decay), proj, 64, to_dev(S0),
+                                              mode="bf16")
+    Yr, Sr = oracle.chunked_deltanet_forward(bf16_round(q), bf16_round(k), bf16_round(v), beta, decay, consts, 64,
+                                             S0)
+    assert rel_err(Y.float().cpu().numpy(), Yr) < BF16_Y_TOL
+    assert fro_rel(S.cpu().numpy(), Sr) < BF16_S_TOL
+
+
+def test_tc_prefill_fp32_inputs_bf16_mode(kdn, proj, consts):
+    q, k, v, beta, decay, S0 = make_inputs(110, 2, 200, 64, True, True)
+    Y, S = kdn.fused_chunked_deltanet_forward(to_dev(q), to_dev(k), to_dev(v), to_dev(beta), to_dev(decay), proj, 64,
+                                              to_dev(S0), mode="bf16")
+    assert Y.dtype == torch.float32
+    Yr, Sr = oracle.chunked_deltanet_forward(bf16_round(q), bf16_round(k), v, beta, decay, consts, 64, S0)
+    assert rel_err(Y.cpu().numpy(), Yr) < BF16_Y_TOL
+    assert fro_rel(S.cpu().numpy(), Sr) < BF16_S_TOL
+
+
+def test_tc_prefill_long_sequence_vs_oracle(kdn, proj, consts):
+    q, k, v, beta, _, _ = make_inputs(111, 2, 8192, 64, False, False)
+    qb, kb, vb = (to_dev(a, torch.bfloat16) for a in (q, k, v))
+    Y, S = kdn.fused_chunked_deltanet_forward(qb, kb, vb, to_dev(beta), None, proj, 64, mode="bf16")
+    Yr, Sr = oracle.chunked_deltanet_forward(bf16_round(q), bf16_round(k), bf16_round(v), beta, None, consts, 64,
+                                             dtype=np.float32)
+    assert rel_err(Y.float().cpu().numpy(), Yr) < BF16_Y_TOL
+    assert fro_rel(S.cpu().numpy(), Sr) < BF16_S_TOL
+
+
+def test_tc_resume_is_bit_exact(kdn, proj):
+    q, k, v, beta, decay, _ = make_inputs(112, 3, 512, 64, True, False)
+    dq, dk, dvv = (to_dev(a, torch.bfloat16) for a in (q, k, v))
+    db, dd = to_dev(beta), to_dev(decay)
+    Y, S = kdn.fused_chunked_deltanet_forward(dq, dk, dvv, db, dd, proj, 64, mode="bf16")
+    Y1, S1 = kdn.fused_chunked_deltanet_forward(dq[:, :192], dk[:, :192], dvv[:, :192], db[:, :192], dd[:, :192],
+                                                proj, 64, mode="bf16")
+    Y2, S2 = kdn.fused_chunked_deltanet_forward(dq[:, 192:], dk[:, 192:], dvv[:, 192:], db[:, 192:], dd[:, 192:],
+                                                proj, 64, S1, mode="bf16")
+    assert torch.equal(torch.cat([Y1, Y2], 1), Y)
+    assert torch.equal(S2, S)
+
+
+def test_tc_full_config1_vs_fp32_path(kdn, proj):
+    """Config 1 at full size (16 heads x 65536 tokens): the tensor-core path
+    against the exact fp32 CUDA-core path (itself pinned to the oracle above)."""
+    H, T = 16, 65536
+    g = torch.Generator(device=DEV).manual_seed(7)
+    q = torch.nn.functional.normalize(torch.randn(H, T, 64, generator=g, device=DEV), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(H, T, 64, generator=g, device=DEV), dim=-1).bfloat16()
+    v = torch.randn(H, T, 64, generator=g, device=DEV).bfloat16()
+    beta = torch.sigmoid(torch.randn(H, T, generator=g, device=DEV))
+    Yt, St = kdn.fused_chunked_deltanet_forward(q, k, v, beta, None, proj, 64, mode="bf16")
+    Yf, Sf = kdn.fused_chunked_deltanet_forward(q, k, v, beta, None, proj, 64, mode="fp32")
+    ey = ((Yt.float() - Yf.float()).norm(dim=-1) / Yf.float().norm(dim=-1).clamp_min(1e-30)).max().item()
+    es = ((St - Sf).norm() / Sf.norm()).item()
+    assert ey < BF16_Y_TOL, ey
+    assert es < BF16_S_TOL, es
