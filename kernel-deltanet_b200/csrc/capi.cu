@@ -123,8 +123,8 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   if (!q || !k || !v || !beta || !y) return fail(KDN_ERR_INVALID, "q/k/v/beta/y is NULL");
   if (!aligned(q, 8) || !aligned(k, 8)) return fail(KDN_ERR_INVALID, "q/k must be 8-byte aligned");
   const bool tc = use_tc_path(proj, dv, chunk, mode);
-  if (tc && (!aligned(q, 16) || !aligned(k, 16)))
-    return fail(KDN_ERR_INVALID, "q/k must be 16-byte aligned for the tensor-core path");
+  if (tc && (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(y, 16)))
+    return fail(KDN_ERR_INVALID, "q/k/v/y must be 16-byte aligned for the tensor-core path");
   const size_t need = tc ? 0 : kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
   if (need > 0 && (!workspace || workspace_bytes < need))
     return fail(KDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);

@@ -1,33 +1,30 @@
 // prefill_tc.cu -- fused tensor-core chunked prefill (KDN_MODE_BF16), sm_100a.
 //
-// One 4-CTA cluster per sequence.  CTA m of the cluster owns features
-// [128m, 128m+128) of D = 512 -- Omega blocks 2m, 2m+1 -- and the matching 128
-// columns of the state S [d_v=64, D].  Per chunk of C = 64 tokens:
+// One CTA (512 threads) per sequence; the whole fp32 state S^T [D=512 x d_v=64]
+// lives in tensor memory (4 slices of 128 features = 4 x 64 TMEM columns) for the
+// entire sequence.  Per chunk of C = 64 tokens:
 //
-//   1  gates (beta, cumulative log decay); k,q rows were prefetched by cp.async
-//      into a K-major 128B-swizzled bf16 tile during the previous chunk
-//   2  tcgen05 (bf16): Z = [k;q] Omega_m^T (M=128 tokens, N=128 features, K=64)  [TMEM]
-//      Omega_m is built once per CTA from the sign bits by the warp butterfly
-//      and is exact in bf16 (integers / 8).
-//   3  u = cos(tau_inv z + b) -> fp16 feature tile F = [U_k; U_q] (un-normalised)
-//      and per-token partial sums of squares
-//   4  tcgen05 (fp16): [G;P]_m = F U_k^T, [X;Yq]_m = F S_m^T                   [TMEM]
-//   5  DSMEM reduce-scatter of the G, P, X, Yq partials and the sums of squares
-//   6  the owner CTA of each 16-row block sums it, applies the feature norms
-//      (phi = u / (||u|| + 1e-8) becomes a row/column scaling) and all-gathers G, X
-//   7  every CTA (CUDA cores): A_ij = beta_i exp(g_i - g_j) G_ij (j<i),
-//      R = beta (v - exp(g) X), E = (I + A)^-1 R by blocked forward substitution;
-//      CTA m writes output rows [16m, 16m+16):
-//      y_i = exp(g_{i-1}) Yq_i + sum_{j<i} exp(g_{i-1} - g_j) P_ij e_j;
-//      E'' = exp(g_{C-1} - g_j) s_kj e_j (fp16)
-//   8  tcgen05 (fp16): S_m^T = exp(g_{C-1}) S_m^T + U_k^T E''                   [TMEM, fp32]
-//   9  S_m^T -> fp16 operand tile for the next chunk's step 4
+//   slice loop s = 0..3 (features [128s, 128s+128), Omega blocks 2s, 2s+1):
+//     L  tcgen05 (bf16): Z = [k;q] Omega_s^T   (M=128 tokens, N=128 features, K=64)
+//        -- the lift of slice s+1 is issued as soon as Z(s) has been read, so it
+//           runs under the cosines of slice s
+//     F  u = cos(tau_inv z + b) -> fp16 tile F = [U_k,s; U_q,s] (un-normalised),
+//        per-token sums of squares; U_k,s is also kept for the state update
+//     M  tcgen05 (fp16): [G;P] += F U_k,s^T,  [X;Yq] += F S_s^T          [TMEM]
+//   then, on the 64x64 chunk matrices (CUDA cores):
+//     feature norms (phi = u / (||u|| + 1e-8) become row/column scalings),
+//     A_ij = beta_i exp(g_i - g_j) G_ij (j<i),  R = beta (v - exp(g) X),
+//     E = (I + A)^-1 R (16x16 diagonal-block inverses + blocked forward substitution),
+//     Aq_ij = exp(g_{i-1} - g_j) P_ij (j<i),  E'' = exp(g_{C-1} - g_j) s_kj e_j (fp16)
+//   O  tcgen05 (fp16): [0; Aq] E -> lanes of the q rows;  y_i = exp(g_{i-1}) Yq_i + (Aq E)_i
+//   S  tcgen05 (fp16): S_s^T = exp(g_{C-1}) S_s^T + U_k,s^T E''   for s = 0..3 [TMEM, fp32]
 //
 // The algebra is the one of the CUDA-core path (prefill_simt.cu), itself the
 // reference chunk step kernels/fused_kernel_deltanet.py:95-149 rearranged.
-// Products run on tcgen05 with fp32 accumulation; the features, the state
-// operand copy and E'' are fp16 (10-bit mantissa, |values| well inside range);
-// the state itself stays fp32 in tensor memory for the whole sequence.
+// Products accumulate in fp32; the features, the state's operand copy and E''
+// are fp16 (10-bit mantissa; cosines are bounded, the other operands saturate);
+// the lift product is bf16 x bf16 and exact up to fp32 accumulation (Omega is
+// integers / 8, checked on the host).
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -40,42 +37,36 @@ namespace {
 
 __device__ int g_tc_error;
 
-constexpr int kG = 4;          // CTAs per sequence (cluster size)
-constexpr int kC = 64;         // chunk
-constexpr int kDV = 64;        // value dim
-constexpr int kThr = 256;      // threads per CTA
+constexpr int kC = 64;       // chunk
+constexpr int kDV = 64;      // value dim
+constexpr int kD = 512;      // lifted dim
+constexpr int kSlices = 4;   // 128-feature slices
+constexpr int kThr = 512;    // threads per CTA (4 warps per TMEM lane quarter)
 constexpr uint32_t kWaitLimit = 1u << 24;
 
-// shared-memory map (bytes from a 1024-aligned base)
-constexpr uint32_t OFF_OMG = 0;        // 16 KiB Omega slice (bf16, K-major; B of the lift)
-constexpr uint32_t OFF_XIN = 16384;    // 16 KiB [k;q] chunk inputs (bf16, K-major; A of the lift)
-constexpr uint32_t OFF_F = 32768;      // 32 KiB features [U_k;U_q] (fp16), 2 K-blocks x 128 rows x 128 B
-constexpr uint32_t OFF_SB = 65536;     // 16 KiB S_m operand (fp16, MN-major); in step 7: E (64x64 f32)
-constexpr uint32_t OFF_EB = 81920;     // 8 KiB  E'' (fp16, MN-major)
-constexpr uint32_t OFF_VB = 90112;     // 16 KiB v rows of the chunk (input dtype, row-major)
-constexpr uint32_t OFF_RS = 106496;    // 64 KiB reduce-scatter inbox [4 src][G,P,X,Yq][16][64] f32
-constexpr uint32_t OFF_AG = 172032;    // 32 KiB all-gather inbox [4 src][G,X][16][64] f32
-constexpr uint32_t OFF_SS = 204800;    // 2 KiB  sums-of-squares inbox [4 src][128] f32
-constexpr uint32_t OFF_MYP = 206848;   // 4 KiB  owned rows of P~, then of Aq
-constexpr uint32_t OFF_MYY = 210944;   // 4 KiB  owned rows of Yq~
-constexpr uint32_t OFF_TD = 215040;    // 4 KiB  diagonal 16x16 blocks of (I + A)^-1
-constexpr uint32_t OFF_US = 219136;    // 4 KiB  forward-substitution scratch [16][64]
-constexpr uint32_t OFF_PH = 223232;    // 512 B  phase of this CTA's 128 features
-constexpr uint32_t OFF_GL = 223744;    // 256 B  g_i (cumulative log decay)
-constexpr uint32_t OFF_BT = 224000;    // 256 B  beta_i
-constexpr uint32_t OFF_EG = 224256;    // 256 B  exp(g_i)
-constexpr uint32_t OFF_EGP = 224512;   // 256 B  exp(g_{i-1})
-constexpr uint32_t OFF_W = 224768;     // 256 B  exp(g_{C-1} - g_i)
-constexpr uint32_t OFF_SSP = 225024;   // 1 KiB  partial sums of squares [2][128]
-constexpr uint32_t OFF_SC = 226048;    // 512 B  token scales s = amp / (amp ||u|| + 1e-8)
-constexpr uint32_t OFF_BAR = 226560;   // mbarrier (8 B) + TMEM address (4 B)
-constexpr uint32_t kSmemBytes = 226576 + 1024;  // + alignment slack
-
 // TMEM columns
-constexpr uint32_t COL_S = 0;     // S_m^T: lanes = features, 64 cols = dv (fp32 master)
-constexpr uint32_t COL_Z = 64;    // lift result: lanes = tokens, 128 cols = features
-constexpr uint32_t COL_GP = 192;  // [G;P]: lanes = [k;q] tokens, 64 cols = k tokens
-constexpr uint32_t COL_XY = 256;  // [X;Yq]: lanes = [k;q] tokens, 64 cols = dv
+constexpr uint32_t COL_S = 0;     // S^T master: slice s at 64 s (lanes = features, cols = dv), fp32
+constexpr uint32_t COL_Z = 256;   // lift result: lanes = [k;q] tokens, 128 cols = features
+constexpr uint32_t COL_GP = 384;  // [G;P]: lanes = [k;q] tokens, 64 cols = k tokens; later [junk; Aq E]
+constexpr uint32_t COL_XY = 448;  // [X;Yq]: lanes = [k;q] tokens, 64 cols = dv
+
+// shared-memory map (bytes from a 1024-aligned base)
+constexpr uint32_t OFF_OMG = 0;        // 64 KiB Omega, slice s at 16 KiB s (bf16, K-major 128 x 64)
+constexpr uint32_t OFF_XIN = 65536;    // 16 KiB [k;q] inputs (bf16, K-major)
+constexpr uint32_t OFF_F = 81920;      // 32 KiB features [U_k;U_q] (fp16, K-major) | algebra: A, R (f32); then
+                                       //        the A operand [0; Aq] (fp16, K-major) of the output product
+constexpr uint32_t OFF_UK = 114688;    // 64 KiB U_k per slice (fp16), A operand of the state update
+constexpr uint32_t OFF_SB = 180224;    // 16 KiB state slice operand (fp16, MN-major)| algebra: E (f32)
+constexpr uint32_t OFF_EB = 196608;    // 8 KiB  E'' (fp16, MN-major), B operand of the state update
+constexpr uint32_t OFF_VB = 204800;    // 8 KiB  v rows of the chunk (bf16)
+constexpr uint32_t OFF_TD = 212992;    // 4 KiB  diagonal 16x16 blocks of (I + A)^-1 | then E (fp16, MN-major,
+constexpr uint32_t OFF_US = 217088;    // 4 KiB  forward-substitution scratch        |  8 KiB over TD+US)
+constexpr uint32_t OFF_PH = 221184;    // 2 KiB  phase b[512]
+constexpr uint32_t OFF_GL = 223232;    // 5 x 256 B: g, beta, exp(g), exp(g_{i-1}), exp(g_{C-1} - g)
+constexpr uint32_t OFF_SSP = 224512;   // 2 KiB  sums of squares per column quarter [4][128]
+constexpr uint32_t OFF_SC = 226560;    // 512 B  token scales s = amp / (amp ||u|| + 1e-8)
+constexpr uint32_t OFF_BAR = 227072;   // 2 mbarriers + TMEM address
+constexpr uint32_t kSmemBytes = 227096 + 1024;  // + alignment slack
 
 struct TcArgs {
   const void* q;
@@ -93,52 +84,66 @@ struct TcArgs {
   int NC;
 };
 
-__device__ __forceinline__ float cos_reduced(float x) {
-  // Cody-Waite reduction to [-pi, pi] (two-constant split of 2*pi), then the
-  // hardware cosine, accurate there to ~2^-21 absolute.
-  const float k = rintf(x * 0.15915494309189535f);
-  float r = fmaf(-k, 6.28318548202514648f, x);
-  r = fmaf(-k, -1.7484556e-07f, r);
-  return __cosf(r);
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// two floats -> packed fp16 pair (a in the low half); values already inside the fp16 range
 __device__ __forceinline__ uint32_t pack_f16(float a, float b) {
-  const float lim = 65504.f;  // saturate instead of overflowing to inf
-  __half2 h = __floats2half2_rn(fminf(fmaxf(a, -lim), lim), fminf(fmaxf(b, -lim), lim));
-  return *reinterpret_cast<uint32_t*>(&h);
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+// same, saturating to the largest finite fp16 instead of overflowing to inf
+__device__ __forceinline__ uint32_t pack_f16_sat(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
 }
 
-// k and q rows of chunk c -> the K-major swizzled input tile (bf16 inputs only)
+// index of element (i, j) of a 64x64 fp32 matrix whose float4 slots are swizzled
+// by row, so that row-wise and column-wise vector accesses are conflict-free
+__device__ __forceinline__ int sx(int i, int j) { return i * 64 + ((((j >> 2) ^ i) & 15) << 2) + (j & 3); }
+
+// k and q rows of chunk c -> the K-major swizzled input tile (bf16 inputs); 512 threads
 __device__ __forceinline__ void prefetch_kq(const TcArgs& a, int64_t n, int c, uint32_t xin, int tid) {
-  const int r = tid >> 1, hh = tid & 1;
+  const int r = tid >> 2, qq = tid & 3;  // row r of [k;q], 16-element quarter qq
   const int64_t t = int64_t(c) * kC + (r & 63);
   const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(r < 64 ? a.k : a.q);
   const bool in = t < a.T;
-  const __nv_bfloat16* src = base + (in ? (n * a.T + t) * 64 + 32 * hh : 0);
+  const __nv_bfloat16* src = base + (in ? (n * a.T + t) * 64 + 16 * qq : 0);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) tc::cp_async16(xin + tc::sw128_offset(r, 32 * hh + 8 * i), src + (in ? 8 * i : 0), in ? 16 : 0);
+  for (int i = 0; i < 2; ++i)
+    tc::cp_async16(xin + tc::sw128_offset(r, 16 * qq + 8 * i), src + (in ? 8 * i : 0), in ? 16 : 0);
 }
 
-// v rows of chunk c -> row-major tile in the input dtype
-__device__ __forceinline__ void prefetch_v(const TcArgs& a, int64_t n, int c, uint32_t vb, int tid) {
-  const int esz = a.in_dtype == KDN_DTYPE_BF16 ? 2 : 4;
-  const int cpr = 64 * esz / 16;  // 16-byte pieces per row
-  const char* base = reinterpret_cast<const char*>(a.v);
-  for (int e = tid; e < 64 * cpr; e += kThr) {
-    const int row = e / cpr, cc = e % cpr;
-    const int64_t t = int64_t(c) * kC + row;
-    const bool in = t < a.T;
-    const char* src = base + (in ? ((n * a.T + t) * 64) * esz + 16 * cc : 0);
-    tc::cp_async16(vb + row * 64 * esz + 16 * cc, src, in ? 16 : 0);
+// fp32 inputs: load and round to bf16 into the input tile
+__device__ __forceinline__ void load_kq_f32(const TcArgs& a, int64_t n, int c, uint8_t* xin, int tid) {
+  const int r = tid >> 2, qq = tid & 3;
+  const int64_t t = int64_t(c) * kC + (r & 63);
+  const float* src = reinterpret_cast<const float*>(r < 64 ? a.k : a.q) + (n * a.T + t) * 64 + 16 * qq;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    uint4 pk = make_uint4(0, 0, 0, 0);
+    if (t < a.T) {
+      const float4 x0 = reinterpret_cast<const float4*>(src)[2 * i];
+      const float4 x1 = reinterpret_cast<const float4*>(src)[2 * i + 1];
+      pk = make_uint4(pack_bf16(x0.x, x0.y), pack_bf16(x0.z, x0.w), pack_bf16(x1.x, x1.y), pack_bf16(x1.z, x1.w));
+    }
+    *reinterpret_cast<uint4*>(xin + tc::sw128_offset(r, 16 * qq + 8 * i)) = pk;
   }
 }
 
-__global__ void __cluster_dims__(kG, 1, 1) __launch_bounds__(kThr, 1)
-    prefill_tc_kernel(TcArgs a, ProjParams P) {
+// v rows of chunk c -> row-major bf16 tile (bf16 inputs); 512 threads, one 16-byte piece each
+__device__ __forceinline__ void prefetch_v(const TcArgs& a, int64_t n, int c, uint32_t vb, int tid) {
+  const int row = tid >> 3, cc = tid & 7;
+  const int64_t t = int64_t(c) * kC + row;
+  const bool in = t < a.T;
+  const char* src = reinterpret_cast<const char*>(a.v) + (in ? ((n * a.T + t) * 64) * 2 + 16 * cc : 0);
+  tc::cp_async16(vb + row * 128 + 16 * cc, src, in ? 16 : 0);
+}
+
+__global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm;
   {
@@ -146,35 +151,32 @@ __global__ void __cluster_dims__(kG, 1, 1) __launch_bounds__(kThr, 1)
     sm = smem_raw + ((1024u - (s & 1023u)) & 1023u);
   }
   const uint32_t sbase = tc::smem_u32(sm);
-  float* Es = reinterpret_cast<float*>(sm + OFF_SB);  // [64][64] during step 7
-  float* RS = reinterpret_cast<float*>(sm + OFF_RS);
-  float* AG = reinterpret_cast<float*>(sm + OFF_AG);
-  float* SS = reinterpret_cast<float*>(sm + OFF_SS);
-  float* myP = reinterpret_cast<float*>(sm + OFF_MYP);
-  float* myY = reinterpret_cast<float*>(sm + OFF_MYY);
+  float* Am = reinterpret_cast<float*>(sm + OFF_F);  // algebra phase views
+  float* Rm = reinterpret_cast<float*>(sm + OFF_F + 16384);
+  float* Es = reinterpret_cast<float*>(sm + OFF_SB);
   float* TD = reinterpret_cast<float*>(sm + OFF_TD);
   float* US = reinterpret_cast<float*>(sm + OFF_US);
   float* ph = reinterpret_cast<float*>(sm + OFF_PH);
   float* gl = reinterpret_cast<float*>(sm + OFF_GL);
-  float* bt = reinterpret_cast<float*>(sm + OFF_BT);
-  float* eg = reinterpret_cast<float*>(sm + OFF_EG);
-  float* egp = reinterpret_cast<float*>(sm + OFF_EGP);
-  float* wdec = reinterpret_cast<float*>(sm + OFF_W);
+  float* bt = gl + 64;
+  float* eg = gl + 128;
+  float* egp = gl + 192;
+  float* wdec = gl + 256;
   float* ssp = reinterpret_cast<float*>(sm + OFF_SSP);
   float* sc = reinterpret_cast<float*>(sm + OFF_SC);
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
+  uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 8);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 16);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t m = tc::cluster_ctarank();
-  const int64_t n = blockIdx.y;
-  const int quarter = warp & 3, half = warp >> 2;
-  const int trow = quarter * 32 + lane;  // TMEM lane owned by this thread
+  const int64_t n = blockIdx.x;
+  const int quarter = warp & 3, cq = warp >> 2;  // TMEM lane quarter, column quarter
+  const int trow = quarter * 32 + lane;          // TMEM lane owned by this thread
   const uint32_t lane_off = uint32_t(quarter * 32) << 16;
   const float amp = P.amp;
-  const bool kq_async = a.in_dtype == KDN_DTYPE_BF16;
+  const bool bf_in = a.in_dtype == KDN_DTYPE_BF16;
   bool ok = true;
-  uint32_t phase = 0;
+  uint32_t ph_lift = 0, ph_mma = 0;
 
   // ---------------------------------------------------------------- setup
   if (warp == 0) {
@@ -182,26 +184,28 @@ __global__ void __cluster_dims__(kG, 1, 1) __launch_bounds__(kThr, 1)
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    tc::mbar_init(mbar, 1);
+    tc::mbar_init(bar_lift, 1);
+    tc::mbar_init(bar_mma, 1);
     tc::fence_mbar_init();
   }
-  // Omega slice: feature row fl (block 2m + fl/64, row fl%64), column d = input index.
-  for (int job = warp; job < 128; job += kThr / 32) {
-    const int bl = job >> 6, d = job & 63;
-    const int blk = 2 * int(m) + bl;
+  // Omega: feature f = 64 blk + i, input index d; one butterfly per (blk, d)
+  for (int job = warp; job < 8 * 64; job += kThr / 32) {
+    const int blk = job >> 6, d = job & 63;
     const float x0 = (d == 2 * lane) ? 1.f : 0.f, x1 = (d == 2 * lane + 1) ? 1.f : 0.f;
     float u0, u1;
     structured_block(x0, x1, P.sign_bits[blk], lane, u0, u1);
-    const int f0 = 64 * bl + 2 * lane;
-    *reinterpret_cast<__nv_bfloat16*>(sm + OFF_OMG + tc::sw128_offset(f0, d)) = __float2bfloat16_rn(u0);
-    *reinterpret_cast<__nv_bfloat16*>(sm + OFF_OMG + tc::sw128_offset(f0 + 1, d)) = __float2bfloat16_rn(u1);
+    const int f0 = 64 * blk + 2 * lane, s = f0 >> 7, fl = f0 & 127;
+    uint8_t* om = sm + OFF_OMG + s * 16384;
+    *reinterpret_cast<__nv_bfloat16*>(om + tc::sw128_offset(fl, d)) = __float2bfloat16_rn(u0);
+    *reinterpret_cast<__nv_bfloat16*>(om + tc::sw128_offset(fl + 1, d)) = __float2bfloat16_rn(u1);
   }
-  if (tid < 128) ph[tid] = P.phase[128 * m + tid];
-  if (kq_async) prefetch_kq(a, n, 0, sbase + OFF_XIN, tid);
-  prefetch_v(a, n, 0, sbase + OFF_VB, tid);
+  for (int i = tid; i < kD; i += kThr) ph[i] = P.phase[i];
+  if (bf_in) {
+    prefetch_kq(a, n, 0, sbase + OFF_XIN, tid);
+    prefetch_v(a, n, 0, sbase + OFF_VB, tid);
+  }
   tc::cp_async_commit();
-  // gates of the next chunk are carried in registers of warp 0
-  float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};
+  float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};  // gates of the coming chunk (warp 0)
   if (warp == 0) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -216,57 +220,31 @@ __global__ void __cluster_dims__(kG, 1, 1) __launch_bounds__(kThr, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tslot;
-
-  // state: S_m^T master (fp32, TMEM) and its fp16 operand copy
-  {
-    float v[32];
-    const int f = 128 * int(m) + trow;
+  // state master S^T (fp32) from the initial state
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int dv = 32 * half + j;
-      v[j] = a.S0 ? a.S0[(n * kDV + dv) * 512 + f] : 0.f;
-    }
-    tc::tmem_st32(tmem + lane_off + COL_S + 32 * half, v);
-    tc::tmem_st_wait();
+  for (int s = 0; s < kSlices; ++s) {
+    float v[16];
+    const int f = 128 * s + trow;
 #pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      uint4 pk = make_uint4(pack_f16(v[8 * c4], v[8 * c4 + 1]), pack_f16(v[8 * c4 + 2], v[8 * c4 + 3]),
-                            pack_f16(v[8 * c4 + 4], v[8 * c4 + 5]), pack_f16(v[8 * c4 + 6], v[8 * c4 + 7]));
-      *reinterpret_cast<uint4*>(sm + OFF_SB + tc::sw128_offset(trow, 32 * half + 8 * c4)) = pk;
-    }
+    for (int j = 0; j < 16; ++j) v[j] = a.S0 ? a.S0[(n * kDV + 16 * cq + j) * kD + f] : 0.f;
+    tc::tmem_st16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
   }
-  tc::fence_proxy_async_smem();
+  tc::tmem_st_wait();
   tc::fence_before_sync();
-  tc::cluster_sync();  // all CTAs of the cluster are running before any DSMEM access
+  __syncthreads();
   tc::fence_after_sync();
 
   const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
   const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
   const uint32_t id_xy = tc::idesc_f16_f32(128, 64, false, true);
   const uint32_t id_ds = tc::idesc_f16_f32(128, 64, true, true);
-  auto AGG = [&](int i) -> float* { return AG + ((i >> 4) * 2 + 0) * 1024 + (i & 15) * 64; };
-  auto AGX = [&](int i) -> float* { return AG + ((i >> 4) * 2 + 1) * 1024 + (i & 15) * 64; };
 
   for (int c = 0; c < a.NC; ++c) {
     const int64_t t0 = int64_t(c) * kC;
     const bool has_next = c + 1 < a.NC;
-    // ------------------------------------------------ 1. inputs and gates
+    // ------------------------------------------------ inputs and gates
     tc::cp_async_wait_all();
-    if (!kq_async) {  // fp32 inputs: load and round to bf16 here
-      const int r = tid >> 1, hh = tid & 1;
-      const int64_t t = t0 + (r & 63);
-      const float* src = reinterpret_cast<const float*>(r < 64 ? a.k : a.q) + (n * a.T + t) * 64 + 32 * hh;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 pk = make_uint4(0, 0, 0, 0);
-        if (t < a.T) {
-          const float4 x0 = reinterpret_cast<const float4*>(src)[2 * i];
-          const float4 x1 = reinterpret_cast<const float4*>(src)[2 * i + 1];
-          pk = make_uint4(pack_bf16(x0.x, x0.y), pack_bf16(x0.z, x0.w), pack_bf16(x1.x, x1.y), pack_bf16(x1.z, x1.w));
-        }
-        *reinterpret_cast<uint4*>(sm + OFF_XIN + tc::sw128_offset(r, 32 * hh + 8 * i)) = pk;
-      }
-    }
+    if (!bf_in) load_kq_f32(a, n, c, sm + OFF_XIN, tid);
     if (warp == 0) {  // beta, inclusive scan of log clamp(decay, 1e-5, 1), derived factors
       const float lg0 = logf(fminf(fmaxf(nd[0], 1e-5f), 1.0f)), lg1 = logf(fminf(fmaxf(nd[1], 1e-5f), 1.0f));
       float s = lg0 + lg1;
@@ -288,7 +266,6 @@ __global__ void __cluster_dims__(kG, 1, 1) __launch_bounds__(kThr, 1)
       egp[2 * lane + 1] = __expf(g0);
       wdec[2 * lane] = __expf(gend - g0);
       wdec[2 * lane + 1] = __expf(gend - g1);
-      // gates of the next chunk (consumed at its step 1)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int64_t tt = t0 + kC + 2 * lane + e;
@@ -305,159 +282,156 @@ __global__ void __cluster_dims__(kG, 1, 1) __launch_bounds__(kThr, 1)
     __syncthreads();
     tc::fence_after_sync();
 
-    // ------------------------------------------------ 2. lift product (bf16)
-    if (tid == 0) {
+    // ------------------------------------------------ slice loop
+    if (tid == 0) {  // lift of slice 0
 #pragma unroll
-      for (int k0 = 0; k0 < 64; k0 += 16) {
-        const uint64_t ad = tc::smem_desc_sw128(sbase + OFF_XIN + 2 * k0, 16, 1024);
-        const uint64_t bd = tc::smem_desc_sw128(sbase + OFF_OMG + 2 * k0, 16, 1024);
-        tc::mma_ss(tmem + COL_Z, ad, bd, id_lift, k0 > 0);
-      }
-      tc::mma_commit(mbar);
+      for (int k0 = 0; k0 < 64; k0 += 16)
+        tc::mma_ss(tmem + COL_Z, tc::smem_desc_sw128(sbase + OFF_XIN + 2 * k0, 16, 1024),
+                   tc::smem_desc_sw128(sbase + OFF_OMG + 2 * k0, 16, 1024), id_lift, k0 > 0);
+      tc::mma_commit(bar_lift);
     }
-    __syncwarp();
-    ok &= tc::mbar_wait_bounded(mbar, phase, kWaitLimit);
-    phase ^= 1;
-    tc::fence_after_sync();
-    // the input tile is free again: prefetch the next chunk's k,q rows into it
-    if (has_next && kq_async) prefetch_kq(a, n, c + 1, sbase + OFF_XIN, tid);
-    tc::cp_async_commit();
-
-    // ------------------------------------------------ 3. features (fp16)
-    {
-      float ss = 0.f;
+    float ss = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < kSlices; ++s) {
+      __syncwarp();
+      ok &= tc::mbar_wait_bounded(bar_lift, ph_lift, kWaitLimit);
+      ph_lift ^= 1;
+      tc::fence_after_sync();
+      float z[32];
+      tc::tmem_ld32(tmem + lane_off + COL_Z + 32 * cq, z);
+      tc::tmem_ld_wait();
+      tc::fence_before_sync();
+      __syncthreads();  // Z has been read by everyone
+      if (tid == 0 && s + 1 < kSlices) {  // lift of the next slice runs under the cosines
+        tc::fence_after_sync();
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        float z[32];
-        tc::tmem_ld32(tmem + lane_off + COL_Z + 64 * half + 32 * part, z);
+        for (int k0 = 0; k0 < 64; k0 += 16)
+          tc::mma_ss(tmem + COL_Z, tc::smem_desc_sw128(sbase + OFF_XIN + 2 * k0, 16, 1024),
+                     tc::smem_desc_sw128(sbase + OFF_OMG + (s + 1) * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
+        tc::mma_commit(bar_lift);
+      }
+      // u = cos(tau_inv z + b): the hardware cosine is accurate to ~1e-6 absolute for
+      // the |arguments| <= 32 met here, far below the fp16 spacing of the stored result
+      uint32_t fp[16];
+      const float4* phs = reinterpret_cast<const float4*>(ph + 128 * s + 32 * cq);
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 b4 = phs[j >> 2];
+        const float u0 = __cosf(fmaf(z[j], P.tau_inv, b4.x));
+        const float u1 = __cosf(fmaf(z[j + 1], P.tau_inv, b4.y));
+        const float u2 = __cosf(fmaf(z[j + 2], P.tau_inv, b4.z));
+        const float u3 = __cosf(fmaf(z[j + 3], P.tau_inv, b4.w));
+        ss = fmaf(u0, u0, fmaf(u1, u1, fmaf(u2, u2, fmaf(u3, u3, ss))));
+        fp[j >> 1] = pack_f16(u0, u1);
+        fp[(j >> 1) + 1] = pack_f16(u2, u3);
+      }
+      uint32_t sp[8];
+      {
+        float v[16];
+        tc::tmem_ld16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
         tc::tmem_ld_wait();
-        const float* phs = ph + 64 * half + 32 * part;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          float u[8];
+        for (int j = 0; j < 8; ++j) sp[j] = pack_f16_sat(v[2 * j], v[2 * j + 1]);
+      }
+      if (s > 0) {  // the previous slice's products must be done with F and SB
+        __syncwarp();
+        ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
+        ph_mma ^= 1;
+      }
+      {
+        const int kb = cq >> 1, e0 = 32 * (cq & 1);
+        uint8_t* fb = sm + OFF_F + kb * 16384;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            u[j] = cos_reduced(fmaf(z[8 * c4 + j], P.tau_inv, phs[8 * c4 + j]));
-            ss = fmaf(u[j], u[j], ss);
+        for (int c8 = 0; c8 < 4; ++c8) {
+          const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
+          const uint32_t off = tc::sw128_offset(trow, e0 + 8 * c8);
+          *reinterpret_cast<uint4*>(fb + off) = pk;
+          if (trow < 64) *reinterpret_cast<uint4*>(sm + OFF_UK + s * 16384 + kb * 8192 + off) = pk;
+        }
+#pragma unroll
+        for (int c8 = 0; c8 < 2; ++c8)
+          *reinterpret_cast<uint4*>(sm + OFF_SB + tc::sw128_offset(trow, 16 * cq + 8 * c8)) =
+              make_uint4(sp[4 * c8], sp[4 * c8 + 1], sp[4 * c8 + 2], sp[4 * c8 + 3]);
+      }
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int k0 = 0; k0 < 128; k0 += 16) {
+          const uint64_t fd = tc::smem_desc_sw128(sbase + OFF_F + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
+          const uint64_t sd = tc::smem_desc_sw128(sbase + OFF_SB + 128 * k0, 16384, 1024);
+          tc::mma_ss(tmem + COL_GP, fd, fd, id_gp, s > 0 || k0 > 0);
+          tc::mma_ss(tmem + COL_XY, fd, sd, id_xy, s > 0 || k0 > 0);
+        }
+        tc::mma_commit(bar_mma);
+      }
+    }
+    ssp[cq * 128 + trow] = ss;
+    // the input tile is free: prefetch the next chunk's k,q rows into it
+    if (has_next && bf_in) prefetch_kq(a, n, c + 1, sbase + OFF_XIN, tid);
+    tc::cp_async_commit();
+    __syncwarp();
+    ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
+    ph_mma ^= 1;
+    tc::fence_after_sync();
+
+    // ------------------------------------------------ chunk matrices
+    float gp[16], xy[16], vv[16];
+    tc::tmem_ld16(tmem + lane_off + COL_GP + 16 * cq, gp);
+    tc::tmem_ld16(tmem + lane_off + COL_XY + 16 * cq, xy);
+    tc::tmem_ld_wait();
+    if (trow < 64) {
+      const int64_t t = t0 + trow;
+      if (bf_in) {
+        const __nv_bfloat16* vr = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_VB) + trow * 64 + 16 * cq;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) vv[j] = __bfloat162float(vr[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          vv[j] = t < a.T ? reinterpret_cast<const float*>(a.v)[(n * a.T + t) * kDV + 16 * cq + j] : 0.f;
+      }
+    }
+    __syncthreads();  // sums of squares visible; v tile consumed
+    if (has_next && bf_in) prefetch_v(a, n, c + 1, sbase + OFF_VB, tid);
+    tc::cp_async_commit();
+    if (tid < 128)
+      sc[tid] = amp / (amp * sqrtf(ssp[tid] + ssp[128 + tid] + ssp[256 + tid] + ssp[384 + tid]) + 1e-8f);
+    __syncthreads();
+    float aq[16], yq[16];  // q-row threads: their row of Aq and of the scaled Yq
+    {
+      const int i = trow & 63;
+      const float si = sc[trow];
+      const float bi = bt[i];
+      if (trow < 64) {  // k row: A (from G) and R (from X)
+        const float gi = gl[i], egi = eg[i];
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+          float4 av, rv;
+          float* ap = &av.x;
+          float* rp = &rv.x;
+#pragma unroll
+          for (int qx = 0; qx < 4; ++qx) {
+            const int jj = 4 * j4 + qx, j = 16 * cq + jj;
+            ap[qx] = (j < i) ? bi * __expf(gi - gl[j]) * gp[jj] * si * sc[j] : 0.f;
+            rp[qx] = bi * (vv[jj] - egi * xy[jj] * si);
           }
-          *reinterpret_cast<uint4*>(sm + OFF_F + half * 16384 + tc::sw128_offset(trow, 32 * part + 8 * c4)) =
-              make_uint4(pack_f16(u[0], u[1]), pack_f16(u[2], u[3]), pack_f16(u[4], u[5]), pack_f16(u[6], u[7]));
+          *reinterpret_cast<float4*>(Am + sx(i, 16 * cq + 4 * j4)) = av;
+          *reinterpret_cast<float4*>(Rm + sx(i, 16 * cq + 4 * j4)) = rv;
+        }
+      } else {  // q row
+        const float gp_i = i > 0 ? gl[i - 1] : 0.f, yscale = si * egp[i];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = 16 * cq + jj;
+          aq[jj] = (j < i) ? __expf(gp_i - gl[j]) * gp[jj] * si * sc[j] : 0.f;
+          yq[jj] = xy[jj] * yscale;
         }
       }
-      ssp[half * 128 + trow] = ss;
-    }
-    tc::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-
-    // ------------------------------------------------ 4. Gram and state products (fp16)
-    if (tid == 0) {
-#pragma unroll
-      for (int k0 = 0; k0 < 128; k0 += 16) {
-        const uint64_t fd = tc::smem_desc_sw128(sbase + OFF_F + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
-        const uint64_t sd = tc::smem_desc_sw128(sbase + OFF_SB + 128 * k0, 16384, 1024);
-        tc::mma_ss(tmem + COL_GP, fd, fd, id_gp, k0 > 0);
-        tc::mma_ss(tmem + COL_XY, fd, sd, id_xy, k0 > 0);
-      }
-      tc::mma_commit(mbar);
-    }
-    __syncwarp();
-    ok &= tc::mbar_wait_bounded(mbar, phase, kWaitLimit);
-    phase ^= 1;
-    tc::fence_after_sync();
-
-    // ------------------------------------------------ 5. reduce-scatter to the row owners
-    {
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        float v[32];
-        tc::tmem_ld32(tmem + lane_off + (which ? COL_XY : COL_GP) + 32 * half, v);
-        tc::tmem_ld_wait();
-        const int mat = 2 * which + (trow >= 64 ? 1 : 0);  // 0 G, 1 P, 2 X, 3 Yq
-        const int i = trow & 63;
-        const uint32_t owner = uint32_t(i >> 4);
-        const uint32_t laddr = sbase + OFF_RS + 4u * uint32_t((((m * 4 + mat) * 16 + (i & 15)) * 64) + 32 * half);
-        const uint32_t raddr = tc::mapa(laddr, owner);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) tc::st_cluster_v4(raddr + 16 * j, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      }
-      if (tid < 128) {
-        const float ss = ssp[tid] + ssp[128 + tid];
-        const uint32_t laddr = sbase + OFF_SS + 4u * (m * 128 + tid);
-#pragma unroll
-        for (uint32_t o = 0; o < kG; ++o) tc::st_cluster_f32(tc::mapa(laddr, o), ss);
-      }
-    }
-    tc::fence_before_sync();
-    tc::cluster_sync();
-    tc::fence_after_sync();
-
-    // ------------------------------------------------ 6. owner reduction, norms, all-gather
-    if (tid < 128) {
-      const float ss = SS[tid] + SS[128 + tid] + SS[256 + tid] + SS[384 + tid];
-      sc[tid] = amp / (amp * sqrtf(ss) + 1e-8f);  // phi = s * u
     }
     __syncthreads();
-#pragma unroll
-    for (int rep = 0; rep < 4; ++rep) {
-      const int e4 = tid + kThr * rep;  // float4 index over [4 mat][16 rows][16]
-      const int mat = e4 >> 8, lr = (e4 >> 4) & 15, c0 = (e4 & 15) * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int s = 0; s < kG; ++s) {
-        const float4 x = *reinterpret_cast<const float4*>(RS + (((s * 4 + mat) * 16 + lr) * 64) + c0);
-        acc.x += x.x;
-        acc.y += x.y;
-        acc.z += x.z;
-        acc.w += x.w;
-      }
-      const int i = 16 * int(m) + lr;
-      const float rs = (mat == 0 || mat == 2) ? sc[i] : sc[64 + i];
-      float cs[4] = {1.f, 1.f, 1.f, 1.f};
-      if (mat < 2) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) cs[q] = sc[c0 + q];
-      }
-      acc.x *= rs * cs[0];
-      acc.y *= rs * cs[1];
-      acc.z *= rs * cs[2];
-      acc.w *= rs * cs[3];
-      if (mat == 1) {
-        *reinterpret_cast<float4*>(myP + lr * 64 + c0) = acc;
-      } else if (mat == 3) {
-        *reinterpret_cast<float4*>(myY + lr * 64 + c0) = acc;
-      } else {
-        const uint32_t laddr = sbase + OFF_AG + 4u * uint32_t(((m * 2 + (mat >> 1)) * 16 + lr) * 64 + c0);
-#pragma unroll
-        for (uint32_t o = 0; o < kG; ++o) tc::st_cluster_v4(tc::mapa(laddr, o), acc.x, acc.y, acc.z, acc.w);
-      }
-    }
-    tc::fence_before_sync();
-    tc::cluster_sync();
-    tc::fence_after_sync();
-
-    // ------------------------------------------------ 7. small chunk algebra (CUDA cores)
-    // A in place of G~, R in place of X~, Aq in place of the owned rows of P~
-    {
-      const bool vbf = a.in_dtype == KDN_DTYPE_BF16;
-      for (int e = tid; e < 64 * 64; e += kThr) {
-        const int i = e >> 6, j = e & 63;
-        float* g = AGG(i) + j;
-        *g = (j < i) ? bt[i] * __expf(gl[i] - gl[j]) * (*g) : 0.f;
-        const float vv = vbf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sm + OFF_VB)[e])
-                             : reinterpret_cast<const float*>(sm + OFF_VB)[e];
-        float* x = AGX(i) + j;
-        *x = bt[i] * (vv - eg[i] * (*x));
-      }
-      for (int e = tid; e < 16 * 64; e += kThr) {
-        const int lr = e >> 6, j = e & 63, i = 16 * int(m) + lr;
-        myP[e] = (j < i) ? myP[e] * __expf((i > 0 ? gl[i - 1] : 0.f) - gl[j]) : 0.f;
-      }
-    }
-    __syncthreads();
-    if (has_next) prefetch_v(a, n, c + 1, sbase + OFF_VB, tid);  // v tile is free now
-    tc::cp_async_commit();
     // diagonal 16x16 blocks of (I + A)^-1: one warp per block, one lane per column
     if (warp < 4 && lane < 16) {
       const int I = warp, j = lane;
@@ -465,164 +439,186 @@ __global__ void __cluster_dims__(kG, 1, 1) __launch_bounds__(kThr, 1)
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
         float s = (r == j) ? 1.f : 0.f;
-        const float* arow = AGG(16 * I + r) + 16 * I;
 #pragma unroll
-        for (int kk = 0; kk < r; ++kk) s = fmaf(-arow[kk], tcol[kk], s);
+        for (int kk = 0; kk < r; ++kk) s = fmaf(-Am[sx(16 * I + r, 16 * I + kk)], tcol[kk], s);
         tcol[r] = (r >= j) ? s : 0.f;
       }
 #pragma unroll
       for (int r = 0; r < 16; ++r) TD[(I * 16 + r) * 16 + j] = tcol[r];
     }
     __syncthreads();
-    // E = (I + A)^-1 R, block row by block row:
-    //   U = R_I - sum_{J<I} A_IJ E_J;  E_I = T_II U
+    // E = (I + A)^-1 R, block row by block row: U = R_I - sum_{J<I} A_IJ E_J ; E_I = T_II U.
+    // E and U are row-major (each warp reads/writes whole rows: conflict-free); A rows are
+    // read as swizzled float4 slots.
     {
-      const int r = tid >> 4, c4 = (tid & 15) * 4;
+      const int r = tid >> 5, c2 = (tid & 31) * 2;
+#pragma unroll
       for (int I = 0; I < 4; ++I) {
-        const float* arow = AGG(16 * I + r);
-        float4 acc = *reinterpret_cast<const float4*>(AGX(16 * I + r) + c4);
-        float4 acc2 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int kk = 0; kk < 16 * I; kk += 2) {
-          const float a0 = arow[kk], a1 = arow[kk + 1];
-          const float4 e0 = *reinterpret_cast<const float4*>(Es + kk * 64 + c4);
-          const float4 e1 = *reinterpret_cast<const float4*>(Es + (kk + 1) * 64 + c4);
-          acc.x = fmaf(-a0, e0.x, acc.x);
-          acc.y = fmaf(-a0, e0.y, acc.y);
-          acc.z = fmaf(-a0, e0.z, acc.z);
-          acc.w = fmaf(-a0, e0.w, acc.w);
-          acc2.x = fmaf(-a1, e1.x, acc2.x);
-          acc2.y = fmaf(-a1, e1.y, acc2.y);
-          acc2.z = fmaf(-a1, e1.z, acc2.z);
-          acc2.w = fmaf(-a1, e1.w, acc2.w);
+        const int row = 16 * I + r;
+        float2 acc = *reinterpret_cast<const float2*>(Rm + sx(row, c2));
+        float2 acc2 = make_float2(0.f, 0.f);
+        const float* arow = Am + row * 64;
+#pragma unroll
+        for (int qs = 0; qs < 4 * I; ++qs) {
+          const float4 a4 = *reinterpret_cast<const float4*>(arow + (((qs ^ row) & 15) << 2));
+          const float2 e0 = *reinterpret_cast<const float2*>(Es + (4 * qs + 0) * 64 + c2);
+          const float2 e1 = *reinterpret_cast<const float2*>(Es + (4 * qs + 1) * 64 + c2);
+          const float2 e2 = *reinterpret_cast<const float2*>(Es + (4 * qs + 2) * 64 + c2);
+          const float2 e3 = *reinterpret_cast<const float2*>(Es + (4 * qs + 3) * 64 + c2);
+          acc.x = fmaf(-a4.x, e0.x, acc.x);
+          acc.y = fmaf(-a4.x, e0.y, acc.y);
+          acc2.x = fmaf(-a4.y, e1.x, acc2.x);
+          acc2.y = fmaf(-a4.y, e1.y, acc2.y);
+          acc.x = fmaf(-a4.z, e2.x, acc.x);
+          acc.y = fmaf(-a4.z, e2.y, acc.y);
+          acc2.x = fmaf(-a4.w, e3.x, acc2.x);
+          acc2.y = fmaf(-a4.w, e3.y, acc2.y);
         }
         acc.x += acc2.x;
         acc.y += acc2.y;
-        acc.z += acc2.z;
-        acc.w += acc2.w;
-        *reinterpret_cast<float4*>(US + r * 64 + c4) = acc;
+        *reinterpret_cast<float2*>(US + r * 64 + c2) = acc;
         __syncthreads();
-        float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
-        const float* trw = TD + (I * 16 + r) * 16;
-        for (int kk = 0; kk <= r; ++kk) {
-          const float tv = trw[kk];
-          const float4 u = *reinterpret_cast<const float4*>(US + kk * 64 + c4);
-          e.x = fmaf(tv, u.x, e.x);
-          e.y = fmaf(tv, u.y, e.y);
-          e.z = fmaf(tv, u.z, e.z);
-          e.w = fmaf(tv, u.w, e.w);
+        float2 e = make_float2(0.f, 0.f), e2 = make_float2(0.f, 0.f);
+        const float4* trw = reinterpret_cast<const float4*>(TD + (I * 16 + r) * 16);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {  // T_II is lower triangular (zeros above)
+          const float4 t4 = trw[q4];
+          const float2 u0 = *reinterpret_cast<const float2*>(US + (4 * q4 + 0) * 64 + c2);
+          const float2 u1 = *reinterpret_cast<const float2*>(US + (4 * q4 + 1) * 64 + c2);
+          const float2 u2 = *reinterpret_cast<const float2*>(US + (4 * q4 + 2) * 64 + c2);
+          const float2 u3 = *reinterpret_cast<const float2*>(US + (4 * q4 + 3) * 64 + c2);
+          e.x = fmaf(t4.x, u0.x, e.x);
+          e.y = fmaf(t4.x, u0.y, e.y);
+          e2.x = fmaf(t4.y, u1.x, e2.x);
+          e2.y = fmaf(t4.y, u1.y, e2.y);
+          e.x = fmaf(t4.z, u2.x, e.x);
+          e.y = fmaf(t4.z, u2.y, e.y);
+          e2.x = fmaf(t4.w, u3.x, e2.x);
+          e2.y = fmaf(t4.w, u3.y, e2.y);
         }
-        *reinterpret_cast<float4*>(Es + (16 * I + r) * 64 + c4) = e;
+        e.x += e2.x;
+        e.y += e2.y;
+        *reinterpret_cast<float2*>(Es + row * 64 + c2) = e;
         __syncthreads();
       }
     }
-    // outputs y for rows [16m, 16m+16)
+    // operands of the output and state products
     {
-      const int r = tid >> 4, c4 = (tid & 15) * 4, i = 16 * int(m) + r;
-      float4 y = *reinterpret_cast<const float4*>(myY + r * 64 + c4);
-      const float gp = egp[i];
-      y.x *= gp;
-      y.y *= gp;
-      y.z *= gp;
-      y.w *= gp;
-      const float* prow = myP + r * 64;
-      for (int j = 0; j < i; ++j) {
-        const float pv = prow[j];
-        const float4 e = *reinterpret_cast<const float4*>(Es + j * 64 + c4);
-        y.x = fmaf(pv, e.x, y.x);
-        y.y = fmaf(pv, e.y, y.y);
-        y.z = fmaf(pv, e.z, y.z);
-        y.w = fmaf(pv, e.w, y.w);
-      }
-      const int64_t t = t0 + i;
-      if (t < a.T) {
-        const int64_t o = (n * a.T + t) * kDV + c4;
-        if (a.y_dtype == KDN_DTYPE_BF16)
-          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.y) + o) =
-              make_uint2(pack_bf16(y.x, y.y), pack_bf16(y.z, y.w));
-        else
-          *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o) = y;
-      }
-    }
-    // E'' = exp(g_{C-1} - g_j) s_kj e_j (fp16, token rows, dv contiguous)
-    for (int e = tid; e < 64 * 8; e += kThr) {
-      const int j = e >> 3, c8 = (e & 7) * 8;
+      const int j = tid >> 3, c8 = (tid & 7) * 8;  // one 8-wide piece of row j of E per thread
+      const float4 e0 = *reinterpret_cast<const float4*>(Es + j * 64 + c8);
+      const float4 e1 = *reinterpret_cast<const float4*>(Es + j * 64 + c8 + 4);
+      const uint32_t off = tc::sw128_offset(j, c8);
+      *reinterpret_cast<uint4*>(sm + OFF_TD + off) =  // E (fp16, MN-major) over TD+US
+          make_uint4(pack_f16_sat(e0.x, e0.y), pack_f16_sat(e0.z, e0.w), pack_f16_sat(e1.x, e1.y),
+                     pack_f16_sat(e1.z, e1.w));
       const float w = wdec[j] * sc[j];
-      const float* er = Es + j * 64 + c8;
-      *reinterpret_cast<uint4*>(sm + OFF_EB + tc::sw128_offset(j, c8)) =
-          make_uint4(pack_f16(w * er[0], w * er[1]), pack_f16(w * er[2], w * er[3]), pack_f16(w * er[4], w * er[5]),
-                     pack_f16(w * er[6], w * er[7]));
+      *reinterpret_cast<uint4*>(sm + OFF_EB + off) =  // E'' = exp(g_{C-1} - g_j) s_kj e_j
+          make_uint4(pack_f16_sat(w * e0.x, w * e0.y), pack_f16_sat(w * e0.z, w * e0.w),
+                     pack_f16_sat(w * e1.x, w * e1.y), pack_f16_sat(w * e1.z, w * e1.w));
+      // A operand [0; Aq] (fp16, K-major, 128 rows x 64) in the (now free) feature tile
+      if (trow < 64) {
+        if (cq < 2)
+          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq) + 0) = make_uint4(0, 0, 0, 0),
+          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq + 8)) = make_uint4(0, 0, 0, 0),
+          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq + 16)) = make_uint4(0, 0, 0, 0),
+          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq + 24)) = make_uint4(0, 0, 0, 0);
+      } else {
+#pragma unroll
+        for (int c8b = 0; c8b < 2; ++c8b)
+          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 16 * cq + 8 * c8b)) =
+              make_uint4(pack_f16_sat(aq[8 * c8b], aq[8 * c8b + 1]), pack_f16_sat(aq[8 * c8b + 2], aq[8 * c8b + 3]),
+                         pack_f16_sat(aq[8 * c8b + 4], aq[8 * c8b + 5]),
+                         pack_f16_sat(aq[8 * c8b + 6], aq[8 * c8b + 7]));
+      }
     }
     // decay of the carried state
     {
       const float gC = eg[63];
       if (gC != 1.0f) {
-        float v[32];
-        tc::tmem_ld32(tmem + lane_off + COL_S + 32 * half, v);
-        tc::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= gC;
-        tc::tmem_st32(tmem + lane_off + COL_S + 32 * half, v);
+        for (int s = 0; s < kSlices; ++s) {
+          float v[16];
+          tc::tmem_ld16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= gC;
+          tc::tmem_st16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
+        }
         tc::tmem_st_wait();
       }
     }
     tc::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
-    tc::fence_after_sync();
 
-    // ------------------------------------------------ 8. state update (fp16 operands, fp32 state)
+    // ------------------------------------------------ output product and state update
     if (tid == 0) {
+      tc::fence_after_sync();
 #pragma unroll
-      for (int k0 = 0; k0 < 64; k0 += 16) {
-        const uint64_t ad = tc::smem_desc_sw128(sbase + OFF_F + 128 * k0, 16384, 1024);
-        const uint64_t bd = tc::smem_desc_sw128(sbase + OFF_EB + 128 * k0, 8192, 1024);
-        tc::mma_ss(tmem + COL_S, ad, bd, id_ds, true);
-      }
-      tc::mma_commit(mbar);
+      for (int k0 = 0; k0 < 64; k0 += 16)  // [junk; Aq E] -> lanes of the q rows
+        tc::mma_ss(tmem + COL_GP, tc::smem_desc_sw128(sbase + OFF_F + 2 * k0, 16, 1024),
+                   tc::smem_desc_sw128(sbase + OFF_TD + 128 * k0, 8192, 1024), id_xy, k0 > 0);
+#pragma unroll
+      for (int s = 0; s < kSlices; ++s)  // S_s^T += U_k,s^T E''
+#pragma unroll
+        for (int k0 = 0; k0 < 64; k0 += 16)
+          tc::mma_ss(tmem + COL_S + 64 * s, tc::smem_desc_sw128(sbase + OFF_UK + s * 16384 + 128 * k0, 8192, 1024),
+                     tc::smem_desc_sw128(sbase + OFF_EB + 128 * k0, 8192, 1024), id_ds, true);
+      tc::mma_commit(bar_mma);
     }
     __syncwarp();
-    ok &= tc::mbar_wait_bounded(mbar, phase, kWaitLimit);
-    phase ^= 1;
+    ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
+    ph_mma ^= 1;
     tc::fence_after_sync();
-
-    // ------------------------------------------------ 9. fp16 operand copy of the state
-    {
-      float v[32];
-      tc::tmem_ld32(tmem + lane_off + COL_S + 32 * half, v);
+    // outputs: y_i = exp(g_{i-1}) s_qi Yq_i + (Aq E)_i, by the threads of the q rows
+    if (trow >= 64) {
+      float ye[16];
+      tc::tmem_ld16(tmem + lane_off + COL_GP + 16 * cq, ye);
       tc::tmem_ld_wait();
+      const int i = trow - 64;
+      const int64_t t = t0 + i;
+      if (t < a.T) {
+        const int64_t o = (n * a.T + t) * kDV + 16 * cq;
+        float yy[16];
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint4 pk = make_uint4(pack_f16(v[8 * c4], v[8 * c4 + 1]), pack_f16(v[8 * c4 + 2], v[8 * c4 + 3]),
-                              pack_f16(v[8 * c4 + 4], v[8 * c4 + 5]), pack_f16(v[8 * c4 + 6], v[8 * c4 + 7]));
-        *reinterpret_cast<uint4*>(sm + OFF_SB + tc::sw128_offset(trow, 32 * half + 8 * c4)) = pk;
+        for (int j = 0; j < 16; ++j) yy[j] = yq[j] + ye[j];
+        if (a.y_dtype == KDN_DTYPE_BF16) {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + o);
+          dst[0] = make_uint4(pack_bf16(yy[0], yy[1]), pack_bf16(yy[2], yy[3]), pack_bf16(yy[4], yy[5]),
+                              pack_bf16(yy[6], yy[7]));
+          dst[1] = make_uint4(pack_bf16(yy[8], yy[9]), pack_bf16(yy[10], yy[11]), pack_bf16(yy[12], yy[13]),
+                              pack_bf16(yy[14], yy[15]));
+        } else {
+          float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) dst[u] = make_float4(yy[4 * u], yy[4 * u + 1], yy[4 * u + 2], yy[4 * u + 3]);
+        }
       }
     }
-    tc::fence_proxy_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
   }
 
   // ---------------------------------------------------------------- output state
-  {
-    float v[32];
-    tc::tmem_ld32(tmem + lane_off + COL_S + 32 * half, v);
-    tc::tmem_ld_wait();
-    const int f = 128 * int(m) + trow;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) a.S_out[(n * kDV + 32 * half + j) * 512 + f] = v[j];
+  for (int s = 0; s < kSlices; ++s) {
+    float v[16];
+    tc::tmem_ld16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
+    tc::tmem_ld_wait();
+    const int f = 128 * s + trow;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a.S_out[(n * kDV + 16 * cq + j) * kD + f] = v[j];
   }
   tc::cp_async_wait_all();
   if (!ok && lane == 0) record_device_error(&g_tc_error, 2);
   tc::fence_before_sync();
-  tc::cluster_sync();  // no CTA leaves while a peer may still address its shared memory
+  __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
 }
 
 }  // namespace
 
 bool tc_prefill_supported(int D, int dv, int C, const ProjParams& P) {
-  if (D != 512 || dv != kDV || C != kC) return false;
+  if (D != kD || dv != kDV || C != kC) return false;
   // the Omega entries (integers / 8) must be exact in bf16 for the lift product
   for (int m = 0; m < 8; ++m) {
     for (int d = 0; d < 64; ++d) {
@@ -666,7 +662,7 @@ cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cuda
   a.NC = int((p.T + kC - 1) / kC);
   cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
   if (e != cudaSuccess) return e;
-  prefill_tc_kernel<<<dim3(kG, unsigned(p.N)), kThr, kSmemBytes, stream>>>(a, P);
+  prefill_tc_kernel<<<unsigned(p.N), kThr, kSmemBytes, stream>>>(a, P);
   return cudaGetLastError();
 }
 
