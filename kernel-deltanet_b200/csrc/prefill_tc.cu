@@ -1,6 +1,6 @@
 // prefill_tc.cu -- fused tensor-core chunked prefill (KDN_MODE_BF16), sm_100a.
 //
-// One CTA (512 threads) per sequence; the whole fp32 state S^T [D=512 x d_v=64]
+// One CTA per sequence: 16 compute warps plus one warp that issues every tcgen05 MMA; the whole fp32 state S^T [D=512 x d_v=64]
 // lives in tensor memory (4 slices of 128 features = 4 x 64 TMEM columns) for the
 // entire sequence.  Per chunk of C = 64 tokens:
 //
@@ -41,7 +41,10 @@ constexpr int kC = 64;       // chunk
 constexpr int kDV = 64;      // value dim
 constexpr int kD = 512;      // lifted dim
 constexpr int kSlices = 4;   // 128-feature slices
-constexpr int kThr = 512;    // threads per CTA (4 warps per TMEM lane quarter)
+constexpr int kComputeWarps = 16;                 // 4 per TMEM lane quarter
+constexpr int kComputeThreads = 32 * kComputeWarps;
+constexpr int kIssuerWarp = kComputeWarps;        // one extra warp issues all tcgen05 MMAs
+constexpr int kThr = 32 * (kComputeWarps + 1);
 constexpr uint32_t kWaitLimit = 1u << 24;
 
 // TMEM columns
@@ -65,8 +68,8 @@ constexpr uint32_t OFF_PH = 221184;    // 2 KiB  phase b[512]
 constexpr uint32_t OFF_GL = 223232;    // 5 x 256 B: g, beta, exp(g), exp(g_{i-1}), exp(g_{C-1} - g)
 constexpr uint32_t OFF_SSP = 224512;   // 2 KiB  sums of squares per column quarter [4][128]
 constexpr uint32_t OFF_SC = 226560;    // 512 B  token scales s = amp / (amp ||u|| + 1e-8)
-constexpr uint32_t OFF_BAR = 227072;   // 2 mbarriers + TMEM address
-constexpr uint32_t kSmemBytes = 227096 + 1024;  // + alignment slack
+constexpr uint32_t OFF_BAR = 227072;   // 6 mbarriers + TMEM address
+constexpr uint32_t kSmemBytes = 227128 + 1024;  // + alignment slack
 
 struct TcArgs {
   const void* q;
@@ -164,19 +167,22 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
   float* wdec = gl + 256;
   float* ssp = reinterpret_cast<float*>(sm + OFF_SSP);
   float* sc = reinterpret_cast<float*>(sm + OFF_SC);
-  uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 8);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 16);
+  uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + OFF_BAR);       // lift products done
+  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 8);    // other products done
+  uint64_t* bar_xin = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 16);   // chunk inputs in shared memory
+  uint64_t* bar_zfree = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 24); // lift result read by all
+  uint64_t* bar_fready = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 32);// feature / state tiles stored
+  uint64_t* bar_ops = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 40);   // output / update operands stored
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 48);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n = blockIdx.x;
-  const int quarter = warp & 3, cq = warp >> 2;  // TMEM lane quarter, column quarter
-  const int trow = quarter * 32 + lane;          // TMEM lane owned by this thread
+  const int quarter = warp & 3, cq = (warp >> 2) & 3;  // TMEM lane quarter, column quarter
+  const int trow = quarter * 32 + lane;                // TMEM lane owned by this thread
   const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-  const float amp = P.amp;
   const bool bf_in = a.in_dtype == KDN_DTYPE_BF16;
+  const bool decayed = a.decay != nullptr;
   bool ok = true;
-  uint32_t ph_lift = 0, ph_mma = 0;
 
   // ---------------------------------------------------------------- setup
   if (warp == 0) {
@@ -186,6 +192,10 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
   if (tid == 0) {
     tc::mbar_init(bar_lift, 1);
     tc::mbar_init(bar_mma, 1);
+    tc::mbar_init(bar_xin, kComputeWarps);
+    tc::mbar_init(bar_zfree, kComputeWarps);
+    tc::mbar_init(bar_fready, kComputeWarps);
+    tc::mbar_init(bar_ops, kComputeWarps);
     tc::fence_mbar_init();
   }
   // Omega: feature f = 64 blk + i, input index d; one butterfly per (blk, d)
@@ -200,341 +210,381 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
     *reinterpret_cast<__nv_bfloat16*>(om + tc::sw128_offset(fl + 1, d)) = __float2bfloat16_rn(u1);
   }
   for (int i = tid; i < kD; i += kThr) ph[i] = P.phase[i];
-  if (bf_in) {
+  if (warp < kComputeWarps && bf_in) {
     prefetch_kq(a, n, 0, sbase + OFF_XIN, tid);
     prefetch_v(a, n, 0, sbase + OFF_VB, tid);
   }
   tc::cp_async_commit();
-  float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};  // gates of the coming chunk (warp 0)
-  if (warp == 0) {
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int64_t tt = 2 * lane + e;
-      if (tt < a.T) {
-        nb[e] = ld_as_f32(a.beta, a.gate_dtype, n * a.T + tt);
-        if (a.decay) nd[e] = ld_as_f32(a.decay, a.gate_dtype, n * a.T + tt);
-      }
-    }
-  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tslot;
-  // state master S^T (fp32) from the initial state
+  if (warp < kComputeWarps) {  // state master S^T (fp32) from the initial state
 #pragma unroll
-  for (int s = 0; s < kSlices; ++s) {
-    float v[16];
-    const int f = 128 * s + trow;
+    for (int s = 0; s < kSlices; ++s) {
+      float v[16];
+      const int f = 128 * s + trow;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = a.S0 ? a.S0[(n * kDV + 16 * cq + j) * kD + f] : 0.f;
-    tc::tmem_st16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
+      for (int j = 0; j < 16; ++j) v[j] = a.S0 ? a.S0[(n * kDV + 16 * cq + j) * kD + f] : 0.f;
+      tc::tmem_st16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
+    }
+    tc::tmem_st_wait();
   }
-  tc::tmem_st_wait();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
-  const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
-  const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
-  const uint32_t id_xy = tc::idesc_f16_f32(128, 64, false, true);
-  const uint32_t id_ds = tc::idesc_f16_f32(128, 64, true, true);
-
-  for (int c = 0; c < a.NC; ++c) {
-    const int64_t t0 = int64_t(c) * kC;
-    const bool has_next = c + 1 < a.NC;
-    // ------------------------------------------------ inputs and gates
-    tc::cp_async_wait_all();
-    if (!bf_in) load_kq_f32(a, n, c, sm + OFF_XIN, tid);
-    if (warp == 0) {  // beta, inclusive scan of log clamp(decay, 1e-5, 1), derived factors
-      const float lg0 = logf(fminf(fmaxf(nd[0], 1e-5f), 1.0f)), lg1 = logf(fminf(fmaxf(nd[1], 1e-5f), 1.0f));
-      float s = lg0 + lg1;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, s, o);
-        if (lane >= o) s += y;
-      }
-      const float g0 = s - lg1, g1 = s;
-      const float gend = __shfl_sync(0xffffffffu, s, 31);
-      const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
-      gl[2 * lane] = g0;
-      gl[2 * lane + 1] = g1;
-      bt[2 * lane] = nb[0];
-      bt[2 * lane + 1] = nb[1];
-      eg[2 * lane] = __expf(g0);
-      eg[2 * lane + 1] = __expf(g1);
-      egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
-      egp[2 * lane + 1] = __expf(g0);
-      wdec[2 * lane] = __expf(gend - g0);
-      wdec[2 * lane + 1] = __expf(gend - g1);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int64_t tt = t0 + kC + 2 * lane + e;
-        nb[e] = 0.f;
-        nd[e] = 1.f;
-        if (has_next && tt < a.T) {
-          nb[e] = ld_as_f32(a.beta, a.gate_dtype, n * a.T + tt);
-          if (a.decay) nd[e] = ld_as_f32(a.decay, a.gate_dtype, n * a.T + tt);
-        }
-      }
-    }
-    tc::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-
-    // ------------------------------------------------ slice loop
-    if (tid == 0) {  // lift of slice 0
-#pragma unroll
-      for (int k0 = 0; k0 < 64; k0 += 16)
-        tc::mma_ss(tmem + COL_Z, tc::smem_desc_sw128(sbase + OFF_XIN + 2 * k0, 16, 1024),
-                   tc::smem_desc_sw128(sbase + OFF_OMG + 2 * k0, 16, 1024), id_lift, k0 > 0);
-      tc::mma_commit(bar_lift);
-    }
-    float ss = 0.f;
-#pragma unroll 1
-    for (int s = 0; s < kSlices; ++s) {
-      __syncwarp();
-      ok &= tc::mbar_wait_bounded(bar_lift, ph_lift, kWaitLimit);
-      ph_lift ^= 1;
-      tc::fence_after_sync();
-      float z[32];
-      tc::tmem_ld32(tmem + lane_off + COL_Z + 32 * cq, z);
-      tc::tmem_ld_wait();
-      tc::fence_before_sync();
-      __syncthreads();  // Z has been read by everyone
-      if (tid == 0 && s + 1 < kSlices) {  // lift of the next slice runs under the cosines
-        tc::fence_after_sync();
+  if (warp == kIssuerWarp) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
+      const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
+      const uint32_t id_xy = tc::idesc_f16_f32(128, 64, false, true);
+      const uint32_t id_ds = tc::idesc_f16_f32(128, 64, true, true);
+      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0;
+      auto lift = [&](int s) {
 #pragma unroll
         for (int k0 = 0; k0 < 64; k0 += 16)
           tc::mma_ss(tmem + COL_Z, tc::smem_desc_sw128(sbase + OFF_XIN + 2 * k0, 16, 1024),
-                     tc::smem_desc_sw128(sbase + OFF_OMG + (s + 1) * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
+                     tc::smem_desc_sw128(sbase + OFF_OMG + s * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
         tc::mma_commit(bar_lift);
-      }
-      // u = cos(tau_inv z + b): the hardware cosine is accurate to ~1e-6 absolute for
-      // the |arguments| <= 32 met here, far below the fp16 spacing of the stored result
-      uint32_t fp[16];
-      const float4* phs = reinterpret_cast<const float4*>(ph + 128 * s + 32 * cq);
+      };
+      for (int c = 0; c < a.NC; ++c) {
+        ok &= tc::mbar_wait_bounded(bar_xin, p_xin, kWaitLimit);
+        p_xin ^= 1;
+        tc::fence_after_sync();
+        lift(0);
+        for (int s = 0; s < kSlices; ++s) {
+          ok &= tc::mbar_wait_bounded(bar_zfree, p_zfree, kWaitLimit);
+          p_zfree ^= 1;
+          tc::fence_after_sync();
+          if (s + 1 < kSlices) lift(s + 1);  // runs under the cosines of slice s
+          ok &= tc::mbar_wait_bounded(bar_fready, p_fready, kWaitLimit);
+          p_fready ^= 1;
+          tc::fence_after_sync();
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 b4 = phs[j >> 2];
-        const float u0 = __cosf(fmaf(z[j], P.tau_inv, b4.x));
-        const float u1 = __cosf(fmaf(z[j + 1], P.tau_inv, b4.y));
-        const float u2 = __cosf(fmaf(z[j + 2], P.tau_inv, b4.z));
-        const float u3 = __cosf(fmaf(z[j + 3], P.tau_inv, b4.w));
-        ss = fmaf(u0, u0, fmaf(u1, u1, fmaf(u2, u2, fmaf(u3, u3, ss))));
-        fp[j >> 1] = pack_f16(u0, u1);
-        fp[(j >> 1) + 1] = pack_f16(u2, u3);
-      }
-      uint32_t sp[8];
-      {
-        float v[16];
-        tc::tmem_ld16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sp[j] = pack_f16_sat(v[2 * j], v[2 * j + 1]);
-      }
-      if (s > 0) {  // the previous slice's products must be done with F and SB
-        __syncwarp();
-        ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
-        ph_mma ^= 1;
-      }
-      {
-        const int kb = cq >> 1, e0 = 32 * (cq & 1);
-        uint8_t* fb = sm + OFF_F + kb * 16384;
-#pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
-          const uint32_t off = tc::sw128_offset(trow, e0 + 8 * c8);
-          *reinterpret_cast<uint4*>(fb + off) = pk;
-          if (trow < 64) *reinterpret_cast<uint4*>(sm + OFF_UK + s * 16384 + kb * 8192 + off) = pk;
+          for (int k0 = 0; k0 < 128; k0 += 16) {
+            const uint64_t fd = tc::smem_desc_sw128(sbase + OFF_F + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
+            const uint64_t sd = tc::smem_desc_sw128(sbase + OFF_SB + 128 * k0, 16384, 1024);
+            tc::mma_ss(tmem + COL_GP, fd, fd, id_gp, s > 0 || k0 > 0);
+            tc::mma_ss(tmem + COL_XY, fd, sd, id_xy, s > 0 || k0 > 0);
+          }
+          tc::mma_commit(bar_mma);
         }
-#pragma unroll
-        for (int c8 = 0; c8 < 2; ++c8)
-          *reinterpret_cast<uint4*>(sm + OFF_SB + tc::sw128_offset(trow, 16 * cq + 8 * c8)) =
-              make_uint4(sp[4 * c8], sp[4 * c8 + 1], sp[4 * c8 + 2], sp[4 * c8 + 3]);
-      }
-      tc::fence_proxy_async_smem();
-      tc::fence_before_sync();
-      __syncthreads();
-      if (tid == 0) {
+        ok &= tc::mbar_wait_bounded(bar_ops, p_ops, kWaitLimit);
+        p_ops ^= 1;
         tc::fence_after_sync();
 #pragma unroll
-        for (int k0 = 0; k0 < 128; k0 += 16) {
-          const uint64_t fd = tc::smem_desc_sw128(sbase + OFF_F + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
-          const uint64_t sd = tc::smem_desc_sw128(sbase + OFF_SB + 128 * k0, 16384, 1024);
-          tc::mma_ss(tmem + COL_GP, fd, fd, id_gp, s > 0 || k0 > 0);
-          tc::mma_ss(tmem + COL_XY, fd, sd, id_xy, s > 0 || k0 > 0);
-        }
+        for (int k0 = 0; k0 < 64; k0 += 16)  // [0; Aq] E -> lanes of the q rows
+          tc::mma_ss(tmem + COL_GP, tc::smem_desc_sw128(sbase + OFF_F + 2 * k0, 16, 1024),
+                     tc::smem_desc_sw128(sbase + OFF_TD + 128 * k0, 8192, 1024), id_xy, k0 > 0);
+#pragma unroll
+        for (int s = 0; s < kSlices; ++s)  // S_s^T += U_k,s^T E''
+#pragma unroll
+          for (int k0 = 0; k0 < 64; k0 += 16)
+            tc::mma_ss(tmem + COL_S + 64 * s,
+                       tc::smem_desc_sw128(sbase + OFF_UK + s * 16384 + 128 * k0, 8192, 1024),
+                       tc::smem_desc_sw128(sbase + OFF_EB + 128 * k0, 8192, 1024), id_ds, true);
         tc::mma_commit(bar_mma);
       }
     }
-    ssp[cq * 128 + trow] = ss;
-    // the input tile is free: prefetch the next chunk's k,q rows into it
-    if (has_next && bf_in) prefetch_kq(a, n, c + 1, sbase + OFF_XIN, tid);
-    tc::cp_async_commit();
     __syncwarp();
-    ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
-    ph_mma ^= 1;
-    tc::fence_after_sync();
-
-    // ------------------------------------------------ chunk matrices
-    float gp[16], xy[16], vv[16];
-    tc::tmem_ld16(tmem + lane_off + COL_GP + 16 * cq, gp);
-    tc::tmem_ld16(tmem + lane_off + COL_XY + 16 * cq, xy);
-    tc::tmem_ld_wait();
-    if (trow < 64) {
-      const int64_t t = t0 + trow;
-      if (bf_in) {
-        const __nv_bfloat16* vr = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_VB) + trow * 64 + 16 * cq;
+  } else {
+    // ============================================================ compute warps
+    uint32_t ph_lift = 0, ph_mma = 0;
+    float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};  // gates of the coming chunk (warp 0)
+    if (warp == 0) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) vv[j] = __bfloat162float(vr[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          vv[j] = t < a.T ? reinterpret_cast<const float*>(a.v)[(n * a.T + t) * kDV + 16 * cq + j] : 0.f;
+      for (int e = 0; e < 2; ++e) {
+        const int64_t tt = 2 * lane + e;
+        if (tt < a.T) {
+          nb[e] = ld_as_f32(a.beta, a.gate_dtype, n * a.T + tt);
+          if (decayed) nd[e] = ld_as_f32(a.decay, a.gate_dtype, n * a.T + tt);
+        }
       }
     }
-    __syncthreads();  // sums of squares visible; v tile consumed
-    if (has_next && bf_in) prefetch_v(a, n, c + 1, sbase + OFF_VB, tid);
-    tc::cp_async_commit();
-    if (tid < 128)
-      sc[tid] = amp / (amp * sqrtf(ssp[tid] + ssp[128 + tid] + ssp[256 + tid] + ssp[384 + tid]) + 1e-8f);
-    __syncthreads();
-    float aq[16], yq[16];  // q-row threads: their row of Aq and of the scaled Yq
-    {
-      const int i = trow & 63;
-      const float si = sc[trow];
-      const float bi = bt[i];
-      if (trow < 64) {  // k row: A (from G) and R (from X)
-        const float gi = gl[i], egi = eg[i];
+    for (int c = 0; c < a.NC; ++c) {
+      const int64_t t0 = int64_t(c) * kC;
+      const bool has_next = c + 1 < a.NC;
+      // -------------------------------------------- chunk inputs ready -> lift of slice 0
+      tc::cp_async_wait_all();
+      if (!bf_in) load_kq_f32(a, n, c, sm + OFF_XIN, tid);
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_xin);
+      tc::named_bar_sync(1, kComputeThreads);  // v rows copied by other threads are visible
+      if (warp == 0) {  // gates: beta, inclusive scan of log clamp(decay, 1e-5, 1), derived factors
+        const float lg0 = decayed ? logf(fminf(fmaxf(nd[0], 1e-5f), 1.0f)) : 0.f;
+        const float lg1 = decayed ? logf(fminf(fmaxf(nd[1], 1e-5f), 1.0f)) : 0.f;
+        float s = lg0 + lg1;
 #pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          float4 av, rv;
-          float* ap = &av.x;
-          float* rp = &rv.x;
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, s, o);
+          if (lane >= o) s += y;
+        }
+        const float g0 = s - lg1, g1 = s;
+        const float gend = __shfl_sync(0xffffffffu, s, 31);
+        const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
+        gl[2 * lane] = g0;
+        gl[2 * lane + 1] = g1;
+        bt[2 * lane] = nb[0];
+        bt[2 * lane + 1] = nb[1];
+        eg[2 * lane] = __expf(g0);
+        eg[2 * lane + 1] = __expf(g1);
+        egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
+        egp[2 * lane + 1] = __expf(g0);
+        wdec[2 * lane] = __expf(gend - g0);
+        wdec[2 * lane + 1] = __expf(gend - g1);
 #pragma unroll
-          for (int qx = 0; qx < 4; ++qx) {
-            const int jj = 4 * j4 + qx, j = 16 * cq + jj;
-            ap[qx] = (j < i) ? bi * __expf(gi - gl[j]) * gp[jj] * si * sc[j] : 0.f;
-            rp[qx] = bi * (vv[jj] - egi * xy[jj] * si);
+        for (int e = 0; e < 2; ++e) {
+          const int64_t tt = t0 + kC + 2 * lane + e;
+          nb[e] = 0.f;
+          nd[e] = 1.f;
+          if (has_next && tt < a.T) {
+            nb[e] = ld_as_f32(a.beta, a.gate_dtype, n * a.T + tt);
+            if (decayed) nd[e] = ld_as_f32(a.decay, a.gate_dtype, n * a.T + tt);
           }
-          *reinterpret_cast<float4*>(Am + sx(i, 16 * cq + 4 * j4)) = av;
-          *reinterpret_cast<float4*>(Rm + sx(i, 16 * cq + 4 * j4)) = rv;
-        }
-      } else {  // q row
-        const float gp_i = i > 0 ? gl[i - 1] : 0.f, yscale = si * egp[i];
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = 16 * cq + jj;
-          aq[jj] = (j < i) ? __expf(gp_i - gl[j]) * gp[jj] * si * sc[j] : 0.f;
-          yq[jj] = xy[jj] * yscale;
         }
       }
-    }
-    __syncthreads();
-    // diagonal 16x16 blocks of (I + A)^-1: one warp per block, one lane per column
-    if (warp < 4 && lane < 16) {
-      const int I = warp, j = lane;
-      float tcol[16];
+
+      // -------------------------------------------- slice loop
+      float ss = 0.f;
+#pragma unroll 1
+      for (int s = 0; s < kSlices; ++s) {
+        ok &= tc::mbar_wait_bounded(bar_lift, ph_lift, kWaitLimit);
+        ph_lift ^= 1;
+        tc::fence_after_sync();
+        float z[32];
+        tc::tmem_ld32(tmem + lane_off + COL_Z + 32 * cq, z);
+        tc::tmem_ld_wait();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_zfree);
+        // u = cos(tau_inv z + b): the hardware cosine is accurate to ~1e-6 absolute for
+        // the |arguments| <= 32 met here, far below the fp16 spacing of the stored result
+        uint32_t fp[16];
+        const float4* phs = reinterpret_cast<const float4*>(ph + 128 * s + 32 * cq);
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        float s = (r == j) ? 1.f : 0.f;
-#pragma unroll
-        for (int kk = 0; kk < r; ++kk) s = fmaf(-Am[sx(16 * I + r, 16 * I + kk)], tcol[kk], s);
-        tcol[r] = (r >= j) ? s : 0.f;
-      }
-#pragma unroll
-      for (int r = 0; r < 16; ++r) TD[(I * 16 + r) * 16 + j] = tcol[r];
-    }
-    __syncthreads();
-    // E = (I + A)^-1 R, block row by block row: U = R_I - sum_{J<I} A_IJ E_J ; E_I = T_II U.
-    // E and U are row-major (each warp reads/writes whole rows: conflict-free); A rows are
-    // read as swizzled float4 slots.
-    {
-      const int r = tid >> 5, c2 = (tid & 31) * 2;
-#pragma unroll
-      for (int I = 0; I < 4; ++I) {
-        const int row = 16 * I + r;
-        float2 acc = *reinterpret_cast<const float2*>(Rm + sx(row, c2));
-        float2 acc2 = make_float2(0.f, 0.f);
-        const float* arow = Am + row * 64;
-#pragma unroll
-        for (int qs = 0; qs < 4 * I; ++qs) {
-          const float4 a4 = *reinterpret_cast<const float4*>(arow + (((qs ^ row) & 15) << 2));
-          const float2 e0 = *reinterpret_cast<const float2*>(Es + (4 * qs + 0) * 64 + c2);
-          const float2 e1 = *reinterpret_cast<const float2*>(Es + (4 * qs + 1) * 64 + c2);
-          const float2 e2 = *reinterpret_cast<const float2*>(Es + (4 * qs + 2) * 64 + c2);
-          const float2 e3 = *reinterpret_cast<const float2*>(Es + (4 * qs + 3) * 64 + c2);
-          acc.x = fmaf(-a4.x, e0.x, acc.x);
-          acc.y = fmaf(-a4.x, e0.y, acc.y);
-          acc2.x = fmaf(-a4.y, e1.x, acc2.x);
-          acc2.y = fmaf(-a4.y, e1.y, acc2.y);
-          acc.x = fmaf(-a4.z, e2.x, acc.x);
-          acc.y = fmaf(-a4.z, e2.y, acc.y);
-          acc2.x = fmaf(-a4.w, e3.x, acc2.x);
-          acc2.y = fmaf(-a4.w, e3.y, acc2.y);
+        for (int j = 0; j < 32; j += 4) {
+          const float4 b4 = phs[j >> 2];
+          const float u0 = __cosf(fmaf(z[j], P.tau_inv, b4.x));
+          const float u1 = __cosf(fmaf(z[j + 1], P.tau_inv, b4.y));
+          const float u2 = __cosf(fmaf(z[j + 2], P.tau_inv, b4.z));
+          const float u3 = __cosf(fmaf(z[j + 3], P.tau_inv, b4.w));
+          ss = fmaf(u0, u0, fmaf(u1, u1, fmaf(u2, u2, fmaf(u3, u3, ss))));
+          fp[j >> 1] = pack_f16(u0, u1);
+          fp[(j >> 1) + 1] = pack_f16(u2, u3);
         }
-        acc.x += acc2.x;
-        acc.y += acc2.y;
-        *reinterpret_cast<float2*>(US + r * 64 + c2) = acc;
-        __syncthreads();
-        float2 e = make_float2(0.f, 0.f), e2 = make_float2(0.f, 0.f);
-        const float4* trw = reinterpret_cast<const float4*>(TD + (I * 16 + r) * 16);
+        uint32_t sp[8];
+        {
+          float v[16];
+          tc::tmem_ld16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
+          tc::tmem_ld_wait();
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {  // T_II is lower triangular (zeros above)
-          const float4 t4 = trw[q4];
-          const float2 u0 = *reinterpret_cast<const float2*>(US + (4 * q4 + 0) * 64 + c2);
-          const float2 u1 = *reinterpret_cast<const float2*>(US + (4 * q4 + 1) * 64 + c2);
-          const float2 u2 = *reinterpret_cast<const float2*>(US + (4 * q4 + 2) * 64 + c2);
-          const float2 u3 = *reinterpret_cast<const float2*>(US + (4 * q4 + 3) * 64 + c2);
-          e.x = fmaf(t4.x, u0.x, e.x);
-          e.y = fmaf(t4.x, u0.y, e.y);
-          e2.x = fmaf(t4.y, u1.x, e2.x);
-          e2.y = fmaf(t4.y, u1.y, e2.y);
-          e.x = fmaf(t4.z, u2.x, e.x);
-          e.y = fmaf(t4.z, u2.y, e.y);
-          e2.x = fmaf(t4.w, u3.x, e2.x);
-          e2.y = fmaf(t4.w, u3.y, e2.y);
+          for (int j = 0; j < 8; ++j) sp[j] = pack_f16_sat(v[2 * j], v[2 * j + 1]);
         }
-        e.x += e2.x;
-        e.y += e2.y;
-        *reinterpret_cast<float2*>(Es + row * 64 + c2) = e;
-        __syncthreads();
+        if (s > 0) {  // the previous slice's products must be done with F and SB
+          ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
+          ph_mma ^= 1;
+        }
+        {
+          const int kb = cq >> 1, e0 = 32 * (cq & 1);
+          uint8_t* fb = sm + OFF_F + kb * 16384;
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
+            const uint32_t off = tc::sw128_offset(trow, e0 + 8 * c8);
+            *reinterpret_cast<uint4*>(fb + off) = pk;
+            if (trow < 64) *reinterpret_cast<uint4*>(sm + OFF_UK + s * 16384 + kb * 8192 + off) = pk;
+          }
+#pragma unroll
+          for (int c8 = 0; c8 < 2; ++c8)
+            *reinterpret_cast<uint4*>(sm + OFF_SB + tc::sw128_offset(trow, 16 * cq + 8 * c8)) =
+                make_uint4(sp[4 * c8], sp[4 * c8 + 1], sp[4 * c8 + 2], sp[4 * c8 + 3]);
+        }
+        tc::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_fready);
       }
-    }
-    // operands of the output and state products
-    {
-      const int j = tid >> 3, c8 = (tid & 7) * 8;  // one 8-wide piece of row j of E per thread
-      const float4 e0 = *reinterpret_cast<const float4*>(Es + j * 64 + c8);
-      const float4 e1 = *reinterpret_cast<const float4*>(Es + j * 64 + c8 + 4);
-      const uint32_t off = tc::sw128_offset(j, c8);
-      *reinterpret_cast<uint4*>(sm + OFF_TD + off) =  // E (fp16, MN-major) over TD+US
-          make_uint4(pack_f16_sat(e0.x, e0.y), pack_f16_sat(e0.z, e0.w), pack_f16_sat(e1.x, e1.y),
-                     pack_f16_sat(e1.z, e1.w));
-      const float w = wdec[j] * sc[j];
-      *reinterpret_cast<uint4*>(sm + OFF_EB + off) =  // E'' = exp(g_{C-1} - g_j) s_kj e_j
-          make_uint4(pack_f16_sat(w * e0.x, w * e0.y), pack_f16_sat(w * e0.z, w * e0.w),
-                     pack_f16_sat(w * e1.x, w * e1.y), pack_f16_sat(w * e1.z, w * e1.w));
-      // A operand [0; Aq] (fp16, K-major, 128 rows x 64) in the (now free) feature tile
+      ssp[cq * 128 + trow] = ss;
+      // all lifts have completed: the input tile is free for the next chunk's k,q rows
+      if (has_next && bf_in) prefetch_kq(a, n, c + 1, sbase + OFF_XIN, tid);
+      tc::cp_async_commit();
+      ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
+      ph_mma ^= 1;
+      tc::fence_after_sync();
+
+      // -------------------------------------------- chunk matrices
+      float gp[16], xy[16], vv[16];
+      tc::tmem_ld16(tmem + lane_off + COL_GP + 16 * cq, gp);
+      tc::tmem_ld16(tmem + lane_off + COL_XY + 16 * cq, xy);
+      tc::tmem_ld_wait();
       if (trow < 64) {
-        if (cq < 2)
-          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq) + 0) = make_uint4(0, 0, 0, 0),
-          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq + 8)) = make_uint4(0, 0, 0, 0),
-          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq + 16)) = make_uint4(0, 0, 0, 0),
-          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq + 24)) = make_uint4(0, 0, 0, 0);
-      } else {
+        const int64_t t = t0 + trow;
+        if (bf_in) {
+          const uint4* vr = reinterpret_cast<const uint4*>(sm + OFF_VB + trow * 128 + 32 * cq);
+          const uint4 w0 = vr[0], w1 = vr[1];
+          const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&w0);
+          const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&w1);
 #pragma unroll
-        for (int c8b = 0; c8b < 2; ++c8b)
-          *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 16 * cq + 8 * c8b)) =
-              make_uint4(pack_f16_sat(aq[8 * c8b], aq[8 * c8b + 1]), pack_f16_sat(aq[8 * c8b + 2], aq[8 * c8b + 3]),
-                         pack_f16_sat(aq[8 * c8b + 4], aq[8 * c8b + 5]),
-                         pack_f16_sat(aq[8 * c8b + 6], aq[8 * c8b + 7]));
+          for (int j = 0; j < 4; ++j) {
+            const float2 f0 = __bfloat1622float2(h0[j]), f1 = __bfloat1622float2(h1[j]);
+            vv[2 * j] = f0.x;
+            vv[2 * j + 1] = f0.y;
+            vv[8 + 2 * j] = f1.x;
+            vv[8 + 2 * j + 1] = f1.y;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            vv[j] = t < a.T ? reinterpret_cast<const float*>(a.v)[(n * a.T + t) * kDV + 16 * cq + j] : 0.f;
+        }
       }
-    }
-    // decay of the carried state
-    {
-      const float gC = eg[63];
-      if (gC != 1.0f) {
+      tc::named_bar_sync(1, kComputeThreads);  // sums of squares and gates visible; v tile consumed
+      if (has_next && bf_in) prefetch_v(a, n, c + 1, sbase + OFF_VB, tid);
+      tc::cp_async_commit();
+      if (tid < 128)
+        sc[tid] = P.amp / (P.amp * sqrtf(ssp[tid] + ssp[128 + tid] + ssp[256 + tid] + ssp[384 + tid]) + 1e-8f);
+      tc::named_bar_sync(1, kComputeThreads);
+      {  // q-row threads park their row of Aq and of the scaled Yq in the (free) lift columns
+        const int i = trow & 63;
+        const float si = sc[trow];
+        const float bi = bt[i];
+        if (trow < 64) {  // k row: A (from G) and R (from X)
+          const float gi = gl[i], egi = eg[i];
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4) {
+            const float4 sj = *reinterpret_cast<const float4*>(sc + 16 * cq + 4 * j4);
+            const float sjv[4] = {sj.x, sj.y, sj.z, sj.w};
+            float4 av, rv;
+            float* ap = &av.x;
+            float* rp = &rv.x;
+#pragma unroll
+            for (int qx = 0; qx < 4; ++qx) {
+              const int jj = 4 * j4 + qx, j = 16 * cq + jj;
+              const float dec = decayed ? __expf(gi - gl[j]) : 1.f;
+              ap[qx] = (j < i) ? bi * dec * gp[jj] * si * sjv[qx] : 0.f;
+              rp[qx] = bi * (vv[jj] - egi * xy[jj] * si);
+            }
+            *reinterpret_cast<float4*>(Am + sx(i, 16 * cq + 4 * j4)) = av;
+            *reinterpret_cast<float4*>(Rm + sx(i, 16 * cq + 4 * j4)) = rv;
+          }
+        } else {  // q row
+          const float gp_i = i > 0 ? gl[i - 1] : 0.f, yscale = si * egp[i];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = 16 * cq + jj;
+            const float dec = decayed ? __expf(gp_i - gl[j]) : 1.f;
+            gp[jj] = (j < i) ? dec * gp[jj] * si * sc[j] : 0.f;
+            xy[jj] *= yscale;
+          }
+        }
+      }
+      if (trow >= 64) {
+        tc::tmem_st16(tmem + lane_off + COL_Z + 16 * cq, gp);
+        tc::tmem_st16(tmem + lane_off + COL_Z + 64 + 16 * cq, xy);
+        tc::tmem_st_wait();
+      }
+      tc::named_bar_sync(1, kComputeThreads);
+      // diagonal 16x16 blocks of (I + A)^-1: one warp per block, one lane per column
+      if (warp < 4 && lane < 16) {
+        const int I = warp, j = lane;
+        float tcol[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          float sacc = (r == j) ? 1.f : 0.f;
+#pragma unroll
+          for (int kk = 0; kk < r; ++kk) sacc = fmaf(-Am[sx(16 * I + r, 16 * I + kk)], tcol[kk], sacc);
+          tcol[r] = (r >= j) ? sacc : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < 16; ++r) TD[(I * 16 + r) * 16 + j] = tcol[r];
+      }
+      tc::named_bar_sync(1, kComputeThreads);
+      // E = (I + A)^-1 R by block rows (U = R_I - sum_{J<I} A_IJ E_J ; E_I = T_II U), on warps
+      // 0-3: warp w owns rows 4w..4w+3 of the block, lane l columns 2l, 2l+1 (E, U row-major)
+      if (warp < 4) {
+        const int c2 = 2 * lane;
+#pragma unroll
+        for (int I = 0; I < 4; ++I) {
+          float2 acc[4];
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr) acc[rr] = *reinterpret_cast<const float2*>(Rm + sx(16 * I + 4 * warp + rr, c2));
+#pragma unroll
+          for (int qs = 0; qs < 4 * I; ++qs) {
+            float2 e[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) e[u] = *reinterpret_cast<const float2*>(Es + (4 * qs + u) * 64 + c2);
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr) {
+              const int row = 16 * I + 4 * warp + rr;
+              const float4 a4 = *reinterpret_cast<const float4*>(Am + row * 64 + (((qs ^ row) & 15) << 2));
+              acc[rr].x = fmaf(-a4.x, e[0].x, acc[rr].x);
+              acc[rr].y = fmaf(-a4.x, e[0].y, acc[rr].y);
+              acc[rr].x = fmaf(-a4.y, e[1].x, acc[rr].x);
+              acc[rr].y = fmaf(-a4.y, e[1].y, acc[rr].y);
+              acc[rr].x = fmaf(-a4.z, e[2].x, acc[rr].x);
+              acc[rr].y = fmaf(-a4.z, e[2].y, acc[rr].y);
+              acc[rr].x = fmaf(-a4.w, e[3].x, acc[rr].x);
+              acc[rr].y = fmaf(-a4.w, e[3].y, acc[rr].y);
+            }
+          }
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr) *reinterpret_cast<float2*>(US + (4 * warp + rr) * 64 + c2) = acc[rr];
+          tc::named_bar_sync(2, 128);
+          float2 ev[4];
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr) ev[rr] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int kk = 0; kk < 16; ++kk) {  // T_II is lower triangular (zeros above)
+            const float2 u = *reinterpret_cast<const float2*>(US + kk * 64 + c2);
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr) {
+              const float tv = TD[(I * 16 + 4 * warp + rr) * 16 + kk];
+              ev[rr].x = fmaf(tv, u.x, ev[rr].x);
+              ev[rr].y = fmaf(tv, u.y, ev[rr].y);
+            }
+          }
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr) *reinterpret_cast<float2*>(Es + (16 * I + 4 * warp + rr) * 64 + c2) = ev[rr];
+          tc::named_bar_sync(2, 128);
+        }
+      }
+      tc::named_bar_sync(1, kComputeThreads);
+      // operands of the output and state products
+      {
+        const int j = tid >> 3, c8 = (tid & 7) * 8;  // one 8-wide piece of row j of E per thread
+        const float4 e0 = *reinterpret_cast<const float4*>(Es + j * 64 + c8);
+        const float4 e1 = *reinterpret_cast<const float4*>(Es + j * 64 + c8 + 4);
+        const uint32_t off = tc::sw128_offset(j, c8);
+        *reinterpret_cast<uint4*>(sm + OFF_TD + off) =  // E (fp16, MN-major) over TD+US
+            make_uint4(pack_f16_sat(e0.x, e0.y), pack_f16_sat(e0.z, e0.w), pack_f16_sat(e1.x, e1.y),
+                       pack_f16_sat(e1.z, e1.w));
+        const float w = wdec[j] * sc[j];
+        *reinterpret_cast<uint4*>(sm + OFF_EB + off) =  // E'' = exp(g_{C-1} - g_j) s_kj e_j
+            make_uint4(pack_f16_sat(w * e0.x, w * e0.y), pack_f16_sat(w * e0.z, w * e0.w),
+                       pack_f16_sat(w * e1.x, w * e1.y), pack_f16_sat(w * e1.z, w * e1.w));
+        // A operand [0; Aq] (fp16, K-major, 128 rows x 64) in the (now free) feature tile
+        if (trow < 64) {
+          if (cq < 2) {
+#pragma unroll
+            for (int z8 = 0; z8 < 4; ++z8)
+              *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 32 * cq + 8 * z8)) = make_uint4(0, 0, 0, 0);
+          }
+        } else {
+          float aq[16];
+          tc::tmem_ld16(tmem + lane_off + COL_Z + 16 * cq, aq);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int c8b = 0; c8b < 2; ++c8b)
+            *reinterpret_cast<uint4*>(sm + OFF_F + tc::sw128_offset(trow, 16 * cq + 8 * c8b)) = make_uint4(
+                pack_f16_sat(aq[8 * c8b], aq[8 * c8b + 1]), pack_f16_sat(aq[8 * c8b + 2], aq[8 * c8b + 3]),
+                pack_f16_sat(aq[8 * c8b + 4], aq[8 * c8b + 5]), pack_f16_sat(aq[8 * c8b + 6], aq[8 * c8b + 7]));
+        }
+      }
+      if (decayed) {  // decay of the carried state
+        const float gC = eg[63];
 #pragma unroll
         for (int s = 0; s < kSlices; ++s) {
           float v[16];
@@ -546,70 +596,54 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
         }
         tc::tmem_st_wait();
       }
-    }
-    tc::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-
-    // ------------------------------------------------ output product and state update
-    if (tid == 0) {
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      tc::named_bar_sync(1, kComputeThreads);  // also: gates of this chunk no longer read
+      if (lane == 0) tc::mbar_arrive(bar_ops);
+      ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
+      ph_mma ^= 1;
       tc::fence_after_sync();
+      // outputs: y_i = exp(g_{i-1}) s_qi Yq_i + (Aq E)_i, by the threads of the q rows
+      if (trow >= 64) {
+        float ye[16], yq[16];
+        tc::tmem_ld16(tmem + lane_off + COL_GP + 16 * cq, ye);
+        tc::tmem_ld16(tmem + lane_off + COL_Z + 64 + 16 * cq, yq);
+        tc::tmem_ld_wait();
+        const int i = trow - 64;
+        const int64_t t = t0 + i;
+        if (t < a.T) {
+          const int64_t o = (n * a.T + t) * kDV + 16 * cq;
+          float yy[16];
 #pragma unroll
-      for (int k0 = 0; k0 < 64; k0 += 16)  // [junk; Aq E] -> lanes of the q rows
-        tc::mma_ss(tmem + COL_GP, tc::smem_desc_sw128(sbase + OFF_F + 2 * k0, 16, 1024),
-                   tc::smem_desc_sw128(sbase + OFF_TD + 128 * k0, 8192, 1024), id_xy, k0 > 0);
+          for (int j = 0; j < 16; ++j) yy[j] = yq[j] + ye[j];
+          if (a.y_dtype == KDN_DTYPE_BF16) {
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + o);
+            dst[0] = make_uint4(pack_bf16(yy[0], yy[1]), pack_bf16(yy[2], yy[3]), pack_bf16(yy[4], yy[5]),
+                                pack_bf16(yy[6], yy[7]));
+            dst[1] = make_uint4(pack_bf16(yy[8], yy[9]), pack_bf16(yy[10], yy[11]), pack_bf16(yy[12], yy[13]),
+                                pack_bf16(yy[14], yy[15]));
+          } else {
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o);
 #pragma unroll
-      for (int s = 0; s < kSlices; ++s)  // S_s^T += U_k,s^T E''
-#pragma unroll
-        for (int k0 = 0; k0 < 64; k0 += 16)
-          tc::mma_ss(tmem + COL_S + 64 * s, tc::smem_desc_sw128(sbase + OFF_UK + s * 16384 + 128 * k0, 8192, 1024),
-                     tc::smem_desc_sw128(sbase + OFF_EB + 128 * k0, 8192, 1024), id_ds, true);
-      tc::mma_commit(bar_mma);
-    }
-    __syncwarp();
-    ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
-    ph_mma ^= 1;
-    tc::fence_after_sync();
-    // outputs: y_i = exp(g_{i-1}) s_qi Yq_i + (Aq E)_i, by the threads of the q rows
-    if (trow >= 64) {
-      float ye[16];
-      tc::tmem_ld16(tmem + lane_off + COL_GP + 16 * cq, ye);
-      tc::tmem_ld_wait();
-      const int i = trow - 64;
-      const int64_t t = t0 + i;
-      if (t < a.T) {
-        const int64_t o = (n * a.T + t) * kDV + 16 * cq;
-        float yy[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) yy[j] = yq[j] + ye[j];
-        if (a.y_dtype == KDN_DTYPE_BF16) {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + o);
-          dst[0] = make_uint4(pack_bf16(yy[0], yy[1]), pack_bf16(yy[2], yy[3]), pack_bf16(yy[4], yy[5]),
-                              pack_bf16(yy[6], yy[7]));
-          dst[1] = make_uint4(pack_bf16(yy[8], yy[9]), pack_bf16(yy[10], yy[11]), pack_bf16(yy[12], yy[13]),
-                              pack_bf16(yy[14], yy[15]));
-        } else {
-          float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) dst[u] = make_float4(yy[4 * u], yy[4 * u + 1], yy[4 * u + 2], yy[4 * u + 3]);
+            for (int u = 0; u < 4; ++u) dst[u] = make_float4(yy[4 * u], yy[4 * u + 1], yy[4 * u + 2], yy[4 * u + 3]);
+          }
         }
       }
+      tc::fence_before_sync();
     }
-    tc::fence_before_sync();
-  }
-
-  // ---------------------------------------------------------------- output state
+    // ------------------------------------------------------------ output state
 #pragma unroll
-  for (int s = 0; s < kSlices; ++s) {
-    float v[16];
-    tc::tmem_ld16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
-    tc::tmem_ld_wait();
-    const int f = 128 * s + trow;
+    for (int s = 0; s < kSlices; ++s) {
+      float v[16];
+      tc::tmem_ld16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
+      tc::tmem_ld_wait();
+      const int f = 128 * s + trow;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) a.S_out[(n * kDV + 16 * cq + j) * kD + f] = v[j];
+      for (int j = 0; j < 16; ++j) a.S_out[(n * kDV + 16 * cq + j) * kD + f] = v[j];
+    }
+    tc::cp_async_wait_all();
   }
-  tc::cp_async_wait_all();
-  if (!ok && lane == 0) record_device_error(&g_tc_error, 2);
+  if (!ok) record_device_error(&g_tc_error, 2);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
