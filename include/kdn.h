@@ -112,6 +112,39 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Size of the scratch array compiled into libkdn for kdn_chunked_prefill_static:
+ * 64 MiB of device memory per device, reserved when the library's module is
+ * loaded there.  At D = 512 that covers N*T up to 14,336 tokens (chunk 64) or
+ * 15,360 (chunk 32); kdn_chunked_prefill_workspace_size(..., KDN_MODE_F32) gives
+ * the exact need.
+ */
+#define KDN_STATIC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/*
+ * kdn_chunked_prefill without a workspace argument, for callers that may not
+ * allocate device memory when they run a prefill (an engine that reserved
+ * nearly all device memory for its own pool up front, a step loop that cannot
+ * take cudaFree's implicit device synchronisation).  It always runs the exact
+ * fp32 CUDA-core path (KDN_MODE_F32); its scratch is the fixed
+ * KDN_STATIC_SCRATCH_BYTES array above, so nothing is allocated per call.
+ *   - Sizes whose scratch need exceeds KDN_STATIC_SCRATCH_BYTES are rejected
+ *     with KDN_ERR_WORKSPACE before any work is enqueued.
+ *   - The first call on each device looks the array's address up
+ *     (cudaGetSymbolAddress with that device current); make that call before
+ *     any stream capture begins.
+ *   - All calls on one device share the array: calls whose kernels overlap
+ *     (unordered streams, several host threads) race.  Serialise them.
+ * Arguments and results are those of kdn_chunked_prefill.  This entry point has
+ * no counterpart in the reference (kernels/fused_kernel_deltanet.py allocates
+ * its temporaries through PyTorch on every call).
+ */
+int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int in_dtype,
+                               const void* beta, const void* decay, int gate_dtype,
+                               const float* initial_state, void* y, int y_dtype,
+                               float* final_state, int64_t N, int64_t T, int32_t dv,
+                               int32_t chunk, const kdn_projection* proj, void* stream);
+
+/*
  * One decode token per (token, head), states addressed through slot_mapping:
  * q, k: [num_tokens, H, d_k]; v, out: [num_tokens, H, dv] (in_dtype / out_dtype);
  * beta, decay: [num_tokens, H] (gate_dtype, decay may be NULL);

@@ -153,6 +153,35 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   return ok();
 }
 
+// Same checks and kernels as kdn_chunked_prefill in KDN_MODE_F32; the workspace is the
+// library's fixed scratch array (prefill_static.cu), for callers that cannot allocate.
+int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int in_dtype, const void* beta,
+                               const void* decay, int gate_dtype, const float* initial_state, void* y, int y_dtype,
+                               float* final_state, int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                               const kdn_projection* proj, void* stream) {
+  if (int rc = check_projection(proj)) return rc;
+  // bound the sizes first so that the scratch computation below cannot overflow
+  if (N < 1 || N > 65535) return fail(KDN_ERR_INVALID, "N=%lld outside [1, 65535]", (long long)N);
+  if (T < 0) return fail(KDN_ERR_INVALID, "T=%lld < 0", (long long)T);
+  if (T > int64_t(KDN_STATIC_SCRATCH_BYTES))
+    return fail(KDN_ERR_WORKSPACE, "T=%lld: far beyond the %u-byte static scratch; use kdn_chunked_prefill",
+                (long long)T, KDN_STATIC_SCRATCH_BYTES);
+  const size_t need = kdn_chunked_prefill_workspace_size(N, T, dv, chunk, proj, KDN_MODE_F32);
+  if (need > size_t(KDN_STATIC_SCRATCH_BYTES))
+    return fail(KDN_ERR_WORKSPACE,
+                "N=%lld T=%lld needs %zu bytes of scratch, more than the %u-byte static scratch "
+                "(KDN_STATIC_SCRATCH_BYTES); split the call or use kdn_chunked_prefill with a workspace",
+                (long long)N, (long long)T, need, KDN_STATIC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (need > 0) {
+    cudaError_t e = kdn::static_prefill_scratch(&scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "static scratch address");
+  }
+  return kdn_chunked_prefill(q, k, v, in_dtype, beta, decay, gate_dtype, initial_state, y, y_dtype, final_state, N, T,
+                             dv, chunk, proj, KDN_MODE_F32, scratch, scratch ? size_t(KDN_STATIC_SCRATCH_BYTES) : 0,
+                             stream);
+}
+
 int kdn_decode_step(const void* q, const void* k, const void* v, int in_dtype, const void* beta, const void* decay,
                     int gate_dtype, void* states, int state_dtype, int64_t num_slots, const void* slot_mapping,
                     int index_dtype, void* out, int out_dtype, int64_t num_tokens, int32_t H, int32_t dv,

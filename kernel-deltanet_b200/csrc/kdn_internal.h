@@ -36,6 +36,10 @@ size_t simt_prefill_workspace(int64_t N, int64_t T, int dv, int C, int D);
 cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
                                 cudaStream_t stream);
 
+// prefill_static.cu: device address of the library's fixed prefill scratch
+// (KDN_STATIC_SCRATCH_BYTES) on the current device, looked up on first use.
+cudaError_t static_prefill_scratch(void** out);
+
 // prefill_tc.cu: fused tensor-core path (bf16 operands, fp32 accumulation/state),
 // one 4-CTA cluster per sequence; needs D=512, dv=64, C=64 and Omega exact in bf16.
 bool tc_prefill_supported(int D, int dv, int C, const ProjParams& P);
