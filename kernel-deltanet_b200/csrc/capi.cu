@@ -5,6 +5,7 @@
 // buffer read by kdn_last_error().  Nothing here allocates device memory.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -66,6 +67,23 @@ bool use_tc_path(const kdn_projection* proj, int32_t dv, int32_t chunk, int mode
   return cached_ok && proj->D == 512 && dv == 64 && chunk == 64;
 }
 
+// Which tensor-core prefill runs: the fused kernel (one CTA per sequence) keeps
+// everything on chip and suits many sequences; the two-phase kernels spread each
+// sequence's chunks over all SMs and suit fewer sequences than SMs.  KDN_PREFILL_PATH
+// = "fused" or "split" forces one (both give the same results up to rounding).
+bool use_split_path(int64_t N) {
+  const char* env = getenv("KDN_PREFILL_PATH");
+  if (env && strcmp(env, "fused") == 0) return false;
+  if (env && strcmp(env, "split") == 0) return true;
+  static thread_local int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  return N < sms;
+}
+
 }  // namespace
 
 extern "C" {
@@ -90,7 +108,8 @@ int kdn_fwht_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t 
 size_t kdn_chunked_prefill_workspace_size(int64_t N, int64_t T, int32_t dv, int32_t chunk,
                                           const kdn_projection* proj, int mode) {
   if (!proj || N <= 0 || T <= 0 || (chunk != 32 && chunk != 64)) return 0;
-  if (proj->D >= 64 && proj->D <= 512 && proj->d_k == 64 && use_tc_path(proj, dv, chunk, mode)) return 0;
+  if (proj->D >= 64 && proj->D <= 512 && proj->d_k == 64 && use_tc_path(proj, dv, chunk, mode))
+    return use_split_path(N) ? kdn::split_prefill_workspace(N, T) : 0;
   return kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
 }
 
@@ -125,7 +144,9 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   const bool tc = use_tc_path(proj, dv, chunk, mode);
   if (tc && (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(y, 16)))
     return fail(KDN_ERR_INVALID, "q/k/v/y must be 16-byte aligned for the tensor-core path");
-  const size_t need = tc ? 0 : kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
+  const bool split = tc && use_split_path(N);
+  const size_t need = tc ? (split ? kdn::split_prefill_workspace(N, T) : 0)
+                         : kdn::simt_prefill_workspace(N, T, dv, chunk, proj->D);
   if (need > 0 && (!workspace || workspace_bytes < need))
     return fail(KDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
   if (need > 0 && !aligned(workspace, 256)) return fail(KDN_ERR_INVALID, "workspace must be 256-byte aligned");
@@ -148,7 +169,9 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   p.C = chunk;
   p.D = proj->D;
   const kdn::ProjParams P = kdn::make_proj_params(*proj);
-  cudaError_t e = tc ? kdn::launch_tc_prefill(p, P, st) : kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st);
+  cudaError_t e = split ? kdn::launch_split_prefill(p, P, workspace, workspace_bytes, st)
+                  : tc  ? kdn::launch_tc_prefill(p, P, st)
+                        : kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return ok();
 }
@@ -243,12 +266,14 @@ int kdn_fork_state(void* states, int64_t num_slots, int64_t bytes_per_slot, int6
 
 int kdn_device_error(void* stream, int* code_out) {
   if (!code_out) return fail(KDN_ERR_INVALID, "code_out is NULL");
-  int code = 0, code_tc = 0;
+  int code = 0, code_tc = 0, code_split = 0;
   cudaError_t e = kdn::decode_read_error(static_cast<cudaStream_t>(stream), &code);
   if (e != cudaSuccess) return cuda_fail(e, "device error read");
   e = kdn::tc_read_error(static_cast<cudaStream_t>(stream), &code_tc);
   if (e != cudaSuccess) return cuda_fail(e, "device error read");
-  *code_out = code ? code : code_tc;
+  e = kdn::split_read_error(static_cast<cudaStream_t>(stream), &code_split);
+  if (e != cudaSuccess) return cuda_fail(e, "device error read");
+  *code_out = code ? code : (code_tc ? code_tc : code_split);
   return ok();
 }
 

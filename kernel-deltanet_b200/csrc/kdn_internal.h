@@ -41,10 +41,18 @@ cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, vo
 cudaError_t static_prefill_scratch(void** out);
 
 // prefill_tc.cu: fused tensor-core path (bf16 operands, fp32 accumulation/state),
-// one 4-CTA cluster per sequence; needs D=512, dv=64, C=64 and Omega exact in bf16.
+// one CTA per sequence; needs D=512, dv=64, C=64 and Omega exact in bf16.
 bool tc_prefill_supported(int D, int dv, int C, const ProjParams& P);
 cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cudaStream_t stream);
 cudaError_t tc_read_error(cudaStream_t stream, int* code);
+
+// prefill_split.cu: the same arithmetic in two phases for few, long sequences -- a
+// chunk-parallel preparation pass writing one record per chunk to the workspace, then
+// a serial state pass per sequence.  Same shape requirements as the fused path.
+size_t split_prefill_workspace(int64_t N, int64_t T);
+cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
+                                 cudaStream_t stream);
+cudaError_t split_read_error(cudaStream_t stream, int* code);
 
 // ---------------------------------------------------------------- decode.cu
 struct DecodeProblem {

@@ -309,15 +309,28 @@ TC_CASES = [
 ]
 
 
-def test_tc_path_selected(kdn, proj):
+@pytest.fixture(params=["fused", "split"])
+def tc_path(request, monkeypatch):
+    """Run a tensor-core test on the fused kernel and on the two-phase kernels."""
+    monkeypatch.setenv("KDN_PREFILL_PATH", request.param)
+    return request.param
+
+
+def test_tc_path_selected(kdn, proj, monkeypatch):
     lib = kdn.load()
     s, _ = proj.kdn_projection(DEV)
-    assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == 0  # fused, no workspace
+    rec = 222208  # bytes of one chunk record of the two-phase path
+    assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == 16 * 1024 * rec  # few sequences: split
+    assert lib.kdn_chunked_prefill_workspace_size(512, 16384, 64, 64, s, 1) == 0  # many sequences: fused
     assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 0) > 0   # CUDA-core path
+    monkeypatch.setenv("KDN_PREFILL_PATH", "fused")
+    assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == 0
+    monkeypatch.setenv("KDN_PREFILL_PATH", "split")
+    assert lib.kdn_chunked_prefill_workspace_size(512, 100, 64, 64, s, 1) == 512 * 2 * rec
 
 
 @pytest.mark.parametrize("case", TC_CASES)
-def test_tc_prefill_vs_oracle(kdn, proj, consts, case):
+def test_tc_prefill_vs_oracle(kdn, proj, consts, case, tc_path):
     seed, N, T, gated, init = case
     q, k, v, beta, decay, S0 = make_inputs(seed, N, T, 64, gated, init)
     qb, kb, vb = (to_dev(a, torch.bfloat16) for a in (q, k, v))
@@ -329,7 +342,7 @@ def test_tc_prefill_vs_oracle(kdn, proj, consts, case):
     assert fro_rel(S.cpu().numpy(), Sr) < BF16_S_TOL
 
 
-def test_tc_prefill_fp32_inputs_bf16_mode(kdn, proj, consts):
+def test_tc_prefill_fp32_inputs_bf16_mode(kdn, proj, consts, tc_path):
     q, k, v, beta, decay, S0 = make_inputs(110, 2, 200, 64, True, True)
     Y, S = kdn.fused_chunked_deltanet_forward(to_dev(q), to_dev(k), to_dev(v), to_dev(beta), to_dev(decay), proj, 64,
                                               to_dev(S0), mode="bf16")
@@ -339,7 +352,7 @@ def test_tc_prefill_fp32_inputs_bf16_mode(kdn, proj, consts):
     assert fro_rel(S.cpu().numpy(), Sr) < BF16_S_TOL
 
 
-def test_tc_prefill_long_sequence_vs_oracle(kdn, proj, consts):
+def test_tc_prefill_long_sequence_vs_oracle(kdn, proj, consts, tc_path):
     q, k, v, beta, _, _ = make_inputs(111, 2, 8192, 64, False, False)
     qb, kb, vb = (to_dev(a, torch.bfloat16) for a in (q, k, v))
     Y, S = kdn.fused_chunked_deltanet_forward(qb, kb, vb, to_dev(beta), None, proj, 64, mode="bf16")
@@ -349,7 +362,7 @@ def test_tc_prefill_long_sequence_vs_oracle(kdn, proj, consts):
     assert fro_rel(S.cpu().numpy(), Sr) < BF16_S_TOL
 
 
-def test_tc_resume_is_bit_exact(kdn, proj):
+def test_tc_resume_is_bit_exact(kdn, proj, tc_path):
     q, k, v, beta, decay, _ = make_inputs(112, 3, 512, 64, True, False)
     dq, dk, dvv = (to_dev(a, torch.bfloat16) for a in (q, k, v))
     db, dd = to_dev(beta), to_dev(decay)
@@ -362,7 +375,7 @@ def test_tc_resume_is_bit_exact(kdn, proj):
     assert torch.equal(S2, S)
 
 
-def test_tc_full_config1_vs_fp32_path(kdn, proj):
+def test_tc_full_config1_vs_fp32_path(kdn, proj, tc_path):
     """Config 1 at full size (16 heads x 65536 tokens): the tensor-core path
     against the exact fp32 CUDA-core path (itself pinned to the oracle above)."""
     H, T = 16, 65536
@@ -377,3 +390,20 @@ def test_tc_full_config1_vs_fp32_path(kdn, proj):
     es = ((St - Sf).norm() / Sf.norm()).item()
     assert ey < BF16_Y_TOL, ey
     assert es < BF16_S_TOL, es
+
+
+def test_tc_fused_and_split_paths_agree(kdn, proj, monkeypatch):
+    """The two tensor-core schedules compute the same chunk algebra; they differ
+    only in where (I + A)^-1 is applied, i.e. in fp16 rounding."""
+    q, k, v, beta, decay, S0 = make_inputs(120, 3, 700, 64, True, True)
+    args = [to_dev(a, torch.bfloat16) for a in (q, k, v)] + [to_dev(beta), to_dev(decay), proj, 64, to_dev(S0)]
+    out = {}
+    for path in ("fused", "split"):
+        monkeypatch.setenv("KDN_PREFILL_PATH", path)
+        out[path] = kdn.fused_chunked_deltanet_forward(*args, mode="bf16")
+    (Yf, Sf), (Ys, Ss) = out["fused"], out["split"]
+    assert rel_err(Ys.float().cpu().numpy(), Yf.float().cpu().numpy()) < BF16_Y_TOL
+    assert fro_rel(Ss.cpu().numpy(), Sf.cpu().numpy()) < BF16_S_TOL
+    from kdn_b200.serving import device_error
+
+    assert device_error() == 0
