@@ -16,8 +16,8 @@
 //   shared-memory layouts the state pass feeds to the tensor core), U (fp32),
 //   Aq (fp16) and the per-token factors.
 //
-//   phase 2, state_pass_kernel -- one CTA per sequence, serial over chunks, only the
-//   state-dependent products (the fp32 state S^T [D=512 x dv=64] stays in TMEM):
+//   phase 2, state_pass_kernel -- two CTAs per sequence (32 value columns each), serial
+//   over chunks, only the state-dependent products (the fp32 state stays in TMEM):
 //     [X; Yq] = [W; U_q] S^T          (tcgen05, K = 512, records streamed by bulk copies)
 //     E = U - X,  E'' = exp(g_{C-1} - g_j) s_kj e_j
 //     S^T = exp(g_{C-1}) S^T + U_k^T E'',  y_i = s_qi exp(g_{i-1}) Yq_i + (Aq E)_i
@@ -49,7 +49,11 @@ constexpr uint32_t REC_U = 196608;    // 16 KiB  U fp32 row-major [64 tokens][64
 constexpr uint32_t REC_AQ = 212992;   // 8 KiB   Aq fp16 K-major SW128 [64 rows x 64]
 constexpr uint32_t REC_VEC = 221184;  // 1 KiB   ew[64] = exp(g_{C-1} - g_j) s_kj, yqs[64] = s_qi exp(g_{i-1}),
                                       //          eC = exp(g_{C-1})
-constexpr uint32_t REC_BYTES = 222208;
+// written by the state pass (phase 2), read by the output pass (phase 3):
+constexpr uint32_t REC_S0 = 222208;   // 64 KiB  state entering the chunk, S^T fp16, two column halves h at
+                                      //          32 KiB h, each MN-major SW64 [512 features x 32]
+constexpr uint32_t REC_E = 287744;    // 8 KiB   E fp16, halves at 4 KiB h, MN-major SW64 [64 tokens x 32]
+constexpr uint32_t REC_BYTES = 295936;
 
 struct SplitArgs {
   TcArgs a;
@@ -91,6 +95,13 @@ constexpr uint32_t P1_SC = 218368;    // 512 B  token scales
 constexpr uint32_t P1_BAR = 218880;   // mbarriers + TMEM address
 constexpr uint32_t kP1Smem = P1_BAR + 128 + 1024;
 
+// shared-memory tile (8 KiB, [64 rows x 128 B] SW128) where W rows of K-block kb are
+// staged for their copy to the record: 0..3 in F, 4 in VB, 5 over TD+US (all free once
+// the W product is issued), 6..7 over U_k slice 0 (free once the W product completes)
+__host__ __device__ constexpr uint32_t w_stage(int kb) {
+  return kb < 4 ? P1_F + 8192 * kb : kb == 4 ? P1_VB : kb == 5 ? P1_TD : P1_UK + 8192 * (kb - 6);
+}
+
 __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, ProjParams P) {
   const TcArgs& a = sa.a;
   extern __shared__ uint8_t smem_raw[];
@@ -118,8 +129,10 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
   uint64_t* bar_zfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 24);
   uint64_t* bar_fready = reinterpret_cast<uint64_t*>(sm + P1_BAR + 32);
   uint64_t* bar_ops = reinterpret_cast<uint64_t*>(sm + P1_BAR + 40);
-  uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P1_BAR + 56);
+  uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);   // round-1 results staged
+  uint64_t* bar_w2 = reinterpret_cast<uint64_t*>(sm + P1_BAR + 56);      // round-2 results staged
+  uint64_t* bar_stfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 64);  // staged tiles copied out
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P1_BAR + 72);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cq = (warp >> 2) & 3;
@@ -143,6 +156,8 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
     tc::mbar_init(bar_fready, kP1Warps);
     tc::mbar_init(bar_ops, kP1Warps);
     tc::mbar_init(bar_wdone, kP1Warps);
+    tc::mbar_init(bar_w2, kP1Warps);
+    tc::mbar_init(bar_stfree, 1);
     tc::fence_mbar_init();
   }
   build_omega(sm + P1_OMG, P, warp, lane, kP1Thr / 32);
@@ -163,7 +178,7 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
       const uint32_t id_n256 = tc::idesc_f16_f32(128, 256, false, true);
       const uint32_t id_n128 = tc::idesc_f16_f32(128, 128, false, true);
       const uint32_t id_n64 = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0, p_wdone = 0;
+      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0, p_wdone = 0, p_w2 = 0;
       auto lift = [&](int s) {
 #pragma unroll
         for (int k0 = 0; k0 < 64; k0 += 16)
@@ -172,6 +187,7 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
         tc::mma_commit(bar_lift);
       };
       for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x) {
+        uint8_t* rec = record(sa, idx / N, idx % N);
         ok &= tc::mbar_wait_bounded(bar_xin, p_xin, kWaitLimit);
         p_xin ^= 1;
         tc::fence_after_sync();
@@ -189,6 +205,12 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
             const uint64_t fd = tc::smem_desc_sw128(sbase + P1_F + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
             tc::mma_ss(tmem + P1_GP, fd, fd, id_gp, s > 0 || k0 > 0);
           }
+          // the slice's features into the record: U_q rows 64..127 of K-blocks 2s, 2s+1 and U_k slice s
+          for (int kb = 0; kb < 2; ++kb)
+            tc::bulk_store(rec + REC_WQ + (2 * s + kb) * 16384 + 8192, sbase + P1_F + kb * 16384 + 8192, 8192);
+          tc::bulk_store(rec + REC_UK + s * 16384, sbase + P1_UK + s * 16384, 16384);
+          tc::bulk_commit();
+          tc::bulk_wait_read();  // F is rewritten once this phase of bar_mma completes
           tc::mma_commit(bar_mma);
         }
         ok &= tc::mbar_wait_bounded(bar_ops, p_ops, kWaitLimit);
@@ -211,12 +233,23 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
           tc::mma_ss(tmem + P1_W2, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
                      tc::smem_desc_sw128(sbase + P1_UK + 49152 + 128 * k0, 8192, 1024), id_n128, k0 > 0);
         tc::mma_commit(bar_mma);
+        // staged W rows of K-blocks 0..5 and U into the record
+        for (int kb = 0; kb < 6; ++kb) tc::bulk_store(rec + REC_WQ + kb * 16384, sbase + w_stage(kb), 8192);
+        tc::bulk_store(rec + REC_U, sbase + P1_UK + 32768, 16384);
+        tc::bulk_commit();
+        ok &= tc::mbar_wait_bounded(bar_w2, p_w2, kWaitLimit);
+        p_w2 ^= 1;
+        for (int kb = 6; kb < 8; ++kb) tc::bulk_store(rec + REC_WQ + kb * 16384, sbase + w_stage(kb), 8192);
+        tc::bulk_commit();
+        tc::bulk_wait_read();  // the staging tiles are free for the next chunk
+        tc::mbar_arrive(bar_stfree);
       }
+      tc::bulk_wait_all();
     }
     __syncwarp();
   } else {
     // ================================================================ compute warps
-    uint32_t ph_lift = 0, ph_mma = 0;
+    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0;
     auto wait_mma = [&]() {
       ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
       ph_mma ^= 1;
@@ -334,17 +367,20 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
           fp[j >> 1] = pack_f16(u0, u1);
           fp[(j >> 1) + 1] = pack_f16(u2, u3);
         }
-        if (s > 0) wait_mma();  // the previous slice's Gram product is done with F
+        if (s > 0) {
+          wait_mma();  // the previous slice's Gram product and copy-out are done with F
+        } else if (idx != blockIdx.x) {  // the previous chunk's staged tiles have been copied out
+          ok &= tc::mbar_wait_bounded(bar_stfree, ph_st, kWaitLimit);
+          ph_st ^= 1;
+        }
         {
           const int kb = cq >> 1, e0 = 32 * (cq & 1);
           uint8_t* fb = sm + P1_F + kb * 16384;
-          uint8_t* gdst = trow < 64 ? rec + REC_UK + s * 16384 + kb * 8192 : rec + REC_WQ + (2 * s + kb) * 16384;
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
             const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
             const uint32_t off = tc::sw128_offset(trow, e0 + 8 * c8);
             *reinterpret_cast<uint4*>(fb + off) = pk;
-            *reinterpret_cast<uint4*>(gdst + off) = pk;  // U_k rows 0..63 | U_q rows 64..127
             if (trow < 64) *reinterpret_cast<uint4*>(sm + P1_UK + s * 16384 + kb * 8192 + off) = pk;
           }
         }
@@ -411,7 +447,9 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
                        pack_f16_sat(vreg[6], vreg[7]));
       }
       tc::named_bar_sync(1, kP1Threads);
-      // diagonal 16x16 blocks of T = (I + A)^-1: one warp per block, one lane per column
+      // T = (I + A)^-1 (fp32, row-major in Es), with 16x16 blocks T_IJ:
+      // (a) diagonal blocks by forward substitution, one thread per column (warps 0..3,
+      //     lanes 0..15), everything above the diagonal zero;
       if (warp < 4 && lane < 16) {
         const int I = warp, j = lane;
         float tcol[16];
@@ -423,63 +461,41 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
           tcol[r] = (r >= j) ? sacc : 0.f;
         }
 #pragma unroll
-        for (int r = 0; r < 16; ++r) TD[(I * 16 + r) * 16 + j] = tcol[r];
+        for (int r = 0; r < 16; ++r) Es[(16 * I + r) * 64 + 16 * I + j] = tcol[r];
+      }
+      for (int e = tid; e < 64 * 64; e += kP1Threads) {  // zeros off the diagonal blocks (lower ones are
+        const int r = e >> 6, cc = e & 63;               // overwritten below)
+        if ((r >> 4) != (cc >> 4)) Es[e] = 0.f;
       }
       tc::named_bar_sync(1, kP1Threads);
-      // T by block rows (U = I_I - sum_{J<I} A_IJ T_J ; T_I = T_II U) on warps 0-3:
-      // warp w owns rows 4w..4w+3 of the block, lane l columns 2l, 2l+1 (row-major)
-      if (warp < 4) {
-        const int c2 = 2 * lane;
-#pragma unroll
-        for (int I = 0; I < 4; ++I) {
-          float2 acc[4];
-#pragma unroll
-          for (int rr = 0; rr < 4; ++rr) {
-            const int row = 16 * I + 4 * warp + rr;
-            acc[rr] = make_float2(c2 == row ? 1.f : 0.f, c2 + 1 == row ? 1.f : 0.f);
+      // (b) off-diagonal blocks level by level (d = I - J = 1, 2, 3), all threads:
+      //     P = sum_{K=J}^{I-1} A_IK T_KJ, then T_IJ = -T_II P
+#pragma unroll 1
+      for (int d = 1; d < 4; ++d) {
+        const int nblk = 4 - d;
+        for (int e = tid; e < nblk * 256; e += kP1Threads) {
+          const int J = e >> 8, I = J + d, r = (e >> 4) & 15, cc = e & 15;
+          const int row = 16 * I + r;
+          float acc = 0.f;
+          for (int k = 16 * J; k < 16 * I; k += 4) {
+            const float4 a4 = *reinterpret_cast<const float4*>(Am + row * 64 + ((((k >> 2) ^ row) & 15) << 2));
+            acc = fmaf(a4.x, Es[k * 64 + 16 * J + cc], acc);
+            acc = fmaf(a4.y, Es[(k + 1) * 64 + 16 * J + cc], acc);
+            acc = fmaf(a4.z, Es[(k + 2) * 64 + 16 * J + cc], acc);
+            acc = fmaf(a4.w, Es[(k + 3) * 64 + 16 * J + cc], acc);
           }
-#pragma unroll
-          for (int qs = 0; qs < 4 * I; ++qs) {
-            float2 e[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) e[u] = *reinterpret_cast<const float2*>(Es + (4 * qs + u) * 64 + c2);
-#pragma unroll
-            for (int rr = 0; rr < 4; ++rr) {
-              const int row = 16 * I + 4 * warp + rr;
-              const float4 a4 = *reinterpret_cast<const float4*>(Am + row * 64 + (((qs ^ row) & 15) << 2));
-              acc[rr].x = fmaf(-a4.x, e[0].x, acc[rr].x);
-              acc[rr].y = fmaf(-a4.x, e[0].y, acc[rr].y);
-              acc[rr].x = fmaf(-a4.y, e[1].x, acc[rr].x);
-              acc[rr].y = fmaf(-a4.y, e[1].y, acc[rr].y);
-              acc[rr].x = fmaf(-a4.z, e[2].x, acc[rr].x);
-              acc[rr].y = fmaf(-a4.z, e[2].y, acc[rr].y);
-              acc[rr].x = fmaf(-a4.w, e[3].x, acc[rr].x);
-              acc[rr].y = fmaf(-a4.w, e[3].y, acc[rr].y);
-            }
-          }
-#pragma unroll
-          for (int rr = 0; rr < 4; ++rr) *reinterpret_cast<float2*>(US + (4 * warp + rr) * 64 + c2) = acc[rr];
-          tc::named_bar_sync(2, 128);
-          float2 ev[4];
-#pragma unroll
-          for (int rr = 0; rr < 4; ++rr) ev[rr] = make_float2(0.f, 0.f);
-#pragma unroll
-          for (int kk = 0; kk < 16; ++kk) {
-            const float2 u = *reinterpret_cast<const float2*>(US + kk * 64 + c2);
-#pragma unroll
-            for (int rr = 0; rr < 4; ++rr) {
-              const float tv = TD[(I * 16 + 4 * warp + rr) * 16 + kk];
-              ev[rr].x = fmaf(tv, u.x, ev[rr].x);
-              ev[rr].y = fmaf(tv, u.y, ev[rr].y);
-            }
-          }
-#pragma unroll
-          for (int rr = 0; rr < 4; ++rr)
-            *reinterpret_cast<float2*>(Es + (16 * I + 4 * warp + rr) * 64 + c2) = ev[rr];
-          tc::named_bar_sync(2, 128);
+          US[e] = acc;
         }
+        tc::named_bar_sync(1, kP1Threads);
+        for (int e = tid; e < nblk * 256; e += kP1Threads) {
+          const int J = e >> 8, I = J + d, r = (e >> 4) & 15, cc = e & 15;
+          float acc = 0.f;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) acc = fmaf(Es[(16 * I + r) * 64 + 16 * I + k], US[(J << 8) + (k << 4) + cc], acc);
+          Es[(16 * I + r) * 64 + 16 * J + cc] = -acc;
+        }
+        tc::named_bar_sync(1, kP1Threads);
       }
-      tc::named_bar_sync(1, kP1Threads);
       // A operand [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major, 128 x 64)
       {
         const int r = tid >> 2, jq = tid & 3, i = r & 63;
@@ -506,8 +522,8 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
       if (lane == 0) tc::mbar_arrive(bar_ops);
       wait_mma();  // W (features 0..383) and U
 
-      // ---------------------------------------- W, U -> record
-      auto drain_w = [&](uint32_t col, int kb) {  // row trow of K-block kb of W (64 columns from col)
+      // ---------------------------------------- W, U -> staging tiles (copied out by the issuer)
+      auto stage_w = [&](uint32_t col, int kb) {  // row trow of K-block kb of W (64 columns from col)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           float v[32];
@@ -515,28 +531,32 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
           tc::tmem_ld_wait();
 #pragma unroll
           for (int m = 0; m < 4; ++m)
-            *reinterpret_cast<uint4*>(rec + REC_WQ + kb * 16384 + tc::sw128_offset(trow, 32 * hh + 8 * m)) =
+            *reinterpret_cast<uint4*>(sm + w_stage(kb) + tc::sw128_offset(trow, 32 * hh + 8 * m)) =
                 make_uint4(pack_f16_sat(v[8 * m], v[8 * m + 1]), pack_f16_sat(v[8 * m + 2], v[8 * m + 3]),
                            pack_f16_sat(v[8 * m + 4], v[8 * m + 5]), pack_f16_sat(v[8 * m + 6], v[8 * m + 7]));
         }
       };
       if (trow < 64) {
-        drain_w(P1_W0 + 64 * cq, cq);  // K-blocks 0..3
-      } else {
+        stage_w(P1_W0 + 64 * cq, cq);                          // K-blocks 0..3
+        if (cq < 2) stage_w(P1_W1 + 64 * cq, 4 + cq);          // K-blocks 4, 5
+      } else {  // U rows, fp32 row-major over U_k slice 2 (free once the W product completed)
         float u[16];
         tc::tmem_ld16(tmem + lane_off + P1_U + 16 * cq, u);
         tc::tmem_ld_wait();
-        float4* dst = reinterpret_cast<float4*>(rec + REC_U + ((trow - 64) * 64 + 16 * cq) * 4);
+        float4* dst = reinterpret_cast<float4*>(sm + P1_UK + 32768 + ((trow - 64) * 64 + 16 * cq) * 4);
 #pragma unroll
         for (int m = 0; m < 4; ++m) dst[m] = make_float4(u[4 * m], u[4 * m + 1], u[4 * m + 2], u[4 * m + 3]);
       }
+      tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(bar_wdone);  // columns 0..127 free for the second round
-      if (trow < 64 && cq < 2) drain_w(P1_W1 + 64 * cq, 4 + cq);  // K-blocks 4, 5
-      wait_mma();                                                  // W features 384..511
-      if (trow < 64 && cq >= 2) drain_w(P1_W2 + 64 * (cq - 2), 4 + cq);  // K-blocks 6, 7
+      if (lane == 0) tc::mbar_arrive(bar_wdone);  // TMEM columns 0..127 free, staged data complete
+      wait_mma();                                  // W features 384..511
+      if (trow < 64 && cq >= 2) stage_w(P1_W2 + 64 * (cq - 2), 4 + cq);  // K-blocks 6, 7
+      tc::fence_proxy_async_smem();
       tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_w2);
     }
     tc::cp_async_wait_all();
   }
@@ -547,24 +567,29 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
 }
 
 // ================================================================ phase 2
-constexpr int kP2Warps = 8;  // compute warps: 2 per TMEM lane quarter (column halves)
+// Two CTAs per sequence, each owning 32 of the 64 value columns: the state's
+// columns evolve independently (X, E and the update are column-wise), so the
+// halves need no communication; both read the same records (the second read
+// mostly hits L2).  Only W and U_k are streamed (128 KiB per chunk): the outputs
+// are left to phase 3, which reads the state and E this pass writes to the record.
+constexpr int kHalf = 32;    // value columns per CTA
+constexpr int kP2Warps = 8;  // compute warps: 2 per TMEM lane quarter, 16 columns each
 constexpr int kP2Issuer = kP2Warps;
 constexpr int kP2Producer = kP2Warps + 1;
 constexpr int kP2Thr = 32 * (kP2Warps + 2);
 
 // TMEM columns (phase 2)
-constexpr uint32_t P2_S = 0;     // S^T master, slice s at 64 s (lanes = features), fp32
-constexpr uint32_t P2_XY = 256;  // [X; Yq] (lanes = [k; q] tokens, 64 cols = dv)
-constexpr uint32_t P2_YE = 320;  // [junk; Aq E]
+constexpr uint32_t P2_S = 0;    // S^T master, slice s at 32 s (lanes = features), fp32
+constexpr uint32_t P2_X = 128;  // X (lanes 0..63 = k tokens), 32 cols
 
 // shared memory (phase 2)
-constexpr uint32_t P2_WQR = 0;       // 2 x 32 KiB ring of [W; U_q] feature slices (K-major)
-constexpr uint32_t P2_UKB = 65536;   // 64 KiB U_k of the chunk (A operand of the state update)
-constexpr uint32_t P2_SOP = 131072;  // 64 KiB S^T operand (fp16, MN-major), slice s at 16 KiB s
-constexpr uint32_t P2_EB = 196608;   // 8 KiB  E'' (fp16, MN-major)
-constexpr uint32_t P2_ET = 204800;   // 8 KiB  E (fp16, MN-major)
-constexpr uint32_t P2_AQB = 212992;  // 16 KiB [0; Aq] (fp16, K-major); rows 0..63 stay zero
-constexpr uint32_t P2_BAR = 229376;
+constexpr int kRing = 5;              // stages of 32 KiB; per chunk 4 items: W features 0..255,
+                                      // W features 256..511, U_k slices (0,1), U_k slices (2,3)
+constexpr uint32_t P2_RING = 0;       // 160 KiB
+constexpr uint32_t P2_SOP = 163840;   // 32 KiB S^T operand (fp16, MN-major SW64 [512 x 32]), slice s at 8 KiB s
+constexpr uint32_t P2_EB = 196608;    // 4 KiB  E'' (fp16, MN-major SW64 [64 x 32])
+constexpr uint32_t P2_ET = 200704;    // 4 KiB  E (fp16, MN-major SW64), copied to the record
+constexpr uint32_t P2_BAR = 204800;
 constexpr uint32_t kP2Smem = P2_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
@@ -577,40 +602,36 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
   }
   const uint32_t sbase = tc::smem_u32(sm);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P2_BAR);
-  uint64_t* wq_full = bars;       // [2] ring slot loaded (bytes)
-  uint64_t* wq_empty = bars + 2;  // [2] ring slot consumed (MMA commit)
-  uint64_t* ukb_full = bars + 4;  // U_k, Aq of the chunk loaded (bytes)
-  uint64_t* ukb_empty = bars + 5; // state update of the previous chunk done (MMA commit)
-  uint64_t* bar_sop = bars + 6;   // [4] state operand slice s stored (8 warps)
-  uint64_t* bar_x = bars + 10;    // [X; Yq] done (MMA commit)
-  uint64_t* bar_e = bars + 11;    // E, E'' stored (8 warps)
-  uint64_t* bar_s = bars + 12;    // state update and Aq E done (MMA commit)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* ring_full = bars;       // [5] stage loaded (bytes)
+  uint64_t* ring_empty = bars + 5;  // [5] stage consumed (MMA commit)
+  uint64_t* bar_sop = bars + 10;    // [4] state operand slice s stored (8 warps)
+  uint64_t* bar_x = bars + 14;      // X done (MMA commit)
+  uint64_t* bar_e = bars + 15;      // E, E'' stored (8 warps)
+  uint64_t* bar_s = bars + 16;      // state update done, record copies read (MMA commit)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 17);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t n = blockIdx.x;
+  const int64_t n = blockIdx.x >> 1;
+  const int half = blockIdx.x & 1;
+  const int col0 = kHalf * half;  // first value column of this CTA
   const int NC = a.NC;
   bool ok = true;
 
   if (warp == 0) {
-    tc::tmem_alloc(tslot, 512);
+    tc::tmem_alloc(tslot, 256);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    tc::mbar_init(&wq_full[0], 1);
-    tc::mbar_init(&wq_full[1], 1);
-    tc::mbar_init(&wq_empty[0], 1);
-    tc::mbar_init(&wq_empty[1], 1);
-    tc::mbar_init(ukb_full, 1);
-    tc::mbar_init(ukb_empty, 1);
+    for (int b = 0; b < kRing; ++b) {
+      tc::mbar_init(&ring_full[b], 1);
+      tc::mbar_init(&ring_empty[b], 1);
+    }
     for (int s = 0; s < kSlices; ++s) tc::mbar_init(&bar_sop[s], kP2Warps);
     tc::mbar_init(bar_x, 1);
     tc::mbar_init(bar_e, kP2Warps);
     tc::mbar_init(bar_s, 1);
     tc::fence_mbar_init();
   }
-  for (int i = tid; i < 8192 / 16; i += kP2Thr) reinterpret_cast<uint4*>(sm + P2_AQB)[i] = make_uint4(0, 0, 0, 0);
-  tc::fence_proxy_async_smem();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -619,135 +640,145 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
   if (warp == kP2Producer) {
     // ================================================================ bulk loads
     if (lane == 0) {
-      uint32_t pe[2] = {0, 0}, pu = 0;
-      int64_t g = 0;  // ring uses so far
-      auto load_slice = [&](const uint8_t* rec, int s) {
-        const int b = int(g & 1);
-        if (g >= 2) {
-          ok &= tc::mbar_wait_bounded(&wq_empty[b], pe[b], kWaitLimit);
+      uint32_t pe[kRing] = {};
+      int64_t g = 0;  // ring items so far
+      auto stage = [&]() {
+        const int b = int(g % kRing);
+        if (g >= kRing) {
+          ok &= tc::mbar_wait_bounded(&ring_empty[b], pe[b], kWaitLimit);
           pe[b] ^= 1;
         }
-        tc::mbar_arrive_expect_tx(&wq_full[b], 32768);
-        for (int o = 0; o < 32768; o += 16384)
-          tc::bulk_load(sbase + P2_WQR + b * 32768 + o, rec + REC_WQ + s * 32768 + o, 16384, &wq_full[b]);
+        tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
         ++g;
+        return sbase + P2_RING + b * 32768;
       };
       for (int c = 0; c < NC; ++c) {
         const uint8_t* rec = record(sa, c, n);
-        load_slice(rec, 0);
-        load_slice(rec, 1);
-        if (c > 0) {  // the previous chunk's state update has read U_k and Aq
-          ok &= tc::mbar_wait_bounded(ukb_empty, pu, kWaitLimit);
-          pu ^= 1;
+        for (int i = 0; i < 2; ++i) {  // W rows (0..63) of K-blocks 4i..4i+3, 8 KiB each
+          const uint32_t dst = stage();
+          for (int kb = 0; kb < 4; ++kb)
+            tc::bulk_load(dst + kb * 8192, rec + REC_WQ + (4 * i + kb) * 16384, 8192, &ring_full[int((g - 1) % kRing)]);
         }
-        tc::mbar_arrive_expect_tx(ukb_full, 65536 + 8192);
-        for (int o = 0; o < 65536; o += 16384) tc::bulk_load(sbase + P2_UKB + o, rec + REC_UK + o, 16384, ukb_full);
-        tc::bulk_load(sbase + P2_AQB + 8192, rec + REC_AQ, 8192, ukb_full);
-        load_slice(rec, 2);
-        load_slice(rec, 3);
+        for (int p = 0; p < 2; ++p) {  // U_k slices 2p, 2p+1
+          const uint32_t dst = stage();
+          for (int o = 0; o < 32768; o += 16384)
+            tc::bulk_load(dst + o, rec + REC_UK + p * 32768 + o, 16384, &ring_full[int((g - 1) % kRing)]);
+        }
       }
     }
     __syncwarp();
   } else if (warp == kP2Issuer) {
     // ================================================================ MMA issuer
     if (lane == 0) {
-      const uint32_t id_x = tc::idesc_f16_f32(128, 64, false, true);
-      const uint32_t id_s = tc::idesc_f16_f32(128, 64, true, true);
-      uint32_t pf[2] = {0, 0}, psop = 0, pe = 0, pu = 0;
+      const uint32_t id_x = tc::idesc_f16_f32(128, kHalf, false, true);
+      const uint32_t id_s = tc::idesc_f16_f32(128, kHalf, true, true);
+      uint32_t pf[kRing] = {}, psop = 0, pe = 0;
       int64_t g = 0;
+      auto take = [&]() {  // wait for the next ring item; returns its stage
+        const int b = int(g % kRing);
+        ok &= tc::mbar_wait_bounded(&ring_full[b], pf[b], kWaitLimit);
+        pf[b] ^= 1;
+        ++g;
+        return b;
+      };
       for (int c = 0; c < NC; ++c) {
-        for (int s = 0; s < kSlices; ++s, ++g) {
-          const int b = int(g & 1);
-          ok &= tc::mbar_wait_bounded(&wq_full[b], pf[b], kWaitLimit);
-          pf[b] ^= 1;
-          ok &= tc::mbar_wait_bounded(&bar_sop[s], psop, kWaitLimit);
+        uint8_t* rec = record(sa, c, n);
+        for (int i = 0; i < 2; ++i) {  // X = W S^T over features 256 i .. 256 i + 255
+          const int b = take();
+          ok &= tc::mbar_wait_bounded(&bar_sop[2 * i], psop, kWaitLimit);
+          ok &= tc::mbar_wait_bounded(&bar_sop[2 * i + 1], psop, kWaitLimit);
           tc::fence_after_sync();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // K = features 128 s + 16 kk
-            const uint64_t ad =
-                tc::smem_desc_sw128(sbase + P2_WQR + b * 32768 + (kk >> 2) * 16384 + 32 * (kk & 3), 16, 1024);
-            const uint64_t bd = tc::smem_desc_sw128(sbase + P2_SOP + s * 16384 + 16 * kk * 128, 8192, 1024);
-            tc::mma_ss(tmem + P2_XY, ad, bd, id_x, s > 0 || kk > 0);
-          }
-          tc::mma_commit(&wq_empty[b]);
+          for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              // M = 128: rows 0..63 are W; rows 64..127 (the next 8 KiB) give lanes nobody reads
+              const uint64_t ad = tc::smem_desc_sw128(sbase + P2_RING + b * 32768 + kb * 8192 + 32 * kk, 16, 1024);
+              const uint64_t bd = tc::smem_desc_sw64(sbase + P2_SOP + (256 * i + 64 * kb + 16 * kk) * 64, 8192, 512);
+              tc::mma_ss(tmem + P2_X, ad, bd, id_x, i > 0 || kb > 0 || kk > 0);
+            }
+          tc::mma_commit(&ring_empty[b]);
         }
         psop ^= 1;
         tc::mma_commit(bar_x);
+        tc::bulk_store(rec + REC_S0 + half * 32768, sbase + P2_SOP, 32768);  // the state entering the chunk
+        tc::bulk_commit();
         ok &= tc::mbar_wait_bounded(bar_e, pe, kWaitLimit);
         pe ^= 1;
-        ok &= tc::mbar_wait_bounded(ukb_full, pu, kWaitLimit);
-        pu ^= 1;
         tc::fence_after_sync();
+        tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET, 4096);
+        tc::bulk_commit();
+        for (int p = 0; p < 2; ++p) {  // S_s^T += U_k,s^T E'' for s = 2p, 2p+1
+          const int b = take();
+          tc::fence_after_sync();
 #pragma unroll
-        for (int s = 0; s < kSlices; ++s)
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int k0 = 0; k0 < 64; k0 += 16)
-            tc::mma_ss(tmem + P2_S + 64 * s, tc::smem_desc_sw128(sbase + P2_UKB + s * 16384 + 128 * k0, 8192, 1024),
-                       tc::smem_desc_sw128(sbase + P2_EB + 128 * k0, 8192, 1024), id_s, true);
-#pragma unroll
-        for (int k0 = 0; k0 < 64; k0 += 16)
-          tc::mma_ss(tmem + P2_YE, tc::smem_desc_sw128(sbase + P2_AQB + 2 * k0, 16, 1024),
-                     tc::smem_desc_sw128(sbase + P2_ET + 128 * k0, 8192, 1024), id_x, k0 > 0);
+            for (int k0 = 0; k0 < 64; k0 += 16)
+              tc::mma_ss(tmem + P2_S + kHalf * (2 * p + h),
+                         tc::smem_desc_sw128(sbase + P2_RING + b * 32768 + h * 16384 + 128 * k0, 8192, 1024),
+                         tc::smem_desc_sw64(sbase + P2_EB + 64 * k0, 8192, 512), id_s, true);
+          tc::mma_commit(&ring_empty[b]);
+        }
+        tc::bulk_wait_read();  // the state operand and E tiles may be rewritten once bar_s completes
         tc::mma_commit(bar_s);
-        tc::mma_commit(ukb_empty);
       }
+      tc::bulk_wait_all();
     }
     __syncwarp();
   } else {
     // ================================================================ compute warps
-    const int quarter = warp & 3, ch = warp >> 2;  // TMEM lane quarter, column half
+    const int quarter = warp & 3, ch = warp >> 2;  // TMEM lane quarter, 16-column half of the CTA's 32
     const int trow = quarter * 32 + lane;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const int cbase = col0 + 16 * ch;  // first value column of this thread
     const bool decayed = a.decay != nullptr;
 #pragma unroll
     for (int s = 0; s < kSlices; ++s) {  // state master from the initial state
-      float v[32];
+      float v[16];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = a.S0 ? a.S0[(n * kDV + 32 * ch + j) * kD + 128 * s + trow] : 0.f;
-      tc::tmem_st32(tmem + lane_off + P2_S + 64 * s + 32 * ch, v);
+      for (int j = 0; j < 16; ++j) v[j] = a.S0 ? a.S0[(n * kDV + cbase + j) * kD + 128 * s + trow] : 0.f;
+      tc::tmem_st16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
     }
     tc::tmem_st_wait();
     uint32_t px = 0, ps = 0;
     // per-chunk factors, loaded one chunk ahead
-    float urow[32], ew = 0.f, yqs = 0.f, eC = 1.f;
+    float urow[16], ew = 0.f, eC = 1.f;
     auto load_factors = [&](int c) {
       const uint8_t* rec = record(sa, c, n);
       const float* vec = reinterpret_cast<const float*>(rec + REC_VEC);
       if (trow < 64) {
-        const float4* u4 = reinterpret_cast<const float4*>(rec + REC_U + (trow * 64 + 32 * ch) * 4);
+        const float4* u4 = reinterpret_cast<const float4*>(rec + REC_U + (trow * 64 + cbase) * 4);
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
+        for (int m = 0; m < 4; ++m) {
           const float4 x = u4[m];
           urow[4 * m] = x.x, urow[4 * m + 1] = x.y, urow[4 * m + 2] = x.z, urow[4 * m + 3] = x.w;
         }
         ew = vec[trow];
-      } else {
-        yqs = vec[trow];
       }
       eC = vec[128];
     };
     load_factors(0);
     for (int c = 0; c < NC; ++c) {
-      float cu[32];
+      float cu[16];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) cu[j] = urow[j];
-      const float cew = ew, cyqs = yqs, ceC = eC;
-      if (c + 1 < NC) load_factors(c + 1);
+      for (int j = 0; j < 16; ++j) cu[j] = urow[j];
+      const float cew = ew, ceC = eC;
       // ---------------------------------------- state operand (fp16) and decay, by slice
 #pragma unroll
       for (int s = 0; s < kSlices; ++s) {
-        float v[32];
-        tc::tmem_ld32(tmem + lane_off + P2_S + 64 * s + 32 * ch, v);
+        float v[16];
+        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int m = 0; m < 4; ++m)
-          *reinterpret_cast<uint4*>(sm + P2_SOP + s * 16384 + tc::sw128_offset(trow, 32 * ch + 8 * m)) =
+        for (int m = 0; m < 2; ++m)
+          *reinterpret_cast<uint4*>(sm + P2_SOP + s * 8192 + tc::sw64_offset(trow, 16 * ch + 8 * m)) =
               make_uint4(pack_f16_sat(v[8 * m], v[8 * m + 1]), pack_f16_sat(v[8 * m + 2], v[8 * m + 3]),
                          pack_f16_sat(v[8 * m + 4], v[8 * m + 5]), pack_f16_sat(v[8 * m + 6], v[8 * m + 7]));
         if (decayed) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= ceC;
-          tc::tmem_st32(tmem + lane_off + P2_S + 64 * s + 32 * ch, v);
+          for (int j = 0; j < 16; ++j) v[j] *= ceC;
+          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
           tc::tmem_st_wait();
         }
         tc::fence_proxy_async_smem();
@@ -755,19 +786,20 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bar_sop[s]);
       }
+      if (c + 1 < NC) load_factors(c + 1);  // in flight while the products run
       // ---------------------------------------- E = U - X, E'' (k rows)
       ok &= tc::mbar_wait_bounded(bar_x, px, kWaitLimit);
       px ^= 1;
       tc::fence_after_sync();
       if (trow < 64) {
-        float x[32];
-        tc::tmem_ld32(tmem + lane_off + P2_XY + 32 * ch, x);
+        float x[16];
+        tc::tmem_ld16(tmem + lane_off + P2_X + 16 * ch, x);
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = cu[j] - x[j];
+        for (int j = 0; j < 16; ++j) x[j] = cu[j] - x[j];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const uint32_t off = tc::sw128_offset(trow, 32 * ch + 8 * m);
+        for (int m = 0; m < 2; ++m) {
+          const uint32_t off = tc::sw64_offset(trow, 16 * ch + 8 * m);
           *reinterpret_cast<uint4*>(sm + P2_ET + off) =
               make_uint4(pack_f16_sat(x[8 * m], x[8 * m + 1]), pack_f16_sat(x[8 * m + 2], x[8 * m + 3]),
                          pack_f16_sat(x[8 * m + 4], x[8 * m + 5]), pack_f16_sat(x[8 * m + 6], x[8 * m + 7]));
@@ -781,20 +813,185 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_e);
-      // ---------------------------------------- outputs (q rows)
-      ok &= tc::mbar_wait_bounded(bar_s, ps, kWaitLimit);
+      ok &= tc::mbar_wait_bounded(bar_s, ps, kWaitLimit);  // the update is in the master
       ps ^= 1;
       tc::fence_after_sync();
-      if (trow >= 64) {
-        const int64_t t = int64_t(c) * kC + (trow - 64);
+    }
+    // ---------------------------------------- final state
+#pragma unroll
+    for (int s = 0; s < kSlices; ++s) {
+      float v[16];
+      tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) a.S_out[(n * kDV + cbase + j) * kD + 128 * s + trow] = v[j];
+    }
+  }
+  if (!ok) record_device_error(&g_split_error, 3);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 256);
+}
+
+// ================================================================ phase 3
+// Outputs of every chunk at once: y_i = yqs_i (U_q S^T)_i + (Aq E)_i with the state
+// entering the chunk and E from the record.  Persistent CTAs; per chunk 4 ring items
+// (feature slice s: U_q K-blocks 2s, 2s+1 and both column halves of the state rows)
+// and one small item (Aq, E).  The accumulators are double-buffered in TMEM so the
+// epilogue of one chunk overlaps the products of the next.
+constexpr int kP3Thr = 128;  // warp 0 issues, warp 1 loads, warps 2 and 3 (the q-row lanes) write y
+
+// shared memory (phase 3)
+constexpr uint32_t P3_RING = 8192;     // 5 x 32 KiB; [U_q kb 2s | U_q kb 2s+1 | S half 0 | S half 1], 8 KiB each
+constexpr uint32_t P3_SMALL = 172032;  // 2 x 16 KiB: [Aq 8 KiB | E half 0 | E half 1]
+constexpr uint32_t P3_BAR = 204800;
+constexpr uint32_t kP3Smem = P3_BAR + 256 + 1024;
+
+__global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
+  const TcArgs& a = sa.a;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm;
+  {
+    const uint32_t s = tc::smem_u32(smem_raw);
+    sm = smem_raw + ((1024u - (s & 1023u)) & 1023u);
+  }
+  const uint32_t sbase = tc::smem_u32(sm);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P3_BAR);
+  uint64_t* ring_full = bars;        // [5]
+  uint64_t* ring_empty = bars + 5;   // [5]
+  uint64_t* small_full = bars + 10;  // [2]
+  uint64_t* small_empty = bars + 12; // [2]
+  uint64_t* acc_full = bars + 14;    // [2] accumulator buffer u complete (MMA commit)
+  uint64_t* acc_free = bars + 16;    // [2] accumulator buffer u read (2 epilogue warps)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 18);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t N = sa.N;
+  const int64_t total = N * a.NC;
+  bool ok = true;
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, 256);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int b = 0; b < kRing; ++b) {
+      tc::mbar_init(&ring_full[b], 1);
+      tc::mbar_init(&ring_empty[b], 1);
+    }
+    for (int u = 0; u < 2; ++u) {
+      tc::mbar_init(&small_full[u], 1);
+      tc::mbar_init(&small_empty[u], 1);
+      tc::mbar_init(&acc_full[u], 1);
+      tc::mbar_init(&acc_free[u], 2);
+    }
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 1) {
+    // ================================================================ bulk loads
+    if (lane == 0) {
+      uint32_t pe[kRing] = {}, ps[2] = {0, 0};
+      int64_t g = 0, j = 0;
+      for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x, ++j) {
+        const uint8_t* rec = record(sa, idx / N, idx % N);
+        for (int s = 0; s < kSlices; ++s, ++g) {
+          const int b = int(g % kRing);
+          if (g >= kRing) {
+            ok &= tc::mbar_wait_bounded(&ring_empty[b], pe[b], kWaitLimit);
+            pe[b] ^= 1;
+          }
+          const uint32_t dst = sbase + P3_RING + b * 32768;
+          tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
+          for (int h = 0; h < 2; ++h) {
+            tc::bulk_load(dst + h * 8192, rec + REC_WQ + (2 * s + h) * 16384 + 8192, 8192, &ring_full[b]);
+            tc::bulk_load(dst + 16384 + h * 8192, rec + REC_S0 + h * 32768 + s * 8192, 8192, &ring_full[b]);
+          }
+        }
+        const int u = int(j & 1);
+        if (j >= 2) {
+          ok &= tc::mbar_wait_bounded(&small_empty[u], ps[u], kWaitLimit);
+          ps[u] ^= 1;
+        }
+        const uint32_t dst = sbase + P3_SMALL + u * 16384;
+        tc::mbar_arrive_expect_tx(&small_full[u], 16384);
+        tc::bulk_load(dst, rec + REC_AQ, 8192, &small_full[u]);
+        tc::bulk_load(dst + 8192, rec + REC_E, 8192, &small_full[u]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 0) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      const uint32_t id = tc::idesc_f16_f32(128, 64, false, true);
+      uint32_t pf[kRing] = {}, psf[2] = {0, 0}, pfree[2] = {0, 0};
+      int64_t g = 0, j = 0;
+      for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x, ++j) {
+        const int u = int(j & 1);
+        if (j >= 2) {  // the epilogue of chunk j - 2 has read accumulator buffer u
+          ok &= tc::mbar_wait_bounded(&acc_free[u], pfree[u], kWaitLimit);
+          pfree[u] ^= 1;
+        }
+        tc::fence_after_sync();
+        const uint32_t dq = tmem + 128 * u, de = dq + 64;
+        for (int s = 0; s < kSlices; ++s, ++g) {
+          const int b = int(g % kRing);
+          ok &= tc::mbar_wait_bounded(&ring_full[b], pf[b], kWaitLimit);
+          pf[b] ^= 1;
+          tc::fence_after_sync();
+          const uint32_t st = sbase + P3_RING + b * 32768;
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              // M = 128 from 8 KiB before the U_q block: its rows land in lanes 64..127
+              const uint64_t ad = tc::smem_desc_sw128(st + h * 8192 - 8192 + 32 * kk, 16, 1024);
+              // N = 64: the two state halves are the two 32-column atoms, 8 KiB apart
+              const uint64_t bd = tc::smem_desc_sw64(st + 16384 + (64 * h + 16 * kk) * 64, 8192, 512);
+              tc::mma_ss(dq, ad, bd, id, s > 0 || h > 0 || kk > 0);
+            }
+          tc::mma_commit(&ring_empty[b]);
+        }
+        ok &= tc::mbar_wait_bounded(&small_full[u], psf[u], kWaitLimit);
+        psf[u] ^= 1;
+        tc::fence_after_sync();
+        const uint32_t sm_small = sbase + P3_SMALL + u * 16384;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_ss(de, tc::smem_desc_sw128(sm_small - 8192 + 32 * kk, 16, 1024),
+                     tc::smem_desc_sw64(sm_small + 8192 + 16 * kk * 64, 4096, 512), id, kk > 0);
+        tc::mma_commit(&small_empty[u]);
+        tc::mma_commit(&acc_full[u]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ================================================================ epilogue (q-row lanes)
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;  // warps 2, 3: lanes 64..127
+    const int i = (warp - 2) * 32 + lane;                  // token row within the chunk
+    uint32_t pa[2] = {0, 0};
+    int64_t j = 0;
+    for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x, ++j) {
+      const int64_t c = idx / N, n = idx % N;
+      const int u = int(j & 1);
+      const float yqs = reinterpret_cast<const float*>(record(sa, c, n) + REC_VEC)[64 + i];
+      ok &= tc::mbar_wait_bounded(&acc_full[u], pa[u], kWaitLimit);
+      pa[u] ^= 1;
+      tc::fence_after_sync();
+      const int64_t t = c * kC + i;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
         float yq[32], ye[32];
-        tc::tmem_ld32(tmem + lane_off + P2_XY + 32 * ch, yq);
-        tc::tmem_ld32(tmem + lane_off + P2_YE + 32 * ch, ye);
+        tc::tmem_ld32(tmem + lane_off + 128 * u + 32 * hh, yq);
+        tc::tmem_ld32(tmem + lane_off + 128 * u + 64 + 32 * hh, ye);
         tc::tmem_ld_wait();
         if (t < a.T) {
-          const int64_t o = (n * a.T + t) * kDV + 32 * ch;
+          const int64_t o = (n * a.T + t) * kDV + 32 * hh;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) yq[j] = fmaf(cyqs, yq[j], ye[j]);
+          for (int q = 0; q < 32; ++q) yq[q] = fmaf(yqs, yq[q], ye[q]);
           if (a.y_dtype == KDN_DTYPE_BF16) {
             uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + o);
 #pragma unroll
@@ -809,21 +1006,14 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
         }
       }
       tc::fence_before_sync();
-    }
-    // ---------------------------------------- final state
-#pragma unroll
-    for (int s = 0; s < kSlices; ++s) {
-      float v[32];
-      tc::tmem_ld32(tmem + lane_off + P2_S + 64 * s + 32 * ch, v);
-      tc::tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) a.S_out[(n * kDV + 32 * ch + j) * kD + 128 * s + trow] = v[j];
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acc_free[u]);
     }
   }
   if (!ok) record_device_error(&g_split_error, 3);
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 512);
+  if (warp == 0) tc::tmem_dealloc(tmem, 256);
 }
 
 }  // namespace
@@ -864,9 +1054,14 @@ cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, v
   if ((e = cudaFuncSetAttribute(state_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP2Smem))) !=
       cudaSuccess)
     return e;
+  if ((e = cudaFuncSetAttribute(output_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP3Smem))) !=
+      cudaSuccess)
+    return e;
   chunk_prep_kernel<<<grid1, kP1Thr, kP1Smem, stream>>>(sa, P);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  state_pass_kernel<<<unsigned(p.N), kP2Thr, kP2Smem, stream>>>(sa);
+  state_pass_kernel<<<unsigned(2 * p.N), kP2Thr, kP2Smem, stream>>>(sa);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  output_pass_kernel<<<grid1, kP3Thr, kP3Smem, stream>>>(sa);
   return cudaGetLastError();
 }
 

@@ -32,6 +32,12 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t e) {
   return r * 128u + ((((e >> 3) ^ r) & 7u) << 4) + ((e & 7u) << 1);
 }
 
+// byte offset of element (row r, element e) in a SW64 block of 16-bit elements
+// (rows of 64 bytes; 16-byte chunk c of row r stored at chunk c ^ ((r >> 1) & 3))
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t r, uint32_t e) {
+  return r * 64u + ((((e >> 3) ^ (r >> 1)) & 3u) << 4) + ((e & 7u) << 1);
+}
+
 // ------------------------------------------------------------ descriptors
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
   uint64_t d = 0;
@@ -40,6 +46,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= uint64_t(1) << 46;  // descriptor version (sm_100)
   d |= uint64_t(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// SWIZZLE_64B variant (atoms of 8 rows x 64 bytes)
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFFu);
+  d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;  // descriptor version (sm_100)
+  d |= uint64_t(4) << 61;  // SWIZZLE_64B
   return d;
 }
 
@@ -209,6 +226,23 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+// shared -> global bulk store, tracked by the issuing thread's bulk async-group
+// (both addresses 16-byte aligned, bytes a multiple of 16)
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of this thread's committed bulk stores have been read
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// this thread's committed bulk stores are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// hint: bring [src, src + bytes) into L2 (bytes a multiple of 16, src 16-byte aligned)
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // named barrier over `nthreads` threads (id 0 is __syncthreads)
