@@ -10,22 +10,26 @@
 //   features, s = amp / (amp ||u|| + 1e-8) the token scales and the gates of the chunk,
 //     G = U_k U_k^T, P = U_q U_k^T                      (tcgen05, fp16 -> fp32)
 //     A_ij = beta_i exp(g_i - g_j) s_i s_j G_ij (j<i),  T = (I + A)^-1   (CUDA cores, fp32)
-//     W = T diag(beta exp(g) s_k) U_k,  U = T diag(beta) V              (tcgen05)
+//     T' = T diag(beta exp(g) s_k),  U = T diag(beta) V                  (U: tcgen05)
 //     Aq_ij = exp(g_{i-1} - g_j) s_qi s_kj P_ij (j<i)
-//   and writes a chunk record: [W; U_q] and U_k (fp16, already in the swizzled
-//   shared-memory layouts the state pass feeds to the tensor core), U (fp32),
-//   Aq (fp16) and the per-token factors.
+//   and writes a chunk record: U_q, U_k, T' (fp16, already in the swizzled shared-memory
+//   layouts the later passes feed to the tensor core), U (fp32), Aq (fp16) and the
+//   per-token factors.
 //
 //   phase 2, state_pass_kernel -- two CTAs per sequence (32 value columns each), serial
 //   over chunks, only the state-dependent products (the fp32 state stays in TMEM):
-//     [X; Yq] = [W; U_q] S^T          (tcgen05, K = 512, records streamed by bulk copies)
-//     E = U - X,  E'' = exp(g_{C-1} - g_j) s_kj e_j
-//     S^T = exp(g_{C-1}) S^T + U_k^T E'',  y_i = s_qi exp(g_{i-1}) Yq_i + (Aq E)_i
+//     Y = U_k S^T (K = 512),  X = T' Y,  E = U - X,  E'' = exp(g_{C-1} - g_j) s_kj e_j
+//     S^T = exp(g_{C-1}) S^T + U_k^T E''
+//   streaming 72 KiB per chunk (U_k serves both as the A operand of Y and, read as its
+//   transpose, of the update); it stores the state entering each chunk and E.
+//
+//   phase 3, output_pass_kernel -- every chunk at once again:
+//     y_i = s_qi exp(g_{i-1}) (U_q S^T)_i + (Aq E)_i
 //
 // This is the chunk algebra of prefill_tc.cu (the reference chunk step
 // kernels/fused_kernel_deltanet.py:95-149) with (I + A)^-1 applied to the state
-// independent parts ahead of time: E = T (beta (v - exp(g) s X')) = U - W S^T.
-// Records take 217 KiB per chunk of the workspace; nothing else is allocated.
+// independent parts ahead of time: E = T (beta (v - exp(g) s X')) = U - T' (U_k S^T).
+// Records take 233 KiB per chunk of the workspace; nothing else is allocated.
 #include <math.h>
 
 #include "kdn_internal.h"
@@ -41,19 +45,20 @@ __device__ int g_split_error;
 constexpr uint32_t kWaitLimit = 1u << 24;
 
 // ------------------------------------------------ chunk record (workspace)
-constexpr uint32_t REC_WQ = 0;        // 128 KiB [W; U_q] fp16, K-major SW128: K-block kb (features
-                                      //          64kb..64kb+63) at 16 KiB kb, rows 0-63 W, 64-127 U_q
-constexpr uint32_t REC_UK = 131072;   // 64 KiB  U_k fp16: slice s at 16 KiB s, half h at 8 KiB h,
+constexpr uint32_t REC_Q = 0;         // 64 KiB  U_q fp16, K-major SW128: K-block kb (features 64kb..64kb+63)
+                                      //          at 8 KiB kb, [64 tokens x 128 B]
+constexpr uint32_t REC_UK = 65536;    // 64 KiB  U_k fp16: slice s at 16 KiB s, half h at 8 KiB h,
                                       //          [64 tokens x 64 features] SW128
-constexpr uint32_t REC_U = 196608;    // 16 KiB  U fp32 row-major [64 tokens][64]
-constexpr uint32_t REC_AQ = 212992;   // 8 KiB   Aq fp16 K-major SW128 [64 rows x 64]
-constexpr uint32_t REC_VEC = 221184;  // 1 KiB   ew[64] = exp(g_{C-1} - g_j) s_kj, yqs[64] = s_qi exp(g_{i-1}),
+constexpr uint32_t REC_TP = 131072;   // 8 KiB   T' = T diag(beta exp(g) s_k) fp16, K-major SW128 [64 x 64]
+constexpr uint32_t REC_U = 139264;    // 16 KiB  U = T diag(beta) V fp32 row-major [64 tokens][64]
+constexpr uint32_t REC_AQ = 155648;   // 8 KiB   Aq fp16 K-major SW128 [64 rows x 64]
+constexpr uint32_t REC_VEC = 163840;  // 1 KiB   ew[64] = exp(g_{C-1} - g_j) s_kj, yqs[64] = s_qi exp(g_{i-1}),
                                       //          eC = exp(g_{C-1})
 // written by the state pass (phase 2), read by the output pass (phase 3):
-constexpr uint32_t REC_S0 = 222208;   // 64 KiB  state entering the chunk, S^T fp16, two column halves h at
+constexpr uint32_t REC_S0 = 164864;   // 64 KiB  state entering the chunk, S^T fp16, two column halves h at
                                       //          32 KiB h, each MN-major SW64 [512 features x 32]
-constexpr uint32_t REC_E = 287744;    // 8 KiB   E fp16, halves at 4 KiB h, MN-major SW64 [64 tokens x 32]
-constexpr uint32_t REC_BYTES = 295936;
+constexpr uint32_t REC_E = 230400;    // 8 KiB   E fp16, halves at 4 KiB h, MN-major SW64 [64 tokens x 32]
+constexpr uint32_t REC_BYTES = 238592;
 
 struct SplitArgs {
   TcArgs a;
@@ -72,12 +77,9 @@ constexpr int kP1Issuer = kP1Warps;
 constexpr int kP1Thr = 32 * (kP1Warps + 1);
 
 // TMEM columns (phase 1)
-constexpr uint32_t P1_Z = 0;     // lift result, 128 cols
-constexpr uint32_t P1_GP = 128;  // [G; P], 64 cols
-constexpr uint32_t P1_W0 = 0;    // W features 0..255 (after the chunk matrices are read)
-constexpr uint32_t P1_W1 = 256;  // W features 256..383
-constexpr uint32_t P1_U = 384;   // U in lanes 64..127
-constexpr uint32_t P1_W2 = 0;    // W features 384..511 (second round)
+constexpr uint32_t P1_Z = 0;     // lift results, 2 x 128 cols (slices s at 128 (s & 1))
+constexpr uint32_t P1_GP = 256;  // [G; P], 64 cols
+constexpr uint32_t P1_U = 0;     // U in lanes 64..127 (after the chunk matrices are read)
 
 // shared memory (phase 1)
 constexpr uint32_t P1_OMG = 0;        // 64 KiB Omega (bf16)
@@ -93,13 +95,45 @@ constexpr uint32_t P1_GL = 215040;    // 5 x 256 B gates: g, beta, exp(g), exp(g
 constexpr uint32_t P1_SSP = 216320;   // 2 KiB  sums of squares per column quarter
 constexpr uint32_t P1_SC = 218368;    // 512 B  token scales
 constexpr uint32_t P1_BAR = 218880;   // mbarriers + TMEM address
-constexpr uint32_t kP1Smem = P1_BAR + 128 + 1024;
+constexpr uint32_t kP1Smem = P1_BAR + 128 + 1024;  // barriers use 112 bytes
 
-// shared-memory tile (8 KiB, [64 rows x 128 B] SW128) where W rows of K-block kb are
-// staged for their copy to the record: 0..3 in F, 4 in VB, 5 over TD+US (all free once
-// the W product is issued), 6..7 over U_k slice 0 (free once the W product completes)
-__host__ __device__ constexpr uint32_t w_stage(int kb) {
-  return kb < 4 ? P1_F + 8192 * kb : kb == 4 ? P1_VB : kb == 5 ? P1_TD : P1_UK + 8192 * (kb - 6);
+// Level d of the blocked inverse T = (I + A)^-1 (16x16 blocks, T row-major in Es,
+// A in the float4-swizzled layout of sx()): for the blocks I - J = d,
+//   P = sum_{K=J}^{I-1} A_IK T_KJ  (into US),  then  T_IJ = -T_II P.
+template <int D>
+__device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, int tid) {
+  constexpr int kElems = (4 - D) * 256;
+  for (int e = tid; e < kElems; e += kP1Threads) {
+    const int J = e >> 8, I = J + D, r = (e >> 4) & 15, cc = e & 15;
+    const int row = 16 * I + r;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < 4 * D; ++q) {
+      const int k = 16 * J + 4 * q;
+      const float4 a4 = *reinterpret_cast<const float4*>(Am + row * 64 + ((((k >> 2) ^ row) & 15) << 2));
+      acc[0] = fmaf(a4.x, Es[k * 64 + 16 * J + cc], acc[0]);
+      acc[1] = fmaf(a4.y, Es[(k + 1) * 64 + 16 * J + cc], acc[1]);
+      acc[2] = fmaf(a4.z, Es[(k + 2) * 64 + 16 * J + cc], acc[2]);
+      acc[3] = fmaf(a4.w, Es[(k + 3) * 64 + 16 * J + cc], acc[3]);
+    }
+    US[e] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  }
+  tc::named_bar_sync(1, kP1Threads);
+  for (int e = tid; e < kElems; e += kP1Threads) {
+    const int J = e >> 8, I = J + D, r = (e >> 4) & 15, cc = e & 15;
+    const float* trow_ = Es + (16 * I + r) * 64 + 16 * I;
+    const float* pcol = US + (J << 8) + cc;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) {
+      acc[0] = fmaf(trow_[k], pcol[k << 4], acc[0]);
+      acc[1] = fmaf(trow_[k + 1], pcol[(k + 1) << 4], acc[1]);
+      acc[2] = fmaf(trow_[k + 2], pcol[(k + 2) << 4], acc[2]);
+      acc[3] = fmaf(trow_[k + 3], pcol[(k + 3) << 4], acc[3]);
+    }
+    Es[(16 * I + r) * 64 + 16 * J + cc] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
+  }
+  tc::named_bar_sync(1, kP1Threads);
 }
 
 __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, ProjParams P) {
@@ -113,7 +147,6 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
   const uint32_t sbase = tc::smem_u32(sm);
   float* Am = reinterpret_cast<float*>(sm + P1_F);
   float* Es = reinterpret_cast<float*>(sm + P1_F + 16384);
-  float* TD = reinterpret_cast<float*>(sm + P1_TD);
   float* US = reinterpret_cast<float*>(sm + P1_US);
   float* ph = reinterpret_cast<float*>(sm + P1_PH);
   float* gl = reinterpret_cast<float*>(sm + P1_GL);
@@ -123,14 +156,13 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
   float* wdec = gl + 256;
   float* ssp = reinterpret_cast<float*>(sm + P1_SSP);
   float* sc = reinterpret_cast<float*>(sm + P1_SC);
-  uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + P1_BAR);
+  uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + P1_BAR + 80);  // [2] lift into slot s & 1 done
   uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + P1_BAR + 8);
   uint64_t* bar_xin = reinterpret_cast<uint64_t*>(sm + P1_BAR + 16);
-  uint64_t* bar_zfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 24);
+  uint64_t* bar_zfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 96);  // [2] slot s & 1 read by all warps
   uint64_t* bar_fready = reinterpret_cast<uint64_t*>(sm + P1_BAR + 32);
   uint64_t* bar_ops = reinterpret_cast<uint64_t*>(sm + P1_BAR + 40);
-  uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);   // round-1 results staged
-  uint64_t* bar_w2 = reinterpret_cast<uint64_t*>(sm + P1_BAR + 56);      // round-2 results staged
+  uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);   // U staged
   uint64_t* bar_stfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 64);  // staged tiles copied out
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P1_BAR + 72);
 
@@ -149,14 +181,15 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    tc::mbar_init(bar_lift, 1);
+    tc::mbar_init(&bar_lift[0], 1);
+    tc::mbar_init(&bar_lift[1], 1);
     tc::mbar_init(bar_mma, 1);
     tc::mbar_init(bar_xin, kP1Warps);
-    tc::mbar_init(bar_zfree, kP1Warps);
+    tc::mbar_init(&bar_zfree[0], kP1Warps);
+    tc::mbar_init(&bar_zfree[1], kP1Warps);
     tc::mbar_init(bar_fready, kP1Warps);
     tc::mbar_init(bar_ops, kP1Warps);
     tc::mbar_init(bar_wdone, kP1Warps);
-    tc::mbar_init(bar_w2, kP1Warps);
     tc::mbar_init(bar_stfree, 1);
     tc::fence_mbar_init();
   }
@@ -175,16 +208,14 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
     if (lane == 0) {
       const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
       const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
-      const uint32_t id_n256 = tc::idesc_f16_f32(128, 256, false, true);
-      const uint32_t id_n128 = tc::idesc_f16_f32(128, 128, false, true);
       const uint32_t id_n64 = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0, p_wdone = 0, p_w2 = 0;
-      auto lift = [&](int s) {
+      uint32_t p_xin = 0, p_zfree[2] = {0, 0}, p_fready = 0, p_ops = 0, p_wdone = 0;
+      auto lift = [&](int s) {  // Z slot s & 1 = [k; q] Omega_s^T
 #pragma unroll
         for (int k0 = 0; k0 < 64; k0 += 16)
-          tc::mma_ss(tmem + P1_Z, tc::smem_desc_sw128(sbase + P1_XIN + 2 * k0, 16, 1024),
+          tc::mma_ss(tmem + P1_Z + 128 * (s & 1), tc::smem_desc_sw128(sbase + P1_XIN + 2 * k0, 16, 1024),
                      tc::smem_desc_sw128(sbase + P1_OMG + s * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
-        tc::mma_commit(bar_lift);
+        tc::mma_commit(&bar_lift[s & 1]);
       };
       for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x) {
         uint8_t* rec = record(sa, idx / N, idx % N);
@@ -192,11 +223,12 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
         p_xin ^= 1;
         tc::fence_after_sync();
         lift(0);
+        lift(1);
         for (int s = 0; s < kSlices; ++s) {
-          ok &= tc::mbar_wait_bounded(bar_zfree, p_zfree, kWaitLimit);
-          p_zfree ^= 1;
+          ok &= tc::mbar_wait_bounded(&bar_zfree[s & 1], p_zfree[s & 1], kWaitLimit);  // slot s & 1 read by all
+          p_zfree[s & 1] ^= 1;
           tc::fence_after_sync();
-          if (s + 1 < kSlices) lift(s + 1);
+          if (s + 2 < kSlices) lift(s + 2);
           ok &= tc::mbar_wait_bounded(bar_fready, p_fready, kWaitLimit);
           p_fready ^= 1;
           tc::fence_after_sync();
@@ -207,39 +239,26 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
           }
           // the slice's features into the record: U_q rows 64..127 of K-blocks 2s, 2s+1 and U_k slice s
           for (int kb = 0; kb < 2; ++kb)
-            tc::bulk_store(rec + REC_WQ + (2 * s + kb) * 16384 + 8192, sbase + P1_F + kb * 16384 + 8192, 8192);
-          tc::bulk_store(rec + REC_UK + s * 16384, sbase + P1_UK + s * 16384, 16384);
+            tc::bulk_store(rec + REC_Q + (2 * s + kb) * 8192, sbase + P1_F + kb * 16384 + 8192, 8192);
           tc::bulk_commit();
           tc::bulk_wait_read();  // F is rewritten once this phase of bar_mma completes
           tc::mma_commit(bar_mma);
+          tc::bulk_store(rec + REC_UK + s * 16384, sbase + P1_UK + s * 16384, 16384);  // read by the chunk's end
+          tc::bulk_commit();
         }
         ok &= tc::mbar_wait_bounded(bar_ops, p_ops, kWaitLimit);
         p_ops ^= 1;
         tc::fence_after_sync();
 #pragma unroll
-        for (int k0 = 0; k0 < 64; k0 += 16) {  // K = the 64 tokens of the chunk
-          const uint64_t ad = tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024);
-          tc::mma_ss(tmem + P1_W0, ad, tc::smem_desc_sw128(sbase + P1_UK + 128 * k0, 8192, 1024), id_n256, k0 > 0);
-          tc::mma_ss(tmem + P1_W1, ad, tc::smem_desc_sw128(sbase + P1_UK + 32768 + 128 * k0, 8192, 1024), id_n128,
-                     k0 > 0);
-          tc::mma_ss(tmem + P1_U, ad, tc::smem_desc_sw128(sbase + P1_VB + 128 * k0, 8192, 1024), id_n64, k0 > 0);
-        }
+        for (int k0 = 0; k0 < 64; k0 += 16)  // U = T diag(beta) V in lanes 64..127
+          tc::mma_ss(tmem + P1_U, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
+                     tc::smem_desc_sw128(sbase + P1_VB + 128 * k0, 8192, 1024), id_n64, k0 > 0);
         tc::mma_commit(bar_mma);
+        tc::bulk_store(rec + REC_TP, sbase + P1_TOP, 8192);  // T' = rows 0..63 of the A operand
+        tc::bulk_commit();
         ok &= tc::mbar_wait_bounded(bar_wdone, p_wdone, kWaitLimit);
         p_wdone ^= 1;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int k0 = 0; k0 < 64; k0 += 16)
-          tc::mma_ss(tmem + P1_W2, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
-                     tc::smem_desc_sw128(sbase + P1_UK + 49152 + 128 * k0, 8192, 1024), id_n128, k0 > 0);
-        tc::mma_commit(bar_mma);
-        // staged W rows of K-blocks 0..5 and U into the record
-        for (int kb = 0; kb < 6; ++kb) tc::bulk_store(rec + REC_WQ + kb * 16384, sbase + w_stage(kb), 8192);
-        tc::bulk_store(rec + REC_U, sbase + P1_UK + 32768, 16384);
-        tc::bulk_commit();
-        ok &= tc::mbar_wait_bounded(bar_w2, p_w2, kWaitLimit);
-        p_w2 ^= 1;
-        for (int kb = 6; kb < 8; ++kb) tc::bulk_store(rec + REC_WQ + kb * 16384, sbase + w_stage(kb), 8192);
+        tc::bulk_store(rec + REC_U, sbase + P1_F, 16384);
         tc::bulk_commit();
         tc::bulk_wait_read();  // the staging tiles are free for the next chunk
         tc::mbar_arrive(bar_stfree);
@@ -249,7 +268,7 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
     __syncwarp();
   } else {
     // ================================================================ compute warps
-    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0;
+    uint32_t ph_lift[2] = {0, 0}, ph_mma = 0, ph_st = 0;
     auto wait_mma = [&]() {
       ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
       ph_mma ^= 1;
@@ -343,15 +362,15 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
       float ss = 0.f;
 #pragma unroll 1
       for (int s = 0; s < kSlices; ++s) {
-        ok &= tc::mbar_wait_bounded(bar_lift, ph_lift, kWaitLimit);
-        ph_lift ^= 1;
+        ok &= tc::mbar_wait_bounded(&bar_lift[s & 1], ph_lift[s & 1], kWaitLimit);
+        ph_lift[s & 1] ^= 1;
         tc::fence_after_sync();
         float z[32];
-        tc::tmem_ld32(tmem + lane_off + P1_Z + 32 * cq, z);
+        tc::tmem_ld32(tmem + lane_off + P1_Z + 128 * (s & 1) + 32 * cq, z);
         tc::tmem_ld_wait();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(bar_zfree);
+        if (lane == 0) tc::mbar_arrive(&bar_zfree[s & 1]);
         // u = cos(tau_inv z + b); the hardware cosine's ~1e-6 absolute error is far
         // below the fp16 spacing of the stored features for the |arguments| <= 32 here
         uint32_t fp[16];
@@ -468,34 +487,10 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
         if ((r >> 4) != (cc >> 4)) Es[e] = 0.f;
       }
       tc::named_bar_sync(1, kP1Threads);
-      // (b) off-diagonal blocks level by level (d = I - J = 1, 2, 3), all threads:
-      //     P = sum_{K=J}^{I-1} A_IK T_KJ, then T_IJ = -T_II P
-#pragma unroll 1
-      for (int d = 1; d < 4; ++d) {
-        const int nblk = 4 - d;
-        for (int e = tid; e < nblk * 256; e += kP1Threads) {
-          const int J = e >> 8, I = J + d, r = (e >> 4) & 15, cc = e & 15;
-          const int row = 16 * I + r;
-          float acc = 0.f;
-          for (int k = 16 * J; k < 16 * I; k += 4) {
-            const float4 a4 = *reinterpret_cast<const float4*>(Am + row * 64 + ((((k >> 2) ^ row) & 15) << 2));
-            acc = fmaf(a4.x, Es[k * 64 + 16 * J + cc], acc);
-            acc = fmaf(a4.y, Es[(k + 1) * 64 + 16 * J + cc], acc);
-            acc = fmaf(a4.z, Es[(k + 2) * 64 + 16 * J + cc], acc);
-            acc = fmaf(a4.w, Es[(k + 3) * 64 + 16 * J + cc], acc);
-          }
-          US[e] = acc;
-        }
-        tc::named_bar_sync(1, kP1Threads);
-        for (int e = tid; e < nblk * 256; e += kP1Threads) {
-          const int J = e >> 8, I = J + d, r = (e >> 4) & 15, cc = e & 15;
-          float acc = 0.f;
-#pragma unroll
-          for (int k = 0; k < 16; ++k) acc = fmaf(Es[(16 * I + r) * 64 + 16 * I + k], US[(J << 8) + (k << 4) + cc], acc);
-          Es[(16 * I + r) * 64 + 16 * J + cc] = -acc;
-        }
-        tc::named_bar_sync(1, kP1Threads);
-      }
+      // (b) off-diagonal blocks level by level (d = I - J = 1, 2, 3), all threads
+      t_level<1>(Am, Es, US, tid);
+      t_level<2>(Am, Es, US, tid);
+      t_level<3>(Am, Es, US, tid);
       // A operand [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major, 128 x 64)
       {
         const int r = tid >> 2, jq = tid & 3, i = r & 63;
@@ -520,43 +515,21 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
       tc::fence_before_sync();
       tc::named_bar_sync(1, kP1Threads);  // also: gates and scales of this chunk no longer read
       if (lane == 0) tc::mbar_arrive(bar_ops);
-      wait_mma();  // W (features 0..383) and U
+      wait_mma();  // U
 
-      // ---------------------------------------- W, U -> staging tiles (copied out by the issuer)
-      auto stage_w = [&](uint32_t col, int kb) {  // row trow of K-block kb of W (64 columns from col)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float v[32];
-          tc::tmem_ld32(tmem + lane_off + col + 32 * hh, v);
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int m = 0; m < 4; ++m)
-            *reinterpret_cast<uint4*>(sm + w_stage(kb) + tc::sw128_offset(trow, 32 * hh + 8 * m)) =
-                make_uint4(pack_f16_sat(v[8 * m], v[8 * m + 1]), pack_f16_sat(v[8 * m + 2], v[8 * m + 3]),
-                           pack_f16_sat(v[8 * m + 4], v[8 * m + 5]), pack_f16_sat(v[8 * m + 6], v[8 * m + 7]));
-        }
-      };
-      if (trow < 64) {
-        stage_w(P1_W0 + 64 * cq, cq);                          // K-blocks 0..3
-        if (cq < 2) stage_w(P1_W1 + 64 * cq, 4 + cq);          // K-blocks 4, 5
-      } else {  // U rows, fp32 row-major over U_k slice 2 (free once the W product completed)
+      // ---------------------------------------- U -> staging tile (F), copied out by the issuer
+      if (trow >= 64) {
         float u[16];
         tc::tmem_ld16(tmem + lane_off + P1_U + 16 * cq, u);
         tc::tmem_ld_wait();
-        float4* dst = reinterpret_cast<float4*>(sm + P1_UK + 32768 + ((trow - 64) * 64 + 16 * cq) * 4);
+        float4* dst = reinterpret_cast<float4*>(sm + P1_F + ((trow - 64) * 64 + 16 * cq) * 4);
 #pragma unroll
         for (int m = 0; m < 4; ++m) dst[m] = make_float4(u[4 * m], u[4 * m + 1], u[4 * m + 2], u[4 * m + 3]);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(bar_wdone);  // TMEM columns 0..127 free, staged data complete
-      wait_mma();                                  // W features 384..511
-      if (trow < 64 && cq >= 2) stage_w(P1_W2 + 64 * (cq - 2), 4 + cq);  // K-blocks 6, 7
-      tc::fence_proxy_async_smem();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(bar_w2);
+      if (lane == 0) tc::mbar_arrive(bar_wdone);
     }
     tc::cp_async_wait_all();
   }
@@ -568,28 +541,34 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
 
 // ================================================================ phase 2
 // Two CTAs per sequence, each owning 32 of the 64 value columns: the state's
-// columns evolve independently (X, E and the update are column-wise), so the
+// columns evolve independently (Y, X, E and the update are column-wise), so the
 // halves need no communication; both read the same records (the second read
-// mostly hits L2).  Only W and U_k are streamed (128 KiB per chunk): the outputs
-// are left to phase 3, which reads the state and E this pass writes to the record.
+// mostly hits L2).  Per chunk only U_k (64 KiB, two ring items held until the update
+// has read them) and T' (8 KiB) are streamed; the outputs are left to phase 3.
+// The chain is serial (state -> Y -> X -> E -> state), so the compute warps meet at a
+// named barrier after each step and one of their threads issues the next products
+// at once; a separate warp keeps the bulk loads ahead.
 constexpr int kHalf = 32;    // value columns per CTA
 constexpr int kP2Warps = 8;  // compute warps: 2 per TMEM lane quarter, 16 columns each
-constexpr int kP2Issuer = kP2Warps;
-constexpr int kP2Producer = kP2Warps + 1;
-constexpr int kP2Thr = 32 * (kP2Warps + 2);
+constexpr int kP2Threads = 32 * kP2Warps;
+constexpr int kP2Producer = kP2Warps;
+constexpr int kP2Thr = 32 * (kP2Warps + 1);
+constexpr int kP2Leader = 32 * 7;  // issues the MMAs: lane 0 of warp 7 (q rows, no E step)
 
 // TMEM columns (phase 2)
 constexpr uint32_t P2_S = 0;    // S^T master, slice s at 32 s (lanes = features), fp32
-constexpr uint32_t P2_X = 128;  // X (lanes 0..63 = k tokens), 32 cols
+constexpr uint32_t P2_Y = 128;  // Y = U_k S^T (lanes 0..63 = k tokens), 32 cols
+constexpr uint32_t P2_X = 160;  // X = T' Y, 32 cols
 
 // shared memory (phase 2)
-constexpr int kRing = 5;              // stages of 32 KiB; per chunk 4 items: W features 0..255,
-                                      // W features 256..511, U_k slices (0,1), U_k slices (2,3)
+constexpr int kRing = 5;              // 32 KiB stages; items: U_k slices (0,1), (2,3) of each chunk
 constexpr uint32_t P2_RING = 0;       // 160 KiB
-constexpr uint32_t P2_SOP = 163840;   // 32 KiB S^T operand (fp16, MN-major SW64 [512 x 32]), slice s at 8 KiB s
-constexpr uint32_t P2_EB = 196608;    // 4 KiB  E'' (fp16, MN-major SW64 [64 x 32])
-constexpr uint32_t P2_ET = 200704;    // 4 KiB  E (fp16, MN-major SW64), copied to the record
-constexpr uint32_t P2_BAR = 204800;
+constexpr uint32_t P2_TP = 163840;    // 2 x 8 KiB T' (fp16, K-major [64 x 64])
+constexpr uint32_t P2_SOP = 180224;   // 32 KiB S^T operand (fp16, MN-major SW64 [512 x 32]), slice s at 8 KiB s
+constexpr uint32_t P2_YB = 212992;    // 4 KiB  Y (fp16, MN-major SW64 [64 x 32])
+constexpr uint32_t P2_EB = 217088;    // 4 KiB  E'' (fp16, MN-major SW64)
+constexpr uint32_t P2_ET = 221184;    // 4 KiB  E (fp16, MN-major SW64), copied to the record
+constexpr uint32_t P2_BAR = 225280;
 constexpr uint32_t kP2Smem = P2_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
@@ -604,11 +583,13 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P2_BAR);
   uint64_t* ring_full = bars;       // [5] stage loaded (bytes)
   uint64_t* ring_empty = bars + 5;  // [5] stage consumed (MMA commit)
-  uint64_t* bar_sop = bars + 10;    // [4] state operand slice s stored (8 warps)
-  uint64_t* bar_x = bars + 14;      // X done (MMA commit)
-  uint64_t* bar_e = bars + 15;      // E, E'' stored (8 warps)
-  uint64_t* bar_s = bars + 16;      // state update done, record copies read (MMA commit)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* tp_full = bars + 10;    // [2] T' loaded (bytes)
+  uint64_t* tp_empty = bars + 12;   // [2] T' consumed (MMA commit)
+  uint64_t* bar_y = bars + 14;      // Y done (MMA commit)
+  uint64_t* bar_x = bars + 15;      // X done (MMA commit)
+  uint64_t* bar_s = bars + 16;      // [2] state update of slices 2p, 2p+1 done (MMA commit; for p = 0
+                                    //     also the record copies have read their tiles)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n = blockIdx.x >> 1;
@@ -626,10 +607,14 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       tc::mbar_init(&ring_full[b], 1);
       tc::mbar_init(&ring_empty[b], 1);
     }
-    for (int s = 0; s < kSlices; ++s) tc::mbar_init(&bar_sop[s], kP2Warps);
+    for (int u = 0; u < 2; ++u) {
+      tc::mbar_init(&tp_full[u], 1);
+      tc::mbar_init(&tp_empty[u], 1);
+    }
+    tc::mbar_init(bar_y, 1);
     tc::mbar_init(bar_x, 1);
-    tc::mbar_init(bar_e, kP2Warps);
-    tc::mbar_init(bar_s, 1);
+    tc::mbar_init(&bar_s[0], 1);
+    tc::mbar_init(&bar_s[1], 1);
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -640,99 +625,50 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
   if (warp == kP2Producer) {
     // ================================================================ bulk loads
     if (lane == 0) {
-      uint32_t pe[kRing] = {};
+      uint32_t pe[kRing] = {}, pt[2] = {0, 0};
       int64_t g = 0;  // ring items so far
-      auto stage = [&]() {
-        const int b = int(g % kRing);
-        if (g >= kRing) {
-          ok &= tc::mbar_wait_bounded(&ring_empty[b], pe[b], kWaitLimit);
-          pe[b] ^= 1;
-        }
-        tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
-        ++g;
-        return sbase + P2_RING + b * 32768;
-      };
       for (int c = 0; c < NC; ++c) {
         const uint8_t* rec = record(sa, c, n);
-        for (int i = 0; i < 2; ++i) {  // W rows (0..63) of K-blocks 4i..4i+3, 8 KiB each
-          const uint32_t dst = stage();
-          for (int kb = 0; kb < 4; ++kb)
-            tc::bulk_load(dst + kb * 8192, rec + REC_WQ + (4 * i + kb) * 16384, 8192, &ring_full[int((g - 1) % kRing)]);
-        }
-        for (int p = 0; p < 2; ++p) {  // U_k slices 2p, 2p+1
-          const uint32_t dst = stage();
+        for (int p = 0; p < 2; ++p, ++g) {  // U_k slices 2p, 2p+1
+          const int b = int(g % kRing);
+          if (g >= kRing) {
+            ok &= tc::mbar_wait_bounded(&ring_empty[b], pe[b], kWaitLimit);
+            pe[b] ^= 1;
+          }
+          tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
           for (int o = 0; o < 32768; o += 16384)
-            tc::bulk_load(dst + o, rec + REC_UK + p * 32768 + o, 16384, &ring_full[int((g - 1) % kRing)]);
+            tc::bulk_load(sbase + P2_RING + b * 32768 + o, rec + REC_UK + p * 32768 + o, 16384, &ring_full[b]);
         }
+        const int u = c & 1;
+        if (c >= 2) {
+          ok &= tc::mbar_wait_bounded(&tp_empty[u], pt[u], kWaitLimit);
+          pt[u] ^= 1;
+        }
+        tc::mbar_arrive_expect_tx(&tp_full[u], 8192);
+        tc::bulk_load(sbase + P2_TP + u * 8192, rec + REC_TP, 8192, &tp_full[u]);
       }
-    }
-    __syncwarp();
-  } else if (warp == kP2Issuer) {
-    // ================================================================ MMA issuer
-    if (lane == 0) {
-      const uint32_t id_x = tc::idesc_f16_f32(128, kHalf, false, true);
-      const uint32_t id_s = tc::idesc_f16_f32(128, kHalf, true, true);
-      uint32_t pf[kRing] = {}, psop = 0, pe = 0;
-      int64_t g = 0;
-      auto take = [&]() {  // wait for the next ring item; returns its stage
-        const int b = int(g % kRing);
-        ok &= tc::mbar_wait_bounded(&ring_full[b], pf[b], kWaitLimit);
-        pf[b] ^= 1;
-        ++g;
-        return b;
-      };
-      for (int c = 0; c < NC; ++c) {
-        uint8_t* rec = record(sa, c, n);
-        for (int i = 0; i < 2; ++i) {  // X = W S^T over features 256 i .. 256 i + 255
-          const int b = take();
-          ok &= tc::mbar_wait_bounded(&bar_sop[2 * i], psop, kWaitLimit);
-          ok &= tc::mbar_wait_bounded(&bar_sop[2 * i + 1], psop, kWaitLimit);
-          tc::fence_after_sync();
-#pragma unroll
-          for (int kb = 0; kb < 4; ++kb)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              // M = 128: rows 0..63 are W; rows 64..127 (the next 8 KiB) give lanes nobody reads
-              const uint64_t ad = tc::smem_desc_sw128(sbase + P2_RING + b * 32768 + kb * 8192 + 32 * kk, 16, 1024);
-              const uint64_t bd = tc::smem_desc_sw64(sbase + P2_SOP + (256 * i + 64 * kb + 16 * kk) * 64, 8192, 512);
-              tc::mma_ss(tmem + P2_X, ad, bd, id_x, i > 0 || kb > 0 || kk > 0);
-            }
-          tc::mma_commit(&ring_empty[b]);
-        }
-        psop ^= 1;
-        tc::mma_commit(bar_x);
-        tc::bulk_store(rec + REC_S0 + half * 32768, sbase + P2_SOP, 32768);  // the state entering the chunk
-        tc::bulk_commit();
-        ok &= tc::mbar_wait_bounded(bar_e, pe, kWaitLimit);
-        pe ^= 1;
-        tc::fence_after_sync();
-        tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET, 4096);
-        tc::bulk_commit();
-        for (int p = 0; p < 2; ++p) {  // S_s^T += U_k,s^T E'' for s = 2p, 2p+1
-          const int b = take();
-          tc::fence_after_sync();
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int k0 = 0; k0 < 64; k0 += 16)
-              tc::mma_ss(tmem + P2_S + kHalf * (2 * p + h),
-                         tc::smem_desc_sw128(sbase + P2_RING + b * 32768 + h * 16384 + 128 * k0, 8192, 1024),
-                         tc::smem_desc_sw64(sbase + P2_EB + 64 * k0, 8192, 512), id_s, true);
-          tc::mma_commit(&ring_empty[b]);
-        }
-        tc::bulk_wait_read();  // the state operand and E tiles may be rewritten once bar_s completes
-        tc::mma_commit(bar_s);
-      }
-      tc::bulk_wait_all();
     }
     __syncwarp();
   } else {
-    // ================================================================ compute warps
+    // ================================================================ compute warps (+ leader)
     const int quarter = warp & 3, ch = warp >> 2;  // TMEM lane quarter, 16-column half of the CTA's 32
     const int trow = quarter * 32 + lane;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const int cbase = col0 + 16 * ch;  // first value column of this thread
     const bool decayed = a.decay != nullptr;
+    const bool leader = tid == kP2Leader;
+    const uint32_t id_k = tc::idesc_f16_f32(128, kHalf, false, true);  // A K-major, B MN-major
+    const uint32_t id_s = tc::idesc_f16_f32(128, kHalf, true, true);   // A MN-major (U_k^T)
+    // descriptor bases; the products only add constant offsets
+    const uint64_t d_ring = tc::smem_desc_sw128(sbase + P2_RING, 16, 1024);     // U_k as A (K-major)
+    const uint64_t d_ringT = tc::smem_desc_sw128(sbase + P2_RING, 8192, 1024);  // U_k^T as A (MN-major)
+    const uint64_t d_sop = tc::smem_desc_sw64(sbase + P2_SOP, 8192, 512);
+    const uint64_t d_tp = tc::smem_desc_sw128(sbase + P2_TP, 16, 1024);
+    const uint64_t d_yb = tc::smem_desc_sw64(sbase + P2_YB, 8192, 512);
+    const uint64_t d_eb = tc::smem_desc_sw64(sbase + P2_EB, 8192, 512);
+    uint32_t pf[kRing] = {}, pt[2] = {0, 0};  // leader: ring / T' phases
+    int64_t g = 0;                             // leader: ring items taken
+    int st[2] = {0, 0};                        // leader: stages of the chunk's two U_k items
 #pragma unroll
     for (int s = 0; s < kSlices; ++s) {  // state master from the initial state
       float v[16];
@@ -741,7 +677,7 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       tc::tmem_st16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
     }
     tc::tmem_st_wait();
-    uint32_t px = 0, ps = 0;
+    uint32_t py = 0, px = 0, ps[2] = {0, 0};
     // per-chunk factors, loaded one chunk ahead
     float urow[16], ew = 0.f, eC = 1.f;
     auto load_factors = [&](int c) {
@@ -758,65 +694,136 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       }
       eC = vec[128];
     };
+    auto store_tile = [&](uint32_t off, const float* v, float w) {  // 16 values of row trow, fp16 SW64
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+        *reinterpret_cast<uint4*>(sm + off + tc::sw64_offset(trow, 16 * ch + 8 * m)) =
+            make_uint4(pack_f16_sat(w * v[8 * m], w * v[8 * m + 1]), pack_f16_sat(w * v[8 * m + 2], w * v[8 * m + 3]),
+                       pack_f16_sat(w * v[8 * m + 4], w * v[8 * m + 5]),
+                       pack_f16_sat(w * v[8 * m + 6], w * v[8 * m + 7]));
+    };
+    auto step_done = [&]() {  // this warp's shared-memory tiles -> tensor core; all compute warps met
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      tc::named_bar_sync(1, kP2Threads);
+      tc::fence_after_sync();
+    };
+    auto wait_mma = [&](uint64_t* bar, uint32_t& phase) {
+      ok &= tc::mbar_wait_bounded(bar, phase, kWaitLimit);
+      phase ^= 1;
+      tc::fence_after_sync();
+    };
     load_factors(0);
     for (int c = 0; c < NC; ++c) {
+      uint8_t* rec = record(sa, c, n);
       float cu[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) cu[j] = urow[j];
       const float cew = ew, ceC = eC;
-      // ---------------------------------------- state operand (fp16) and decay, by slice
+      // ---------------------------------------- per slice pair: state operand (fp16), decay, Y
 #pragma unroll
-      for (int s = 0; s < kSlices; ++s) {
-        float v[16];
-        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
+      for (int p = 0; p < 2; ++p) {
+        if (c > 0) wait_mma(&bar_s[p], ps[p]);  // the previous chunk's update of slices 2p, 2p+1
+        float v[32];
+        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p) + 16 * ch, *reinterpret_cast<float(*)[16]>(v));
+        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p + 1) + 16 * ch,
+                      *reinterpret_cast<float(*)[16]>(v + 16));
         tc::tmem_ld_wait();
-#pragma unroll
-        for (int m = 0; m < 2; ++m)
-          *reinterpret_cast<uint4*>(sm + P2_SOP + s * 8192 + tc::sw64_offset(trow, 16 * ch + 8 * m)) =
-              make_uint4(pack_f16_sat(v[8 * m], v[8 * m + 1]), pack_f16_sat(v[8 * m + 2], v[8 * m + 3]),
-                         pack_f16_sat(v[8 * m + 4], v[8 * m + 5]), pack_f16_sat(v[8 * m + 6], v[8 * m + 7]));
+        store_tile(P2_SOP + (2 * p) * 8192, v, 1.f);
+        store_tile(P2_SOP + (2 * p + 1) * 8192, v + 16, 1.f);
         if (decayed) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] *= ceC;
-          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
+          for (int j = 0; j < 32; ++j) v[j] *= ceC;
+          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p) + 16 * ch, *reinterpret_cast<float(*)[16]>(v));
+          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p + 1) + 16 * ch,
+                        *reinterpret_cast<float(*)[16]>(v + 16));
           tc::tmem_st_wait();
         }
-        tc::fence_proxy_async_smem();
-        tc::fence_before_sync();
+        step_done();
+        if (leader) {  // Y += U_k S^T over the features of slices 2p, 2p+1
+          const int b = int(g % kRing);
+          st[p] = b;
+          ok &= tc::mbar_wait_bounded(&ring_full[b], pf[b], kWaitLimit);
+          pf[b] ^= 1;
+          ++g;
+          tc::fence_after_sync();
+          const uint64_t da = tc::desc_add(d_ring, uint32_t(b) * 32768);
+          const uint64_t db = tc::desc_add(d_sop, uint32_t(p) * 16384);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)      // slice 2p + h
+#pragma unroll
+            for (int kb = 0; kb < 2; ++kb)  // its 64-feature halves
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                // M = 128: rows 0..63 are the chunk's tokens; rows 64..127 (the next 8 KiB) give
+                // lanes nobody reads
+                tc::mma_ss(tmem + P2_Y, tc::desc_add(da, h * 16384 + kb * 8192 + 32 * kk),
+                           tc::desc_add(db, (128 * h + 64 * kb + 16 * kk) * 64), id_k,
+                           p > 0 || h > 0 || kb > 0 || kk > 0);
+          if (p == 1) {
+            tc::mma_commit(bar_y);
+            tc::bulk_store(rec + REC_S0 + half * 32768, sbase + P2_SOP, 32768);  // the state entering the chunk
+            tc::bulk_commit();
+          }
+        }
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bar_sop[s]);
       }
       if (c + 1 < NC) load_factors(c + 1);  // in flight while the products run
-      // ---------------------------------------- E = U - X, E'' (k rows)
-      ok &= tc::mbar_wait_bounded(bar_x, px, kWaitLimit);
-      px ^= 1;
-      tc::fence_after_sync();
+      // ---------------------------------------- Y (fp16), then X = T' Y
+      wait_mma(bar_y, py);
+      if (trow < 64) {
+        float y[16];
+        tc::tmem_ld16(tmem + lane_off + P2_Y + 16 * ch, y);
+        tc::tmem_ld_wait();
+        store_tile(P2_YB, y, 1.f);
+      }
+      step_done();
+      const int u = c & 1;
+      if (leader) {
+        ok &= tc::mbar_wait_bounded(&tp_full[u], pt[u], kWaitLimit);
+        pt[u] ^= 1;
+        tc::fence_after_sync();
+        const uint64_t da = tc::desc_add(d_tp, uint32_t(u) * 8192);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // K = the 64 tokens; rows 64..127 of A: unread lanes
+          tc::mma_ss(tmem + P2_X, tc::desc_add(da, 32 * kk), tc::desc_add(d_yb, 16 * kk * 64), id_k, kk > 0);
+        tc::mma_commit(&tp_empty[u]);
+        tc::mma_commit(bar_x);
+      }
+      __syncwarp();
+      // ---------------------------------------- E = U - X, E'', then the update
+      wait_mma(bar_x, px);
       if (trow < 64) {
         float x[16];
         tc::tmem_ld16(tmem + lane_off + P2_X + 16 * ch, x);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) x[j] = cu[j] - x[j];
+        store_tile(P2_ET, x, 1.f);
+        store_tile(P2_EB, x, cew);
+      }
+      step_done();
+      if (leader) {
+        tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET, 4096);
+        tc::bulk_commit();
+        for (int p = 0; p < 2; ++p) {  // S_s^T += U_k,s^T E'' for s = 2p, 2p+1
+          const uint64_t da = tc::desc_add(d_ringT, uint32_t(st[p]) * 32768);
 #pragma unroll
-        for (int m = 0; m < 2; ++m) {
-          const uint32_t off = tc::sw64_offset(trow, 16 * ch + 8 * m);
-          *reinterpret_cast<uint4*>(sm + P2_ET + off) =
-              make_uint4(pack_f16_sat(x[8 * m], x[8 * m + 1]), pack_f16_sat(x[8 * m + 2], x[8 * m + 3]),
-                         pack_f16_sat(x[8 * m + 4], x[8 * m + 5]), pack_f16_sat(x[8 * m + 6], x[8 * m + 7]));
-          *reinterpret_cast<uint4*>(sm + P2_EB + off) = make_uint4(
-              pack_f16_sat(cew * x[8 * m], cew * x[8 * m + 1]), pack_f16_sat(cew * x[8 * m + 2], cew * x[8 * m + 3]),
-              pack_f16_sat(cew * x[8 * m + 4], cew * x[8 * m + 5]),
-              pack_f16_sat(cew * x[8 * m + 6], cew * x[8 * m + 7]));
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int k0 = 0; k0 < 64; k0 += 16)
+              tc::mma_ss(tmem + P2_S + kHalf * (2 * p + h), tc::desc_add(da, h * 16384 + 128 * k0),
+                         tc::desc_add(d_eb, 64 * k0), id_s, true);
+          tc::mma_commit(&ring_empty[st[p]]);
+          if (p == 0) tc::bulk_wait_read();  // the state operand and E tiles are rewritten after bar_s[0]
+          tc::mma_commit(&bar_s[p]);
         }
       }
-      tc::fence_proxy_async_smem();
-      tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(bar_e);
-      ok &= tc::mbar_wait_bounded(bar_s, ps, kWaitLimit);  // the update is in the master
-      ps ^= 1;
-      tc::fence_after_sync();
     }
+    wait_mma(&bar_s[0], ps[0]);
+    wait_mma(&bar_s[1], ps[1]);
+    if (leader) tc::bulk_wait_all();
     // ---------------------------------------- final state
 #pragma unroll
     for (int s = 0; s < kSlices; ++s) {
@@ -907,7 +914,7 @@ __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
           const uint32_t dst = sbase + P3_RING + b * 32768;
           tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
           for (int h = 0; h < 2; ++h) {
-            tc::bulk_load(dst + h * 8192, rec + REC_WQ + (2 * s + h) * 16384 + 8192, 8192, &ring_full[b]);
+            tc::bulk_load(dst + h * 8192, rec + REC_Q + (2 * s + h) * 8192, 8192, &ring_full[b]);
             tc::bulk_load(dst + 16384 + h * 8192, rec + REC_S0 + h * 32768 + s * 8192, 8192, &ring_full[b]);
           }
         }

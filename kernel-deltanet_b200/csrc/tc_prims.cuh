@@ -60,6 +60,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo_
   return d;
 }
 
+// descriptor of the operand `byte_off` bytes further on: the start address field holds
+// addr >> 4 in 14 bits, so for shared-memory addresses below 256 KiB adding never carries
+// into the neighbouring fields (byte_off a multiple of 16)
+__host__ __device__ __forceinline__ uint64_t desc_add(uint64_t desc, uint32_t byte_off) {
+  return desc + uint64_t(byte_off >> 4);
+}
+
 // kind::f16 instruction descriptor: bf16 x bf16 -> f32, dense.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                          // D format: f32

@@ -319,7 +319,7 @@ def tc_path(request, monkeypatch):
 def test_tc_path_selected(kdn, proj, monkeypatch):
     lib = kdn.load()
     s, _ = proj.kdn_projection(DEV)
-    rec = 295936  # bytes of one chunk record of the two-phase path
+    rec = 238592  # bytes of one chunk record of the two-phase path
     assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == 16 * 1024 * rec  # few sequences: split
     assert lib.kdn_chunked_prefill_workspace_size(512, 16384, 64, 64, s, 1) == 0  # many sequences: fused
     assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 0) > 0   # CUDA-core path
