@@ -19,8 +19,10 @@ baseline (the numpy port of the reference path, timed on a bounded sample).
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -32,6 +34,21 @@ for _p in (ROOT, os.path.join(ROOT, "kernel-deltanet_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "KDN layer prefill tokens/s at T=64k,D=512 (1–8 B200); decode steps/s"
+
+# Algorithmic work per chunk (64 tokens) of one sequence, per kernel of the two-phase
+# tensor-core prefill (the path the library selects for fewer sequences than SMs):
+#   chunk_prep : lift 2*128*64*512 + Gram 2*128*512*64 + U 2*64*64*64 FLOP; reads k,q,v
+#                (bf16) and gates, writes the chunk record (U_q, U_k, T', U, Aq, factors)
+#   state_pass : Y 2*64*512*64 + X 2*64*64*64 + update 2*512*64*64 FLOP; reads U_k, T', U,
+#                factors, writes the entering state (fp16) and E
+#   output_pass: 2*64*512*64 + 2*64*64*64 FLOP; reads U_q, state, E, Aq, writes y (bf16)
+SPLIT_KERNELS = [
+    ("chunk_prep_kernel", 2 * 128 * 64 * 512 + 2 * 128 * 512 * 64 + 2 * 64 ** 3,
+     3 * 64 * 64 * 2 + 64 * 4 + 65536 * 2 + 8192 + 16384 + 8192 + 1024),
+    ("state_pass_kernel", 2 * 64 * 512 * 64 + 2 * 64 ** 3 + 2 * 512 * 64 * 64,
+     65536 + 8192 + 16384 + 1024 + 65536 + 8192),
+    ("output_pass_kernel", 2 * 64 * 512 * 64 + 2 * 64 ** 3, 65536 + 65536 + 8192 + 8192 + 256 + 64 * 64 * 2),
+]
 B, H, T, DK, DV, D, C = 1, 16, 65536, 64, 64, 512, 64
 FLOP_PER_TOKEN_HEAD = 360448  # 5 D-wide + 4 C-wide GEMMs per chunk / C (algorithmic count)
 DEC_STREAMS, DEC_H = 64, 16
@@ -59,18 +76,38 @@ class ClockSampler:
         self.proc = None
         self.path = f"/tmp/kdn_clocks_{os.getpid()}.csv"
 
-    def start(self):
+    def _lines(self):
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
+            with open(self.path) as f:
+                return f.read().count("\n")
+        except OSError:
+            return 0
+
+    def start(self):
+        """Start sampling every 25 ms; returns once samples are flowing."""
+        self.first = 0
+        try:
+            self.f = open(self.path, "w", buffering=1)
+            cmd = ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                   "-lms", "25"]
+            if shutil.which("stdbuf"):
+                cmd = ["stdbuf", "-oL"] + cmd  # one line per sample, readable while it runs
+            self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while self._lines() < 2 and time.time() - t0 < 10:
+            time.sleep(0.02)
+
+    def mark(self):
+        """Call right before the timed region: later samples are the ones reported."""
+        self.first = self._lines()
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        last = self._lines()
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -78,7 +115,9 @@ class ClockSampler:
             self.proc.kill()
         self.f.close()
         rows = []
-        for line in open(self.path):
+        for i, line in enumerate(open(self.path)):
+            if not (self.first <= i < last):
+                continue
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -221,18 +260,34 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # per-launch events, recorded by the library on the launch stream inside the timed region
+    nmarks = 8
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(nmarks)] for _ in range(args.steps)]
+    for row in marks:
+        for ev in row:
+            ev.record()  # creates the CUDA event
+    handles = [(ctypes.c_void_p * nmarks)(*[ev.cuda_event for ev in row]) for row in marks]
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    for _ in range(2):  # keep the GPU busy while the sampler starts
+        step()
+    torch.cuda.synchronize()
+    clocks.mark()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        lib.kdn_set_prefill_events(handles[i], nmarks)
         step()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     clk = clocks.stop()
+    nlaunch = int(lib.kdn_prefill_launch_count())
+    launch_ms = [statistics.mean(marks[i][j].elapsed_time(marks[i][j + 1]) for i in range(args.steps))
+                 for j in range(min(nlaunch, nmarks - 1))]
     if world > 1:
         dist.barrier()
         t = torch.tensor([ms], device=dev)
@@ -279,12 +334,42 @@ def run_ours(args):
         return
     tokens = world * B * T
     flops = FLOP_PER_TOKEN_HEAD * B * H * T
-    achieved = flops / (ms * 1e-3) / 1e12
-    traffic = None
+    traffic_db = {}
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
-        traffic = json.load(open(tp)).get("prefill_step_bytes")
-    launches_per_step = 1  # the fused tensor-core prefill is one launch per step
+        traffic_db = json.load(open(tp))
+    chunks = B * H * ((T + C - 1) // C)
+    if nlaunch == len(SPLIT_KERNELS):
+        j = max(range(nlaunch), key=lambda i: launch_ms[i])
+        kname, kflop, kbytes = SPLIT_KERNELS[j]
+        k_ms = launch_ms[j]
+        kflops, kb = kflop * chunks, kbytes * chunks
+        t_frac = kflops / (k_ms * 1e-3) / 1e12 / peaks["bf16_tflops"]
+        h_frac = kb / (k_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]
+        kinfo = traffic_db.get(kname, {})
+        if h_frac >= t_frac:
+            roof = {"bound": "hbm", "achieved": kb / (k_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": h_frac}
+        else:
+            roof = {"bound": "tensor", "achieved": kflops / (k_ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": t_frac}
+        roof["traffic"] = kinfo.get("bytes_per_launch")
+        roof["kernel"] = kname
+        roof["kernel_ms"] = k_ms
+        roof["note"] = (f"dominant kernel of {nlaunch} launches per step (ms each: "
+                        f"{', '.join(f'{SPLIT_KERNELS[i][0]} {launch_ms[i]:.3f}' for i in range(nlaunch))}); "
+                        f"algorithmic {kflop} FLOP and {kbytes} B per chunk-sequence x {chunks} chunks; "
+                        f"tensor {t_frac:.3f} / hbm {h_frac:.3f} of {peaks['src']} peaks (burst); the state "
+                        f"pass is a serial chain per sequence (latency bound); whole step "
+                        f"{flops / (ms * 1e-3) / 1e12:.1f} TFLOP/s algorithmic")
+    else:
+        achieved = flops / (ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"], "traffic": traffic_db.get("prefill_tc_kernel", {}).get(
+                    "bytes_per_launch"),
+                "note": f"algorithmic {FLOP_PER_TOKEN_HEAD} FLOP/token-head over the step ({nlaunch} launches); "
+                        f"peak {peaks['src']} burst"}
+    launches_per_step = nlaunch
     line = {
         "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -293,10 +378,7 @@ def run_ours(args):
                                "bf16 in, fp32 accumulate/state", "global_batch": world * B, "seq_len": T,
                    "heads": H, "parallelism": f"dp{world} (whole sequences per rank, no communication)",
                    "l2": "inputs 402 MB per step > 126 MB L2 (no flush needed)"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
-                     "note": f"algorithmic {FLOP_PER_TOKEN_HEAD} FLOP/token-head over the whole prefill step "
-                             f"({launches_per_step} launches); peak {peaks['src']} burst"},
+        "roofline": roof,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": launches_per_step * args.steps,
@@ -308,15 +390,38 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def run_prefill_only(n_seq: int, seq: int):
+    """Two prefill calls on seeded inputs of [n_seq, seq] (the case `ncu` captures use)."""
+    import torch
+
+    import kdn_b200
+
+    dev = torch.device("cuda", 0)
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    q, k, v, beta = prefill_inputs(dev, 7, n_heads=n_seq, seq=seq)
+    y = torch.empty(n_seq, seq, DV, device=dev, dtype=torch.bfloat16)
+    S = torch.empty(n_seq, DV, D, device=dev, dtype=torch.float32)
+    for _ in range(2):
+        kdn_b200.fused_chunked_deltanet_forward(q, k, v, beta, None, proj, C, mode="bf16", out=y, final_state=S)
+    torch.cuda.synchronize()
+    print(json.dumps({"prefill_only": [n_seq, seq], "launches_per_call": int(kdn_b200.load().kdn_prefill_launch_count()),
+                      "path": os.environ.get("KDN_PREFILL_PATH", "auto")}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-seq", type=int, default=4096, help="tokens per CPU-baseline sample (16 heads)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-only", type=int, nargs=2, metavar=("N", "T"),
+                    help="only run two prefill calls of N sequences x T tokens (for profiler captures)")
     args = ap.parse_args()
+    if args.prefill_only:
+        run_prefill_only(*args.prefill_only)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

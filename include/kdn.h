@@ -112,6 +112,17 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Measurement hook (no counterpart in the reference): the next kdn_chunked_prefill
+ * call made by this thread records events[0] (cudaEvent_t, created by the caller) on
+ * its stream before its first kernel launch and events[i] after launch i, for i <
+ * count; later calls record nothing until the hook is set again.  count = 0 disarms.
+ */
+int kdn_set_prefill_events(void* const* events, int count);
+
+/* Number of kernels the last kdn_chunked_prefill call of this thread launched. */
+int kdn_prefill_launch_count(void);
+
+/*
  * Size of the scratch array compiled into libkdn for kdn_chunked_prefill_static:
  * 64 MiB of device memory per device, reserved when the library's module is
  * loaded there.  At D = 512 that covers N*T up to 14,336 tokens (chunk 64) or

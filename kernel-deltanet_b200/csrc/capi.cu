@@ -15,6 +15,8 @@
 namespace {
 
 thread_local std::string g_last_error;
+thread_local kdn::LaunchMarks g_marks;       // armed by kdn_set_prefill_events for the next prefill
+thread_local int g_last_prefill_launches = 0;
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -169,9 +171,12 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   p.C = chunk;
   p.D = proj->D;
   const kdn::ProjParams P = kdn::make_proj_params(*proj);
-  cudaError_t e = split ? kdn::launch_split_prefill(p, P, workspace, workspace_bytes, st)
-                  : tc  ? kdn::launch_tc_prefill(p, P, st)
-                        : kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st);
+  kdn::LaunchMarks marks = g_marks;
+  g_marks = kdn::LaunchMarks();
+  cudaError_t e = split ? kdn::launch_split_prefill(p, P, workspace, workspace_bytes, st, marks)
+                  : tc  ? kdn::launch_tc_prefill(p, P, st, marks)
+                        : kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st, marks);
+  g_last_prefill_launches = marks.launches;
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return ok();
 }
@@ -204,6 +209,16 @@ int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int 
                              dv, chunk, proj, KDN_MODE_F32, scratch, scratch ? size_t(KDN_STATIC_SCRATCH_BYTES) : 0,
                              stream);
 }
+
+int kdn_set_prefill_events(void* const* events, int count) {
+  if (count < 0 || (count > 0 && !events)) return fail(KDN_ERR_INVALID, "events/count");
+  g_marks = kdn::LaunchMarks();
+  g_marks.ev = count > 0 ? reinterpret_cast<cudaEvent_t*>(const_cast<void**>(events)) : nullptr;
+  g_marks.cap = count;
+  return ok();
+}
+
+int kdn_prefill_launch_count(void) { return g_last_prefill_launches; }
 
 int kdn_decode_step(const void* q, const void* k, const void* v, int in_dtype, const void* beta, const void* decay,
                     int gate_dtype, void* states, int state_dtype, int64_t num_slots, const void* slot_mapping,

@@ -31,10 +31,27 @@ struct PrefillProblem {
   int dv, C, D;
 };
 
+// Per-launch event marks of one prefill call (measurement hook behind
+// kdn_set_prefill_events): ev[0] is recorded before the first launch and ev[i] after
+// launch i while i < cap; `launches` counts the kernels the call launched.
+struct LaunchMarks {
+  cudaEvent_t* ev = nullptr;
+  int cap = 0;
+  int launches = 0;
+  void begin(cudaStream_t s) {
+    launches = 0;
+    if (cap > 0) cudaEventRecord(ev[0], s);
+  }
+  void after(cudaStream_t s) {
+    ++launches;
+    if (launches < cap) cudaEventRecord(ev[launches], s);
+  }
+};
+
 // prefill_simt.cu: exact fp32 arithmetic on CUDA cores, three launches over a workspace.
 size_t simt_prefill_workspace(int64_t N, int64_t T, int dv, int C, int D);
 cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
-                                cudaStream_t stream);
+                                cudaStream_t stream, LaunchMarks& marks);
 
 // prefill_static.cu: device address of the library's fixed prefill scratch
 // (KDN_STATIC_SCRATCH_BYTES) on the current device, looked up on first use.
@@ -43,7 +60,7 @@ cudaError_t static_prefill_scratch(void** out);
 // prefill_tc.cu: fused tensor-core path (bf16 operands, fp32 accumulation/state),
 // one CTA per sequence; needs D=512, dv=64, C=64 and Omega exact in bf16.
 bool tc_prefill_supported(int D, int dv, int C, const ProjParams& P);
-cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cudaStream_t stream);
+cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cudaStream_t stream, LaunchMarks& marks);
 cudaError_t tc_read_error(cudaStream_t stream, int* code);
 
 // prefill_split.cu: the same arithmetic in two phases for few, long sequences -- a
@@ -51,7 +68,7 @@ cudaError_t tc_read_error(cudaStream_t stream, int* code);
 // a serial state pass per sequence.  Same shape requirements as the fused path.
 size_t split_prefill_workspace(int64_t N, int64_t T);
 cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream, LaunchMarks& marks);
 cudaError_t split_read_error(cudaStream_t stream, int* code);
 
 // ---------------------------------------------------------------- decode.cu

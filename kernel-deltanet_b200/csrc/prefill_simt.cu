@@ -348,14 +348,17 @@ size_t chain_smem_bytes(int D) {
 }
 
 template <int C>
-cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjParams& P, cudaStream_t stream) {
+cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjParams& P, cudaStream_t stream,
+                     LaunchMarks& marks) {
   cudaError_t err;
+  marks.begin(stream);
   {
     int64_t vecs = 2 * p.N * w.Tp;
     int64_t blocks = (vecs + 7) / 8;
     if (blocks > 148 * 16) blocks = 148 * 16;
     simt_lift_kernel<<<unsigned(blocks), kThreads, 0, stream>>>(p, w, P);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    marks.after(stream);
   }
   {
     const size_t smem = prep_smem_bytes<C>();
@@ -363,6 +366,7 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
     if (err != cudaSuccess) return err;
     simt_prep_kernel<C><<<dim3(w.NC, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    marks.after(stream);
   }
   {
     const size_t smem = chain_smem_bytes<C>(p.D);
@@ -370,6 +374,7 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
     if (err != cudaSuccess) return err;
     simt_chain_kernel<C><<<dim3(p.dv / kRowTile, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    marks.after(stream);
   }
   return cudaSuccess;
 }
@@ -383,12 +388,12 @@ size_t simt_prefill_workspace(int64_t N, int64_t T, int dv, int C, int D) {
 }
 
 cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, LaunchMarks& marks) {
   size_t need = 0;
   Workspace w = carve(ws, p.N, p.T, p.dv, p.C, p.D, &need);
   if (ws_bytes < need) return cudaErrorInvalidValue;
-  if (p.C == 64) return launch_c<64>(p, w, P, stream);
-  return launch_c<32>(p, w, P, stream);
+  if (p.C == 64) return launch_c<64>(p, w, P, stream, marks);
+  return launch_c<32>(p, w, P, stream, marks);
 }
 
 }  // namespace kdn

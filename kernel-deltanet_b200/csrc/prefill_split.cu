@@ -1031,7 +1031,7 @@ size_t split_prefill_workspace(int64_t N, int64_t T) {
 }
 
 cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, LaunchMarks& marks) {
   if (ws_bytes < split_prefill_workspace(p.N, p.T)) return cudaErrorInvalidValue;
   SplitArgs sa;
   sa.a.q = p.q;
@@ -1064,12 +1064,17 @@ cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, v
   if ((e = cudaFuncSetAttribute(output_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP3Smem))) !=
       cudaSuccess)
     return e;
+  marks.begin(stream);
   chunk_prep_kernel<<<grid1, kP1Thr, kP1Smem, stream>>>(sa, P);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  marks.after(stream);
   state_pass_kernel<<<unsigned(2 * p.N), kP2Thr, kP2Smem, stream>>>(sa);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  marks.after(stream);
   output_pass_kernel<<<grid1, kP3Thr, kP3Smem, stream>>>(sa);
-  return cudaGetLastError();
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  marks.after(stream);
+  return cudaSuccess;
 }
 
 cudaError_t split_read_error(cudaStream_t stream, int* code) {

@@ -590,7 +590,7 @@ bool tc_prefill_supported(int D, int dv, int C, const ProjParams& P) {
   return true;
 }
 
-cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cudaStream_t stream) {
+cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cudaStream_t stream, LaunchMarks& marks) {
   TcArgs a;
   a.q = p.q;
   a.k = p.k;
@@ -607,8 +607,11 @@ cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cuda
   a.NC = int((p.T + kC - 1) / kC);
   cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
   if (e != cudaSuccess) return e;
+  marks.begin(stream);
   prefill_tc_kernel<<<unsigned(p.N), kThr, kSmemBytes, stream>>>(a, P);
-  return cudaGetLastError();
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  marks.after(stream);
+  return cudaSuccess;
 }
 
 cudaError_t tc_read_error(cudaStream_t stream, int* code) {

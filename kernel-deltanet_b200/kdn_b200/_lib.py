@@ -57,6 +57,8 @@ SIGNATURES = {
                                    ctypes.POINTER(KdnProjection), _INT, _P, ctypes.c_size_t, _P]),
     "kdn_chunked_prefill_static": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _P, _INT, _P, _I64, _I64, _I32, _I32,
                                           ctypes.POINTER(KdnProjection), _P]),
+    "kdn_set_prefill_events": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT]),
+    "kdn_prefill_launch_count": (_INT, []),
     "kdn_decode_step": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _INT, _I64, _P, _INT, _P, _INT, _I64, _I32, _I32,
                                ctypes.POINTER(KdnProjection), _INT, _P]),
     "kdn_fork_state": (_INT, [_P, _I64, _I64, _I64, _I64, _P]),

@@ -141,3 +141,9 @@ def test_projection_buffers_match_golden(golden_dir):
             for st, d in enumerate((g["d1"], g["d2"], g["d3"])):
                 bits = sum(1 << i for i in range(64) if d[m, i] < 0)
                 assert s.sign_bits[m][st] == bits
+
+
+def test_prefill_event_hook_argument_checks(lib):
+    assert lib.kdn_set_prefill_events(None, 1) == 1
+    assert lib.kdn_set_prefill_events(None, 0) == 0
+    assert lib.kdn_prefill_launch_count() == 0
