@@ -31,6 +31,8 @@
 // independent parts ahead of time: E = T (beta (v - exp(g) s X')) = U - T' (U_k S^T).
 // Records take 233 KiB per chunk of the workspace; nothing else is allocated.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "kdn_internal.h"
 #include "tc_chunk.cuh"
@@ -50,7 +52,8 @@ constexpr uint32_t REC_Q = 0;         // 64 KiB  U_q fp16, K-major SW128: K-bloc
 constexpr uint32_t REC_UK = 65536;    // 64 KiB  U_k fp16: slice s at 16 KiB s, half h at 8 KiB h,
                                       //          [64 tokens x 64 features] SW128
 constexpr uint32_t REC_TP = 131072;   // 8 KiB   T' = T diag(beta exp(g) s_k) fp16, K-major SW128 [64 x 64]
-constexpr uint32_t REC_U = 139264;    // 16 KiB  U = T diag(beta) V fp32 row-major [64 tokens][64]
+constexpr uint32_t REC_U = 139264;    // 16 KiB  U = T diag(beta) V fp32: column half h (value columns
+                                      //          32h..32h+31) at 8 KiB h, row-major [64 tokens][32]
 constexpr uint32_t REC_AQ = 155648;   // 8 KiB   Aq fp16 K-major SW128 [64 rows x 64]
 constexpr uint32_t REC_VEC = 163840;  // 1 KiB   ew[64] = exp(g_{C-1} - g_j) s_kj, yqs[64] = s_qi exp(g_{i-1}),
                                       //          eC = exp(g_{C-1})
@@ -63,11 +66,58 @@ constexpr uint32_t REC_BYTES = 238592;
 struct SplitArgs {
   TcArgs a;
   int64_t N;
-  uint8_t* ws;  // N * NC records, chunk-major: record (c, n) at (c N + n) REC_BYTES
+  uint8_t* ws;       // N * NC records, chunk-major: record (c, n) at (c N + n) REC_BYTES
+  uint32_t* abort;   // persistent launch: set by any wait that gives up, so that every other
+                     // wait gives up at once (nullptr for the separate launches)
 };
 
 __device__ __forceinline__ uint8_t* record(const SplitArgs& sa, int64_t c, int64_t n) {
   return sa.ws + (c * sa.N + n) * int64_t(REC_BYTES);
+}
+
+__device__ __forceinline__ bool aborted(const uint32_t* abort) {
+  return abort && *reinterpret_cast<const volatile uint32_t*>(abort) != 0u;
+}
+__device__ __forceinline__ void set_abort(uint32_t* abort) {
+  if (abort) atomicExch(abort, 1u);
+}
+
+// bounded mbarrier wait of this path; gives up early once another wait has given up
+__device__ __forceinline__ bool split_wait(uint64_t* bar, uint32_t parity, uint32_t* abort) {
+  for (uint32_t i = 0; i < kWaitLimit; i += 1024) {
+    for (int j = 0; j < 1024; ++j)
+      if (tc::mbar_try_wait(bar, parity)) return true;
+    if (aborted(abort)) return false;
+  }
+  set_abort(abort);
+  return false;
+}
+
+// ---- hand-over flags between the phases of the persistent launch (global memory)
+constexpr uint32_t kFlagSpins = 1u << 24;  // bounded: ~10 s of polling at most
+// wait until *flag >= target (acquire at GPU scope)
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t target, uint32_t* abort) {
+  for (uint32_t i = 0; i < kFlagSpins; ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v >= target) return true;
+    if ((i & 63u) == 63u && aborted(abort)) return false;
+    __nanosleep(64);
+  }
+  set_abort(abort);
+  return false;
+}
+// completed writes of this thread (generic, and bulk copies already waited for) are ordered
+// before *flag = v at GPU scope
+__device__ __forceinline__ void publish_store(uint32_t* flag, uint32_t v) {
+  tc::fence_proxy_async_global();
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+// the same for writes made by other threads of the CTA that synchronised with this one
+__device__ __forceinline__ void publish_flag(uint32_t* flag, uint32_t v) {
+  tc::fence_proxy_async_global();
+  __threadfence();
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
 }
 
 // ================================================================ phase 1
@@ -136,14 +186,11 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
   tc::named_bar_sync(1, kP1Threads);
 }
 
-__global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, ProjParams P) {
+// Phase 1 on CTAs cta = 0..ncta-1 (544 threads, `tmem` = 512 allocated columns).  With
+// rec_ready, each finished record is published there (1) for the state pass.
+__device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams& P, uint8_t* sm, uint32_t tmem,
+                                          int64_t cta, int64_t ncta, uint32_t* rec_ready, bool& ok) {
   const TcArgs& a = sa.a;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm;
-  {
-    const uint32_t s = tc::smem_u32(smem_raw);
-    sm = smem_raw + ((1024u - (s & 1023u)) & 1023u);
-  }
   const uint32_t sbase = tc::smem_u32(sm);
   float* Am = reinterpret_cast<float*>(sm + P1_F);
   float* Es = reinterpret_cast<float*>(sm + P1_F + 16384);
@@ -164,7 +211,6 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
   uint64_t* bar_ops = reinterpret_cast<uint64_t*>(sm + P1_BAR + 40);
   uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);   // U staged
   uint64_t* bar_stfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 64);  // staged tiles copied out
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P1_BAR + 72);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cq = (warp >> 2) & 3;
@@ -174,12 +220,7 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
   const bool decayed = a.decay != nullptr;
   const int64_t N = sa.N;
   const int64_t total = N * a.NC;
-  bool ok = true;
 
-  if (warp == 0) {
-    tc::tmem_alloc(tslot, 512);
-    tc::tmem_relinquish();
-  }
   if (tid == 0) {
     tc::mbar_init(&bar_lift[0], 1);
     tc::mbar_init(&bar_lift[1], 1);
@@ -195,13 +236,12 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
   }
   build_omega(sm + P1_OMG, P, warp, lane, kP1Thr / 32);
   for (int i = tid; i < kD; i += kP1Thr) ph[i] = P.phase[i];
-  if (warp < kP1Warps && bf_in && blockIdx.x < total)
-    prefetch_kq(a, int64_t(blockIdx.x) % N, int(int64_t(blockIdx.x) / N), sbase + P1_XIN, tid);
+  if (warp < kP1Warps && bf_in && cta < total)
+    prefetch_kq(a, int64_t(cta) % N, int(int64_t(cta) / N), sbase + P1_XIN, tid);
   tc::cp_async_commit();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = *tslot;
 
   if (warp == kP1Issuer) {
     // ================================================================ MMA issuer
@@ -217,19 +257,19 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
                      tc::smem_desc_sw128(sbase + P1_OMG + s * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
         tc::mma_commit(&bar_lift[s & 1]);
       };
-      for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x) {
+      for (int64_t idx = cta; idx < total; idx += ncta) {
         uint8_t* rec = record(sa, idx / N, idx % N);
-        ok &= tc::mbar_wait_bounded(bar_xin, p_xin, kWaitLimit);
+        ok &= split_wait(bar_xin, p_xin, sa.abort);
         p_xin ^= 1;
         tc::fence_after_sync();
         lift(0);
         lift(1);
         for (int s = 0; s < kSlices; ++s) {
-          ok &= tc::mbar_wait_bounded(&bar_zfree[s & 1], p_zfree[s & 1], kWaitLimit);  // slot s & 1 read by all
+          ok &= split_wait(&bar_zfree[s & 1], p_zfree[s & 1], sa.abort);  // slot s & 1 read by all
           p_zfree[s & 1] ^= 1;
           tc::fence_after_sync();
           if (s + 2 < kSlices) lift(s + 2);
-          ok &= tc::mbar_wait_bounded(bar_fready, p_fready, kWaitLimit);
+          ok &= split_wait(bar_fready, p_fready, sa.abort);
           p_fready ^= 1;
           tc::fence_after_sync();
 #pragma unroll
@@ -246,7 +286,7 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
           tc::bulk_store(rec + REC_UK + s * 16384, sbase + P1_UK + s * 16384, 16384);  // read by the chunk's end
           tc::bulk_commit();
         }
-        ok &= tc::mbar_wait_bounded(bar_ops, p_ops, kWaitLimit);
+        ok &= split_wait(bar_ops, p_ops, sa.abort);
         p_ops ^= 1;
         tc::fence_after_sync();
 #pragma unroll
@@ -256,11 +296,16 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
         tc::mma_commit(bar_mma);
         tc::bulk_store(rec + REC_TP, sbase + P1_TOP, 8192);  // T' = rows 0..63 of the A operand
         tc::bulk_commit();
-        ok &= tc::mbar_wait_bounded(bar_wdone, p_wdone, kWaitLimit);
+        ok &= split_wait(bar_wdone, p_wdone, sa.abort);
         p_wdone ^= 1;
         tc::bulk_store(rec + REC_U, sbase + P1_F, 16384);
         tc::bulk_commit();
-        tc::bulk_wait_read();  // the staging tiles are free for the next chunk
+        if (rec_ready) {  // the whole record is in memory: publish it
+          tc::bulk_wait_all();
+          publish_flag(rec_ready + idx, 1u);
+        } else {
+          tc::bulk_wait_read();  // the staging tiles are free for the next chunk
+        }
         tc::mbar_arrive(bar_stfree);
       }
       tc::bulk_wait_all();
@@ -270,13 +315,13 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
     // ================================================================ compute warps
     uint32_t ph_lift[2] = {0, 0}, ph_mma = 0, ph_st = 0;
     auto wait_mma = [&]() {
-      ok &= tc::mbar_wait_bounded(bar_mma, ph_mma, kWaitLimit);
+      ok &= split_wait(bar_mma, ph_mma, sa.abort);
       ph_mma ^= 1;
       tc::fence_after_sync();
     };
     float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};  // gates of the coming chunk (warp 0)
-    if (warp == 0 && blockIdx.x < total) {
-      const int64_t n0 = int64_t(blockIdx.x) % N, t00 = (int64_t(blockIdx.x) / N) * kC;
+    if (warp == 0 && cta < total) {
+      const int64_t n0 = int64_t(cta) % N, t00 = (int64_t(cta) / N) * kC;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int64_t tt = t00 + 2 * lane + e;
@@ -286,9 +331,9 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
         }
       }
     }
-    for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x) {
+    for (int64_t idx = cta; idx < total; idx += ncta) {
       const int64_t n = idx % N, c = idx / N, t0 = c * kC;
-      const int64_t nidx = idx + gridDim.x;
+      const int64_t nidx = idx + ncta;
       const bool has_next = nidx < total;
       const int64_t nn = nidx % N, ncn = nidx / N;
       uint8_t* rec = record(sa, c, n);
@@ -362,7 +407,7 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
       float ss = 0.f;
 #pragma unroll 1
       for (int s = 0; s < kSlices; ++s) {
-        ok &= tc::mbar_wait_bounded(&bar_lift[s & 1], ph_lift[s & 1], kWaitLimit);
+        ok &= split_wait(&bar_lift[s & 1], ph_lift[s & 1], sa.abort);
         ph_lift[s & 1] ^= 1;
         tc::fence_after_sync();
         float z[32];
@@ -388,8 +433,8 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
         }
         if (s > 0) {
           wait_mma();  // the previous slice's Gram product and copy-out are done with F
-        } else if (idx != blockIdx.x) {  // the previous chunk's staged tiles have been copied out
-          ok &= tc::mbar_wait_bounded(bar_stfree, ph_st, kWaitLimit);
+        } else if (idx != cta) {  // the previous chunk's staged tiles have been copied out
+          ok &= split_wait(bar_stfree, ph_st, sa.abort);
           ph_st ^= 1;
         }
         {
@@ -522,21 +567,22 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
         float u[16];
         tc::tmem_ld16(tmem + lane_off + P1_U + 16 * cq, u);
         tc::tmem_ld_wait();
-        float4* dst = reinterpret_cast<float4*>(sm + P1_F + ((trow - 64) * 64 + 16 * cq) * 4);
+        float4* dst =
+            reinterpret_cast<float4*>(sm + P1_F + (cq >> 1) * 8192 + ((trow - 64) * 32 + 16 * (cq & 1)) * 4);
 #pragma unroll
         for (int m = 0; m < 4; ++m) dst[m] = make_float4(u[4 * m], u[4 * m + 1], u[4 * m + 2], u[4 * m + 3]);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
+      if (rec_ready) __threadfence();  // this thread's record stores (Aq, factors) before the publication
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_wdone);
     }
     tc::cp_async_wait_all();
   }
-  if (!ok) record_device_error(&g_split_error, 3);
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 512);
+  tc::fence_after_sync();
 }
 
 // ================================================================ phase 2
@@ -561,24 +607,25 @@ constexpr uint32_t P2_Y = 128;  // Y = U_k S^T (lanes 0..63 = k tokens), 32 cols
 constexpr uint32_t P2_X = 160;  // X = T' Y, 32 cols
 
 // shared memory (phase 2)
-constexpr int kRing = 5;              // 32 KiB stages; items: U_k slices (0,1), (2,3) of each chunk
-constexpr uint32_t P2_RING = 0;       // 160 KiB
-constexpr uint32_t P2_TP = 163840;    // 2 x 8 KiB T' (fp16, K-major [64 x 64])
-constexpr uint32_t P2_SOP = 180224;   // 32 KiB S^T operand (fp16, MN-major SW64 [512 x 32]), slice s at 8 KiB s
-constexpr uint32_t P2_YB = 212992;    // 4 KiB  Y (fp16, MN-major SW64 [64 x 32])
-constexpr uint32_t P2_EB = 217088;    // 4 KiB  E'' (fp16, MN-major SW64)
-constexpr uint32_t P2_ET = 221184;    // 4 KiB  E (fp16, MN-major SW64), copied to the record
-constexpr uint32_t P2_BAR = 225280;
+constexpr int kRing = 4;              // 32 KiB stages; items: U_k slices (0,1), (2,3) of each chunk
+constexpr uint32_t P2_RING = 0;       // 128 KiB
+constexpr uint32_t P2_TP = 131072;    // 2 x 8 KiB T' (fp16, K-major [64 x 64])
+constexpr uint32_t P2_FAC = 147456;   // 2 x 9 KiB per-chunk factors: the CTA's half of U (fp32 [64][32]),
+constexpr uint32_t P2_FAC_BYTES = 9216;  //   then ew[64], yqs[64], eC
+constexpr uint32_t P2_SOP = 165888;   // 32 KiB S^T operand (fp16, MN-major SW64 [512 x 32]), slice s at 8 KiB s
+constexpr uint32_t P2_YB = 198656;    // 4 KiB  Y (fp16, MN-major SW64 [64 x 32])
+constexpr uint32_t P2_EB = 202752;    // 4 KiB  E'' (fp16, MN-major SW64)
+constexpr uint32_t P2_ET = 206848;    // 4 KiB  E (fp16, MN-major SW64), copied to the record
+constexpr uint32_t P2_BAR = 210944;
 constexpr uint32_t kP2Smem = P2_BAR + 256 + 1024;
 
-__global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
+// Phase 2 on CTA cta (sequence cta / 2, value columns 32 (cta % 2)..+31; warps 0..8 work,
+// others idle; `tmem` >= 256 allocated columns).  With rec_ready it waits for each record
+// to be published; with out_prog it publishes, per sequence and column half, how many
+// chunks have their entering state and E in the records.
+__device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uint32_t tmem, int64_t cta,
+                                           const uint32_t* rec_ready, uint32_t* out_prog, bool& ok) {
   const TcArgs& a = sa.a;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm;
-  {
-    const uint32_t s = tc::smem_u32(smem_raw);
-    sm = smem_raw + ((1024u - (s & 1023u)) & 1023u);
-  }
   const uint32_t sbase = tc::smem_u32(sm);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P2_BAR);
   uint64_t* ring_full = bars;       // [5] stage loaded (bytes)
@@ -589,19 +636,16 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
   uint64_t* bar_x = bars + 15;      // X done (MMA commit)
   uint64_t* bar_s = bars + 16;      // [2] state update of slices 2p, 2p+1 done (MMA commit; for p = 0
                                     //     also the record copies have read their tiles)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* fac_full = bars + 18;   // [2] factors of the chunk loaded (bytes)
+  uint64_t* fac_empty = bars + 20;  // [2] factors copied to registers (8 compute warps)
+
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t n = blockIdx.x >> 1;
-  const int half = blockIdx.x & 1;
+  const int64_t n = cta >> 1;
+  const int half = int(cta & 1);
   const int col0 = kHalf * half;  // first value column of this CTA
   const int NC = a.NC;
-  bool ok = true;
 
-  if (warp == 0) {
-    tc::tmem_alloc(tslot, 256);
-    tc::tmem_relinquish();
-  }
   if (tid == 0) {
     for (int b = 0; b < kRing; ++b) {
       tc::mbar_init(&ring_full[b], 1);
@@ -615,24 +659,31 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
     tc::mbar_init(bar_x, 1);
     tc::mbar_init(&bar_s[0], 1);
     tc::mbar_init(&bar_s[1], 1);
+    for (int u = 0; u < 2; ++u) {
+      tc::mbar_init(&fac_full[u], 1);
+      tc::mbar_init(&fac_empty[u], kP2Warps);
+    }
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = *tslot;
 
   if (warp == kP2Producer) {
     // ================================================================ bulk loads
     if (lane == 0) {
-      uint32_t pe[kRing] = {}, pt[2] = {0, 0};
+      uint32_t pe[kRing] = {}, pt[2] = {0, 0}, pfe[2] = {0, 0};
       int64_t g = 0;  // ring items so far
       for (int c = 0; c < NC; ++c) {
         const uint8_t* rec = record(sa, c, n);
+        if (rec_ready) {  // the record has been published by the preparation pass
+          ok &= wait_flag(rec_ready + int64_t(c) * sa.N + n, 1u, sa.abort);
+          tc::fence_proxy_async_global();
+        }
         for (int p = 0; p < 2; ++p, ++g) {  // U_k slices 2p, 2p+1
           const int b = int(g % kRing);
           if (g >= kRing) {
-            ok &= tc::mbar_wait_bounded(&ring_empty[b], pe[b], kWaitLimit);
+            ok &= split_wait(&ring_empty[b], pe[b], sa.abort);
             pe[b] ^= 1;
           }
           tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
@@ -641,15 +692,20 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
         }
         const int u = c & 1;
         if (c >= 2) {
-          ok &= tc::mbar_wait_bounded(&tp_empty[u], pt[u], kWaitLimit);
+          ok &= split_wait(&tp_empty[u], pt[u], sa.abort);
           pt[u] ^= 1;
+          ok &= split_wait(&fac_empty[u], pfe[u], sa.abort);
+          pfe[u] ^= 1;
         }
         tc::mbar_arrive_expect_tx(&tp_full[u], 8192);
         tc::bulk_load(sbase + P2_TP + u * 8192, rec + REC_TP, 8192, &tp_full[u]);
+        tc::mbar_arrive_expect_tx(&fac_full[u], 8192 + 1024);
+        tc::bulk_load(sbase + P2_FAC + u * P2_FAC_BYTES, rec + REC_U + half * 8192, 8192, &fac_full[u]);
+        tc::bulk_load(sbase + P2_FAC + u * P2_FAC_BYTES + 8192, rec + REC_VEC, 1024, &fac_full[u]);
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < kP2Warps) {
     // ================================================================ compute warps (+ leader)
     const int quarter = warp & 3, ch = warp >> 2;  // TMEM lane quarter, 16-column half of the CTA's 32
     const int trow = quarter * 32 + lane;
@@ -678,22 +734,7 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
     }
     tc::tmem_st_wait();
     uint32_t py = 0, px = 0, ps[2] = {0, 0};
-    // per-chunk factors, loaded one chunk ahead
-    float urow[16], ew = 0.f, eC = 1.f;
-    auto load_factors = [&](int c) {
-      const uint8_t* rec = record(sa, c, n);
-      const float* vec = reinterpret_cast<const float*>(rec + REC_VEC);
-      if (trow < 64) {
-        const float4* u4 = reinterpret_cast<const float4*>(rec + REC_U + (trow * 64 + cbase) * 4);
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const float4 x = u4[m];
-          urow[4 * m] = x.x, urow[4 * m + 1] = x.y, urow[4 * m + 2] = x.z, urow[4 * m + 3] = x.w;
-        }
-        ew = vec[trow];
-      }
-      eC = vec[128];
-    };
+    uint32_t pff[2] = {0, 0};
     auto store_tile = [&](uint32_t off, const float* v, float w) {  // 16 values of row trow, fp16 SW64
 #pragma unroll
       for (int m = 0; m < 2; ++m)
@@ -709,17 +750,32 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       tc::fence_after_sync();
     };
     auto wait_mma = [&](uint64_t* bar, uint32_t& phase) {
-      ok &= tc::mbar_wait_bounded(bar, phase, kWaitLimit);
+      ok &= split_wait(bar, phase, sa.abort);
       phase ^= 1;
       tc::fence_after_sync();
     };
-    load_factors(0);
     for (int c = 0; c < NC; ++c) {
       uint8_t* rec = record(sa, c, n);
-      float cu[16];
+      // ---------------------------------------- the chunk's factors (shared memory -> registers)
+      float cu[16], cew = 0.f, ceC;
+      {
+        const int u = c & 1;
+        ok &= split_wait(&fac_full[u], pff[u], sa.abort);
+        pff[u] ^= 1;
+        const float* fac = reinterpret_cast<const float*>(sm + P2_FAC + u * P2_FAC_BYTES);
+        if (trow < 64) {
+          const float4* u4 = reinterpret_cast<const float4*>(fac + trow * 32 + 16 * ch);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) cu[j] = urow[j];
-      const float cew = ew, ceC = eC;
+          for (int m = 0; m < 4; ++m) {
+            const float4 x = u4[m];
+            cu[4 * m] = x.x, cu[4 * m + 1] = x.y, cu[4 * m + 2] = x.z, cu[4 * m + 3] = x.w;
+          }
+          cew = fac[2048 + trow];
+        }
+        ceC = fac[2048 + 128];
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&fac_empty[u]);
+      }
       // ---------------------------------------- per slice pair: state operand (fp16), decay, Y
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
@@ -743,7 +799,7 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
         if (leader) {  // Y += U_k S^T over the features of slices 2p, 2p+1
           const int b = int(g % kRing);
           st[p] = b;
-          ok &= tc::mbar_wait_bounded(&ring_full[b], pf[b], kWaitLimit);
+          ok &= split_wait(&ring_full[b], pf[b], sa.abort);
           pf[b] ^= 1;
           ++g;
           tc::fence_after_sync();
@@ -762,13 +818,16 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
                            p > 0 || h > 0 || kb > 0 || kk > 0);
           if (p == 1) {
             tc::mma_commit(bar_y);
+            if (out_prog && c > 0) {  // while Y runs: chunks 0..c-1 of this half are in the record
+              tc::bulk_wait_all();
+              publish_store(out_prog + 2 * n + half, uint32_t(c));
+            }
             tc::bulk_store(rec + REC_S0 + half * 32768, sbase + P2_SOP, 32768);  // the state entering the chunk
             tc::bulk_commit();
           }
         }
         __syncwarp();
       }
-      if (c + 1 < NC) load_factors(c + 1);  // in flight while the products run
       // ---------------------------------------- Y (fp16), then X = T' Y
       wait_mma(bar_y, py);
       if (trow < 64) {
@@ -780,7 +839,7 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       step_done();
       const int u = c & 1;
       if (leader) {
-        ok &= tc::mbar_wait_bounded(&tp_full[u], pt[u], kWaitLimit);
+        ok &= split_wait(&tp_full[u], pt[u], sa.abort);
         pt[u] ^= 1;
         tc::fence_after_sync();
         const uint64_t da = tc::desc_add(d_tp, uint32_t(u) * 8192);
@@ -806,6 +865,7 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       if (leader) {
         tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET, 4096);
         tc::bulk_commit();
+
         for (int p = 0; p < 2; ++p) {  // S_s^T += U_k,s^T E'' for s = 2p, 2p+1
           const uint64_t da = tc::desc_add(d_ringT, uint32_t(st[p]) * 32768);
 #pragma unroll
@@ -823,7 +883,10 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
     }
     wait_mma(&bar_s[0], ps[0]);
     wait_mma(&bar_s[1], ps[1]);
-    if (leader) tc::bulk_wait_all();
+    if (leader) {
+      tc::bulk_wait_all();
+      if (out_prog) publish_store(out_prog + 2 * n + half, uint32_t(NC));
+    }
     // ---------------------------------------- final state
 #pragma unroll
     for (int s = 0; s < kSlices; ++s) {
@@ -834,10 +897,6 @@ __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
       for (int j = 0; j < 16; ++j) a.S_out[(n * kDV + cbase + j) * kD + 128 * s + trow] = v[j];
     }
   }
-  if (!ok) record_device_error(&g_split_error, 3);
-  tc::fence_before_sync();
-  __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 256);
 }
 
 // ================================================================ phase 3
@@ -850,36 +909,28 @@ constexpr int kP3Thr = 128;  // warp 0 issues, warp 1 loads, warps 2 and 3 (the 
 
 // shared memory (phase 3)
 constexpr uint32_t P3_RING = 8192;     // 5 x 32 KiB; [U_q kb 2s | U_q kb 2s+1 | S half 0 | S half 1], 8 KiB each
-constexpr uint32_t P3_SMALL = 172032;  // 2 x 16 KiB: [Aq 8 KiB | E half 0 | E half 1]
-constexpr uint32_t P3_BAR = 204800;
+constexpr uint32_t P3_SMALL = 172032;  // 2 x 17 KiB: [Aq 8 KiB | E half 0 | E half 1 | yqs]
+constexpr uint32_t P3_SMALL_BYTES = 17408;
+constexpr uint32_t P3_BAR = 206848;
 constexpr uint32_t kP3Smem = P3_BAR + 256 + 1024;
 
-__global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
+// Phase 3 on CTAs cta = 0..ncta-1 (warps 0..3 work, others idle; `tmem` >= 256 columns).
+// With out_prog it waits until both column halves of the state pass are past each chunk.
+__device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, uint32_t tmem, int64_t cta,
+                                            int64_t ncta, const uint32_t* out_prog, bool& ok) {
   const TcArgs& a = sa.a;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm;
-  {
-    const uint32_t s = tc::smem_u32(smem_raw);
-    sm = smem_raw + ((1024u - (s & 1023u)) & 1023u);
-  }
   const uint32_t sbase = tc::smem_u32(sm);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P3_BAR);
   uint64_t* ring_full = bars;        // [5]
   uint64_t* ring_empty = bars + 5;   // [5]
   uint64_t* small_full = bars + 10;  // [2]
-  uint64_t* small_empty = bars + 12; // [2]
+  uint64_t* small_empty = bars + 12; // [2] small item u read by the MMAs and by the epilogue (2 warps)
   uint64_t* acc_full = bars + 14;    // [2] accumulator buffer u complete (MMA commit)
   uint64_t* acc_free = bars + 16;    // [2] accumulator buffer u read (2 epilogue warps)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t N = sa.N;
   const int64_t total = N * a.NC;
-  bool ok = true;
-  if (warp == 0) {
-    tc::tmem_alloc(tslot, 256);
-    tc::tmem_relinquish();
-  }
   if (tid == 0) {
     for (int b = 0; b < kRing; ++b) {
       tc::mbar_init(&ring_full[b], 1);
@@ -887,7 +938,7 @@ __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
     }
     for (int u = 0; u < 2; ++u) {
       tc::mbar_init(&small_full[u], 1);
-      tc::mbar_init(&small_empty[u], 1);
+      tc::mbar_init(&small_empty[u], 2);
       tc::mbar_init(&acc_full[u], 1);
       tc::mbar_init(&acc_free[u], 2);
     }
@@ -896,19 +947,24 @@ __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = *tslot;
 
   if (warp == 1) {
     // ================================================================ bulk loads
     if (lane == 0) {
       uint32_t pe[kRing] = {}, ps[2] = {0, 0};
       int64_t g = 0, j = 0;
-      for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x, ++j) {
+      for (int64_t idx = cta; idx < total; idx += ncta, ++j) {
         const uint8_t* rec = record(sa, idx / N, idx % N);
+        if (out_prog) {  // both column halves of the state pass are done with this chunk
+          const uint32_t need = uint32_t(idx / N) + 1u;
+          ok &= wait_flag(out_prog + 2 * (idx % N), need, sa.abort);
+          ok &= wait_flag(out_prog + 2 * (idx % N) + 1, need, sa.abort);
+          tc::fence_proxy_async_global();
+        }
         for (int s = 0; s < kSlices; ++s, ++g) {
           const int b = int(g % kRing);
           if (g >= kRing) {
-            ok &= tc::mbar_wait_bounded(&ring_empty[b], pe[b], kWaitLimit);
+            ok &= split_wait(&ring_empty[b], pe[b], sa.abort);
             pe[b] ^= 1;
           }
           const uint32_t dst = sbase + P3_RING + b * 32768;
@@ -920,13 +976,14 @@ __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
         }
         const int u = int(j & 1);
         if (j >= 2) {
-          ok &= tc::mbar_wait_bounded(&small_empty[u], ps[u], kWaitLimit);
+          ok &= split_wait(&small_empty[u], ps[u], sa.abort);
           ps[u] ^= 1;
         }
-        const uint32_t dst = sbase + P3_SMALL + u * 16384;
-        tc::mbar_arrive_expect_tx(&small_full[u], 16384);
+        const uint32_t dst = sbase + P3_SMALL + u * P3_SMALL_BYTES;
+        tc::mbar_arrive_expect_tx(&small_full[u], 16384 + 256);
         tc::bulk_load(dst, rec + REC_AQ, 8192, &small_full[u]);
         tc::bulk_load(dst + 8192, rec + REC_E, 8192, &small_full[u]);
+        tc::bulk_load(dst + 16384, rec + REC_VEC + 256, 256, &small_full[u]);  // yqs
       }
     }
     __syncwarp();
@@ -936,17 +993,17 @@ __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
       const uint32_t id = tc::idesc_f16_f32(128, 64, false, true);
       uint32_t pf[kRing] = {}, psf[2] = {0, 0}, pfree[2] = {0, 0};
       int64_t g = 0, j = 0;
-      for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x, ++j) {
+      for (int64_t idx = cta; idx < total; idx += ncta, ++j) {
         const int u = int(j & 1);
         if (j >= 2) {  // the epilogue of chunk j - 2 has read accumulator buffer u
-          ok &= tc::mbar_wait_bounded(&acc_free[u], pfree[u], kWaitLimit);
+          ok &= split_wait(&acc_free[u], pfree[u], sa.abort);
           pfree[u] ^= 1;
         }
         tc::fence_after_sync();
         const uint32_t dq = tmem + 128 * u, de = dq + 64;
         for (int s = 0; s < kSlices; ++s, ++g) {
           const int b = int(g % kRing);
-          ok &= tc::mbar_wait_bounded(&ring_full[b], pf[b], kWaitLimit);
+          ok &= split_wait(&ring_full[b], pf[b], sa.abort);
           pf[b] ^= 1;
           tc::fence_after_sync();
           const uint32_t st = sbase + P3_RING + b * 32768;
@@ -962,32 +1019,33 @@ __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
             }
           tc::mma_commit(&ring_empty[b]);
         }
-        ok &= tc::mbar_wait_bounded(&small_full[u], psf[u], kWaitLimit);
+        ok &= split_wait(&small_full[u], psf[u], sa.abort);
         psf[u] ^= 1;
         tc::fence_after_sync();
-        const uint32_t sm_small = sbase + P3_SMALL + u * 16384;
+        const uint32_t sm_small = sbase + P3_SMALL + u * P3_SMALL_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           tc::mma_ss(de, tc::smem_desc_sw128(sm_small - 8192 + 32 * kk, 16, 1024),
                      tc::smem_desc_sw64(sm_small + 8192 + 16 * kk * 64, 4096, 512), id, kk > 0);
-        tc::mma_commit(&small_empty[u]);
         tc::mma_commit(&acc_full[u]);
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < 4) {
     // ================================================================ epilogue (q-row lanes)
     const uint32_t lane_off = uint32_t(warp * 32) << 16;  // warps 2, 3: lanes 64..127
     const int i = (warp - 2) * 32 + lane;                  // token row within the chunk
     uint32_t pa[2] = {0, 0};
     int64_t j = 0;
-    for (int64_t idx = blockIdx.x; idx < total; idx += gridDim.x, ++j) {
+    for (int64_t idx = cta; idx < total; idx += ncta, ++j) {
       const int64_t c = idx / N, n = idx % N;
       const int u = int(j & 1);
-      const float yqs = reinterpret_cast<const float*>(record(sa, c, n) + REC_VEC)[64 + i];
-      ok &= tc::mbar_wait_bounded(&acc_full[u], pa[u], kWaitLimit);
+      ok &= split_wait(&acc_full[u], pa[u], sa.abort);
       pa[u] ^= 1;
       tc::fence_after_sync();
+      const float yqs = reinterpret_cast<const float*>(sm + P3_SMALL + u * P3_SMALL_BYTES + 16384)[i];
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&small_empty[u]);
       const int64_t t = c * kC + i;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -1017,17 +1075,92 @@ __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
       if (lane == 0) tc::mbar_arrive(&acc_free[u]);
     }
   }
+}
+
+
+// ================================================================ kernels
+// One shared-memory size for all launches of this path (the largest role); the TMEM
+// address slot sits above every role's layout.
+constexpr uint32_t kSplitTslot = 225536;
+constexpr uint32_t kSplitSmem = kSplitTslot + 16 + 1024;
+static_assert(kSplitTslot >= P2_BAR + 8 * 20 && kSplitTslot >= P1_BAR + 112 && kSplitTslot >= P3_BAR + 8 * 18,
+              "TMEM slot overlaps a role's barriers");
+
+__device__ __forceinline__ uint8_t* split_smem() {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t s = tc::smem_u32(smem_raw);
+  return smem_raw + ((1024u - (s & 1023u)) & 1023u);
+}
+
+__device__ __forceinline__ uint32_t split_tmem_alloc(uint8_t* sm, uint32_t cols) {
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kSplitTslot);
+  if ((threadIdx.x >> 5) == 0) {
+    tc::tmem_alloc(tslot, cols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  return *tslot;
+}
+
+__device__ __forceinline__ void split_finish(uint32_t tmem, uint32_t cols, bool ok) {
   if (!ok) record_device_error(&g_split_error, 3);
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 256);
+  if ((threadIdx.x >> 5) == 0) tc::tmem_dealloc(tmem, cols);
+}
+
+__global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, ProjParams P) {
+  uint8_t* sm = split_smem();
+  const uint32_t tmem = split_tmem_alloc(sm, 512);
+  bool ok = true;
+  prep_role(sa, P, sm, tmem, blockIdx.x, gridDim.x, nullptr, ok);
+  split_finish(tmem, 512, ok);
+}
+
+__global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
+  uint8_t* sm = split_smem();
+  const uint32_t tmem = split_tmem_alloc(sm, 256);
+  bool ok = true;
+  state_role(sa, sm, tmem, blockIdx.x, nullptr, nullptr, ok);
+  split_finish(tmem, 256, ok);
+}
+
+__global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
+  uint8_t* sm = split_smem();
+  const uint32_t tmem = split_tmem_alloc(sm, 256);
+  bool ok = true;
+  output_role(sa, sm, tmem, blockIdx.x, gridDim.x, nullptr, ok);
+  split_finish(tmem, 256, ok);
+}
+
+// All three phases in one cooperative launch (one CTA per SM, all resident): CTAs
+// 0..n_state-1 run the state pass while the others prepare the records it waits for and
+// then produce the outputs of the chunks it has finished.  Hand-over through the
+// per-chunk flags (zeroed before the launch); every wait on them is bounded.
+__global__ void __launch_bounds__(kP1Thr, 1) split_persistent_kernel(SplitArgs sa, ProjParams P, uint32_t* rec_ready,
+                                                                      uint32_t* out_prog, int n_state) {
+  uint8_t* sm = split_smem();
+  const uint32_t tmem = split_tmem_alloc(sm, 512);
+  bool ok = true;
+  if (int(blockIdx.x) < n_state) {
+    state_role(sa, sm, tmem, blockIdx.x, rec_ready, out_prog, ok);
+  } else {
+    const int64_t cta = int64_t(blockIdx.x) - n_state, ncta = int64_t(gridDim.x) - n_state;
+    prep_role(sa, P, sm, tmem, cta, ncta, rec_ready, ok);
+    output_role(sa, sm, tmem, cta, ncta, out_prog, ok);
+  }
+  split_finish(tmem, 512, ok);
 }
 
 }  // namespace
 
+// records, then the hand-over words of the persistent launch: one per record, two per
+// sequence, the abort word
 size_t split_prefill_workspace(int64_t N, int64_t T) {
   const int64_t NC = (T + kC - 1) / kC;
-  return size_t(N) * size_t(NC) * REC_BYTES;
+  return size_t(N) * size_t(NC) * REC_BYTES + ((size_t(N) * (size_t(NC) + 2) * 4 + 4 + 255) & ~size_t(255));
 }
 
 cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
@@ -1049,29 +1182,48 @@ cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, v
   sa.a.NC = int((p.T + kC - 1) / kC);
   sa.N = p.N;
   sa.ws = static_cast<uint8_t*>(ws);
-  int dev = 0, sms = 0;
+  sa.abort = nullptr;
+  int dev = 0, sms = 0, coop = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess) return e;
   const int64_t total = p.N * int64_t(sa.a.NC);
+  for (const void* f : {(const void*)chunk_prep_kernel, (const void*)state_pass_kernel, (const void*)output_pass_kernel,
+                        (const void*)split_persistent_kernel})
+    if ((e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSplitSmem))) != cudaSuccess)
+      return e;
+  // one launch for all phases when every CTA fits at once and the state pass leaves SMs
+  // for the other two (KDN_SPLIT_PERSISTENT=0 forces the three launches)
+  const int n_state = int(2 * p.N);
+  int per_sm = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, split_persistent_kernel, kP1Thr, kSplitSmem)) !=
+      cudaSuccess)
+    return e;
+  const char* env = getenv("KDN_SPLIT_PERSISTENT");
+  const bool persistent = coop && per_sm >= 1 && n_state + 8 <= sms && !(env && strcmp(env, "0") == 0);
+  if (persistent) {
+    uint32_t* rec_ready = reinterpret_cast<uint32_t*>(sa.ws + size_t(total) * REC_BYTES);
+    uint32_t* out_prog = rec_ready + total;
+    sa.abort = out_prog + 2 * p.N;
+    if ((e = cudaMemsetAsync(rec_ready, 0, (size_t(total) + 2 * p.N + 1) * 4, stream)) != cudaSuccess) return e;
+    marks.begin(stream);
+    void* args[] = {&sa, const_cast<ProjParams*>(&P), &rec_ready, &out_prog, const_cast<int*>(&n_state)};
+    if ((e = cudaLaunchCooperativeKernel((const void*)split_persistent_kernel, dim3(unsigned(sms)), dim3(kP1Thr), args,
+                                         kSplitSmem, stream)) != cudaSuccess)
+      return e;
+    marks.after(stream);
+    return cudaSuccess;
+  }
   const unsigned grid1 = unsigned(total < sms ? total : sms);
-  if ((e = cudaFuncSetAttribute(chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP1Smem))) !=
-      cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(state_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP2Smem))) !=
-      cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(output_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kP3Smem))) !=
-      cudaSuccess)
-    return e;
   marks.begin(stream);
-  chunk_prep_kernel<<<grid1, kP1Thr, kP1Smem, stream>>>(sa, P);
+  chunk_prep_kernel<<<grid1, kP1Thr, kSplitSmem, stream>>>(sa, P);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   marks.after(stream);
-  state_pass_kernel<<<unsigned(2 * p.N), kP2Thr, kP2Smem, stream>>>(sa);
+  state_pass_kernel<<<unsigned(2 * p.N), kP2Thr, kSplitSmem, stream>>>(sa);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   marks.after(stream);
-  output_pass_kernel<<<grid1, kP3Thr, kP3Smem, stream>>>(sa);
+  output_pass_kernel<<<grid1, kP3Thr, kSplitSmem, stream>>>(sa);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   marks.after(stream);
   return cudaSuccess;

@@ -246,6 +246,12 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // this thread's committed bulk stores are complete
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// all but the two most recently committed bulk groups of this thread are complete
+__device__ __forceinline__ void bulk_wait_pending2() { asm volatile("cp.async.bulk.wait_group 2;" ::: "memory"); }
+// order this thread's generic-proxy and async-proxy (bulk copy) global accesses
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
 // hint: bring [src, src + bytes) into L2 (bytes a multiple of 16, src 16-byte aligned)
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {

@@ -309,24 +309,31 @@ TC_CASES = [
 ]
 
 
-@pytest.fixture(params=["fused", "split"])
+@pytest.fixture(params=["fused", "split", "split3"])
 def tc_path(request, monkeypatch):
-    """Run a tensor-core test on the fused kernel and on the two-phase kernels."""
-    monkeypatch.setenv("KDN_PREFILL_PATH", request.param)
+    """Run a tensor-core test on the fused kernel, on the two-phase kernels in one persistent
+    launch, and on the two-phase kernels as three separate launches."""
+    monkeypatch.setenv("KDN_PREFILL_PATH", "fused" if request.param == "fused" else "split")
+    monkeypatch.setenv("KDN_SPLIT_PERSISTENT", "0" if request.param == "split3" else "1")
     return request.param
+
+
+def split_ws(n, t, rec=238592):
+    """Workspace bytes of the two-phase path: chunk records, hand-over flags, abort word."""
+    chunks = n * ((t + 63) // 64)
+    return chunks * rec + (((chunks + 2 * n) * 4 + 4 + 255) & ~255)
 
 
 def test_tc_path_selected(kdn, proj, monkeypatch):
     lib = kdn.load()
     s, _ = proj.kdn_projection(DEV)
-    rec = 238592  # bytes of one chunk record of the two-phase path
-    assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == 16 * 1024 * rec  # few sequences: split
+    assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == split_ws(16, 65536)  # few: split
     assert lib.kdn_chunked_prefill_workspace_size(512, 16384, 64, 64, s, 1) == 0  # many sequences: fused
     assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 0) > 0   # CUDA-core path
     monkeypatch.setenv("KDN_PREFILL_PATH", "fused")
     assert lib.kdn_chunked_prefill_workspace_size(16, 65536, 64, 64, s, 1) == 0
     monkeypatch.setenv("KDN_PREFILL_PATH", "split")
-    assert lib.kdn_chunked_prefill_workspace_size(512, 100, 64, 64, s, 1) == 512 * 2 * rec
+    assert lib.kdn_chunked_prefill_workspace_size(512, 100, 64, 64, s, 1) == split_ws(512, 100)
 
 
 @pytest.mark.parametrize("case", TC_CASES)
@@ -398,12 +405,14 @@ def test_tc_fused_and_split_paths_agree(kdn, proj, monkeypatch):
     q, k, v, beta, decay, S0 = make_inputs(120, 3, 700, 64, True, True)
     args = [to_dev(a, torch.bfloat16) for a in (q, k, v)] + [to_dev(beta), to_dev(decay), proj, 64, to_dev(S0)]
     out = {}
-    for path in ("fused", "split"):
+    for path, persistent in (("fused", "1"), ("split", "1"), ("split", "0")):
         monkeypatch.setenv("KDN_PREFILL_PATH", path)
-        out[path] = kdn.fused_chunked_deltanet_forward(*args, mode="bf16")
-    (Yf, Sf), (Ys, Ss) = out["fused"], out["split"]
+        monkeypatch.setenv("KDN_SPLIT_PERSISTENT", persistent)
+        out[path + persistent] = kdn.fused_chunked_deltanet_forward(*args, mode="bf16")
+    (Yf, Sf), (Ys, Ss), (Y3, S3) = out["fused1"], out["split1"], out["split0"]
     assert rel_err(Ys.float().cpu().numpy(), Yf.float().cpu().numpy()) < BF16_Y_TOL
     assert fro_rel(Ss.cpu().numpy(), Sf.cpu().numpy()) < BF16_S_TOL
+    assert torch.equal(Ys, Y3) and torch.equal(Ss, S3)  # same arithmetic, one launch or three
     from kdn_b200.serving import device_error
 
     assert device_error() == 0
