@@ -156,6 +156,52 @@ int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int 
                                int32_t chunk, const kdn_projection* proj, void* stream);
 
 /*
+ * Affine semigroup of block state maps (exact fp32 on CUDA cores).  The state map of
+ * a block of tokens is affine, S_out = S_in A + B, with S [dv, D], A [D, D], B [dv, D];
+ * blocks compose as (A1, B1) o (A2, B2) = (A1 A2, B1 A2 + B2).
+ *
+ * kdn_affine_compose: batched composition over [batch] pairs.  A1, A2, A_out:
+ * [batch, D, D]; B1, B2, B_out: [batch, dv, D].  A_out (with A1) or B_out (with B1) may
+ * be NULL to skip that half; B2 may be NULL (zero).  Outputs must not overlap inputs.
+ * D, dv: multiples of 16; every pointer 16-byte aligned.
+ * Replaces compose_transitions, kernels/blelloch_scan.py:42-56 (also
+ * AffineSemigroupVerifier.compose, core/associative_algebra.py:45-60).
+ */
+int kdn_affine_compose(const float* A1, const float* B1, const float* A2, const float* B2, float* A_out,
+                       float* B_out, int64_t batch, int32_t D, int32_t dv, void* stream);
+
+/*
+ * Exclusive prefix states of a sequence of n_c block maps applied to S0:
+ *   states[0] = S0 (zeros if NULL),  states[c+1] = states[c] A[c] + B[c]
+ * and, if final_state is not NULL, final_state = states[n_c-1] A[n_c-1] + B[n_c-1].
+ * A: [n_c, batch, D, D]; B: [n_c, batch, dv, D]; S0, final_state: [batch, dv, D];
+ * states: [n_c, batch, dv, D] (S0 may be states itself).  n_c = 0 copies S0 (or
+ * zeros) to final_state.  Outputs must not overlap A, B or each other.
+ * Replaces blelloch_prefix_scan / sequential_prefix_scan, kernels/blelloch_scan.py:59-150
+ * (same result: the state-only chain needs dv x D x D products per block where the
+ * tree composes D x D transitions).
+ */
+int kdn_affine_prefix_states(const float* A, const float* B, const float* S0, float* states, float* final_state,
+                             int64_t n_c, int64_t batch, int32_t D, int32_t dv, void* stream);
+
+/*
+ * Affine map of one block of T tokens of each of N sequences (exact fp32):
+ *   A[n] = prod_t decay_t (I - beta_t phi(k_t) phi(k_t)^T)   (the homogeneous part)
+ *   B[n] = the state the block leaves when it starts from zeros
+ * so that for every entering state S_out = S_in A + B.  k, v, beta, decay as in
+ * kdn_chunked_prefill (no q: nothing is read out).  A_out [N, D, D] or B_out [N, dv, D]
+ * may be NULL (not computed; v may be NULL when B_out is).  Workspace:
+ * kdn_block_transition_workspace_size.  T = 0 gives A = I, B = 0.
+ * The reference forms these maps per chunk for its sequence-parallel scan
+ * (kernels/blelloch_scan.py:8-12: A_c = gamma (I - phi_k^T W phi_k), B_c = V^T W_c phi_k).
+ */
+size_t kdn_block_transition_workspace_size(int64_t N, int64_t T, int32_t chunk, const kdn_projection* proj);
+int kdn_block_transition(const void* k, const void* v, int in_dtype, const void* beta, const void* decay,
+                         int gate_dtype, float* A_out, float* B_out, int64_t N, int64_t T, int32_t dv,
+                         int32_t chunk, const kdn_projection* proj, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/*
  * One decode token per (token, head), states addressed through slot_mapping:
  * q, k: [num_tokens, H, d_k]; v, out: [num_tokens, H, dv] (in_dtype / out_dtype);
  * beta, decay: [num_tokens, H] (gate_dtype, decay may be NULL);

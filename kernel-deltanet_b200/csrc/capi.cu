@@ -86,6 +86,20 @@ bool use_split_path(int64_t N) {
   return N < sms;
 }
 
+bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {
+  if (!a || !b || abytes == 0 || bbytes == 0) return false;
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  return pa < pb + bbytes && pb < pa + abytes;
+}
+
+int check_affine_dims(int64_t batch, int32_t D, int32_t dv, bool need_dv) {
+  if (batch < 1 || batch > 65535) return fail(KDN_ERR_INVALID, "batch=%lld outside [1, 65535]", (long long)batch);
+  if (D < 16 || D > 8192 || D % 16 != 0) return fail(KDN_ERR_UNSUPPORTED, "D=%d: a multiple of 16 in [16, 8192]", D);
+  if (need_dv && (dv < 16 || dv > 8192 || dv % 16 != 0))
+    return fail(KDN_ERR_UNSUPPORTED, "dv=%d: a multiple of 16 in [16, 8192]", dv);
+  return KDN_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -219,6 +233,122 @@ int kdn_set_prefill_events(void* const* events, int count) {
 }
 
 int kdn_prefill_launch_count(void) { return g_last_prefill_launches; }
+
+int kdn_affine_compose(const float* A1, const float* B1, const float* A2, const float* B2, float* A_out,
+                       float* B_out, int64_t batch, int32_t D, int32_t dv, void* stream) {
+  if (!A_out && !B_out) return ok();
+  if (int rc = check_affine_dims(batch, D, dv, B_out != nullptr)) return rc;
+  if (!A2) return fail(KDN_ERR_INVALID, "A2 is NULL");
+  if (A_out && !A1) return fail(KDN_ERR_INVALID, "A1 is NULL but A_out is not");
+  if (B_out && !B1) return fail(KDN_ERR_INVALID, "B1 is NULL but B_out is not");
+  for (const void* p : {static_cast<const void*>(A1), static_cast<const void*>(B1), static_cast<const void*>(A2),
+                        static_cast<const void*>(B2), static_cast<const void*>(A_out), static_cast<const void*>(B_out)})
+    if (!aligned(p, 16)) return fail(KDN_ERR_INVALID, "affine operands must be 16-byte aligned");
+  const size_t abytes = sizeof(float) * size_t(batch) * D * D;
+  const size_t bbytes = B_out ? sizeof(float) * size_t(batch) * dv * D : 0;
+  const void* ins[4] = {A1, B1, A2, B2};
+  const size_t insz[4] = {A_out ? abytes : 0, bbytes, abytes, bbytes};
+  for (int i = 0; i < 4; ++i)
+    if (overlaps(A_out, A_out ? abytes : 0, ins[i], insz[i]) || overlaps(B_out, bbytes, ins[i], insz[i]))
+      return fail(KDN_ERR_INVALID, "affine compose outputs overlap an input");
+  if (overlaps(A_out, A_out ? abytes : 0, B_out, bbytes)) return fail(KDN_ERR_INVALID, "A_out overlaps B_out");
+  cudaError_t e = kdn::launch_affine_compose(A1, B1, A2, B2, A_out, B_out, batch, D, dv,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "affine compose launch");
+  return ok();
+}
+
+int kdn_affine_prefix_states(const float* A, const float* B, const float* S0, float* states, float* final_state,
+                             int64_t n_c, int64_t batch, int32_t D, int32_t dv, void* stream) {
+  if (int rc = check_affine_dims(batch, D, dv, true)) return rc;
+  if (n_c < 0 || n_c > (int64_t(1) << 20)) return fail(KDN_ERR_INVALID, "n_c=%lld outside [0, 2^20]", (long long)n_c);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t sbytes = sizeof(float) * size_t(batch) * dv * D;
+  if (n_c == 0) {
+    if (!final_state) return ok();
+    cudaError_t e = S0 ? (S0 == final_state ? cudaSuccess
+                                            : cudaMemcpyAsync(final_state, S0, sbytes, cudaMemcpyDeviceToDevice, st))
+                       : cudaMemsetAsync(final_state, 0, sbytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "prefix state copy");
+    return ok();
+  }
+  if (!A || !B || !states) return fail(KDN_ERR_INVALID, "A/B/states is NULL");
+  for (const void* p : {static_cast<const void*>(A), static_cast<const void*>(B), static_cast<const void*>(S0),
+                        static_cast<const void*>(states), static_cast<const void*>(final_state)})
+    if (!aligned(p, 16)) return fail(KDN_ERR_INVALID, "affine operands must be 16-byte aligned");
+  const size_t abytes = sizeof(float) * size_t(n_c) * batch * D * D, bbytes = sbytes * size_t(n_c);
+  if (overlaps(states, bbytes, A, abytes) || overlaps(states, bbytes, B, bbytes) ||
+      overlaps(final_state, sbytes, A, abytes) || overlaps(final_state, sbytes, B, bbytes) ||
+      overlaps(final_state, sbytes, states, bbytes))
+    return fail(KDN_ERR_INVALID, "prefix-state outputs overlap A, B or each other");
+  if (S0 && S0 != states && overlaps(S0, sbytes, states, bbytes))
+    return fail(KDN_ERR_INVALID, "S0 overlaps states without being states[0]");
+  cudaError_t e = kdn::launch_affine_prefix_states(A, B, S0, states, final_state, n_c, batch, D, dv, st);
+  if (e != cudaSuccess) return cuda_fail(e, "prefix states launch");
+  return ok();
+}
+
+size_t kdn_block_transition_workspace_size(int64_t N, int64_t T, int32_t chunk, const kdn_projection* proj) {
+  if (!proj || N <= 0 || T <= 0 || (chunk != 32 && chunk != 64) || proj->D < 64 || proj->D > 512) return 0;
+  return kdn::simt_prefill_workspace(N, T, 0, chunk, proj->D);
+}
+
+int kdn_block_transition(const void* k, const void* v, int in_dtype, const void* beta, const void* decay,
+                         int gate_dtype, float* A_out, float* B_out, int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                         const kdn_projection* proj, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_projection(proj)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N < 1 || N > 65535) return fail(KDN_ERR_INVALID, "N=%lld outside [1, 65535]", (long long)N);
+  if (T < 0) return fail(KDN_ERR_INVALID, "T=%lld < 0", (long long)T);
+  if (B_out && (dv < 16 || dv > 512 || dv % 16 != 0))
+    return fail(KDN_ERR_UNSUPPORTED, "dv=%d: dv must be a multiple of 16 in [16, 512]", dv);
+  if (chunk != 32 && chunk != 64) return fail(KDN_ERR_UNSUPPORTED, "chunk=%d: chunk must be 32 or 64", chunk);
+  if (!valid_dtype(in_dtype) || !valid_dtype(gate_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
+  if (!A_out && !B_out) return ok();
+  const int D = proj->D;
+  if (T == 0) {
+    if (A_out) {
+      cudaError_t e = kdn::launch_affine_identity(A_out, N, D, st);
+      if (e != cudaSuccess) return cuda_fail(e, "identity launch");
+    }
+    if (B_out) {
+      cudaError_t e = cudaMemsetAsync(B_out, 0, sizeof(float) * size_t(N) * dv * D, st);
+      if (e != cudaSuccess) return cuda_fail(e, "zero state");
+    }
+    return ok();
+  }
+  if (!k || !beta) return fail(KDN_ERR_INVALID, "k/beta is NULL");
+  if (B_out && !v) return fail(KDN_ERR_INVALID, "v is NULL but B_out is not");
+  if (!aligned(k, 8)) return fail(KDN_ERR_INVALID, "k must be 8-byte aligned");
+  const size_t need = kdn::simt_prefill_workspace(N, T, 0, chunk, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(KDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(KDN_ERR_INVALID, "workspace must be 256-byte aligned");
+  kdn::PrefillProblem p;
+  p.q = nullptr;
+  p.k = k;
+  p.v = v;
+  p.in_dtype = in_dtype;
+  p.beta = beta;
+  p.decay = decay;
+  p.gate_dtype = gate_dtype;
+  p.S0 = nullptr;
+  p.y = nullptr;
+  p.y_dtype = KDN_DTYPE_F32;
+  p.S_out = B_out;
+  p.N = N;
+  p.T = T;
+  p.dv = B_out ? dv : 0;
+  p.C = chunk;
+  p.D = D;
+  p.a_rows = A_out ? D : 0;
+  p.A_out = A_out;
+  const kdn::ProjParams P = kdn::make_proj_params(*proj);
+  kdn::LaunchMarks marks;
+  cudaError_t e = kdn::launch_simt_prefill(p, P, workspace, workspace_bytes, st, marks);
+  if (e != cudaSuccess) return cuda_fail(e, "block transition launch");
+  return ok();
+}
 
 int kdn_decode_step(const void* q, const void* k, const void* v, int in_dtype, const void* beta, const void* decay,
                     int gate_dtype, void* states, int state_dtype, int64_t num_slots, const void* slot_mapping,

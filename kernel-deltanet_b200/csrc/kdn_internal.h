@@ -24,11 +24,16 @@ struct PrefillProblem {
   const void* decay;  // may be null (== 1)
   int gate_dtype;
   const float* S0;  // may be null (zeros)
-  void* y;
+  void* y;          // may be null on the CUDA-core path (no readout: q is not lifted)
   int y_dtype;
   float* S_out;
   int64_t N, T;
   int dv, C, D;
+  // Block transition (CUDA-core path only): a_rows extra state rows, started at the
+  // identity and driven with v = 0, run ahead of the dv value rows; after the pass they
+  // hold the homogeneous part A of the block's affine map, written to A_out [N, a_rows, D].
+  int a_rows = 0;
+  float* A_out = nullptr;
 };
 
 // Per-launch event marks of one prefill call (measurement hook behind
@@ -70,6 +75,17 @@ size_t split_prefill_workspace(int64_t N, int64_t T);
 cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
                                  cudaStream_t stream, LaunchMarks& marks);
 cudaError_t split_read_error(cudaStream_t stream, int* code);
+
+// ---------------------------------------------------------------- affine.cu
+// (A1,B1) o (A2,B2) = (A1 A2, B1 A2 + B2), batched; A_out or B_out may be null (not computed).
+cudaError_t launch_affine_compose(const float* A1, const float* B1, const float* A2, const float* B2, float* A_out,
+                                  float* B_out, int64_t batch, int D, int dv, cudaStream_t stream);
+// A [batch, D, D] = identity
+cudaError_t launch_affine_identity(float* A, int64_t batch, int D, cudaStream_t stream);
+// states[0] = S0 (zeros if null), states[c+1] = states[c] A_c + B_c; final = states[n_c-1] A + B.
+cudaError_t launch_affine_prefix_states(const float* A, const float* B, const float* S0, float* states,
+                                        float* final_state, int64_t n_c, int64_t batch, int D, int dv,
+                                        cudaStream_t stream);
 
 // ---------------------------------------------------------------- decode.cu
 struct DecodeProblem {

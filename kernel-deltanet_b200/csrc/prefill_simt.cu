@@ -61,14 +61,16 @@ Workspace carve(void* base, int64_t N, int64_t T, int dv, int C, int D, size_t* 
   return w;
 }
 
-// (1) lift k and q rows into [N, Tp, D]; padded rows (t >= T) become zeros.
+// (1) lift k and q rows into [N, Tp, D]; padded rows (t >= T) become zeros.  Without a
+// readout (y null) only k is lifted.
 __global__ void __launch_bounds__(kThreads) simt_lift_kernel(PrefillProblem p, Workspace w, ProjParams P) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int64_t rows = p.N * w.Tp;
   const int D = p.D;
-  for (int64_t r = warp; r < 2 * rows; r += nwarps) {
+  const int64_t total = p.y ? 2 * rows : rows;
+  for (int64_t r = warp; r < total; r += nwarps) {
     const bool isq = r >= rows;
     const int64_t row = isq ? r - rows : r;
     const int64_t n = row / w.Tp, t = row % w.Tp;
@@ -87,7 +89,8 @@ __global__ void __launch_bounds__(kThreads) simt_lift_kernel(PrefillProblem p, W
 }
 
 // (2) per (chunk c, sequence n): G = K K^T, P = Q K^T, gates, T = (I + A)^-1, Aq.
-template <int C>
+// kQ = false (no readout): P and Aq are skipped (Aq is written as zeros).
+template <int C, bool kQ>
 __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, Workspace w) {
   constexpr int R = C / 16;  // each thread owns an R x R tile of G and of P
   constexpr int LD = C + 1;
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, W
     for (int e = tid; e < C * 64; e += kThreads) {
       const int r = e >> 6, cc = e & 63;
       Ks[r * 65 + cc] = Kg[int64_t(r) * D + d0 + cc];
-      Qs[r * 65 + cc] = Qg[int64_t(r) * D + d0 + cc];
+      if (kQ) Qs[r * 65 + cc] = Qg[int64_t(r) * D + d0 + cc];
     }
     __syncthreads();
 #pragma unroll 4
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, W
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         a[r] = Ks[(ti * R + r) * 65 + dd];
-        qq[r] = Qs[(ti * R + r) * 65 + dd];
+        qq[r] = kQ ? Qs[(ti * R + r) * 65 + dd] : 0.f;
         b[r] = Ks[(tj * R + r) * 65 + dd];
       }
 #pragma unroll
@@ -135,7 +138,7 @@ __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, W
 #pragma unroll
         for (int s = 0; s < R; ++s) {
           g[r][s] = fmaf(a[r], b[s], g[r][s]);
-          pq[r][s] = fmaf(qq[r], b[s], pq[r][s]);
+          if (kQ) pq[r][s] = fmaf(qq[r], b[s], pq[r][s]);
         }
     }
     __syncthreads();
@@ -215,7 +218,9 @@ constexpr size_t prep_smem_bytes() {
   return sizeof(float) * (2 * C * 65 + 3 * C * (C + 1) + 2 * C);
 }
 
-// (3) per (16-row tile of S, sequence n): the serial pass over chunks.
+// (3) per (16-row tile of S, sequence n): the serial pass over chunks.  Tiles below
+// p.a_rows belong to the block transition's homogeneous map (identity start, v = 0,
+// no readout, result to A_out); the others are value rows (S0, v, y, S_out).
 template <int C>
 __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, Workspace w) {
   constexpr int TPR = kThreads / C;    // threads per chunk row
@@ -238,11 +243,18 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
   const int tid = threadIdx.x;
   const int i = tid / TPR;
   const int v0 = (tid % TPR) * VPT;
-  const int row0 = vt * kRowTile;
+  const bool a_tile = vt * kRowTile < p.a_rows;
+  const int row0 = a_tile ? vt * kRowTile : vt * kRowTile - p.a_rows;
+  const bool readout = !a_tile && p.y != nullptr;  // uniform per CTA
 
   for (int e = tid; e < kRowTile * D; e += kThreads) {
     const int r = e / D, d = e % D;
-    S[r * SD + d] = p.S0 ? p.S0[(n * p.dv + row0 + r) * int64_t(D) + d] : 0.f;
+    float s0 = 0.f;
+    if (a_tile)
+      s0 = (row0 + r == d) ? 1.f : 0.f;
+    else if (p.S0)
+      s0 = p.S0[(n * p.dv + row0 + r) * int64_t(D) + d];
+    S[r * SD + d] = s0;
   }
   __syncthreads();
 
@@ -267,17 +279,26 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
       for (int e = tid; e < C * 64; e += kThreads) {
         const int r = e >> 6, cc = e & 63;
         Ks[r * 65 + cc] = Kg[int64_t(r) * D + d0 + cc];
-        Qs[r * 65 + cc] = Qg[int64_t(r) * D + d0 + cc];
+        if (readout) Qs[r * 65 + cc] = Qg[int64_t(r) * D + d0 + cc];
       }
       __syncthreads();
+      if (readout) {
 #pragma unroll 4
-      for (int dd = 0; dd < 64; ++dd) {
-        const float kd = Ks[i * 65 + dd], qd = Qs[i * 65 + dd];
+        for (int dd = 0; dd < 64; ++dd) {
+          const float kd = Ks[i * 65 + dd], qd = Qs[i * 65 + dd];
 #pragma unroll
-        for (int u = 0; u < VPT; ++u) {
-          const float s = S[(v0 + u) * SD + d0 + dd];
-          x[u] = fmaf(kd, s, x[u]);
-          yq[u] = fmaf(qd, s, yq[u]);
+          for (int u = 0; u < VPT; ++u) {
+            const float s = S[(v0 + u) * SD + d0 + dd];
+            x[u] = fmaf(kd, s, x[u]);
+            yq[u] = fmaf(qd, s, yq[u]);
+          }
+        }
+      } else {
+#pragma unroll 4
+        for (int dd = 0; dd < 64; ++dd) {
+          const float kd = Ks[i * 65 + dd];
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) x[u] = fmaf(kd, S[(v0 + u) * SD + d0 + dd], x[u]);
         }
       }
     }
@@ -287,7 +308,7 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
 #pragma unroll
     for (int u = 0; u < VPT; ++u) {
       float vv = 0.f;
-      if (t < p.T) vv = ld_as_f32(p.v, p.in_dtype, (n * p.T + t) * p.dv + row0 + v0 + u);
+      if (!a_tile && t < p.T) vv = ld_as_f32(p.v, p.in_dtype, (n * p.T + t) * p.dv + row0 + v0 + u);
       Rs[i * kRowTile + v0 + u] = beta_i * (vv - gi * x[u]);
     }
     __syncthreads();
@@ -304,17 +325,19 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
     for (int u = 0; u < VPT; ++u) Es[i * kRowTile + v0 + u] = e_[u];
     __syncthreads();
     // y_i = exp(g_{i-1}) yq_i + sum_{j<i} Aq_ij e_j ;  then E''_i = exp(g_{C-1} - g_i) e_i into Rs
-    float yv[VPT];
+    if (readout) {
+      float yv[VPT];
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) yv[u] = gprev * yq[u];
-    for (int j = 0; j < i; ++j) {
-      const float aij = Am[i * LD + j];
+      for (int u = 0; u < VPT; ++u) yv[u] = gprev * yq[u];
+      for (int j = 0; j < i; ++j) {
+        const float aij = Am[i * LD + j];
 #pragma unroll
-      for (int u = 0; u < VPT; ++u) yv[u] = fmaf(aij, Es[j * kRowTile + v0 + u], yv[u]);
-    }
-    if (t < p.T) {
+        for (int u = 0; u < VPT; ++u) yv[u] = fmaf(aij, Es[j * kRowTile + v0 + u], yv[u]);
+      }
+      if (t < p.T) {
 #pragma unroll
-      for (int u = 0; u < VPT; ++u) st_from_f32(p.y, p.y_dtype, (n * p.T + t) * p.dv + row0 + v0 + u, yv[u]);
+        for (int u = 0; u < VPT; ++u) st_from_f32(p.y, p.y_dtype, (n * p.T + t) * p.dv + row0 + v0 + u, yv[u]);
+      }
     }
 #pragma unroll
     for (int u = 0; u < VPT; ++u) Rs[i * kRowTile + v0 + u] = wi * e_[u];
@@ -336,9 +359,10 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
     __syncthreads();
   }
 
+  float* dst = a_tile ? p.A_out + (n * p.a_rows + row0) * int64_t(D) : p.S_out + (n * p.dv + row0) * int64_t(D);
   for (int e = tid; e < kRowTile * D; e += kThreads) {
     const int r = e / D, d = e % D;
-    p.S_out[(n * p.dv + row0 + r) * int64_t(D) + d] = S[r * SD + d];
+    dst[int64_t(r) * D + d] = S[r * SD + d];
   }
 }
 
@@ -362,9 +386,10 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
   }
   {
     const size_t smem = prep_smem_bytes<C>();
-    err = cudaFuncSetAttribute(simt_prep_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    auto prep = p.y ? simt_prep_kernel<C, true> : simt_prep_kernel<C, false>;
+    err = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return err;
-    simt_prep_kernel<C><<<dim3(w.NC, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
+    prep<<<dim3(w.NC, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     marks.after(stream);
   }
@@ -372,7 +397,7 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
     const size_t smem = chain_smem_bytes<C>(p.D);
     err = cudaFuncSetAttribute(simt_chain_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return err;
-    simt_chain_kernel<C><<<dim3(p.dv / kRowTile, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
+    simt_chain_kernel<C><<<dim3((p.a_rows + p.dv) / kRowTile, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     marks.after(stream);
   }

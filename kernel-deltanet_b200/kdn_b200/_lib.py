@@ -59,6 +59,11 @@ SIGNATURES = {
                                           ctypes.POINTER(KdnProjection), _P]),
     "kdn_set_prefill_events": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT]),
     "kdn_prefill_launch_count": (_INT, []),
+    "kdn_affine_compose": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
+    "kdn_affine_prefix_states": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _P]),
+    "kdn_block_transition_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I32, ctypes.POINTER(KdnProjection)]),
+    "kdn_block_transition": (_INT, [_P, _P, _INT, _P, _P, _INT, _P, _P, _I64, _I64, _I32, _I32,
+                                    ctypes.POINTER(KdnProjection), _P, ctypes.c_size_t, _P]),
     "kdn_decode_step": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _INT, _I64, _P, _INT, _P, _INT, _I64, _I32, _I32,
                                ctypes.POINTER(KdnProjection), _INT, _P]),
     "kdn_fork_state": (_INT, [_P, _I64, _I64, _I64, _I64, _P]),

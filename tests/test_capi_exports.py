@@ -147,3 +147,33 @@ def test_prefill_event_hook_argument_checks(lib):
     assert lib.kdn_set_prefill_events(None, 1) == 1
     assert lib.kdn_set_prefill_events(None, 0) == 0
     assert lib.kdn_prefill_launch_count() == 0
+
+
+def test_affine_argument_checks(lib):
+    # overlapping output / input, misalignment, unsupported sizes: rejected before any launch
+    assert lib.kdn_affine_compose(4096, 8192, 16384, None, 4096, 1 << 20, 1, 64, 16, None) == 1
+    assert b"overlap" in lib.kdn_last_error()
+    assert lib.kdn_affine_compose(4104, 8192, 16384, None, 1 << 20, 1 << 21, 1, 64, 16, None) == 1
+    assert lib.kdn_affine_compose(4096, 8192, 16384, None, 1 << 20, 1 << 21, 1, 40, 16, None) == 2
+    assert lib.kdn_affine_compose(4096, 8192, 16384, None, 1 << 20, 1 << 21, 0, 64, 16, None) == 1
+    assert lib.kdn_affine_compose(None, None, 16384, None, None, None, 1, 64, 16, None) == 0  # nothing asked
+    assert lib.kdn_affine_compose(None, 8192, 16384, None, 1 << 20, None, 1, 64, 16, None) == 1  # A1 missing
+    assert lib.kdn_affine_prefix_states(4096, 1 << 20, None, 1 << 24, None, -1, 1, 64, 16, None) == 1
+    assert lib.kdn_affine_prefix_states(None, None, None, 1 << 24, None, 2, 1, 64, 16, None) == 1
+    # final_state overlapping the states it is computed from
+    assert lib.kdn_affine_prefix_states(1 << 30, 1 << 31, None, 1 << 24, 1 << 24, 2, 1, 64, 16, None) == 1
+
+
+def test_block_transition_argument_checks(lib):
+    p = _proj()
+    assert lib.kdn_block_transition_workspace_size(2, 130, 64, p) > 0
+    assert lib.kdn_block_transition_workspace_size(2, 130, 48, p) == 0
+    call = lambda **kw: lib.kdn_block_transition(
+        kw.get("k", 8), kw.get("v", 8), 0, 8, None, 0, kw.get("A", 4096), kw.get("B", 8192), 2, 130,
+        kw.get("dv", 64), kw.get("C", 64), p, kw.get("ws", 256), kw.get("wsb", 16), None)
+    assert call() == 4
+    assert b"workspace" in lib.kdn_last_error()
+    assert call(C=48) == 2
+    assert call(dv=24) == 2
+    assert call(v=None) == 1            # B asked without values
+    assert call(A=None, B=None) == 0    # nothing asked
