@@ -84,13 +84,25 @@ __device__ __forceinline__ void set_abort(uint32_t* abort) {
 
 // bounded mbarrier wait of this path; gives up early once another wait has given up
 __device__ __forceinline__ bool split_wait(uint64_t* bar, uint32_t parity, uint32_t* abort) {
-  for (uint32_t i = 0; i < kWaitLimit; i += 1024) {
-    for (int j = 0; j < 1024; ++j)
-      if (tc::mbar_try_wait(bar, parity)) return true;
-    if (aborted(abort)) return false;
+  uint32_t n = 0;
+  while (!tc::mbar_try_wait(bar, parity)) {
+    if ((++n & 1023u) == 0 && (n >= kWaitLimit || aborted(abort))) {
+      set_abort(abort);
+      return false;
+    }
   }
-  set_abort(abort);
-  return false;
+  return true;
+}
+
+// Phase parities of a group of barriers live in one register, bit i for barrier i: an
+// array indexed by a run-time slot would sit in local memory, and beside this path's
+// shared-memory carve-out the L1 is too small to keep it (each access became an L2
+// round trip of hundreds of cycles on the issuing thread's chain).  These wait for the
+// phase whose parity is bit i of `bits`, then flip the bit.
+__device__ __forceinline__ bool split_wait_bit(uint64_t* bar, uint32_t& bits, int i, uint32_t* abort) {
+  const bool r = split_wait(bar, (bits >> i) & 1u, abort);
+  bits ^= 1u << i;
+  return r;
 }
 
 // ---- hand-over flags between the phases of the persistent launch (global memory)
@@ -249,7 +261,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
       const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
       const uint32_t id_n64 = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t p_xin = 0, p_zfree[2] = {0, 0}, p_fready = 0, p_ops = 0, p_wdone = 0;
+      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0, p_wdone = 0;
       auto lift = [&](int s) {  // Z slot s & 1 = [k; q] Omega_s^T
 #pragma unroll
         for (int k0 = 0; k0 < 64; k0 += 16)
@@ -265,8 +277,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         lift(0);
         lift(1);
         for (int s = 0; s < kSlices; ++s) {
-          ok &= split_wait(&bar_zfree[s & 1], p_zfree[s & 1], sa.abort);  // slot s & 1 read by all
-          p_zfree[s & 1] ^= 1;
+          ok &= split_wait_bit(&bar_zfree[s & 1], p_zfree, s & 1, sa.abort);  // slot s & 1 read by all
           tc::fence_after_sync();
           if (s + 2 < kSlices) lift(s + 2);
           ok &= split_wait(bar_fready, p_fready, sa.abort);
@@ -313,7 +324,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
     __syncwarp();
   } else {
     // ================================================================ compute warps
-    uint32_t ph_lift[2] = {0, 0}, ph_mma = 0, ph_st = 0;
+    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0;
     auto wait_mma = [&]() {
       ok &= split_wait(bar_mma, ph_mma, sa.abort);
       ph_mma ^= 1;
@@ -407,8 +418,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       float ss = 0.f;
 #pragma unroll 1
       for (int s = 0; s < kSlices; ++s) {
-        ok &= split_wait(&bar_lift[s & 1], ph_lift[s & 1], sa.abort);
-        ph_lift[s & 1] ^= 1;
+        ok &= split_wait_bit(&bar_lift[s & 1], ph_lift, s & 1, sa.abort);
         tc::fence_after_sync();
         float z[32];
         tc::tmem_ld32(tmem + lane_off + P1_Z + 128 * (s & 1) + 32 * cq, z);
@@ -591,15 +601,19 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
 // halves need no communication; both read the same records (the second read
 // mostly hits L2).  Per chunk only U_k (64 KiB, two ring items held until the update
 // has read them) and T' (8 KiB) are streamed; the outputs are left to phase 3.
-// The chain is serial (state -> Y -> X -> E -> state), so the compute warps meet at a
-// named barrier after each step and one of their threads issues the next products
-// at once; a separate warp keeps the bulk loads ahead.
+// The chain is serial (state -> Y -> X -> E -> state).  Every role has its own warp so
+// that no step waits behind another's work: 8 compute warps move tiles between TMEM
+// and shared memory, one thread issues the tensor-core products as soon as a tile's
+// warps have arrived, one keeps the bulk loads ahead, and one copies the entering state
+// and E into the record (and publishes the progress) off the chain.
 constexpr int kHalf = 32;    // value columns per CTA
 constexpr int kP2Warps = 8;  // compute warps: 2 per TMEM lane quarter, 16 columns each
 constexpr int kP2Threads = 32 * kP2Warps;
-constexpr int kP2Producer = kP2Warps;
-constexpr int kP2Thr = 32 * (kP2Warps + 1);
-constexpr int kP2Leader = 32 * 7;  // issues the MMAs: lane 0 of warp 7 (q rows, no E step)
+constexpr int kP2Producer = kP2Warps;      // bulk loads (lane 0)
+constexpr int kP2Issuer = kP2Warps + 1;    // tensor-core products (lane 0)
+constexpr int kP2Store = kP2Warps + 2;     // record copies and progress words (lane 0)
+constexpr int kP2Thr = 32 * (kP2Warps + 3);
+constexpr int kP2Bars = 22;
 
 // TMEM columns (phase 2)
 constexpr uint32_t P2_S = 0;    // S^T master, slice s at 32 s (lanes = features), fp32
@@ -618,8 +632,9 @@ constexpr uint32_t P2_EB = 202752;    // 4 KiB  E'' (fp16, MN-major SW64)
 constexpr uint32_t P2_ET = 206848;    // 4 KiB  E (fp16, MN-major SW64), copied to the record
 constexpr uint32_t P2_BAR = 210944;
 constexpr uint32_t kP2Smem = P2_BAR + 256 + 1024;
+static_assert(8 * kP2Bars <= 256, "phase-2 barriers overflow their slot");
 
-// Phase 2 on CTA cta (sequence cta / 2, value columns 32 (cta % 2)..+31; warps 0..8 work,
+// Phase 2 on CTA cta (sequence cta / 2, value columns 32 (cta % 2)..+31; warps 0..10 work,
 // others idle; `tmem` >= 256 allocated columns).  With rec_ready it waits for each record
 // to be published; with out_prog it publishes, per sequence and column half, how many
 // chunks have their entering state and E in the records.
@@ -628,17 +643,18 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
   const TcArgs& a = sa.a;
   const uint32_t sbase = tc::smem_u32(sm);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P2_BAR);
-  uint64_t* ring_full = bars;       // [5] stage loaded (bytes)
-  uint64_t* ring_empty = bars + 5;  // [5] stage consumed (MMA commit)
-  uint64_t* tp_full = bars + 10;    // [2] T' loaded (bytes)
-  uint64_t* tp_empty = bars + 12;   // [2] T' consumed (MMA commit)
-  uint64_t* bar_y = bars + 14;      // Y done (MMA commit)
-  uint64_t* bar_x = bars + 15;      // X done (MMA commit)
-  uint64_t* bar_s = bars + 16;      // [2] state update of slices 2p, 2p+1 done (MMA commit; for p = 0
-                                    //     also the record copies have read their tiles)
-  uint64_t* fac_full = bars + 18;   // [2] factors of the chunk loaded (bytes)
-  uint64_t* fac_empty = bars + 20;  // [2] factors copied to registers (8 compute warps)
-
+  uint64_t* ring_full = bars;        // [4] stage loaded (bytes) and the state operand of its slice pair
+                                     //     written (8 compute warps)
+  uint64_t* ring_empty = bars + 4;   // [4] stage consumed (MMA commit)
+  uint64_t* tp_full = bars + 8;      // [2] T' loaded (bytes) and the Y operand written (8 compute warps)
+  uint64_t* tp_empty = bars + 10;    // [2] T' consumed (MMA commit)
+  uint64_t* bar_y = bars + 12;       // Y done (MMA commit)
+  uint64_t* bar_x = bars + 13;       // X done (MMA commit)
+  uint64_t* bar_s = bars + 14;       // [2] state update of slices 2p, 2p+1 done (MMA commit)
+  uint64_t* fac_full = bars + 16;    // [2] factors of the chunk loaded (bytes)
+  uint64_t* fac_empty = bars + 18;   // [2] factors copied to registers (8 compute warps)
+  uint64_t* bar_e = bars + 20;       // E'' operand and E tile written (8 compute warps)
+  uint64_t* bar_stfree = bars + 21;  // the record copies have read the state operand and E (store warp)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n = cta >> 1;
@@ -648,31 +664,36 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
 
   if (tid == 0) {
     for (int b = 0; b < kRing; ++b) {
-      tc::mbar_init(&ring_full[b], 1);
+      tc::mbar_init(&ring_full[b], 1 + kP2Warps);
       tc::mbar_init(&ring_empty[b], 1);
     }
     for (int u = 0; u < 2; ++u) {
-      tc::mbar_init(&tp_full[u], 1);
+      tc::mbar_init(&tp_full[u], 1 + kP2Warps);
       tc::mbar_init(&tp_empty[u], 1);
-    }
-    tc::mbar_init(bar_y, 1);
-    tc::mbar_init(bar_x, 1);
-    tc::mbar_init(&bar_s[0], 1);
-    tc::mbar_init(&bar_s[1], 1);
-    for (int u = 0; u < 2; ++u) {
+      tc::mbar_init(&bar_s[u], 1);
       tc::mbar_init(&fac_full[u], 1);
       tc::mbar_init(&fac_empty[u], kP2Warps);
     }
+    tc::mbar_init(bar_y, 1);
+    tc::mbar_init(bar_x, 1);
+    tc::mbar_init(bar_e, kP2Warps);
+    tc::mbar_init(bar_stfree, 1);
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
+  auto wait_bar = [&](uint64_t* bar, uint32_t& phase) {
+    ok &= split_wait(bar, phase, sa.abort);
+    phase ^= 1;
+    tc::fence_after_sync();
+  };
+
   if (warp == kP2Producer) {
     // ================================================================ bulk loads
     if (lane == 0) {
-      uint32_t pe[kRing] = {}, pt[2] = {0, 0}, pfe[2] = {0, 0};
+      uint32_t pe = 0, pt = 0, pfe = 0;  // phase bits per slot
       int64_t g = 0;  // ring items so far
       for (int c = 0; c < NC; ++c) {
         const uint8_t* rec = record(sa, c, n);
@@ -683,8 +704,7 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         for (int p = 0; p < 2; ++p, ++g) {  // U_k slices 2p, 2p+1
           const int b = int(g % kRing);
           if (g >= kRing) {
-            ok &= split_wait(&ring_empty[b], pe[b], sa.abort);
-            pe[b] ^= 1;
+            ok &= split_wait_bit(&ring_empty[b], pe, b, sa.abort);
           }
           tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
           for (int o = 0; o < 32768; o += 16384)
@@ -692,10 +712,8 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         }
         const int u = c & 1;
         if (c >= 2) {
-          ok &= split_wait(&tp_empty[u], pt[u], sa.abort);
-          pt[u] ^= 1;
-          ok &= split_wait(&fac_empty[u], pfe[u], sa.abort);
-          pfe[u] ^= 1;
+          ok &= split_wait_bit(&tp_empty[u], pt, u, sa.abort);
+          ok &= split_wait_bit(&fac_empty[u], pfe, u, sa.abort);
         }
         tc::mbar_arrive_expect_tx(&tp_full[u], 8192);
         tc::bulk_load(sbase + P2_TP + u * 8192, rec + REC_TP, 8192, &tp_full[u]);
@@ -705,26 +723,102 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
       }
     }
     __syncwarp();
+  } else if (warp == kP2Issuer) {
+    // ================================================================ tensor-core products
+    if (lane == 0) {
+      const uint32_t id_k = tc::idesc_f16_f32(128, kHalf, false, true);  // A K-major, B MN-major
+      const uint32_t id_s = tc::idesc_f16_f32(128, kHalf, true, true);   // A MN-major (U_k^T)
+      // descriptor bases; the products only add constant offsets
+      const uint64_t d_ring = tc::smem_desc_sw128(sbase + P2_RING, 16, 1024);     // U_k as A (K-major)
+      const uint64_t d_ringT = tc::smem_desc_sw128(sbase + P2_RING, 8192, 1024);  // U_k^T as A (MN-major)
+      const uint64_t d_sop = tc::smem_desc_sw64(sbase + P2_SOP, 8192, 512);
+      const uint64_t d_tp = tc::smem_desc_sw128(sbase + P2_TP, 16, 1024);
+      const uint64_t d_yb = tc::smem_desc_sw64(sbase + P2_YB, 8192, 512);
+      const uint64_t d_eb = tc::smem_desc_sw64(sbase + P2_EB, 8192, 512);
+      uint32_t pf = 0, pt = 0, pe = 0;  // pf, pt: phase bits per slot
+      for (int c = 0; c < NC; ++c) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {  // Y += U_k S^T over the features of slices 2p, 2p+1
+          const int b = (2 * c + p) & (kRing - 1);  // item 2c + p: its U_k slices and state operand
+          ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
+          tc::fence_after_sync();
+          const uint64_t da = tc::desc_add(d_ring, uint32_t(b) * 32768);
+          const uint64_t db = tc::desc_add(d_sop, uint32_t(p) * 16384);
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {  // slice 2p + (j >> 1), its 64-feature half j & 1
+            const uint64_t a0 = tc::desc_add(da, uint32_t(j) * 8192);
+            const uint64_t b0 = tc::desc_add(db, uint32_t(j) * 4096);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              // M = 128: rows 0..63 are the chunk's tokens; rows 64..127 (the next 8 KiB) give
+              // lanes nobody reads
+              tc::mma_ss(tmem + P2_Y, tc::desc_add(a0, 32 * kk), tc::desc_add(b0, 1024 * kk), id_k,
+                         p > 0 || j > 0 || kk > 0);
+          }
+        }
+        tc::mma_commit(bar_y);
+        // X = T' Y
+        const int u = c & 1;
+        ok &= split_wait_bit(&tp_full[u], pt, u, sa.abort);  // T' and the Y operand
+        tc::fence_after_sync();
+        const uint64_t dt = tc::desc_add(d_tp, uint32_t(u) * 8192);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // K = the 64 tokens; rows 64..127 of A: unread lanes
+          tc::mma_ss(tmem + P2_X, tc::desc_add(dt, 32 * kk), tc::desc_add(d_yb, 16 * kk * 64), id_k, kk > 0);
+        tc::mma_commit(&tp_empty[u]);
+        tc::mma_commit(bar_x);
+        // S_s^T += U_k,s^T E'' for s = 2p, 2p+1
+        wait_bar(bar_e, pe);
+#pragma unroll 1
+        for (int p = 0; p < 2; ++p) {
+          const int b = (2 * c + p) & (kRing - 1);
+          const uint64_t da = tc::desc_add(d_ringT, uint32_t(b) * 32768);
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t a0 = tc::desc_add(da, uint32_t(h) * 16384);
+            const uint32_t dcol = tmem + P2_S + kHalf * (2 * p + h);
+#pragma unroll
+            for (int k0 = 0; k0 < 64; k0 += 16)
+              tc::mma_ss(dcol, tc::desc_add(a0, 128 * k0), tc::desc_add(d_eb, 64 * k0), id_s, true);
+          }
+          tc::mma_commit(&ring_empty[b]);
+          tc::mma_commit(&bar_s[p]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kP2Store) {
+    // ================================================================ record copies, progress
+    if (lane == 0) {
+      uint32_t pf = 0, pe = 0;  // pf: phase bits per ring slot
+      for (int c = 0; c < NC; ++c) {
+        uint8_t* rec = record(sa, c, n);
+        for (int p = 0; p < 2; ++p) {  // both state-operand pairs written (their ring items loaded)
+          const int b = (2 * c + p) & (kRing - 1);
+          ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
+        }
+        tc::bulk_store(rec + REC_S0 + half * 32768, sbase + P2_SOP, 32768);  // the state entering the chunk
+        tc::bulk_commit();
+        wait_bar(bar_e, pe);
+        tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET, 4096);
+        tc::bulk_commit();
+        tc::bulk_wait_read();
+        tc::mbar_arrive(bar_stfree);  // the state operand and E may be rewritten
+        if (out_prog) {               // chunks 0..c of this half are in the record
+          tc::bulk_wait_all();
+          publish_store(out_prog + 2 * n + half, uint32_t(c + 1));
+        }
+      }
+      tc::bulk_wait_all();
+    }
+    __syncwarp();
   } else if (warp < kP2Warps) {
-    // ================================================================ compute warps (+ leader)
+    // ================================================================ compute warps
     const int quarter = warp & 3, ch = warp >> 2;  // TMEM lane quarter, 16-column half of the CTA's 32
     const int trow = quarter * 32 + lane;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const int cbase = col0 + 16 * ch;  // first value column of this thread
     const bool decayed = a.decay != nullptr;
-    const bool leader = tid == kP2Leader;
-    const uint32_t id_k = tc::idesc_f16_f32(128, kHalf, false, true);  // A K-major, B MN-major
-    const uint32_t id_s = tc::idesc_f16_f32(128, kHalf, true, true);   // A MN-major (U_k^T)
-    // descriptor bases; the products only add constant offsets
-    const uint64_t d_ring = tc::smem_desc_sw128(sbase + P2_RING, 16, 1024);     // U_k as A (K-major)
-    const uint64_t d_ringT = tc::smem_desc_sw128(sbase + P2_RING, 8192, 1024);  // U_k^T as A (MN-major)
-    const uint64_t d_sop = tc::smem_desc_sw64(sbase + P2_SOP, 8192, 512);
-    const uint64_t d_tp = tc::smem_desc_sw128(sbase + P2_TP, 16, 1024);
-    const uint64_t d_yb = tc::smem_desc_sw64(sbase + P2_YB, 8192, 512);
-    const uint64_t d_eb = tc::smem_desc_sw64(sbase + P2_EB, 8192, 512);
-    uint32_t pf[kRing] = {}, pt[2] = {0, 0};  // leader: ring / T' phases
-    int64_t g = 0;                             // leader: ring items taken
-    int st[2] = {0, 0};                        // leader: stages of the chunk's two U_k items
 #pragma unroll
     for (int s = 0; s < kSlices; ++s) {  // state master from the initial state
       float v[16];
@@ -733,8 +827,7 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
       tc::tmem_st16(tmem + lane_off + P2_S + kHalf * s + 16 * ch, v);
     }
     tc::tmem_st_wait();
-    uint32_t py = 0, px = 0, ps[2] = {0, 0};
-    uint32_t pff[2] = {0, 0};
+    uint32_t py = 0, px = 0, ps[2] = {0, 0}, pff = 0, pst = 0;  // pff: phase bits per slot
     auto store_tile = [&](uint32_t off, const float* v, float w) {  // 16 values of row trow, fp16 SW64
 #pragma unroll
       for (int m = 0; m < 2; ++m)
@@ -743,25 +836,18 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
                        pack_f16_sat(w * v[8 * m + 4], w * v[8 * m + 5]),
                        pack_f16_sat(w * v[8 * m + 6], w * v[8 * m + 7]));
     };
-    auto step_done = [&]() {  // this warp's shared-memory tiles -> tensor core; all compute warps met
+    auto signal = [&](uint64_t* bar) {  // this warp's tiles -> tensor core / bulk copies
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      tc::named_bar_sync(1, kP2Threads);
-      tc::fence_after_sync();
-    };
-    auto wait_mma = [&](uint64_t* bar, uint32_t& phase) {
-      ok &= split_wait(bar, phase, sa.abort);
-      phase ^= 1;
-      tc::fence_after_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar);
     };
     for (int c = 0; c < NC; ++c) {
-      uint8_t* rec = record(sa, c, n);
       // ---------------------------------------- the chunk's factors (shared memory -> registers)
       float cu[16], cew = 0.f, ceC;
       {
         const int u = c & 1;
-        ok &= split_wait(&fac_full[u], pff[u], sa.abort);
-        pff[u] ^= 1;
+        ok &= split_wait_bit(&fac_full[u], pff, u, sa.abort);
         const float* fac = reinterpret_cast<const float*>(sm + P2_FAC + u * P2_FAC_BYTES);
         if (trow < 64) {
           const float4* u4 = reinterpret_cast<const float4*>(fac + trow * 32 + 16 * ch);
@@ -776,82 +862,37 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&fac_empty[u]);
       }
-      // ---------------------------------------- per slice pair: state operand (fp16), decay, Y
+      if (c > 0) wait_bar(bar_stfree, pst);  // the previous chunk's state operand and E have been copied
+      // ---------------------------------------- per slice pair: state operand (fp16), decay
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (c > 0) wait_mma(&bar_s[p], ps[p]);  // the previous chunk's update of slices 2p, 2p+1
-        float v[32];
-        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p) + 16 * ch, *reinterpret_cast<float(*)[16]>(v));
-        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p + 1) + 16 * ch,
-                      *reinterpret_cast<float(*)[16]>(v + 16));
-        tc::tmem_ld_wait();
-        store_tile(P2_SOP + (2 * p) * 8192, v, 1.f);
-        store_tile(P2_SOP + (2 * p + 1) * 8192, v + 16, 1.f);
-        if (decayed) {
+        if (c > 0) wait_bar(&bar_s[p], ps[p]);  // the previous chunk's update of slices 2p, 2p+1
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= ceC;
-          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p) + 16 * ch, *reinterpret_cast<float(*)[16]>(v));
-          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p + 1) + 16 * ch,
-                        *reinterpret_cast<float(*)[16]>(v + 16));
-          tc::tmem_st_wait();
-        }
-        step_done();
-        if (leader) {  // Y += U_k S^T over the features of slices 2p, 2p+1
-          const int b = int(g % kRing);
-          st[p] = b;
-          ok &= split_wait(&ring_full[b], pf[b], sa.abort);
-          pf[b] ^= 1;
-          ++g;
-          tc::fence_after_sync();
-          const uint64_t da = tc::desc_add(d_ring, uint32_t(b) * 32768);
-          const uint64_t db = tc::desc_add(d_sop, uint32_t(p) * 16384);
+        for (int h = 0; h < 2; ++h) {  // slice 2p + h
+          float v[16];
+          tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p + h) + 16 * ch, v);
+          tc::tmem_ld_wait();
+          store_tile(P2_SOP + (2 * p + h) * 8192, v, 1.f);
+          if (decayed) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h)      // slice 2p + h
-#pragma unroll
-            for (int kb = 0; kb < 2; ++kb)  // its 64-feature halves
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                // M = 128: rows 0..63 are the chunk's tokens; rows 64..127 (the next 8 KiB) give
-                // lanes nobody reads
-                tc::mma_ss(tmem + P2_Y, tc::desc_add(da, h * 16384 + kb * 8192 + 32 * kk),
-                           tc::desc_add(db, (128 * h + 64 * kb + 16 * kk) * 64), id_k,
-                           p > 0 || h > 0 || kb > 0 || kk > 0);
-          if (p == 1) {
-            tc::mma_commit(bar_y);
-            if (out_prog && c > 0) {  // while Y runs: chunks 0..c-1 of this half are in the record
-              tc::bulk_wait_all();
-              publish_store(out_prog + 2 * n + half, uint32_t(c));
-            }
-            tc::bulk_store(rec + REC_S0 + half * 32768, sbase + P2_SOP, 32768);  // the state entering the chunk
-            tc::bulk_commit();
+            for (int j = 0; j < 16; ++j) v[j] *= ceC;
+            tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p + h) + 16 * ch, v);
           }
         }
-        __syncwarp();
+        if (decayed) tc::tmem_st_wait();
+        signal(&ring_full[(2 * c + p) & (kRing - 1)]);
       }
-      // ---------------------------------------- Y (fp16), then X = T' Y
-      wait_mma(bar_y, py);
+      // ---------------------------------------- Y (fp16) for X = T' Y
+      wait_bar(bar_y, py);
       if (trow < 64) {
         float y[16];
         tc::tmem_ld16(tmem + lane_off + P2_Y + 16 * ch, y);
         tc::tmem_ld_wait();
         store_tile(P2_YB, y, 1.f);
       }
-      step_done();
-      const int u = c & 1;
-      if (leader) {
-        ok &= split_wait(&tp_full[u], pt[u], sa.abort);
-        pt[u] ^= 1;
-        tc::fence_after_sync();
-        const uint64_t da = tc::desc_add(d_tp, uint32_t(u) * 8192);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)  // K = the 64 tokens; rows 64..127 of A: unread lanes
-          tc::mma_ss(tmem + P2_X, tc::desc_add(da, 32 * kk), tc::desc_add(d_yb, 16 * kk * 64), id_k, kk > 0);
-        tc::mma_commit(&tp_empty[u]);
-        tc::mma_commit(bar_x);
-      }
-      __syncwarp();
-      // ---------------------------------------- E = U - X, E'', then the update
-      wait_mma(bar_x, px);
+      signal(&tp_full[c & 1]);
+      // ---------------------------------------- E = U - X and E'' for the update
+      wait_bar(bar_x, px);
       if (trow < 64) {
         float x[16];
         tc::tmem_ld16(tmem + lane_off + P2_X + 16 * ch, x);
@@ -861,32 +902,10 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         store_tile(P2_ET, x, 1.f);
         store_tile(P2_EB, x, cew);
       }
-      step_done();
-      if (leader) {
-        tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET, 4096);
-        tc::bulk_commit();
-
-        for (int p = 0; p < 2; ++p) {  // S_s^T += U_k,s^T E'' for s = 2p, 2p+1
-          const uint64_t da = tc::desc_add(d_ringT, uint32_t(st[p]) * 32768);
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int k0 = 0; k0 < 64; k0 += 16)
-              tc::mma_ss(tmem + P2_S + kHalf * (2 * p + h), tc::desc_add(da, h * 16384 + 128 * k0),
-                         tc::desc_add(d_eb, 64 * k0), id_s, true);
-          tc::mma_commit(&ring_empty[st[p]]);
-          if (p == 0) tc::bulk_wait_read();  // the state operand and E tiles are rewritten after bar_s[0]
-          tc::mma_commit(&bar_s[p]);
-        }
-      }
-      __syncwarp();
+      signal(bar_e);
     }
-    wait_mma(&bar_s[0], ps[0]);
-    wait_mma(&bar_s[1], ps[1]);
-    if (leader) {
-      tc::bulk_wait_all();
-      if (out_prog) publish_store(out_prog + 2 * n + half, uint32_t(NC));
-    }
+    wait_bar(&bar_s[0], ps[0]);
+    wait_bar(&bar_s[1], ps[1]);
     // ---------------------------------------- final state
 #pragma unroll
     for (int s = 0; s < kSlices; ++s) {
@@ -951,7 +970,7 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
   if (warp == 1) {
     // ================================================================ bulk loads
     if (lane == 0) {
-      uint32_t pe[kRing] = {}, ps[2] = {0, 0};
+      uint32_t pe = 0, ps = 0;  // phase bits per slot
       int64_t g = 0, j = 0;
       for (int64_t idx = cta; idx < total; idx += ncta, ++j) {
         const uint8_t* rec = record(sa, idx / N, idx % N);
@@ -964,8 +983,7 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
         for (int s = 0; s < kSlices; ++s, ++g) {
           const int b = int(g % kRing);
           if (g >= kRing) {
-            ok &= split_wait(&ring_empty[b], pe[b], sa.abort);
-            pe[b] ^= 1;
+            ok &= split_wait_bit(&ring_empty[b], pe, b, sa.abort);
           }
           const uint32_t dst = sbase + P3_RING + b * 32768;
           tc::mbar_arrive_expect_tx(&ring_full[b], 32768);
@@ -976,8 +994,7 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
         }
         const int u = int(j & 1);
         if (j >= 2) {
-          ok &= split_wait(&small_empty[u], ps[u], sa.abort);
-          ps[u] ^= 1;
+          ok &= split_wait_bit(&small_empty[u], ps, u, sa.abort);
         }
         const uint32_t dst = sbase + P3_SMALL + u * P3_SMALL_BYTES;
         tc::mbar_arrive_expect_tx(&small_full[u], 16384 + 256);
@@ -991,20 +1008,18 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
     // ================================================================ MMA issuer
     if (lane == 0) {
       const uint32_t id = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t pf[kRing] = {}, psf[2] = {0, 0}, pfree[2] = {0, 0};
+      uint32_t pf = 0, psf = 0, pfree = 0;  // phase bits per slot
       int64_t g = 0, j = 0;
       for (int64_t idx = cta; idx < total; idx += ncta, ++j) {
         const int u = int(j & 1);
         if (j >= 2) {  // the epilogue of chunk j - 2 has read accumulator buffer u
-          ok &= split_wait(&acc_free[u], pfree[u], sa.abort);
-          pfree[u] ^= 1;
+          ok &= split_wait_bit(&acc_free[u], pfree, u, sa.abort);
         }
         tc::fence_after_sync();
         const uint32_t dq = tmem + 128 * u, de = dq + 64;
         for (int s = 0; s < kSlices; ++s, ++g) {
           const int b = int(g % kRing);
-          ok &= split_wait(&ring_full[b], pf[b], sa.abort);
-          pf[b] ^= 1;
+          ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
           tc::fence_after_sync();
           const uint32_t st = sbase + P3_RING + b * 32768;
 #pragma unroll
@@ -1019,8 +1034,7 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
             }
           tc::mma_commit(&ring_empty[b]);
         }
-        ok &= split_wait(&small_full[u], psf[u], sa.abort);
-        psf[u] ^= 1;
+        ok &= split_wait_bit(&small_full[u], psf, u, sa.abort);
         tc::fence_after_sync();
         const uint32_t sm_small = sbase + P3_SMALL + u * P3_SMALL_BYTES;
 #pragma unroll
@@ -1035,13 +1049,12 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
     // ================================================================ epilogue (q-row lanes)
     const uint32_t lane_off = uint32_t(warp * 32) << 16;  // warps 2, 3: lanes 64..127
     const int i = (warp - 2) * 32 + lane;                  // token row within the chunk
-    uint32_t pa[2] = {0, 0};
+    uint32_t pa = 0;  // phase bits per slot
     int64_t j = 0;
     for (int64_t idx = cta; idx < total; idx += ncta, ++j) {
       const int64_t c = idx / N, n = idx % N;
       const int u = int(j & 1);
-      ok &= split_wait(&acc_full[u], pa[u], sa.abort);
-      pa[u] ^= 1;
+      ok &= split_wait_bit(&acc_full[u], pa, u, sa.abort);
       tc::fence_after_sync();
       const float yqs = reinterpret_cast<const float*>(sm + P3_SMALL + u * P3_SMALL_BYTES + 16384)[i];
       __syncwarp();
@@ -1083,7 +1096,7 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
 // address slot sits above every role's layout.
 constexpr uint32_t kSplitTslot = 225536;
 constexpr uint32_t kSplitSmem = kSplitTslot + 16 + 1024;
-static_assert(kSplitTslot >= P2_BAR + 8 * 20 && kSplitTslot >= P1_BAR + 112 && kSplitTslot >= P3_BAR + 8 * 18,
+static_assert(kSplitTslot >= P2_BAR + 8 * kP2Bars && kSplitTslot >= P1_BAR + 112 && kSplitTslot >= P3_BAR + 8 * 18,
               "TMEM slot overlaps a role's barriers");
 
 __device__ __forceinline__ uint8_t* split_smem() {
