@@ -125,18 +125,12 @@ __device__ __forceinline__ void publish_store(uint32_t* flag, uint32_t v) {
   tc::fence_proxy_async_global();
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
 }
-// the same for writes made by other threads of the CTA that synchronised with this one
-__device__ __forceinline__ void publish_flag(uint32_t* flag, uint32_t v) {
-  tc::fence_proxy_async_global();
-  __threadfence();
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
-}
-
 // ================================================================ phase 1
 constexpr int kP1Warps = 16;  // compute warps, 4 per TMEM lane quarter
 constexpr int kP1Threads = 32 * kP1Warps;
-constexpr int kP1Issuer = kP1Warps;
-constexpr int kP1Thr = 32 * (kP1Warps + 1);
+constexpr int kP1Issuer = kP1Warps;         // issues every MMA (lane 0)
+constexpr int kP1Publisher = kP1Warps + 1;  // copies the record out and publishes it (lane 0)
+constexpr int kP1Thr = 32 * (kP1Warps + 2);
 
 // TMEM columns (phase 1)
 constexpr uint32_t P1_Z = 0;     // lift results, 2 x 128 cols (slices s at 128 (s & 1))
@@ -147,10 +141,10 @@ constexpr uint32_t P1_U = 0;     // U in lanes 64..127 (after the chunk matrices
 constexpr uint32_t P1_OMG = 0;        // 64 KiB Omega (bf16)
 constexpr uint32_t P1_XIN = 65536;    // 16 KiB [k; q] (bf16, K-major)
 constexpr uint32_t P1_F = 81920;      // 32 KiB slice features [U_k; U_q] | algebra: A (f32), T (f32)
-constexpr uint32_t P1_UK = 114688;    // 64 KiB U_k, all slices (fp16), B operand of W
+constexpr uint32_t P1_AQ = 114688;    // 8 KiB  Aq (fp16, K-major SW128), copied to the record
+constexpr uint32_t P1_VEC = 122880;   // 1 KiB  per-token factors of the state pass, copied to the record
 constexpr uint32_t P1_VB = 180224;    // 8 KiB  V (fp16, MN-major), B operand of U
 constexpr uint32_t P1_TOP = 188416;   // 16 KiB [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major)
-constexpr uint32_t P1_TD = 204800;    // 4 KiB  diagonal 16x16 blocks of T
 constexpr uint32_t P1_US = 208896;    // 4 KiB  forward-substitution scratch
 constexpr uint32_t P1_PH = 212992;    // 2 KiB  phase b[512]
 constexpr uint32_t P1_GL = 215040;    // 5 x 256 B gates: g, beta, exp(g), exp(g_{i-1}), exp(g_{C-1} - g)
@@ -198,8 +192,9 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
   tc::named_bar_sync(1, kP1Threads);
 }
 
-// Phase 1 on CTAs cta = 0..ncta-1 (544 threads, `tmem` = 512 allocated columns).  With
-// rec_ready, each finished record is published there (1) for the state pass.
+// Phase 1 on CTAs cta = 0..ncta-1 (576 threads: 16 compute warps, an MMA issuer and a record
+// publisher; `tmem` = 512 allocated columns).  With rec_ready, each finished record is
+// published there (1) for the state pass.
 __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams& P, uint8_t* sm, uint32_t tmem,
                                           int64_t cta, int64_t ncta, uint32_t* rec_ready, bool& ok) {
   const TcArgs& a = sa.a;
@@ -223,6 +218,8 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   uint64_t* bar_ops = reinterpret_cast<uint64_t*>(sm + P1_BAR + 40);
   uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);   // U staged
   uint64_t* bar_stfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 64);  // staged tiles copied out
+  uint64_t* bar_fdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 24);   // slice's Gram product done and its
+                                                                          // features copied out (2 arrivals)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cq = (warp >> 2) & 3;
@@ -244,6 +241,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
     tc::mbar_init(bar_ops, kP1Warps);
     tc::mbar_init(bar_wdone, kP1Warps);
     tc::mbar_init(bar_stfree, 1);
+    tc::mbar_init(bar_fdone, 2);
     tc::fence_mbar_init();
   }
   build_omega(sm + P1_OMG, P, warp, lane, kP1Thr / 32);
@@ -261,7 +259,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
       const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
       const uint32_t id_n64 = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0, p_wdone = 0;
+      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0;
       auto lift = [&](int s) {  // Z slot s & 1 = [k; q] Omega_s^T
 #pragma unroll
         for (int k0 = 0; k0 < 64; k0 += 16)
@@ -270,7 +268,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         tc::mma_commit(&bar_lift[s & 1]);
       };
       for (int64_t idx = cta; idx < total; idx += ncta) {
-        uint8_t* rec = record(sa, idx / N, idx % N);
         ok &= split_wait(bar_xin, p_xin, sa.abort);
         p_xin ^= 1;
         tc::fence_after_sync();
@@ -288,14 +285,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
             const uint64_t fd = tc::smem_desc_sw128(sbase + P1_F + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
             tc::mma_ss(tmem + P1_GP, fd, fd, id_gp, s > 0 || k0 > 0);
           }
-          // the slice's features into the record: U_q rows 64..127 of K-blocks 2s, 2s+1 and U_k slice s
-          for (int kb = 0; kb < 2; ++kb)
-            tc::bulk_store(rec + REC_Q + (2 * s + kb) * 8192, sbase + P1_F + kb * 16384 + 8192, 8192);
-          tc::bulk_commit();
-          tc::bulk_wait_read();  // F is rewritten once this phase of bar_mma completes
-          tc::mma_commit(bar_mma);
-          tc::bulk_store(rec + REC_UK + s * 16384, sbase + P1_UK + s * 16384, 16384);  // read by the chunk's end
-          tc::bulk_commit();
+          tc::mma_commit(bar_fdone);  // F is rewritten once the publisher has copied it out too
         }
         ok &= split_wait(bar_ops, p_ops, sa.abort);
         p_ops ^= 1;
@@ -305,26 +295,48 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
           tc::mma_ss(tmem + P1_U, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
                      tc::smem_desc_sw128(sbase + P1_VB + 128 * k0, 8192, 1024), id_n64, k0 > 0);
         tc::mma_commit(bar_mma);
-        tc::bulk_store(rec + REC_TP, sbase + P1_TOP, 8192);  // T' = rows 0..63 of the A operand
-        tc::bulk_commit();
+      }
+    }
+    __syncwarp();
+  } else if (warp == kP1Publisher) {
+    // ================================================================ record copies, publication
+    if (lane == 0) {
+      uint32_t p_fready = 0, p_wdone = 0;
+      for (int64_t idx = cta; idx < total; idx += ncta) {
+        uint8_t* rec = record(sa, idx / N, idx % N);
+        for (int s = 0; s < kSlices; ++s) {
+          // the slice's features: U_q (rows 64..127) as K-blocks 2s, 2s+1 and U_k (rows 0..63) as slice s
+          ok &= split_wait(bar_fready, p_fready, sa.abort);
+          p_fready ^= 1;
+          for (int kb = 0; kb < 2; ++kb) {
+            tc::bulk_store(rec + REC_Q + (2 * s + kb) * 8192, sbase + P1_F + kb * 16384 + 8192, 8192);
+            tc::bulk_store(rec + REC_UK + s * 16384 + kb * 8192, sbase + P1_F + kb * 16384, 8192);
+          }
+          tc::bulk_commit();
+          tc::bulk_wait_read();
+          tc::mbar_arrive(bar_fdone);
+        }
+        // T' (rows 0..63 of the U product's A operand), U, Aq and the factors
         ok &= split_wait(bar_wdone, p_wdone, sa.abort);
         p_wdone ^= 1;
+        tc::bulk_store(rec + REC_TP, sbase + P1_TOP, 8192);
         tc::bulk_store(rec + REC_U, sbase + P1_F, 16384);
+        tc::bulk_store(rec + REC_AQ, sbase + P1_AQ, 8192);
+        tc::bulk_store(rec + REC_VEC, sbase + P1_VEC, 1024);
         tc::bulk_commit();
-        if (rec_ready) {  // the whole record is in memory: publish it
+        tc::bulk_wait_read();
+        tc::mbar_arrive(bar_stfree);  // the staging tiles take the next chunk
+        if (rec_ready) {              // every byte of the record came through this thread's copies
           tc::bulk_wait_all();
-          publish_flag(rec_ready + idx, 1u);
-        } else {
-          tc::bulk_wait_read();  // the staging tiles are free for the next chunk
+          publish_store(rec_ready + idx, 1u);
         }
-        tc::mbar_arrive(bar_stfree);
       }
       tc::bulk_wait_all();
     }
     __syncwarp();
-  } else {
+  } else if (warp < kP1Warps) {
     // ================================================================ compute warps
-    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0;
+    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0, ph_fd = 0;
     auto wait_mma = [&]() {
       ok &= split_wait(bar_mma, ph_mma, sa.abort);
       ph_mma ^= 1;
@@ -347,7 +359,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       const int64_t nidx = idx + ncta;
       const bool has_next = nidx < total;
       const int64_t nn = nidx % N, ncn = nidx / N;
-      uint8_t* rec = record(sa, c, n);
       // ---------------------------------------- chunk inputs -> lift of slice 0
       tc::cp_async_wait_all();
       if (!bf_in) load_kq_f32(a, n, int(c), sm + P1_XIN, tid);
@@ -442,7 +453,9 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
           fp[(j >> 1) + 1] = pack_f16(u2, u3);
         }
         if (s > 0) {
-          wait_mma();  // the previous slice's Gram product and copy-out are done with F
+          ok &= split_wait(bar_fdone, ph_fd, sa.abort);  // the previous slice's Gram product and copy-out
+          ph_fd ^= 1;                                      // are done with F
+          tc::fence_after_sync();
         } else if (idx != cta) {  // the previous chunk's staged tiles have been copied out
           ok &= split_wait(bar_stfree, ph_st, sa.abort);
           ph_st ^= 1;
@@ -455,7 +468,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
             const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
             const uint32_t off = tc::sw128_offset(trow, e0 + 8 * c8);
             *reinterpret_cast<uint4*>(fb + off) = pk;
-            if (trow < 64) *reinterpret_cast<uint4*>(sm + P1_UK + s * 16384 + kb * 8192 + off) = pk;
           }
         }
         tc::fence_proxy_async_smem();
@@ -467,7 +479,9 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       // every lift of this chunk has completed: the input tile takes the next chunk
       if (has_next && bf_in) prefetch_kq(a, nn, int(ncn), sbase + P1_XIN, tid);
       tc::cp_async_commit();
-      wait_mma();  // Gram product of the last slice
+      ok &= split_wait(bar_fdone, ph_fd, sa.abort);  // Gram product (and copy-out) of the last slice
+      ph_fd ^= 1;
+      tc::fence_after_sync();
 
       // ---------------------------------------- chunk matrices
       float gp[16];
@@ -505,13 +519,13 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
           }
 #pragma unroll
           for (int h = 0; h < 2; ++h)
-            *reinterpret_cast<uint4*>(rec + REC_AQ + tc::sw128_offset(i, 16 * cq + 8 * h)) = make_uint4(
+            *reinterpret_cast<uint4*>(sm + P1_AQ + tc::sw128_offset(i, 16 * cq + 8 * h)) = make_uint4(
                 pack_f16_sat(aq[8 * h], aq[8 * h + 1]), pack_f16_sat(aq[8 * h + 2], aq[8 * h + 3]),
                 pack_f16_sat(aq[8 * h + 4], aq[8 * h + 5]), pack_f16_sat(aq[8 * h + 6], aq[8 * h + 7]));
         }
       }
       {  // per-token factors of the state pass, and V (fp16) as the B operand of U
-        float* vec = reinterpret_cast<float*>(rec + REC_VEC);
+        float* vec = reinterpret_cast<float*>(sm + P1_VEC);
         if (tid < 64) vec[tid] = wdec[tid] * sc[tid];
         else if (tid < 128) vec[tid] = sc[tid] * egp[tid - 64];
         else if (tid == 128) vec[128] = eg[63];
@@ -584,7 +598,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      if (rec_ready) __threadfence();  // this thread's record stores (Aq, factors) before the publication
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_wdone);
     }
@@ -608,7 +621,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
 // and E into the record (and publishes the progress) off the chain.
 constexpr int kHalf = 32;    // value columns per CTA
 constexpr int kP2Warps = 8;  // compute warps: 2 per TMEM lane quarter, 16 columns each
-constexpr int kP2Threads = 32 * kP2Warps;
 constexpr int kP2Producer = kP2Warps;      // bulk loads (lane 0)
 constexpr int kP2Issuer = kP2Warps + 1;    // tensor-core products (lane 0)
 constexpr int kP2Store = kP2Warps + 2;     // record copies and progress words (lane 0)
@@ -1096,6 +1108,8 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
 // address slot sits above every role's layout.
 constexpr uint32_t kSplitTslot = 225536;
 constexpr uint32_t kSplitSmem = kSplitTslot + 16 + 1024;
+static_assert(kP1Smem <= kSplitSmem && kP2Smem <= kSplitSmem && kP3Smem <= kSplitSmem,
+              "a role's shared memory exceeds the launch's");
 static_assert(kSplitTslot >= P2_BAR + 8 * kP2Bars && kSplitTslot >= P1_BAR + 112 && kSplitTslot >= P3_BAR + 8 * 18,
               "TMEM slot overlaps a role's barriers");
 
