@@ -156,6 +156,15 @@ int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int 
                                int32_t chunk, const kdn_projection* proj, void* stream);
 
 /*
+ * Strided block copy for streaming a sequence segment between host and device (no
+ * reference counterpart): `rows` blocks of `width_bytes`, `src_pitch` / `dst_pitch` bytes
+ * apart, copied on `stream` in either direction (host memory should be pinned for the copy
+ * to be asynchronous).  One [B, T_seg, d] slice of a [B, T, d] tensor is one call.
+ */
+int kdn_copy_rows(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes, size_t rows,
+                  void* stream);
+
+/*
  * Affine semigroup of block state maps (exact fp32 on CUDA cores).  The state map of
  * a block of tokens is affine, S_out = S_in A + B, with S [dv, D], A [D, D], B [dv, D];
  * blocks compose as (A1, B1) o (A2, B2) = (A1 A2, B1 A2 + B2).

@@ -234,6 +234,18 @@ int kdn_set_prefill_events(void* const* events, int count) {
 
 int kdn_prefill_launch_count(void) { return g_last_prefill_launches; }
 
+int kdn_copy_rows(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes, size_t rows,
+                  void* stream) {
+  if (rows == 0 || width_bytes == 0) return ok();
+  if (!dst || !src) return fail(KDN_ERR_INVALID, "dst/src is NULL");
+  if (dst_pitch < width_bytes || src_pitch < width_bytes)
+    return fail(KDN_ERR_INVALID, "pitch below the row width (%zu, %zu < %zu)", dst_pitch, src_pitch, width_bytes);
+  cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width_bytes, rows, cudaMemcpyDefault,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "strided copy");
+  return ok();
+}
+
 int kdn_affine_compose(const float* A1, const float* B1, const float* A2, const float* B2, float* A_out,
                        float* B_out, int64_t batch, int32_t D, int32_t dv, void* stream) {
   if (!A_out && !B_out) return ok();

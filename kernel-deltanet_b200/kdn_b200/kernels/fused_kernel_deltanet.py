@@ -15,8 +15,11 @@ reference keeps it in the input dtype -- fp32 state is this build's contract).
 Arithmetic modes: ``"fp32"`` (exact fp32, CUDA cores) and ``"bf16"`` (bf16
 tensor-core products with fp32 accumulation and fp32 state); default: "bf16"
 for bfloat16 inputs, "fp32" otherwise.  The work runs in libkdn on the
-tensors' CUDA device and current stream; there is no CPU path.  Backward is
-not implemented (the reference recomputes through autograd, :158-179).
+tensors' CUDA device and current stream; there is no CPU path.  Host
+(CPU) tensors are accepted with ``device="cuda"``: the sequence is then streamed
+through that device in segments of ``segment_tokens`` (copies in and out overlap
+the kernels) and the results come back as host tensors, complete on return.
+Backward is not implemented (the reference recomputes through autograd, :158-179).
 """
 
 from __future__ import annotations
@@ -60,7 +63,15 @@ def fused_chunked_deltanet_forward(
     workspace: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
     final_state: Optional[torch.Tensor] = None,
+    device=None,
+    segment_tokens: int = 8192,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
+    if not q.is_cuda:
+        if device is None:
+            raise RuntimeError("kdn_b200 runs on CUDA tensors only (no CPU fallback); pass device='cuda' to stream "
+                               "host tensors through the GPU")
+        return _streamed_forward(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state, mode,
+                                 torch.device(device), out, final_state, segment_tokens)
     dev = _check_cuda(q, k, v, beta, decay, initial_state)
     if q.dim() != 3 or k.shape != q.shape or v.dim() != 3 or v.shape[:2] != q.shape[:2]:
         raise RuntimeError(f"expected q,k [B,T,d_k] and v [B,T,d_v]; got {tuple(q.shape)}, {tuple(k.shape)}, "
@@ -105,6 +116,109 @@ def fused_chunked_deltanet_forward(
         B, T, dv, chunk_size, proj, mcode, workspace.data_ptr(), ws_bytes, _lib.stream_handle(dev))
     _lib.check(rc, "kdn_chunked_prefill")
     return y, S
+
+
+def _copy_rows(lib, dst, src, stream):
+    """dst[b, :n] = src[b, :n] for every b (same dtype; rows contiguous inside, pitched between)."""
+    rows, n = src.shape[0], src.shape[1]
+    esz = src.element_size()
+    width = n * (src[0, 0].numel()) * esz
+    rc = lib.kdn_copy_rows(dst.data_ptr(), dst.stride(0) * esz, src.data_ptr(), src.stride(0) * esz, width, rows,
+                           stream.cuda_stream)
+    _lib.check(rc, "kdn_copy_rows")
+
+
+def _streamed_forward(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state, mode, dev, out, final_state,
+                      segment_tokens):
+    """Host tensors in, host tensors out, the work on `dev`: the sequence is cut into segments of whole
+    chunks; while segment i runs, the inputs of segment i+1 are copied in and the outputs of segment
+    i-1 are copied out (two copy streams, double-buffered device segments).  The fp32 state is
+    carried from segment to segment on the device, so the result equals one call over the whole
+    sequence (the chunks and their arithmetic are the same)."""
+    if dev.type != "cuda":
+        raise RuntimeError(f"device must be a CUDA device, got {dev}")
+    for t in (k, v, beta, decay, initial_state, out, final_state):
+        if t is not None and t.is_cuda:
+            raise RuntimeError("stream from the host: every tensor argument must be a host tensor")
+    if q.dim() != 3 or k.shape != q.shape or v.dim() != 3 or v.shape[:2] != q.shape[:2]:
+        raise RuntimeError(f"expected q,k [B,T,d_k] and v [B,T,d_v]; got {tuple(q.shape)}, {tuple(k.shape)}, "
+                           f"{tuple(v.shape)}")
+    B, T, d_k = q.shape
+    dv = v.shape[-1]
+    D = fwht_proj.D
+    if beta.shape != (B, T) or (decay is not None and decay.shape != (B, T)):
+        raise RuntimeError("beta/decay must be [B, T]")
+    in_dtype = q.dtype if q.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    gate_dtype = beta.dtype if beta.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    src = [t.to(dt).contiguous() for t, dt in ((q, in_dtype), (k, in_dtype), (v, in_dtype))]
+    gates = [beta.to(gate_dtype).contiguous()] + ([decay.to(gate_dtype).contiguous()] if decay is not None else [])
+    y_host = out if out is not None else torch.empty(B, T, dv, dtype=in_dtype, pin_memory=True)
+    if y_host.shape != (B, T, dv) or y_host.dtype != in_dtype or not y_host.is_contiguous():
+        raise RuntimeError(f"out must be a contiguous host tensor [B, T, d_v] of {in_dtype}")
+    S_host = final_state if final_state is not None else torch.empty(B, dv, D, dtype=torch.float32, pin_memory=True)
+    if S_host.shape != (B, dv, D) or S_host.dtype != torch.float32 or not S_host.is_contiguous():
+        raise RuntimeError("final_state must be a contiguous host float32 tensor [B, d_v, D]")
+    seg = max(chunk_size, (int(segment_tokens) // chunk_size) * chunk_size)
+    proj = fwht_proj  # its device constants are built per device on demand
+    compute = torch.cuda.current_stream(dev)
+    copy_in = torch.cuda.Stream(dev)
+    copy_out = torch.cuda.Stream(dev)
+    with torch.cuda.device(dev):
+        nb = 2
+        dsrc = [[torch.empty(B, seg, t.shape[-1], dtype=t.dtype, device=dev) for t in src] for _ in range(nb)]
+        dgate = [[torch.empty(B, seg, dtype=g.dtype, device=dev) for g in gates] for _ in range(nb)]
+        dy = [torch.empty(B, seg, dv, dtype=in_dtype, device=dev) for _ in range(nb)]
+        dS = [torch.empty(B, dv, D, dtype=torch.float32, device=dev) for _ in range(2)]
+        if initial_state is not None:
+            if initial_state.shape != (B, dv, D):
+                raise RuntimeError(f"initial_state must be [B, d_v, D] = {(B, dv, D)}")
+            dS[1].copy_(initial_state.to(torch.float32), non_blocking=False)
+        lib = _lib.load()
+        pstruct, _phase = proj.kdn_projection(dev)
+        mcode = _MODES[mode if mode is not None else ("bf16" if in_dtype == torch.bfloat16 else "fp32")]
+        ws_bytes = int(lib.kdn_chunked_prefill_workspace_size(B, seg, dv, chunk_size, pstruct, mcode))
+        ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+        freed = [torch.cuda.Event() for _ in range(nb)]   # segment buffer i % nb may be refilled
+        loaded = [torch.cuda.Event() for _ in range(nb)]
+        done = [torch.cuda.Event() for _ in range(nb)]
+        nseg = (T + seg - 1) // seg
+        S_prev = dS[1] if initial_state is not None else None
+        for i in range(nseg):
+            t0, t1 = i * seg, min(T, (i + 1) * seg)
+            n = t1 - t0
+            b = i % nb
+            with torch.cuda.stream(copy_in):
+                if i >= nb:
+                    copy_in.wait_event(freed[b])
+                for hs, ds in zip(src + gates, dsrc[b] + dgate[b]):  # one strided copy per tensor
+                    _copy_rows(lib, ds, hs[:, t0:t1], copy_in)
+                loaded[b].record(copy_in)
+            compute.wait_event(loaded[b])
+            S_next = dS[i % 2]
+            qq, kk, vv = (x[:, :n].contiguous() if n < seg else x for x in dsrc[b])
+            gg = [x[:, :n].contiguous() if n < seg else x for x in dgate[b]]
+            dd = gg[1] if decay is not None else None
+            if n == seg:
+                yy = dy[b]
+                fused_chunked_deltanet_forward(qq, kk, vv, gg[0], dd, proj, chunk_size, S_prev, mode=mode,
+                                               workspace=ws, out=yy, final_state=S_next)
+            else:  # the last, shorter segment
+                yy, _ = fused_chunked_deltanet_forward(qq, kk, vv, gg[0], dd, proj, chunk_size, S_prev, mode=mode,
+                                                       workspace=ws, final_state=S_next)
+            done[b].record(compute)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done[b])
+                _copy_rows(lib, y_host[:, t0:t1], yy[:, :n], copy_out)
+                if i == nseg - 1:
+                    S_host.copy_(S_next, non_blocking=True)
+                freed[b].record(copy_out)
+            yy.record_stream(copy_out)
+            S_prev = S_next
+        if nseg == 0:  # T == 0: the state passes through
+            S_host.copy_(initial_state.to(torch.float32) if initial_state is not None else torch.zeros_like(S_host))
+        compute.wait_stream(copy_out)
+        compute.synchronize()  # host results are complete when the call returns
+    return y_host, S_host
 
 
 class FusedKernelDeltaNetFunction(torch.autograd.Function):
