@@ -412,6 +412,16 @@ def run_prefill_only(n_seq: int, seq: int):
                       "path": os.environ.get("KDN_PREFILL_PATH", "auto")}))
 
 
+def run_decode_only(steps: int):
+    """Only the decode workload for `steps` steps (the case `ncu` captures use)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    r = bench_decode(dev, steps=steps, warmup=3, peaks=load_peaks())
+    torch.cuda.synchronize()
+    print(json.dumps({"decode_only": steps, "ms_per_step": r["ms_per_step"], "gbs": r["roofline"]["achieved"]}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -422,7 +432,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-only", type=int, nargs=2, metavar=("N", "T"),
                     help="only run two prefill calls of N sequences x T tokens (for profiler captures)")
+    ap.add_argument("--decode-only", type=int, metavar="STEPS",
+                    help="only run the decode workload for STEPS steps (for profiler captures)")
     args = ap.parse_args()
+    if args.decode_only:
+        run_decode_only(args.decode_only)
+        return
     if args.prefill_only:
         run_prefill_only(*args.prefill_only)
         return

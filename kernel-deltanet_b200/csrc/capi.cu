@@ -379,7 +379,8 @@ int kdn_decode_step(const void* q, const void* k, const void* v, int in_dtype, c
     return fail(KDN_ERR_INVALID, "bad dtype");
   if (index_dtype != KDN_INDEX_I32 && index_dtype != KDN_INDEX_I64) return fail(KDN_ERR_INVALID, "bad index dtype");
   if (readout != KDN_READOUT_PRE && readout != KDN_READOUT_POST) return fail(KDN_ERR_INVALID, "bad readout");
-  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(states, 8)) return fail(KDN_ERR_INVALID, "misaligned q/k/states");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(states, 16))
+    return fail(KDN_ERR_INVALID, "q/k/v/states must be 16-byte aligned (they are moved by bulk copies)");
   kdn::DecodeProblem p;
   p.q = q;
   p.k = k;

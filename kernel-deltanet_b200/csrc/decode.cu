@@ -7,20 +7,53 @@
 //   post-update readout (optional): y = lambda S phi(q) + beta (v - lambda S phi(k)) (phi(k) . phi(q))
 // (kernels/kernel_deltanet_fused.py:288-300; benchmarks/run_full_batch_decoding.py:43-54)
 //
-// Grid (dv/16, H, num_tokens), 128 threads: each CTA owns 16 rows of one head's
-// state and streams them once (one read, one write -- the bandwidth floor).
-// The lift of q and k is split over the 4 warps by 64-wide block, shared through
-// shared memory; each lane then keeps the features of its columns in registers.
+// The step reads and writes every state row once, so it is a streaming kernel: one
+// persistent CTA per SM walks units (token, head) -- each as items of 16 state rows (32 KiB
+// of fp32 state at D = 512, contiguous in the slot pool) -- through a ring of shared-memory
+// stages.  A loader warp keeps bulk loads of the next items (state rows, v; q and k with a
+// unit's first item) in flight (it fetches the slots and gates of 32 units at a time, one
+// per lane, so that no per-item global load sits on its path); 4 lift warps compute the
+// features of each unit once (two 64-wide blocks each) up to two units ahead; 8 row warps
+// keep a unit's normalised features in registers, update each item's rows (2 rows per
+// warp), write them back with coalesced stores straight from registers and release the
+// stage.  (The step is instruction-bound, not DRAM-bound, so lifting once per head rather
+// than once per 16 rows is what matters.)  Loads of later items overlap the stores of earlier
+// ones continuously, where a CTA that holds its rows in registers for its whole life
+// reads, computes and writes in series.
 #include "kdn_internal.h"
+#include "tc_prims.cuh"
 
 namespace kdn {
 namespace {
 
 __device__ int g_decode_error;
 
-constexpr int kWarps = 4;
-constexpr int kRowsPerWarp = 4;
-constexpr int kRowsPerCta = kWarps * kRowsPerWarp;  // 16
+constexpr int kDecWarps = 8;                    // row warps (0..7)
+constexpr int kLiftWarp0 = kDecWarps;           // lift warps 8..11, two 64-wide feature blocks each
+constexpr int kLiftWarps = 4;
+constexpr int kDecLoader = kDecWarps + kLiftWarps;  // warp 12
+constexpr int kDecThr = 32 * (kDecWarps + kLiftWarps + 1);
+constexpr int kFeatBufs = 2;
+static_assert(2 * kLiftWarps == kMaxBlocks, "two feature blocks per lift warp");
+constexpr int kItemRows = 16;                   // state rows per work item
+constexpr int kStages = 6;
+constexpr uint32_t kStateBytes = kItemRows * kMaxBlocks * 64 * 4;  // 32 KiB: fp32 rows at D = 512
+constexpr uint32_t kStageBytes = kStateBytes + 128;                 // + v of the item's rows (below)
+constexpr uint32_t STG_V = kStateBytes;  // v of the item's 16 rows (64 B fp32 / 32 B bf16), bulk-loaded with them
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+// shared memory layout
+constexpr uint32_t DEC_STAGE = 0;                                   // kStages x 32 KiB
+constexpr uint32_t DEC_PHI = kStages * kStageBytes;                 // [2 items][k, q][512] floats
+constexpr uint32_t DEC_SS = DEC_PHI + 2 * 2 * kMaxBlocks * 64 * 4;  // [2 items][k, q][8] floats
+constexpr uint32_t DEC_META = DEC_SS + 2 * 2 * kMaxBlocks * 4;      // [kStages] int64 slot (or < 0)
+constexpr uint32_t DEC_GATE = DEC_META + kStages * 8;               // [kStages] {beta, decay}
+constexpr uint32_t DEC_PH = DEC_GATE + kStages * 8;                 // phase b[D]
+constexpr uint32_t DEC_QK = DEC_PH + kMaxBlocks * 64 * 4;           // [2 units][q, k][d_k] (fp32 or bf16)
+constexpr uint32_t DEC_QKV = DEC_QK + 2 * 2 * kDk * 4;              // [2 units] int: the unit has a valid slot
+constexpr uint32_t DEC_BAR = DEC_QKV + 16;                          // full, empty: [kStages] each, then
+                                                                    // feat_ready, feat_free, qk_full, qk_free: [2] each
+constexpr uint32_t kDecSmem = DEC_BAR + (2 * kStages + 4 * kFeatBufs) * 8;
 
 template <typename ST>
 struct StateIO;
@@ -43,122 +76,291 @@ struct StateIO<__nv_bfloat16> {
   }
 };
 
-template <typename ST>
-__global__ void __launch_bounds__(kWarps * 32) decode_kernel(DecodeProblem p, ProjParams P) {
-  __shared__ float s_phi[2][kMaxBlocks * 64];  // un-normalised cos features of k (0) and q (1)
-  __shared__ float s_ss[2][kWarps];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int rg = blockIdx.x, h = blockIdx.y;
-  const int64_t t = blockIdx.z;
-  const int D = 64 * P.M;
-  const int64_t th = t * p.H + h;
-  const int row0 = rg * kRowsPerCta + warp * kRowsPerWarp;
-
-  int64_t slot = p.index_dtype == KDN_INDEX_I64 ? reinterpret_cast<const int64_t*>(p.slot_mapping)[t]
-                                                : int64_t(reinterpret_cast<const int32_t*>(p.slot_mapping)[t]);
-  if (slot < 0 || slot >= p.num_slots) {
-    if (slot >= p.num_slots && threadIdx.x == 0 && rg == 0) record_device_error(&g_decode_error, kErrSlotOutOfRange);
-    if (lane < kRowsPerWarp) st_from_f32(p.out, p.out_dtype, th * p.dv + row0 + lane, 0.f);
-    return;
+// bounded wait; after one wait has given up, the others of the CTA give up at once
+__device__ __forceinline__ bool dec_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  uint32_t n = 0;
+  while (!tc::mbar_try_wait(bar, parity)) {
+    if ((++n & 1023u) == 0 && (n >= kWaitLimit || *abort)) {
+      *abort = 1;
+      return false;
+    }
   }
-  ST* Srow = reinterpret_cast<ST*>(p.states) + ((slot * p.H + h) * int64_t(p.dv) + row0) * D;
+  return true;
+}
 
-  // 1. issue the state loads first; the lift below overlaps their latency
-  float2 s[kRowsPerWarp][kMaxBlocks];
-#pragma unroll
-  for (int r = 0; r < kRowsPerWarp; ++r)
-#pragma unroll
-    for (int m = 0; m < kMaxBlocks; ++m)
-      s[r][m] = (m < P.M) ? StateIO<ST>::load(Srow + int64_t(r) * D + 64 * m + 2 * lane) : make_float2(0.f, 0.f);
+// the state rows of group g of unit (token, head) th = t * H + h
+template <typename ST>
+__device__ __forceinline__ int64_t rows_offset(int64_t slot, int64_t th, const DecodeProblem& p, int g, int D) {
+  return ((slot * p.H + th % p.H) * int64_t(p.dv) + int64_t(g) * kItemRows) * D;
+}
 
-  // 2. lift: warp w handles blocks m = w, w+4 of both k and q
-  {
-    float ss[2] = {0.f, 0.f};
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const float2 xv = ld2_as_f32(which ? p.q : p.k, p.in_dtype, th * kDk + 2 * lane);
-#pragma unroll
-      for (int mm = 0; mm < kMaxBlocks / kWarps; ++mm) {
-        const int m = warp + kWarps * mm;
-        if (m < P.M) {
-          float u0, u1;
-          structured_block(xv.x, xv.y, P.sign_bits[m], lane, u0, u1);
-          const int f = 64 * m + 2 * lane;
-          const float c0 = P.amp * cosf(fmaf(u0, P.tau_inv, P.phase[f]));
-          const float c1 = P.amp * cosf(fmaf(u1, P.tau_inv, P.phase[f + 1]));
-          s_phi[which][f] = c0;
-          s_phi[which][f + 1] = c1;
-          ss[which] = fmaf(c0, c0, fmaf(c1, c1, ss[which]));
+template <typename ST>
+__global__ void __launch_bounds__(kDecThr, 1) decode_kernel(DecodeProblem p, ProjParams P) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + DEC_BAR);
+  uint64_t* empty = full + kStages;
+  uint64_t* feat_ready = empty + kStages;      // [2] features of an item computed (8 lift warps)
+  uint64_t* feat_free = feat_ready + kFeatBufs;  // [2] features copied to registers (8 row warps)
+  uint64_t* qk_full = feat_free + kFeatBufs;     // [2] a unit's q and k loaded (bytes)
+  uint64_t* qk_free = qk_full + kFeatBufs;       // [2] a unit's q and k read (8 lift warps)
+  int* qk_valid = reinterpret_cast<int*>(sm + DEC_QKV);
+  int64_t* meta = reinterpret_cast<int64_t*>(sm + DEC_META);
+  __shared__ int abort_flag;
+  volatile int* abort = &abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int D = 64 * P.M;
+  const int G = p.dv / kItemRows;
+  const uint32_t item_bytes = uint32_t(kItemRows) * uint32_t(D) * uint32_t(sizeof(ST));
+  const int64_t units = p.num_tokens * p.H;  // (token, head) pairs
+  bool ok = true;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], kDecWarps);  // the row warps are done with the stage
+    }
+    for (int b = 0; b < kFeatBufs; ++b) {
+      tc::mbar_init(&feat_ready[b], kLiftWarps);
+      tc::mbar_init(&feat_free[b], kDecWarps);
+      tc::mbar_init(&qk_full[b], 1);
+      tc::mbar_init(&qk_free[b], kLiftWarps);
+    }
+    abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  for (int f = tid; f < D; f += kDecThr) reinterpret_cast<float*>(sm + DEC_PH)[f] = P.phase[f];
+  __syncthreads();
+
+  if (warp == kDecLoader) {
+    // ================================================================ loads
+    uint32_t pe = 0, pq = 0;  // phase bits per stage / per q-k buffer
+    int k = 0, n = 0;         // items, units so far
+    const uint32_t esz = p.in_dtype == KDN_DTYPE_BF16 ? 2u : 4u;
+    for (int64_t u0 = blockIdx.x; u0 < units; u0 += int64_t(gridDim.x) * 32) {
+      // slots and gates of the next 32 units of this CTA, one per lane
+      const int64_t mine = u0 + int64_t(lane) * gridDim.x;
+      int64_t slot = -1;
+      float gb = 0.f, gd = 1.f;
+      if (mine < units) {
+        const int64_t t = mine / p.H;
+        slot = p.index_dtype == KDN_INDEX_I64 ? reinterpret_cast<const int64_t*>(p.slot_mapping)[t]
+                                              : int64_t(reinterpret_cast<const int32_t*>(p.slot_mapping)[t]);
+        if (slot >= p.num_slots && mine % p.H == 0) record_device_error(&g_decode_error, kErrSlotOutOfRange);
+        gb = ld_as_f32(p.beta, p.gate_dtype, mine);
+        gd = p.decay ? ld_as_f32(p.decay, p.gate_dtype, mine) : 1.f;
+      }
+      for (int j = 0; j < 32; ++j) {
+        const int64_t th = u0 + int64_t(j) * gridDim.x;
+        if (th >= units) break;
+        const int64_t sj = __shfl_sync(0xffffffffu, slot, j);
+        const float bj = __shfl_sync(0xffffffffu, gb, j), dj = __shfl_sync(0xffffffffu, gd, j);
+        if (lane != 0) {
+          k += G;
+          ++n;
+          continue;
+        }
+        const bool valid = sj >= 0 && sj < p.num_slots;
+        {  // the unit's q and k, for its features
+          const int b = n % kFeatBufs;
+          if (n >= kFeatBufs) {
+            ok &= dec_wait(&qk_free[b], (pq >> b) & 1u, abort);
+            pq ^= 1u << b;
+          }
+          qk_valid[b] = valid ? 1 : 0;
+          if (valid) {
+            const uint32_t dst = tc::smem_u32(sm + DEC_QK) + b * 2 * kDk * 4;
+            tc::mbar_arrive_expect_tx(&qk_full[b], 2 * kDk * esz);
+            tc::bulk_load(dst, static_cast<const uint8_t*>(p.q) + th * kDk * esz, kDk * esz, &qk_full[b]);
+            tc::bulk_load(dst + kDk * 4, static_cast<const uint8_t*>(p.k) + th * kDk * esz, kDk * esz, &qk_full[b]);
+          } else {
+            tc::mbar_arrive(&qk_full[b]);
+          }
+          ++n;
+        }
+        for (int g = 0; g < G; ++g, ++k) {
+          const int st = k % kStages;
+          if (k >= kStages) {
+            ok &= dec_wait(&empty[st], (pe >> st) & 1u, abort);
+            pe ^= 1u << st;
+          }
+          meta[st] = valid ? sj : -1;
+          if (valid) {
+            reinterpret_cast<float2*>(sm + DEC_GATE)[st] = make_float2(bj, dj);
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.states) +
+                                 rows_offset<ST>(sj, th, p, g, D) * int64_t(sizeof(ST));
+            const uint32_t stage = tc::smem_u32(sm + DEC_STAGE + st * kStageBytes);
+            tc::mbar_arrive_expect_tx(&full[st], item_bytes + kItemRows * esz);
+            for (uint32_t o = 0; o < item_bytes; o += 16384) {
+              const uint32_t n = item_bytes - o < 16384 ? item_bytes - o : 16384;
+              tc::bulk_load(stage + o, src + o, n, &full[st]);
+            }
+            tc::bulk_load(stage + STG_V,
+                          static_cast<const uint8_t*>(p.v) + (th * int64_t(p.dv) + int64_t(g) * kItemRows) * esz,
+                          kItemRows * esz, &full[st]);
+          } else {
+            tc::mbar_arrive(&full[st]);  // nothing to load: the row warps zero the outputs
+          }
         }
       }
+      __syncwarp();
     }
-    ss[0] = warp_sum(ss[0]);
-    ss[1] = warp_sum(ss[1]);
-    if (lane == 0) {
-      s_ss[0][warp] = ss[0];
-      s_ss[1][warp] = ss[1];
+  } else if (warp >= kLiftWarp0 && warp < kLiftWarp0 + kLiftWarps) {
+    // ================================================================ lift warps (blocks w, w + 4)
+    const int w = warp - kLiftWarp0;
+    const float* ph = reinterpret_cast<const float*>(sm + DEC_PH);
+    uint64_t bits[2][3] = {};  // the blocks' sign words, selected with static indices (a run-time
+#pragma unroll                // index into the parameter block would copy it to local memory)
+    for (int mm = 0; mm < kMaxBlocks; ++mm)
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        if (mm == w + kLiftWarps * e)
+          bits[e][0] = P.sign_bits[mm][0], bits[e][1] = P.sign_bits[mm][1], bits[e][2] = P.sign_bits[mm][2];
+    uint32_t pq = 0, pfree = 0;
+    int n = 0;  // units so far
+    for (int64_t th = blockIdx.x; th < units; th += gridDim.x, ++n) {
+      const int buf = n % kFeatBufs;
+      if (n >= kFeatBufs) {  // the row warps have taken this buffer's previous features
+        ok &= dec_wait(&feat_free[buf], (pfree >> buf) & 1u, abort);
+        pfree ^= 1u << buf;
+      }
+      ok &= dec_wait(&qk_full[buf], (pq >> buf) & 1u, abort);
+      pq ^= 1u << buf;
+      float* phi = reinterpret_cast<float*>(sm + DEC_PHI) + buf * 2 * kMaxBlocks * 64;
+      float* ss = reinterpret_cast<float*>(sm + DEC_SS) + buf * 2 * kMaxBlocks;
+      const uint8_t* qk = sm + DEC_QK + buf * 2 * kDk * 4;
+      if (qk_valid[buf]) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int m = w + kLiftWarps * e;
+          if (m >= P.M) continue;
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            const float2 xv = ld2_as_f32(qk + (which ? 0 : kDk * 4), p.in_dtype, 2 * lane);
+            float u0, u1;
+            structured_block(xv.x, xv.y, bits[e], lane, u0, u1);
+            const int f = 64 * m + 2 * lane;
+            const float c0 = P.amp * cosf(fmaf(u0, P.tau_inv, ph[f]));
+            const float c1 = P.amp * cosf(fmaf(u1, P.tau_inv, ph[f + 1]));
+            phi[which * kMaxBlocks * 64 + f] = c0;
+            phi[which * kMaxBlocks * 64 + f + 1] = c1;
+            const float sw = warp_sum(fmaf(c0, c0, c1 * c1));
+            if (lane == 0) ss[which * kMaxBlocks + m] = sw;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(&qk_free[buf]);
+        tc::mbar_arrive(&feat_ready[buf]);
+      }
+    }
+  } else if (warp < kDecWarps) {
+    // ================================================================ row warps (2 rows each)
+    uint32_t pf = 0, pready = 0;
+    int k = 0, n = 0;
+    for (int64_t th = blockIdx.x; th < units; th += gridDim.x, ++n) {
+      const int buf = n % kFeatBufs;
+      float2 fk[kMaxBlocks], fq[kMaxBlocks];
+      float kq = 0.f;
+      for (int g = 0; g < G; ++g, ++k) {
+        const int st = k % kStages;
+        ok &= dec_wait(&full[st], (pf >> st) & 1u, abort);  // the item's state rows and v
+        pf ^= 1u << st;
+        const int64_t slot = meta[st];
+        if (g == 0) {  // the unit's features: normalised into registers, then the buffer is released
+          ok &= dec_wait(&feat_ready[buf], (pready >> buf) & 1u, abort);
+          pready ^= 1u << buf;
+          const float* phi = reinterpret_cast<const float*>(sm + DEC_PHI) + buf * 2 * kMaxBlocks * 64;
+          const float* ss = reinterpret_cast<const float*>(sm + DEC_SS) + buf * 2 * kMaxBlocks;
+          float nk = 0.f, nq = 0.f;
+          for (int m = 0; m < P.M; ++m) {
+            nk += ss[m];
+            nq += ss[kMaxBlocks + m];
+          }
+          const float sk = 1.0f / (sqrtf(nk) + 1e-8f), sq = 1.0f / (sqrtf(nq) + 1e-8f);
+          kq = 0.f;
+#pragma unroll
+          for (int m = 0; m < kMaxBlocks; ++m) {
+            fk[m] = make_float2(0.f, 0.f);
+            fq[m] = make_float2(0.f, 0.f);
+            if (m < P.M) {
+              const int f = 64 * m + 2 * lane;
+              fk[m] = make_float2(phi[f] * sk, phi[f + 1] * sk);
+              fq[m] = make_float2(phi[kMaxBlocks * 64 + f] * sq, phi[kMaxBlocks * 64 + f + 1] * sq);
+              kq = fmaf(fk[m].x, fq[m].x, fmaf(fk[m].y, fq[m].y, kq));
+            }
+          }
+          if (p.readout == KDN_READOUT_POST) kq = warp_sum(kq);
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&feat_free[buf]);
+        }
+        const uint8_t* stg = sm + DEC_STAGE + st * kStageBytes;
+        const float2 gate = reinterpret_cast<const float2*>(sm + DEC_GATE)[st];
+        const float beta = gate.x, lam = gate.y;
+        const ST* stage = reinterpret_cast<const ST*>(stg);
+        ST* gstate = slot >= 0 ? reinterpret_cast<ST*>(p.states) + rows_offset<ST>(slot, th, p, g, D) : nullptr;
+#pragma unroll
+        for (int rr = 0; rr < kItemRows / kDecWarps; ++rr) {
+          const int r = warp * (kItemRows / kDecWarps) + rr;  // row within the item
+          const int64_t orow = th * p.dv + int64_t(g) * kItemRows + r;
+          if (slot < 0) {  // padding token (or a slot out of range): zero output, state untouched
+            if (lane == 0) st_from_f32(p.out, p.out_dtype, orow, 0.f);
+            continue;
+          }
+          const ST* row = stage + int64_t(r) * D;
+          ST* grow = gstate + int64_t(r) * D;
+          float2 sv[kMaxBlocks];
+          float dk = 0.f, dq = 0.f;
+#pragma unroll
+          for (int m = 0; m < kMaxBlocks; ++m) {
+            sv[m] = (m < P.M) ? StateIO<ST>::load(row + 64 * m + 2 * lane) : make_float2(0.f, 0.f);
+            dk = fmaf(sv[m].x, fk[m].x, fmaf(sv[m].y, fk[m].y, dk));
+            dq = fmaf(sv[m].x, fq[m].x, fmaf(sv[m].y, fq[m].y, dq));
+          }
+          dk = warp_sum(dk);
+          dq = warp_sum(dq);
+          const float coef = beta * (ld_as_f32(stg + STG_V, p.in_dtype, r) - lam * dk);
+#pragma unroll
+          for (int m = 0; m < kMaxBlocks; ++m)  // written back straight to the slot pool
+            if (m < P.M)
+              StateIO<ST>::store(grow + 64 * m + 2 * lane, fmaf(lam, sv[m].x, coef * fk[m].x),
+                                 fmaf(lam, sv[m].y, coef * fk[m].y));
+          if (lane == 0) {
+            const float yv = p.readout == KDN_READOUT_POST ? fmaf(lam, dq, coef * kq) : dq;
+            st_from_f32(p.out, p.out_dtype, orow, yv);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[st]);  // this warp has read its rows of the stage
+      }
     }
   }
+  if (!ok) record_device_error(&g_decode_error, kErrDecodeWaitTimeout);
   __syncthreads();
-  float nk = 0.f, nq = 0.f;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    nk += s_ss[0][w];
-    nq += s_ss[1][w];
-  }
-  const float sk = 1.0f / (sqrtf(nk) + 1e-8f), sq = 1.0f / (sqrtf(nq) + 1e-8f);
-  float2 fk[kMaxBlocks], fq[kMaxBlocks];
-  float kq = 0.f;
-#pragma unroll
-  for (int m = 0; m < kMaxBlocks; ++m) {
-    fk[m] = make_float2(0.f, 0.f);
-    fq[m] = make_float2(0.f, 0.f);
-    if (m < P.M) {
-      const int f = 64 * m + 2 * lane;
-      fk[m] = make_float2(s_phi[0][f] * sk, s_phi[0][f + 1] * sk);
-      fq[m] = make_float2(s_phi[1][f] * sq, s_phi[1][f + 1] * sq);
-      kq = fmaf(fk[m].x, fq[m].x, fmaf(fk[m].y, fq[m].y, kq));
-    }
-  }
-  if (p.readout == KDN_READOUT_POST) kq = warp_sum(kq);
-
-  const float beta = ld_as_f32(p.beta, p.gate_dtype, th);
-  const float lam = p.decay ? ld_as_f32(p.decay, p.gate_dtype, th) : 1.0f;
-
-  // 3. per row: the two dot products, the rank-1 update, the write-back
-#pragma unroll
-  for (int r = 0; r < kRowsPerWarp; ++r) {
-    float dk = 0.f, dq = 0.f;
-#pragma unroll
-    for (int m = 0; m < kMaxBlocks; ++m) {
-      dk = fmaf(s[r][m].x, fk[m].x, fmaf(s[r][m].y, fk[m].y, dk));
-      dq = fmaf(s[r][m].x, fq[m].x, fmaf(s[r][m].y, fq[m].y, dq));
-    }
-    dk = warp_sum(dk);
-    dq = warp_sum(dq);
-    const float vr = ld_as_f32(p.v, p.in_dtype, th * p.dv + row0 + r);
-    const float coef = beta * (vr - lam * dk);
-#pragma unroll
-    for (int m = 0; m < kMaxBlocks; ++m)
-      if (m < P.M)
-        StateIO<ST>::store(Srow + int64_t(r) * D + 64 * m + 2 * lane, fmaf(lam, s[r][m].x, coef * fk[m].x),
-                           fmaf(lam, s[r][m].y, coef * fk[m].y));
-    if (lane == r) {
-      const float yv = p.readout == KDN_READOUT_POST ? fmaf(lam, dq, coef * kq) : dq;
-      st_from_f32(p.out, p.out_dtype, th * p.dv + row0 + r, yv);
-    }
-  }
 }
 
 }  // namespace
 
 cudaError_t launch_decode(const DecodeProblem& p, const ProjParams& P, cudaStream_t stream) {
   if (p.num_tokens == 0) return cudaSuccess;
-  dim3 grid(p.dv / kRowsPerCta, p.H, unsigned(p.num_tokens));
-  if (p.state_dtype == KDN_DTYPE_BF16)
-    decode_kernel<__nv_bfloat16><<<grid, kWarps * 32, 0, stream>>>(p, P);
-  else
-    decode_kernel<float><<<grid, kWarps * 32, 0, stream>>>(p, P);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  const int64_t items = p.num_tokens * p.H * (p.dv / kItemRows);
+  const unsigned grid = unsigned(items < sms ? items : sms);
+  cudaError_t e;
+  if (p.state_dtype == KDN_DTYPE_BF16) {
+    e = cudaFuncSetAttribute(decode_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmem));
+    if (e != cudaSuccess) return e;
+    decode_kernel<__nv_bfloat16><<<grid, kDecThr, kDecSmem, stream>>>(p, P);
+  } else {
+    e = cudaFuncSetAttribute(decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmem));
+    if (e != cudaSuccess) return e;
+    decode_kernel<float><<<grid, kDecThr, kDecSmem, stream>>>(p, P);
+  }
   return cudaGetLastError();
 }
 

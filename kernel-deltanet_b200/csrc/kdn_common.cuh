@@ -114,5 +114,8 @@ __device__ __forceinline__ void record_device_error(int* word, int code) { atomi
 
 // device error codes
 constexpr int kErrSlotOutOfRange = 1;
+constexpr int kErrTcWaitTimeout = 2;     // fused tensor-core prefill: a bounded wait gave up
+constexpr int kErrSplitWaitTimeout = 3;  // two-phase prefill: a bounded wait gave up
+constexpr int kErrDecodeWaitTimeout = 4; // decode: a bounded wait gave up
 
 }  // namespace kdn

@@ -1132,7 +1132,7 @@ __device__ __forceinline__ uint32_t split_tmem_alloc(uint8_t* sm, uint32_t cols)
 }
 
 __device__ __forceinline__ void split_finish(uint32_t tmem, uint32_t cols, bool ok) {
-  if (!ok) record_device_error(&g_split_error, 3);
+  if (!ok) record_device_error(&g_split_error, kErrSplitWaitTimeout);
   tc::fence_before_sync();
   __syncthreads();
   if ((threadIdx.x >> 5) == 0) tc::tmem_dealloc(tmem, cols);

@@ -554,7 +554,7 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
     }
     tc::cp_async_wait_all();
   }
-  if (!ok) record_device_error(&g_tc_error, 2);
+  if (!ok) record_device_error(&g_tc_error, kErrTcWaitTimeout);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
