@@ -235,6 +235,45 @@ def bench_decode(dev, steps, warmup, peaks):
                          "note": f"state 128 MiB ~ L2 126 MB; peak {peaks['src']}"}}
 
 
+RAGGED_LENS = [128, 1024, 8192, 16384]  # the reference's ragged-batch example (serving/vllm_ragged_batching.py)
+
+
+def bench_ragged(dev, steps, warmup):
+    """Ragged prefill of four requests of different lengths x 16 heads over a slot pool (bf16 inputs)."""
+    import torch
+
+    import kdn_b200
+
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    total = sum(RAGGED_LENS)
+    g = torch.Generator(device=dev).manual_seed(11)
+    q = torch.nn.functional.normalize(torch.randn(total, H, DK, generator=g, device=dev), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(total, H, DK, generator=g, device=dev), dim=-1).bfloat16()
+    v = torch.randn(total, H, DV, generator=g, device=dev).bfloat16()
+    beta = torch.sigmoid(torch.randn(total, H, generator=g, device=dev))
+    cu = torch.tensor([0] + list(__import__("itertools").accumulate(RAGGED_LENS)), device=dev)
+    pool = torch.zeros(8, H, DV, D, device=dev)
+    slots = torch.tensor([5, 0, 3, 6], device=dev)
+    out = torch.empty(total, H, DV, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        kdn_b200.ragged_prefill(q, k, v, beta, None, cu, pool, slots, out, proj, mode="bf16")
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"metric": f"ragged prefill tokens/s ({len(RAGGED_LENS)} requests of {RAGGED_LENS} tokens x {H} heads, "
+                      "slot pool, bf16)", "value": total / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "steps": steps}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -325,6 +364,7 @@ def run_ours(args):
         e2e_ms = float(t.item())
 
     dec = bench_decode(dev, steps=200, warmup=5, peaks=peaks)
+    rag = bench_ragged(dev, steps=10, warmup=3)
 
     if world > 1:
         dist.barrier()
@@ -388,6 +428,7 @@ def run_ours(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk,
         "decode": dec,
+        "ragged": rag,
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.ref_seq)

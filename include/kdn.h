@@ -156,6 +156,19 @@ int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int 
                                int32_t chunk, const kdn_projection* proj, void* stream);
 
 /*
+ * Layout change of a ragged serving batch (no reference counterpart; the reference packs
+ * requests the same way, serving/vllm_ragged_batching.py:57-67, then loops over them).
+ * Element (sequence i, token t, head h) of the packed [total_tokens, H, row] tensor sits at
+ * ((cu[i] + t) * H + h); in the head-major form sequence i is one [H, T_i, row] block
+ * starting at cu[i] * H, the layout kdn_chunked_prefill reads.  to_head_major = 1 packs ->
+ * head-major, 0 the reverse.  cu_seqlens: device [num_seqs + 1] (index_dtype), nondecreasing
+ * from 0 to total_tokens (rows outside that are left untouched).  row_bytes: bytes per (token,
+ * head) row.  src and dst must not overlap.
+ */
+int kdn_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype, int64_t num_seqs,
+                         int64_t total_tokens, int32_t H, int64_t row_bytes, int to_head_major, void* stream);
+
+/*
  * Strided block copy for streaming a sequence segment between host and device (no
  * reference counterpart): `rows` blocks of `width_bytes`, `src_pitch` / `dst_pitch` bytes
  * apart, copied on `stream` in either direction (host memory should be pinned for the copy

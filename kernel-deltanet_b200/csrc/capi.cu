@@ -234,6 +234,22 @@ int kdn_set_prefill_events(void* const* events, int count) {
 
 int kdn_prefill_launch_count(void) { return g_last_prefill_launches; }
 
+int kdn_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype, int64_t num_seqs,
+                         int64_t total_tokens, int32_t H, int64_t row_bytes, int to_head_major, void* stream) {
+  if (total_tokens == 0) return ok();
+  if (!src || !dst || !cu_seqlens) return fail(KDN_ERR_INVALID, "src/dst/cu_seqlens is NULL");
+  if (num_seqs < 1 || total_tokens < 0 || H < 1 || row_bytes < 1)
+    return fail(KDN_ERR_INVALID, "num_seqs=%lld total=%lld H=%d row_bytes=%lld", (long long)num_seqs,
+                (long long)total_tokens, H, (long long)row_bytes);
+  if (index_dtype != KDN_INDEX_I32 && index_dtype != KDN_INDEX_I64) return fail(KDN_ERR_INVALID, "bad index dtype");
+  const size_t bytes = size_t(total_tokens) * H * size_t(row_bytes);
+  if (overlaps(src, bytes, dst, bytes)) return fail(KDN_ERR_INVALID, "src and dst overlap");
+  cudaError_t e = kdn::launch_ragged_transpose(src, dst, cu_seqlens, index_dtype, num_seqs, total_tokens, H, row_bytes,
+                                               to_head_major, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "ragged transpose launch");
+  return ok();
+}
+
 int kdn_copy_rows(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes, size_t rows,
                   void* stream) {
   if (rows == 0 || width_bytes == 0) return ok();

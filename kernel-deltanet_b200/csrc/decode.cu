@@ -349,8 +349,8 @@ cudaError_t launch_decode(const DecodeProblem& p, const ProjParams& P, cudaStrea
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       sms = 148;
   }
-  const int64_t items = p.num_tokens * p.H * (p.dv / kItemRows);
-  const unsigned grid = unsigned(items < sms ? items : sms);
+  const int64_t units = p.num_tokens * p.H;  // (token, head) pairs, walked by persistent CTAs
+  const unsigned grid = unsigned(units < sms ? units : sms);
   cudaError_t e;
   if (p.state_dtype == KDN_DTYPE_BF16) {
     e = cudaFuncSetAttribute(decode_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmem));

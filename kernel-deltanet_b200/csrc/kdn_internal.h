@@ -87,6 +87,12 @@ cudaError_t launch_affine_prefix_states(const float* A, const float* B, const fl
                                         float* final_state, int64_t n_c, int64_t batch, int D, int dv,
                                         cudaStream_t stream);
 
+// ---------------------------------------------------------------- ragged.cu
+// rows of a packed [total, H, w] batch <-> per-sequence head-major [H, T_i, w] blocks
+cudaError_t launch_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype,
+                                    int64_t num_seqs, int64_t total_tokens, int H, int64_t row_bytes,
+                                    int to_head_major, cudaStream_t stream);
+
 // ---------------------------------------------------------------- decode.cu
 struct DecodeProblem {
   const void* q;
