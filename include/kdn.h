@@ -156,6 +156,22 @@ int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int 
                                int32_t chunk, const kdn_projection* proj, void* stream);
 
 /*
+ * Row-parallel output projection with its all-reduce fused in (head tensor parallelism,
+ * serving/tensor_parallel_runner.py:51-75; experiments/run_kaggle_dual_gpu_cluster.py:99-112
+ * run a local GEMM and then an all-reduce).  y: [M, K] bf16 (this rank's heads' outputs),
+ * w: [N, K] bf16 (this rank's slice of the projection), both row-major; the kernel computes
+ * y w^T on the tensor cores with fp32 accumulation and
+ *   - with out_multicast (the NVSwitch multicast address of a symmetric [M, N] fp32 buffer):
+ *     adds each tile into every member's copy (multimem.red); the buffer must be zero on
+ *     every rank before any rank launches, and a barrier across ranks must follow before
+ *     the sum is read -- the caller owns both steps;
+ *   - otherwise stores y w^T into out ([M, N] fp32).
+ * N % 256 == 0, K % 64 == 0, pointers 16-byte aligned.  No reference entry point.
+ */
+int kdn_tp_out_proj(const void* y, const void* w, float* out, float* out_multicast, int64_t M, int32_t N, int32_t K,
+                    void* stream);
+
+/*
  * Layout change of a ragged serving batch (no reference counterpart; the reference packs
  * requests the same way, serving/vllm_ragged_batching.py:57-67, then loops over them).
  * Element (sequence i, token t, head h) of the packed [total_tokens, H, row] tensor sits at

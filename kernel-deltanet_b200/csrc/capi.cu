@@ -234,6 +234,20 @@ int kdn_set_prefill_events(void* const* events, int count) {
 
 int kdn_prefill_launch_count(void) { return g_last_prefill_launches; }
 
+int kdn_tp_out_proj(const void* y, const void* w, float* out, float* out_multicast, int64_t M, int32_t N, int32_t K,
+                    void* stream) {
+  if (M < 0 || M > (int64_t(65535) * 128)) return fail(KDN_ERR_INVALID, "M=%lld outside [0, 65535*128]", (long long)M);
+  if (M == 0) return ok();
+  if (N < 256 || N % 256 != 0 || N > 65535 * 256) return fail(KDN_ERR_UNSUPPORTED, "N=%d: a positive multiple of 256", N);
+  if (K < 64 || K % 64 != 0) return fail(KDN_ERR_UNSUPPORTED, "K=%d: a positive multiple of 64", K);
+  if (!y || !w || (!out && !out_multicast)) return fail(KDN_ERR_INVALID, "y/w/out is NULL");
+  if (!aligned(y, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(out_multicast, 16))
+    return fail(KDN_ERR_INVALID, "y/w/out must be 16-byte aligned");
+  cudaError_t e = kdn::launch_tp_proj(y, w, out, out_multicast, M, N, K, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-parallel projection launch");
+  return ok();
+}
+
 int kdn_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype, int64_t num_seqs,
                          int64_t total_tokens, int32_t H, int64_t row_bytes, int to_head_major, void* stream) {
   if (total_tokens == 0) return ok();
@@ -447,7 +461,10 @@ int kdn_device_error(void* stream, int* code_out) {
   if (e != cudaSuccess) return cuda_fail(e, "device error read");
   e = kdn::split_read_error(static_cast<cudaStream_t>(stream), &code_split);
   if (e != cudaSuccess) return cuda_fail(e, "device error read");
-  *code_out = code ? code : (code_tc ? code_tc : code_split);
+  int code_proj = 0;
+  e = kdn::tp_proj_read_error(static_cast<cudaStream_t>(stream), &code_proj);
+  if (e != cudaSuccess) return cuda_fail(e, "device error read");
+  *code_out = code ? code : (code_tc ? code_tc : (code_split ? code_split : code_proj));
   return ok();
 }
 

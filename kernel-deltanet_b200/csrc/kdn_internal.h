@@ -87,6 +87,13 @@ cudaError_t launch_affine_prefix_states(const float* A, const float* B, const fl
                                         float* final_state, int64_t n_c, int64_t batch, int D, int dv,
                                         cudaStream_t stream);
 
+// ---------------------------------------------------------------- tp_proj.cu
+// out (+)= Y W^T across ranks: stores into `out`, or adds into every rank's copy through the
+// multicast address `out_mc` when given.  N % 256 == 0, K % 64 == 0.
+cudaError_t launch_tp_proj(const void* Y, const void* W, float* out, float* out_mc, int64_t M, int N, int K,
+                           cudaStream_t stream);
+cudaError_t tp_proj_read_error(cudaStream_t stream, int* code);
+
 // ---------------------------------------------------------------- ragged.cu
 // rows of a packed [total, H, w] batch <-> per-sequence head-major [H, T_i, w] blocks
 cudaError_t launch_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype,

@@ -59,6 +59,7 @@ SIGNATURES = {
                                           ctypes.POINTER(KdnProjection), _P]),
     "kdn_set_prefill_events": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT]),
     "kdn_prefill_launch_count": (_INT, []),
+    "kdn_tp_out_proj": (_INT, [_P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "kdn_ragged_transpose": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I32, _I64, _INT, _P]),
     "kdn_copy_rows": (_INT, [_P, ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _P]),
     "kdn_affine_compose": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),

@@ -23,6 +23,14 @@ Two ways to spread the work:
 The host orchestration (``entering_state``) takes the prefix fold as an argument
 so that its rank logic runs under any backend; the library fold
 (``kdn_affine_prefix_states``) is the default.
+
+* Head tensor parallelism, output side (``row_parallel_out_proj``): rank r holds the
+  scan outputs of its heads and its slice of the output projection; the layer output
+  sum_r Y_r W_r^T is needed on every rank (serving/tensor_parallel_runner.py:51-75 runs a
+  local GEMM, then an all-reduce).  One kernel (``kdn_tp_out_proj``) computes the tiles on
+  the tensor cores and adds each into every rank's copy of a symmetric output buffer through
+  its NVSwitch multicast address; a zeroing + barrier before and a barrier after (bounded,
+  from torch's symmetric memory) frame it.
 """
 
 from __future__ import annotations
@@ -117,3 +125,78 @@ def sequence_parallel_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         A, B = chunk_block_transition(k, v, beta, decay, fwht_proj, chunk_size)
         S_in = entering_state(A, B, initial_state, group)
     return fused_chunked_deltanet_forward(q, k, v, beta, decay, fwht_proj, chunk_size, S_in, mode=mode)
+
+
+# ------------------------------------------------------------------ head-TP output projection
+_SYMM: dict = {}
+_BARRIER_TIMEOUT_MS = 60_000
+
+
+def _symmetric_output(M: int, N: int, dev: torch.device, group):
+    """A cached symmetric [M, N] fp32 buffer of `group` on `dev` and its handle."""
+    import torch.distributed._symmetric_memory as symm_mem
+
+    name = (group or dist.group.WORLD).group_name
+    key = (M, N, dev.index, name)
+    if key not in _SYMM:
+        buf = symm_mem.empty(M, N, dtype=torch.float32, device=dev)
+        hdl = symm_mem.rendezvous(buf, name)
+        _SYMM[key] = (buf, hdl)
+    return _SYMM[key]
+
+
+def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=None, *,
+                          allow_unfused: bool = False) -> Tuple[torch.Tensor, str]:
+    """sum over the ranks of `group` of y_local @ w_local^T, returned on every rank.
+
+    y_local [M, K] and w_local [N, K] (bfloat16; K = local heads x d_v; N % 256 == 0,
+    K % 64 == 0).  Returns (out [M, N] float32, path) with path "fused-multicast" (one
+    kernel: tensor-core tiles reduced into every rank's copy through NVSwitch), "local"
+    (one rank: the same kernel, stores) or, only when `allow_unfused` and the group has no
+    multicast support, "unfused-nccl" (the kernel's product, then an NCCL all-reduce: the
+    reference's two-step form).  The returned tensor of the fused path is the cached
+    symmetric buffer: it is overwritten by the next call with the same shape.
+    """
+    from . import _lib
+
+    if y_local.dim() != 2 or w_local.dim() != 2 or y_local.shape[1] != w_local.shape[1]:
+        raise RuntimeError(f"expected y [M, K] and w [N, K]; got {tuple(y_local.shape)}, {tuple(w_local.shape)}")
+    if not (y_local.is_cuda and w_local.is_cuda):
+        raise RuntimeError("kdn_b200 runs on CUDA tensors only (no CPU fallback)")
+    M, K = y_local.shape
+    N = w_local.shape[0]
+    dev = y_local.device
+    y = y_local.to(torch.bfloat16).contiguous()
+    w = w_local.to(torch.bfloat16).contiguous()
+    lib = _lib.load()
+    stream = _lib.stream_handle(dev)
+    _, world = _world(group)
+    if world == 1:
+        out = torch.empty(M, N, device=dev, dtype=torch.float32)
+        _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), out.data_ptr(), None, M, N, K, stream),
+                   "kdn_tp_out_proj")
+        return out, "local"
+    from torch._C._autograd import DeviceType
+    from torch._C._distributed_c10d import _SymmetricMemory
+
+    buf, hdl = _symmetric_output(M, N, dev, group)
+    if not _SymmetricMemory.has_multicast_support(DeviceType.CUDA, dev.index) or not hdl.multicast_ptr:
+        if not allow_unfused:
+            raise RuntimeError("no NVSwitch multicast for this group: the fused projection is unavailable "
+                               "(pass allow_unfused=True for the GEMM + NCCL all-reduce form)")
+        out = torch.empty(M, N, device=dev, dtype=torch.float32)
+        _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), out.data_ptr(), None, M, N, K, stream),
+                   "kdn_tp_out_proj")
+        dist.all_reduce(out, group=group)
+        return out, "unfused-nccl"
+    buf.zero_()
+    hdl.barrier(channel=0, timeout_ms=_BARRIER_TIMEOUT_MS)  # every copy is zero before anyone adds
+    _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), None, hdl.multicast_ptr, M, N, K, stream),
+               "kdn_tp_out_proj")
+    hdl.barrier(channel=0, timeout_ms=_BARRIER_TIMEOUT_MS)  # every rank's tiles are in every copy
+    return buf, "fused-multicast"
+
+
+def release_symmetric_buffers() -> None:
+    """Drop the cached symmetric output buffers (call before destroying the process group)."""
+    _SYMM.clear()

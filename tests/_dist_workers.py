@@ -146,3 +146,38 @@ def nccl_sequence_parallel(rank, world, port, result_path, mode):
         traceback.print_exc()
     with open(f"{result_path}.{rank}", "w") as f:
         f.write("ok" if ok else "fail")
+
+
+def nccl_tp_out_proj(rank, world, port, result_path, M, N, K):
+    """row_parallel_out_proj (fused multicast reduction) vs torch matmuls + NCCL all-reduce."""
+    ok = False
+    try:
+        import torch
+
+        from kdn_b200 import distributed as kd
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist = _init(rank, world, port, "nccl")
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        y = torch.randn(M, K, generator=g, device=dev).bfloat16()
+        w = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).bfloat16()
+        ref = y.float() @ w.float().t()
+        dist.all_reduce(ref)
+        paths = []
+        for _ in range(3):  # repeated calls reuse the symmetric buffer (zeroed every call)
+            out, path = kd.row_parallel_out_proj(y, w, allow_unfused=True)
+            torch.cuda.synchronize()
+            err = float((out - ref).abs().max() / ref.abs().max())
+            paths.append(path)
+        ok = err < 1e-4 and paths[0] in ("fused-multicast", "unfused-nccl")
+        print(f"rank {rank}: path {paths[0]} err {err:.3e}", flush=True)
+        with open(f"{result_path}.path", "w") as f:
+            f.write(paths[0])
+        kd.release_symmetric_buffers()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        traceback.print_exc()
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write("ok" if ok else "fail")

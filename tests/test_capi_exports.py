@@ -177,3 +177,11 @@ def test_block_transition_argument_checks(lib):
     assert call(dv=24) == 2
     assert call(v=None) == 1            # B asked without values
     assert call(A=None, B=None) == 0    # nothing asked
+
+
+def test_tp_out_proj_argument_checks(lib):
+    assert lib.kdn_tp_out_proj(4096, 8192, 16384, None, 128, 200, 64, None) == 2   # N not a multiple of 256
+    assert lib.kdn_tp_out_proj(4096, 8192, 16384, None, 128, 256, 48, None) == 2   # K not a multiple of 64
+    assert lib.kdn_tp_out_proj(4104, 8192, 16384, None, 128, 256, 64, None) == 1   # misaligned
+    assert lib.kdn_tp_out_proj(4096, 8192, None, None, 128, 256, 64, None) == 1    # no output
+    assert lib.kdn_tp_out_proj(4096, 8192, 16384, None, 0, 256, 64, None) == 0     # nothing to do
