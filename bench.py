@@ -274,6 +274,99 @@ def bench_ragged(dev, steps, warmup):
             "steps": steps}
 
 
+# head-TP layer of the reference's TP benchmark (serving/tensor_parallel_runner.py:84-87): B=2, T=16384,
+# d_model=2048, 16 heads x d_v=64, so the row-parallel output projection is [32768, 1024/world] x [1024/world, 2048]
+TP_M, TP_N, TP_HEADS, TP_DV = 2 * 16384, 2048, 16, 64
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (nominal 900)
+
+
+def bench_tp_out_proj(dev, rank, world, steps=10, warmup=3):
+    """Row-parallel output projection + all-reduce over `world` GPUs: the fused kernel in both forms
+    against the unfused forms (our GEMM + NCCL fp32 all-reduce; the reference's torch bf16 GEMM + NCCL
+    bf16 all-reduce).  Every rank takes part; times are max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import kdn_b200
+    from kdn_b200 import distributed as kd
+
+    lib = kdn_b200.load()
+    K = TP_HEADS * TP_DV // world
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    y = torch.randn(TP_M, K, generator=g, device=dev).bfloat16()
+    w = (torch.randn(TP_N, K, generator=g, device=dev) / K ** 0.5).bfloat16()
+    out32 = torch.empty(TP_M, TP_N, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def unfused():
+        kdn_b200._lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), out32.data_ptr(), 0, None, TP_M, TP_N,
+                                                K, stream), "kdn_tp_out_proj")
+        dist.all_reduce(out32)
+
+    def reference_form():
+        dist.all_reduce(y @ w.t())
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    res = {m: timed(lambda m=m: kd.row_parallel_out_proj(y, w, method=m)) for m in ("two-phase", "peer", "one-shot")}
+    res["peer_bf16"] = timed(lambda: kd.row_parallel_out_proj(y, w, method="peer", out_dtype=torch.bfloat16))
+    _, auto_path = kd.row_parallel_out_proj(y, w)
+    res["unfused_nccl_fp32"] = timed(unfused)
+    res["reference_torch_bf16_nccl"] = timed(reference_form)
+    err = {}
+    for m in ("two-phase", "peer", "peer_bf16"):
+        fused, _ = kd.row_parallel_out_proj(y, w, method=m[:4] if m == "peer_bf16" else m,
+                                            out_dtype=torch.bfloat16 if m == "peer_bf16" else torch.float32)
+        fused = fused.float()
+        unfused()
+        torch.cuda.synchronize()
+        err[m] = float((fused - out32).abs().max() / out32.abs().max())
+    kd.release_symmetric_buffers()
+    method = auto_path.replace("fused-", "")
+    out_bytes = TP_M * TP_N * 4
+    # per GPU and direction: two-phase (1 + 1/w) B, peer 2 (w - 1)/w B, one-shot w B (into each GPU)
+    link_bytes = out_bytes * {"two-phase": 1 + 1 / world, "peer": 2 * (world - 1) / world, "one-shot": world}[method]
+    t_link = link_bytes / (NVLINK_GBS * 1e9) * 1e3
+    t_tensor = 2 * TP_M * TP_N * K / (load_peaks()["bf16_tflops"] * 1e12) * 1e3
+    ms = res[method]
+    return {"metric": f"row-parallel out-proj + all-reduce ms ([{TP_M}, {K}] x [{K}, {TP_N}] per rank, fp32 sum)",
+            "value": ms, "unit": "ms", "higher_is_better": False, "auto_path": auto_path, "ms": res,
+            "max_rel_err_vs_nccl": err,
+            "roofline": {"bound": "nvlink", "achieved": link_bytes / (ms * 1e-3) / 1e9, "peak": NVLINK_GBS,
+                         "unit": "GB/s", "frac": max(t_link, t_tensor) / ms,
+                         "note": f"{method} form (the auto choice): {link_bytes / out_bytes:.3f} x {out_bytes} B per "
+                                 f"GPU and direction over NVLink "
+                                 f"({t_link:.3f} ms at {NVLINK_GBS:.0f} GB/s measured peer copy) vs tensor "
+                                 f"{t_tensor:.3f} ms; frac = max of both / measured"}}
+
+
+def run_tp_proj_only(args):
+    """Only the head-TP output projection comparison (world > 1 under torchrun)."""
+    import torch
+
+    rank, world, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world < 2:
+        raise SystemExit("--tp-proj-only needs 2 or more ranks (torchrun)")
+    r = bench_tp_out_proj(dev, rank, world, steps=args.steps, warmup=args.warmup)
+    if rank == 0:
+        print(json.dumps({"tp_out_proj": r, "n_gpus": world}), flush=True)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -365,6 +458,7 @@ def run_ours(args):
 
     dec = bench_decode(dev, steps=200, warmup=5, peaks=peaks)
     rag = bench_ragged(dev, steps=10, warmup=3)
+    tpp = bench_tp_out_proj(dev, rank, world) if world > 1 else None
 
     if world > 1:
         dist.barrier()
@@ -430,6 +524,8 @@ def run_ours(args):
         "decode": dec,
         "ragged": rag,
     }
+    if tpp is not None:
+        line["tp_out_proj"] = tpp
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.ref_seq)
     print(json.dumps(line), flush=True)
@@ -475,7 +571,15 @@ def main():
                     help="only run two prefill calls of N sequences x T tokens (for profiler captures)")
     ap.add_argument("--decode-only", type=int, metavar="STEPS",
                     help="only run the decode workload for STEPS steps (for profiler captures)")
+    ap.add_argument("--tp-proj-only", action="store_true",
+                    help="only compare the head-TP output projection forms (2+ ranks under torchrun)")
     args = ap.parse_args()
+    if args.tp_proj_only:
+        run_tp_proj_only(args)
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+        return
     if args.decode_only:
         run_decode_only(args.decode_only)
         return

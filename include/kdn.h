@@ -165,11 +165,42 @@ int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int 
  *     adds each tile into every member's copy (multimem.red); the buffer must be zero on
  *     every rank before any rank launches, and a barrier across ranks must follow before
  *     the sum is read -- the caller owns both steps;
- *   - otherwise stores y w^T into out ([M, N] fp32).
+ *   - otherwise stores y w^T into out ([M, N], out_dtype KDN_DTYPE_F32 or KDN_DTYPE_BF16).
  * N % 256 == 0, K % 64 == 0, pointers 16-byte aligned.  No reference entry point.
  */
-int kdn_tp_out_proj(const void* y, const void* w, float* out, float* out_multicast, int64_t M, int32_t N, int32_t K,
-                    void* stream);
+int kdn_tp_out_proj(const void* y, const void* w, void* out, int out_dtype, float* out_multicast, int64_t M, int32_t N,
+                    int32_t K, void* stream);
+
+/*
+ * The two-phase (bandwidth-optimal) form of kdn_tp_out_proj for the same sum over ranks.
+ * Every rank stores its tiles of y w^T into its own copy `out` of the symmetric [M, N] fp32
+ * buffer and announces each tile by adding 1 to every rank's copy of that tile's counter
+ * (tile_counters: a symmetric uint32 buffer of kdn_tp_out_proj_tiles(M, N) entries; its
+ * multicast address alongside).  The owner of tile t (t % world == rank) waits until its copy
+ * of counter t reaches `target`, then writes the sum of all copies of the tile into every copy
+ * (multimem.ld_reduce + multimem.st).  The counters only grow: they start at zero on every
+ * rank and call number c (1, 2, ...) passes target = c * world.  A barrier across ranks must
+ * follow before the sum is read or `out` is written again.  No reference entry point.
+ */
+int64_t kdn_tp_out_proj_tiles(int64_t M, int32_t N);
+int kdn_tp_out_proj_allreduce(const void* y, const void* w, float* out, float* out_multicast, uint32_t* tile_counters,
+                              uint32_t* tile_counters_multicast, uint32_t target, int32_t rank, int32_t world,
+                              int64_t M, int32_t N, int32_t K, void* stream);
+
+/*
+ * The same two-phase projection over peer pointers instead of a multicast address (for
+ * world 2, where it moves fewer bytes, and for GPUs without NVSwitch multicast).  outs and
+ * tile_counters are HOST arrays of `world` device pointers (world <= 8): every rank's copy of
+ * the [M, N] output and of the counters, index = rank, all mapped into this process (a
+ * symmetric allocation's peer pointers).  Tiles are announced by adding 1 to every rank's
+ * counter; the owner of tile t reads the tile from every copy, adds them in rank order (fp32)
+ * and stores the sum into every copy.  out_dtype KDN_DTYPE_BF16: the copies hold bf16 (each
+ * rank's product rounded once, the sum rounded once), half the bytes.  Same counter and barrier rules as
+ * kdn_tp_out_proj_allreduce.  No reference entry point.
+ */
+int kdn_tp_out_proj_allreduce_peer(const void* y, const void* w, void* const* outs, int out_dtype,
+                                   uint32_t* const* tile_counters, uint32_t target, int32_t rank, int32_t world,
+                                   int64_t M, int32_t N, int32_t K, void* stream);
 
 /*
  * Layout change of a ragged serving batch (no reference counterpart; the reference packs

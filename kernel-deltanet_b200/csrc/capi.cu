@@ -234,16 +234,65 @@ int kdn_set_prefill_events(void* const* events, int count) {
 
 int kdn_prefill_launch_count(void) { return g_last_prefill_launches; }
 
-int kdn_tp_out_proj(const void* y, const void* w, float* out, float* out_multicast, int64_t M, int32_t N, int32_t K,
-                    void* stream) {
+int kdn_tp_out_proj(const void* y, const void* w, void* out, int out_dtype, float* out_multicast, int64_t M, int32_t N,
+                    int32_t K, void* stream) {
   if (M < 0 || M > (int64_t(65535) * 128)) return fail(KDN_ERR_INVALID, "M=%lld outside [0, 65535*128]", (long long)M);
   if (M == 0) return ok();
   if (N < 256 || N % 256 != 0 || N > 65535 * 256) return fail(KDN_ERR_UNSUPPORTED, "N=%d: a positive multiple of 256", N);
   if (K < 64 || K % 64 != 0) return fail(KDN_ERR_UNSUPPORTED, "K=%d: a positive multiple of 64", K);
   if (!y || !w || (!out && !out_multicast)) return fail(KDN_ERR_INVALID, "y/w/out is NULL");
+  if (out_dtype != KDN_DTYPE_F32 && out_dtype != KDN_DTYPE_BF16) return fail(KDN_ERR_INVALID, "bad output dtype");
+  if (out_multicast && out_dtype != KDN_DTYPE_F32)
+    return fail(KDN_ERR_UNSUPPORTED, "the multicast sum is formed in the fp32 output");
   if (!aligned(y, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(out_multicast, 16))
     return fail(KDN_ERR_INVALID, "y/w/out must be 16-byte aligned");
-  cudaError_t e = kdn::launch_tp_proj(y, w, out, out_multicast, M, N, K, static_cast<cudaStream_t>(stream));
+  cudaError_t e = kdn::launch_tp_proj(y, w, out, out_dtype == KDN_DTYPE_BF16, out_multicast, M, N, K,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-parallel projection launch");
+  return ok();
+}
+
+int64_t kdn_tp_out_proj_tiles(int64_t M, int32_t N) {
+  if (M < 0 || N < 256 || N % 256 != 0) return 0;
+  return kdn::tp_proj_tiles(M, N);
+}
+
+int kdn_tp_out_proj_allreduce(const void* y, const void* w, float* out, float* out_multicast, uint32_t* tile_counters,
+                              uint32_t* tile_counters_multicast, uint32_t target, int32_t rank, int32_t world,
+                              int64_t M, int32_t N, int32_t K, void* stream) {
+  if (M < 0 || M > (int64_t(65535) * 128)) return fail(KDN_ERR_INVALID, "M=%lld outside [0, 65535*128]", (long long)M);
+  if (world < 1 || rank < 0 || rank >= world) return fail(KDN_ERR_INVALID, "rank=%d world=%d", rank, world);
+  if (M == 0) return ok();
+  if (N < 256 || N % 256 != 0 || N > 65535 * 256) return fail(KDN_ERR_UNSUPPORTED, "N=%d: a positive multiple of 256", N);
+  if (K < 64 || K % 64 != 0) return fail(KDN_ERR_UNSUPPORTED, "K=%d: a positive multiple of 64", K);
+  if (!y || !w || !out || !out_multicast || !tile_counters || !tile_counters_multicast)
+    return fail(KDN_ERR_INVALID, "y/w/out/out_multicast/tile_counters is NULL");
+  if (!aligned(y, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(out_multicast, 16) ||
+      !aligned(tile_counters, 4) || !aligned(tile_counters_multicast, 4))
+    return fail(KDN_ERR_INVALID, "y/w/out must be 16-byte aligned, the counters 4-byte aligned");
+  cudaError_t e = kdn::launch_tp_proj_reduce(y, w, out, out_multicast, tile_counters, tile_counters_multicast, target,
+                                             rank, world, M, N, K, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-parallel projection launch");
+  return ok();
+}
+
+int kdn_tp_out_proj_allreduce_peer(const void* y, const void* w, void* const* outs, int out_dtype,
+                                   uint32_t* const* tile_counters, uint32_t target, int32_t rank, int32_t world,
+                                   int64_t M, int32_t N, int32_t K, void* stream) {
+  if (M < 0 || M > (int64_t(65535) * 128)) return fail(KDN_ERR_INVALID, "M=%lld outside [0, 65535*128]", (long long)M);
+  if (world < 1 || world > kdn::tp_proj_max_world() || rank < 0 || rank >= world)
+    return fail(KDN_ERR_INVALID, "rank=%d world=%d (world <= %d)", rank, world, kdn::tp_proj_max_world());
+  if (M == 0) return ok();
+  if (N < 256 || N % 256 != 0 || N > 65535 * 256) return fail(KDN_ERR_UNSUPPORTED, "N=%d: a positive multiple of 256", N);
+  if (K < 64 || K % 64 != 0) return fail(KDN_ERR_UNSUPPORTED, "K=%d: a positive multiple of 64", K);
+  if (!y || !w || !outs || !tile_counters) return fail(KDN_ERR_INVALID, "y/w/outs/tile_counters is NULL");
+  if (out_dtype != KDN_DTYPE_F32 && out_dtype != KDN_DTYPE_BF16) return fail(KDN_ERR_INVALID, "bad output dtype");
+  if (!aligned(y, 16) || !aligned(w, 16)) return fail(KDN_ERR_INVALID, "y/w must be 16-byte aligned");
+  for (int p = 0; p < world; ++p)
+    if (!outs[p] || !tile_counters[p] || !aligned(outs[p], 16) || !aligned(tile_counters[p], 4))
+      return fail(KDN_ERR_INVALID, "copy %d of the output/counters is NULL or misaligned", p);
+  cudaError_t e = kdn::launch_tp_proj_reduce_peer(y, w, outs, out_dtype == KDN_DTYPE_BF16, tile_counters, target, rank,
+                                                  world, M, N, K, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tensor-parallel projection launch");
   return ok();
 }

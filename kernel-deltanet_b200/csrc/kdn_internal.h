@@ -90,8 +90,19 @@ cudaError_t launch_affine_prefix_states(const float* A, const float* B, const fl
 // ---------------------------------------------------------------- tp_proj.cu
 // out (+)= Y W^T across ranks: stores into `out`, or adds into every rank's copy through the
 // multicast address `out_mc` when given.  N % 256 == 0, K % 64 == 0.
-cudaError_t launch_tp_proj(const void* Y, const void* W, float* out, float* out_mc, int64_t M, int N, int K,
-                           cudaStream_t stream);
+cudaError_t launch_tp_proj(const void* Y, const void* W, void* out, bool out_bf16, float* out_mc, int64_t M, int N,
+                           int K, cudaStream_t stream);
+// two-phase form: tiles stored into `out` (this rank's copy) and announced on the tile counters;
+// the owner (tile % world == rank) reduces each tile once every counter reaches `target`.
+cudaError_t launch_tp_proj_reduce(const void* Y, const void* W, float* out, float* out_mc, uint32_t* flags,
+                                  uint32_t* flags_mc, uint32_t target, int rank, int world, int64_t M, int N, int K,
+                                  cudaStream_t stream);
+// peer form: every rank's copies of the output and the counters by their peer pointers (world <= 8)
+cudaError_t launch_tp_proj_reduce_peer(const void* Y, const void* W, void* const* outs, bool out_bf16,
+                                       uint32_t* const* flags, uint32_t target, int rank, int world, int64_t M, int N,
+                                       int K, cudaStream_t stream);
+int tp_proj_max_world();
+int64_t tp_proj_tiles(int64_t M, int N);
 cudaError_t tp_proj_read_error(cudaStream_t stream, int* code);
 
 // ---------------------------------------------------------------- ragged.cu

@@ -1,20 +1,38 @@
-// tp_proj.cu -- row-parallel output projection with the all-reduce fused into its epilogue.
+// tp_proj.cu -- row-parallel output projection with the all-reduce fused into the same kernel.
 //
 // Head tensor parallelism (serving/tensor_parallel_runner.py:51-75,
 // experiments/run_kaggle_dual_gpu_cluster.py:99-112): rank r holds the scan outputs of its
 // heads, Y_r [M, K] (M tokens, K = local heads x d_v), and its slice of the output projection,
 // W_r [N, K]; the layer output is sum_r Y_r W_r^T [M, N] on every rank.  The reference runs
-// a local GEMM and then an all-reduce.  Here one kernel does both: each CTA computes a
-// 128 x 256 tile on the tensor cores (bf16 operands, fp32 accumulation in TMEM) and its
-// epilogue adds the tile into every rank's copy of the output through the NVSwitch multicast
-// address of a symmetric buffer (`multimem.red.add`), so the reduction traffic of one tile
-// overlaps the products of the next ones.  Without a multicast address (one rank) the tile
-// is stored.  Before the launch the output must be zero on every rank, and after it a
-// barrier across ranks makes the sums visible; the host wrapper does both.
+// a local GEMM and then an all-reduce.  Here one persistent kernel does both.  Each CTA walks
+// 128 x 256 output tiles; a tile is computed on the tensor cores (bf16 operands, fp32
+// accumulation in TMEM) and written out from registers in one of three ways:
 //
-// Operands are staged by cp.async into 128-byte-swizzled K-major tiles (3 stages of K = 64);
-// one thread issues the MMAs; the accumulator goes through shared memory so that each warp
-// writes whole rows (coalesced 16-byte vectors).
+//   kStore       one rank: plain stores into `out` (fp32 or bf16).
+//   kMulticastAdd (one-shot) `multimem.red.add` through the NVSwitch multicast address of a
+//                symmetric buffer adds the tile into every rank's copy.  One pass, no waits, but
+//                every GPU receives world x the output bytes: the form for small M.
+//   kReduceOwned (two-phase, the bandwidth-optimal form) the tile is stored into this rank's
+//                copy of the symmetric buffer and announced by a release `multimem.red` on a
+//                per-tile counter (every rank's copy of the counter goes up by one).  The tiles
+//                this rank owns (t % world == rank) are reduced, while the tile warps go on
+//                computing, by four reducer warps per CTA: each waits until every rank has
+//                announced tile t, reads the sum of all copies with `multimem.ld_reduce` (the
+//                switch adds) and writes it to every copy with `multimem.st`.  Each GPU sends
+//                and receives about (1 + 1/world) x the output bytes over NVLink, whatever the
+//                world size, and the reduction of early tiles overlaps the products of later ones.
+//
+// The peer form (kReduceOwnedPeer) runs the same owner scheme over peer pointers: the owner
+// reads the tile from every rank's copy, adds in rank order in fp32 and stores the sum into
+// every copy (fp32, or bf16 copies: half the bytes), 2 (world - 1) / world x the output bytes
+// each way per GPU -- fewer than the multicast form at world 2, and no multicast needed.
+//
+// The grid is at most one CTA per SM (all resident) and the reducer warps only wait on tiles
+// whose tile warps never wait on another rank, so every wait ends; each is bounded all the same
+// and a timeout sets the error word.
+// Operands are staged by cp.async into 128-byte-swizzled K-major tiles (4 stages of K = 64,
+// the next tile's first three loading during this tile's epilogue); one thread issues the
+// MMAs; each epilogue thread writes 32-column pieces of its accumulator row from registers.
 #include "kdn_internal.h"
 #include "tc_prims.cuh"
 
@@ -22,28 +40,40 @@ namespace kdn {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStagesP = 3;
-constexpr int kThrP = 128;
+constexpr int kStagesP = 4;
+constexpr int kThrP = 128;              // the tile warps (0-3): loads, MMA issue, epilogue
+constexpr int kThrAll = kThrP + 128;    // + the reducer warps (4-7) of the two-phase form
 constexpr uint32_t kATile = kBM * kBK * 2;  // 16 KiB
 constexpr uint32_t kBTile = kBN * kBK * 2;  // 32 KiB
 constexpr uint32_t kStageP = kATile + kBTile;
-constexpr int kOutLd = kBN + 4;  // padded row stride (floats) of the staged accumulator
-constexpr uint32_t kOutBytes = kBM * kOutLd * 4;
-constexpr uint32_t kMainBytes = kStageP * kStagesP > kOutBytes ? kStageP * kStagesP : kOutBytes;
-constexpr uint32_t P_BAR = kMainBytes;  // consumed[3], done
+constexpr uint32_t kStagesBytes = kStageP * kStagesP;
+constexpr uint32_t P_BAR = kStagesBytes;  // consumed[4], done
 constexpr uint32_t P_TSLOT = P_BAR + 8 * (kStagesP + 1);
-constexpr uint32_t kProjSmem = P_TSLOT + 16 + 1024;
+constexpr uint32_t P_FLAG = P_TSLOT + 16;
+constexpr uint32_t kProjSmem = P_FLAG + 16 + 1024;
+static_assert(kProjSmem <= 227 * 1024, "projection tiles exceed shared memory");
 constexpr uint32_t kWaitLimitP = 1u << 24;
+constexpr uint32_t kFlagPollLimit = 1u << 22;
 
 __device__ int g_proj_error;
+
+enum Mode : int { kStore = 0, kMulticastAdd = 1, kReduceOwned = 2, kReduceOwnedPeer = 3 };
+constexpr int kMaxWorld = 8;
 
 struct ProjArgs {
   const __nv_bfloat16* Y;  // [M, K]
   const __nv_bfloat16* W;  // [N, K]
-  float* out;              // [M, N] this rank's copy (stores when no multicast address)
-  float* out_mc;           // [M, N] multicast address of the symmetric output, or null
+  float* out;              // [M, N] this rank's copy (fp32, or bf16 when out_bf16)
+  float* out_mc;           // [M, N] multicast address of the symmetric output (modes 1, 2)
+  uint32_t* flags;         // [tiles] this rank's copy of the tile counters (mode 2)
+  uint32_t* flags_mc;      // [tiles] their multicast address (mode 2)
   int64_t M;
   int N, K;
+  int mode, rank, world;
+  int out_bf16;  // modes 0 and 3: the output copies hold bf16 (the sum is still formed in fp32)
+  uint32_t target;  // counter value meaning "every rank has announced this tile" in this call
+  float* peer_out[kMaxWorld];        // mode 3: every rank's copy of the output (this rank's included)
+  uint32_t* peer_flags[kMaxWorld];   // mode 3: every rank's copy of the tile counters
 };
 
 __device__ __forceinline__ bool proj_wait(uint64_t* bar, uint32_t parity) {
@@ -52,7 +82,7 @@ __device__ __forceinline__ bool proj_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-// stage k-block kt of the CTA's A rows [m0, m0+128) and B rows [n0, n0+256) (zero past M)
+// stage k-block kt of the A rows [m0, m0+128) and B rows [n0, n0+256) (zero past M)
 __device__ __forceinline__ void load_stage(const ProjArgs& a, uint32_t sbase, int64_t m0, int n0, int kt, int tid) {
   const int k0 = kt * kBK;
 #pragma unroll
@@ -70,23 +100,58 @@ __device__ __forceinline__ void load_stage(const ProjArgs& a, uint32_t sbase, in
   }
 }
 
-__device__ __forceinline__ void red_v4(float* addr, float4 v) {
+__device__ __forceinline__ void red_add_v4(float* addr, float4 v) {
   asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x),
                "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
 }
+__device__ __forceinline__ float4 ld_reduce_v4(const float* addr) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_v4_all(float* addr, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void announce(uint32_t* flag_mc) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag_mc) : "memory");
+}
+__device__ __forceinline__ void announce_peer(uint32_t* flag) {
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
+}
+__device__ __forceinline__ float4 ld_peer_v4(const float* p) {
+  float4 v;
+  asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
-__global__ void __launch_bounds__(kThrP, 1) tp_proj_kernel(ProjArgs a) {
+__device__ __forceinline__ void tile_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThrP) : "memory"); }
+
+__global__ void __launch_bounds__(kThrAll, 1) tp_proj_kernel(ProjArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = tc::smem_u32(sm);
   uint64_t* consumed = reinterpret_cast<uint64_t*>(sm + P_BAR);
   uint64_t* done = consumed + kStagesP;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_TSLOT);
+  unsigned int* claim = reinterpret_cast<unsigned int*>(sm + P_FLAG);  // next unit of this CTA's reduction list
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kBN;
-  const int64_t m0 = int64_t(blockIdx.y) * kBM;
   const int KT = a.K / kBK;
+  const int tiles_n = a.N / kBN;
+  const int64_t tiles = ((a.M + kBM - 1) / kBM) * tiles_n;
   bool ok = true;
 
   if (warp == 0) {
@@ -96,104 +161,365 @@ __global__ void __launch_bounds__(kThrP, 1) tp_proj_kernel(ProjArgs a) {
   if (tid == 0) {
     for (int s = 0; s < kStagesP; ++s) tc::mbar_init(&consumed[s], 1);
     tc::mbar_init(done, 1);
+    *claim = 0u;
     tc::fence_mbar_init();
-  }
-  for (int s = 0; s < kStagesP - 1; ++s) {
-    if (s < KT) load_stage(a, sbase + s * kStageP, m0, n0, s, tid);
-    tc::cp_async_commit();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tslot;
   const uint32_t idesc = tc::idesc_bf16_f32(kBM, kBN, false, false);
-  uint32_t pc = 0;  // phase bits of consumed[]
+  uint32_t issued = 0;  // bit s: parity of the commits made so far on consumed[s]
+  uint32_t pd = 0;      // phase of `done`
 
-  for (int kt = 0; kt < KT; ++kt) {
-    const int s = kt % kStagesP;
-    asm volatile("cp.async.wait_group %0;" ::"n"(kStagesP - 2) : "memory");  // this thread's part of stage kt
-    tc::fence_proxy_async_smem();
-    __syncthreads();  // every thread's part
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t st = sbase + s * kStageP;
-#pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk)
-        tc::mma_ss(tmem, tc::smem_desc_sw128(st + 32 * kk, 16, 1024), tc::smem_desc_sw128(st + kATile + 32 * kk, 16, 1024),
-                   idesc, kt > 0 || kk > 0);
-      tc::mma_commit(&consumed[s]);
+  // ---------------------------------------------------------------- tile warps: compute the tiles
+  if (warp < kThrP / 32) {
+  auto prologue = [&](int64_t t) {  // the first k-blocks of tile t
+    for (int s = 0; s < kStagesP - 1; ++s) {
+      if (s < KT) load_stage(a, sbase + s * kStageP, (t / tiles_n) * kBM, int(t % tiles_n) * kBN, s, tid);
+      tc::cp_async_commit();
     }
-    // refill the stage the previous products read with k-block kt + 2
-    const int nk = kt + kStagesP - 1;
-    if (nk < KT) {
-      const int ns = nk % kStagesP;
-      if (kt >= 1) {  // stage ns was last read by the products of k-block kt - 1
-        ok &= proj_wait(&consumed[ns], (pc >> ns) & 1u);
-        pc ^= 1u << ns;
+  };
+  if (blockIdx.x < tiles) prologue(blockIdx.x);
+#pragma unroll 1
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int n0 = int(t % tiles_n) * kBN;
+    const int64_t m0 = (t / tiles_n) * kBM;
+#pragma unroll 1
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % kStagesP;
+      asm volatile("cp.async.wait_group %0;" ::"n"(kStagesP - 2) : "memory");  // this thread's part of stage kt
+      tc::fence_proxy_async_smem();
+      tile_sync();  // every thread's part
+      if (tid == 0) {
+        tc::fence_after_sync();
+        const uint32_t st = sbase + s * kStageP;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          tc::mma_ss(tmem, tc::smem_desc_sw128(st + 32 * kk, 16, 1024),
+                     tc::smem_desc_sw128(st + kATile + 32 * kk, 16, 1024), idesc, kt > 0 || kk > 0);
+        tc::mma_commit(&consumed[s]);
       }
-      load_stage(a, sbase + ns * kStageP, m0, n0, nk, tid);
+      issued ^= 1u << s;
+      // refill the stage the products of k-block kt - 1 read with k-block kt + 2
+      const int nk = kt + kStagesP - 1;
+      if (nk < KT) {
+        const int ns = nk % kStagesP;
+        if (kt >= 1) ok &= proj_wait(&consumed[ns], ((issued >> ns) & 1u) ^ 1u);  // its latest commit
+        load_stage(a, sbase + ns * kStageP, m0, n0, nk, tid);
+      }
+      tc::cp_async_commit();
     }
-    tc::cp_async_commit();
-  }
-  if (tid == 0) tc::mma_commit(done);
-  ok &= proj_wait(done, 0);
-  tc::fence_after_sync();
+    if (tid == 0) tc::mma_commit(done);
+    ok &= proj_wait(done, pd);
+    pd ^= 1u;
+    tc::fence_after_sync();
+    // every stage is free: the next tile's first k-blocks load while this one is written out
+    if (t + gridDim.x < tiles) prologue(t + gridDim.x);
 
-  // accumulator -> shared memory (row r = lane of warp r / 32), then whole rows out
-  tc::cp_async_wait_all();  // (every staged load was consumed; nothing is in flight)
-  float* Os = reinterpret_cast<float*>(sm);
-  const int r = 32 * warp + lane;
+    // accumulator -> registers -> global: thread r writes 32-column pieces of row m0 + r (whole
+    // 128-byte lines in fp32, 64 bytes in bf16); the next tile's first k-blocks are already loading
+    const int r = 32 * warp + lane;
+    const int64_t row = m0 + r;
+    if (a.mode == kMulticastAdd) {
+      // one-shot: through the last stage buffer (free until the next tile's k-block 3 loads, after
+      // this epilogue), 64 columns at a time, so that a warp instruction adds two whole 256-byte row
+      // pieces (scattered 16-byte adds starve the multicast path)
+      float* Os = reinterpret_cast<float*>(sm + (kStagesP - 1) * kStageP);
+      constexpr int kLd = 64 + 4;
+      static_assert(kBM * kLd * 4 <= kStageP, "staging exceeds a stage buffer");
 #pragma unroll 1
-  for (int c0 = 0; c0 < kBN; c0 += 32) {
-    float v[32];
-    tc::tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + c0, v);
-    tc::tmem_ld_wait();
+      for (int c0 = 0; c0 < kBN; c0 += 64) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 4)
-      *reinterpret_cast<float4*>(Os + r * kOutLd + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-  }
-  tc::fence_before_sync();
-  __syncthreads();
+        for (int hh = 0; hh < 2; ++hh) {
+          float v[32];
+          tc::tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + c0 + 32 * hh, v);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(Os + r * kLd + 32 * hh + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+        tile_sync();
+#pragma unroll 4
+        for (int rr = 2 * warp + (lane >> 4); rr < kBM; rr += 2 * (kThrP / 32)) {
+          if (m0 + rr < a.M)
+            red_add_v4(a.out_mc + (m0 + rr) * a.N + n0 + c0 + 4 * (lane & 15),
+                       *reinterpret_cast<const float4*>(Os + rr * kLd + 4 * (lane & 15)));
+        }
+        tile_sync();
+      }
+    }
 #pragma unroll 1
-  for (int rr = warp; rr < kBM; rr += kThrP / 32) {
-    const int64_t row = m0 + rr;
-    if (row >= a.M) break;
+    for (int c0 = 0; c0 < kBN && a.mode != kMulticastAdd; c0 += 32) {
+      float v[32];
+      tc::tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + c0, v);
+      tc::tmem_ld_wait();
+      if (row < a.M) {
+        const int64_t off = row * a.N + n0 + c0;
+        if (a.out_bf16) {
 #pragma unroll
-    for (int h = 0; h < kBN / 128; ++h) {
-      const int col = 128 * h + 4 * lane;
-      const float4 v = *reinterpret_cast<const float4*>(Os + rr * kOutLd + col);
-      const int64_t off = row * a.N + n0 + col;
-      if (a.out_mc)
-        red_v4(a.out_mc + off, v);
+          for (int j = 0; j < 32; j += 8) {
+            uint4 pk;
+            uint32_t* w32 = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 b = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+              w32[e] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + off + j) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(a.out + off + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+      }
+    }
+    tc::fence_before_sync();
+    tile_sync();  // every row of the tile is written; TMEM may take the next tile's products
+    if (a.mode >= kReduceOwned && tid == 0) {
+      __threadfence_system();
+      if (a.mode == kReduceOwned)
+        announce(a.flags_mc + t);
       else
-        *reinterpret_cast<float4*>(a.out + off) = v;
+        for (int p = 0; p < a.world; ++p) announce_peer(a.peer_flags[p] + t);
     }
   }
-  if (a.out_mc) __threadfence_system();  // the reductions before the kernel's completion
+
+  }
+
+  // ---------------------------------------------------------------- reduction of the owned tiles
+  // (owner forms) CTA b reduces the owned tiles j = b, b + grid, ... (tile t = rank + j * world),
+  // a quarter tile (32 rows) per unit, units claimed in production order from a shared counter:
+  // the reducer warps from the start, the tile warps as soon as they have no tile left to compute.
+  if (a.mode >= kReduceOwned && a.rank < tiles) {
+    const int64_t owned = (tiles - a.rank + a.world - 1) / a.world;
+    const int64_t mine = owned > blockIdx.x ? (owned - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const unsigned int units = unsigned(mine * 4);
+#pragma unroll 1
+    while (true) {
+      unsigned int u = 0;
+      if (lane == 0) u = atomicAdd(claim, 1u);
+      u = __shfl_sync(0xffffffffu, u, 0);
+      if (u >= units) break;
+      const int64_t t = a.rank + (blockIdx.x + int64_t(u >> 2) * gridDim.x) * a.world;
+      int good = 0;
+      if (lane == 0)
+        for (uint32_t n = 0; n < kFlagPollLimit; ++n)
+          if (int32_t(ld_acquire_sys(a.flags + t) - a.target) >= 0) {
+            good = 1;
+            break;
+          }
+      good = __shfl_sync(0xffffffffu, good, 0);
+      __syncwarp();  // the acquire before every lane's reads
+      if (!good) {
+        ok = false;
+        continue;
+      }
+      const int n0 = int(t % tiles_n) * kBN;
+      const int64_t m0 = (t / tiles_n) * kBM + 32 * (u & 3);
+      if (a.mode == kReduceOwned) {
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {  // 8 rows x 2 vectors per lane in flight
+          float4 v[8][2];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = m0 + r0 + i;
+            if (row < a.M) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) v[i][h] = ld_reduce_v4(a.out_mc + row * a.N + n0 + 128 * h + 4 * lane);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = m0 + r0 + i;
+            if (row < a.M) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) st_v4_all(a.out_mc + row * a.N + n0 + 128 * h + 4 * lane, v[i][h]);
+            }
+          }
+        }
+      } else if (a.out_bf16) {  // peer form, bf16 copies: a lane takes 8 columns (16 B) of a row
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {
+          float acc[8][8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.peer_out[p]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) {
+                const float4 raw = ld_peer_v4(reinterpret_cast<const float*>(src + row * a.N + n0 + 8 * lane));
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __bfloat1622float2(h2[e]);
+                  acc[i][2 * e] += f.x;
+                  acc[i][2 * e + 1] += f.y;
+                }
+              }
+            }
+          }
+          uint4 pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint32_t* w32 = reinterpret_cast<uint32_t*>(&pk[i]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 b = __floats2bfloat162_rn(acc[i][2 * e], acc[i][2 * e + 1]);
+              w32[e] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+          }
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) *reinterpret_cast<uint4*>(dst + row * a.N + n0 + 8 * lane) = pk[i];
+            }
+          }
+        }
+      } else {  // peer form: read every copy, add in rank order, write the sum into every copy
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {  // 8 rows x 2 vectors per lane, one copy at a time
+          float4 v[8][2];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) v[i][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            const float* src = a.peer_out[p];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float4 x = ld_peer_v4(src + row * a.N + n0 + 128 * h + 4 * lane);
+                  v[i][h].x += x.x;
+                  v[i][h].y += x.y;
+                  v[i][h].z += x.z;
+                  v[i][h].w += x.w;
+                }
+              }
+            }
+          }
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            float* dst = a.peer_out[p];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                  *reinterpret_cast<float4*>(dst + row * a.N + n0 + 128 * h + 4 * lane) = v[i][h];
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  if (a.mode != kStore) __threadfence_system();  // the remote writes before the kernel's completion
   if (!ok) record_device_error(&g_proj_error, kErrProjWaitTimeout);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, kBN);
 }
 
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess)
+      n = 148;
+  }
+  return n;
+}
+
+cudaError_t launch(const ProjArgs& a, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(tp_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmem));
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = ((a.M + kBM - 1) / kBM) * (a.N / kBN);
+  const int64_t grid = tiles < sm_count() ? tiles : sm_count();
+  tp_proj_kernel<<<unsigned(grid), kThrAll, kProjSmem, stream>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
-cudaError_t launch_tp_proj(const void* Y, const void* W, float* out, float* out_mc, int64_t M, int N, int K,
-                           cudaStream_t stream) {
-  ProjArgs a;
+int64_t tp_proj_tiles(int64_t M, int N) { return ((M + kBM - 1) / kBM) * (N / kBN); }
+
+cudaError_t launch_tp_proj(const void* Y, const void* W, void* out, bool out_bf16, float* out_mc, int64_t M, int N,
+                           int K, cudaStream_t stream) {
+  ProjArgs a{};
   a.Y = static_cast<const __nv_bfloat16*>(Y);
   a.W = static_cast<const __nv_bfloat16*>(W);
-  a.out = out;
+  a.out = static_cast<float*>(out);
+  a.out_bf16 = out_bf16 ? 1 : 0;
   a.out_mc = out_mc;
   a.M = M;
   a.N = N;
   a.K = K;
-  cudaError_t e = cudaFuncSetAttribute(tp_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmem));
-  if (e != cudaSuccess) return e;
-  dim3 grid(unsigned(N / kBN), unsigned((M + kBM - 1) / kBM));
-  tp_proj_kernel<<<grid, kThrP, kProjSmem, stream>>>(a);
-  return cudaGetLastError();
+  a.mode = out_mc ? kMulticastAdd : kStore;
+  a.world = 1;
+  return launch(a, stream);
 }
+
+cudaError_t launch_tp_proj_reduce(const void* Y, const void* W, float* out, float* out_mc, uint32_t* flags,
+                                  uint32_t* flags_mc, uint32_t target, int rank, int world, int64_t M, int N, int K,
+                                  cudaStream_t stream) {
+  ProjArgs a{};
+  a.Y = static_cast<const __nv_bfloat16*>(Y);
+  a.W = static_cast<const __nv_bfloat16*>(W);
+  a.out = out;
+  a.out_mc = out_mc;
+  a.flags = flags;
+  a.flags_mc = flags_mc;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = kReduceOwned;
+  a.rank = rank;
+  a.world = world;
+  a.target = target;
+  return launch(a, stream);
+}
+
+cudaError_t launch_tp_proj_reduce_peer(const void* Y, const void* W, void* const* outs, bool out_bf16,
+                                       uint32_t* const* flags, uint32_t target, int rank, int world, int64_t M, int N,
+                                       int K, cudaStream_t stream) {
+  if (world < 1 || world > kMaxWorld) return cudaErrorInvalidValue;
+  ProjArgs a{};
+  a.Y = static_cast<const __nv_bfloat16*>(Y);
+  a.W = static_cast<const __nv_bfloat16*>(W);
+  a.out = static_cast<float*>(outs[rank]);
+  a.out_bf16 = out_bf16 ? 1 : 0;
+  a.flags = flags[rank];
+  for (int p = 0; p < world; ++p) {
+    a.peer_out[p] = static_cast<float*>(outs[p]);
+    a.peer_flags[p] = flags[p];
+  }
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = kReduceOwnedPeer;
+  a.rank = rank;
+  a.world = world;
+  a.target = target;
+  return launch(a, stream);
+}
+
+int tp_proj_max_world() { return kMaxWorld; }
 
 cudaError_t tp_proj_read_error(cudaStream_t stream, int* code) {
   int h = 0;

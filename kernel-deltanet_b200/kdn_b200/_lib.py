@@ -46,6 +46,7 @@ _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
 _INT = ctypes.c_int
+_U32 = ctypes.c_uint32
 
 # name -> (restype, argtypes); the list is also what the export test checks
 SIGNATURES = {
@@ -59,7 +60,11 @@ SIGNATURES = {
                                           ctypes.POINTER(KdnProjection), _P]),
     "kdn_set_prefill_events": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT]),
     "kdn_prefill_launch_count": (_INT, []),
-    "kdn_tp_out_proj": (_INT, [_P, _P, _P, _P, _I64, _I32, _I32, _P]),
+    "kdn_tp_out_proj": (_INT, [_P, _P, _P, _INT, _P, _I64, _I32, _I32, _P]),
+    "kdn_tp_out_proj_tiles": (_I64, [_I64, _I32]),
+    "kdn_tp_out_proj_allreduce": (_INT, [_P, _P, _P, _P, _P, _P, _U32, _I32, _I32, _I64, _I32, _I32, _P]),
+    "kdn_tp_out_proj_allreduce_peer": (_INT, [_P, _P, ctypes.POINTER(_P), _INT, ctypes.POINTER(_P), _U32, _I32, _I32,
+                                              _I64, _I32, _I32, _P]),
     "kdn_ragged_transpose": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I32, _I64, _INT, _P]),
     "kdn_copy_rows": (_INT, [_P, ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _P]),
     "kdn_affine_compose": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),

@@ -130,35 +130,79 @@ def sequence_parallel_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 # ------------------------------------------------------------------ head-TP output projection
 _SYMM: dict = {}
 _BARRIER_TIMEOUT_MS = 60_000
+ONE_SHOT_MAX_BYTES = 2 << 20  # "auto" picks the one-shot form up to this output size
 
 
-def _symmetric_output(M: int, N: int, dev: torch.device, group):
-    """A cached symmetric [M, N] fp32 buffer of `group` on `dev` and its handle."""
-    import torch.distributed._symmetric_memory as symm_mem
+class _SymmetricOutput:
+    """A symmetric allocation of `group` holding the [M, N] output (fp32 or bf16) and, behind
+    it, one uint32 counter per output tile (zeroed once, at creation, on every rank)."""
 
-    name = (group or dist.group.WORLD).group_name
-    key = (M, N, dev.index, name)
+    def __init__(self, M: int, N: int, dtype: torch.dtype, dev: torch.device, group, lib):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        name = (group or dist.group.WORLD).group_name
+        esize = torch.empty((), dtype=dtype).element_size()
+        self.tiles = int(lib.kdn_tp_out_proj_tiles(M, N))
+        self.ctr_off = (M * N * esize + 15) // 16 * 16  # byte offset of the counters (16-byte aligned)
+        self.raw = symm_mem.empty(self.ctr_off + 4 * self.tiles, dtype=torch.uint8, device=dev)
+        self.hdl = symm_mem.rendezvous(self.raw, name)
+        self.out = self.raw[:M * N * esize].view(dtype).view(M, N)
+        self.counters = self.raw[self.ctr_off:].view(torch.int32)
+        self.counters.zero_()
+        self.calls = 0  # owner-scheme calls made on this buffer: the counters reach calls * world
+        self.hdl.barrier(channel=0, timeout_ms=_BARRIER_TIMEOUT_MS)
+
+    def multicast(self, byte_offset: int = 0) -> int:
+        return int(self.hdl.multicast_ptr) + byte_offset
+
+    def peer_ptrs(self, byte_offset: int = 0):
+        """Every rank's copy (rank order), mapped into this process, at a byte offset."""
+        return [int(p) + byte_offset for p in self.hdl.buffer_ptrs]
+
+
+def _symmetric_output(M: int, N: int, dtype: torch.dtype, dev: torch.device, group, lib) -> _SymmetricOutput:
+    key = (M, N, dtype, dev.index, (group or dist.group.WORLD).group_name)
     if key not in _SYMM:
-        buf = symm_mem.empty(M, N, dtype=torch.float32, device=dev)
-        hdl = symm_mem.rendezvous(buf, name)
-        _SYMM[key] = (buf, hdl)
+        _SYMM[key] = _SymmetricOutput(M, N, dtype, dev, group, lib)
     return _SYMM[key]
 
 
-def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=None, *,
+def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=None, *, method: str = "auto",
+                          out_dtype: torch.dtype = torch.float32,
                           allow_unfused: bool = False) -> Tuple[torch.Tensor, str]:
     """sum over the ranks of `group` of y_local @ w_local^T, returned on every rank.
 
     y_local [M, K] and w_local [N, K] (bfloat16; K = local heads x d_v; N % 256 == 0,
-    K % 64 == 0).  Returns (out [M, N] float32, path) with path "fused-multicast" (one
-    kernel: tensor-core tiles reduced into every rank's copy through NVSwitch), "local"
-    (one rank: the same kernel, stores) or, only when `allow_unfused` and the group has no
-    multicast support, "unfused-nccl" (the kernel's product, then an NCCL all-reduce: the
-    reference's two-step form).  The returned tensor of the fused path is the cached
-    symmetric buffer: it is overwritten by the next call with the same shape.
+    K % 64 == 0).  Returns (out [M, N] float32, path).  With one rank the kernel stores its
+    product (path "local").  Otherwise one kernel computes the tiles on the tensor cores and
+    reduces them across the ranks (path "fused-<method>"):
+      * "two-phase": every rank stores its tiles locally and announces them; the owner of each
+        tile sums all copies in the NVSwitch (multimem.ld_reduce) and writes the sum to every
+        copy (multimem.st): (1 + 1/world) x the output bytes cross each GPU's links;
+      * "peer": the same owner scheme over peer pointers (loads from every copy, stores into
+        every copy): 2 (world - 1) / world x the output bytes, fewer than two-phase at world 2,
+        and no multicast needed;
+      * "one-shot": each tile is added into every copy through the multicast address as it is
+        produced (one pass, world x the output bytes into each GPU);
+      * "auto": one-shot up to ONE_SHOT_MAX_BYTES of output, else peer at world 2 (or without
+        multicast), else two-phase.
+    The sum is formed in fp32 and is identical on every rank.  out_dtype torch.bfloat16 (the
+    reference's layer dtype; "local" and "peer" only, "auto" then picks "peer"): every rank's
+    product is rounded to bf16 once and the sum once, and half the bytes move.  Only when `allow_unfused` and the group
+    cannot map symmetric memory: the kernel's product and then an NCCL all-reduce (path
+    "unfused-nccl", the reference's two-step form).  The tensor returned by a fused path is a
+    cached symmetric buffer, overwritten by the next call with the same shape.
     """
+    import ctypes
+
     from . import _lib
 
+    if method not in ("auto", "one-shot", "two-phase", "peer"):
+        raise ValueError(f"method must be 'auto', 'one-shot', 'two-phase' or 'peer', got {method!r}")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"out_dtype must be torch.float32 or torch.bfloat16, got {out_dtype}")
+    if out_dtype == torch.bfloat16 and method in ("one-shot", "two-phase"):
+        raise ValueError(f"method {method!r} sums in the fp32 output; bf16 output takes 'peer' (or 'auto')")
     if y_local.dim() != 2 or w_local.dim() != 2 or y_local.shape[1] != w_local.shape[1]:
         raise RuntimeError(f"expected y [M, K] and w [N, K]; got {tuple(y_local.shape)}, {tuple(w_local.shape)}")
     if not (y_local.is_cuda and w_local.is_cuda):
@@ -170,31 +214,57 @@ def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=No
     w = w_local.to(torch.bfloat16).contiguous()
     lib = _lib.load()
     stream = _lib.stream_handle(dev)
-    _, world = _world(group)
+    rank, world = _world(group)
+
+    def local_product():
+        out = torch.empty(M, N, device=dev, dtype=out_dtype)
+        _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), out.data_ptr(), _lib.dtype_code(out), None, M, N,
+                                       K, stream), "kdn_tp_out_proj")
+        return out
+
     if world == 1:
-        out = torch.empty(M, N, device=dev, dtype=torch.float32)
-        _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), out.data_ptr(), None, M, N, K, stream),
-                   "kdn_tp_out_proj")
-        return out, "local"
+        return local_product(), "local"
     from torch._C._autograd import DeviceType
     from torch._C._distributed_c10d import _SymmetricMemory
 
-    buf, hdl = _symmetric_output(M, N, dev, group)
-    if not _SymmetricMemory.has_multicast_support(DeviceType.CUDA, dev.index) or not hdl.multicast_ptr:
+    try:
+        so = _symmetric_output(M, N, out_dtype, dev, group, lib)
+    except RuntimeError:
         if not allow_unfused:
-            raise RuntimeError("no NVSwitch multicast for this group: the fused projection is unavailable "
-                               "(pass allow_unfused=True for the GEMM + NCCL all-reduce form)")
-        out = torch.empty(M, N, device=dev, dtype=torch.float32)
-        _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), out.data_ptr(), None, M, N, K, stream),
-                   "kdn_tp_out_proj")
+            raise
+        out = local_product()
         dist.all_reduce(out, group=group)
         return out, "unfused-nccl"
-    buf.zero_()
-    hdl.barrier(channel=0, timeout_ms=_BARRIER_TIMEOUT_MS)  # every copy is zero before anyone adds
-    _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), None, hdl.multicast_ptr, M, N, K, stream),
-               "kdn_tp_out_proj")
-    hdl.barrier(channel=0, timeout_ms=_BARRIER_TIMEOUT_MS)  # every rank's tiles are in every copy
-    return buf, "fused-multicast"
+    has_mc = bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, dev.index)) and bool(so.hdl.multicast_ptr)
+    if method == "auto":
+        if out_dtype == torch.bfloat16:
+            method = "peer"
+        elif has_mc and M * N * 4 <= ONE_SHOT_MAX_BYTES:
+            method = "one-shot"
+        else:
+            method = "peer" if (world == 2 or not has_mc) else "two-phase"
+    if method in ("one-shot", "two-phase") and not has_mc:
+        raise RuntimeError(f"no NVSwitch multicast for this group: method {method!r} is unavailable (use 'peer')")
+    if method == "one-shot":
+        so.out.zero_()
+        so.hdl.barrier(channel=0, timeout_ms=_BARRIER_TIMEOUT_MS)  # every copy is zero before anyone adds
+        _lib.check(lib.kdn_tp_out_proj(y.data_ptr(), w.data_ptr(), None, _lib.KDN_DTYPE_F32, so.multicast(), M, N, K,
+                                       stream), "kdn_tp_out_proj")
+    else:
+        so.calls += 1
+        target = (so.calls * world) & 0xFFFFFFFF
+        if method == "two-phase":
+            rc = lib.kdn_tp_out_proj_allreduce(y.data_ptr(), w.data_ptr(), so.out.data_ptr(), so.multicast(),
+                                               so.counters.data_ptr(), so.multicast(so.ctr_off), target, rank, world,
+                                               M, N, K, stream)
+        else:
+            outs = (ctypes.c_void_p * world)(*so.peer_ptrs(0))
+            ctrs = (ctypes.c_void_p * world)(*so.peer_ptrs(so.ctr_off))
+            rc = lib.kdn_tp_out_proj_allreduce_peer(y.data_ptr(), w.data_ptr(), outs, _lib.dtype_code(so.out), ctrs,
+                                                    target, rank, world, M, N, K, stream)
+        _lib.check(rc, "kdn_tp_out_proj_allreduce")
+    so.hdl.barrier(channel=0, timeout_ms=_BARRIER_TIMEOUT_MS)  # every rank's tiles are in every copy
+    return so.out, "fused-" + method
 
 
 def release_symmetric_buffers() -> None:

@@ -164,16 +164,25 @@ def nccl_tp_out_proj(rank, world, port, result_path, M, N, K):
         w = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).bfloat16()
         ref = y.float() @ w.float().t()
         dist.all_reduce(ref)
-        paths = []
-        for _ in range(3):  # repeated calls reuse the symmetric buffer (zeroed every call)
-            out, path = kd.row_parallel_out_proj(y, w, allow_unfused=True)
+        paths, errs = [], []
+        # repeated and alternating calls reuse one symmetric buffer and its tile counters
+        for method in ("two-phase", "one-shot", "peer", "two-phase", "peer", "one-shot", "auto"):
+            out, path = kd.row_parallel_out_proj(y, w, method=method, allow_unfused=True)
             torch.cuda.synchronize()
-            err = float((out - ref).abs().max() / ref.abs().max())
+            errs.append(float((out - ref).abs().max() / ref.abs().max()))
             paths.append(path)
-        ok = err < 1e-4 and paths[0] in ("fused-multicast", "unfused-nccl")
-        print(f"rank {rank}: path {paths[0]} err {err:.3e}", flush=True)
+        out, path = kd.row_parallel_out_proj(y, w, method="auto", out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        err_bf16 = float((out.float() - ref).abs().max() / ref.abs().max())
+        paths.append(path + "-bf16")
+        same = torch.tensor([float(out.float().sum())], device=dev, dtype=torch.float64)
+        everyone = [torch.zeros_like(same) for _ in range(world)]
+        dist.all_gather(everyone, same)  # the owner's sum is copied: every rank holds the same bits
+        ok = (max(errs) < 1e-4 and err_bf16 < 1e-2 and all(float(e) == float(same) for e in everyone)
+              and all(p.startswith("fused-") or p == "unfused-nccl" for p in paths[:-1]))
+        print(f"rank {rank}: paths {paths} errs {[f'{e:.1e}' for e in errs]} bf16 {err_bf16:.1e}", flush=True)
         with open(f"{result_path}.path", "w") as f:
-            f.write(paths[0])
+            f.write(",".join(paths))
         kd.release_symmetric_buffers()
         dist.barrier()
         dist.destroy_process_group()

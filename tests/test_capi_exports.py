@@ -180,8 +180,45 @@ def test_block_transition_argument_checks(lib):
 
 
 def test_tp_out_proj_argument_checks(lib):
-    assert lib.kdn_tp_out_proj(4096, 8192, 16384, None, 128, 200, 64, None) == 2   # N not a multiple of 256
-    assert lib.kdn_tp_out_proj(4096, 8192, 16384, None, 128, 256, 48, None) == 2   # K not a multiple of 64
-    assert lib.kdn_tp_out_proj(4104, 8192, 16384, None, 128, 256, 64, None) == 1   # misaligned
-    assert lib.kdn_tp_out_proj(4096, 8192, None, None, 128, 256, 64, None) == 1    # no output
-    assert lib.kdn_tp_out_proj(4096, 8192, 16384, None, 0, 256, 64, None) == 0     # nothing to do
+    assert lib.kdn_tp_out_proj(4096, 8192, 16384, 0, None, 128, 200, 64, None) == 2   # N not a multiple of 256
+    assert lib.kdn_tp_out_proj(4096, 8192, 16384, 0, None, 128, 256, 48, None) == 2   # K not a multiple of 64
+    assert lib.kdn_tp_out_proj(4104, 8192, 16384, 0, None, 128, 256, 64, None) == 1   # misaligned
+    assert lib.kdn_tp_out_proj(4096, 8192, None, 0, None, 128, 256, 64, None) == 1    # no output
+    assert lib.kdn_tp_out_proj(4096, 8192, 16384, 7, None, 128, 256, 64, None) == 1   # bad dtype
+    assert lib.kdn_tp_out_proj(4096, 8192, None, 1, 16384, 128, 256, 64, None) == 2   # multicast sum is fp32
+    assert lib.kdn_tp_out_proj(4096, 8192, 16384, 0, None, 0, 256, 64, None) == 0     # nothing to do
+
+
+def test_tp_out_proj_allreduce_argument_checks(lib):
+    P = 4096
+    assert lib.kdn_tp_out_proj_tiles(300, 512) == 3 * 2
+    assert lib.kdn_tp_out_proj_tiles(300, 500) == 0
+    args = lambda **kw: [kw.get(n, d) for n, d in (("y", P), ("w", P), ("out", P), ("mc", P), ("fl", P), ("flmc", P),
+                                                   ("target", 2), ("rank", 0), ("world", 2), ("M", 128), ("N", 256),
+                                                   ("K", 64))] + [None]
+    assert lib.kdn_tp_out_proj_allreduce(*args(rank=2)) == 1          # rank outside the world
+    assert lib.kdn_tp_out_proj_allreduce(*args(world=0, rank=0)) == 1
+    assert lib.kdn_tp_out_proj_allreduce(*args(N=384)) == 2           # N not a multiple of 256
+    assert lib.kdn_tp_out_proj_allreduce(*args(K=96)) == 2            # K not a multiple of 64
+    assert lib.kdn_tp_out_proj_allreduce(*args(fl=None)) == 1         # no counters
+    assert lib.kdn_tp_out_proj_allreduce(*args(mc=P + 8)) == 1        # misaligned multicast output
+    assert lib.kdn_tp_out_proj_allreduce(*args(flmc=P + 2)) == 1      # misaligned counters
+    assert lib.kdn_tp_out_proj_allreduce(*args(M=0)) == 0             # nothing to do
+
+
+def test_tp_out_proj_allreduce_peer_argument_checks(lib):
+    import ctypes
+
+    P = 4096
+    arr = lambda *v: (ctypes.c_void_p * len(v))(*v)
+    call = lambda outs, ctrs, rank=0, world=2, N=256, K=64, M=128, dt=0: lib.kdn_tp_out_proj_allreduce_peer(
+        P, P, outs, dt, ctrs, 2, rank, world, M, N, K, None)
+    assert call(arr(P, P), arr(P, P), world=9) == 1                # more ranks than the kernel takes
+    assert call(arr(P, P), arr(P, P), rank=2) == 1
+    assert call(arr(P, P), arr(P, P), N=128) == 2
+    assert call(arr(P, P), arr(P, P), K=32) == 2
+    assert call(arr(P, None), arr(P, P)) == 1                      # a missing copy
+    assert call(arr(P, P + 4), arr(P, P)) == 1                     # a misaligned copy
+    assert call(None, arr(P, P)) == 1
+    assert call(arr(P, P), arr(P, P), dt=5) == 1                   # bad output dtype
+    assert call(arr(P, P), arr(P, P), M=0) == 0
