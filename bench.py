@@ -353,6 +353,97 @@ def bench_tp_out_proj(dev, rank, world, steps=10, warmup=3):
                                  f"{t_tensor:.3f} ms; frac = max of both / measured"}}
 
 
+# config 4: 22-block 20:2 hybrid LM, 64 sequences of lengths uniform in
+# [4096, 65536] sharded over 8 GPUs (8 per GPU), ragged prefill then 256 greedy decode steps
+LM_SEQS, LM_SEQS_PER_GPU, LM_DECODE_STEPS = 64, 8, 256
+
+
+def bench_hybrid_lm(dev, rank, world, decode_steps=LM_DECODE_STEPS):
+    """Per-GPU shard of config 4 through kdn_b200.models.KernelDeltaNetLM (bf16 weights and activations,
+    tensor-core Kernel-DeltaNet prefill, fp32 recurrent state).  Rank r takes sequences [8r, 8r + 8) of the
+    seeded 64 (mod 64 beyond 8 ranks).  Returns aggregate prefill and decode tokens/s (max time over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from kdn_b200.models import KernelDeltaNetLM
+
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = KernelDeltaNetLM(mode="bf16")
+    model = model.to(dev, torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(4242)
+    lens_all = torch.randint(4096, 65537, (LM_SEQS,), generator=g).tolist()
+    ids_all = [torch.randint(0, model.vocab_size, (n,), generator=g) for n in lens_all]
+    pick = [(LM_SEQS_PER_GPU * rank + i) % LM_SEQS for i in range(LM_SEQS_PER_GPU)]
+    lens = [lens_all[i] for i in pick]
+    ids = torch.cat([ids_all[i] for i in pick]).to(dev)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    cache = model.new_cache(len(lens), max(lens) + decode_steps + 1)
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, r
+
+    # warm-up: a short ragged prefill and a few decode steps (cuBLAS / SDPA / libkdn initialisation)
+    wcache = model.new_cache(2, 300)
+    model.prefill(ids[:260], [0, 130, 260], wcache)
+    for _ in range(3):
+        model.decode_step(torch.zeros(2, dtype=torch.int64, device=dev), wcache)
+    del wcache
+    pre_ms, logits = timed(lambda: model.prefill(ids, cu, cache))
+
+    graph = model.capture_decode(cache, greedy=True)  # one decode step as a CUDA graph, argmax fed back
+    graph.tokens.copy_(torch.argmax(logits, dim=-1))
+
+    def decode():
+        for _ in range(decode_steps):
+            graph.step()
+        return graph.tokens
+
+    dec_ms, last = timed(decode)
+    ok = bool(torch.isfinite(logits.float()).all()) and int(last.min()) >= 0
+    del graph, cache, model
+    torch.cuda.empty_cache()
+    prompt_tokens = world * sum(lens)  # every rank holds a shard of the same size class
+    return {"metric": "config4 20:2 hybrid LM (22 blocks, d_model 2048, 32x64 heads, SwiGLU 8192, vocab 32000, "
+                      "anchors [10, 21]): ragged prefill tokens/s; greedy decode tokens/s",
+            "prefill": {"value": world * sum(lens) / (pre_ms * 1e-3), "unit": "tokens/s", "ms": pre_ms,
+                        "prompt_tokens_per_gpu": sum(lens)},
+            "decode": {"value": world * len(lens) * decode_steps / (dec_ms * 1e-3), "unit": "tokens/s",
+                       "ms_per_step": dec_ms / decode_steps, "steps": decode_steps},
+            "sequences_per_gpu": len(lens), "lengths_rank0": lens if rank == 0 else None,
+            "decode_note": "each step one CUDA-graph replay (22 layers + LM head + argmax); anchors read the "
+                           "cache's whole key range under the length mask",
+            "finite": ok, "dtype": "bf16 weights/activations, fp32 recurrent state",
+            "data": "synthetic token ids (uniform over the vocab), random init", "prompt_tokens": prompt_tokens}
+
+
+def run_lm_only(args):
+    """Only the config-4 hybrid LM shard (any world size; torchrun for N > 1)."""
+    import torch
+
+    rank, world, local = dist_init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    r = bench_hybrid_lm(dev, rank, world, decode_steps=args.lm_decode_steps)
+    if rank == 0:
+        print(json.dumps({"hybrid_lm": r, "n_gpus": world}), flush=True)
+
+
 def run_tp_proj_only(args):
     """Only the head-TP output projection comparison (world > 1 under torchrun)."""
     import torch
@@ -571,9 +662,18 @@ def main():
                     help="only run two prefill calls of N sequences x T tokens (for profiler captures)")
     ap.add_argument("--decode-only", type=int, metavar="STEPS",
                     help="only run the decode workload for STEPS steps (for profiler captures)")
+    ap.add_argument("--lm-only", action="store_true", help="only run the config-4 hybrid LM shard")
+    ap.add_argument("--lm-decode-steps", type=int, default=LM_DECODE_STEPS)
     ap.add_argument("--tp-proj-only", action="store_true",
                     help="only compare the head-TP output projection forms (2+ ranks under torchrun)")
     args = ap.parse_args()
+    if args.lm_only:
+        run_lm_only(args)
+        import torch.distributed as dist
+
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        return
     if args.tp_proj_only:
         run_tp_proj_only(args)
         import torch.distributed as dist

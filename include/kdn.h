@@ -203,6 +203,25 @@ int kdn_tp_out_proj_allreduce_peer(const void* y, const void* w, void* const* ou
                                    int64_t M, int32_t N, int32_t K, void* stream);
 
 /*
+ * Element-wise steps of the hybrid decoder block (layers/hybrid_kernel_deltanet_block.py),
+ * each one pass over its data; fp32 arithmetic, dtype KDN_DTYPE_F32 or KDN_DTYPE_BF16 storage.
+ *   kdn_rmsnorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * weight  (RMSNorm, :16-25); x, out
+ *     [n, d] (same dtype, 16-byte aligned, d a multiple of 8 for bf16 / 4 for fp32).
+ *   kdn_swiglu: out[r, j] = silu(gate_up[r, j]) * gate_up[r, d_ff + j]  (SwiGLU, :45-46);
+ *     gate_up [n, 2 d_ff], out [n, d_ff].
+ *   kdn_mixer_inputs: z [n, 3 H 64 + H] (the fused q|k|v|beta projection) -> q, k [n, H, 64]
+ *     L2-normalised per head (layers/kernel_deltanet_layer.py:98-99), v [n, H, 64], and fp32
+ *     beta = sigmoid(z_beta) [n, H] (serving/tensor_parallel_runner.py:62) and decay =
+ *     sigmoid(logit_decay[h]) [n, H] (kernel_deltanet_layer.py:71-73).  d_head must be 64.
+ * No reference entry points (the reference runs these as separate torch ops).
+ */
+int kdn_rmsnorm(const void* x, int dtype, const void* weight, int weight_dtype, void* out, int64_t n, int32_t d,
+                float eps, void* stream);
+int kdn_swiglu(const void* gate_up, void* out, int dtype, int64_t n, int32_t d_ff, void* stream);
+int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, const void* logit_decay,
+                     int logit_dtype, void* q, void* k, void* v, float* beta, float* decay, void* stream);
+
+/*
  * Layout change of a ragged serving batch (no reference counterpart; the reference packs
  * requests the same way, serving/vllm_ragged_batching.py:57-67, then loops over them).
  * Element (sequence i, token t, head h) of the packed [total_tokens, H, row] tensor sits at

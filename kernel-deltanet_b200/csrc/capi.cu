@@ -297,6 +297,49 @@ int kdn_tp_out_proj_allreduce_peer(const void* y, const void* w, void* const* ou
   return ok();
 }
 
+static bool float_dtype(int dt) { return dt == KDN_DTYPE_F32 || dt == KDN_DTYPE_BF16; }
+static int vec_elems(int dt) { return dt == KDN_DTYPE_BF16 ? 8 : 4; }
+
+int kdn_rmsnorm(const void* x, int dtype, const void* weight, int weight_dtype, void* out, int64_t n, int32_t d,
+                float eps, void* stream) {
+  if (n < 0 || d < 1) return fail(KDN_ERR_INVALID, "n=%lld d=%d", (long long)n, d);
+  if (n == 0) return ok();
+  if (!x || !weight || !out) return fail(KDN_ERR_INVALID, "x/weight/out is NULL");
+  if (!float_dtype(dtype) || !float_dtype(weight_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
+  if (d % vec_elems(dtype) != 0) return fail(KDN_ERR_UNSUPPORTED, "d=%d: a multiple of %d", d, vec_elems(dtype));
+  if (!aligned(x, 16) || !aligned(out, 16)) return fail(KDN_ERR_INVALID, "x/out must be 16-byte aligned");
+  cudaError_t e = kdn::launch_rmsnorm(x, weight, weight_dtype, out, dtype, n, d, eps, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return ok();
+}
+
+int kdn_swiglu(const void* gate_up, void* out, int dtype, int64_t n, int32_t d_ff, void* stream) {
+  if (n < 0 || d_ff < 1) return fail(KDN_ERR_INVALID, "n=%lld d_ff=%d", (long long)n, d_ff);
+  if (n == 0) return ok();
+  if (!gate_up || !out) return fail(KDN_ERR_INVALID, "gate_up/out is NULL");
+  if (!float_dtype(dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
+  if (d_ff % vec_elems(dtype) != 0) return fail(KDN_ERR_UNSUPPORTED, "d_ff=%d: a multiple of %d", d_ff, vec_elems(dtype));
+  if (!aligned(gate_up, 16) || !aligned(out, 16)) return fail(KDN_ERR_INVALID, "gate_up/out must be 16-byte aligned");
+  cudaError_t e = kdn::launch_swiglu(gate_up, out, dtype, n, d_ff, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "swiglu launch");
+  return ok();
+}
+
+int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, const void* logit_decay,
+                     int logit_dtype, void* q, void* k, void* v, float* beta, float* decay, void* stream) {
+  if (n < 0 || H < 1) return fail(KDN_ERR_INVALID, "n=%lld H=%d", (long long)n, H);
+  if (d_head != 64) return fail(KDN_ERR_UNSUPPORTED, "d_head=%d (the lift takes 64)", d_head);
+  if (n == 0) return ok();
+  if (!z || !logit_decay || !q || !k || !v || !beta || !decay) return fail(KDN_ERR_INVALID, "a pointer is NULL");
+  if (!float_dtype(dtype) || !float_dtype(logit_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
+  if (!aligned(z, 4) || !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
+    return fail(KDN_ERR_INVALID, "z must be 4-byte, q/k/v 16-byte aligned");
+  cudaError_t e = kdn::launch_mixer_inputs(z, dtype, n, H, logit_decay, logit_dtype, q, k, v, beta, decay,
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "mixer-input launch");
+  return ok();
+}
+
 int kdn_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype, int64_t num_seqs,
                          int64_t total_tokens, int32_t H, int64_t row_bytes, int to_head_major, void* stream) {
   if (total_tokens == 0) return ok();

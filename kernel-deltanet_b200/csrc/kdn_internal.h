@@ -105,6 +105,14 @@ int tp_proj_max_world();
 int64_t tp_proj_tiles(int64_t M, int N);
 cudaError_t tp_proj_read_error(cudaStream_t stream, int* code);
 
+// ---------------------------------------------------------------- glue.cu
+// element-wise steps of the hybrid block: RMSNorm, SwiGLU, the mixer-input split
+cudaError_t launch_rmsnorm(const void* x, const void* w, int wdt, void* out, int dt, int64_t n, int d, float eps,
+                           cudaStream_t stream);
+cudaError_t launch_swiglu(const void* gu, void* out, int dt, int64_t n, int f, cudaStream_t stream);
+cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, const void* logit_decay, int lddt, void* q,
+                                void* k, void* v, float* beta, float* decay, cudaStream_t stream);
+
 // ---------------------------------------------------------------- ragged.cu
 // rows of a packed [total, H, w] batch <-> per-sequence head-major [H, T_i, w] blocks
 cudaError_t launch_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype,

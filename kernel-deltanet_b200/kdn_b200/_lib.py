@@ -66,6 +66,9 @@ SIGNATURES = {
     "kdn_tp_out_proj_allreduce_peer": (_INT, [_P, _P, ctypes.POINTER(_P), _INT, ctypes.POINTER(_P), _U32, _I32, _I32,
                                               _I64, _I32, _I32, _P]),
     "kdn_ragged_transpose": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I32, _I64, _INT, _P]),
+    "kdn_rmsnorm": (_INT, [_P, _INT, _P, _INT, _P, _I64, _I32, ctypes.c_float, _P]),
+    "kdn_swiglu": (_INT, [_P, _P, _INT, _I64, _I32, _P]),
+    "kdn_mixer_inputs": (_INT, [_P, _INT, _I64, _I32, _I32, _P, _INT, _P, _P, _P, _P, _P, _P]),
     "kdn_copy_rows": (_INT, [_P, ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _P]),
     "kdn_affine_compose": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "kdn_affine_prefix_states": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _P]),

@@ -55,12 +55,21 @@ class FastWalshHadamardProjection(nn.Module):
         self.tau_star = float(d_k) ** 0.25
         self.tau_star_inv = 1.0 / self.tau_star
 
-        # draw order of kernels/fwht.py:66-86: d1, d2, d3, then the phase b
+        # draw order of kernels/fwht.py:66-86: d1, d2, d3, then the phase b -- always on the host
+        # generator, whatever default device the caller constructs modules on
+        with torch.device("cpu"):
+            self._draw(seed)
+        self._proj_cache: dict = {}
+
+    def _draw(self, seed: int) -> None:
+        d_k = self.d_k
+        D = self.D
         gen = torch.Generator().manual_seed(seed)
         d1 = torch.where(torch.rand(self.M, d_k, generator=gen) > 0.5, 1.0, -1.0)
         d2 = torch.where(torch.rand(self.M, d_k, generator=gen) > 0.5, 1.0, -1.0)
         d3 = torch.where(torch.rand(self.M, d_k, generator=gen) > 0.5, 1.0, -1.0)
         b = torch.rand(D, generator=gen) * (2.0 * math.pi)
+        self._phase_host = b.clone()  # fp32, not a buffer: dtype casts of the module leave it alone
 
         bits = [pack_sign_bits(d) for d in (d1, d2, d3)]  # [stage][m]
         as_i64 = lambda u: u - (1 << 64) if u >= (1 << 63) else u  # uint64 bit pattern in an int64
@@ -82,7 +91,6 @@ class FastWalshHadamardProjection(nn.Module):
             W = torch.diag(d3[m].double()) @ W
             blocks.append((H @ W) * self.scale_norm)
         self.register_buffer("Omega", torch.cat(blocks, 0).float())
-        self._proj_cache: dict = {}
 
     # ------------------------------------------------------------------ ABI
     def kdn_projection(self, device: torch.device) -> tuple[_lib.KdnProjection, torch.Tensor]:
@@ -95,7 +103,9 @@ class FastWalshHadamardProjection(nn.Module):
             if cached is not None and cached[1].data_ptr() != 0:
                 phase = cached[1]
             else:
-                phase = self.b.detach().to(device=device, dtype=torch.float32).contiguous()
+                # from the host copy drawn at construction: a module-wide dtype cast (model.to(bf16))
+                # rounds the buffer b, never this copy
+                phase = self._phase_host.to(device=device).contiguous()
         s = _lib.KdnProjection()
         s.d_k = self.d_k
         s.D = self.D

@@ -22,6 +22,7 @@ from .projection import ProjectionConstants, make_projection_constants, build_om
 from .chunked import chunked_deltanet_forward
 from .recurrence import token_recurrence, decode_step, decode_step_post
 from .affine import compose, chunk_block_transition, apply_transition
+from . import hybrid_lm
 
 __all__ = [
     "ProjectionConstants",

@@ -17,6 +17,14 @@ def pytest_configure(config):
 
 
 @pytest.fixture(scope="session")
+def lib():
+    """libkdn.so with its signatures (loading needs no GPU)."""
+    from kdn_b200 import _lib
+
+    return _lib.load()
+
+
+@pytest.fixture(scope="session")
 def golden_dir():
     return GOLDEN
 

@@ -18,13 +18,6 @@ def _declared():
     return sorted(set(re.findall(r"\b(kdn_[a-z0-9_]+)\s*\(", text)))
 
 
-@pytest.fixture(scope="module")
-def lib():
-    from kdn_b200 import _lib
-
-    return _lib.load()
-
-
 def test_header_declares_entry_points():
     names = _declared()
     for n in ("kdn_fwht_lift", "kdn_chunked_prefill", "kdn_decode_step", "kdn_fork_state", "kdn_last_error"):

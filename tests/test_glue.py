@@ -1,0 +1,63 @@
+"""Element-wise kernels of the hybrid block (kdn_rmsnorm, kdn_swiglu, kdn_mixer_inputs).
+
+CPU: argument checks of the C entries (no device work).  GPU: each kernel against the same
+formula in torch fp32 -- fp32 storage within 1e-6 relative, bf16 storage within one bf16
+rounding of the fp32 result (2^-8 relative).
+"""
+
+import pytest
+import torch
+
+
+def test_glue_argument_checks(lib):
+    P = 4096
+    assert lib.kdn_rmsnorm(P, 1, P, 0, P, 4, 2052, 1e-6, None) == 2       # d not a multiple of 8 (bf16)
+    assert lib.kdn_rmsnorm(P + 4, 1, P, 0, P, 4, 2048, 1e-6, None) == 1   # misaligned x
+    assert lib.kdn_rmsnorm(P, 5, P, 0, P, 4, 2048, 1e-6, None) == 1       # bad dtype
+    assert lib.kdn_rmsnorm(P, 1, P, 0, P, 0, 2048, 1e-6, None) == 0       # nothing to do
+    assert lib.kdn_swiglu(P, P, 0, 4, 6, None) == 2                        # d_ff not a multiple of 4 (fp32)
+    assert lib.kdn_swiglu(None, P, 0, 4, 8, None) == 1
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 32, P, 0, P, P, P, P, P, None) == 2   # d_head must be 64
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, None, 0, P, P, P, P, P, None) == 1
+    assert lib.kdn_mixer_inputs(P, 1, 0, 2, 64, P, 0, P, P, P, P, P, None) == 0
+
+
+def _close(got, ref, dtype):
+    tol = 1e-6 if dtype == torch.float32 else 2.0 ** -8
+    return bool(((got.float() - ref).abs() <= tol * ref.abs() + 1e-6).all())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rmsnorm_and_swiglu(dtype):
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(333, 2048, generator=g, device="cuda").to(dtype)
+    w = (1 + 0.1 * torch.randn(2048, generator=g, device="cuda")).to(dtype)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert _close(glue.rms_norm(x, w, 1e-6), ref, dtype)
+    gu = torch.randn(77, 2 * 8192, generator=g, device="cuda").to(dtype)
+    gf = gu.float()
+    ref = torch.nn.functional.silu(gf[:, :8192]) * gf[:, 8192:]
+    assert _close(glue.swiglu_product(gu), ref, dtype)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,H", [(torch.float32, 3), (torch.bfloat16, 32)])
+def test_mixer_inputs(dtype, H):
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    n = 129
+    z = torch.randn(n, 3 * H * 64 + H, generator=g, device="cuda").to(dtype)
+    ld = torch.randn(H, generator=g, device="cuda")
+    q, k, v, beta, decay = glue.mixer_inputs(z, H, ld)
+    zf = z.float()
+    rq = torch.nn.functional.normalize(zf[:, :H * 64].view(n, H, 64), dim=-1)
+    rk = torch.nn.functional.normalize(zf[:, H * 64:2 * H * 64].view(n, H, 64), dim=-1)
+    assert _close(q, rq, dtype) and _close(k, rk, dtype)
+    assert torch.equal(v, z[:, 2 * H * 64:3 * H * 64].reshape(n, H, 64))
+    assert _close(beta, torch.sigmoid(zf[:, 3 * H * 64:]), torch.float32)
+    assert _close(decay, torch.sigmoid(ld).expand(n, H), torch.float32)
