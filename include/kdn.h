@@ -203,6 +203,28 @@ int kdn_tp_out_proj_allreduce_peer(const void* y, const void* w, void* const* ou
                                    int64_t M, int32_t N, int32_t K, void* stream);
 
 /*
+ * Backward of kdn_chunked_prefill (the reference differentiates its prefill by recompute +
+ * autograd, kernels/fused_kernel_deltanet.py:158-179; this is that gradient, computed directly).
+ * Given the forward's inputs and dy = dL/dY [N, T, dv] (dy_dtype), optionally dL/d(final
+ * state) [N, dv, D] fp32, it writes fp32 gradients: dq, dk [N, T, d_k], dv_out [N, T, dv],
+ * dbeta [N, T], ddecay [N, T] (when decay is given; zero where the decay is clamped, i.e.
+ * outside [1e-5, 1]) and, if d_initial_state is not NULL, dL/d(initial state) [N, dv, D].
+ * Exact fp32 on CUDA cores: the forward is recomputed with checkpoints (the state entering
+ * every chunk), then one reverse pass over chunks carries the state's adjoint, one parallel
+ * pass forms every chunk's gradients, and the lift is differentiated through its butterfly.
+ * dv a multiple of 16 up to 128; chunk 32 or 64; workspace from
+ * kdn_chunked_prefill_backward_workspace_size (256-byte aligned).
+ */
+size_t kdn_chunked_prefill_backward_workspace_size(int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                                                   const kdn_projection* proj);
+int kdn_chunked_prefill_backward(const void* q, const void* k, const void* v, int in_dtype, const void* beta,
+                                 const void* decay, int gate_dtype, const float* initial_state, const void* dy,
+                                 int dy_dtype, const float* d_final_state, float* dq, float* dk, float* dv_out,
+                                 float* dbeta, float* ddecay, float* d_initial_state, int64_t N, int64_t T,
+                                 int32_t dv, int32_t chunk, const kdn_projection* proj, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/*
  * Element-wise steps of the hybrid decoder block (layers/hybrid_kernel_deltanet_block.py),
  * each one pass over its data; fp32 arithmetic, dtype KDN_DTYPE_F32 or KDN_DTYPE_BF16 storage.
  *   kdn_rmsnorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * weight  (RMSNorm, :16-25); x, out

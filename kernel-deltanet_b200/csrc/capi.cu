@@ -195,6 +195,77 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   return ok();
 }
 
+size_t kdn_chunked_prefill_backward_workspace_size(int64_t N, int64_t T, int32_t dv, int32_t chunk,
+                                                   const kdn_projection* proj) {
+  if (!proj || N < 1 || T < 1 || dv < 16 || (chunk != 32 && chunk != 64)) return 0;
+  return kdn::simt_backward_workspace(N, T, dv, chunk, proj->D);
+}
+
+int kdn_chunked_prefill_backward(const void* q, const void* k, const void* v, int in_dtype, const void* beta,
+                                 const void* decay, int gate_dtype, const float* initial_state, const void* dy,
+                                 int dy_dtype, const float* d_final_state, float* dq, float* dk, float* dv_out,
+                                 float* dbeta, float* ddecay, float* d_initial_state, int64_t N, int64_t T,
+                                 int32_t dv, int32_t chunk, const kdn_projection* proj, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (int rc = check_projection(proj)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N < 1 || N > 65535) return fail(KDN_ERR_INVALID, "N=%lld outside [1, 65535]", (long long)N);
+  if (T < 0) return fail(KDN_ERR_INVALID, "T=%lld < 0", (long long)T);
+  if (dv < 16 || dv > 128 || dv % 16 != 0)
+    return fail(KDN_ERR_UNSUPPORTED, "dv=%d: the backward takes a multiple of 16 in [16, 128]", dv);
+  if (chunk != 32 && chunk != 64) return fail(KDN_ERR_UNSUPPORTED, "chunk=%d: chunk must be 32 or 64", chunk);
+  if (!valid_dtype(in_dtype) || !valid_dtype(gate_dtype) || !valid_dtype(dy_dtype))
+    return fail(KDN_ERR_INVALID, "bad dtype");
+  const size_t state_bytes = sizeof(float) * size_t(N) * dv * proj->D;
+  if (T == 0) {  // no tokens: the initial state's gradient is the final state's
+    if (!d_initial_state) return ok();
+    cudaError_t e = d_final_state ? cudaMemcpyAsync(d_initial_state, d_final_state, state_bytes,
+                                                    cudaMemcpyDeviceToDevice, st)
+                                  : cudaMemsetAsync(d_initial_state, 0, state_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "empty backward state copy");
+    return ok();
+  }
+  if (!q || !k || !v || !beta || !dy || !dq || !dk || !dv_out || !dbeta)
+    return fail(KDN_ERR_INVALID, "q/k/v/beta/dy or a gradient output is NULL");
+  if (!aligned(q, 8) || !aligned(k, 8)) return fail(KDN_ERR_INVALID, "q/k must be 8-byte aligned");
+  if (!aligned(dq, 8) || !aligned(dk, 8)) return fail(KDN_ERR_INVALID, "dq/dk must be 8-byte aligned");
+  const size_t need = kdn::simt_backward_workspace(N, T, dv, chunk, proj->D);
+  if (!workspace || workspace_bytes < need)
+    return fail(KDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(KDN_ERR_INVALID, "workspace must be 256-byte aligned");
+  kdn::BackwardProblem b;
+  b.fwd.q = q;
+  b.fwd.k = k;
+  b.fwd.v = v;
+  b.fwd.in_dtype = in_dtype;
+  b.fwd.beta = beta;
+  b.fwd.decay = decay;
+  b.fwd.gate_dtype = gate_dtype;
+  b.fwd.S0 = initial_state;
+  b.fwd.y = nullptr;
+  b.fwd.y_dtype = KDN_DTYPE_F32;
+  b.fwd.S_out = nullptr;
+  b.fwd.N = N;
+  b.fwd.T = T;
+  b.fwd.dv = dv;
+  b.fwd.C = chunk;
+  b.fwd.D = proj->D;
+  b.dy = dy;
+  b.dy_dtype = dy_dtype;
+  b.dS_final = d_final_state;
+  b.dq = dq;
+  b.dk = dk;
+  b.dv_out = dv_out;
+  b.dbeta = dbeta;
+  b.ddecay = decay ? ddecay : nullptr;
+  b.dS0 = d_initial_state;
+  b.omega = nullptr;
+  const kdn::ProjParams P = kdn::make_proj_params(*proj);
+  cudaError_t e = kdn::launch_simt_backward(b, P, workspace, workspace_bytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+  return ok();
+}
+
 // Same checks and kernels as kdn_chunked_prefill in KDN_MODE_F32; the workspace is the
 // library's fixed scratch array (prefill_static.cu), for callers that cannot allocate.
 int kdn_chunked_prefill_static(const void* q, const void* k, const void* v, int in_dtype, const void* beta,

@@ -34,6 +34,12 @@ struct PrefillProblem {
   // hold the homogeneous part A of the block's affine map, written to A_out [N, a_rows, D].
   int a_rows = 0;
   float* A_out = nullptr;
+  // Backward recompute (CUDA-core path): lift and pair q even without a readout, and keep
+  // the state entering every chunk, S_chunks [N, NC, dv, D], and the chunk-local new-value
+  // rows e_i, E_rows [N, NC * C, dv].
+  bool with_q = false;
+  float* S_chunks = nullptr;
+  float* E_rows = nullptr;
 };
 
 // Per-launch event marks of one prefill call (measurement hook behind
@@ -55,6 +61,24 @@ struct LaunchMarks {
 
 // prefill_simt.cu: exact fp32 arithmetic on CUDA cores, three launches over a workspace.
 size_t simt_prefill_workspace(int64_t N, int64_t T, int dv, int C, int D);
+// Backward of the chunked prefill (exact fp32; forward recompute with checkpoints, reverse
+// adjoint pass over chunks, per-chunk gradients, lift backward).  Outputs fp32.
+struct BackwardProblem {
+  PrefillProblem fwd;     // q, k, v, beta, decay, S0, N, T, dv, C, D (y unused)
+  const void* dy;         // [N, T, dv]
+  int dy_dtype;
+  const float* dS_final;  // [N, dv, D] or null (zero)
+  float* dq;              // [N, T, d_k]
+  float* dk;
+  float* dv_out;          // [N, T, dv]
+  float* dbeta;           // [N, T]
+  float* ddecay;          // [N, T] or null
+  float* dS0;             // [N, dv, D] or null
+  const float* omega;     // unused (the lift is differentiated through its butterfly)
+};
+size_t simt_backward_workspace(int64_t N, int64_t T, int dv, int C, int D);
+cudaError_t launch_simt_backward(const BackwardProblem& b, const ProjParams& P, void* ws, size_t ws_bytes,
+                                 cudaStream_t stream);
 cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, void* ws, size_t ws_bytes,
                                 cudaStream_t stream, LaunchMarks& marks);
 

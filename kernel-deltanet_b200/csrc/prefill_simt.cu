@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kThreads) simt_lift_kernel(PrefillProblem p, W
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int64_t rows = p.N * w.Tp;
   const int D = p.D;
-  const int64_t total = p.y ? 2 * rows : rows;
+  const int64_t total = (p.y || p.with_q) ? 2 * rows : rows;
   for (int64_t r = warp; r < total; r += nwarps) {
     const bool isq = r >= rows;
     const int64_t row = isq ? r - rows : r;
@@ -259,6 +259,10 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
   __syncthreads();
 
   for (int c = 0; c < w.NC; ++c) {
+    if (p.S_chunks && !a_tile) {  // checkpoint: the state entering chunk c
+      float* Sc = p.S_chunks + ((n * w.NC + c) * p.dv + row0) * int64_t(D);
+      for (int e = tid; e < kRowTile * D; e += kThreads) Sc[e] = S[(e / D) * SD + e % D];
+    }
     const float* Tg = w.Tinv + (n * w.NC + c) * int64_t(C) * C;
     const float* Ag = w.Aq + (n * w.NC + c) * int64_t(C) * C;
     const float* Gg = w.gates + (n * w.NC + c) * int64_t(C) * 4;
@@ -323,6 +327,10 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
     }
 #pragma unroll
     for (int u = 0; u < VPT; ++u) Es[i * kRowTile + v0 + u] = e_[u];
+    if (p.E_rows && !a_tile) {
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) p.E_rows[(n * w.Tp + t) * p.dv + row0 + v0 + u] = e_[u];
+    }
     __syncthreads();
     // y_i = exp(g_{i-1}) yq_i + sum_{j<i} Aq_ij e_j ;  then E''_i = exp(g_{C-1} - g_i) e_i into Rs
     if (readout) {
@@ -386,7 +394,7 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
   }
   {
     const size_t smem = prep_smem_bytes<C>();
-    auto prep = p.y ? simt_prep_kernel<C, true> : simt_prep_kernel<C, false>;
+    auto prep = (p.y || p.with_q) ? simt_prep_kernel<C, true> : simt_prep_kernel<C, false>;
     err = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return err;
     prep<<<dim3(w.NC, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
@@ -400,6 +408,586 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
     simt_chain_kernel<C><<<dim3((p.a_rows + p.dv) / kRowTile, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     marks.after(stream);
+  }
+  return cudaSuccess;
+}
+
+// ============================================================================ backward
+//
+// Gradient of the chunked prefill (the reference differentiates it by recompute + autograd,
+// kernels/fused_kernel_deltanet.py:158-179).  With the chunk algebra of the file header
+// (R_i the pseudo-value right-hand side, E = T R the new-value rows, P_ij = Aq_ij,
+// Gs_i = exp(g_{i-1}), G_i = exp(g_i), Rg_i = exp(g_{C-1} - g_i)) and dY, dS_C the adjoints of the
+// chunk's outputs and of the state leaving it, reverse-mode gives
+//
+//   dE_i  = Rg_i (dS_C k_i) + sum_{i'>i} P_{i'i} dY_{i'}          dR = T^T dE
+//   dS_0  = G_{C-1} dS_C + sum_i (Gs_i dY_i q_i^T - beta_i G_i dR_i k_i^T)
+//   dA_ij = -(dR_i . E_j)  (j < i)                                  (T = (I + A)^-1)
+//   dq_i  = Gs_i (dY_i S_0) + sum_j Mq_ij k_j,   Mq_ij = (dY_i . E_j) exp(g_{i-1} - g_j)
+//   dk_i  = sum_i' Mq_{i'i} q_i' - beta_i G_i (dR_i S_0) + Rg_i (E_i dS_C) + sum_j (Ab_ij + Ab_ji) k_j,
+//           Ab_ij = dA_ij beta_i exp(g_i - g_j)
+//   dv_i  = beta_i dR_i,   dbeta_i = dR_i . (v_i - G_i S_0 k_i) + sum_j dA_ij exp(g_i - g_j) k_i . k_j
+//   d g_i collects every exp(g .) factor; d log decay_l = sum_{i >= l} d g_i (within the chunk),
+//   zero where the decay is clamped (outside [1e-5, 1]).
+// The feature gradients go back through the lift (lift_backward_kernel).  Passes: the forward
+// chain with checkpoints (S entering each chunk, E rows), (B1) the reverse pass over chunks for
+// dS (sequential, per 16-row tile), (B2) the per-chunk gradients (parallel), (B3) the lift.
+
+// (B1) per (sequence, 16-row tile of dS): chunks in reverse; stores dS_C of every chunk and dR
+template <int C>
+__global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem b, Workspace w,
+                                                                float* __restrict__ dS_chunks,
+                                                                float* __restrict__ dR_rows) {
+  constexpr int TPR = kThreads / C;
+  constexpr int VPT = kRowTile / TPR;
+  constexpr int LD = C + 1;
+  const PrefillProblem& p = b.fwd;
+  const int D = p.D;
+  const int SD = D + 1;
+  extern __shared__ float sm[];
+  float* dS = sm;                    // [16][SD]
+  float* Ks = dS + kRowTile * SD;    // [C][65]
+  float* Tm = Ks + C * 65;           // [C][LD]
+  float* Am = Tm + C * LD;           // [C][LD]
+  float* gt = Am + C * LD;           // [C][4]
+  float* Ys = gt + C * 4;            // [C][16]: dY, then Gs_i dY_i
+  float* Ws = Ys + C * kRowTile;     // [C][16]: dE, then beta_i G_i dR_i
+
+  const int64_t n = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int i = tid / TPR;
+  const int v0 = (tid % TPR) * VPT;
+  const int row0 = blockIdx.x * kRowTile;
+
+  for (int e = tid; e < kRowTile * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    dS[r * SD + d] = b.dS_final ? b.dS_final[(n * p.dv + row0 + r) * int64_t(D) + d] : 0.f;
+  }
+  __syncthreads();
+
+  for (int c = w.NC - 1; c >= 0; --c) {
+    float* dSc = dS_chunks + ((n * w.NC + c) * p.dv + row0) * int64_t(D);
+    for (int e = tid; e < kRowTile * D; e += kThreads) dSc[e] = dS[(e / D) * SD + e % D];
+    const float* Tg = w.Tinv + (n * w.NC + c) * int64_t(C) * C;
+    const float* Ag = w.Aq + (n * w.NC + c) * int64_t(C) * C;
+    const float* Gg = w.gates + (n * w.NC + c) * int64_t(C) * 4;
+    for (int e = tid; e < C * C; e += kThreads) {
+      Tm[(e / C) * LD + (e % C)] = Tg[e];
+      Am[(e / C) * LD + (e % C)] = Ag[e];
+    }
+    for (int e = tid; e < C * 4; e += kThreads) gt[e] = Gg[e];
+
+    // x_i = k_i . dS_v  (C x 16)
+    const float* Kg = w.phik + (n * w.Tp + int64_t(c) * C) * D;
+    const float* Qg = w.phiq + (n * w.Tp + int64_t(c) * C) * D;
+    float x[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) x[u] = 0.f;
+    for (int d0 = 0; d0 < D; d0 += 64) {
+      __syncthreads();
+      for (int e = tid; e < C * 64; e += kThreads) {
+        const int r = e >> 6, cc = e & 63;
+        Ks[r * 65 + cc] = Kg[int64_t(r) * D + d0 + cc];
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int dd = 0; dd < 64; ++dd) {
+        const float kd = Ks[i * 65 + dd];
+#pragma unroll
+        for (int u = 0; u < VPT; ++u) x[u] = fmaf(kd, dS[(v0 + u) * SD + d0 + dd], x[u]);
+      }
+    }
+    const int64_t t = int64_t(c) * C + i;
+#pragma unroll
+    for (int u = 0; u < VPT; ++u)
+      Ys[i * kRowTile + v0 + u] = t < p.T ? ld_as_f32(b.dy, b.dy_dtype, (n * p.T + t) * p.dv + row0 + v0 + u) : 0.f;
+    __syncthreads();
+    // dE_i = Rg_i x_i + sum_{i'>i} P_{i'i} dY_{i'}
+    const float rg = gt[4 * i + 2];
+    float de[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) de[u] = rg * x[u];
+    for (int j = i + 1; j < C; ++j) {
+      const float a = Am[j * LD + i];
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) de[u] = fmaf(a, Ys[j * kRowTile + v0 + u], de[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) Ws[i * kRowTile + v0 + u] = de[u];
+    __syncthreads();
+    // dR_i = dE_i + sum_{i'>i} T_{i'i} dE_{i'}
+    float dr[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) dr[u] = de[u];
+    for (int j = i + 1; j < C; ++j) {
+      const float tj = Tm[j * LD + i];
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) dr[u] = fmaf(tj, Ws[j * kRowTile + v0 + u], dr[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) dR_rows[(n * w.Tp + t) * p.dv + row0 + v0 + u] = dr[u];
+    __syncthreads();  // every read of dE and dY is done
+    const float gprev = gt[4 * i + 0], gi = gt[4 * i + 1], beta_i = gt[4 * i + 3];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+      Ws[i * kRowTile + v0 + u] = beta_i * gi * dr[u];
+      Ys[i * kRowTile + v0 + u] *= gprev;
+    }
+    __syncthreads();
+    // dS <- G_{C-1} dS + sum_i (Gs_i dY_i q_i^T - beta_i G_i dR_i k_i^T)
+    const float gC = gt[4 * (C - 1) + 1];
+    for (int d = tid; d < D; d += kThreads) {
+      float acc[kRowTile];
+#pragma unroll
+      for (int r = 0; r < kRowTile; ++r) acc[r] = gC * dS[r * SD + d];
+      for (int j = 0; j < C; ++j) {
+        const float kv = Kg[int64_t(j) * D + d], qv = Qg[int64_t(j) * D + d];
+#pragma unroll
+        for (int r = 0; r < kRowTile; ++r)
+          acc[r] = fmaf(Ys[j * kRowTile + r], qv, fmaf(-Ws[j * kRowTile + r], kv, acc[r]));
+      }
+#pragma unroll
+      for (int r = 0; r < kRowTile; ++r) dS[r * SD + d] = acc[r];
+    }
+    __syncthreads();
+  }
+  if (b.dS0) {
+    for (int e = tid; e < kRowTile * D; e += kThreads) {
+      const int r = e / D, d = e % D;
+      b.dS0[(n * p.dv + row0 + r) * int64_t(D) + d] = dS[r * SD + d];
+    }
+  }
+}
+
+// (B2) per (chunk, sequence): the gradients of the chunk's tokens.  The feature gradients
+// overwrite the chunk's lifted features in the workspace (dq -> phiq rows, dk -> phik rows).
+constexpr int kSlab = 32;
+
+template <int C>
+size_t grad_smem_bytes(int dv) {
+  return sizeof(float) * (size_t(3) * C * (dv + 1) + 2 * C * (C + 1) + 2 * C * (kSlab + 1) +
+                          2 * size_t(dv) * (kSlab + 1) + 9 * C + 8);
+}
+
+template <int C>
+__global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, Workspace w,
+                                                             const float* __restrict__ dS_chunks,
+                                                             const float* __restrict__ dR_rows) {
+  constexpr int R = C / 16;             // C x C tile per thread: R x R
+  constexpr int LD = C + 1;
+  constexpr int SL = kSlab + 1;
+  constexpr int TPR2 = kThreads / C;    // threads per token row in the slab phase
+  constexpr int CPT = kSlab / TPR2;     // slab columns per thread
+  const PrefillProblem& p = b.fwd;
+  const int D = p.D, dv = p.dv, LV = dv + 1;
+  extern __shared__ float sm[];
+  float* Em = sm;                  // [C][LV] E rows
+  float* Xm = Em + C * LV;         // [C][LV] dR rows
+  float* Ym = Xm + C * LV;         // [C][LV] dY rows
+  float* M1 = Ym + C * LV;         // [C][LD] Gram k.k, then Ab + Ab^T
+  float* M2 = M1 + C * LD;         // [C][LD] Mq
+  float* Ks = M2 + C * LD;         // [C][SL]
+  float* Qs = Ks + C * SL;         // [C][SL]
+  float* S0s = Qs + C * SL;        // [dv][SL]
+  float* dSs = S0s + dv * SL;      // [dv][SL]
+  float* gl = dSs + dv * SL;       // [C] g_i
+  float* bt = gl + C;              // [C] beta_i
+  float* lm = bt + C;              // [C] decay as given (1 past T)
+  float* dg = lm + C;              // [C] d g_i
+  float* dbA = dg + C;             // [C] the Gram part of d beta_i
+  float* s1 = dbA + C;             // [C] dR_i . (S_0 k_i)
+  float* s2 = s1 + C;              // [C] dY_i . (S_0 q_i)
+  float* s3 = s2 + C;              // [C] E_i . (dS_C k_i)
+  float* xv = s3 + C;              // [C] dR_i . v_i
+  float* red = xv + C;             // [8] <dS_C, S_0> partials
+
+  const int c = blockIdx.x;
+  const int64_t n = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t t0 = int64_t(c) * C;
+  float* Kg = w.phik + (n * w.Tp + t0) * D;
+  float* Qg = w.phiq + (n * w.Tp + t0) * D;
+  const float* S0g = p.S_chunks + (n * w.NC + c) * int64_t(dv) * D;
+  const float* dSg = dS_chunks + (n * w.NC + c) * int64_t(dv) * D;
+
+  if (tid < 32) {  // gates in log space, as the prep pass forms them (pads: beta 0, decay 1)
+    float gsum = 0.f;
+    for (int base = 0; base < C; base += 32) {
+      const int ii = base + lane;
+      const int64_t t = t0 + ii;
+      float dec = 1.f, be = 0.f;
+      if (t < p.T) {
+        dec = p.decay ? ld_as_f32(p.decay, p.gate_dtype, n * p.T + t) : 1.f;
+        be = ld_as_f32(p.beta, p.gate_dtype, n * p.T + t);
+      }
+      float lg = logf(fminf(fmaxf(dec, 1e-5f), 1.0f));
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {  // inclusive scan over the warp
+        const float y = __shfl_up_sync(0xffffffffu, lg, o);
+        if (lane >= o) lg += y;
+      }
+      gl[ii] = gsum + lg;
+      gsum += __shfl_sync(0xffffffffu, lg, 31);
+      bt[ii] = be;
+      lm[ii] = dec;
+    }
+  }
+  for (int e = tid; e < C * dv; e += kThreads) {
+    const int ii = e / dv, v = e % dv;
+    const int64_t t = t0 + ii;
+    Em[ii * LV + v] = p.E_rows[(n * w.Tp + t) * dv + v];
+    Xm[ii * LV + v] = dR_rows[(n * w.Tp + t) * dv + v];
+    Ym[ii * LV + v] = t < p.T ? ld_as_f32(b.dy, b.dy_dtype, (n * p.T + t) * dv + v) : 0.f;
+  }
+  for (int e = tid; e < C; e += kThreads) dg[e] = dbA[e] = s1[e] = s2[e] = s3[e] = 0.f;
+  __syncthreads();
+
+  // ---- sweep 1: Gram k.k and <dS_C, S_0>
+  const int ti = tid / 16, tj = tid % 16;
+  float gk[R][R];
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int q = 0; q < R; ++q) gk[a][q] = 0.f;
+  float dss = 0.f;
+  for (int d0 = 0; d0 < D; d0 += kSlab) {
+    for (int e = tid; e < C * kSlab; e += kThreads) {
+      const int r = e / kSlab, cc = e % kSlab;
+      Ks[r * SL + cc] = Kg[int64_t(r) * D + d0 + cc];
+    }
+    for (int e = tid; e < dv * kSlab; e += kThreads) {
+      const int r = e / kSlab, cc = e % kSlab;
+      dss = fmaf(S0g[int64_t(r) * D + d0 + cc], dSg[int64_t(r) * D + d0 + cc], dss);
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int dd = 0; dd < kSlab; ++dd) {
+      float ka[R], kb[R];
+#pragma unroll
+      for (int a = 0; a < R; ++a) {
+        ka[a] = Ks[(R * ti + a) * SL + dd];
+        kb[a] = Ks[(R * tj + a) * SL + dd];
+      }
+#pragma unroll
+      for (int a = 0; a < R; ++a)
+#pragma unroll
+        for (int q = 0; q < R; ++q) gk[a][q] = fmaf(ka[a], kb[q], gk[a][q]);
+    }
+    __syncthreads();
+  }
+  dss = warp_sum(dss);
+  if (lane == 0) red[warp] = dss;
+
+  // ---- C x C phase: dA, dY.E, the exp(g) factors, d g and d beta contributions
+  float dA[R][R], dP[R][R];
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int q = 0; q < R; ++q) dA[a][q] = dP[a][q] = 0.f;
+  for (int v = 0; v < dv; ++v) {
+    float xa[R], ya[R], eb[R];
+#pragma unroll
+    for (int a = 0; a < R; ++a) {
+      xa[a] = Xm[(R * ti + a) * LV + v];
+      ya[a] = Ym[(R * ti + a) * LV + v];
+      eb[a] = Em[(R * tj + a) * LV + v];
+    }
+#pragma unroll
+    for (int a = 0; a < R; ++a)
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        dA[a][q] = fmaf(-xa[a], eb[q], dA[a][q]);
+        dP[a][q] = fmaf(ya[a], eb[q], dP[a][q]);
+      }
+  }
+  const float* Pg = w.Aq + (n * w.NC + c) * int64_t(C) * C;
+  float ab[R][R], mq[R][R];
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      const int ii = R * ti + a, jj = R * tj + q;
+      ab[a][q] = mq[a][q] = 0.f;
+      if (jj < ii) {
+        const float eij = expf(gl[ii] - gl[jj]);
+        const float aij = bt[ii] * eij * gk[a][q];
+        const float ca = dA[a][q] * aij;  // d g through A
+        atomicAdd(&dg[ii], ca);
+        atomicAdd(&dg[jj], -ca);
+        atomicAdd(&dbA[ii], dA[a][q] * eij * gk[a][q]);
+        const float cp = dP[a][q] * Pg[ii * C + jj];  // d g through P
+        atomicAdd(&dg[ii - 1], cp);
+        atomicAdd(&dg[jj], -cp);
+        mq[a][q] = dP[a][q] * expf(gl[ii - 1] - gl[jj]);
+        ab[a][q] = dA[a][q] * bt[ii] * eij;
+      }
+    }
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      M1[(R * ti + a) * LD + R * tj + q] = ab[a][q];
+      M2[(R * ti + a) * LD + R * tj + q] = mq[a][q];
+    }
+  __syncthreads();
+  float sym[R][R];
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int q = 0; q < R; ++q) sym[a][q] = ab[a][q] + M1[(R * tj + q) * LD + R * ti + a];
+  __syncthreads();
+#pragma unroll
+  for (int a = 0; a < R; ++a)
+#pragma unroll
+    for (int q = 0; q < R; ++q) M1[(R * ti + a) * LD + R * tj + q] = sym[a][q];
+
+  // ---- sweep 2: feature gradients, 32 columns at a time
+  const int i = tid / TPR2;
+  const int cb = (tid % TPR2) * CPT;
+  const float Gs_i = i > 0 ? expf(gl[i - 1]) : 1.f;
+  const float G_i = expf(gl[i]);
+  const float Rg_i = expf(gl[C - 1] - gl[i]);
+  const float bG = bt[i] * G_i;
+  float p1 = 0.f, p2 = 0.f, p3 = 0.f;
+  for (int d0 = 0; d0 < D; d0 += kSlab) {
+    __syncthreads();
+    for (int e = tid; e < C * kSlab; e += kThreads) {
+      const int r = e / kSlab, cc = e % kSlab;
+      Ks[r * SL + cc] = Kg[int64_t(r) * D + d0 + cc];
+      Qs[r * SL + cc] = Qg[int64_t(r) * D + d0 + cc];
+    }
+    for (int e = tid; e < dv * kSlab; e += kThreads) {
+      const int r = e / kSlab, cc = e % kSlab;
+      S0s[r * SL + cc] = S0g[int64_t(r) * D + d0 + cc];
+      dSs[r * SL + cc] = dSg[int64_t(r) * D + d0 + cc];
+    }
+    __syncthreads();
+    float yS[CPT], xS[CPT], wS[CPT], mK[CPT], mQ[CPT], aK[CPT];
+#pragma unroll
+    for (int q = 0; q < CPT; ++q) yS[q] = xS[q] = wS[q] = mK[q] = mQ[q] = aK[q] = 0.f;
+    for (int v = 0; v < dv; ++v) {
+      const float yi = Ym[i * LV + v], xi = Xm[i * LV + v], ei = Em[i * LV + v];
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) {
+        const float s0 = S0s[v * SL + cb + q], ds = dSs[v * SL + cb + q];
+        yS[q] = fmaf(yi, s0, yS[q]);
+        xS[q] = fmaf(xi, s0, xS[q]);
+        wS[q] = fmaf(ei, ds, wS[q]);
+      }
+    }
+    for (int j = 0; j < C; ++j) {
+      const float m_ij = M2[i * LD + j], m_ji = M2[j * LD + i], a_ij = M1[i * LD + j];
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) {
+        const float kj = Ks[j * SL + cb + q], qj = Qs[j * SL + cb + q];
+        mK[q] = fmaf(m_ij, kj, mK[q]);
+        aK[q] = fmaf(a_ij, kj, aK[q]);
+        mQ[q] = fmaf(m_ji, qj, mQ[q]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < CPT; ++q) {
+      const float ki = Ks[i * SL + cb + q], qi = Qs[i * SL + cb + q];
+      p1 = fmaf(ki, xS[q], p1);
+      p2 = fmaf(qi, yS[q], p2);
+      p3 = fmaf(ki, wS[q], p3);
+      Qg[int64_t(i) * D + d0 + cb + q] = fmaf(Gs_i, yS[q], mK[q]);
+      Kg[int64_t(i) * D + d0 + cb + q] = mQ[q] - bG * xS[q] + Rg_i * wS[q] + aK[q];
+    }
+  }
+#pragma unroll
+  for (int o = TPR2 / 2; o > 0; o >>= 1) {
+    p1 += __shfl_xor_sync(0xffffffffu, p1, o);
+    p2 += __shfl_xor_sync(0xffffffffu, p2, o);
+    p3 += __shfl_xor_sync(0xffffffffu, p3, o);
+  }
+  if (tid % TPR2 == 0) {
+    s1[i] = p1;
+    s2[i] = p2;
+    s3[i] = p3;
+  }
+  if (tid < C) {
+    float acc = 0.f;
+    for (int v = 0; v < dv; ++v) {
+      const int64_t t = t0 + tid;
+      const float vv = t < p.T ? ld_as_f32(p.v, p.in_dtype, (n * p.T + t) * dv + v) : 0.f;
+      acc = fmaf(Xm[tid * LV + v], vv, acc);
+    }
+    xv[tid] = acc;
+  }
+  __syncthreads();
+  if (tid < C) {  // per-token d g terms
+    const int ii = tid;
+    const float e_i = expf(gl[C - 1] - gl[ii]) * s3[ii];
+    atomicAdd(&dg[C - 1], e_i);
+    atomicAdd(&dg[ii], -e_i - bt[ii] * expf(gl[ii]) * s1[ii]);
+    if (ii > 0) atomicAdd(&dg[ii - 1], expf(gl[ii - 1]) * s2[ii]);
+    if (ii == C - 1) {
+      float tot = 0.f;
+      for (int q = 0; q < kThreads / 32; ++q) tot += red[q];
+      atomicAdd(&dg[C - 1], expf(gl[C - 1]) * tot);
+    }
+  }
+  __syncthreads();
+  if (tid < C) {
+    const int ii = tid;
+    const int64_t t = t0 + ii;
+    if (t < p.T) {
+      float dlog = 0.f;
+      for (int q = ii; q < C; ++q) dlog += dg[q];
+      b.dbeta[n * p.T + t] = xv[ii] - expf(gl[ii]) * s1[ii] + dbA[ii];
+      if (b.ddecay) {
+        const float dec = lm[ii];
+        b.ddecay[n * p.T + t] = (dec >= 1e-5f && dec <= 1.0f) ? dlog / dec : 0.f;
+      }
+    }
+  }
+  for (int e = tid; e < C * dv; e += kThreads) {
+    const int ii = e / dv, v = e % dv;
+    const int64_t t = t0 + ii;
+    if (t < p.T) b.dv_out[(n * p.T + t) * dv + v] = bt[ii] * Xm[ii * LV + v];
+  }
+}
+
+// transpose of structured_block: x = D1 H D2 H D3 H y / 8 (per-lane pairs, as the forward)
+__device__ __forceinline__ void structured_block_t(float y0, float y1, const uint64_t (&bits)[3], int lane,
+                                                   float& x0, float& x1) {
+  float v0 = y0, v1 = y1;
+  fwht64(v0, v1, lane);
+  apply_signs(v0, v1, bits[2], lane);
+  fwht64(v0, v1, lane);
+  apply_signs(v0, v1, bits[1], lane);
+  fwht64(v0, v1, lane);
+  apply_signs(v0, v1, bits[0], lane);
+  x0 = v0 * 0.125f;
+  x1 = v1 * 0.125f;
+}
+
+// (B3) one warp per token row of q or k: dx = tau_inv Omega^T dz with
+// dz = -amp sin(z) (dphi / e - u (u . dphi) / (|u| e^2)),  e = |u| + 1e-8
+__global__ void __launch_bounds__(kThreads) lift_backward_kernel(BackwardProblem b, Workspace w, ProjParams P) {
+  const PrefillProblem& p = b.fwd;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int64_t rows = p.N * p.T;
+  const int D = p.D;
+  for (int64_t r = warp; r < 2 * rows; r += nwarps) {
+    const bool isq = r >= rows;
+    const int64_t row = isq ? r - rows : r;
+    const int64_t n = row / p.T, t = row % p.T;
+    const float2 xv = ld2_as_f32(isq ? p.q : p.k, p.in_dtype, row * kDk + 2 * lane);
+    const float* g = (isq ? w.phiq : w.phik) + (n * w.Tp + t) * D;
+    float z[kMaxBlocks][2], u[kMaxBlocks][2], gg[kMaxBlocks][2];
+    float ss = 0.f, ug = 0.f;
+#pragma unroll
+    for (int m = 0; m < kMaxBlocks; ++m) {
+      z[m][0] = z[m][1] = u[m][0] = u[m][1] = gg[m][0] = gg[m][1] = 0.f;
+      if (m < P.M) {
+        float a0, a1;
+        structured_block(xv.x, xv.y, P.sign_bits[m], lane, a0, a1);
+        const int f = 64 * m + 2 * lane;
+        const float2 ph = *reinterpret_cast<const float2*>(P.phase + f);
+        z[m][0] = fmaf(a0, P.tau_inv, ph.x);
+        z[m][1] = fmaf(a1, P.tau_inv, ph.y);
+        u[m][0] = P.amp * cosf(z[m][0]);
+        u[m][1] = P.amp * cosf(z[m][1]);
+        const float2 gv = *reinterpret_cast<const float2*>(g + f);
+        gg[m][0] = gv.x;
+        gg[m][1] = gv.y;
+        ss = fmaf(u[m][0], u[m][0], fmaf(u[m][1], u[m][1], ss));
+        ug = fmaf(u[m][0], gv.x, fmaf(u[m][1], gv.y, ug));
+      }
+    }
+    ss = warp_sum(ss);
+    ug = warp_sum(ug);
+    const float nrm = sqrtf(ss);
+    const float e = nrm + 1e-8f;
+    const float c1 = 1.f / e, c2 = ug / (fmaxf(nrm, 1e-30f) * e * e);
+    float dx0 = 0.f, dx1 = 0.f;
+#pragma unroll
+    for (int m = 0; m < kMaxBlocks; ++m) {
+      if (m < P.M) {
+        const float dz0 = -(gg[m][0] * c1 - u[m][0] * c2) * P.amp * sinf(z[m][0]);
+        const float dz1 = -(gg[m][1] * c1 - u[m][1] * c2) * P.amp * sinf(z[m][1]);
+        float a0, a1;
+        structured_block_t(dz0, dz1, P.sign_bits[m], lane, a0, a1);
+        dx0 += a0;
+        dx1 += a1;
+      }
+    }
+    float* dst = (isq ? b.dq : b.dk) + row * kDk + 2 * lane;
+    dst[0] = dx0 * P.tau_inv;
+    dst[1] = dx1 * P.tau_inv;
+  }
+}
+
+template <int C>
+size_t adjoint_smem_bytes(int D) {
+  return sizeof(float) * (size_t(kRowTile) * (D + 1) + C * 65 + 2 * C * (C + 1) + 4 * C + 2 * C * kRowTile);
+}
+
+struct BackwardExtra {
+  float* S_chunks;
+  float* dS_chunks;
+  float* E_rows;
+  float* dR_rows;
+  float* S_scratch;
+};
+
+BackwardExtra carve_backward(void* base, int64_t N, int64_t T, int dv, int C, int D, size_t* total) {
+  size_t off = 0;
+  Workspace w = carve(base, N, T, dv, C, D, &off);
+  char* bp = static_cast<char*>(base);
+  auto take = [&](size_t bytes) {
+    char* q = bp ? bp + off : nullptr;
+    off = align256(off + bytes);
+    return reinterpret_cast<float*>(q);
+  };
+  BackwardExtra x;
+  x.S_chunks = take(sizeof(float) * size_t(N) * w.NC * dv * D);
+  x.dS_chunks = take(sizeof(float) * size_t(N) * w.NC * dv * D);
+  x.E_rows = take(sizeof(float) * size_t(N) * w.Tp * dv);
+  x.dR_rows = take(sizeof(float) * size_t(N) * w.Tp * dv);
+  x.S_scratch = take(sizeof(float) * size_t(N) * dv * D);
+  if (total) *total = off;
+  return x;
+}
+
+template <int C>
+cudaError_t launch_backward_c(BackwardProblem b, const Workspace& w, const BackwardExtra& x, const ProjParams& P,
+                              cudaStream_t stream) {
+  LaunchMarks none;
+  b.fwd.y = nullptr;
+  b.fwd.with_q = true;
+  b.fwd.S_chunks = x.S_chunks;
+  b.fwd.E_rows = x.E_rows;
+  b.fwd.S_out = x.S_scratch;
+  b.fwd.a_rows = 0;
+  b.fwd.A_out = nullptr;
+  cudaError_t err = launch_c<C>(b.fwd, w, P, stream, none);  // lift, prep, chain with checkpoints
+  if (err != cudaSuccess) return err;
+  {
+    const size_t smem = adjoint_smem_bytes<C>(b.fwd.D);
+    err = cudaFuncSetAttribute(simt_adjoint_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return err;
+    simt_adjoint_kernel<C><<<dim3(b.fwd.dv / kRowTile, unsigned(b.fwd.N)), kThreads, smem, stream>>>(
+        b, w, x.dS_chunks, x.dR_rows);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  }
+  {
+    const size_t smem = grad_smem_bytes<C>(b.fwd.dv);
+    err = cudaFuncSetAttribute(simt_grad_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return err;
+    simt_grad_kernel<C><<<dim3(w.NC, unsigned(b.fwd.N)), kThreads, smem, stream>>>(b, w, x.dS_chunks, x.dR_rows);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  }
+  {
+    int64_t blocks = (2 * b.fwd.N * b.fwd.T + 7) / 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks < 1) blocks = 1;
+    lift_backward_kernel<<<unsigned(blocks), kThreads, 0, stream>>>(b, w, P);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
   }
   return cudaSuccess;
 }
@@ -419,6 +1007,22 @@ cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, vo
   if (ws_bytes < need) return cudaErrorInvalidValue;
   if (p.C == 64) return launch_c<64>(p, w, P, stream, marks);
   return launch_c<32>(p, w, P, stream, marks);
+}
+
+size_t simt_backward_workspace(int64_t N, int64_t T, int dv, int C, int D) {
+  size_t total = 0;
+  carve_backward(nullptr, N, T, dv, C, D, &total);
+  return total;
+}
+
+cudaError_t launch_simt_backward(const BackwardProblem& b, const ProjParams& P, void* ws, size_t ws_bytes,
+                                 cudaStream_t stream) {
+  size_t need = 0;
+  BackwardExtra x = carve_backward(ws, b.fwd.N, b.fwd.T, b.fwd.dv, b.fwd.C, b.fwd.D, &need);
+  if (ws_bytes < need) return cudaErrorInvalidValue;
+  Workspace w = carve(ws, b.fwd.N, b.fwd.T, b.fwd.dv, b.fwd.C, b.fwd.D, nullptr);
+  if (b.fwd.C == 64) return launch_backward_c<64>(b, w, x, P, stream);
+  return launch_backward_c<32>(b, w, x, P, stream);
 }
 
 }  // namespace kdn

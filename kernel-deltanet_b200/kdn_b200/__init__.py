@@ -17,12 +17,14 @@ All compute goes through libkdn.so (C ABI in include/kdn.h).
 from ._lib import LIB_PATH, load
 from .distributed import sequence_parallel_prefill, shard_range
 from .kernels import (FastWalshHadamardProjection, FusedKernelDeltaNet, blelloch_prefix_scan, chunk_block_transition,
-                      compose_transitions, fused_chunked_deltanet_forward, sequential_prefix_scan)
+                      chunked_deltanet_backward, compose_transitions, fused_chunked_deltanet_forward,
+                      sequential_prefix_scan)
 from .layers import KernelDeltaNetLayer, KernelTTTLayer
 from .serving import fork_recurrent_state, hybrid_recurrent_forward, ragged_prefill
 from .models import HybridCache, KernelDeltaNetLM
 
 __all__ = ["load", "LIB_PATH", "FastWalshHadamardProjection", "fused_chunked_deltanet_forward",
+           "chunked_deltanet_backward",
            "FusedKernelDeltaNet", "KernelDeltaNetLayer", "KernelTTTLayer", "hybrid_recurrent_forward",
            "fork_recurrent_state", "compose_transitions", "blelloch_prefix_scan", "sequential_prefix_scan",
            "chunk_block_transition", "sequence_parallel_prefill", "shard_range", "ragged_prefill",

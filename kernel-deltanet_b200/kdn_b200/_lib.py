@@ -58,6 +58,11 @@ SIGNATURES = {
                                    ctypes.POINTER(KdnProjection), _INT, _P, ctypes.c_size_t, _P]),
     "kdn_chunked_prefill_static": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _P, _INT, _P, _I64, _I64, _I32, _I32,
                                           ctypes.POINTER(KdnProjection), _P]),
+    "kdn_chunked_prefill_backward_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I32, _I32,
+                                                                       ctypes.POINTER(KdnProjection)]),
+    "kdn_chunked_prefill_backward": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _P, _INT, _P, _P, _P, _P, _P, _P, _P,
+                                            _I64, _I64, _I32, _I32, ctypes.POINTER(KdnProjection), _P,
+                                            ctypes.c_size_t, _P]),
     "kdn_set_prefill_events": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT]),
     "kdn_prefill_launch_count": (_INT, []),
     "kdn_tp_out_proj": (_INT, [_P, _P, _P, _INT, _P, _I64, _I32, _I32, _P]),

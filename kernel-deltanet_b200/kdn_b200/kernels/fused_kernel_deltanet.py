@@ -19,7 +19,11 @@ tensors' CUDA device and current stream; there is no CPU path.  Host
 (CPU) tensors are accepted with ``device="cuda"``: the sequence is then streamed
 through that device in segments of ``segment_tokens`` (copies in and out overlap
 the kernels) and the results come back as host tensors, complete on return.
-Backward is not implemented (the reference recomputes through autograd, :158-179).
+Gradients: when any of q, k, v, beta, decay, initial_state requires grad (and grad mode
+is on), the call goes through an autograd Function whose backward is the libkdn backward
+(``kdn_chunked_prefill_backward``: exact fp32, forward recomputed with chunk checkpoints),
+for dY and d(final state) alike; the reference gets the same gradients by recompute +
+autograd (:158-179).  ``chunked_deltanet_backward`` exposes that backward directly.
 """
 
 from __future__ import annotations
@@ -50,6 +54,33 @@ def _check_cuda(*ts):
 
 
 def fused_chunked_deltanet_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    beta: torch.Tensor,
+    decay: Optional[torch.Tensor],
+    fwht_proj: FastWalshHadamardProjection,
+    chunk_size: int = 64,
+    initial_state: Optional[torch.Tensor] = None,
+    *,
+    mode: Optional[str] = None,
+    workspace: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    final_state: Optional[torch.Tensor] = None,
+    device=None,
+    segment_tokens: int = 8192,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    needs_grad = torch.is_grad_enabled() and any(
+        t is not None and t.requires_grad for t in (q, k, v, beta, decay, initial_state))
+    if needs_grad:
+        if out is not None or final_state is not None or not q.is_cuda:
+            raise RuntimeError("inputs that require grad take neither out=/final_state= buffers nor host tensors")
+        return _PrefillWithGrad.apply(q, k, v, beta, decay, initial_state, fwht_proj, chunk_size, mode)
+    return _forward_impl(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state, mode=mode, workspace=workspace,
+                         out=out, final_state=final_state, device=device, segment_tokens=segment_tokens)
+
+
+def _forward_impl(
     q: torch.Tensor,
     k: torch.Tensor,
     v: torch.Tensor,
@@ -221,17 +252,93 @@ def _streamed_forward(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state
     return y_host, S_host
 
 
+def chunked_deltanet_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+                              decay: Optional[torch.Tensor], dY: torch.Tensor,
+                              fwht_proj: FastWalshHadamardProjection, chunk_size: int = 64,
+                              initial_state: Optional[torch.Tensor] = None,
+                              d_final_state: Optional[torch.Tensor] = None) -> dict:
+    """Gradients of the chunked prefill (libkdn ``kdn_chunked_prefill_backward``, exact fp32).
+
+    Same shapes as the forward; dY [B, T, d_v] is dL/dY and d_final_state [B, d_v, D] (or None)
+    dL/d(final state).  Returns fp32 tensors {"dq", "dk", "dv", "dbeta", "ddecay" (None without
+    decay), "d_initial_state"} -- the gradients the reference's recompute + autograd gives
+    (kernels/fused_kernel_deltanet.py:167-179), plus the initial state's."""
+    dev = _check_cuda(q, k, v, beta, decay, dY, initial_state, d_final_state)
+    B, T, d_k = q.shape
+    dv = v.shape[-1]
+    D = fwht_proj.D
+    if k.shape != q.shape or v.shape[:2] != (B, T) or dY.shape != v.shape or beta.shape != (B, T):
+        raise RuntimeError("shape mismatch between q, k, v, beta and dY")
+    in_dtype = q.dtype if q.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    gate_dtype = beta.dtype if beta.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    qc, kc, vc = (t.detach().to(in_dtype).contiguous() for t in (q, k, v))
+    bc = beta.detach().to(gate_dtype).contiguous()
+    dc = None if decay is None else decay.detach().to(gate_dtype).contiguous()
+    yc = dY.detach().to(torch.float32 if dY.dtype not in (torch.float32, torch.bfloat16) else dY.dtype).contiguous()
+    S0 = None if initial_state is None else initial_state.detach().to(torch.float32).contiguous()
+    dSf = None if d_final_state is None else d_final_state.detach().to(torch.float32).contiguous()
+    f32 = dict(device=dev, dtype=torch.float32)
+    dq, dk = torch.empty(B, T, d_k, **f32), torch.empty(B, T, d_k, **f32)
+    dvv = torch.empty(B, T, dv, **f32)
+    db = torch.empty(B, T, **f32)
+    dd = torch.empty(B, T, **f32) if dc is not None else None
+    dS0 = torch.empty(B, dv, D, **f32)
+    lib = _lib.load()
+    proj, _phase = fwht_proj.kdn_projection(dev)
+    ws_bytes = int(lib.kdn_chunked_prefill_backward_workspace_size(B, T, dv, chunk_size, proj))
+    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    rc = lib.kdn_chunked_prefill_backward(
+        qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), _lib.dtype_code(qc), bc.data_ptr(), _lib.ptr(dc),
+        _lib.dtype_code(bc), _lib.ptr(S0), yc.data_ptr(), _lib.dtype_code(yc), _lib.ptr(dSf), dq.data_ptr(),
+        dk.data_ptr(), dvv.data_ptr(), db.data_ptr(), _lib.ptr(dd), dS0.data_ptr(), B, T, dv, chunk_size, proj,
+        ws.data_ptr(), ws_bytes, _lib.stream_handle(dev))
+    _lib.check(rc, "kdn_chunked_prefill_backward")
+    return {"dq": dq, "dk": dk, "dv": dvv, "dbeta": db, "ddecay": dd, "d_initial_state": dS0}
+
+
+def _grad_as(g: Optional[torch.Tensor], like: Optional[torch.Tensor]):
+    if g is None or like is None or not like.requires_grad:
+        return None
+    return g.to(like.dtype)
+
+
+class _PrefillWithGrad(torch.autograd.Function):
+    """(Y, final state) with the libkdn backward for both outputs."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, beta, decay, initial_state, fwht_proj, chunk_size, mode):
+        Y, S = _forward_impl(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state, mode=mode)
+        ctx.save_for_backward(q, k, v, beta, decay, initial_state)
+        ctx.fwht_proj, ctx.chunk_size = fwht_proj, chunk_size
+        return Y, S
+
+    @staticmethod
+    def backward(ctx, dY, dS):
+        q, k, v, beta, decay, S0 = ctx.saved_tensors
+        if dY is None:
+            dY = torch.zeros(v.shape, device=v.device, dtype=torch.float32)
+        g = chunked_deltanet_backward(q, k, v, beta, decay, dY, ctx.fwht_proj, ctx.chunk_size, S0, dS)
+        return (_grad_as(g["dq"], q), _grad_as(g["dk"], k), _grad_as(g["dv"], v), _grad_as(g["dbeta"], beta),
+                _grad_as(g["ddecay"], decay), _grad_as(g["d_initial_state"], S0), None, None, None)
+
+
 class FusedKernelDeltaNetFunction(torch.autograd.Function):
-    """Forward-only autograd wrapper (kernels/fused_kernel_deltanet.py:158-179 recomputes for backward)."""
+    """Autograd Function of the reference (kernels/fused_kernel_deltanet.py:158-179): Y only.
+    Its backward is the libkdn backward rather than recompute + autograd (same gradients)."""
 
     @staticmethod
     def forward(ctx, q, k, v, beta, decay, fwht_proj, chunk_size=64):
-        Y, _ = fused_chunked_deltanet_forward(q, k, v, beta, decay, fwht_proj, chunk_size)
+        Y, _ = _forward_impl(q, k, v, beta, decay, fwht_proj, chunk_size)
+        ctx.save_for_backward(q, k, v, beta, decay)
+        ctx.fwht_proj, ctx.chunk_size = fwht_proj, chunk_size
         return Y
 
     @staticmethod
     def backward(ctx, grad_output):
-        raise NotImplementedError("kdn_b200: the backward pass of the chunked scan is not implemented")
+        q, k, v, beta, decay = ctx.saved_tensors
+        g = chunked_deltanet_backward(q, k, v, beta, decay, grad_output, ctx.fwht_proj, ctx.chunk_size)
+        return (g["dq"].to(q.dtype), g["dk"].to(k.dtype), g["dv"].to(v.dtype), g["dbeta"].to(beta.dtype),
+                None if decay is None else g["ddecay"].to(decay.dtype), None, None)
 
 
 class FusedKernelDeltaNet(nn.Module):

@@ -2,12 +2,12 @@
 
 Run once in a container where the reference checkout is available:
 
-    python tests/golden/make_golden.py /path/to/kernel-deltanet
+    python tests/golden/make_golden.py /path/to/kernel-deltanet [--only-backward]
 
 It imports the reference's own modules
 
     kernels/fwht.py                     FastWalshHadamardProjection
-    kernels/fused_kernel_deltanet.py    fused_chunked_deltanet_forward
+    kernels/fused_kernel_deltanet.py    fused_chunked_deltanet_forward, FusedKernelDeltaNetFunction
     kernels/blelloch_scan.py            compose_transitions
     tests/test_fused_kernel.py          sequential_deltanet_reference
     benchmarks/run_full_batch_decoding.py  step_recurrent_state
@@ -55,7 +55,39 @@ PREFILL_CASES = {
 }
 
 
+BACKWARD_CASES = {
+    # name: (seed, N, T, d_k, dv, C, gated)
+    "backward_t130_gated": (21, 1, 130, 64, 64, 64, True),
+    "backward_t63_n2": (22, 2, 63, 64, 64, 64, False),
+    "backward_c32_dv128_gated": (23, 1, 96, 64, 128, 32, True),
+}
+
+
+def backward_fixtures(ref_root: str) -> None:
+    """Gradients from the reference's autograd Function (kernels/fused_kernel_deltanet.py:158-179):
+    recompute the forward under autograd, then d(Y . dY)/d(q, k, v, beta, decay), fp32 on CPU."""
+    sys.path.insert(0, ref_root)
+    import torch
+
+    torch.set_num_threads(1)
+    from kernels.fwht import FastWalshHadamardProjection
+    from kernels.fused_kernel_deltanet import FusedKernelDeltaNetFunction
+
+    p = FastWalshHadamardProjection(64, 512, seed=42)
+    for name, (seed, N, T, d_k, dv, C, gated) in BACKWARD_CASES.items():
+        q, k, v, beta, decay, _ = _inputs(seed, N, T, d_k, dv, gated, False)
+        dY = np.random.default_rng(seed + 1000).standard_normal((N, T, dv)).astype(np.float32)
+        ins = [torch.from_numpy(a).requires_grad_(True) for a in (q, k, v, beta, decay)]
+        Y = FusedKernelDeltaNetFunction.apply(*ins, p, C)
+        Y.backward(torch.from_numpy(dY))
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), q=q, k=k, v=v, beta=beta, decay=decay, dY=dY,
+                            Y=Y.detach().numpy(), dq=ins[0].grad.numpy(), dk=ins[1].grad.numpy(),
+                            dv=ins[2].grad.numpy(), dbeta=ins[3].grad.numpy(), ddecay=ins[4].grad.numpy(),
+                            meta=np.array([seed, N, T, d_k, dv, C, int(gated)]))
+
+
 def main(ref_root: str) -> None:
+    backward_fixtures(ref_root)
     sys.path.insert(0, ref_root)
     import torch
 
@@ -140,4 +172,9 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KDN_REFERENCE_ROOT", ""))
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = args[0] if args else os.environ.get("KDN_REFERENCE_ROOT", "")
+    if "--only-backward" in sys.argv:
+        backward_fixtures(root)
+    else:
+        main(root)
