@@ -398,12 +398,11 @@ def bench_hybrid_lm(dev, rank, world, decode_steps=LM_DECODE_STEPS):
             ms = float(t.item())
         return ms, r
 
-    # warm-up: a short ragged prefill and a few decode steps (cuBLAS / SDPA / libkdn initialisation)
-    wcache = model.new_cache(2, 300)
-    model.prefill(ids[:260], [0, 130, 260], wcache)
+    # warm-up: one untimed prefill of the same batch (library initialisation, allocator growth to the
+    # workload's buffer sizes) and a few eager decode steps; the timed prefill then overwrites the cache
+    model.prefill(ids, cu, cache)
     for _ in range(3):
-        model.decode_step(torch.zeros(2, dtype=torch.int64, device=dev), wcache)
-    del wcache
+        model.decode_step(torch.zeros(len(lens), dtype=torch.int64, device=dev), cache)
     pre_ms, logits = timed(lambda: model.prefill(ids, cu, cache))
 
     graph = model.capture_decode(cache, greedy=True)  # one decode step as a CUDA graph, argmax fed back
@@ -426,8 +425,8 @@ def bench_hybrid_lm(dev, rank, world, decode_steps=LM_DECODE_STEPS):
             "decode": {"value": world * len(lens) * decode_steps / (dec_ms * 1e-3), "unit": "tokens/s",
                        "ms_per_step": dec_ms / decode_steps, "steps": decode_steps},
             "sequences_per_gpu": len(lens), "lengths_rank0": lens if rank == 0 else None,
-            "decode_note": "each step one CUDA-graph replay (22 layers + LM head + argmax); anchors read the "
-                           "cache's whole key range under the length mask",
+            "decode_note": "each step one CUDA-graph replay (22 layers + LM head + argmax); anchors use libkdn's "
+                           "split-K decode attention over each sequence's live keys",
             "finite": ok, "dtype": "bf16 weights/activations, fp32 recurrent state",
             "data": "synthetic token ids (uniform over the vocab), random init", "prompt_tokens": prompt_tokens}
 
@@ -442,6 +441,32 @@ def run_lm_only(args):
     r = bench_hybrid_lm(dev, rank, world, decode_steps=args.lm_decode_steps)
     if rank == 0:
         print(json.dumps({"hybrid_lm": r, "n_gpus": world}), flush=True)
+
+
+BWD_N, BWD_T = 16, 4096
+
+
+def bench_backward(dev, steps=3):
+    """The libkdn backward (exact fp32) of a [16 heads x 4096 tokens] prefill: dL/d(q, k, v, beta) for a
+    given dL/dY (per rank; not a headline)."""
+    import torch
+
+    from kdn_b200 import FastWalshHadamardProjection, chunked_deltanet_backward
+
+    proj = FastWalshHadamardProjection().to(dev)
+    q, k, v, beta = (t.float() for t in prefill_inputs(dev, 99, n_heads=BWD_N, seq=BWD_T))
+    dY = torch.randn(BWD_N, BWD_T, DV, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+    chunked_deltanet_backward(q, k, v, beta, None, dY, proj, C)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        chunked_deltanet_backward(q, k, v, beta, None, dY, proj, C)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"metric": f"prefill backward token-heads/s ({BWD_N} heads x {BWD_T} tokens, exact fp32, per GPU)",
+            "value": BWD_N * BWD_T / (ms * 1e-3), "unit": "token-heads/s", "ms": ms, "steps": steps}
 
 
 def run_tp_proj_only(args):
@@ -550,6 +575,8 @@ def run_ours(args):
     dec = bench_decode(dev, steps=200, warmup=5, peaks=peaks)
     rag = bench_ragged(dev, steps=10, warmup=3)
     tpp = bench_tp_out_proj(dev, rank, world) if world > 1 else None
+    bwd = bench_backward(dev)
+    lm = bench_hybrid_lm(dev, rank, world) if not args.no_lm else None
 
     if world > 1:
         dist.barrier()
@@ -617,6 +644,9 @@ def run_ours(args):
     }
     if tpp is not None:
         line["tp_out_proj"] = tpp
+    line["backward"] = bwd
+    if lm is not None:
+        line["hybrid_lm"] = lm
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.ref_seq)
     print(json.dumps(line), flush=True)
@@ -663,6 +693,7 @@ def main():
     ap.add_argument("--decode-only", type=int, metavar="STEPS",
                     help="only run the decode workload for STEPS steps (for profiler captures)")
     ap.add_argument("--lm-only", action="store_true", help="only run the config-4 hybrid LM shard")
+    ap.add_argument("--no-lm", action="store_true", help="skip the config-4 hybrid LM shard in the full run")
     ap.add_argument("--lm-decode-steps", type=int, default=LM_DECODE_STEPS)
     ap.add_argument("--tp-proj-only", action="store_true",
                     help="only compare the head-TP output projection forms (2+ ranks under torchrun)")

@@ -225,6 +225,19 @@ int kdn_chunked_prefill_backward(const void* q, const void* k, const void* v, in
                                  size_t workspace_bytes, void* stream);
 
 /*
+ * One-token softmax attention over a KV cache (the anchor layers' decode step in the hybrid
+ * model; the reference keeps those layers as Llama attention, models/upcycling_llama_bridge.py:240-249).
+ * q [B, H, 64], k_cache / v_cache [B, H, max_len, 64] (dtype), lengths [B] int64 on the device:
+ * query (b, h) attends to cache positions [0, lengths[b]] with scale 1/8; out [B, H, 64].
+ * Positions past a sequence's length cost nothing.  A length >= max_len yields a zero output
+ * row (the positions it names do not exist).  workspace: kdn_decode_attention_workspace_size.
+ */
+size_t kdn_decode_attention_workspace_size(int64_t B, int32_t H, int64_t max_len);
+int kdn_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* lengths, void* out,
+                         int dtype, int64_t B, int32_t H, int64_t max_len, int32_t d_head, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/*
  * Element-wise steps of the hybrid decoder block (layers/hybrid_kernel_deltanet_block.py),
  * each one pass over its data; fp32 arithmetic, dtype KDN_DTYPE_F32 or KDN_DTYPE_BF16 storage.
  *   kdn_rmsnorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * weight  (RMSNorm, :16-25); x, out

@@ -369,6 +369,33 @@ int kdn_tp_out_proj_allreduce_peer(const void* y, const void* w, void* const* ou
 }
 
 static bool float_dtype(int dt) { return dt == KDN_DTYPE_F32 || dt == KDN_DTYPE_BF16; }
+
+size_t kdn_decode_attention_workspace_size(int64_t B, int32_t H, int64_t max_len) {
+  if (B < 1 || H < 1 || max_len < 1) return 0;
+  return kdn::decode_attn_workspace(B, H, max_len);
+}
+
+int kdn_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* lengths, void* out,
+                         int dtype, int64_t B, int32_t H, int64_t max_len, int32_t d_head, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (B < 0 || H < 1 || max_len < 1) return fail(KDN_ERR_INVALID, "B=%lld H=%d max_len=%lld", (long long)B, H,
+                                                 (long long)max_len);
+  if (d_head != 64) return fail(KDN_ERR_UNSUPPORTED, "d_head=%d (64 only)", d_head);
+  if (B == 0) return ok();
+  if (B > 65535 || H > 65535 || kdn::decode_attn_splits(max_len) > (1 << 30))
+    return fail(KDN_ERR_UNSUPPORTED, "grid too large");
+  if (!q || !k_cache || !v_cache || !lengths || !out) return fail(KDN_ERR_INVALID, "a pointer is NULL");
+  if (!float_dtype(dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 8) || !aligned(lengths, 8))
+    return fail(KDN_ERR_INVALID, "q/k_cache/v_cache must be 16-byte aligned");
+  const size_t need = kdn::decode_attn_workspace(B, H, max_len);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
+    return fail(KDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+  cudaError_t e = kdn::launch_decode_attn(q, k_cache, v_cache, lengths, out, dtype, B, H, max_len,
+                                          static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
+  return ok();
+}
 static int vec_elems(int dt) { return dt == KDN_DTYPE_BF16 ? 8 : 4; }
 
 int kdn_rmsnorm(const void* x, int dtype, const void* weight, int weight_dtype, void* out, int64_t n, int32_t d,

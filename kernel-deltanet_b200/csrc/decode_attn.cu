@@ -1,0 +1,209 @@
+// decode_attn.cu -- one-token softmax attention over a KV cache (the anchor layers' decode step).
+//
+// The hybrid model's anchor layers (models/upcycling_llama_bridge.py:240-249) attend, at every
+// decode step, from one query per (sequence, head) to every cached key of that sequence.  That is
+// a pure streaming read of K and V (256 bytes per key at d = 64, bf16); with a few sequences the
+// (sequence, head) pairs alone cannot fill the GPU, so the key range is split: CTA (b, h, s) reduces
+// keys [s*kKeys, (s+1)*kKeys) of sequence b to a partial (running max, sum of exponentials, weighted
+// value sum), and a second kernel merges the partials of (b, h).  CTAs past a sequence's length
+// exit at once, so the cost follows the live lengths even when the launch (e.g. inside a CUDA graph)
+// is sized for the cache's capacity.
+//
+// In a CTA each lane scores whole keys (its 64-element key row against the query held in
+// registers), the warp keeps an online softmax over its keys, and the value rows are summed with
+// each lane owning two output dimensions.
+#include <math.h>
+
+#include "kdn_common.cuh"
+#include "kdn_internal.h"
+
+namespace kdn {
+namespace {
+
+constexpr int kHd = 64;        // head dimension
+constexpr int kKeys = 512;     // keys per CTA
+constexpr int kWarps = 4;
+constexpr int kPart = kHd + 2; // partial record: m, l, acc[64]
+
+template <typename T>
+__device__ __forceinline__ void load_row(const T* p, float* f) {  // 64 elements
+  if constexpr (sizeof(T) == 2) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 u = reinterpret_cast<const uint4*>(p)[c];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        f[8 * c + 2 * i] = t.x;
+        f[8 * c + 2 * i + 1] = t.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const float4 t = reinterpret_cast<const float4*>(p)[c];
+      f[4 * c] = t.x;
+      f[4 * c + 1] = t.y;
+      f[4 * c + 2] = t.z;
+      f[4 * c + 3] = t.w;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float2 load_pair(const T* p) {
+  if constexpr (sizeof(T) == 2) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  return *reinterpret_cast<const float2*>(p);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kWarps) decode_attn_partial_kernel(const T* __restrict__ q,
+                                                                          const T* __restrict__ kc,
+                                                                          const T* __restrict__ vc,
+                                                                          const int64_t* __restrict__ lengths,
+                                                                          float* __restrict__ part, int H,
+                                                                          int64_t max_len, int splits, float scale) {
+  __shared__ float red[kWarps][kPart];
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t nkeys = lengths[b] + 1;  // positions [0, lengths[b]]
+  const int64_t k0 = int64_t(s) * kKeys;
+  float* out = part + ((int64_t(b) * H + h) * splits + s) * kPart;
+  if (k0 >= nkeys || nkeys > max_len) {  // nothing of this sequence here (or a length out of range)
+    if (threadIdx.x == 0) {
+      out[0] = -INFINITY;
+      out[1] = 0.f;
+    }
+    if (threadIdx.x < kHd) out[2 + threadIdx.x] = 0.f;
+    return;
+  }
+  const int64_t k1 = (k0 + kKeys < nkeys) ? k0 + kKeys : nkeys;
+  const int64_t bh = int64_t(b) * H + h;
+  float qf[kHd];
+  load_row(q + bh * kHd, qf);
+  const T* kb = kc + bh * max_len * kHd;
+  const T* vb = vc + bh * max_len * kHd;
+  float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
+  for (int64_t j0 = k0 + 32 * warp; j0 < k1; j0 += 32 * kWarps) {
+    const int64_t j = j0 + lane;
+    float sc = -INFINITY;
+    if (j < k1) {
+      float kf[kHd];
+      load_row(kb + j * kHd, kf);
+      float dot = 0.f;
+#pragma unroll
+      for (int d = 0; d < kHd; ++d) dot = fmaf(qf[d], kf[d], dot);
+      sc = dot * scale;
+    }
+    float mx = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float mn = fmaxf(m, mx);  // finite: the group has at least one key
+    const float corr = expf(m - mn);
+    const float p = (j < k1) ? expf(sc - mn) : 0.f;
+    float ps = p;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    l = l * corr + ps;
+    a0 *= corr;
+    a1 *= corr;
+    const int cnt = int((k1 - j0) < 32 ? (k1 - j0) : 32);
+    for (int r = 0; r < cnt; ++r) {
+      const float pr = __shfl_sync(0xffffffffu, p, r);
+      const float2 vv = load_pair(vb + (j0 + r) * kHd + 2 * lane);
+      a0 = fmaf(pr, vv.x, a0);
+      a1 = fmaf(pr, vv.y, a1);
+    }
+    m = mn;
+  }
+  if (lane == 0) {
+    red[warp][0] = m;
+    red[warp][1] = l;
+  }
+  red[warp][2 + 2 * lane] = a0;
+  red[warp][3 + 2 * lane] = a1;
+  __syncthreads();
+  if (warp == 0) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, red[w][0]);
+    float L = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = red[w][0] == -INFINITY ? 0.f : expf(red[w][0] - M);
+      L = fmaf(red[w][1], f, L);
+      o0 = fmaf(red[w][2 + 2 * lane], f, o0);
+      o1 = fmaf(red[w][3 + 2 * lane], f, o1);
+    }
+    if (lane == 0) {
+      out[0] = M;
+      out[1] = L;
+    }
+    out[2 + 2 * lane] = o0;
+    out[3 + 2 * lane] = o1;
+  }
+}
+
+// one warp per (b, h): merge the partials, o = sum_s acc_s e^{m_s - M} / sum_s l_s e^{m_s - M}
+template <typename T>
+__global__ void __launch_bounds__(256) decode_attn_merge_kernel(const float* __restrict__ part, T* __restrict__ o,
+                                                                int64_t BH, int splits) {
+  const int64_t bh = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (bh >= BH) return;
+  const float* p = part + bh * splits * kPart;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, p[s * kPart]);
+  float L = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float ms = p[s * kPart];
+    if (ms == -INFINITY) continue;
+    const float f = expf(ms - M);
+    L = fmaf(p[s * kPart + 1], f, L);
+    o0 = fmaf(p[s * kPart + 2 + 2 * lane], f, o0);
+    o1 = fmaf(p[s * kPart + 3 + 2 * lane], f, o1);
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  if constexpr (sizeof(T) == 2)
+    reinterpret_cast<__nv_bfloat162*>(o + bh * kHd)[lane] = __floats2bfloat162_rn(o0 * inv, o1 * inv);
+  else
+    reinterpret_cast<float2*>(o + bh * kHd)[lane] = make_float2(o0 * inv, o1 * inv);
+}
+
+}  // namespace
+
+int decode_attn_splits(int64_t max_len) { return int((max_len + kKeys - 1) / kKeys); }
+
+size_t decode_attn_workspace(int64_t B, int H, int64_t max_len) {
+  return sizeof(float) * size_t(B) * H * decode_attn_splits(max_len) * kPart;
+}
+
+cudaError_t launch_decode_attn(const void* q, const void* k_cache, const void* v_cache, const int64_t* lengths,
+                               void* out, int dt, int64_t B, int H, int64_t max_len, float* part,
+                               cudaStream_t stream) {
+  const int splits = decode_attn_splits(max_len);
+  const dim3 grid{unsigned(splits), unsigned(H), unsigned(B)};
+  const float scale = 0.125f;  // 1 / sqrt(64)
+  if (dt == KDN_DTYPE_BF16) {
+    decode_attn_partial_kernel<__nv_bfloat16><<<grid, 32 * kWarps, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
+        static_cast<const __nv_bfloat16*>(v_cache), lengths, part, H, max_len, splits, scale);
+  } else {
+    decode_attn_partial_kernel<float><<<grid, 32 * kWarps, 0, stream>>>(
+        static_cast<const float*>(q), static_cast<const float*>(k_cache), static_cast<const float*>(v_cache), lengths,
+        part, H, max_len, splits, scale);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int64_t BH = B * H;
+  const unsigned mg = unsigned((BH + 7) / 8);
+  if (dt == KDN_DTYPE_BF16)
+    decode_attn_merge_kernel<__nv_bfloat16><<<mg, 256, 0, stream>>>(part, static_cast<__nv_bfloat16*>(out), BH,
+                                                                    splits);
+  else
+    decode_attn_merge_kernel<float><<<mg, 256, 0, stream>>>(part, static_cast<float*>(out), BH, splits);
+  return cudaGetLastError();
+}
+
+}  // namespace kdn

@@ -137,6 +137,14 @@ cudaError_t launch_swiglu(const void* gu, void* out, int dt, int64_t n, int f, c
 cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, const void* logit_decay, int lddt, void* q,
                                 void* k, void* v, float* beta, float* decay, cudaStream_t stream);
 
+// ---------------------------------------------------------------- decode_attn.cu
+// one query per (sequence, head) against its cached keys [0, lengths[b]] (d = 64), split-K
+int decode_attn_splits(int64_t max_len);
+size_t decode_attn_workspace(int64_t B, int H, int64_t max_len);
+cudaError_t launch_decode_attn(const void* q, const void* k_cache, const void* v_cache, const int64_t* lengths,
+                               void* out, int dt, int64_t B, int H, int64_t max_len, float* part,
+                               cudaStream_t stream);
+
 // ---------------------------------------------------------------- ragged.cu
 // rows of a packed [total, H, w] batch <-> per-sequence head-major [H, T_i, w] blocks
 cudaError_t launch_ragged_transpose(const void* src, void* dst, const void* cu_seqlens, int index_dtype,

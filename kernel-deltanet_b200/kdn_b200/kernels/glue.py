@@ -3,10 +3,13 @@
 ``rms_norm`` (layers/hybrid_kernel_deltanet_block.py:23-25), ``swiglu_product`` (silu(gate) * up,
 :45-46) and ``mixer_inputs`` (split of the fused q|k|v|beta projection: unit-norm q, k per head,
 v, beta = sigmoid, decay = sigmoid(logit_decay) per head) -- the C entries kdn_rmsnorm,
-kdn_swiglu and kdn_mixer_inputs.  Errors raise RuntimeError; there is no CPU path.
+kdn_swiglu and kdn_mixer_inputs -- and ``decode_attention`` (the anchors' one-token attention over
+their KV cache, kdn_decode_attention).  Errors raise RuntimeError; there is no CPU path.
 """
 
 from __future__ import annotations
+
+from typing import Optional
 
 import torch
 
@@ -59,3 +62,25 @@ def mixer_inputs(z: torch.Tensor, num_heads: int, logit_decay: torch.Tensor, d_h
                                             beta.data_ptr(), decay.data_ptr(), _lib.stream_handle(z.device)),
                "kdn_mixer_inputs")
     return q, k, v, beta, decay
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lengths: torch.Tensor,
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q [B, H, 64], caches [>=B, H, max_len, 64], lengths [B] int64 (device) -> softmax(q K^T / 8) V over
+    positions [0, lengths[b]] of cache row b, [B, H, 64] in q's dtype (kdn_decode_attention)."""
+    _cuda(q, k_cache, v_cache, lengths)
+    B, H, dh = q.shape
+    max_len = k_cache.shape[2]
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()) or k_cache.dtype != q.dtype:
+        raise RuntimeError("k_cache / v_cache must be contiguous and of q's dtype")
+    lib = _lib.load()
+    need = int(lib.kdn_decode_attention_workspace_size(B, H, max_len))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need // 4, 1), device=q.device, dtype=torch.float32)
+    qc = q.contiguous()
+    lc = lengths.to(torch.int64).contiguous()
+    out = torch.empty_like(qc)
+    _lib.check(lib.kdn_decode_attention(qc.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lc.data_ptr(),
+                                        out.data_ptr(), _lib.dtype_code(qc), B, H, max_len, dh, workspace.data_ptr(),
+                                        need, _lib.stream_handle(q.device)), "kdn_decode_attention")
+    return out

@@ -24,7 +24,8 @@ Mixers:
   its hybrid models (models/upcycling_llama_bridge.py:240-249, anchors at [10, 21]):
   multi-head causal softmax attention with rotary positions (the retained Llama attention,
   rotate-half convention, models/upcycling_llama_bridge.py:138-140) and a KV cache for decode.
-  It is library attention (torch SDPA), not part of the Kernel-DeltaNet hot path.
+  The prefill is library attention (torch SDPA); the one-token decode is libkdn's split-K
+  kdn_decode_attention, which reads only each sequence's live keys.
 """
 
 from __future__ import annotations
@@ -116,7 +117,7 @@ class KernelDeltaNetMixer(nn.Module):
 
 
 # SDPA back ends for the anchors: flash (then memory-efficient) for the causal prefill, memory-efficient
-# for the masked one-token decode.  cuDNN's back end is left out: it builds a new graph (with a device
+# for the masked one-token decode when the libkdn decode attention (d_head 64) does not apply.  cuDNN's back end is left out: it builds a new graph (with a device
 # query of tens of milliseconds) for every new sequence length, which made the host the bottleneck.
 _PREFILL_BACKENDS = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
 _DECODE_BACKENDS = [SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
@@ -177,10 +178,13 @@ class SoftmaxAnchor(nn.Module):
         rows = torch.arange(B, device=x.device)
         k_cache[rows, :, lengths] = k
         v_cache[rows, :, lengths] = v
-        mask = (torch.arange(span, device=x.device)[None, :] <= lengths[:, None])[:, None, None, :]
-        with sdpa_kernel(_DECODE_BACKENDS):
-            o = F.scaled_dot_product_attention(q.unsqueeze(2), k_cache[:B, :, :span], v_cache[:B, :, :span],
-                                               attn_mask=mask)
+        if self.d_head == 64 and k_cache.shape[0] == B and q.dtype in (torch.float32, torch.bfloat16):
+            o = glue.decode_attention(q, k_cache, v_cache, lengths)  # split-K over the live lengths only
+        else:
+            mask = (torch.arange(span, device=x.device)[None, :] <= lengths[:, None])[:, None, None, :]
+            with sdpa_kernel(_DECODE_BACKENDS):
+                o = F.scaled_dot_product_attention(q.unsqueeze(2), k_cache[:B, :, :span], v_cache[:B, :, :span],
+                                                   attn_mask=mask)
         return self.w_out(o.reshape(B, -1))
 
 

@@ -20,6 +20,11 @@ def test_glue_argument_checks(lib):
     assert lib.kdn_mixer_inputs(P, 1, 4, 2, 32, P, 0, P, P, P, P, P, None) == 2   # d_head must be 64
     assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, None, 0, P, P, P, P, P, None) == 1
     assert lib.kdn_mixer_inputs(P, 1, 0, 2, 64, P, 0, P, P, P, P, P, None) == 0
+    assert lib.kdn_decode_attention(P, P, P, P, P, 1, 2, 4, 100, 32, P, 1 << 20, None) == 2   # d_head 64 only
+    assert lib.kdn_decode_attention(P, None, P, P, P, 1, 2, 4, 100, 64, P, 1 << 20, None) == 1
+    assert lib.kdn_decode_attention(P, P, P, P, P, 1, 2, 4, 100, 64, P, 8, None) == 4        # workspace too small
+    assert lib.kdn_decode_attention(P, P, P, P, P, 1, 0, 4, 100, 64, None, 0, None) == 0     # no sequences
+    assert lib.kdn_decode_attention_workspace_size(2, 4, 1000) == 4 * 2 * 4 * 2 * 66
 
 
 def _close(got, ref, dtype):
@@ -61,3 +66,28 @@ def test_mixer_inputs(dtype, H):
     assert torch.equal(v, z[:, 2 * H * 64:3 * H * 64].reshape(n, H, 64))
     assert _close(beta, torch.sigmoid(zf[:, 3 * H * 64:]), torch.float32)
     assert _close(decay, torch.sigmoid(ld).expand(n, H), torch.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_attention(dtype):
+    """Split-K one-token attention over ragged cache lengths (split boundaries 511/512/513) against
+    a float64 softmax; a length past the cache gives a zero row."""
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    B, H, L = 7, 3, 1100
+    q = torch.randn(B, H, 64, generator=g, device="cuda").to(dtype)
+    kc = torch.randn(B, H, L, 64, generator=g, device="cuda").to(dtype)
+    vc = torch.randn(B, H, L, 64, generator=g, device="cuda").to(dtype)
+    lengths = torch.tensor([0, 511, 512, 513, 1000, L - 1, L + 5], device="cuda")
+    out = glue.decode_attention(q, kc, vc, lengths).double()
+    for b in range(B):
+        n = int(lengths[b]) + 1
+        if n > L:
+            assert float(out[b].abs().max()) == 0.0
+            continue
+        s = torch.einsum("hd,hjd->hj", q[b].double(), kc[b, :, :n].double()) / 8.0
+        ref = torch.einsum("hj,hjd->hd", torch.softmax(s, dim=-1), vc[b, :, :n].double())
+        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        assert float((out[b] - ref).abs().max()) <= tol * max(1.0, float(ref.abs().max())), b
