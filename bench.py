@@ -553,7 +553,7 @@ def run_ours(args):
 
     def e2e_step():
         kdn_b200.fused_chunked_deltanet_forward(hq, hk, hv, hb, None, proj, C, mode="bf16", out=hy, final_state=hS,
-                                                device=dev, segment_tokens=E2E_SEGMENT)
+                                                device=dev, segment_tokens=args.e2e_segment)
 
     for _ in range(2):
         e2e_step()
@@ -694,6 +694,7 @@ def main():
                     help="only run the decode workload for STEPS steps (for profiler captures)")
     ap.add_argument("--lm-only", action="store_true", help="only run the config-4 hybrid LM shard")
     ap.add_argument("--no-lm", action="store_true", help="skip the config-4 hybrid LM shard in the full run")
+    ap.add_argument("--e2e-segment", type=int, default=E2E_SEGMENT, help="tokens per streamed segment (e2e)")
     ap.add_argument("--lm-decode-steps", type=int, default=LM_DECODE_STEPS)
     ap.add_argument("--tp-proj-only", action="store_true",
                     help="only compare the head-TP output projection forms (2+ ranks under torchrun)")
