@@ -33,6 +33,9 @@
 // Operands are staged by cp.async into 128-byte-swizzled K-major tiles (4 stages of K = 64,
 // the next tile's first three loading during this tile's epilogue); one thread issues the
 // MMAs; each epilogue thread writes 32-column pieces of its accumulator row from registers.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "kdn_internal.h"
 #include "tc_prims.cuh"
 
@@ -136,6 +139,150 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Reduction of the owned tiles (owner forms): CTA b reduces the owned tiles j = b, b + grid, ... (tile
+// t = rank + j * world), a quarter tile (32 rows) per unit, units claimed in production order from the
+// CTA's shared counter `claim` by every warp that calls this (reducer warps from the start, tile warps
+// once they have no tile left to compute).
+__device__ __forceinline__ void reduce_owned(const ProjArgs& a, unsigned int* claim, int64_t tiles, int tiles_n, int lane,
+                             bool& ok) {
+  if (a.mode >= kReduceOwned && a.rank < tiles) {
+    const int64_t owned = (tiles - a.rank + a.world - 1) / a.world;
+    const int64_t mine = owned > blockIdx.x ? (owned - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const unsigned int units = unsigned(mine * 4);
+#pragma unroll 1
+    while (true) {
+      unsigned int u = 0;
+      if (lane == 0) u = atomicAdd(claim, 1u);
+      u = __shfl_sync(0xffffffffu, u, 0);
+      if (u >= units) break;
+      const int64_t t = a.rank + (blockIdx.x + int64_t(u >> 2) * gridDim.x) * a.world;
+      int good = 0;
+      if (lane == 0)
+        for (uint32_t n = 0; n < kFlagPollLimit; ++n)
+          if (int32_t(ld_acquire_sys(a.flags + t) - a.target) >= 0) {
+            good = 1;
+            break;
+          }
+      good = __shfl_sync(0xffffffffu, good, 0);
+      __syncwarp();  // the acquire before every lane's reads
+      if (!good) {
+        ok = false;
+        continue;
+      }
+      const int n0 = int(t % tiles_n) * kBN;
+      const int64_t m0 = (t / tiles_n) * kBM + 32 * (u & 3);
+      if (a.mode == kReduceOwned) {
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {  // 8 rows x 2 vectors per lane in flight
+          float4 v[8][2];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = m0 + r0 + i;
+            if (row < a.M) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) v[i][h] = ld_reduce_v4(a.out_mc + row * a.N + n0 + 128 * h + 4 * lane);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = m0 + r0 + i;
+            if (row < a.M) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) st_v4_all(a.out_mc + row * a.N + n0 + 128 * h + 4 * lane, v[i][h]);
+            }
+          }
+        }
+      } else if (a.out_bf16) {  // peer form, bf16 copies: a lane takes 8 columns (16 B) of a row
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {
+          float acc[8][8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.peer_out[p]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) {
+                const float4 raw = ld_peer_v4(reinterpret_cast<const float*>(src + row * a.N + n0 + 8 * lane));
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __bfloat1622float2(h2[e]);
+                  acc[i][2 * e] += f.x;
+                  acc[i][2 * e + 1] += f.y;
+                }
+              }
+            }
+          }
+          uint4 pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint32_t* w32 = reinterpret_cast<uint32_t*>(&pk[i]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 b = __floats2bfloat162_rn(acc[i][2 * e], acc[i][2 * e + 1]);
+              w32[e] = *reinterpret_cast<const uint32_t*>(&b);
+            }
+          }
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) *reinterpret_cast<uint4*>(dst + row * a.N + n0 + 8 * lane) = pk[i];
+            }
+          }
+        }
+      } else {  // peer form: read every copy, add in rank order, write the sum into every copy
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {  // 8 rows x 2 vectors per lane, one copy at a time
+          float4 v[8][2];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) v[i][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            const float* src = a.peer_out[p];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float4 x = ld_peer_v4(src + row * a.N + n0 + 128 * h + 4 * lane);
+                  v[i][h].x += x.x;
+                  v[i][h].y += x.y;
+                  v[i][h].z += x.z;
+                  v[i][h].w += x.w;
+                }
+              }
+            }
+          }
+#pragma unroll 1
+          for (int p = 0; p < a.world; ++p) {
+            float* dst = a.peer_out[p];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t row = m0 + r0 + i;
+              if (row < a.M) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                  *reinterpret_cast<float4*>(dst + row * a.N + n0 + 128 * h + 4 * lane) = v[i][h];
+              }
+            }
+          }
+        }
+      }
+    }
+  }
 }
 
 __device__ __forceinline__ void tile_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThrP) : "memory"); }
@@ -288,151 +435,196 @@ __global__ void __launch_bounds__(kThrAll, 1) tp_proj_kernel(ProjArgs a) {
 
   }
 
-  // ---------------------------------------------------------------- reduction of the owned tiles
-  // (owner forms) CTA b reduces the owned tiles j = b, b + grid, ... (tile t = rank + j * world),
-  // a quarter tile (32 rows) per unit, units claimed in production order from a shared counter:
-  // the reducer warps from the start, the tile warps as soon as they have no tile left to compute.
-  if (a.mode >= kReduceOwned && a.rank < tiles) {
-    const int64_t owned = (tiles - a.rank + a.world - 1) / a.world;
-    const int64_t mine = owned > blockIdx.x ? (owned - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-    const unsigned int units = unsigned(mine * 4);
-#pragma unroll 1
-    while (true) {
-      unsigned int u = 0;
-      if (lane == 0) u = atomicAdd(claim, 1u);
-      u = __shfl_sync(0xffffffffu, u, 0);
-      if (u >= units) break;
-      const int64_t t = a.rank + (blockIdx.x + int64_t(u >> 2) * gridDim.x) * a.world;
-      int good = 0;
-      if (lane == 0)
-        for (uint32_t n = 0; n < kFlagPollLimit; ++n)
-          if (int32_t(ld_acquire_sys(a.flags + t) - a.target) >= 0) {
-            good = 1;
-            break;
-          }
-      good = __shfl_sync(0xffffffffu, good, 0);
-      __syncwarp();  // the acquire before every lane's reads
-      if (!good) {
-        ok = false;
-        continue;
-      }
-      const int n0 = int(t % tiles_n) * kBN;
-      const int64_t m0 = (t / tiles_n) * kBM + 32 * (u & 3);
-      if (a.mode == kReduceOwned) {
-#pragma unroll 1
-        for (int r0 = 0; r0 < 32; r0 += 8) {  // 8 rows x 2 vectors per lane in flight
-          float4 v[8][2];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int64_t row = m0 + r0 + i;
-            if (row < a.M) {
-#pragma unroll
-              for (int h = 0; h < 2; ++h) v[i][h] = ld_reduce_v4(a.out_mc + row * a.N + n0 + 128 * h + 4 * lane);
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int64_t row = m0 + r0 + i;
-            if (row < a.M) {
-#pragma unroll
-              for (int h = 0; h < 2; ++h) st_v4_all(a.out_mc + row * a.N + n0 + 128 * h + 4 * lane, v[i][h]);
-            }
-          }
-        }
-      } else if (a.out_bf16) {  // peer form, bf16 copies: a lane takes 8 columns (16 B) of a row
-#pragma unroll 1
-        for (int r0 = 0; r0 < 32; r0 += 8) {
-          float acc[8][8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-#pragma unroll 1
-          for (int p = 0; p < a.world; ++p) {
-            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.peer_out[p]);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int64_t row = m0 + r0 + i;
-              if (row < a.M) {
-                const float4 raw = ld_peer_v4(reinterpret_cast<const float*>(src + row * a.N + n0 + 8 * lane));
-                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = __bfloat1622float2(h2[e]);
-                  acc[i][2 * e] += f.x;
-                  acc[i][2 * e + 1] += f.y;
-                }
-              }
-            }
-          }
-          uint4 pk[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            uint32_t* w32 = reinterpret_cast<uint32_t*>(&pk[i]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 b = __floats2bfloat162_rn(acc[i][2 * e], acc[i][2 * e + 1]);
-              w32[e] = *reinterpret_cast<const uint32_t*>(&b);
-            }
-          }
-#pragma unroll 1
-          for (int p = 0; p < a.world; ++p) {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int64_t row = m0 + r0 + i;
-              if (row < a.M) *reinterpret_cast<uint4*>(dst + row * a.N + n0 + 8 * lane) = pk[i];
-            }
-          }
-        }
-      } else {  // peer form: read every copy, add in rank order, write the sum into every copy
-#pragma unroll 1
-        for (int r0 = 0; r0 < 32; r0 += 8) {  // 8 rows x 2 vectors per lane, one copy at a time
-          float4 v[8][2];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) v[i][h] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-          for (int p = 0; p < a.world; ++p) {
-            const float* src = a.peer_out[p];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int64_t row = m0 + r0 + i;
-              if (row < a.M) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const float4 x = ld_peer_v4(src + row * a.N + n0 + 128 * h + 4 * lane);
-                  v[i][h].x += x.x;
-                  v[i][h].y += x.y;
-                  v[i][h].z += x.z;
-                  v[i][h].w += x.w;
-                }
-              }
-            }
-          }
-#pragma unroll 1
-          for (int p = 0; p < a.world; ++p) {
-            float* dst = a.peer_out[p];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int64_t row = m0 + r0 + i;
-              if (row < a.M) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                  *reinterpret_cast<float4*>(dst + row * a.N + n0 + 128 * h + 4 * lane) = v[i][h];
-              }
-            }
-          }
-        }
-      }
-    }
-  }
+  reduce_owned(a, claim, tiles, tiles_n, lane, ok);
   if (a.mode != kStore) __threadfence_system();  // the remote writes before the kernel's completion
   if (!ok) record_device_error(&g_proj_error, kErrProjWaitTimeout);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, kBN);
+}
+
+// ---------------------------------------------------------------------------- TMA-fed form
+// Same tiles and outputs (modes kStore, kReduceOwned, kReduceOwnedPeer), warp-specialised: warp 4
+// issues the TMA loads of a 4-stage ring (one thread, two tensor-map copies per k-block), warp 5
+// issues the MMAs into one of two 256-column TMEM accumulators, warps 0-3 drain the other
+// accumulator (so a tile's epilogue overlaps the next tile's products) and then join the
+// reduction, warps 6-7 reduce owned tiles from the start.
+constexpr int kEpiWarps = 4, kProdWarp = 4, kMmaWarp = 5, kRedWarp0 = 6, kRedWarps = 2;
+constexpr int kThrT = 32 * (kRedWarp0 + kRedWarps);
+constexpr int kStagesT = 4;
+constexpr uint32_t T_BAR = kStageP * kStagesT;  // full[4], empty[4], acc_full[2], acc_empty[2]
+constexpr uint32_t T_TSLOT = T_BAR + 8 * (2 * kStagesT + 4);
+constexpr uint32_t T_CLAIM = T_TSLOT + 16;
+constexpr uint32_t kProjSmemT = T_CLAIM + 16 + 1024;
+static_assert(kProjSmemT <= 227 * 1024, "TMA projection ring exceeds shared memory");
+
+// 2-D tensor-map tile into shared memory; completion counted in bytes on `bar` (no multicast)
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const __grid_constant__ CUtensorMap mapA,
+                                                               const __grid_constant__ CUtensorMap mapB) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = tc::smem_u32(sm);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + T_BAR);
+  uint64_t* empty = full + kStagesT;
+  uint64_t* accf = empty + kStagesT;
+  uint64_t* acce = accf + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + T_TSLOT);
+  unsigned int* claim = reinterpret_cast<unsigned int*>(sm + T_CLAIM);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KT = a.K / kBK;
+  const int tiles_n = a.N / kBN;
+  const int64_t tiles = ((a.M + kBM - 1) / kBM) * tiles_n;
+  bool ok = true;
+
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc(tslot, 2 * kBN);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kStagesT; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&accf[b], 1);
+      tc::mbar_init(&acce[b], kEpiWarps);
+    }
+    *claim = 0u;
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot;
+
+  if (warp == kProdWarp) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int n0 = int(t % tiles_n) * kBN;
+        const int m0 = int((t / tiles_n) * kBM);
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const uint32_t s = it % kStagesT;
+          if (it >= kStagesT) ok &= proj_wait(&empty[s], ((it / kStagesT) - 1) & 1u);  // its previous use is read
+          tc::mbar_arrive_expect_tx(&full[s], kStageP);
+          const uint32_t st = sbase + s * kStageP;
+          tma_load_2d(st, &mapA, kt * kBK, m0, &full[s]);
+          tma_load_2d(st + kATile, &mapB, kt * kBK, n0, &full[s]);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16_f32(kBM, kBN, false, false);
+      uint32_t it = 0, tcount = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++tcount) {
+        const uint32_t ab = tcount & 1u;
+        if (tcount >= 2) ok &= proj_wait(&acce[ab], ((tcount >> 1) - 1) & 1u);  // drained two tiles ago
+        tc::fence_after_sync();
+        const uint32_t acc = tmem + kBN * ab;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const uint32_t s = it % kStagesT;
+          ok &= proj_wait(&full[s], (it / kStagesT) & 1u);
+          tc::fence_after_sync();
+          const uint32_t st = sbase + s * kStageP;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc::mma_ss(acc, tc::smem_desc_sw128(st + 32 * kk, 16, 1024),
+                       tc::smem_desc_sw128(st + kATile + 32 * kk, 16, 1024), idesc, kt > 0 || kk > 0);
+          tc::mma_commit(&empty[s]);
+        }
+        tc::mma_commit(&accf[ab]);
+      }
+    }
+  } else if (warp < kEpiWarps) {
+    uint32_t tcount = 0;
+    const int r = 32 * warp + lane;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++tcount) {
+      const uint32_t ab = tcount & 1u;
+      ok &= proj_wait(&accf[ab], (tcount >> 1) & 1u);
+      tc::fence_after_sync();
+      const int n0 = int(t % tiles_n) * kBN;
+      const int64_t row = (t / tiles_n) * kBM + r;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + kBN * ab + c0, v);
+        tc::tmem_ld_wait();
+        if (row < a.M) {
+          const int64_t off = row * a.N + n0 + c0;
+          if (a.out_bf16) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 pk;
+              uint32_t* w32 = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+                w32[e] = *reinterpret_cast<const uint32_t*>(&b2);
+              }
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + off + j) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(a.out + off + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acce[ab]);  // this warp's TMEM lanes are read
+      if (a.mode >= kReduceOwned) {
+        tc::named_bar_sync(1, 32 * kEpiWarps);  // every row of the tile is written
+        if (tid == 0) {
+          __threadfence_system();
+          if (a.mode == kReduceOwned)
+            announce(a.flags_mc + t);
+          else
+            for (int p = 0; p < a.world; ++p) announce_peer(a.peer_flags[p] + t);
+        }
+      }
+    }
+  }
+  if (warp < kEpiWarps || warp >= kRedWarp0) reduce_owned(a, claim, tiles, tiles_n, lane, ok);
+  if (a.mode != kStore) __threadfence_system();
+  if (!ok) record_device_error(&g_proj_error, kErrProjWaitTimeout);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp) tc::tmem_dealloc(tmem, 2 * kBN);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// bf16 [rows, K] row-major, boxes of 64 (K) x box_rows, 128-byte swizzle (the MMA operand layout)
+bool encode_operand(CUtensorMap* map, const void* base, int64_t rows, int K, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+  const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int sm_count() {
@@ -447,10 +639,20 @@ int sm_count() {
 }
 
 cudaError_t launch(const ProjArgs& a, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(tp_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmem));
-  if (e != cudaSuccess) return e;
   const int64_t tiles = ((a.M + kBM - 1) / kBM) * (a.N / kBN);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
+  CUtensorMap mapA, mapB;
+  if (a.mode != kMulticastAdd && encode_operand(&mapA, a.Y, a.M, a.K, kBM) &&
+      encode_operand(&mapB, a.W, a.N, a.K, kBN)) {
+    cudaError_t e =
+        cudaFuncSetAttribute(tp_proj_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmemT));
+    if (e != cudaSuccess) return e;
+    tp_proj_tma_kernel<<<unsigned(grid), kThrT, kProjSmemT, stream>>>(a, mapA, mapB);
+    return cudaGetLastError();
+  }
+  // the one-shot multicast form (staged epilogue), or no tensor-map encoder: the cp.async kernel
+  cudaError_t e = cudaFuncSetAttribute(tp_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmem));
+  if (e != cudaSuccess) return e;
   tp_proj_kernel<<<unsigned(grid), kThrAll, kProjSmem, stream>>>(a);
   return cudaGetLastError();
 }
