@@ -447,8 +447,8 @@ __global__ void __launch_bounds__(kThrAll, 1) tp_proj_kernel(ProjArgs a) {
 // Same tiles and outputs (modes kStore, kReduceOwned, kReduceOwnedPeer), warp-specialised: warp 4
 // issues the TMA loads of a 4-stage ring (one thread, two tensor-map copies per k-block), warp 5
 // issues the MMAs into one of two 256-column TMEM accumulators, warps 0-3 drain the other
-// accumulator (so a tile's epilogue overlaps the next tile's products) and then join the
-// reduction, warps 6-7 reduce owned tiles from the start.
+// accumulator (so a tile's epilogue overlaps the next tile's products), warps 6-7 reduce owned
+// tiles from the start, and every other warp joins the reduction once its role has no work left.
 constexpr int kEpiWarps = 4, kProdWarp = 4, kMmaWarp = 5, kRedWarp0 = 6, kRedWarps = 2;
 constexpr int kThrT = 32 * (kRedWarp0 + kRedWarps);
 constexpr int kStagesT = 4;
@@ -594,7 +594,7 @@ __global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const
       }
     }
   }
-  if (warp < kEpiWarps || warp >= kRedWarp0) reduce_owned(a, claim, tiles, tiles_n, lane, ok);
+  reduce_owned(a, claim, tiles, tiles_n, lane, ok);  // every warp, once its own role has no work left
   if (a.mode != kStore) __threadfence_system();
   if (!ok) record_device_error(&g_proj_error, kErrProjWaitTimeout);
   tc::fence_before_sync();
