@@ -203,6 +203,23 @@ int kdn_tp_out_proj_allreduce_peer(const void* y, const void* w, void* const* ou
                                    int64_t M, int32_t N, int32_t K, void* stream);
 
 /*
+ * Varlen form of kdn_chunked_prefill (tensor-core arithmetic, KDN_MODE_BF16; D = 512, dv = 64,
+ * chunk 64): N independent scans of different lengths in one launch, one CTA per scan.  Scan n
+ * reads rows [scan_offsets[n], scan_offsets[n] + scan_lengths[n]) of q, k [total_rows, 64],
+ * v [total_rows, dv], beta / decay [total_rows] and writes the same rows of y; its state is row n
+ * of initial_state / final_state [N, dv, D] (fp32).  scan_offsets / scan_lengths: int64 arrays on
+ * the device; a scan whose rows fall outside [0, total_rows) is not run (its state is copied
+ * through) and kdn_device_error reports it.  Give the longest scans the lowest indices: CTAs start
+ * in index order.  The serving batch of the reference (serving/vllm_ragged_batching.py:41-103)
+ * runs its requests one after another instead.
+ */
+int kdn_chunked_prefill_varlen(const void* q, const void* k, const void* v, int in_dtype, const void* beta,
+                               const void* decay, int gate_dtype, const float* initial_state, void* y, int y_dtype,
+                               float* final_state, const int64_t* scan_offsets, const int64_t* scan_lengths,
+                               int64_t N, int64_t total_rows, int32_t dv, int32_t chunk, const kdn_projection* proj,
+                               void* stream);
+
+/*
  * Backward of kdn_chunked_prefill (the reference differentiates its prefill by recompute +
  * autograd, kernels/fused_kernel_deltanet.py:158-179; this is that gradient, computed directly).
  * Given the forward's inputs and dy = dL/dY [N, T, dv] (dy_dtype), optionally dL/d(final

@@ -195,6 +195,52 @@ int kdn_chunked_prefill(const void* q, const void* k, const void* v, int in_dtyp
   return ok();
 }
 
+int kdn_chunked_prefill_varlen(const void* q, const void* k, const void* v, int in_dtype, const void* beta,
+                               const void* decay, int gate_dtype, const float* initial_state, void* y, int y_dtype,
+                               float* final_state, const int64_t* scan_offsets, const int64_t* scan_lengths,
+                               int64_t N, int64_t total_rows, int32_t dv, int32_t chunk, const kdn_projection* proj,
+                               void* stream) {
+  if (int rc = check_projection(proj)) return rc;
+  if (N < 1 || N > (int64_t(1) << 31) - 1) return fail(KDN_ERR_INVALID, "N=%lld", (long long)N);
+  if (total_rows < 0) return fail(KDN_ERR_INVALID, "total_rows=%lld", (long long)total_rows);
+  if (!valid_dtype(in_dtype) || !valid_dtype(gate_dtype) || !valid_dtype(y_dtype))
+    return fail(KDN_ERR_INVALID, "bad dtype");
+  if (!use_tc_path(proj, dv, chunk, KDN_MODE_BF16))
+    return fail(KDN_ERR_UNSUPPORTED, "the varlen prefill runs the tensor-core path only (D=512, dv=64, chunk=64)");
+  if (!q || !k || !v || !beta || !y || !final_state || !scan_offsets || !scan_lengths)
+    return fail(KDN_ERR_INVALID, "q/k/v/beta/y/final_state/scan_offsets/scan_lengths is NULL");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(y, 16) || !aligned(scan_offsets, 8) ||
+      !aligned(scan_lengths, 8))
+    return fail(KDN_ERR_INVALID, "q/k/v/y must be 16-byte aligned, the scan arrays 8-byte aligned");
+  kdn::PrefillProblem p;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.in_dtype = in_dtype;
+  p.beta = beta;
+  p.decay = decay;
+  p.gate_dtype = gate_dtype;
+  p.S0 = initial_state;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  p.S_out = final_state;
+  p.N = N;
+  p.T = 0;
+  p.dv = dv;
+  p.C = chunk;
+  p.D = proj->D;
+  p.var_off = scan_offsets;
+  p.var_len = scan_lengths;
+  p.var_rows = total_rows;
+  const kdn::ProjParams P = kdn::make_proj_params(*proj);
+  kdn::LaunchMarks marks = g_marks;
+  g_marks = kdn::LaunchMarks();
+  cudaError_t e = kdn::launch_tc_prefill(p, P, static_cast<cudaStream_t>(stream), marks);
+  g_last_prefill_launches = marks.launches;
+  if (e != cudaSuccess) return cuda_fail(e, "varlen prefill launch");
+  return ok();
+}
+
 size_t kdn_chunked_prefill_backward_workspace_size(int64_t N, int64_t T, int32_t dv, int32_t chunk,
                                                    const kdn_projection* proj) {
   if (!proj || N < 1 || T < 1 || dv < 16 || (chunk != 32 && chunk != 64)) return 0;

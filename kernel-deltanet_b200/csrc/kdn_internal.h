@@ -40,6 +40,10 @@ struct PrefillProblem {
   bool with_q = false;
   float* S_chunks = nullptr;
   float* E_rows = nullptr;
+  // Varlen batch (fused tensor-core path only): see TcArgs::var_off
+  const int64_t* var_off = nullptr;
+  const int64_t* var_len = nullptr;
+  int64_t var_rows = 0;
 };
 
 // Per-launch event marks of one prefill call (measurement hook behind

@@ -67,7 +67,8 @@ constexpr uint32_t OFF_SC = 226560;    // 512 B  token scales s = amp / (amp ||u
 constexpr uint32_t OFF_BAR = 227072;   // 6 mbarriers + TMEM address
 constexpr uint32_t kSmemBytes = 227128 + 1024;  // + alignment slack
 
-__global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParams P) {
+template <bool kVar>
+__global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a_in, ProjParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm;
   {
@@ -97,7 +98,28 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 48);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t n = blockIdx.x;
+  const int64_t ns = blockIdx.x;  // scan index: rows of the initial / final state
+  TcArgs a = a_in;
+  int64_t n = ns;                 // token-block index of the scan's inputs and outputs
+  if (kVar) {                     // varlen batch: rebase the token-side pointers on this scan's rows
+    const int64_t base = a_in.var_off[ns], len = a_in.var_len[ns];
+    n = 0;
+    if (base < 0 || len < 0 || base > a_in.var_rows - len) {  // malformed: no token access, state passes
+      a.T = 0;
+      if (tid == 0) record_device_error(&g_tc_error, kErrSlotOutOfRange);
+    } else {
+      const int64_t in_es = a.in_dtype == KDN_DTYPE_BF16 ? 2 : 4, g_es = a.gate_dtype == KDN_DTYPE_BF16 ? 2 : 4;
+      const int64_t y_es = a.y_dtype == KDN_DTYPE_BF16 ? 2 : 4;
+      a.T = len;
+      a.q = static_cast<const char*>(a.q) + base * 64 * in_es;
+      a.k = static_cast<const char*>(a.k) + base * 64 * in_es;
+      a.v = static_cast<const char*>(a.v) + base * kDV * in_es;
+      a.beta = static_cast<const char*>(a.beta) + base * g_es;
+      if (a.decay) a.decay = static_cast<const char*>(a.decay) + base * g_es;
+      a.y = static_cast<char*>(a.y) + base * kDV * y_es;
+    }
+    a.NC = int((a.T + kC - 1) / kC);
+  }
   const int quarter = warp & 3, cq = (warp >> 2) & 3;  // TMEM lane quarter, column quarter
   const int trow = quarter * 32 + lane;                // TMEM lane owned by this thread
   const uint32_t lane_off = uint32_t(quarter * 32) << 16;
@@ -136,7 +158,7 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
       float v[16];
       const int f = 128 * s + trow;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = a.S0 ? a.S0[(n * kDV + 16 * cq + j) * kD + f] : 0.f;
+      for (int j = 0; j < 16; ++j) v[j] = a.S0 ? a.S0[(ns * kDV + 16 * cq + j) * kD + f] : 0.f;
       tc::tmem_st16(tmem + lane_off + COL_S + 64 * s + 16 * cq, v);
     }
     tc::tmem_st_wait();
@@ -550,7 +572,7 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a, ProjParam
       tc::tmem_ld_wait();
       const int f = 128 * s + trow;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) a.S_out[(n * kDV + 16 * cq + j) * kD + f] = v[j];
+      for (int j = 0; j < 16; ++j) a.S_out[(ns * kDV + 16 * cq + j) * kD + f] = v[j];
     }
     tc::cp_async_wait_all();
   }
@@ -605,10 +627,14 @@ cudaError_t launch_tc_prefill(const PrefillProblem& p, const ProjParams& P, cuda
   a.S_out = p.S_out;
   a.T = p.T;
   a.NC = int((p.T + kC - 1) / kC);
-  cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+  a.var_off = p.var_off;
+  a.var_len = p.var_len;
+  a.var_rows = p.var_rows;
+  auto kern = a.var_off ? prefill_tc_kernel<true> : prefill_tc_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
   if (e != cudaSuccess) return e;
   marks.begin(stream);
-  prefill_tc_kernel<<<unsigned(p.N), kThr, kSmemBytes, stream>>>(a, P);
+  kern<<<unsigned(p.N), kThr, kSmemBytes, stream>>>(a, P);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   marks.after(stream);
   return cudaSuccess;

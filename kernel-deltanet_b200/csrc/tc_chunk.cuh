@@ -33,6 +33,11 @@ struct TcArgs {
   float* S_out;
   int64_t T;
   int NC;
+  // varlen batches (fused path): scan n reads token rows [var_off[n], var_off[n] + var_len[n]) of
+  // q, k, v, y, beta, decay (rows counted in tokens); null = the uniform [N, T] layout
+  const int64_t* var_off = nullptr;
+  const int64_t* var_len = nullptr;
+  int64_t var_rows = 0;  // rows in the varlen tensors (bounds of var_off + var_len)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {

@@ -58,6 +58,8 @@ SIGNATURES = {
                                    ctypes.POINTER(KdnProjection), _INT, _P, ctypes.c_size_t, _P]),
     "kdn_chunked_prefill_static": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _P, _INT, _P, _I64, _I64, _I32, _I32,
                                           ctypes.POINTER(KdnProjection), _P]),
+    "kdn_chunked_prefill_varlen": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _P, _INT, _P, _P, _P, _I64, _I64, _I32,
+                                          _I32, ctypes.POINTER(KdnProjection), _P]),
     "kdn_chunked_prefill_backward_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I32, _I32,
                                                                        ctypes.POINTER(KdnProjection)]),
     "kdn_chunked_prefill_backward": (_INT, [_P, _P, _P, _INT, _P, _P, _INT, _P, _P, _INT, _P, _P, _P, _P, _P, _P, _P,

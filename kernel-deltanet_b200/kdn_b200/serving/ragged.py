@@ -19,10 +19,12 @@ keeps one recurrent state per stream.  Here:
 * ``output`` is written in place; everything runs on the current CUDA stream.
 
 The packed tensors are moved to per-sequence head-major blocks ([H, T_i, .], no padding)
-by ``kdn_ragged_transpose``; each sequence then runs the exact chunked prefill of
-``fused_chunked_deltanet_forward`` (so the arithmetic, paths and tolerances are those of
-that op), several sequences in one call when they are adjacent, of equal length, and
-map to consecutive slots.  ``fork_recurrent_state`` copies a slot for a forked request.
+by ``kdn_ragged_transpose``.  In bf16 mode a batch with at least as many (sequence, head)
+scans as SMs then runs as ONE varlen launch (``kdn_chunked_prefill_varlen``: one CTA per
+scan on the tensor-core path, longest first).  Otherwise each sequence runs the exact chunked
+prefill of ``fused_chunked_deltanet_forward`` (so the arithmetic, paths and tolerances are those
+of that op), several sequences in one call when they are adjacent, of equal length, and map to
+consecutive slots.  ``fork_recurrent_state`` copies a slot for a forked request.
 """
 
 from __future__ import annotations
@@ -53,6 +55,47 @@ def _to_head_major(lib, src: torch.Tensor, cu_dev: torch.Tensor, num_seqs: int, 
                                   total, H, row_bytes, 1, _lib.stream_handle(dev))
     _lib.check(rc, "kdn_ragged_transpose")
     return dst
+
+
+def _varlen_prefill(lib, qh, kh, vh, bh, dh, yh, lens, starts, sl, mask, pool, proj, H, dv, total, dev) -> bool:
+    """All (sequence, head) scans of the batch in one launch (kdn_chunked_prefill_varlen: one CTA per
+    scan on the tensor-core path), longest scans first; states gathered from and scattered back to the
+    pool.  Used when the batch has more than one non-empty sequence and at least as many scans as SMs
+    (fewer scans run better through the per-sequence path, which spreads a sequence over the GPU).
+    Returns False when it does not apply."""
+    live = [i for i, n in enumerate(lens) if n > 0]
+    if len(live) < 2 or len(live) * H < torch.cuda.get_device_properties(dev).multi_processor_count:
+        return False
+    order = sorted(live, key=lambda i: -lens[i])
+    offs = [starts[i] * H + h * lens[i] for i in order for h in range(H)]
+    lns = [lens[i] for i in order for h in range(H)]
+    rows = [sl[i] * H + h for i in order for h in range(H)]
+    N = len(offs)
+    view = pool.view(pool.shape[0] * H, dv, -1)
+    rows_dev = torch.tensor(rows, device=dev, dtype=torch.int64)
+    fresh = [mask is not None and not bool(mask[i]) for i in order]
+    S0 = None
+    if not all(fresh):
+        S0 = view.index_select(0, rows_dev)
+        if any(fresh):
+            keep = torch.tensor([0.0 if f else 1.0 for f in fresh for _ in range(H)], device=dev)
+            S0.mul_(keep[:, None, None])
+    S_out = torch.empty(N, dv, view.shape[-1], device=dev, dtype=torch.float32)
+    offs_dev = torch.tensor(offs, device=dev, dtype=torch.int64)
+    lns_dev = torch.tensor(lns, device=dev, dtype=torch.int64)
+    p, _phase = proj.kdn_projection(dev)
+    rc = lib.kdn_chunked_prefill_varlen(
+        qh.data_ptr(), kh.data_ptr(), vh.data_ptr(), _lib.dtype_code(qh), bh.data_ptr(), _lib.ptr(dh),
+        _lib.dtype_code(bh), _lib.ptr(S0), yh.data_ptr(), _lib.dtype_code(yh), S_out.data_ptr(), offs_dev.data_ptr(),
+        lns_dev.data_ptr(), N, total * H, dv, 64, p, _lib.stream_handle(dev))
+    if rc == 2:  # KDN_ERR_UNSUPPORTED (e.g. a projection whose constants the tensor-core lift cannot hold)
+        return False
+    _lib.check(rc, "kdn_chunked_prefill_varlen")
+    view.index_copy_(0, rows_dev, S_out)
+    for i, n in enumerate(lens):  # empty sequences: a fresh one leaves a zero state
+        if n == 0 and mask is not None and not bool(mask[i]):
+            pool[sl[i]].zero_()
+    return True
 
 
 def ragged_prefill(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, beta: torch.Tensor,
@@ -115,11 +158,16 @@ def ragged_prefill(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, 
     yh = torch.empty(total * H * dv, device=dev, dtype=output.dtype if output.dtype in (torch.float32, torch.bfloat16)
                      else in_dtype)
 
-    # ---------------------------------------------------------------- one prefill per run of sequences
     lens = (cu[1:] - cu[:-1]).tolist()
     starts = cu[:-1].tolist()
     sl = slots.tolist()
-    i = 0
+    run_mode = mode or ("bf16" if in_dtype == torch.bfloat16 else "fp32")
+    batched = (run_mode == "bf16" and d_k == 64 and dv == 64 and proj.D == 512 and chunk_size == 64
+               and _varlen_prefill(lib, qh, kh, vh, bh, dh, yh, lens, starts, sl, mask, recurrent_states, proj, H,
+                                   dv, total, dev))
+
+    # ---------------------------------------------------------------- one prefill per run of sequences
+    i = num_seqs if batched else 0
     while i < num_seqs:
         j = i + 1  # extend the run: equal length, next slot, same start rule
         while (j < num_seqs and lens[j] == lens[i] and sl[j] == sl[j - 1] + 1

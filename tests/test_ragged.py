@@ -84,3 +84,77 @@ def test_ragged_prefill_matches_oracle_per_sequence(mode):
         y_ref, S_ref = oracle.chunked_deltanet_forward(tr(q), tr(k), tr(v), tr(beta), tr(decay), consts, 64, S0)
         assert rel_err(np.swapaxes(y[a:b], 0, 1), y_ref) < tol_y, i
         assert fro_rel(S[s], S_ref) < tol_s, i
+
+
+@pytest.mark.gpu
+def test_varlen_batch_one_launch_matches_oracle():
+    """Enough (sequence, head) scans to take the one-launch varlen path (80 sequences x 2 heads >=
+    SMs): lengths 0 to 300 including 1 and chunk multiples, fresh and carried states, arbitrary slots."""
+    import kdn_b200
+    from kdn_b200 import _lib
+
+    dev = "cuda:0"
+    rng = np.random.default_rng(21)
+    nseq = 80
+    lens = [int(x) for x in rng.integers(0, 300, nseq)]
+    lens[:6] = [0, 1, 64, 128, 299, 0]
+    slots = [int(s) for s in rng.permutation(96)[:nseq]]
+    fresh = [bool(x) for x in rng.integers(0, 2, nseq)]
+    q, k, v, beta, decay, pool, cu = _batch(9, lens, num_slots=96)
+    q, k, v = (torch.from_numpy(a).bfloat16().double().numpy() for a in (q, k, v))
+    d = lambda a, t=torch.float32: torch.from_numpy(np.ascontiguousarray(a)).to(dev, t)
+    states = d(pool)
+    out = torch.empty(sum(lens), 2, 64, device=dev, dtype=torch.bfloat16)
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    kdn_b200.load().kdn_prefill_launch_count()
+    kdn_b200.ragged_prefill(d(q, torch.bfloat16), d(k, torch.bfloat16), d(v, torch.bfloat16), d(beta), d(decay),
+                            torch.tensor(cu, device=dev), states, torch.tensor(slots, device=dev), out, proj,
+                            mode="bf16", initial_state_mask=torch.tensor([not f for f in fresh]))
+    torch.cuda.synchronize()
+    assert kdn_b200.load().kdn_prefill_launch_count() == 1  # the last prefill call was the single varlen launch
+    consts = oracle.make_projection_constants()
+    y = out.float().cpu().numpy()
+    S = states.cpu().numpy()
+    for i, (T, s, f) in enumerate(zip(lens, slots, fresh)):
+        a, b = cu[i], cu[i + 1]
+        S0 = np.zeros((2, 64, 512)) if f else pool[s]
+        if T == 0:
+            assert fro_rel(S[s], S0) < 1e-7
+            continue
+        tr = lambda x: np.ascontiguousarray(np.swapaxes(x[a:b], 0, 1))
+        y_ref, S_ref = oracle.chunked_deltanet_forward(tr(q), tr(k), tr(v), tr(beta), tr(decay), consts, 64, S0)
+        assert rel_err(np.swapaxes(y[a:b], 0, 1), y_ref) < 2e-2, i
+        assert fro_rel(S[s], S_ref) < 1e-2, i
+    untouched = sorted(set(range(96)) - set(slots))
+    assert np.array_equal(S[untouched], pool[untouched].astype(np.float32))
+
+
+@pytest.mark.gpu
+def test_varlen_rejects_rows_outside_the_batch():
+    """A scan whose rows fall outside the tensors is not run: its state passes through and the
+    device error word reports it (bounds checked in the kernel; nothing is read out of range)."""
+    import kdn_b200
+    from kdn_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    lib = kdn_b200.load()
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    p, _ = proj.kdn_projection(dev)
+    rows = 256
+    q = torch.nn.functional.normalize(torch.randn(rows, 64, device=dev), dim=-1).bfloat16()
+    v = torch.randn(rows, 64, device=dev).bfloat16()
+    beta = torch.full((rows,), 0.5, device=dev)
+    y = torch.zeros(rows, 64, device=dev, dtype=torch.bfloat16)
+    S0 = torch.randn(2, 64, 512, device=dev)
+    S = torch.empty_like(S0)
+    offs = torch.tensor([0, 200], device=dev)
+    lens = torch.tensor([128, 100], device=dev)  # scan 1 would read rows 200..299 of 256
+    rc = lib.kdn_chunked_prefill_varlen(q.data_ptr(), q.data_ptr(), v.data_ptr(), _lib.KDN_DTYPE_BF16,
+                                        beta.data_ptr(), None, _lib.KDN_DTYPE_F32, S0.data_ptr(), y.data_ptr(),
+                                        _lib.KDN_DTYPE_BF16, S.data_ptr(), offs.data_ptr(), lens.data_ptr(), 2, rows,
+                                        64, 64, p, _lib.stream_handle(dev))
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert torch.equal(S[1], S0[1])
+    assert float(y[200:].float().abs().max()) == 0.0
+    assert kdn_b200.serving.vllm_kernel_deltanet_op.device_error(dev) != 0
