@@ -323,13 +323,15 @@ def bench_tp_out_proj(dev, rank, world, steps=10, warmup=3):
 
     res = {m: timed(lambda m=m: kd.row_parallel_out_proj(y, w, method=m)) for m in ("two-phase", "peer", "one-shot")}
     res["peer_bf16"] = timed(lambda: kd.row_parallel_out_proj(y, w, method="peer", out_dtype=torch.bfloat16))
+    res["two-phase_bf16"] = timed(lambda: kd.row_parallel_out_proj(y, w, method="two-phase",
+                                                                   out_dtype=torch.bfloat16))
     _, auto_path = kd.row_parallel_out_proj(y, w)
     res["unfused_nccl_fp32"] = timed(unfused)
     res["reference_torch_bf16_nccl"] = timed(reference_form)
     err = {}
-    for m in ("two-phase", "peer", "peer_bf16"):
-        fused, _ = kd.row_parallel_out_proj(y, w, method=m[:4] if m == "peer_bf16" else m,
-                                            out_dtype=torch.bfloat16 if m == "peer_bf16" else torch.float32)
+    for m in ("two-phase", "peer", "peer_bf16", "two-phase_bf16"):
+        fused, _ = kd.row_parallel_out_proj(y, w, method=m.replace("_bf16", ""),
+                                            out_dtype=torch.bfloat16 if m.endswith("_bf16") else torch.float32)
         fused = fused.float()
         unfused()
         torch.cuda.synchronize()

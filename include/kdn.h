@@ -173,8 +173,9 @@ int kdn_tp_out_proj(const void* y, const void* w, void* out, int out_dtype, floa
 
 /*
  * The two-phase (bandwidth-optimal) form of kdn_tp_out_proj for the same sum over ranks.
- * Every rank stores its tiles of y w^T into its own copy `out` of the symmetric [M, N] fp32
- * buffer and announces each tile by adding 1 to every rank's copy of that tile's counter
+ * Every rank stores its tiles of y w^T into its own copy `out` of the symmetric [M, N] buffer
+ * (out_dtype KDN_DTYPE_F32, or KDN_DTYPE_BF16: the switch sums the bf16 copies in fp32 and the
+ * sum is rounded once) and announces each tile by adding 1 to every rank's copy of that tile's counter
  * (tile_counters: a symmetric uint32 buffer of kdn_tp_out_proj_tiles(M, N) entries; its
  * multicast address alongside).  The owner of tile t (t % world == rank) waits until its copy
  * of counter t reaches `target`, then writes the sum of all copies of the tile into every copy
@@ -183,9 +184,9 @@ int kdn_tp_out_proj(const void* y, const void* w, void* out, int out_dtype, floa
  * follow before the sum is read or `out` is written again.  No reference entry point.
  */
 int64_t kdn_tp_out_proj_tiles(int64_t M, int32_t N);
-int kdn_tp_out_proj_allreduce(const void* y, const void* w, float* out, float* out_multicast, uint32_t* tile_counters,
-                              uint32_t* tile_counters_multicast, uint32_t target, int32_t rank, int32_t world,
-                              int64_t M, int32_t N, int32_t K, void* stream);
+int kdn_tp_out_proj_allreduce(const void* y, const void* w, void* out, void* out_multicast, int out_dtype,
+                              uint32_t* tile_counters, uint32_t* tile_counters_multicast, uint32_t target, int32_t rank,
+                              int32_t world, int64_t M, int32_t N, int32_t K, void* stream);
 
 /*
  * The same two-phase projection over peer pointers instead of a multicast address (for

@@ -374,9 +374,9 @@ int64_t kdn_tp_out_proj_tiles(int64_t M, int32_t N) {
   return kdn::tp_proj_tiles(M, N);
 }
 
-int kdn_tp_out_proj_allreduce(const void* y, const void* w, float* out, float* out_multicast, uint32_t* tile_counters,
-                              uint32_t* tile_counters_multicast, uint32_t target, int32_t rank, int32_t world,
-                              int64_t M, int32_t N, int32_t K, void* stream) {
+int kdn_tp_out_proj_allreduce(const void* y, const void* w, void* out, void* out_multicast, int out_dtype,
+                              uint32_t* tile_counters, uint32_t* tile_counters_multicast, uint32_t target, int32_t rank,
+                              int32_t world, int64_t M, int32_t N, int32_t K, void* stream) {
   if (M < 0 || M > (int64_t(65535) * 128)) return fail(KDN_ERR_INVALID, "M=%lld outside [0, 65535*128]", (long long)M);
   if (world < 1 || rank < 0 || rank >= world) return fail(KDN_ERR_INVALID, "rank=%d world=%d", rank, world);
   if (M == 0) return ok();
@@ -387,8 +387,10 @@ int kdn_tp_out_proj_allreduce(const void* y, const void* w, float* out, float* o
   if (!aligned(y, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(out_multicast, 16) ||
       !aligned(tile_counters, 4) || !aligned(tile_counters_multicast, 4))
     return fail(KDN_ERR_INVALID, "y/w/out must be 16-byte aligned, the counters 4-byte aligned");
-  cudaError_t e = kdn::launch_tp_proj_reduce(y, w, out, out_multicast, tile_counters, tile_counters_multicast, target,
-                                             rank, world, M, N, K, static_cast<cudaStream_t>(stream));
+  if (out_dtype != KDN_DTYPE_F32 && out_dtype != KDN_DTYPE_BF16) return fail(KDN_ERR_INVALID, "bad output dtype");
+  cudaError_t e = kdn::launch_tp_proj_reduce(y, w, out, out_multicast, out_dtype == KDN_DTYPE_BF16, tile_counters,
+                                             tile_counters_multicast, target, rank, world, M, N, K,
+                                             static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "tensor-parallel projection launch");
   return ok();
 }

@@ -122,9 +122,9 @@ cudaError_t launch_tp_proj(const void* Y, const void* W, void* out, bool out_bf1
                            int K, cudaStream_t stream);
 // two-phase form: tiles stored into `out` (this rank's copy) and announced on the tile counters;
 // the owner (tile % world == rank) reduces each tile once every counter reaches `target`.
-cudaError_t launch_tp_proj_reduce(const void* Y, const void* W, float* out, float* out_mc, uint32_t* flags,
-                                  uint32_t* flags_mc, uint32_t target, int rank, int world, int64_t M, int N, int K,
-                                  cudaStream_t stream);
+cudaError_t launch_tp_proj_reduce(const void* Y, const void* W, void* out, void* out_mc, bool out_bf16,
+                                  uint32_t* flags, uint32_t* flags_mc, uint32_t target, int rank, int world, int64_t M,
+                                  int N, int K, cudaStream_t stream);
 // peer form: every rank's copies of the output and the counters by their peer pointers (world <= 8)
 cudaError_t launch_tp_proj_reduce_peer(const void* Y, const void* W, void* const* outs, bool out_bf16,
                                        uint32_t* const* flags, uint32_t target, int rank, int world, int64_t M, int N,

@@ -12,8 +12,8 @@
 //   kMulticastAdd (one-shot) `multimem.red.add` through the NVSwitch multicast address of a
 //                symmetric buffer adds the tile into every rank's copy.  One pass, no waits, but
 //                every GPU receives world x the output bytes: the form for small M.
-//   kReduceOwned (two-phase, the bandwidth-optimal form) the tile is stored into this rank's
-//                copy of the symmetric buffer and announced by a release `multimem.red` on a
+//   kReduceOwned (two-phase, the bandwidth-optimal form; fp32 or bf16 copies) the tile is stored
+//                into this rank's copy of the symmetric buffer and announced by a release `multimem.red` on a
 //                per-tile counter (every rank's copy of the counter goes up by one).  The tiles
 //                this rank owns (t % world == rank) are reduced, while the tile warps go on
 //                computing, by four reducer warps per CTA: each waits until every rank has
@@ -121,6 +121,20 @@ __device__ __forceinline__ void st_v4_all(float* addr, float4 v) {
                "f"(v.z), "f"(v.w)
                : "memory");
 }
+// bf16 copies: eight values per 16 bytes, summed by the switch in fp32 and rounded once
+__device__ __forceinline__ uint4 ld_reduce_bf16x8(const void* addr) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_bf16x8_all(void* addr, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ void announce(uint32_t* flag_mc) {
   asm volatile("multimem.red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag_mc) : "memory");
 }
@@ -173,7 +187,23 @@ __device__ __forceinline__ void reduce_owned(const ProjArgs& a, unsigned int* cl
       }
       const int n0 = int(t % tiles_n) * kBN;
       const int64_t m0 = (t / tiles_n) * kBM + 32 * (u & 3);
-      if (a.mode == kReduceOwned) {
+      if (a.mode == kReduceOwned && a.out_bf16) {  // bf16 copies: a lane takes 8 columns (16 B) of a row
+        __nv_bfloat16* mc = reinterpret_cast<__nv_bfloat16*>(a.out_mc);
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {
+          uint4 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = m0 + r0 + i;
+            if (row < a.M) v[i] = ld_reduce_bf16x8(mc + row * a.N + n0 + 8 * lane);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t row = m0 + r0 + i;
+            if (row < a.M) st_bf16x8_all(mc + row * a.N + n0 + 8 * lane, v[i]);
+          }
+        }
+      } else if (a.mode == kReduceOwned) {
 #pragma unroll 1
         for (int r0 = 0; r0 < 32; r0 += 8) {  // 8 rows x 2 vectors per lane in flight
           float4 v[8][2];
@@ -677,14 +707,15 @@ cudaError_t launch_tp_proj(const void* Y, const void* W, void* out, bool out_bf1
   return launch(a, stream);
 }
 
-cudaError_t launch_tp_proj_reduce(const void* Y, const void* W, float* out, float* out_mc, uint32_t* flags,
-                                  uint32_t* flags_mc, uint32_t target, int rank, int world, int64_t M, int N, int K,
-                                  cudaStream_t stream) {
+cudaError_t launch_tp_proj_reduce(const void* Y, const void* W, void* out, void* out_mc, bool out_bf16,
+                                  uint32_t* flags, uint32_t* flags_mc, uint32_t target, int rank, int world, int64_t M,
+                                  int N, int K, cudaStream_t stream) {
   ProjArgs a{};
   a.Y = static_cast<const __nv_bfloat16*>(Y);
   a.W = static_cast<const __nv_bfloat16*>(W);
-  a.out = out;
-  a.out_mc = out_mc;
+  a.out = static_cast<float*>(out);
+  a.out_mc = static_cast<float*>(out_mc);
+  a.out_bf16 = out_bf16 ? 1 : 0;
   a.flags = flags;
   a.flags_mc = flags_mc;
   a.M = M;

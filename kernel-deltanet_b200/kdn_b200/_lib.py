@@ -69,7 +69,7 @@ SIGNATURES = {
     "kdn_prefill_launch_count": (_INT, []),
     "kdn_tp_out_proj": (_INT, [_P, _P, _P, _INT, _P, _I64, _I32, _I32, _P]),
     "kdn_tp_out_proj_tiles": (_I64, [_I64, _I32]),
-    "kdn_tp_out_proj_allreduce": (_INT, [_P, _P, _P, _P, _P, _P, _U32, _I32, _I32, _I64, _I32, _I32, _P]),
+    "kdn_tp_out_proj_allreduce": (_INT, [_P, _P, _P, _P, _INT, _P, _P, _U32, _I32, _I32, _I64, _I32, _I32, _P]),
     "kdn_tp_out_proj_allreduce_peer": (_INT, [_P, _P, ctypes.POINTER(_P), _INT, ctypes.POINTER(_P), _U32, _I32, _I32,
                                               _I64, _I32, _I32, _P]),
     "kdn_ragged_transpose": (_INT, [_P, _P, _P, _INT, _I64, _I64, _I32, _I64, _INT, _P]),

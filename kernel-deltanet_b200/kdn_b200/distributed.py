@@ -177,18 +177,19 @@ def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=No
     product (path "local").  Otherwise one kernel computes the tiles on the tensor cores and
     reduces them across the ranks (path "fused-<method>"):
       * "two-phase": every rank stores its tiles locally and announces them; the owner of each
-        tile sums all copies in the NVSwitch (multimem.ld_reduce) and writes the sum to every
-        copy (multimem.st): (1 + 1/world) x the output bytes cross each GPU's links;
+        tile sums all copies in the NVSwitch (multimem.ld_reduce, fp32 accumulation for bf16
+        copies too) and writes the sum to every copy (multimem.st): (1 + 1/world) x the output
+        bytes cross each GPU's links;
       * "peer": the same owner scheme over peer pointers (loads from every copy, stores into
         every copy): 2 (world - 1) / world x the output bytes, fewer than two-phase at world 2,
         and no multicast needed;
       * "one-shot": each tile is added into every copy through the multicast address as it is
         produced (one pass, world x the output bytes into each GPU);
-      * "auto": one-shot up to ONE_SHOT_MAX_BYTES of output, else peer at world 2 (or without
-        multicast), else two-phase.
+      * "auto": peer at world 2 (or without multicast), else two-phase -- and for fp32 outputs up
+        to ONE_SHOT_MAX_BYTES, one-shot.
     The sum is formed in fp32 and is identical on every rank.  out_dtype torch.bfloat16 (the
-    reference's layer dtype; "local" and "peer" only, "auto" then picks "peer"): every rank's
-    product is rounded to bf16 once and the sum once, and half the bytes move.  Only when `allow_unfused` and the group
+    reference's layer dtype; every method but one-shot): every rank's product is rounded to bf16
+    once and the sum once, and half the bytes move.  Only when `allow_unfused` and the group
     cannot map symmetric memory: the kernel's product and then an NCCL all-reduce (path
     "unfused-nccl", the reference's two-step form).  The tensor returned by a fused path is a
     cached symmetric buffer, overwritten by the next call with the same shape.
@@ -201,8 +202,8 @@ def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=No
         raise ValueError(f"method must be 'auto', 'one-shot', 'two-phase' or 'peer', got {method!r}")
     if out_dtype not in (torch.float32, torch.bfloat16):
         raise ValueError(f"out_dtype must be torch.float32 or torch.bfloat16, got {out_dtype}")
-    if out_dtype == torch.bfloat16 and method in ("one-shot", "two-phase"):
-        raise ValueError(f"method {method!r} sums in the fp32 output; bf16 output takes 'peer' (or 'auto')")
+    if out_dtype == torch.bfloat16 and method == "one-shot":
+        raise ValueError("the one-shot method adds into the fp32 output; bf16 output takes 'two-phase' or 'peer'")
     if y_local.dim() != 2 or w_local.dim() != 2 or y_local.shape[1] != w_local.shape[1]:
         raise RuntimeError(f"expected y [M, K] and w [N, K]; got {tuple(y_local.shape)}, {tuple(w_local.shape)}")
     if not (y_local.is_cuda and w_local.is_cuda):
@@ -238,7 +239,7 @@ def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=No
     has_mc = bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, dev.index)) and bool(so.hdl.multicast_ptr)
     if method == "auto":
         if out_dtype == torch.bfloat16:
-            method = "peer"
+            method = "peer" if (world == 2 or not has_mc) else "two-phase"
         elif has_mc and M * N * 4 <= ONE_SHOT_MAX_BYTES:
             method = "one-shot"
         else:
@@ -255,8 +256,8 @@ def row_parallel_out_proj(y_local: torch.Tensor, w_local: torch.Tensor, group=No
         target = (so.calls * world) & 0xFFFFFFFF
         if method == "two-phase":
             rc = lib.kdn_tp_out_proj_allreduce(y.data_ptr(), w.data_ptr(), so.out.data_ptr(), so.multicast(),
-                                               so.counters.data_ptr(), so.multicast(so.ctr_off), target, rank, world,
-                                               M, N, K, stream)
+                                               _lib.dtype_code(so.out), so.counters.data_ptr(),
+                                               so.multicast(so.ctr_off), target, rank, world, M, N, K, stream)
         else:
             outs = (ctypes.c_void_p * world)(*so.peer_ptrs(0))
             ctrs = (ctypes.c_void_p * world)(*so.peer_ptrs(so.ctr_off))

@@ -171,10 +171,12 @@ def nccl_tp_out_proj(rank, world, port, result_path, M, N, K):
             torch.cuda.synchronize()
             errs.append(float((out - ref).abs().max() / ref.abs().max()))
             paths.append(path)
-        out, path = kd.row_parallel_out_proj(y, w, method="auto", out_dtype=torch.bfloat16)
-        torch.cuda.synchronize()
-        err_bf16 = float((out.float() - ref).abs().max() / ref.abs().max())
-        paths.append(path + "-bf16")
+        err_bf16 = 0.0
+        for method in ("two-phase", "auto"):  # the switch's fp32 sum of bf16 copies, then peer (auto at world 2)
+            out, path = kd.row_parallel_out_proj(y, w, method=method, out_dtype=torch.bfloat16)
+            torch.cuda.synchronize()
+            err_bf16 = max(err_bf16, float((out.float() - ref).abs().max() / ref.abs().max()))
+            paths.append(path + "-bf16")
         same = torch.tensor([float(out.float().sum())], device=dev, dtype=torch.float64)
         everyone = [torch.zeros_like(same) for _ in range(world)]
         dist.all_gather(everyone, same)  # the owner's sum is copied: every rank holds the same bits

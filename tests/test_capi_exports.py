@@ -186,7 +186,8 @@ def test_tp_out_proj_allreduce_argument_checks(lib):
     P = 4096
     assert lib.kdn_tp_out_proj_tiles(300, 512) == 3 * 2
     assert lib.kdn_tp_out_proj_tiles(300, 500) == 0
-    args = lambda **kw: [kw.get(n, d) for n, d in (("y", P), ("w", P), ("out", P), ("mc", P), ("fl", P), ("flmc", P),
+    args = lambda **kw: [kw.get(n, d) for n, d in (("y", P), ("w", P), ("out", P), ("mc", P), ("dt", 0), ("fl", P),
+                                                   ("flmc", P),
                                                    ("target", 2), ("rank", 0), ("world", 2), ("M", 128), ("N", 256),
                                                    ("K", 64))] + [None]
     assert lib.kdn_tp_out_proj_allreduce(*args(rank=2)) == 1          # rank outside the world
@@ -196,6 +197,7 @@ def test_tp_out_proj_allreduce_argument_checks(lib):
     assert lib.kdn_tp_out_proj_allreduce(*args(fl=None)) == 1         # no counters
     assert lib.kdn_tp_out_proj_allreduce(*args(mc=P + 8)) == 1        # misaligned multicast output
     assert lib.kdn_tp_out_proj_allreduce(*args(flmc=P + 2)) == 1      # misaligned counters
+    assert lib.kdn_tp_out_proj_allreduce(*args(dt=3)) == 1            # bad output dtype
     assert lib.kdn_tp_out_proj_allreduce(*args(M=0)) == 0             # nothing to do
 
 
