@@ -11,7 +11,8 @@
 //
 // In a CTA each lane scores whole keys (its 64-element key row against the query held in
 // registers), the warp keeps an online softmax over its keys, and the value rows are summed with
-// each lane owning two output dimensions.
+// each lane owning two output dimensions; a group's value rows are loaded together with its key rows,
+// so both are in flight at once.
 #include <math.h>
 
 #include "kdn_common.cuh"
@@ -87,6 +88,11 @@ __global__ void __launch_bounds__(32 * kWarps) decode_attn_partial_kernel(const 
   float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
   for (int64_t j0 = k0 + 32 * warp; j0 < k1; j0 += 32 * kWarps) {
     const int64_t j = j0 + lane;
+    const int cnt = int((k1 - j0) < 32 ? (k1 - j0) : 32);
+    float2 vv[32];  // this lane's two columns of the group's value rows, loaded with the key rows
+#pragma unroll
+    for (int r = 0; r < 32; ++r)
+      vv[r] = r < cnt ? load_pair(vb + (j0 + r) * kHd + 2 * lane) : make_float2(0.f, 0.f);
     float sc = -INFINITY;
     if (j < k1) {
       float kf[kHd];
@@ -108,12 +114,11 @@ __global__ void __launch_bounds__(32 * kWarps) decode_attn_partial_kernel(const 
     l = l * corr + ps;
     a0 *= corr;
     a1 *= corr;
-    const int cnt = int((k1 - j0) < 32 ? (k1 - j0) : 32);
-    for (int r = 0; r < cnt; ++r) {
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {  // p is 0 past the group's keys (and vv is 0 there)
       const float pr = __shfl_sync(0xffffffffu, p, r);
-      const float2 vv = load_pair(vb + (j0 + r) * kHd + 2 * lane);
-      a0 = fmaf(pr, vv.x, a0);
-      a1 = fmaf(pr, vv.y, a1);
+      a0 = fmaf(pr, vv[r].x, a0);
+      a1 = fmaf(pr, vv[r].y, a1);
     }
     m = mn;
   }
