@@ -477,12 +477,15 @@ __global__ void __launch_bounds__(kThrAll, 1) tp_proj_kernel(ProjArgs a) {
 // Same tiles and outputs (modes kStore, kReduceOwned, kReduceOwnedPeer), warp-specialised: warp 4
 // issues the TMA loads of a 4-stage ring (one thread, two tensor-map copies per k-block), warp 5
 // issues the MMAs into one of two 256-column TMEM accumulators, warps 0-3 drain the other
-// accumulator (so a tile's epilogue overlaps the next tile's products), warps 6-7 reduce owned
+// accumulator through swizzled shared-memory blocks and TMA stores (so a tile's epilogue overlaps
+// the next tile's products), warps 6-7 reduce owned
 // tiles from the start, and every other warp joins the reduction once its role has no work left.
 constexpr int kEpiWarps = 4, kProdWarp = 4, kMmaWarp = 5, kRedWarp0 = 6, kRedWarps = 2;
 constexpr int kThrT = 32 * (kRedWarp0 + kRedWarps);
 constexpr int kStagesT = 4;
-constexpr uint32_t T_BAR = kStageP * kStagesT;  // full[4], empty[4], acc_full[2], acc_empty[2]
+constexpr uint32_t T_STG = kStageP * kStagesT;  // two 16 KiB output staging buffers (TMA stores)
+constexpr uint32_t kStgBytes = 16384;
+constexpr uint32_t T_BAR = T_STG + 2 * kStgBytes;  // full[4], empty[4], acc_full[2], acc_empty[2]
 constexpr uint32_t T_TSLOT = T_BAR + 8 * (2 * kStagesT + 4);
 constexpr uint32_t T_CLAIM = T_TSLOT + 16;
 constexpr uint32_t kProjSmemT = T_CLAIM + 16 + 1024;
@@ -497,8 +500,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// shared -> global 2-D tensor-map store of a staged block (this CTA's bulk group)
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const __grid_constant__ CUtensorMap mapA,
-                                                               const __grid_constant__ CUtensorMap mapB) {
+                                                               const __grid_constant__ CUtensorMap mapB,
+                                                               const __grid_constant__ CUtensorMap mapO) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = tc::smem_u32(sm);
@@ -575,54 +588,70 @@ __global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const
       }
     }
   } else if (warp < kEpiWarps) {
-    uint32_t tcount = 0;
+    // accumulator -> registers -> a 128-byte-swizzled staging block in shared memory (thread r: row r,
+    // eight 16-byte chunks) -> one TMA store per block of 32 fp32 / 64 bf16 columns x 128 rows
+    uint32_t tcount = 0, sc = 0;
     const int r = 32 * warp + lane;
+    const int cols = a.out_bf16 ? 64 : 32;  // columns per staged block (128 bytes a row)
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++tcount) {
       const uint32_t ab = tcount & 1u;
       ok &= proj_wait(&accf[ab], (tcount >> 1) & 1u);
       tc::fence_after_sync();
       const int n0 = int(t % tiles_n) * kBN;
-      const int64_t row = (t / tiles_n) * kBM + r;
+      const int m0 = int((t / tiles_n) * kBM);
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        float v[32];
-        tc::tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + kBN * ab + c0, v);
-        tc::tmem_ld_wait();
-        if (row < a.M) {
-          const int64_t off = row * a.N + n0 + c0;
-          if (a.out_bf16) {
+      for (int c0 = 0; c0 < kBN; c0 += cols, ++sc) {
+        const uint32_t buf = sbase + T_STG + (sc & 1u) * kStgBytes;
+        if (tid == 0 && sc >= 2) bulk_wait_read_le1();  // the store that last read this buffer is done
+        tc::named_bar_sync(1, 32 * kEpiWarps);
+        uint32_t w[32];  // the row's 128 bytes
+        if (a.out_bf16) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 pk;
-              uint32_t* w32 = reinterpret_cast<uint32_t*>(&pk);
+          for (int h = 0; h < 2; ++h) {
+            float v[32];
+            tc::tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + kBN * ab + c0 + 32 * h, v);
+            tc::tmem_ld_wait();
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
-                w32[e] = *reinterpret_cast<const uint32_t*>(&b2);
-              }
-              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + off + j) = pk;
+            for (int e = 0; e < 16; ++e) {
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+              w[16 * h + e] = *reinterpret_cast<const uint32_t*>(&b2);
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(a.out + off + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
           }
+        } else {
+          float v[32];
+          tc::tmem_ld32(tmem + (uint32_t(32 * warp) << 16) + kBN * ab + c0, v);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(v[e]);
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t dst = buf + uint32_t(r) * 128u + ((uint32_t(c) ^ (uint32_t(r) & 7u)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[4 * c]), "r"(w[4 * c + 1]),
+                       "r"(w[4 * c + 2]), "r"(w[4 * c + 3])
+                       : "memory");
+        }
+        tc::fence_proxy_async_smem();  // the block is visible to the TMA engine
+        tc::named_bar_sync(1, 32 * kEpiWarps);
+        if (tid == 0) {
+          tma_store_2d(&mapO, buf, n0 + c0, m0);  // rows past M are not written
+          tc::bulk_commit();
         }
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acce[ab]);  // this warp's TMEM lanes are read
-      if (a.mode >= kReduceOwned) {
-        tc::named_bar_sync(1, 32 * kEpiWarps);  // every row of the tile is written
-        if (tid == 0) {
-          __threadfence_system();
-          if (a.mode == kReduceOwned)
-            announce(a.flags_mc + t);
-          else
-            for (int p = 0; p < a.world; ++p) announce_peer(a.peer_flags[p] + t);
-        }
+      if (a.mode >= kReduceOwned && tid == 0) {
+        tc::bulk_wait_all();  // every block of the tile is in global memory
+        tc::fence_proxy_async_global();
+        __threadfence_system();
+        if (a.mode == kReduceOwned)
+          announce(a.flags_mc + t);
+        else
+          for (int p = 0; p < a.world; ++p) announce_peer(a.peer_flags[p] + t);
       }
     }
+    if (tid == 0) tc::bulk_wait_all();  // no store may still read shared memory when the CTA ends
   }
   reduce_owned(a, claim, tiles, tiles_n, lane, ok);  // every warp, once its own role has no work left
   if (a.mode != kStore) __threadfence_system();
@@ -642,6 +671,20 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
   return fn;
+}
+
+// the [M, N] output (fp32 or bf16), boxes of 128 bytes x 128 rows, 128-byte swizzle (the staged blocks)
+bool encode_output(CUtensorMap* map, void* base, int64_t M, int N, bool bf16) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t es = bf16 ? 2 : 4;
+  const cuuint64_t dims[2] = {cuuint64_t(N), cuuint64_t(M)};
+  const cuuint64_t strides[1] = {cuuint64_t(N) * es};
+  const cuuint32_t box[2] = {cuuint32_t(128 / es), cuuint32_t(kBM)};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // bf16 [rows, K] row-major, boxes of 64 (K) x box_rows, 128-byte swizzle (the MMA operand layout)
@@ -671,13 +714,13 @@ int sm_count() {
 cudaError_t launch(const ProjArgs& a, cudaStream_t stream) {
   const int64_t tiles = ((a.M + kBM - 1) / kBM) * (a.N / kBN);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
-  CUtensorMap mapA, mapB;
+  CUtensorMap mapA, mapB, mapO;
   if (a.mode != kMulticastAdd && encode_operand(&mapA, a.Y, a.M, a.K, kBM) &&
-      encode_operand(&mapB, a.W, a.N, a.K, kBN)) {
+      encode_operand(&mapB, a.W, a.N, a.K, kBN) && encode_output(&mapO, a.out, a.M, a.N, a.out_bf16 != 0)) {
     cudaError_t e =
         cudaFuncSetAttribute(tp_proj_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmemT));
     if (e != cudaSuccess) return e;
-    tp_proj_tma_kernel<<<unsigned(grid), kThrT, kProjSmemT, stream>>>(a, mapA, mapB);
+    tp_proj_tma_kernel<<<unsigned(grid), kThrT, kProjSmemT, stream>>>(a, mapA, mapB, mapO);
     return cudaGetLastError();
   }
   // the one-shot multicast form (staged epilogue), or no tensor-map encoder: the cp.async kernel
