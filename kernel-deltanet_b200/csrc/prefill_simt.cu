@@ -16,7 +16,7 @@
 //
 // Launches: (1) lift k and q into the workspace, (2) per (chunk, sequence):
 // Gram matrices, gates, T and the decayed q.k matrix, (3) per (sequence,
-// 16-row tile of S): the serial pass over chunks.
+// tile of 4, 8 or 16 rows of S): the serial pass over chunks.
 #include <math.h>
 
 #include "kdn_internal.h"
@@ -26,7 +26,6 @@ namespace kdn {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kRowTile = 16;  // rows of S per chain CTA
 
 struct Workspace {
   float* phik;   // [N, Tp, D]
@@ -218,36 +217,37 @@ constexpr size_t prep_smem_bytes() {
   return sizeof(float) * (2 * C * 65 + 3 * C * (C + 1) + 2 * C);
 }
 
-// (3) per (16-row tile of S, sequence n): the serial pass over chunks.  Tiles below
+// (3) per (tile of RT rows of S, sequence n): the serial pass over chunks (RT = 16, or 8 when the
+// tiles of 16 would leave SMs idle).  Tiles below
 // p.a_rows belong to the block transition's homogeneous map (identity start, v = 0,
 // no readout, result to A_out); the others are value rows (S0, v, y, S_out).
-template <int C>
+template <int C, int RT>
 __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, Workspace w) {
   constexpr int TPR = kThreads / C;    // threads per chunk row
-  constexpr int VPT = kRowTile / TPR;  // state rows per thread in the (C x 16) phases
+  constexpr int VPT = RT / TPR;  // state rows per thread in the (C x RT) phases
   constexpr int LD = C + 1;
   const int D = p.D;
   const int SD = D + 1;  // padded row stride of the S tile
   extern __shared__ float sm[];
-  float* S = sm;                     // [16][SD]
-  float* Ks = S + kRowTile * SD;     // [C][65]
+  float* S = sm;                     // [RT][SD]
+  float* Ks = S + RT * SD;     // [C][65]
   float* Qs = Ks + C * 65;           // [C][65]
   float* Tm = Qs + C * 65;           // [C][LD]
   float* Am = Tm + C * LD;           // [C][LD]
   float* gt = Am + C * LD;           // [C][4]
   float* Rs = gt + C * 4;            // [C][16]
-  float* Es = Rs + C * kRowTile;     // [C][16]
+  float* Es = Rs + C * RT;     // [C][16]
 
   const int vt = blockIdx.x;
   const int64_t n = blockIdx.y;
   const int tid = threadIdx.x;
   const int i = tid / TPR;
   const int v0 = (tid % TPR) * VPT;
-  const bool a_tile = vt * kRowTile < p.a_rows;
-  const int row0 = a_tile ? vt * kRowTile : vt * kRowTile - p.a_rows;
+  const bool a_tile = vt * RT < p.a_rows;
+  const int row0 = a_tile ? vt * RT : vt * RT - p.a_rows;
   const bool readout = !a_tile && p.y != nullptr;  // uniform per CTA
 
-  for (int e = tid; e < kRowTile * D; e += kThreads) {
+  for (int e = tid; e < RT * D; e += kThreads) {
     const int r = e / D, d = e % D;
     float s0 = 0.f;
     if (a_tile)
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
   for (int c = 0; c < w.NC; ++c) {
     if (p.S_chunks && !a_tile) {  // checkpoint: the state entering chunk c
       float* Sc = p.S_chunks + ((n * w.NC + c) * p.dv + row0) * int64_t(D);
-      for (int e = tid; e < kRowTile * D; e += kThreads) Sc[e] = S[(e / D) * SD + e % D];
+      for (int e = tid; e < RT * D; e += kThreads) Sc[e] = S[(e / D) * SD + e % D];
     }
     const float* Tg = w.Tinv + (n * w.NC + c) * int64_t(C) * C;
     const float* Ag = w.Aq + (n * w.NC + c) * int64_t(C) * C;
@@ -313,20 +313,20 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
     for (int u = 0; u < VPT; ++u) {
       float vv = 0.f;
       if (!a_tile && t < p.T) vv = ld_as_f32(p.v, p.in_dtype, (n * p.T + t) * p.dv + row0 + v0 + u);
-      Rs[i * kRowTile + v0 + u] = beta_i * (vv - gi * x[u]);
+      Rs[i * RT + v0 + u] = beta_i * (vv - gi * x[u]);
     }
     __syncthreads();
     // E = T R  (T unit lower triangular)
     float e_[VPT];
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) e_[u] = Rs[i * kRowTile + v0 + u];
+    for (int u = 0; u < VPT; ++u) e_[u] = Rs[i * RT + v0 + u];
     for (int j = 0; j < i; ++j) {
       const float tij = Tm[i * LD + j];
 #pragma unroll
-      for (int u = 0; u < VPT; ++u) e_[u] = fmaf(tij, Rs[j * kRowTile + v0 + u], e_[u]);
+      for (int u = 0; u < VPT; ++u) e_[u] = fmaf(tij, Rs[j * RT + v0 + u], e_[u]);
     }
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) Es[i * kRowTile + v0 + u] = e_[u];
+    for (int u = 0; u < VPT; ++u) Es[i * RT + v0 + u] = e_[u];
     if (p.E_rows && !a_tile) {
 #pragma unroll
       for (int u = 0; u < VPT; ++u) p.E_rows[(n * w.Tp + t) * p.dv + row0 + v0 + u] = e_[u];
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
       for (int j = 0; j < i; ++j) {
         const float aij = Am[i * LD + j];
 #pragma unroll
-        for (int u = 0; u < VPT; ++u) yv[u] = fmaf(aij, Es[j * kRowTile + v0 + u], yv[u]);
+        for (int u = 0; u < VPT; ++u) yv[u] = fmaf(aij, Es[j * RT + v0 + u], yv[u]);
       }
       if (t < p.T) {
 #pragma unroll
@@ -348,35 +348,50 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(PrefillProblem p, 
       }
     }
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) Rs[i * kRowTile + v0 + u] = wi * e_[u];
+    for (int u = 0; u < VPT; ++u) Rs[i * RT + v0 + u] = wi * e_[u];
     __syncthreads();
     // S <- exp(g_{C-1}) S + E''^T K
     const float gC = gt[4 * (C - 1) + 1];
     for (int d = tid; d < D; d += kThreads) {
-      float acc[kRowTile];
+      float acc[RT];
 #pragma unroll
-      for (int r = 0; r < kRowTile; ++r) acc[r] = gC * S[r * SD + d];
+      for (int r = 0; r < RT; ++r) acc[r] = gC * S[r * SD + d];
       for (int j = 0; j < C; ++j) {
         const float kv = Kg[int64_t(j) * D + d];
 #pragma unroll
-        for (int r = 0; r < kRowTile; ++r) acc[r] = fmaf(Rs[j * kRowTile + r], kv, acc[r]);
+        for (int r = 0; r < RT; ++r) acc[r] = fmaf(Rs[j * RT + r], kv, acc[r]);
       }
 #pragma unroll
-      for (int r = 0; r < kRowTile; ++r) S[r * SD + d] = acc[r];
+      for (int r = 0; r < RT; ++r) S[r * SD + d] = acc[r];
     }
     __syncthreads();
   }
 
   float* dst = a_tile ? p.A_out + (n * p.a_rows + row0) * int64_t(D) : p.S_out + (n * p.dv + row0) * int64_t(D);
-  for (int e = tid; e < kRowTile * D; e += kThreads) {
+  for (int e = tid; e < RT * D; e += kThreads) {
     const int r = e / D, d = e % D;
     dst[int64_t(r) * D + d] = S[r * SD + d];
   }
 }
 
-template <int C>
+template <int C, int RT>
 size_t chain_smem_bytes(int D) {
-  return sizeof(float) * (size_t(kRowTile) * (D + 1) + 2 * C * 65 + 2 * C * (C + 1) + 4 * C + 2 * C * kRowTile);
+  return sizeof(float) * (size_t(RT) * (D + 1) + 2 * C * 65 + 2 * C * (C + 1) + 4 * C + 2 * C * RT);
+}
+
+// rows of S per chain CTA: 16, or 8 when 16-row tiles would leave SMs idle (few sequences), or 4
+// (chunk 64) when 8-row tiles would too; the chains are latency-bound, so more CTAs -- on more SMs,
+// then two per SM -- shorten them
+int chain_rows(int64_t rows, int64_t N, int C) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess)
+      sms = 148;
+  }
+  if ((rows / 16) * N >= sms) return 16;
+  return (C == 64 && (rows / 8) * N < sms) ? 4 : 8;
 }
 
 template <int C>
@@ -402,10 +417,16 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
     marks.after(stream);
   }
   {
-    const size_t smem = chain_smem_bytes<C>(p.D);
-    err = cudaFuncSetAttribute(simt_chain_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    const int rt = chain_rows(p.a_rows + p.dv, p.N, C);
+    const size_t smem = rt == 4   ? chain_smem_bytes<C, (C == 64 ? 4 : 8)>(p.D)
+                        : rt == 8 ? chain_smem_bytes<C, 8>(p.D)
+                                  : chain_smem_bytes<C, 16>(p.D);
+    auto chain = rt == 4 ? simt_chain_kernel<C, (C == 64 ? 4 : 8)>
+                 : rt == 8 ? simt_chain_kernel<C, 8>
+                           : simt_chain_kernel<C, 16>;
+    err = cudaFuncSetAttribute(chain, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return err;
-    simt_chain_kernel<C><<<dim3((p.a_rows + p.dv) / kRowTile, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
+    chain<<<dim3((p.a_rows + p.dv) / rt, unsigned(p.N)), kThreads, smem, stream>>>(p, w);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     marks.after(stream);
   }
@@ -431,35 +452,35 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
 //   zero where the decay is clamped (outside [1e-5, 1]).
 // The feature gradients go back through the lift (lift_backward_kernel).  Passes: the forward
 // chain with checkpoints (S entering each chunk, E rows), (B1) the reverse pass over chunks for
-// dS (sequential, per 16-row tile), (B2) the per-chunk gradients (parallel), (B3) the lift.
+// dS (sequential, per tile of 8 or 16 rows), (B2) the per-chunk gradients (parallel), (B3) the lift.
 
-// (B1) per (sequence, 16-row tile of dS): chunks in reverse; stores dS_C of every chunk and dR
-template <int C>
+// (B1) per (sequence, tile of RT rows of dS): chunks in reverse; stores dS_C of every chunk and dR
+template <int C, int RT>
 __global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem b, Workspace w,
                                                                 float* __restrict__ dS_chunks,
                                                                 float* __restrict__ dR_rows) {
   constexpr int TPR = kThreads / C;
-  constexpr int VPT = kRowTile / TPR;
+  constexpr int VPT = RT / TPR;
   constexpr int LD = C + 1;
   const PrefillProblem& p = b.fwd;
   const int D = p.D;
   const int SD = D + 1;
   extern __shared__ float sm[];
-  float* dS = sm;                    // [16][SD]
-  float* Ks = dS + kRowTile * SD;    // [C][65]
+  float* dS = sm;                    // [RT][SD]
+  float* Ks = dS + RT * SD;    // [C][65]
   float* Tm = Ks + C * 65;           // [C][LD]
   float* Am = Tm + C * LD;           // [C][LD]
   float* gt = Am + C * LD;           // [C][4]
-  float* Ys = gt + C * 4;            // [C][16]: dY, then Gs_i dY_i
-  float* Ws = Ys + C * kRowTile;     // [C][16]: dE, then beta_i G_i dR_i
+  float* Ys = gt + C * 4;            // [C][RT]: dY, then Gs_i dY_i
+  float* Ws = Ys + C * RT;     // [C][RT]: dE, then beta_i G_i dR_i
 
   const int64_t n = blockIdx.y;
   const int tid = threadIdx.x;
   const int i = tid / TPR;
   const int v0 = (tid % TPR) * VPT;
-  const int row0 = blockIdx.x * kRowTile;
+  const int row0 = blockIdx.x * RT;
 
-  for (int e = tid; e < kRowTile * D; e += kThreads) {
+  for (int e = tid; e < RT * D; e += kThreads) {
     const int r = e / D, d = e % D;
     dS[r * SD + d] = b.dS_final ? b.dS_final[(n * p.dv + row0 + r) * int64_t(D) + d] : 0.f;
   }
@@ -467,7 +488,7 @@ __global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem 
 
   for (int c = w.NC - 1; c >= 0; --c) {
     float* dSc = dS_chunks + ((n * w.NC + c) * p.dv + row0) * int64_t(D);
-    for (int e = tid; e < kRowTile * D; e += kThreads) dSc[e] = dS[(e / D) * SD + e % D];
+    for (int e = tid; e < RT * D; e += kThreads) dSc[e] = dS[(e / D) * SD + e % D];
     const float* Tg = w.Tinv + (n * w.NC + c) * int64_t(C) * C;
     const float* Ag = w.Aq + (n * w.NC + c) * int64_t(C) * C;
     const float* Gg = w.gates + (n * w.NC + c) * int64_t(C) * 4;
@@ -500,7 +521,7 @@ __global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem 
     const int64_t t = int64_t(c) * C + i;
 #pragma unroll
     for (int u = 0; u < VPT; ++u)
-      Ys[i * kRowTile + v0 + u] = t < p.T ? ld_as_f32(b.dy, b.dy_dtype, (n * p.T + t) * p.dv + row0 + v0 + u) : 0.f;
+      Ys[i * RT + v0 + u] = t < p.T ? ld_as_f32(b.dy, b.dy_dtype, (n * p.T + t) * p.dv + row0 + v0 + u) : 0.f;
     __syncthreads();
     // dE_i = Rg_i x_i + sum_{i'>i} P_{i'i} dY_{i'}
     const float rg = gt[4 * i + 2];
@@ -510,10 +531,10 @@ __global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem 
     for (int j = i + 1; j < C; ++j) {
       const float a = Am[j * LD + i];
 #pragma unroll
-      for (int u = 0; u < VPT; ++u) de[u] = fmaf(a, Ys[j * kRowTile + v0 + u], de[u]);
+      for (int u = 0; u < VPT; ++u) de[u] = fmaf(a, Ys[j * RT + v0 + u], de[u]);
     }
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) Ws[i * kRowTile + v0 + u] = de[u];
+    for (int u = 0; u < VPT; ++u) Ws[i * RT + v0 + u] = de[u];
     __syncthreads();
     // dR_i = dE_i + sum_{i'>i} T_{i'i} dE_{i'}
     float dr[VPT];
@@ -522,7 +543,7 @@ __global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem 
     for (int j = i + 1; j < C; ++j) {
       const float tj = Tm[j * LD + i];
 #pragma unroll
-      for (int u = 0; u < VPT; ++u) dr[u] = fmaf(tj, Ws[j * kRowTile + v0 + u], dr[u]);
+      for (int u = 0; u < VPT; ++u) dr[u] = fmaf(tj, Ws[j * RT + v0 + u], dr[u]);
     }
 #pragma unroll
     for (int u = 0; u < VPT; ++u) dR_rows[(n * w.Tp + t) * p.dv + row0 + v0 + u] = dr[u];
@@ -530,29 +551,29 @@ __global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem 
     const float gprev = gt[4 * i + 0], gi = gt[4 * i + 1], beta_i = gt[4 * i + 3];
 #pragma unroll
     for (int u = 0; u < VPT; ++u) {
-      Ws[i * kRowTile + v0 + u] = beta_i * gi * dr[u];
-      Ys[i * kRowTile + v0 + u] *= gprev;
+      Ws[i * RT + v0 + u] = beta_i * gi * dr[u];
+      Ys[i * RT + v0 + u] *= gprev;
     }
     __syncthreads();
     // dS <- G_{C-1} dS + sum_i (Gs_i dY_i q_i^T - beta_i G_i dR_i k_i^T)
     const float gC = gt[4 * (C - 1) + 1];
     for (int d = tid; d < D; d += kThreads) {
-      float acc[kRowTile];
+      float acc[RT];
 #pragma unroll
-      for (int r = 0; r < kRowTile; ++r) acc[r] = gC * dS[r * SD + d];
+      for (int r = 0; r < RT; ++r) acc[r] = gC * dS[r * SD + d];
       for (int j = 0; j < C; ++j) {
         const float kv = Kg[int64_t(j) * D + d], qv = Qg[int64_t(j) * D + d];
 #pragma unroll
-        for (int r = 0; r < kRowTile; ++r)
-          acc[r] = fmaf(Ys[j * kRowTile + r], qv, fmaf(-Ws[j * kRowTile + r], kv, acc[r]));
+        for (int r = 0; r < RT; ++r)
+          acc[r] = fmaf(Ys[j * RT + r], qv, fmaf(-Ws[j * RT + r], kv, acc[r]));
       }
 #pragma unroll
-      for (int r = 0; r < kRowTile; ++r) dS[r * SD + d] = acc[r];
+      for (int r = 0; r < RT; ++r) dS[r * SD + d] = acc[r];
     }
     __syncthreads();
   }
   if (b.dS0) {
-    for (int e = tid; e < kRowTile * D; e += kThreads) {
+    for (int e = tid; e < RT * D; e += kThreads) {
       const int r = e / D, d = e % D;
       b.dS0[(n * p.dv + row0 + r) * int64_t(D) + d] = dS[r * SD + d];
     }
@@ -922,9 +943,9 @@ __global__ void __launch_bounds__(kThreads) lift_backward_kernel(BackwardProblem
   }
 }
 
-template <int C>
+template <int C, int RT>
 size_t adjoint_smem_bytes(int D) {
-  return sizeof(float) * (size_t(kRowTile) * (D + 1) + C * 65 + 2 * C * (C + 1) + 4 * C + 2 * C * kRowTile);
+  return sizeof(float) * (size_t(RT) * (D + 1) + C * 65 + 2 * C * (C + 1) + 4 * C + 2 * C * RT);
 }
 
 struct BackwardExtra {
@@ -968,11 +989,13 @@ cudaError_t launch_backward_c(BackwardProblem b, const Workspace& w, const Backw
   cudaError_t err = launch_c<C>(b.fwd, w, P, stream, none);  // lift, prep, chain with checkpoints
   if (err != cudaSuccess) return err;
   {
-    const size_t smem = adjoint_smem_bytes<C>(b.fwd.D);
-    err = cudaFuncSetAttribute(simt_adjoint_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    // tiles of at least 8 rows here: the adjoint loads K and Q per chunk, and 4-row tiles measured slower
+    const int rt = chain_rows(b.fwd.dv, b.fwd.N, C) == 16 ? 16 : 8;
+    const size_t smem = rt == 8 ? adjoint_smem_bytes<C, 8>(b.fwd.D) : adjoint_smem_bytes<C, 16>(b.fwd.D);
+    auto adjoint = rt == 8 ? simt_adjoint_kernel<C, 8> : simt_adjoint_kernel<C, 16>;
+    err = cudaFuncSetAttribute(adjoint, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return err;
-    simt_adjoint_kernel<C><<<dim3(b.fwd.dv / kRowTile, unsigned(b.fwd.N)), kThreads, smem, stream>>>(
-        b, w, x.dS_chunks, x.dR_rows);
+    adjoint<<<dim3(b.fwd.dv / rt, unsigned(b.fwd.N)), kThreads, smem, stream>>>(b, w, x.dS_chunks, x.dR_rows);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
   }
   {
