@@ -299,35 +299,49 @@ __global__ void __launch_bounds__(kDecThr, 1) decode_kernel(DecodeProblem p, Pro
         const float beta = gate.x, lam = gate.y;
         const ST* stage = reinterpret_cast<const ST*>(stg);
         ST* gstate = slot >= 0 ? reinterpret_cast<ST*>(p.states) + rows_offset<ST>(slot, th, p, g, D) : nullptr;
+        constexpr int kRowsPerWarp = kItemRows / kDecWarps;
+        const int r0 = warp * kRowsPerWarp;  // this warp's first row within the item
+        if (slot < 0) {  // padding token (or a slot out of range): zero outputs, state untouched
 #pragma unroll
-        for (int rr = 0; rr < kItemRows / kDecWarps; ++rr) {
-          const int r = warp * (kItemRows / kDecWarps) + rr;  // row within the item
-          const int64_t orow = th * p.dv + int64_t(g) * kItemRows + r;
-          if (slot < 0) {  // padding token (or a slot out of range): zero output, state untouched
-            if (lane == 0) st_from_f32(p.out, p.out_dtype, orow, 0.f);
-            continue;
+          for (int rr = 0; rr < kRowsPerWarp; ++rr)
+            if (lane == 0) st_from_f32(p.out, p.out_dtype, th * p.dv + int64_t(g) * kItemRows + r0 + rr, 0.f);
+        } else {
+          // both rows in one block: their loads, dot products and warp reductions interleave
+          float2 sv[kRowsPerWarp][kMaxBlocks];
+          float dk[kRowsPerWarp], dq[kRowsPerWarp];
+#pragma unroll
+          for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+            const ST* row = stage + int64_t(r0 + rr) * D;
+            dk[rr] = dq[rr] = 0.f;
+#pragma unroll
+            for (int m = 0; m < kMaxBlocks; ++m) {
+              sv[rr][m] = (m < P.M) ? StateIO<ST>::load(row + 64 * m + 2 * lane) : make_float2(0.f, 0.f);
+              dk[rr] = fmaf(sv[rr][m].x, fk[m].x, fmaf(sv[rr][m].y, fk[m].y, dk[rr]));
+              dq[rr] = fmaf(sv[rr][m].x, fq[m].x, fmaf(sv[rr][m].y, fq[m].y, dq[rr]));
+            }
           }
-          const ST* row = stage + int64_t(r) * D;
-          ST* grow = gstate + int64_t(r) * D;
-          float2 sv[kMaxBlocks];
-          float dk = 0.f, dq = 0.f;
 #pragma unroll
-          for (int m = 0; m < kMaxBlocks; ++m) {
-            sv[m] = (m < P.M) ? StateIO<ST>::load(row + 64 * m + 2 * lane) : make_float2(0.f, 0.f);
-            dk = fmaf(sv[m].x, fk[m].x, fmaf(sv[m].y, fk[m].y, dk));
-            dq = fmaf(sv[m].x, fq[m].x, fmaf(sv[m].y, fq[m].y, dq));
-          }
-          dk = warp_sum(dk);
-          dq = warp_sum(dq);
-          const float coef = beta * (ld_as_f32(stg + STG_V, p.in_dtype, r) - lam * dk);
+          for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-          for (int m = 0; m < kMaxBlocks; ++m)  // written back straight to the slot pool
-            if (m < P.M)
-              StateIO<ST>::store(grow + 64 * m + 2 * lane, fmaf(lam, sv[m].x, coef * fk[m].x),
-                                 fmaf(lam, sv[m].y, coef * fk[m].y));
-          if (lane == 0) {
-            const float yv = p.readout == KDN_READOUT_POST ? fmaf(lam, dq, coef * kq) : dq;
-            st_from_f32(p.out, p.out_dtype, orow, yv);
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+              dk[rr] += __shfl_xor_sync(0xffffffffu, dk[rr], o);
+              dq[rr] += __shfl_xor_sync(0xffffffffu, dq[rr], o);
+            }
+#pragma unroll
+          for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+            const int r = r0 + rr;
+            const int64_t orow = th * p.dv + int64_t(g) * kItemRows + r;
+            ST* grow = gstate + int64_t(r) * D;
+            const float coef = beta * (ld_as_f32(stg + STG_V, p.in_dtype, r) - lam * dk[rr]);
+#pragma unroll
+            for (int m = 0; m < kMaxBlocks; ++m)  // written back straight to the slot pool
+              if (m < P.M)
+                StateIO<ST>::store(grow + 64 * m + 2 * lane, fmaf(lam, sv[rr][m].x, coef * fk[m].x),
+                                   fmaf(lam, sv[rr][m].y, coef * fk[m].y));
+            if (lane == 0) {
+              const float yv = p.readout == KDN_READOUT_POST ? fmaf(lam, dq[rr], coef * kq) : dq[rr];
+              st_from_f32(p.out, p.out_dtype, orow, yv);
+            }
           }
         }
         __syncwarp();
