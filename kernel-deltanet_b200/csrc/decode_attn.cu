@@ -9,10 +9,11 @@
 // exit at once, so the cost follows the live lengths even when the launch (e.g. inside a CUDA graph)
 // is sized for the cache's capacity.
 //
-// In a CTA each lane scores whole keys (its 64-element key row against the query held in
-// registers), the warp keeps an online softmax over its keys, and the value rows are summed with
-// each lane owning two output dimensions; a group's value rows are loaded together with its key rows,
-// so both are in flight at once.
+// In a CTA a warp takes groups of 32 keys: 8 lanes share a key and its value row (8 elements each, so a
+// warp instruction reads four whole contiguous rows) and finish the key's dot product with 3 shuffles.
+// The warp keeps an online softmax over its keys; each lane accumulates its 8 value dimensions over its
+// own keys, and the 4 key subgroups of a warp are summed once, at the end.  All of a group's key and
+// value chunks are loaded before any is used, so 16 loads per lane are in flight at once.
 #include <math.h>
 
 #include "kdn_common.cuh"
@@ -52,11 +53,37 @@ __device__ __forceinline__ void load_row(const T* p, float* f) {  // 64 elements
   }
 }
 
+// 8 consecutive elements of a cache row (16 bytes of bf16, 32 of fp32)
 template <typename T>
-__device__ __forceinline__ float2 load_pair(const T* p) {
-  if constexpr (sizeof(T) == 2) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
-  return *reinterpret_cast<const float2*>(p);
-}
+struct Chunk;
+template <>
+struct Chunk<__nv_bfloat16> {
+  uint4 u;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { u = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void zero() { u = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ void to_float(float* f) const {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+      f[2 * e] = t.x;
+      f[2 * e + 1] = t.y;
+    }
+  }
+};
+template <>
+struct Chunk<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = reinterpret_cast<const float4*>(p)[0];
+    b = reinterpret_cast<const float4*>(p)[1];
+  }
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void to_float(float* f) const {
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+};
 
 template <typename T>
 __global__ void __launch_bounds__(32 * kWarps) decode_attn_partial_kernel(const T* __restrict__ q,
@@ -81,53 +108,87 @@ __global__ void __launch_bounds__(32 * kWarps) decode_attn_partial_kernel(const 
   }
   const int64_t k1 = (k0 + kKeys < nkeys) ? k0 + kKeys : nkeys;
   const int64_t bh = int64_t(b) * H + h;
-  float qf[kHd];
-  load_row(q + bh * kHd, qf);
+  // lane l takes the 16-byte chunk sub = l % 8 of keys (l / 8) + 4 i (i < 8): a warp instruction reads four
+  // whole contiguous key rows, and the 8 lanes of a key finish its dot product with 3 shuffles
+  const int sub = lane & 7, grp = lane >> 3;
+  float qs[8];  // this lane's 8 query elements [8 sub, 8 sub + 8)
+  {
+    float qf[kHd];
+    load_row(q + bh * kHd, qf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qs[e] = qf[8 * sub + e];
+  }
   const T* kb = kc + bh * max_len * kHd;
   const T* vb = vc + bh * max_len * kHd;
-  float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
+  float m = -INFINITY, l = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // dims [8 sub, 8 sub + 8)
   for (int64_t j0 = k0 + 32 * warp; j0 < k1; j0 += 32 * kWarps) {
-    const int64_t j = j0 + lane;
     const int cnt = int((k1 - j0) < 32 ? (k1 - j0) : 32);
-    float2 vv[32];  // this lane's two columns of the group's value rows, loaded with the key rows
+    // all of this lane's key and value chunks of the group in flight at once
+    Chunk<T> kr[8], vr[8];
 #pragma unroll
-    for (int r = 0; r < 32; ++r)
-      vv[r] = r < cnt ? load_pair(vb + (j0 + r) * kHd + 2 * lane) : make_float2(0.f, 0.f);
-    float sc = -INFINITY;
-    if (j < k1) {
-      float kf[kHd];
-      load_row(kb + j * kHd, kf);
+    for (int i = 0; i < 8; ++i) {
+      const int kk = grp + 4 * i;  // key within the group
+      if (kk < cnt) {
+        kr[i].load(kb + (j0 + kk) * kHd + 8 * sub);
+        vr[i].load(vb + (j0 + kk) * kHd + 8 * sub);
+      } else {
+        kr[i].zero();
+        vr[i].zero();
+      }
+    }
+    float sc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float kf[8];
+      kr[i].to_float(kf);
       float dot = 0.f;
 #pragma unroll
-      for (int d = 0; d < kHd; ++d) dot = fmaf(qf[d], kf[d], dot);
-      sc = dot * scale;
+      for (int e = 0; e < 8; ++e) dot = fmaf(qs[e], kf[e], dot);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+      sc[i] = grp + 4 * i < cnt ? dot * scale : -INFINITY;
     }
-    float mx = sc;
+    float mx = sc[0];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, sc[i]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
     const float mn = fmaxf(m, mx);  // finite: the group has at least one key
     const float corr = expf(m - mn);
-    const float p = (j < k1) ? expf(sc - mn) : 0.f;
-    float ps = p;
+    float ps = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= corr;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float p = (grp + 4 * i < cnt) ? expf(sc[i] - mn) : 0.f;
+      ps += p;
+      float vf[8];
+      vr[i].to_float(vf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(p, vf[e], acc[e]);
+    }
+    // a key's probability sits in all 8 of its lanes: sum one lane per key subgroup (lanes 0, 8, 16, 24)
+    ps = (sub == 0) ? ps : 0.f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
     l = l * corr + ps;
-    a0 *= corr;
-    a1 *= corr;
-#pragma unroll
-    for (int r = 0; r < 32; ++r) {  // p is 0 past the group's keys (and vv is 0 there)
-      const float pr = __shfl_sync(0xffffffffu, p, r);
-      a0 = fmaf(pr, vv[r].x, a0);
-      a1 = fmaf(pr, vv[r].y, a1);
-    }
     m = mn;
+  }
+  // the 4 key subgroups share the running max, so their value sums add directly
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 8);
+    acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 16);
   }
   if (lane == 0) {
     red[warp][0] = m;
     red[warp][1] = l;
   }
-  red[warp][2 + 2 * lane] = a0;
-  red[warp][3 + 2 * lane] = a1;
+  if (grp == 0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) red[warp][2 + 8 * sub + e] = acc[e];
+  }
   __syncthreads();
   if (warp == 0) {
     float M = -INFINITY;
