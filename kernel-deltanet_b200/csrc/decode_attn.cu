@@ -23,35 +23,9 @@ namespace kdn {
 namespace {
 
 constexpr int kHd = 64;        // head dimension
-constexpr int kKeys = 512;     // keys per CTA
+constexpr int kKeys = 1024;    // keys per CTA
 constexpr int kWarps = 4;
 constexpr int kPart = kHd + 2; // partial record: m, l, acc[64]
-
-template <typename T>
-__device__ __forceinline__ void load_row(const T* p, float* f) {  // 64 elements
-  if constexpr (sizeof(T) == 2) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint4 u = reinterpret_cast<const uint4*>(p)[c];
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-        f[8 * c + 2 * i] = t.x;
-        f[8 * c + 2 * i + 1] = t.y;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const float4 t = reinterpret_cast<const float4*>(p)[c];
-      f[4 * c] = t.x;
-      f[4 * c + 1] = t.y;
-      f[4 * c + 2] = t.z;
-      f[4 * c + 3] = t.w;
-    }
-  }
-}
 
 // 8 consecutive elements of a cache row (16 bytes of bf16, 32 of fp32)
 template <typename T>
@@ -113,10 +87,9 @@ __global__ void __launch_bounds__(32 * kWarps) decode_attn_partial_kernel(const 
   const int sub = lane & 7, grp = lane >> 3;
   float qs[8];  // this lane's 8 query elements [8 sub, 8 sub + 8)
   {
-    float qf[kHd];
-    load_row(q + bh * kHd, qf);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qs[e] = qf[8 * sub + e];
+    Chunk<T> qc;
+    qc.load(q + bh * kHd + 8 * sub);
+    qc.to_float(qs);
   }
   const T* kb = kc + bh * max_len * kHd;
   const T* vb = vc + bh * max_len * kHd;

@@ -24,7 +24,7 @@ def test_glue_argument_checks(lib):
     assert lib.kdn_decode_attention(P, None, P, P, P, 1, 2, 4, 100, 64, P, 1 << 20, None) == 1
     assert lib.kdn_decode_attention(P, P, P, P, P, 1, 2, 4, 100, 64, P, 8, None) == 4        # workspace too small
     assert lib.kdn_decode_attention(P, P, P, P, P, 1, 0, 4, 100, 64, None, 0, None) == 0     # no sequences
-    assert lib.kdn_decode_attention_workspace_size(2, 4, 1000) == 4 * 2 * 4 * 2 * 66
+    assert lib.kdn_decode_attention_workspace_size(2, 4, 2000) == 4 * 2 * 4 * 2 * 66  # 1024 keys per split
 
 
 def _close(got, ref, dtype):
@@ -71,16 +71,16 @@ def test_mixer_inputs(dtype, H):
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_decode_attention(dtype):
-    """Split-K one-token attention over ragged cache lengths (split boundaries 511/512/513) against
+    """Split-K one-token attention over ragged cache lengths (split boundaries 1023/1024/1025) against
     a float64 softmax; a length past the cache gives a zero row."""
     from kdn_b200.kernels import glue
 
     g = torch.Generator(device="cuda").manual_seed(3)
-    B, H, L = 7, 3, 1100
+    B, H, L = 9, 3, 2200
     q = torch.randn(B, H, 64, generator=g, device="cuda").to(dtype)
     kc = torch.randn(B, H, L, 64, generator=g, device="cuda").to(dtype)
     vc = torch.randn(B, H, L, 64, generator=g, device="cuda").to(dtype)
-    lengths = torch.tensor([0, 511, 512, 513, 1000, L - 1, L + 5], device="cuda")
+    lengths = torch.tensor([0, 30, 511, 1022, 1023, 1024, 2000, L - 1, L + 5], device="cuda")
     out = glue.decode_attention(q, kc, vc, lengths).double()
     for b in range(B):
         n = int(lengths[b]) + 1
