@@ -260,6 +260,9 @@ int kdn_decode_attention(const void* q, const void* k_cache, const void* v_cache
  * each one pass over its data; fp32 arithmetic, dtype KDN_DTYPE_F32 or KDN_DTYPE_BF16 storage.
  *   kdn_rmsnorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * weight  (RMSNorm, :16-25); x, out
  *     [n, d] (same dtype, 16-byte aligned, d a multiple of 8 for bf16 / 4 for fp32).
+ *   kdn_add_rmsnorm: h = x + residual, rounded to dtype and stored to h_out (the residual add
+ *     of :89 / :96), then out = RMSNorm(h) as kdn_rmsnorm; residual NULL is kdn_rmsnorm.  h_out
+ *     may be x; with a residual, out must not alias x, residual or h_out.
  *   kdn_swiglu: out[r, j] = silu(gate_up[r, j]) * gate_up[r, d_ff + j]  (SwiGLU, :45-46);
  *     gate_up [n, 2 d_ff], out [n, d_ff].
  *   kdn_mixer_inputs: z [n, 3 H 64 + H] (the fused q|k|v|beta projection) -> q, k [n, H, 64]
@@ -270,6 +273,8 @@ int kdn_decode_attention(const void* q, const void* k_cache, const void* v_cache
  */
 int kdn_rmsnorm(const void* x, int dtype, const void* weight, int weight_dtype, void* out, int64_t n, int32_t d,
                 float eps, void* stream);
+int kdn_add_rmsnorm(const void* x, const void* residual, int dtype, const void* weight, int weight_dtype, void* h_out,
+                    void* out, int64_t n, int32_t d, float eps, void* stream);
 int kdn_swiglu(const void* gate_up, void* out, int dtype, int64_t n, int32_t d_ff, void* stream);
 int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, const void* logit_decay,
                      int logit_dtype, void* q, void* k, void* v, float* beta, float* decay, void* stream);

@@ -448,13 +448,23 @@ static int vec_elems(int dt) { return dt == KDN_DTYPE_BF16 ? 8 : 4; }
 
 int kdn_rmsnorm(const void* x, int dtype, const void* weight, int weight_dtype, void* out, int64_t n, int32_t d,
                 float eps, void* stream) {
+  return kdn_add_rmsnorm(x, nullptr, dtype, weight, weight_dtype, nullptr, out, n, d, eps, stream);
+}
+
+int kdn_add_rmsnorm(const void* x, const void* residual, int dtype, const void* weight, int weight_dtype, void* h_out,
+                    void* out, int64_t n, int32_t d, float eps, void* stream) {
   if (n < 0 || d < 1) return fail(KDN_ERR_INVALID, "n=%lld d=%d", (long long)n, d);
   if (n == 0) return ok();
   if (!x || !weight || !out) return fail(KDN_ERR_INVALID, "x/weight/out is NULL");
+  if (residual && !h_out) return fail(KDN_ERR_INVALID, "h_out is NULL (needed with a residual)");
   if (!float_dtype(dtype) || !float_dtype(weight_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
   if (d % vec_elems(dtype) != 0) return fail(KDN_ERR_UNSUPPORTED, "d=%d: a multiple of %d", d, vec_elems(dtype));
-  if (!aligned(x, 16) || !aligned(out, 16)) return fail(KDN_ERR_INVALID, "x/out must be 16-byte aligned");
-  cudaError_t e = kdn::launch_rmsnorm(x, weight, weight_dtype, out, dtype, n, d, eps, static_cast<cudaStream_t>(stream));
+  if (!aligned(x, 16) || !aligned(out, 16) || (residual && (!aligned(residual, 16) || !aligned(h_out, 16))))
+    return fail(KDN_ERR_INVALID, "x/residual/h_out/out must be 16-byte aligned");
+  if (residual && (out == x || out == residual || out == h_out))
+    return fail(KDN_ERR_INVALID, "out must not alias x, residual or h_out");
+  cudaError_t e = kdn::launch_rmsnorm(x, residual, weight, weight_dtype, residual ? h_out : nullptr, out, dtype, n, d,
+                                      eps, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
   return ok();
 }

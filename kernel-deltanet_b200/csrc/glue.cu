@@ -1,7 +1,7 @@
 // glue.cu -- the element-wise steps between the hybrid LM's GEMMs, one HBM pass each.
 //
 // A pre-norm hybrid block (layers/hybrid_kernel_deltanet_block.py:85-96) surrounds its GEMMs
-// with RMSNorm (:23-25), SwiGLU's silu(gate) * up (:45-46) and, in the Kernel-DeltaNet mixer,
+// with residual adds and RMSNorm (:23-25; an add and the norm after it are one kernel), SwiGLU's silu(gate) * up (:45-46) and, in the Kernel-DeltaNet mixer,
 // the split of the fused q|k|v|beta projection into unit-norm q and k per head
 // (layers/kernel_deltanet_layer.py:98-99), v, beta = sigmoid(.) (serving/tensor_parallel_runner.py:62)
 // and the per-head decay sigmoid(logit_decay) (kernel_deltanet_layer.py:71-73).  Written as
@@ -61,30 +61,83 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-// one warp per row: out = x * rsqrt(mean(x^2) + eps) * w
 template <typename T>
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const void* __restrict__ w, int wdt,
+__device__ __forceinline__ float round_to(float v) {  // the value a T tensor would hold
+  if constexpr (sizeof(T) == 2) return __bfloat162float(__float2bfloat16_rn(v));
+  return v;
+}
+
+// one warp per row: h = x + res (when res is given: rounded to T and stored to h_out, as a separate
+// add would leave it), out = h * rsqrt(mean(h^2) + eps) * w.  The first kRowVecs 16-byte vectors of
+// each lane stay in registers between the two passes (d <= 2048 bf16 / 1024 fp32 is one read of the
+// row); the rest is read again from h_out (or x).  h_out may be x; out must not alias x, res or h_out.
+constexpr int kRowVecs = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const T* x, const T* res,
+                                                      const void* __restrict__ w, int wdt, bool wvec, T* h_out,
                                                       T* __restrict__ out, int64_t n, int d, float eps) {
   constexpr int V = V16<T>::N;
   const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
+  const int nv = d / V;
   const T* xr = x + row * d;
-  float ss = 0.f;
-  for (int c = lane * V; c < d; c += 32 * V) {
-    float f[V];
-    load16(xr + c, f);
+  const T* rr = res ? res + row * d : nullptr;
+  T* hr = res ? h_out + row * d : nullptr;
+  auto load_h = [&](int vi, float* f) {
+    load16(xr + vi * V, f);
+    if (rr) {
+      float r[V];
+      load16(rr + vi * V, r);
 #pragma unroll
-    for (int i = 0; i < V; ++i) ss = fmaf(f[i], f[i], ss);
+      for (int j = 0; j < V; ++j) f[j] = round_to<T>(f[j] + r[j]);
+    }
+  };
+  float keep[kRowVecs][V];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowVecs; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nv) {
+      load_h(vi, keep[i]);
+#pragma unroll
+      for (int j = 0; j < V; ++j) ss = fmaf(keep[i][j], keep[i][j], ss);
+    }
+  }
+  for (int vi = lane + 32 * kRowVecs; vi < nv; vi += 32) {  // long rows
+    float f[V];
+    load_h(vi, f);
+#pragma unroll
+    for (int j = 0; j < V; ++j) ss = fmaf(f[j], f[j], ss);
+    if (hr) store16(hr + vi * V, f);
   }
   const float r = rsqrtf(warp_sum(ss) / float(d) + eps);
   T* orow = out + row * d;
-  for (int c = lane * V; c < d; c += 32 * V) {
-    float f[V];
-    load16(xr + c, f);  // second read of the row: an L1 hit
+  auto finish = [&](int vi, float* f) {
+    float wf[V];
+    if (wvec) {
+      load16(static_cast<const T*>(w) + vi * V, wf);
+    } else {
 #pragma unroll
-    for (int i = 0; i < V; ++i) f[i] = f[i] * r * ld_as_f32(w, wdt, c + i);
-    store16(orow + c, f);
+      for (int j = 0; j < V; ++j) wf[j] = ld_as_f32(w, wdt, vi * V + j);
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) f[j] = f[j] * r * wf[j];
+    store16(orow + vi * V, f);
+  };
+#pragma unroll
+  for (int i = 0; i < kRowVecs; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nv) {
+      if (hr) store16(hr + vi * V, keep[i]);
+      finish(vi, keep[i]);
+    }
+  }
+  for (int vi = lane + 32 * kRowVecs; vi < nv; vi += 32) {
+    float f[V];
+    load16((hr ? hr : xr) + vi * V, f);  // this lane's own earlier store when h is written
+    finish(vi, f);
   }
 }
 
@@ -155,15 +208,18 @@ int grid_for(int64_t items, int per_block) {
 
 }  // namespace
 
-cudaError_t launch_rmsnorm(const void* x, const void* w, int wdt, void* out, int dt, int64_t n, int d, float eps,
-                           cudaStream_t stream) {
+cudaError_t launch_rmsnorm(const void* x, const void* res, const void* w, int wdt, void* h_out, void* out, int dt,
+                           int64_t n, int d, float eps, cudaStream_t stream) {
   const int grid = grid_for(n, 8);
+  const bool wvec = wdt == dt && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
   if (dt == KDN_DTYPE_BF16)
-    rmsnorm_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), w, wdt,
-                                                             static_cast<__nv_bfloat16*>(out), n, d, eps);
+    rmsnorm_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(res), w, wdt, wvec,
+        static_cast<__nv_bfloat16*>(h_out), static_cast<__nv_bfloat16*>(out), n, d, eps);
   else
-    rmsnorm_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), w, wdt, static_cast<float*>(out), n,
-                                                     d, eps);
+    rmsnorm_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), static_cast<const float*>(res), w,
+                                                     wdt, wvec, static_cast<float*>(h_out), static_cast<float*>(out),
+                                                     n, d, eps);
   return cudaGetLastError();
 }
 

@@ -135,8 +135,8 @@ cudaError_t tp_proj_read_error(cudaStream_t stream, int* code);
 
 // ---------------------------------------------------------------- glue.cu
 // element-wise steps of the hybrid block: RMSNorm, SwiGLU, the mixer-input split
-cudaError_t launch_rmsnorm(const void* x, const void* w, int wdt, void* out, int dt, int64_t n, int d, float eps,
-                           cudaStream_t stream);
+cudaError_t launch_rmsnorm(const void* x, const void* res, const void* w, int wdt, void* h_out, void* out, int dt,
+                           int64_t n, int d, float eps, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* gu, void* out, int dt, int64_t n, int f, cudaStream_t stream);
 cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, const void* logit_decay, int lddt, void* q,
                                 void* k, void* v, float* beta, float* decay, cudaStream_t stream);

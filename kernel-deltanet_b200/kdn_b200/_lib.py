@@ -76,6 +76,7 @@ SIGNATURES = {
     "kdn_decode_attention_workspace_size": (ctypes.c_size_t, [_I64, _I32, _I64]),
     "kdn_decode_attention": (_INT, [_P, _P, _P, _P, _P, _INT, _I64, _I32, _I64, _I32, _P, ctypes.c_size_t, _P]),
     "kdn_rmsnorm": (_INT, [_P, _INT, _P, _INT, _P, _I64, _I32, ctypes.c_float, _P]),
+    "kdn_add_rmsnorm": (_INT, [_P, _P, _INT, _P, _INT, _P, _P, _I64, _I32, ctypes.c_float, _P]),
     "kdn_swiglu": (_INT, [_P, _P, _INT, _I64, _I32, _P]),
     "kdn_mixer_inputs": (_INT, [_P, _INT, _I64, _I32, _I32, _P, _INT, _P, _P, _P, _P, _P, _P]),
     "kdn_copy_rows": (_INT, [_P, ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _P]),

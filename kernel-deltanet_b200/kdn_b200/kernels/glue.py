@@ -34,6 +34,23 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return out
 
 
+def add_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float):
+    """(h, RMSNorm(h)) with h = x + residual, in one pass (kdn_add_rmsnorm); h is rounded to x's dtype
+    as a separate add would leave it."""
+    _cuda(x, residual, weight)
+    if residual.shape != x.shape or residual.dtype != x.dtype:
+        raise RuntimeError("residual must match x in shape and dtype")
+    xc, rc = x.contiguous(), residual.contiguous()
+    h, out = torch.empty_like(xc), torch.empty_like(xc)
+    d = xc.shape[-1]
+    w = weight.contiguous()
+    _lib.check(_lib.load().kdn_add_rmsnorm(xc.data_ptr(), rc.data_ptr(), _lib.dtype_code(xc), w.data_ptr(),
+                                           _lib.dtype_code(w), h.data_ptr(), out.data_ptr(), xc.numel() // d, d, eps,
+                                           _lib.stream_handle(x.device)),
+               "kdn_add_rmsnorm")
+    return h, out
+
+
 def swiglu_product(gate_up: torch.Tensor) -> torch.Tensor:
     """[n, 2 d_ff] (gate columns first) -> silu(gate) * up [n, d_ff]."""
     _cuda(gate_up)

@@ -56,6 +56,10 @@ class RMSNorm(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return glue.rms_norm(x, self.weight, self.eps)
 
+    def add_forward(self, x: torch.Tensor, residual: torch.Tensor):
+        """(h, RMSNorm(h)) with h = x + residual: the residual add and the norm after it in one pass."""
+        return glue.add_rms_norm(x, residual, self.weight, self.eps)
+
 
 class SwiGLUFFN(nn.Module):
     """W_down(silu(x W_gate) * (x W_up)) (layers/hybrid_kernel_deltanet_block.py:28-46); the gate and

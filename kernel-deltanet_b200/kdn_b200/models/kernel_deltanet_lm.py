@@ -141,15 +141,23 @@ class KernelDeltaNetLM(nn.Module):
         B = cache.batch
         rows = torch.arange(B, device=tokens.device)
         x = self.embed(tokens)
+        delta = None  # the FFN output not yet added to the residual stream x
         for li, layer in enumerate(self.layers):
-            h = layer.norm1(x)
+            # each residual add runs fused with the RMSNorm that follows it
+            if delta is None:
+                h = layer.norm1(x)
+            else:
+                x, h = layer.norm1.add_forward(x, delta)
             if layer.anchor:
                 mixed = layer.mixer.decode(h, cache.k_cache[li], cache.v_cache[li], cache.lengths_dev, span)
             else:
                 mixed = layer.mixer.decode(h, cache.states[li], rows)
-            x = layer.finish(x, mixed)
+            x, h = layer.norm2.add_forward(x, mixed)
+            delta = layer.ffn(h)
         cache.lengths_dev += 1
-        return self.lm_head(self.final_norm(x))
+        if delta is None:
+            return self.lm_head(self.final_norm(x))
+        return self.lm_head(self.final_norm.add_forward(x, delta)[1])
 
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, cache: HybridCache) -> torch.Tensor:

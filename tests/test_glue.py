@@ -1,4 +1,4 @@
-"""Element-wise kernels of the hybrid block (kdn_rmsnorm, kdn_swiglu, kdn_mixer_inputs).
+"""Element-wise kernels of the hybrid block (kdn_rmsnorm, kdn_add_rmsnorm, kdn_swiglu, kdn_mixer_inputs).
 
 CPU: argument checks of the C entries (no device work).  GPU: each kernel against the same
 formula in torch fp32 -- fp32 storage within 1e-6 relative, bf16 storage within one bf16
@@ -15,6 +15,12 @@ def test_glue_argument_checks(lib):
     assert lib.kdn_rmsnorm(P + 4, 1, P, 0, P, 4, 2048, 1e-6, None) == 1   # misaligned x
     assert lib.kdn_rmsnorm(P, 5, P, 0, P, 4, 2048, 1e-6, None) == 1       # bad dtype
     assert lib.kdn_rmsnorm(P, 1, P, 0, P, 0, 2048, 1e-6, None) == 0       # nothing to do
+    Q, R, O = P + 65536, P + 2 * 65536, P + 3 * 65536
+    assert lib.kdn_add_rmsnorm(P, Q, 1, R, 0, None, O, 4, 2048, 1e-6, None) == 1   # h_out NULL with a residual
+    assert lib.kdn_add_rmsnorm(P, Q, 1, R, 0, P, P, 4, 2048, 1e-6, None) == 1      # out aliases x / h_out
+    assert lib.kdn_add_rmsnorm(P, Q + 8, 1, R, 0, P, O, 4, 2048, 1e-6, None) == 1  # misaligned residual
+    assert lib.kdn_add_rmsnorm(P, Q, 1, R, 0, P, O, 4, 2044, 1e-6, None) == 2      # d not a multiple of 8
+    assert lib.kdn_add_rmsnorm(P, Q, 1, R, 0, P, O, 0, 2048, 1e-6, None) == 0      # nothing to do
     assert lib.kdn_swiglu(P, P, 0, 4, 6, None) == 2                        # d_ff not a multiple of 4 (fp32)
     assert lib.kdn_swiglu(None, P, 0, 4, 8, None) == 1
     assert lib.kdn_mixer_inputs(P, 1, 4, 2, 32, P, 0, P, P, P, P, P, None) == 2   # d_head must be 64
@@ -47,6 +53,30 @@ def test_rmsnorm_and_swiglu(dtype):
     gf = gu.float()
     ref = torch.nn.functional.silu(gf[:, :8192]) * gf[:, 8192:]
     assert _close(glue.swiglu_product(gu), ref, dtype)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("d", [64, 2048, 4104, 8192])
+def test_add_rmsnorm(dtype, d):
+    """h = x + r rounded to the storage dtype (bit-equal to torch's add), then RMSNorm(h); rows of
+    d <= 256 vectors per warp stay in registers, longer ones (4104, 8192; fp32 2048) are read back.
+    Weights of another dtype (fp32 weights on bf16 rows) take the element-load path."""
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(19, d, generator=g, device="cuda").to(dtype)
+    r = torch.randn(19, d, generator=g, device="cuda").to(dtype)
+    for w in ((1 + 0.1 * torch.randn(d, generator=g, device="cuda")).to(dtype),
+              1 + 0.1 * torch.randn(d, generator=g, device="cuda")):
+        h, out = glue.add_rms_norm(x, r, w, 1e-6)
+        href = x + r
+        assert torch.equal(h, href)
+        hf = href.float()
+        ref = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+        assert _close(out, ref, dtype)
+        assert _close(glue.rms_norm(x, w, 1e-6), x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True)
+                                                                          + 1e-6) * w.float(), dtype)
 
 
 @pytest.mark.gpu
