@@ -235,6 +235,37 @@ def bench_decode(dev, steps, warmup, peaks):
                          "note": f"state 128 MiB ~ L2 126 MB; peak {peaks['src']}"}}
 
 
+def bench_lift(dev, peaks, steps=10, warmup=3):
+    """The standalone feature lift (FastWalshHadamardProjection.forward -> kdn_fwht_lift) over config 1's
+    q: 16 x 65536 unit-norm vectors, bf16 in and out.  HBM bound: 128 B read + 1 KiB written per vector
+    (1.2 GB per call, larger than L2)."""
+    import torch
+
+    import kdn_b200
+
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    x = prefill_inputs(dev, 7)[0]
+    out = None
+    for _ in range(warmup):
+        out = proj(x)
+    del out
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        out = proj(x)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    n = x.numel() // DK
+    gbs = n * (DK + D) * 2 / (ms * 1e-3) / 1e9
+    return {"metric": f"standalone feature lift vectors/s ({H} x {T} vectors, d_k {DK} -> D {D}, bf16 in/out)",
+            "value": n / (ms * 1e-3), "unit": "vectors/s", "ms": ms, "steps": steps,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                         "note": f"{(DK + D) * 2} algorithmic bytes per vector; peak {peaks['src']}"}}
+
+
 RAGGED_LENS = [128, 1024, 8192, 16384]  # the reference's ragged-batch example (serving/vllm_ragged_batching.py)
 
 
@@ -575,6 +606,7 @@ def run_ours(args):
         e2e_ms = float(t.item())
 
     dec = bench_decode(dev, steps=200, warmup=5, peaks=peaks)
+    lift = bench_lift(dev, peaks)
     rag = bench_ragged(dev, steps=10, warmup=3)
     tpp = bench_tp_out_proj(dev, rank, world) if world > 1 else None
     bwd = bench_backward(dev)
@@ -642,6 +674,7 @@ def run_ours(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk,
         "decode": dec,
+        "lift": lift,
         "ragged": rag,
     }
     if tpp is not None:

@@ -6,6 +6,8 @@
     [8, 32, 16384, 64] (1 GiB of K and V), live lengths 4096..16383.
 ``python -m kdn_b200._profile_cases backward`` -- the prefill backward (exact fp32), 16 heads x 4096
     tokens, decay 1.
+``python -m kdn_b200._profile_cases lift`` -- the standalone feature lift, 4 x 65536 unit vectors, bf16 in
+    and out (32 MiB in, 256 MiB out).
 Each case runs its call three times (two warm-ups, one to capture) and exits 0.
 """
 
@@ -41,6 +43,17 @@ def decode_attn():
     torch.cuda.synchronize()
 
 
+def lift():
+    from .kernels.fwht import FastWalshHadamardProjection
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.nn.functional.normalize(torch.randn(4, 65536, 64, generator=g, device="cuda"), dim=-1).bfloat16()
+    p = FastWalshHadamardProjection().to("cuda")
+    for _ in range(3):
+        p(x)
+    torch.cuda.synchronize()
+
+
 def backward():
     from .kernels.fused_kernel_deltanet import chunked_deltanet_backward
     from .kernels.fwht import FastWalshHadamardProjection
@@ -59,5 +72,5 @@ def backward():
 
 
 if __name__ == "__main__":
-    {"tp_proj": tp_proj, "decode_attn": decode_attn, "backward": backward}[sys.argv[1]]()
+    {"tp_proj": tp_proj, "decode_attn": decode_attn, "backward": backward, "lift": lift}[sys.argv[1]]()
     print("ok")

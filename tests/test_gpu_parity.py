@@ -89,6 +89,41 @@ def test_lift_many_vectors_and_bf16(proj, consts):
     np.testing.assert_allclose(np.linalg.norm(got, axis=-1), 1.0, atol=1e-5)
 
 
+@pytest.mark.parametrize("D", [512, 128])
+def test_lift_paths_and_mixed_dtypes(kdn, D):
+    """kdn_fwht_lift through the C ABI: the lane-pair kernel (16-byte aligned rows) with a ragged last
+    group of 16 vectors, D < 512 and every input/output dtype pair, and the one-warp-per-vector kernel
+    (rows only 8-byte aligned), all against the oracle."""
+    from kdn_b200 import _lib
+
+    lib = _lib.load()
+    p = kdn.FastWalshHadamardProjection(64, D, 11).to(DEV)
+    c = oracle.make_projection_constants(64, D, 11)
+    pstruct, _phase = p.kdn_projection(torch.device(DEV))
+    rng = np.random.default_rng(4)
+    n = 16 * 37 + 5
+    x = rng.standard_normal((n, 64)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=-1, keepdims=True)
+    for xd in (torch.float32, torch.bfloat16):
+        xt = to_dev(x, xd)
+        ref = oracle.lift(xt.float().cpu().numpy(), c)
+        for od in (torch.float32, torch.bfloat16):
+            out = torch.full((n, D), float("nan"), device=DEV, dtype=od)
+            rc = lib.kdn_fwht_lift(xt.data_ptr(), _lib.dtype_code(xt), out.data_ptr(), _lib.dtype_code(out), n,
+                                   pstruct, None)
+            torch.cuda.synchronize()
+            assert rc == 0
+            tol = 2e-5 if od == torch.float32 else 1e-2
+            assert rel_err(out.float().cpu().numpy(), ref) < tol, (xd, od)
+    # 8-byte aligned (not 16): input rows start 2 floats into a padded buffer, output 2 floats in
+    xb = torch.zeros(n * 64 + 2, device=DEV)
+    xb[2:] = to_dev(x).reshape(-1)
+    ob = torch.full((n * D + 2,), float("nan"), device=DEV)
+    assert lib.kdn_fwht_lift(xb.data_ptr() + 8, 0, ob.data_ptr() + 8, 0, n, pstruct, None) == 0
+    torch.cuda.synchronize()
+    assert rel_err(ob[2:].view(n, D).cpu().numpy(), oracle.lift(x, c)) < 2e-5
+
+
 # --------------------------------------------------------------- prefill
 GOLDEN_PREFILL = ["prefill_t130_gated_s0", "prefill_t63", "prefill_t64", "prefill_t1",
                   "prefill_c32_dv128_gated", "prefill_t256_c64"]
