@@ -116,7 +116,9 @@ int kdn_fwht_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t 
   if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
   if (!aligned(x, 8) || !aligned(out, 8)) return fail(KDN_ERR_INVALID, "x/out must be 8-byte aligned");
   const kdn::ProjParams P = kdn::make_proj_params(*proj);
-  cudaError_t e = kdn::launch_lift(x, x_dtype, out, out_dtype, n, P, static_cast<cudaStream_t>(stream));
+  // the tensor-core lift needs the dense Omega exact in bf16: the same condition as the tensor-core prefill
+  const bool omega_exact = proj->D == 512 && use_tc_path(proj, 64, 64, KDN_MODE_BF16);
+  cudaError_t e = kdn::launch_lift(x, x_dtype, out, out_dtype, n, P, omega_exact, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lift launch");
   return ok();
 }
@@ -712,7 +714,10 @@ int kdn_device_error(void* stream, int* code_out) {
   int code_proj = 0;
   e = kdn::tp_proj_read_error(static_cast<cudaStream_t>(stream), &code_proj);
   if (e != cudaSuccess) return cuda_fail(e, "device error read");
-  *code_out = code ? code : (code_tc ? code_tc : (code_split ? code_split : code_proj));
+  int code_lift = 0;
+  e = kdn::lift_read_error(static_cast<cudaStream_t>(stream), &code_lift);
+  if (e != cudaSuccess) return cuda_fail(e, "device error read");
+  *code_out = code ? code : (code_tc ? code_tc : (code_split ? code_split : (code_proj ? code_proj : code_lift)));
   return ok();
 }
 

@@ -118,5 +118,6 @@ constexpr int kErrTcWaitTimeout = 2;     // fused tensor-core prefill: a bounded
 constexpr int kErrSplitWaitTimeout = 3;  // two-phase prefill: a bounded wait gave up
 constexpr int kErrDecodeWaitTimeout = 4; // decode: a bounded wait gave up
 constexpr int kErrProjWaitTimeout = 5;   // tensor-parallel projection: a bounded wait gave up
+constexpr int kErrLiftWaitTimeout = 6;   // tensor-core lift: a bounded wait gave up
 
 }  // namespace kdn

@@ -12,7 +12,8 @@ namespace kdn {
 
 // ------------------------------------------------------------------ lift.cu
 cudaError_t launch_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t n, const ProjParams& P,
-                        cudaStream_t stream);
+                        bool omega_bf16_exact, cudaStream_t stream);
+cudaError_t lift_read_error(cudaStream_t stream, int* code);
 
 // ------------------------------------------------------------ prefill paths
 struct PrefillProblem {

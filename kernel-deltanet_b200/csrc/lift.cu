@@ -16,13 +16,28 @@
 // inputs are loaded before the current group is computed.  Cosines: the argument is reduced by the
 // nearest multiple of 2 pi (Cody and Waite's method, 2 pi split in two floats), then __cosf.
 //
+// Tensor-core kernel (lift_tc_kernel; bf16 inputs, D = 512, Omega exact in bf16): the three transforms
+// of a block are one dense product x Omega^T.  Omega = H D3 H D2 H D1 / 8 has entries that are integers / 8;
+// when those are exact in bf16 (checked on the host per sign pattern) a bf16 x bf16 product with fp32
+// accumulation is exact up to the accumulation order.  A persistent CTA per SM builds Omega once
+// (64 KiB, the B operand), then per tile of 128 vectors one thread issues 16 tcgen05 MMAs into 512 TMEM
+// columns (lanes = vectors, columns = features).  Eight epilogue warps (two per TMEM lane quarter, one
+// column half each) take the cosines in place in TMEM with the sum of squares (pass 1), exchange the two
+// halves' sums through shared memory, then scale each row and write it through a swizzled per-warp
+// staging buffer as coalesced 16-byte stores (pass 2).  The next tile's inputs are loaded during the
+// epilogue.  KDN_LIFT_PATH=pair forces the CUDA-core kernel.
+//
 // Fallback (lift_kernel): one warp per vector, for inputs or outputs that are not 16-byte aligned.
 #include <cuda_fp16.h>
 
 #include <type_traits>
 
+#include <stdlib.h>
+#include <string.h>
+
 #include "kdn_internal.h"
 #include "lift.cuh"
+#include "tc_chunk.cuh"
 
 namespace kdn {
 namespace {
@@ -248,6 +263,209 @@ __global__ void __launch_bounds__(256) lift_kernel(const void* __restrict__ x, i
   }
 }
 
+// ---------------------------------------------------------------- tensor-core lift
+__device__ int g_lift_error;
+
+namespace tcl {
+constexpr int kTile = 128;                      // vectors per tile (MMA M)
+constexpr int kEpiWarps = 8;                    // 2 per TMEM lane quarter, one column half each
+constexpr int kIssuerWarp = kEpiWarps;          // warp 8 issues the MMAs
+constexpr int kThreads = 32 * (kEpiWarps + 1);
+constexpr uint32_t kWaitLimit = 1u << 24;
+// shared memory, bytes from a 1024-aligned base
+constexpr uint32_t OFF_OMG = 0;       // 64 KiB Omega (bf16, K-major SW128), slice s (features 128 s..) at 16 KiB s
+constexpr uint32_t OFF_X = 65536;     // 16 KiB input tile (bf16, K-major SW128, 128 rows x 64)
+constexpr uint32_t OFF_STG = 81920;   // 8 x 4 KiB write-back staging (32 rows x 128 B), one per epilogue warp
+constexpr uint32_t OFF_PH = 114688;   // 2 KiB phase b[512]
+constexpr uint32_t OFF_SS = 116736;   // 1 KiB sums of squares [column half][row]
+constexpr uint32_t OFF_BAR = 117760;  // 2 mbarriers + TMEM address
+constexpr uint32_t kSmem = OFF_BAR + 64 + 1024;  // + alignment slack
+}  // namespace tcl
+
+template <typename TO>
+__global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                    TO* __restrict__ out, int64_t n, ProjParams P) {
+  using namespace tcl;
+  extern __shared__ uint8_t lift_tc_raw[];
+  uint8_t* sm;
+  {
+    const uint32_t a = tc::smem_u32(lift_tc_raw);
+    sm = lift_tc_raw + ((1024u - (a & 1023u)) & 1023u);
+  }
+  const uint32_t sbase = tc::smem_u32(sm);
+  float* ph = reinterpret_cast<float*>(sm + OFF_PH);
+  float* ssx = reinterpret_cast<float*>(sm + OFF_SS);
+  uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + OFF_BAR);       // a tile's products are done
+  uint64_t* bar_ready = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 8);  // TMEM read out, next tile loaded
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 16);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t tiles = (n + kTile - 1) / kTile;
+  bool ok = true;
+
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, 512);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(bar_lift, 1);
+    tc::mbar_init(bar_ready, kEpiWarps);
+    tc::fence_mbar_init();
+  }
+  tcc::build_omega(sm + OFF_OMG, P, warp, lane, kThreads / 32);
+  for (int i = tid; i < 64 * kMaxBlocks; i += kThreads) ph[i] = P.phase[i];
+  // the 128 x 64 input tile of tile t, swizzled for the A operand (epilogue threads; rows past n read as 0)
+  auto load_tile = [&](int64_t t) {
+    const int64_t row0 = t * kTile;
+    for (int j = tid; j < kTile * 8; j += 32 * kEpiWarps) {
+      const int r = j >> 3, c = j & 7;
+      const bool in = row0 + r < n;
+      tc::cp_async16(sbase + OFF_X + tc::sw128_offset(r, 8 * c), x + (in ? (row0 + r) * kDk + 8 * c : 0),
+                     in ? 16 : 0);
+    }
+    tc::cp_async_commit();
+  };
+  if (warp < kEpiWarps && int64_t(blockIdx.x) < tiles) load_tile(blockIdx.x);
+  if (warp < kEpiWarps) tc::cp_async_wait_all();
+  tc::fence_proxy_async_smem();  // Omega (generic stores) and the first tile, for the tensor core
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot;
+
+  if (warp == kIssuerWarp) {
+    if (lane == 0) {
+      const uint32_t id = tc::idesc_bf16_f32(128, 128, false, false);
+      uint32_t pr = 0;
+      int64_t i = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+        if (i > 0) {  // the epilogue has read TMEM out and loaded this tile
+          ok &= tc::mbar_wait_bounded(bar_ready, pr, kWaitLimit);
+          pr ^= 1;
+          tc::fence_after_sync();
+        }
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+#pragma unroll
+          for (int k0 = 0; k0 < 64; k0 += 16)
+            tc::mma_ss(tmem + 128 * s, tc::smem_desc_sw128(sbase + OFF_X + 2 * k0, 16, 1024),
+                       tc::smem_desc_sw128(sbase + OFF_OMG + s * 16384 + 2 * k0, 16, 1024), id, k0 > 0);
+        tc::mma_commit(bar_lift);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3, ch = warp >> 2;  // TMEM lane quarter, column half
+    const uint32_t lane_off = uint32_t(32 * q) << 16;
+    const int row = 32 * q + lane;           // this thread's row of the tile
+    uint8_t* stg = sm + OFF_STG + warp * 4096;
+    uint32_t pl = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+      ok &= tc::mbar_wait_bounded(bar_lift, pl, kWaitLimit);
+      pl ^= 1;
+      tc::fence_after_sync();
+      const int64_t next = t + gridDim.x;
+      if (next < tiles) load_tile(next);  // the products of this tile have read the input tile
+      // pass 1: cos(tau^-1 z + b) in place, sum of squares over this half's 256 features
+      float ss = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint32_t col = 256 * ch + 32 * cc;
+        float z[32];
+        tc::tmem_ld32(tmem + lane_off + col, z);
+        tc::tmem_ld_wait();
+        const float4* b4 = reinterpret_cast<const float4*>(ph + col);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 b = b4[j >> 2];
+          z[j] = cos_reduced(fmaf(z[j], P.tau_inv, b.x));
+          z[j + 1] = cos_reduced(fmaf(z[j + 1], P.tau_inv, b.y));
+          z[j + 2] = cos_reduced(fmaf(z[j + 2], P.tau_inv, b.z));
+          z[j + 3] = cos_reduced(fmaf(z[j + 3], P.tau_inv, b.w));
+          ss = fmaf(z[j], z[j], fmaf(z[j + 1], z[j + 1], fmaf(z[j + 2], z[j + 2], fmaf(z[j + 3], z[j + 3], ss))));
+        }
+        tc::tmem_st32(tmem + lane_off + col, z);
+      }
+      tc::tmem_st_wait();
+      ssx[128 * ch + row] = ss;
+      tc::named_bar_sync(1, 32 * kEpiWarps);
+      // phi = amp cos / (amp ||cos|| + 1e-8)
+      const float scale = P.amp / fmaf(P.amp, sqrtf(ssx[row] + ssx[128 + row]), 1e-8f);
+      // pass 2: 128 output bytes of each row at a time (64 bf16 or 32 fp32 columns), scaled and transposed
+      // through the staging (row r's 16-byte chunk c at c ^ (r & 7)) into whole-row 128-byte stores
+      constexpr int kCols = 128 / int(sizeof(TO));
+      const int64_t grow0 = t * kTile + 32 * q;  // output row of lane 0 of this warp
+#pragma unroll 1
+      for (int blk = 0; blk < 256 / kCols; ++blk) {
+        const uint32_t col = 256 * ch + kCols * blk;
+        if constexpr (sizeof(TO) == 2) {
+          float a[32], b[32];
+          tc::tmem_ld32(tmem + lane_off + col, a);
+          tc::tmem_ld32(tmem + lane_off + col + 32, b);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float* v = c < 4 ? a + 8 * c : b + 8 * (c - 4);
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * e] * scale, v[2 * e + 1] * scale);
+              w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        } else {
+          float a[32];
+          tc::tmem_ld32(tmem + lane_off + col, a);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                make_float4(a[4 * c] * scale, a[4 * c + 1] * scale, a[4 * c + 2] * scale, a[4 * c + 3] * scale);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int jj = lane + 32 * k, r = jj >> 3, c = jj & 7;
+          const uint4 u = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+          if (grow0 + r < n)
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (grow0 + r) * 512 + col) + 16 * c) = u;
+        }
+        __syncwarp();  // the staging is rewritten by the next block
+      }
+      if (next < tiles) {  // TMEM read out and the next tile in shared memory: hand both to the issuer
+        tc::cp_async_wait_all();
+        tc::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_ready);
+      }
+    }
+  }
+  if (!ok) record_device_error(&g_lift_error, kErrLiftWaitTimeout);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 512);
+}
+
+template <typename TO>
+cudaError_t launch_tc(const void* x, void* out, int64_t n, const ProjParams& P, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(lift_tc_kernel<TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tcl::kSmem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = (n + tcl::kTile - 1) / tcl::kTile;
+  const int64_t blocks = tiles < sms ? tiles : sms;  // persistent: one CTA per SM
+  lift_tc_kernel<TO><<<dim3(unsigned(blocks)), tcl::kThreads, tcl::kSmem, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<TO*>(out), n, P);
+  return cudaGetLastError();
+}
+
 template <typename TI, typename TO>
 cudaError_t launch_pair(const void* x, void* out, int64_t n, const ProjParams& P, cudaStream_t stream) {
   constexpr int kLiftWarps = LiftStage<TO>::kWarps;
@@ -274,9 +492,14 @@ cudaError_t launch_pair(const void* x, void* out, int64_t n, const ProjParams& P
 }  // namespace
 
 cudaError_t launch_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t n, const ProjParams& P,
-                        cudaStream_t stream) {
+                        bool omega_bf16_exact, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   const bool a16 = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const char* path = getenv("KDN_LIFT_PATH");
+  const bool force_pair = path && strcmp(path, "pair") == 0;
+  if (a16 && omega_bf16_exact && P.M == kMaxBlocks && x_dtype == KDN_DTYPE_BF16 && !force_pair)
+    return out_dtype == KDN_DTYPE_BF16 ? launch_tc<__nv_bfloat16>(x, out, n, P, stream)
+                                       : launch_tc<float>(x, out, n, P, stream);
   if (a16 && P.M >= 1 && P.M <= kMaxBlocks) {
     const bool ib = x_dtype == KDN_DTYPE_BF16, ob = out_dtype == KDN_DTYPE_BF16;
     if (ib && ob) return launch_pair<__nv_bfloat16, __nv_bfloat16>(x, out, n, P, stream);
@@ -289,6 +512,21 @@ cudaError_t launch_lift(const void* x, int x_dtype, void* out, int out_dtype, in
   if (blocks > 148 * 16) blocks = 148 * 16;
   lift_kernel<<<dim3(unsigned(blocks)), threads, 0, stream>>>(x, x_dtype, out, out_dtype, n, P);
   return cudaGetLastError();
+}
+
+cudaError_t lift_read_error(cudaStream_t stream, int* code) {
+  int h = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&h, g_lift_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return e;
+  if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return e;
+  if (h != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_lift_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return e;
+    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return e;
+  }
+  *code = h;
+  return cudaSuccess;
 }
 
 }  // namespace kdn

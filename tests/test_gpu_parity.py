@@ -89,19 +89,23 @@ def test_lift_many_vectors_and_bf16(proj, consts):
     np.testing.assert_allclose(np.linalg.norm(got, axis=-1), 1.0, atol=1e-5)
 
 
-@pytest.mark.parametrize("D", [512, 128])
-def test_lift_paths_and_mixed_dtypes(kdn, D):
-    """kdn_fwht_lift through the C ABI: the lane-pair kernel (16-byte aligned rows) with a ragged last
-    group of 16 vectors, D < 512 and every input/output dtype pair, and the one-warp-per-vector kernel
-    (rows only 8-byte aligned), all against the oracle."""
+@pytest.mark.parametrize("D,seed", [(512, 42), (128, 11)])
+@pytest.mark.parametrize("path", ["", "pair"])
+def test_lift_paths_and_mixed_dtypes(kdn, monkeypatch, D, seed, path):
+    """kdn_fwht_lift through the C ABI on every input/output dtype pair, with a ragged last tile:
+    bf16 inputs at D = 512 with a bf16-exact Omega (seed 42) take the tensor-core kernel unless
+    KDN_LIFT_PATH=pair; the rest take the lane-pair kernel; rows only 8-byte aligned take the
+    one-warp kernel.  All against the oracle."""
     from kdn_b200 import _lib
+    from kdn_b200.serving.vllm_kernel_deltanet_op import device_error
 
+    monkeypatch.setenv("KDN_LIFT_PATH", path)
     lib = _lib.load()
-    p = kdn.FastWalshHadamardProjection(64, D, 11).to(DEV)
-    c = oracle.make_projection_constants(64, D, 11)
+    p = kdn.FastWalshHadamardProjection(64, D, seed).to(DEV)
+    c = oracle.make_projection_constants(64, D, seed)
     pstruct, _phase = p.kdn_projection(torch.device(DEV))
     rng = np.random.default_rng(4)
-    n = 16 * 37 + 5
+    n = 128 * 9 + 37  # also 16 * 74 + 5: a ragged last group for both kernels
     x = rng.standard_normal((n, 64)).astype(np.float32)
     x /= np.linalg.norm(x, axis=-1, keepdims=True)
     for xd in (torch.float32, torch.bfloat16):
@@ -115,6 +119,7 @@ def test_lift_paths_and_mixed_dtypes(kdn, D):
             assert rc == 0
             tol = 2e-5 if od == torch.float32 else 1e-2
             assert rel_err(out.float().cpu().numpy(), ref) < tol, (xd, od)
+    assert device_error(DEV) == 0
     # 8-byte aligned (not 16): input rows start 2 floats into a padded buffer, output 2 floats in
     xb = torch.zeros(n * 64 + 2, device=DEV)
     xb[2:] = to_dev(x).reshape(-1)
@@ -122,6 +127,20 @@ def test_lift_paths_and_mixed_dtypes(kdn, D):
     assert lib.kdn_fwht_lift(xb.data_ptr() + 8, 0, ob.data_ptr() + 8, 0, n, pstruct, None) == 0
     torch.cuda.synchronize()
     assert rel_err(ob[2:].view(n, D).cpu().numpy(), oracle.lift(x, c)) < 2e-5
+
+
+def test_lift_tensor_core_path_agrees(kdn, proj, monkeypatch):
+    """The default projection's Omega is bf16-exact, so bf16 inputs take the tensor-core lift: on a batch
+    of several tiles per CTA it agrees with the lane-pair kernel element by element to within one bf16 ulp."""
+    g = torch.Generator(device=DEV).manual_seed(9)
+    xb = torch.nn.functional.normalize(torch.randn(148 * 128 * 3 + 77, 64, generator=g, device=DEV), dim=-1).bfloat16()
+    monkeypatch.setenv("KDN_LIFT_PATH", "")
+    a = proj(xb).float()
+    monkeypatch.setenv("KDN_LIFT_PATH", "pair")
+    b = proj(xb).float()
+    # at most one bf16 ulp apart (the two kernels round different fp32 values; ulp <= 2^-7 |x|)
+    assert bool(((a - b).abs() <= 2.0 ** -7 * torch.maximum(a.abs(), b.abs()) + 1e-6).all())
+    np.testing.assert_allclose(a.norm(dim=-1).cpu().numpy(), 1.0, atol=1e-2)
 
 
 # --------------------------------------------------------------- prefill
