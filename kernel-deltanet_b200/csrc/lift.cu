@@ -22,10 +22,12 @@
 // accumulation is exact up to the accumulation order.  A persistent CTA per SM builds Omega once
 // (64 KiB, the B operand), then per tile of 128 vectors one thread issues 16 tcgen05 MMAs into 512 TMEM
 // columns (lanes = vectors, columns = features).  Eight epilogue warps (two per TMEM lane quarter, one
-// column half each) take the cosines in place in TMEM with the sum of squares (pass 1), exchange the two
-// halves' sums through shared memory, then scale each row and write it through a swizzled per-warp
-// staging buffer as coalesced 16-byte stores (pass 2).  The next tile's inputs are loaded during the
-// epilogue.  KDN_LIFT_PATH=pair forces the CUDA-core kernel.
+// column half each) take the cosines with the sum of squares (pass 1) and exchange the two halves' sums
+// through shared memory, then scale each row and write it as coalesced 16-byte stores (pass 2).  For bf16
+// outputs pass 1 stages the cosines in shared memory as fp16, so TMEM goes back to the issuer before pass 2
+// and the next tile's products overlap the write-back; for fp32 outputs the cosines stay in TMEM (written
+// back in place) and pass 2 goes through a per-warp staging buffer.  The next tile's inputs are loaded
+// during the epilogue.  KDN_LIFT_PATH=pair forces the CUDA-core kernel.
 //
 // Fallback (lift_kernel): one warp per vector, for inputs or outputs that are not 16-byte aligned.
 #include <cuda_fp16.h>
@@ -275,10 +277,12 @@ constexpr uint32_t kWaitLimit = 1u << 24;
 // shared memory, bytes from a 1024-aligned base
 constexpr uint32_t OFF_OMG = 0;       // 64 KiB Omega (bf16, K-major SW128), slice s (features 128 s..) at 16 KiB s
 constexpr uint32_t OFF_X = 65536;     // 16 KiB input tile (bf16, K-major SW128, 128 rows x 64)
-constexpr uint32_t OFF_STG = 81920;   // 8 x 4 KiB write-back staging (32 rows x 128 B), one per epilogue warp
-constexpr uint32_t OFF_PH = 114688;   // 2 KiB phase b[512]
-constexpr uint32_t OFF_SS = 116736;   // 1 KiB sums of squares [column half][row]
-constexpr uint32_t OFF_BAR = 117760;  // 2 mbarriers + TMEM address
+constexpr uint32_t OFF_STG = 81920;   // fp32 outputs: 8 x 4 KiB write-back staging (32 rows x 128 B), one per
+                                      // epilogue warp; bf16 outputs: 128 KiB of fp16 cosines (128 rows x 1 KiB,
+                                      // row r's 16-byte chunk c at c ^ (r & 7))
+constexpr uint32_t OFF_PH = 212992;   // 2 KiB phase b[512]
+constexpr uint32_t OFF_SS = 215040;   // 1 KiB sums of squares [column half][row]
+constexpr uint32_t OFF_BAR = 216064;  // 2 mbarriers + TMEM address
 constexpr uint32_t kSmem = OFF_BAR + 64 + 1024;  // + alignment slack
 }  // namespace tcl
 
@@ -365,55 +369,101 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
       tc::fence_after_sync();
       const int64_t next = t + gridDim.x;
       if (next < tiles) load_tile(next);  // the products of this tile have read the input tile
-      // pass 1: cos(tau^-1 z + b) in place, sum of squares over this half's 256 features
-      float ss = 0.f;
+      if constexpr (sizeof(TO) == 2) {
+        // bf16 outputs. Pass 1: cos(tau^-1 z + b) and the sum of squares over this half's 256 features, the
+        // cosines staged as fp16 (2^-12 rounding, inside the output's 2^-9) so that TMEM can go back to the
+        // issuer before the write-back: the next tile's products overlap pass 2.
+        uint8_t* cs = sm + OFF_STG;
+        float ss = 0.f;
 #pragma unroll 1
-      for (int cc = 0; cc < 8; ++cc) {
-        const uint32_t col = 256 * ch + 32 * cc;
-        float z[32];
-        tc::tmem_ld32(tmem + lane_off + col, z);
-        tc::tmem_ld_wait();
-        const float4* b4 = reinterpret_cast<const float4*>(ph + col);
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 b = b4[j >> 2];
-          z[j] = cos_reduced(fmaf(z[j], P.tau_inv, b.x));
-          z[j + 1] = cos_reduced(fmaf(z[j + 1], P.tau_inv, b.y));
-          z[j + 2] = cos_reduced(fmaf(z[j + 2], P.tau_inv, b.z));
-          z[j + 3] = cos_reduced(fmaf(z[j + 3], P.tau_inv, b.w));
-          ss = fmaf(z[j], z[j], fmaf(z[j + 1], z[j + 1], fmaf(z[j + 2], z[j + 2], fmaf(z[j + 3], z[j + 3], ss))));
-        }
-        tc::tmem_st32(tmem + lane_off + col, z);
-      }
-      tc::tmem_st_wait();
-      ssx[128 * ch + row] = ss;
-      tc::named_bar_sync(1, 32 * kEpiWarps);
-      // phi = amp cos / (amp ||cos|| + 1e-8)
-      const float scale = P.amp / fmaf(P.amp, sqrtf(ssx[row] + ssx[128 + row]), 1e-8f);
-      // pass 2: 128 output bytes of each row at a time (64 bf16 or 32 fp32 columns), scaled and transposed
-      // through the staging (row r's 16-byte chunk c at c ^ (r & 7)) into whole-row 128-byte stores
-      constexpr int kCols = 128 / int(sizeof(TO));
-      const int64_t grow0 = t * kTile + 32 * q;  // output row of lane 0 of this warp
-#pragma unroll 1
-      for (int blk = 0; blk < 256 / kCols; ++blk) {
-        const uint32_t col = 256 * ch + kCols * blk;
-        if constexpr (sizeof(TO) == 2) {
-          float a[32], b[32];
-          tc::tmem_ld32(tmem + lane_off + col, a);
-          tc::tmem_ld32(tmem + lane_off + col + 32, b);
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint32_t col = 256 * ch + 32 * cc;
+          float z[32];
+          tc::tmem_ld32(tmem + lane_off + col, z);
           tc::tmem_ld_wait();
+          const float4* b4 = reinterpret_cast<const float4*>(ph + col);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const float* v = c < 4 ? a + 8 * c : b + 8 * (c - 4);
+          for (int j = 0; j < 32; j += 4) {
+            const float4 b = b4[j >> 2];
+            z[j] = cos_reduced(fmaf(z[j], P.tau_inv, b.x));
+            z[j + 1] = cos_reduced(fmaf(z[j + 1], P.tau_inv, b.y));
+            z[j + 2] = cos_reduced(fmaf(z[j + 2], P.tau_inv, b.z));
+            z[j + 3] = cos_reduced(fmaf(z[j + 3], P.tau_inv, b.w));
+            ss = fmaf(z[j], z[j], fmaf(z[j + 1], z[j + 1], fmaf(z[j + 2], z[j + 2], fmaf(z[j + 3], z[j + 3], ss))));
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {  // chunk (col / 8 + k) of this thread's row: features col + 8k ..
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * e] * scale, v[2 * e + 1] * scale);
+              const __half2 h2 = __floats2half2_rn(z[8 * k + 2 * e], z[8 * k + 2 * e + 1]);
               w[e] = *reinterpret_cast<const uint32_t*>(&h2);
             }
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            const int c = int(col >> 3) + k;
+            *reinterpret_cast<uint4*>(cs + row * 1024 + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
-        } else {
+        }
+        ssx[128 * ch + row] = ss;
+        tc::named_bar_sync(1, 32 * kEpiWarps);
+        // phi = amp cos / (amp ||cos|| + 1e-8)
+        const float scale = P.amp / fmaf(P.amp, sqrtf(ssx[row] + ssx[128 + row]), 1e-8f);
+        if (next < tiles) {  // every warp has read TMEM and its scale; the next tile is in shared memory
+          tc::cp_async_wait_all();
+          tc::fence_proxy_async_smem();
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(bar_ready);
+        }
+        // pass 2: per row of this warp's quarter, its half's 512 output bytes as one coalesced store
+        const int64_t grow0 = t * kTile + 32 * q;
+#pragma unroll 1
+        for (int k = 0; k < 32; ++k) {
+          const float sc = __shfl_sync(0xffffffffu, scale, k);
+          const int r = 32 * q + k, c = 32 * ch + lane;
+          const uint4 u = *reinterpret_cast<const uint4*>(cs + r * 1024 + ((c ^ (r & 7)) << 4));
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+            o[e] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          if (grow0 + k < n) *reinterpret_cast<uint4*>(out + (grow0 + k) * 512 + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        __syncwarp();  // this warp's staging rows are rewritten by its next tile
+      } else {
+        // fp32 outputs. Pass 1: cos(tau^-1 z + b) in place in TMEM, sum of squares over this half's 256 features
+        float ss = 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint32_t col = 256 * ch + 32 * cc;
+          float z[32];
+          tc::tmem_ld32(tmem + lane_off + col, z);
+          tc::tmem_ld_wait();
+          const float4* b4 = reinterpret_cast<const float4*>(ph + col);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 b = b4[j >> 2];
+            z[j] = cos_reduced(fmaf(z[j], P.tau_inv, b.x));
+            z[j + 1] = cos_reduced(fmaf(z[j + 1], P.tau_inv, b.y));
+            z[j + 2] = cos_reduced(fmaf(z[j + 2], P.tau_inv, b.z));
+            z[j + 3] = cos_reduced(fmaf(z[j + 3], P.tau_inv, b.w));
+            ss = fmaf(z[j], z[j], fmaf(z[j + 1], z[j + 1], fmaf(z[j + 2], z[j + 2], fmaf(z[j + 3], z[j + 3], ss))));
+          }
+          tc::tmem_st32(tmem + lane_off + col, z);
+        }
+        tc::tmem_st_wait();
+        ssx[128 * ch + row] = ss;
+        tc::named_bar_sync(1, 32 * kEpiWarps);
+        // phi = amp cos / (amp ||cos|| + 1e-8)
+        const float scale = P.amp / fmaf(P.amp, sqrtf(ssx[row] + ssx[128 + row]), 1e-8f);
+        // pass 2: 128 output bytes (32 fp32 columns) of each row at a time, scaled and transposed through the
+        // staging (row r's 16-byte chunk c at c ^ (r & 7)) into whole-row 128-byte stores
+        const int64_t grow0 = t * kTile + 32 * q;  // output row of lane 0 of this warp
+#pragma unroll 1
+        for (int blk = 0; blk < 8; ++blk) {
+          const uint32_t col = 256 * ch + 32 * blk;
           float a[32];
           tc::tmem_ld32(tmem + lane_off + col, a);
           tc::tmem_ld_wait();
@@ -421,23 +471,23 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
           for (int c = 0; c < 8; ++c)
             *reinterpret_cast<float4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
                 make_float4(a[4 * c] * scale, a[4 * c + 1] * scale, a[4 * c + 2] * scale, a[4 * c + 3] * scale);
-        }
-        __syncwarp();
+          __syncwarp();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int jj = lane + 32 * k, r = jj >> 3, c = jj & 7;
-          const uint4 u = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
-          if (grow0 + r < n)
-            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (grow0 + r) * 512 + col) + 16 * c) = u;
+          for (int k = 0; k < 8; ++k) {
+            const int jj = lane + 32 * k, r = jj >> 3, c = jj & 7;
+            const uint4 u = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+            if (grow0 + r < n)
+              *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (grow0 + r) * 512 + col) + 16 * c) = u;
+          }
+          __syncwarp();  // the staging is rewritten by the next block
         }
-        __syncwarp();  // the staging is rewritten by the next block
-      }
-      if (next < tiles) {  // TMEM read out and the next tile in shared memory: hand both to the issuer
-        tc::cp_async_wait_all();
-        tc::fence_proxy_async_smem();
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(bar_ready);
+        if (next < tiles) {  // TMEM read out and the next tile in shared memory: hand both to the issuer
+          tc::cp_async_wait_all();
+          tc::fence_proxy_async_smem();
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(bar_ready);
+        }
       }
     }
   }
