@@ -82,6 +82,9 @@ const char* kdn_last_error(void);
  * x: [n, d_k] (x_dtype), out: [n, D] (out_dtype).
  * Replaces FastWalshHadamardProjection.forward, kernels/fwht.py:113-130
  * (and the pybind fwht_forward of kernels/fwht_cuda.cpp:8-30).
+ * bf16 inputs with D = 512, 16-byte aligned x and out, and an Omega exact in bf16 run on the
+ * tensor cores; other cases on CUDA cores (environment KDN_LIFT_PATH=pair forces the CUDA-core
+ * kernel).  A tensor-core wait that gives up is reported by kdn_device_error (code 6).
  */
 int kdn_fwht_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t n,
                   const kdn_projection* proj, void* stream);
@@ -376,8 +379,10 @@ int kdn_fork_state(void* states, int64_t num_slots, int64_t bytes_per_slot,
 
 /*
  * Read and clear the device-side error word of the current device (written by
- * kernels whose bounds checks skipped a bad index).  Synchronises `stream`.
- * *code_out = 0 when nothing was recorded.
+ * kernels whose bounds checks skipped a bad index, or whose bounded waits gave up).
+ * Synchronises `stream`.  *code_out = 0 when nothing was recorded; otherwise 1 = a slot,
+ * length or offset out of range, 2 = fused tensor-core prefill wait, 3 = two-phase prefill
+ * wait, 4 = decode wait, 5 = tensor-parallel projection wait, 6 = tensor-core lift wait.
  */
 int kdn_device_error(void* stream, int* code_out);
 
