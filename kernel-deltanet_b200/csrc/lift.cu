@@ -265,6 +265,19 @@ __global__ void __launch_bounds__(256) lift_kernel(const void* __restrict__ x, i
   }
 }
 
+// Raise Kernel's dynamic shared-memory limit to `bytes` on device `dev`.  The attribute is held per
+// function and device, so it is set once for each device a kernel runs on (one table per kernel; devices
+// past the table: on every call).
+template <auto Kernel>
+cudaError_t allow_smem(int bytes, int dev) {
+  constexpr int kDevs = 64;
+  static bool done[kDevs] = {};
+  if (dev >= 0 && dev < kDevs && done[dev]) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < kDevs) done[dev] = true;
+  return e;
+}
+
 // ---------------------------------------------------------------- tensor-core lift
 __device__ int g_lift_error;
 
@@ -499,16 +512,12 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
 
 template <typename TO>
 cudaError_t launch_tc(const void* x, void* out, int64_t n, const ProjParams& P, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(lift_tc_kernel<TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(tcl::kSmem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  int sms = 148;
   int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if ((e = allow_smem<lift_tc_kernel<TO>>(int(tcl::kSmem), dev)) != cudaSuccess) return e;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t tiles = (n + tcl::kTile - 1) / tcl::kTile;
   const int64_t blocks = tiles < sms ? tiles : sms;  // persistent: one CTA per SM
   lift_tc_kernel<TO><<<dim3(unsigned(blocks)), tcl::kThreads, tcl::kSmem, stream>>>(
@@ -521,16 +530,12 @@ cudaError_t launch_pair(const void* x, void* out, int64_t n, const ProjParams& P
   constexpr int kLiftWarps = LiftStage<TO>::kWarps;
   constexpr size_t kLiftSmem = size_t(kLiftWarps) * kStageElems * sizeof(typename LiftStage<TO>::S);
   static_assert(kLiftWarps <= kMaxLiftWarps, "lift warps exceed the scale table");
-  static bool configured = false;  // the attribute is per function; setting it twice is harmless
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(lift_pair_kernel<TI, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               int(kLiftSmem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  int sms = 148;
   int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if ((e = allow_smem<lift_pair_kernel<TI, TO>>(int(kLiftSmem), dev)) != cudaSuccess) return e;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t groups = (n + kGroupVecs - 1) / kGroupVecs;
   int64_t blocks = (groups + kLiftWarps - 1) / kLiftWarps;
   if (blocks > sms) blocks = sms;  // persistent: one CTA per SM
