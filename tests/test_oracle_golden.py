@@ -48,6 +48,19 @@ def test_omega_blocks_are_scaled_orthogonal():
         np.testing.assert_allclose(blk @ blk.T, 4096.0 * np.eye(64), atol=1e-9)
 
 
+@pytest.mark.parametrize("seed", [42, 7, 11, 0])
+def test_omega_is_exact_in_bf16(seed):
+    """The tensor-core lift and prefill multiply by Omega in bf16, which is exact only when every entry
+    (an integer / 8) has at most 8 significant bits; the library checks this per sign pattern and falls
+    back to CUDA cores otherwise.  The reference's default seed and the seeds the tests use pass."""
+    import torch
+
+    om = oracle.build_omega(oracle.make_projection_constants(64, 512, seed))
+    np.testing.assert_array_equal(8 * om, np.round(8 * om))
+    om32 = om.astype(np.float32)
+    np.testing.assert_array_equal(torch.from_numpy(om32).bfloat16().float().numpy(), om32)
+
+
 NAMES = ["prefill_t130_gated_s0", "prefill_t63", "prefill_t64", "prefill_t1",
          "prefill_c32_dv128_gated", "prefill_t256_c64"]
 
