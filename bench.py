@@ -158,81 +158,197 @@ def prefill_inputs(dev, seed, n_heads=H, seq=T):
     return q.bfloat16(), k.bfloat16(), v.bfloat16(), beta
 
 
-def cpu_baseline(seq_sample: int):
-    """The numpy port of the reference path on the host cores (bounded sample)."""
-    import numpy as np
+def cpu_inputs(n_heads: int, seq: int, seed: int = 0):
+    """Seeded config-1 inputs on the host (float32): q, k unit vectors, v Gaussian, beta = sigmoid."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    q = torch.nn.functional.normalize(torch.randn(n_heads, seq, DK, generator=g), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(n_heads, seq, DK, generator=g), dim=-1)
+    v = torch.randn(n_heads, seq, DV, generator=g)
+    beta = torch.sigmoid(torch.randn(n_heads, seq, generator=g))
+    return q, k, v, beta
+
+
+def cpu_baseline(seq_sample: int, inputs=None):
+    """The reference's CPU PyTorch prefill (fused_chunked_deltanet_forward with the dense-Omega lift,
+    restated in torch: oracle/torch_chunked.py) on all host cores, one config-1 sequence of
+    `seq_sample` tokens x 16 heads in float32."""
+    import torch
 
     import oracle
+    from oracle.torch_chunked import TorchProjection, chunked_forward
 
-    c = oracle.make_projection_constants()
-    rng = np.random.default_rng(0)
-    q = rng.standard_normal((H, seq_sample, DK)).astype(np.float32)
-    k = rng.standard_normal((H, seq_sample, DK)).astype(np.float32)
-    q /= np.linalg.norm(q, axis=-1, keepdims=True)
-    k /= np.linalg.norm(k, axis=-1, keepdims=True)
-    v = rng.standard_normal((H, seq_sample, DV)).astype(np.float32)
-    beta = (1 / (1 + np.exp(-rng.standard_normal((H, seq_sample))))).astype(np.float32)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    proj = TorchProjection(oracle.make_projection_constants())
+    q, k, v, beta = inputs if inputs is not None else cpu_inputs(H, seq_sample)
     t0 = time.perf_counter()
-    oracle.chunked_deltanet_forward(q, k, v, beta, None, c, C, None, np.float32)
+    with torch.no_grad():
+        chunked_forward(q, k, v, beta, None, proj, C)
     el = time.perf_counter() - t0
-    return {"value": B * seq_sample / el, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"B=1 H={H} T={seq_sample} (fp32 numpy port of kernels/fused_kernel_deltanet.py, "
-                      f"{os.cpu_count()} host threads), {el:.2f} s"}
+    return {"value": B * seq_sample / el, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"B=1 H={H} T={seq_sample}{' (config 1 in full)' if seq_sample == T else ''}: the "
+                      f"reference's CPU torch path (kernels/fused_kernel_deltanet.py:31-155 with the dense lift "
+                      f"of kernels/fwht.py:113-130, restated in oracle/torch_chunked.py), fp32, "
+                      f"{torch.get_num_threads()} host threads, {el:.2f} s",
+            "seconds": el}
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU PyTorch path on the host cores, config 1 (B=1, H=16,
+    T=65536) per step; if one step takes longer than 12 s the later steps time the first half of the
+    sequence instead (the path is linear in T, so tokens/s is unchanged), keeping the run bounded."""
     rank, world, _ = dist_init("gloo")
     if rank != 0:
         return
     seq = args.ref_seq
-    vals = []
+    inputs = cpu_inputs(H, seq)
+    vals, samples = [], []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(seq)
+        r = cpu_baseline(seq, inputs)
         if i >= args.warmup:
             vals.append(r["value"])
+            samples.append(seq)
+        if r["seconds"] > 12.0 and seq > 4096:
+            seq //= 2
+            inputs = tuple(x[:, :seq].contiguous() for x in inputs)
     v = statistics.median(vals)
     r["value"] = v
+    r["sample"] += f"; timed steps over T = {sorted(set(samples))}"
+    r.pop("seconds", None)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * B * seq / v,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * B * T / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"config1 prefill sample B=1 H={H} T={seq} of T=65536, d_k=64->D=512, d_v=64, "
-                                   f"C=64 (CPU, host cores)", "global_batch": 1, "seq_len": seq,
-                       "parallelism": "host threads"},
+            "config": {"workload": f"config1 prefill: B=1 seq, H={H}, T={T}, d_k={DK}->D={D}, d_v={DV}, C={C} "
+                                   f"(CPU, host cores; ms_per_step scaled to T={T})", "global_batch": 1,
+                       "seq_len": T, "heads": H, "parallelism": f"{r['cores']} host threads"},
             "cpu_baseline": r,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def bench_decode(dev, steps, warmup, peaks):
+def bench_decode(dev, steps, warmup, peaks, rank=0, world=1):
+    """Config 3: 64 streams x 16 heads, fp32 state, one token per stream per step, the streams
+    sharded over the ranks (64 / world each, no communication).  A step is one token on every stream;
+    steps/s = 1 / the slowest rank's step time."""
     import torch
 
     import kdn_b200
+    from kdn_b200.distributed import max_over_ranks, shard_range
 
+    lo, hi = shard_range(DEC_STREAMS, rank, world)
+    ns = hi - lo
     proj = kdn_b200.FastWalshHadamardProjection().to(dev)
-    g = torch.Generator(device=dev).manual_seed(5)
-    states = 0.02 * torch.randn(DEC_STREAMS, DEC_H, DV, D, generator=g, device=dev)
-    qs = torch.nn.functional.normalize(torch.randn(steps + warmup, DEC_STREAMS, DEC_H, DK, generator=g, device=dev), dim=-1)
-    ks = torch.nn.functional.normalize(torch.randn(steps + warmup, DEC_STREAMS, DEC_H, DK, generator=g, device=dev), dim=-1)
-    vs = torch.randn(steps + warmup, DEC_STREAMS, DEC_H, DV, generator=g, device=dev)
-    bs = torch.sigmoid(torch.randn(steps + warmup, DEC_STREAMS, DEC_H, generator=g, device=dev))
-    slots = torch.arange(DEC_STREAMS, device=dev, dtype=torch.int64)
-    out = torch.empty(DEC_STREAMS, DEC_H, DV, device=dev)
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    states = 0.02 * torch.randn(ns, DEC_H, DV, D, generator=g, device=dev)
+    n_in = min(steps + warmup, 64)  # token inputs cycle through 64 pre-drawn steps
+    qs = torch.nn.functional.normalize(torch.randn(n_in, ns, DEC_H, DK, generator=g, device=dev), dim=-1)
+    ks = torch.nn.functional.normalize(torch.randn(n_in, ns, DEC_H, DK, generator=g, device=dev), dim=-1)
+    vs = torch.randn(n_in, ns, DEC_H, DV, generator=g, device=dev)
+    bs = torch.sigmoid(torch.randn(n_in, ns, DEC_H, generator=g, device=dev))
+    slots = torch.arange(ns, device=dev, dtype=torch.int64)
+    out = torch.empty(ns, DEC_H, DV, device=dev)
+    step = lambda i: kdn_b200.hybrid_recurrent_forward(qs[i % n_in], ks[i % n_in], vs[i % n_in], bs[i % n_in], None,
+                                                       states, slots, out, fwht_proj=proj)
     for i in range(warmup):
-        kdn_b200.hybrid_recurrent_forward(qs[i], ks[i], vs[i], bs[i], None, states, slots, out, fwht_proj=proj)
+        step(i)
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(warmup, warmup + steps):
-        kdn_b200.hybrid_recurrent_forward(qs[i], ks[i], vs[i], bs[i], None, states, slots, out, fwht_proj=proj)
+        step(i)
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, device=dev)
     gbs = DEC_STREAMS * DEC_H * DEC_BYTES_PER_HEAD / (ms * 1e-3) / 1e9
-    return {"metric": "decode steps/s (64 streams x 16 heads, fp32 state 128 MiB)", "value": 1e3 / ms,
-            "unit": "steps/s", "ms_per_step": ms, "steps": steps,
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / peaks["hbm_gbs"], "traffic": None,
-                         "note": f"state 128 MiB ~ L2 126 MB; peak {peaks['src']}"}}
+    per_gpu_state = ns * DEC_H * DV * D * 4
+    return {"metric": f"decode steps/s (64 streams x 16 heads, fp32 state 128 MiB, {ns} streams per GPU)",
+            "value": 1e3 / ms, "unit": "steps/s", "ms_per_step": ms, "steps": steps, "streams_per_gpu": ns,
+            "scaling": "strong",
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / world / peaks["hbm_gbs"], "traffic": None,
+                         "note": f"per GPU; state {per_gpu_state / 2**20:.0f} MiB per GPU "
+                                 f"({'fits in' if per_gpu_state < 120e6 else 'about'} the 126 MB L2); "
+                                 f"peak {peaks['src']}"}}
+
+
+# config 2 (BASELINE.json configs[2]): B=32 x H=16 = 512 independent scans of T=16384, sharded over the ranks
+CFG2_SCANS, CFG2_T = 512, 16384
+
+
+def bench_config2(dev, peaks, rank=0, world=1, steps=5, warmup=2):
+    """Config 2: 512 (batch, head) scans x 16384 tokens, bf16 inputs, fp32 state; rank r takes a
+    contiguous share of the scans (strong scaling, no communication).  tokens/s counts B*T = 32 x 16384
+    tokens per step over the slowest rank's time; the roofline is the rank's prefill kernel against its
+    share of the algorithmic FLOPs."""
+    import torch
+
+    import kdn_b200
+    from kdn_b200.distributed import max_over_ranks, shard_range
+
+    lo, hi = shard_range(CFG2_SCANS, rank, world)
+    n = hi - lo
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    q, k, v, beta = prefill_inputs(dev, 2000 + rank, n_heads=n, seq=CFG2_T)
+    y = torch.empty(n, CFG2_T, DV, device=dev, dtype=torch.bfloat16)
+    S = torch.empty(n, DV, D, device=dev, dtype=torch.float32)
+    lib = kdn_b200.load()
+    pstruct, _ = proj.kdn_projection(dev)
+    ws_bytes = int(lib.kdn_chunked_prefill_workspace_size(n, CFG2_T, DV, C, pstruct, 1))
+    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+    step = lambda: kdn_b200.fused_chunked_deltanet_forward(q, k, v, beta, None, proj, C, mode="bf16", workspace=ws,
+                                                           out=y, final_state=S)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1) / steps
+    ms = max_over_ranks(ms_local, device=dev)
+    path = "split" if ws_bytes > 0 else "fused"
+    tflops = FLOP_PER_TOKEN_HEAD * n * CFG2_T / (ms * 1e-3) / 1e12
+    del q, k, v, beta, y, S, ws
+    torch.cuda.empty_cache()
+    return {"metric": "config2 batched prefill tokens/s (B=32 x H=16 = 512 scans, T=16384, bf16 in, fp32 state)",
+            "value": 32 * CFG2_T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "scans_per_gpu": n, "scaling": "strong", "path": path,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tflops / peaks["bf16_tflops"], "traffic": None,
+                         "note": f"per GPU: {FLOP_PER_TOKEN_HEAD} FLOP/token-head x {n} x {CFG2_T} over the "
+                                 f"slowest rank's step; {path} kernel path; peak {peaks['src']} burst"}}
+
+
+def sp_error(dev, rank, world, n_heads=4, seq=16384):
+    """Sequence-parallel prefill (row e2): rank r runs token block r of one sequence per head with the
+    entering state folded from the other ranks' block maps (one NCCL all_gather); its block's outputs
+    and the last rank's final state are compared with one single-GPU pass over the whole sequence
+    (computed on every rank).  Returns the max over ranks of the relative errors (bf16 mode)."""
+    import torch
+
+    import kdn_b200
+    from kdn_b200.distributed import max_over_ranks, sequence_parallel_prefill, shard_range
+
+    proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+    q, k, v, beta = prefill_inputs(dev, 31337, n_heads=n_heads, seq=seq)
+    Y, S = kdn_b200.fused_chunked_deltanet_forward(q, k, v, beta, None, proj, C, mode="bf16")
+    lo, hi = shard_range(seq // C, rank, world)
+    a, b = lo * C, hi * C
+    Yr, Sr = sequence_parallel_prefill(q[:, a:b].contiguous(), k[:, a:b].contiguous(), v[:, a:b].contiguous(),
+                                       beta[:, a:b].contiguous(), None, proj, C, mode="bf16")
+    ey = ((Yr.float() - Y[:, a:b].float()).norm(dim=-1) / Y[:, a:b].float().norm(dim=-1).clamp_min(1e-30)).max()
+    es = ((Sr - S).norm() / S.norm()) if rank == world - 1 else torch.zeros((), device=dev)
+    return {"y_block_vs_single_pass": max_over_ranks(float(ey), device=dev),
+            "final_state_vs_single_pass": max_over_ranks(float(es), device=dev),
+            "case": f"{n_heads} heads x {seq} tokens, bf16 mode, blocks of whole chunks per rank"}
 
 
 def bench_lift(dev, peaks, steps=10, warmup=3):
@@ -605,10 +721,12 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    dec = bench_decode(dev, steps=200, warmup=5, peaks=peaks)
+    dec = bench_decode(dev, steps=1024, warmup=5, peaks=peaks, rank=rank, world=world)
+    cfg2 = bench_config2(dev, peaks, rank, world)
     lift = bench_lift(dev, peaks)
     rag = bench_ragged(dev, steps=10, warmup=3)
     tpp = bench_tp_out_proj(dev, rank, world) if world > 1 else None
+    sp = sp_error(dev, rank, world) if world > 1 else None
     bwd = bench_backward(dev)
     lm = bench_hybrid_lm(dev, rank, world) if not args.no_lm else None
 
@@ -674,16 +792,20 @@ def run_ours(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk,
         "decode": dec,
+        "config2": cfg2,
         "lift": lift,
         "ragged": rag,
     }
     if tpp is not None:
         line["tp_out_proj"] = tpp
+    if sp is not None:
+        line["sequence_parallel"] = sp
     line["backward"] = bwd
     if lm is not None:
         line["hybrid_lm"] = lm
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.ref_seq)
+        line["cpu_baseline"].pop("seconds", None)
     print(json.dumps(line), flush=True)
 
 
@@ -705,6 +827,55 @@ def run_prefill_only(n_seq: int, seq: int):
                       "path": os.environ.get("KDN_PREFILL_PATH", "auto")}))
 
 
+def run_case(name: str):
+    """One fixed, seeded invocation of a single kernel, three calls (two warm-ups, one to capture), for
+    profiler captures of kernels outside the headline step:
+      tp_proj      the TMA-fed projection kernel, one rank: Y [32768, 512] x W [2048, 512]^T, bf16 -> fp32
+      decode_attn  split-K decode attention, bf16 caches [8, 32, 16384, 64], live lengths 4096..16383
+      backward     the prefill backward (exact fp32), 16 heads x 4096 tokens, decay 1
+      lift         the standalone feature lift, 4 x 65536 unit vectors, bf16 in and out"""
+    import torch
+
+    import kdn_b200
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    if name == "tp_proj":
+        from kdn_b200.distributed import row_parallel_out_proj
+
+        y = torch.randn(32768, 512, generator=g, device=dev).bfloat16()
+        w = (torch.randn(2048, 512, generator=g, device=dev) / 22.6).bfloat16()
+        call = lambda: row_parallel_out_proj(y, w)
+    elif name == "decode_attn":
+        from kdn_b200.kernels.glue import decode_attention
+
+        Bq, Hq, L = 8, 32, 16384
+        q = torch.randn(Bq, Hq, 64, generator=g, device=dev).bfloat16()
+        kc = torch.randn(Bq, Hq, L, 64, generator=g, device=dev).bfloat16()
+        vc = torch.randn(Bq, Hq, L, 64, generator=g, device=dev).bfloat16()
+        lengths = torch.randint(4096, L, (Bq,), generator=g, device=dev)
+        call = lambda: decode_attention(q, kc, vc, lengths)
+    elif name == "lift":
+        x = torch.nn.functional.normalize(torch.randn(4, 65536, 64, generator=g, device=dev), dim=-1).bfloat16()
+        p = kdn_b200.FastWalshHadamardProjection().to(dev)
+        call = lambda: p(x)
+    elif name == "backward":
+        Nb, Tb = 16, 4096
+        q = torch.nn.functional.normalize(torch.randn(Nb, Tb, 64, generator=g, device=dev), dim=-1)
+        k = torch.nn.functional.normalize(torch.randn(Nb, Tb, 64, generator=g, device=dev), dim=-1)
+        v = torch.randn(Nb, Tb, 64, generator=g, device=dev)
+        beta = torch.sigmoid(torch.randn(Nb, Tb, generator=g, device=dev))
+        dY = torch.randn(Nb, Tb, 64, generator=g, device=dev)
+        proj = kdn_b200.FastWalshHadamardProjection().to(dev)
+        call = lambda: kdn_b200.chunked_deltanet_backward(q, k, v, beta, None, dY, proj, 64)
+    else:
+        raise SystemExit(f"unknown case {name!r}")
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": name, "ok": True}))
+
+
 def run_decode_only(steps: int):
     """Only the decode workload for `steps` steps (the case `ncu` captures use)."""
     import torch
@@ -721,10 +892,12 @@ def main():
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ref-seq", type=int, default=4096, help="tokens per CPU-baseline sample (16 heads)")
+    ap.add_argument("--ref-seq", type=int, default=T, help="tokens per CPU-baseline sample (16 heads)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-only", type=int, nargs=2, metavar=("N", "T"),
                     help="only run two prefill calls of N sequences x T tokens (for profiler captures)")
+    ap.add_argument("--case", choices=["tp_proj", "decode_attn", "backward", "lift"],
+                    help="only run one fixed single-kernel invocation three times (for profiler captures)")
     ap.add_argument("--decode-only", type=int, metavar="STEPS",
                     help="only run the decode workload for STEPS steps (for profiler captures)")
     ap.add_argument("--lm-only", action="store_true", help="only run the config-4 hybrid LM shard")
@@ -746,6 +919,9 @@ def main():
         import torch.distributed as dist
 
         dist.destroy_process_group()
+        return
+    if args.case:
+        run_case(args.case)
         return
     if args.decode_only:
         run_decode_only(args.decode_only)

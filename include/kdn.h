@@ -128,9 +128,11 @@ int kdn_prefill_launch_count(void);
 /*
  * Size of the scratch array compiled into libkdn for kdn_chunked_prefill_static:
  * 64 MiB of device memory per device, reserved when the library's module is
- * loaded there.  At D = 512 that covers N*T up to 14,336 tokens (chunk 64) or
- * 15,360 (chunk 32); kdn_chunked_prefill_workspace_size(..., KDN_MODE_F32) gives
- * the exact need.
+ * loaded there.  Each sequence is padded to whole chunks, so the limit is on
+ * N * Tp with Tp = T rounded up to a multiple of the chunk: at D = 512 and
+ * d_v = 64, N * Tp up to 14,336 tokens (chunk 64) or 15,360 (chunk 32) -- for
+ * example N = 224 sequences of T <= 64, but N = 14,336 of T = 1 do not fit.
+ * kdn_chunked_prefill_workspace_size(..., KDN_MODE_F32) gives the exact need.
  */
 #define KDN_STATIC_SCRATCH_BYTES (64u * 1024u * 1024u)
 
@@ -144,8 +146,9 @@ int kdn_prefill_launch_count(void);
  *   - Sizes whose scratch need exceeds KDN_STATIC_SCRATCH_BYTES are rejected
  *     with KDN_ERR_WORKSPACE before any work is enqueued.
  *   - The first call on each device looks the array's address up
- *     (cudaGetSymbolAddress with that device current); make that call before
- *     any stream capture begins.
+ *     (cudaGetSymbolAddress with that device current), and looks it up again
+ *     if the device's context has changed since (a device reset); make the
+ *     first call on a device before any stream capture begins.
  *   - All calls on one device share the array: calls whose kernels overlap
  *     (unordered streams, several host threads) race.  Serialise them.
  * Arguments and results are those of kdn_chunked_prefill.  This entry point has

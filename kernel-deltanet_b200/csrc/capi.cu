@@ -8,9 +8,29 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <string>
 
 #include "kdn_internal.h"
+
+namespace kdn {
+
+int current_sm_count() {
+  constexpr int kDevs = 64;
+  static std::atomic<int> cache[kDevs] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < kDevs) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  if (dev >= 0 && dev < kDevs) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+}  // namespace kdn
 
 namespace {
 
@@ -77,13 +97,7 @@ bool use_split_path(int64_t N) {
   const char* env = getenv("KDN_PREFILL_PATH");
   if (env && strcmp(env, "fused") == 0) return false;
   if (env && strcmp(env, "split") == 0) return true;
-  static thread_local int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      sms = 148;
-  }
-  return N < sms;
+  return N < kdn::current_sm_count();
 }
 
 bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {

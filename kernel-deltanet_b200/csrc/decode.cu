@@ -357,12 +357,7 @@ __global__ void __launch_bounds__(kDecThr, 1) decode_kernel(DecodeProblem p, Pro
 
 cudaError_t launch_decode(const DecodeProblem& p, const ProjParams& P, cudaStream_t stream) {
   if (p.num_tokens == 0) return cudaSuccess;
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      sms = 148;
-  }
+  const int sms = current_sm_count();
   const int64_t units = p.num_tokens * p.H;  // (token, head) pairs, walked by persistent CTAs
   const unsigned grid = unsigned(units < sms ? units : sms);
   cudaError_t e;

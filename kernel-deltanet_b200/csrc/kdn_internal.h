@@ -10,6 +10,11 @@
 
 namespace kdn {
 
+// Multiprocessor count of the current device, looked up once per device and cached in a
+// table of atomics (safe when several host threads drive several devices); 148 if the
+// lookup fails.
+int current_sm_count();
+
 // ------------------------------------------------------------------ lift.cu
 cudaError_t launch_lift(const void* x, int x_dtype, void* out, int out_dtype, int64_t n, const ProjParams& P,
                         bool omega_bf16_exact, cudaStream_t stream);
@@ -88,7 +93,8 @@ cudaError_t launch_simt_prefill(const PrefillProblem& p, const ProjParams& P, vo
                                 cudaStream_t stream, LaunchMarks& marks);
 
 // prefill_static.cu: device address of the library's fixed prefill scratch
-// (KDN_STATIC_SCRATCH_BYTES) on the current device, looked up on first use.
+// (KDN_STATIC_SCRATCH_BYTES) on the current device, looked up on first use and again
+// whenever the device's current context has changed (after a device reset).
 cudaError_t static_prefill_scratch(void** out);
 
 // prefill_tc.cu: fused tensor-core path (bf16 operands, fp32 accumulation/state),

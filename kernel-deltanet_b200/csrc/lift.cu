@@ -37,6 +37,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "kdn_internal.h"
 #include "lift.cuh"
 #include "tc_chunk.cuh"
@@ -271,10 +273,10 @@ __global__ void __launch_bounds__(256) lift_kernel(const void* __restrict__ x, i
 template <auto Kernel>
 cudaError_t allow_smem(int bytes, int dev) {
   constexpr int kDevs = 64;
-  static bool done[kDevs] = {};
-  if (dev >= 0 && dev < kDevs && done[dev]) return cudaSuccess;
+  static std::atomic<bool> done[kDevs] = {};  // host threads may launch on several devices at once
+  if (dev >= 0 && dev < kDevs && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
   const cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess && dev >= 0 && dev < kDevs) done[dev] = true;
+  if (e == cudaSuccess && dev >= 0 && dev < kDevs) done[dev].store(true, std::memory_order_release);
   return e;
 }
 

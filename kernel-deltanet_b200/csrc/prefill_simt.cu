@@ -383,13 +383,7 @@ size_t chain_smem_bytes(int D) {
 // (chunk 64) when 8-row tiles would too; the chains are latency-bound, so more CTAs -- on more SMs,
 // then two per SM -- shorten them
 int chain_rows(int64_t rows, int64_t N, int C) {
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
-                                                  cudaSuccess)
-      sms = 148;
-  }
+  const int sms = current_sm_count();
   if ((rows / 16) * N >= sms) return 16;
   return (C == 64 && (rows / 8) * N < sms) ? 4 : 8;
 }

@@ -33,8 +33,9 @@ __global__ void __launch_bounds__(256) ragged_transpose_kernel(const uint8_t* __
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   for (int64_t row = warp; row < total; row += nwarps) {
     const int64_t i = seq_of(cu, num_seqs, row);
-    const int64_t c0 = int64_t(cu[i]), Ti = int64_t(cu[i + 1]) - c0, t = row - c0;
-    if (t < 0 || t >= Ti || c0 + Ti > total) continue;  // malformed offsets: touch nothing
+    const int64_t c0 = int64_t(cu[i]), c1 = int64_t(cu[i + 1]), Ti = c1 - c0, t = row - c0;
+    // malformed offsets (negative, decreasing or past the end): touch nothing
+    if (c0 < 0 || c1 < c0 || c1 > total || t < 0 || t >= Ti) continue;
     for (int h = 0; h < H; ++h) {
       const int64_t packed = (row * H + h) * row_bytes;
       const int64_t hm = (c0 * H + int64_t(h) * Ti + t) * row_bytes;

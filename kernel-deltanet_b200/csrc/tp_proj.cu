@@ -700,16 +700,7 @@ bool encode_operand(CUtensorMap* map, const void* base, int64_t rows, int K, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) !=
-                                                  cudaSuccess)
-      n = 148;
-  }
-  return n;
-}
+int sm_count() { return current_sm_count(); }
 
 cudaError_t launch(const ProjArgs& a, cudaStream_t stream) {
   const int64_t tiles = ((a.M + kBM - 1) / kBM) * (a.N / kBN);

@@ -69,6 +69,33 @@ class FastWalshHadamardProjection(nn.Module):
         d2 = torch.where(torch.rand(self.M, d_k, generator=gen) > 0.5, 1.0, -1.0)
         d3 = torch.where(torch.rand(self.M, d_k, generator=gen) > 0.5, 1.0, -1.0)
         b = torch.rand(D, generator=gen) * (2.0 * math.pi)
+        self._set_constants(d1, d2, d3, b)
+
+    @classmethod
+    def from_reference(cls, ref) -> "FastWalshHadamardProjection":
+        """The projection an existing reference ``FastWalshHadamardProjection`` computes, taken from
+        its buffers ``d1, d2, d3`` (signs [M, d_k]) and ``b`` (phase [D]) (kernels/fwht.py:88-92), not
+        re-drawn, so any seed (or hand-edited buffers) carries over exactly.  Build it once per
+        reference projection and keep it: construction packs the sign bits and forms Omega."""
+        d_k, D = int(ref.d_k), int(ref.D)
+        self = cls.__new__(cls)
+        nn.Module.__init__(self)
+        self.d_k, self.D, self.M = d_k, D, D // d_k
+        self.seed = getattr(ref, "seed", None)
+        self.scale_norm = 1.0 / math.sqrt(d_k)
+        self.tau_star = float(d_k) ** 0.25
+        self.tau_star_inv = 1.0 / self.tau_star
+        host = lambda t: torch.as_tensor(t).detach().to("cpu", torch.float32).clone()
+        with torch.device("cpu"):
+            self._set_constants(host(ref.d1), host(ref.d2), host(ref.d3), host(ref.b))
+        self._proj_cache = {}
+        return self
+
+    def _set_constants(self, d1: torch.Tensor, d2: torch.Tensor, d3: torch.Tensor, b: torch.Tensor) -> None:
+        """Register the sign, phase and dense Omega buffers for signs d1, d2, d3 [M, d_k] and phase b [D]."""
+        d_k = self.d_k
+        if tuple(d1.shape) != (self.M, d_k) or tuple(b.shape) != (self.D,):
+            raise ValueError(f"signs must be [{self.M}, {d_k}] and the phase [{self.D}]")
         self._phase_host = b.clone()  # fp32, not a buffer: dtype casts of the module leave it alone
 
         bits = [pack_sign_bits(d) for d in (d1, d2, d3)]  # [stage][m]

@@ -136,6 +136,35 @@ def test_projection_buffers_match_golden(golden_dir):
                 assert s.sign_bits[m][st] == bits
 
 
+def test_projection_from_reference_buffers(golden_dir):
+    """A projection built from a reference projection's d1/d2/d3/b buffers (seed 7 here, the reference's
+    own draws from the golden fixture) carries the same sign bits and phase into the kdn_projection
+    struct as one drawn with that seed -- and is not the default seed's projection."""
+    import types
+
+    import numpy as np
+    import torch
+    from kdn_b200 import FastWalshHadamardProjection
+
+    g = np.load(os.path.join(golden_dir, "lift_seed7.npz"))
+    ref = types.SimpleNamespace(d_k=64, D=512, d1=torch.from_numpy(g["d1"]), d2=torch.from_numpy(g["d2"]),
+                                d3=torch.from_numpy(g["d3"]), b=torch.from_numpy(g["b"]))
+    p = FastWalshHadamardProjection.from_reference(ref)
+    drawn = FastWalshHadamardProjection(64, 512, 7)
+    default = FastWalshHadamardProjection(64, 512, 42)
+    s, ph = p.kdn_projection("cpu")
+    s7, ph7 = drawn.kdn_projection("cpu")
+    s42, _ = default.kdn_projection("cpu")
+    bits = lambda st: [[st.sign_bits[m][i] for i in range(3)] for m in range(8)]
+    assert bits(s) == bits(s7) and bits(s) != bits(s42)
+    for m in range(8):
+        for st, d in enumerate((g["d1"], g["d2"], g["d3"])):
+            assert s.sign_bits[m][st] == sum(1 << i for i in range(64) if d[m, i] < 0)
+    assert torch.equal(ph, ph7) and torch.equal(ph, torch.from_numpy(g["b"]))
+    np.testing.assert_array_equal(p.Omega.numpy(), g["omega"])
+    assert (s.d_k, s.D, s.tau_inv, s.amp) == (s7.d_k, s7.D, s7.tau_inv, s7.amp)
+
+
 def test_prefill_event_hook_argument_checks(lib):
     assert lib.kdn_set_prefill_events(None, 1) == 1
     assert lib.kdn_set_prefill_events(None, 0) == 0

@@ -158,3 +158,34 @@ def test_varlen_rejects_rows_outside_the_batch():
     assert torch.equal(S[1], S0[1])
     assert float(y[200:].float().abs().max()) == 0.0
     assert kdn_b200.serving.vllm_kernel_deltanet_op.device_error(dev) != 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cu_list", [[-1000, 10], [0, 4, -2, 10], [0, 6, 20]])
+def test_ragged_transpose_leaves_malformed_rows_untouched(cu_list):
+    """kdn_ragged_transpose skips every row of a sequence whose offsets are negative, decreasing or
+    past the end (the C entry point does not validate cu_seqlens; the kernel guards each row):
+    those rows of dst keep their contents and nothing outside the tensors is touched."""
+    import kdn_b200
+    from kdn_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    lib = kdn_b200.load()
+    total, H, w = 10, 2, 64
+    src = torch.randn(total, H, w, device=dev)
+    guard = 64
+    buf = torch.full((guard + total + guard, H, w), 5.0, device=dev)  # guard rows on both sides
+    dst = buf[guard:guard + total]
+    cu = torch.tensor(cu_list, device=dev, dtype=torch.int64)
+    rc = lib.kdn_ragged_transpose(src.data_ptr(), dst.data_ptr(), cu.data_ptr(), _lib.KDN_INDEX_I64,
+                                  len(cu_list) - 1, total, H, w * 4, 1, _lib.stream_handle(dev))
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert bool((buf[:guard] == 5.0).all()) and bool((buf[guard + total:] == 5.0).all())
+    good = [i for i in range(len(cu_list) - 1) if 0 <= cu_list[i] <= cu_list[i + 1] <= total]
+    rows = dst.reshape(-1, w)
+    for i in good:  # well-formed sequences: their head-major block
+        c0, c1 = cu_list[i], cu_list[i + 1]
+        assert torch.equal(rows[c0 * H:c1 * H], src[c0:c1].transpose(0, 1).reshape(-1, w))
+    n_written = sum((cu_list[i + 1] - cu_list[i]) * H for i in good)
+    assert int((rows == 5.0).all(-1).sum()) == total * H - n_written

@@ -3,9 +3,13 @@ array (no workspace argument, no allocation per call).
 
 The GPU test checks two calls in a row (the second continuing the first's state,
 on different tokens, so stale scratch would show) against kdn_chunked_prefill with
-a caller workspace, within the fp32-mode tolerance, and that the second call
-changes the device's free memory by nothing.  The CPU test checks the size limit.
-This file is named to be collected last; it passes alone as well.
+a caller workspace: the same kernels over the same scratch layout, so the results
+must be bit-identical.  It also checks that a call rejected for its size leaves
+the outputs untouched (nothing was enqueued) and that the second call takes no
+device memory (no drop of a whole 2 MiB allocation granule in the device's free
+memory; the test assumes no other process allocates on the GPU meanwhile).  The
+CPU test checks the size limit.  This file is named to be collected last; it
+passes alone as well.
 """
 
 import ctypes
@@ -107,12 +111,25 @@ def test_static_prefill_matches_workspace_entry_two_calls():
         torch.cuda.synchronize()
         free_after.append(torch.cuda.mem_get_info(0)[0])
         s_in = s
-    assert free_after[1] == free_after[0], "the second call changed the device's free memory"
+    assert free_after[0] - free_after[1] < 2 << 20, "the second call took device memory"
 
     for i in range(2):
         y, s = outs[i]
         assert torch.isfinite(y).all() and torch.isfinite(s).all()
         assert _rel(y.cpu().numpy(), ref_y[i].cpu().numpy()) <= F32_TOL
         assert _rel(s.cpu().numpy(), ref_s[i].cpu().numpy()) <= F32_TOL
+        # same kernels, same scratch layout: stale scratch would break bit-equality
+        assert torch.equal(y, ref_y[i]) and torch.equal(s, ref_s[i])
+
+    # a call rejected for its size enqueues nothing: its outputs keep their contents
+    big = [torch.zeros(4, 4096, 64, device=DEV) for _ in range(3)]
+    bb = torch.zeros(4, 4096, device=DEV)
+    yb = torch.full((4, 4096, dv), 7.0, device=DEV)
+    sb = torch.full((4, dv, 512), 7.0, device=DEV)
+    rc = lib.kdn_chunked_prefill_static(ptr(big[0]), ptr(big[1]), ptr(big[2]), 0, ptr(bb), None, 0, None, ptr(yb),
+                                        0, ptr(sb), 4, 4096, dv, C, P, stream)
+    assert rc == 4 and b"KDN_STATIC_SCRATCH_BYTES" in lib.kdn_last_error()
+    torch.cuda.synchronize()
+    assert bool((yb == 7.0).all()) and bool((sb == 7.0).all())
     code = ctypes.c_int(-1)
     assert lib.kdn_device_error(stream, ctypes.byref(code)) == 0 and code.value == 0
