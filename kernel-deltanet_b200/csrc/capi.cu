@@ -91,13 +91,17 @@ bool use_tc_path(const kdn_projection* proj, int32_t dv, int32_t chunk, int mode
 
 // Which tensor-core prefill runs: the fused kernel (one CTA per sequence) keeps
 // everything on chip and suits many sequences; the two-phase kernels spread each
-// sequence's chunks over all SMs and suit fewer sequences than SMs.  KDN_PREFILL_PATH
+// sequence's chunks over all SMs and suit up to half as many sequences as SMs.  KDN_PREFILL_PATH
 // = "fused" or "split" forces one (both give the same results up to rounding).
 bool use_split_path(int64_t N) {
   const char* env = getenv("KDN_PREFILL_PATH");
   if (env && strcmp(env, "fused") == 0) return false;
   if (env && strcmp(env, "split") == 0) return true;
-  return N < kdn::current_sm_count();
+  // Measured on B200 (T = 16384, bf16): the one-CTA-per-sequence kernel takes about the same time
+  // for any N up to the SM count (one wave, latency bound), while the two-phase path grows with N
+  // (its preparation shares the SMs); the two cross between N = 64 (split 2.7 ms, fused 3.5 ms)
+  // and N = 96 (split 4.3 ms, fused 3.5 ms).
+  return N <= kdn::current_sm_count() / 2;
 }
 
 bool overlaps(const void* a, size_t abytes, const void* b, size_t bbytes) {

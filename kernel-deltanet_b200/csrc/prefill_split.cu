@@ -1220,15 +1220,16 @@ cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, v
                         (const void*)split_persistent_kernel})
     if ((e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSplitSmem))) != cudaSuccess)
       return e;
-  // one launch for all phases when every CTA fits at once and the state pass leaves SMs
-  // for the other two (KDN_SPLIT_PERSISTENT=0 forces the three launches)
+  // one launch for all phases when every CTA fits at once and the state pass leaves at least half
+  // of the SMs for the other two (KDN_SPLIT_PERSISTENT=0 forces the three launches); measured at
+  // T = 16384: 32 sequences 1.66 ms in one launch vs 1.73 ms in three, 48 sequences 3.9 vs 2.2 ms
   const int n_state = int(2 * p.N);
   int per_sm = 0;
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, split_persistent_kernel, kP1Thr, kSplitSmem)) !=
       cudaSuccess)
     return e;
   const char* env = getenv("KDN_SPLIT_PERSISTENT");
-  const bool persistent = coop && per_sm >= 1 && n_state + 8 <= sms && !(env && strcmp(env, "0") == 0);
+  const bool persistent = coop && per_sm >= 1 && 2 * n_state <= sms && !(env && strcmp(env, "0") == 0);
   if (persistent) {
     uint32_t* rec_ready = reinterpret_cast<uint32_t*>(sa.ws + size_t(total) * REC_BYTES);
     uint32_t* out_prog = rec_ready + total;
