@@ -135,14 +135,21 @@ constexpr int kP1Thr = 32 * (kP1Warps + 2);
 // TMEM columns (phase 1)
 constexpr uint32_t P1_Z = 0;     // lift results, 2 x 128 cols (slices s at 128 (s & 1))
 constexpr uint32_t P1_GP = 256;  // [G; P], 64 cols
-constexpr uint32_t P1_U = 0;     // U in lanes 64..127 (after the chunk matrices are read)
+constexpr uint32_t P1_U = 320;   // U in lanes 64..127, 64 cols (apart from the lift slots, so that the
+                                 // next chunk's first lifts can run during this chunk's algebra)
 
 // shared memory (phase 1)
 constexpr uint32_t P1_OMG = 0;        // 64 KiB Omega (bf16)
 constexpr uint32_t P1_XIN = 65536;    // 16 KiB [k; q] (bf16, K-major)
-constexpr uint32_t P1_F = 81920;      // 32 KiB slice features [U_k; U_q] | algebra: A (f32), T (f32)
+constexpr uint32_t P1_F = 81920;      // 32 KiB slice features [U_k; U_q] of even slices | algebra: A (f32),
+                                      //        then the U staging tile
 constexpr uint32_t P1_AQ = 114688;    // 8 KiB  Aq (fp16, K-major SW128), copied to the record
 constexpr uint32_t P1_VEC = 122880;   // 1 KiB  per-token factors of the state pass, copied to the record
+constexpr uint32_t P1_F1 = 124928;    // 32 KiB slice features of odd slices (two buffers: a slice's
+                                      //        features are written while the previous slice's Gram
+                                      //        product and copy-out still read the other buffer)
+constexpr uint32_t P1_ES = 157696;    // 17 KiB T = (I + A)^-1 (fp32), rows kEsLd floats apart
+constexpr int kEsLd = 68;             // padded row: the row-wise float4 reads of 8 rows hit distinct banks
 constexpr uint32_t P1_VB = 180224;    // 8 KiB  V (fp16, MN-major), B operand of U
 constexpr uint32_t P1_TOP = 188416;   // 16 KiB [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major)
 constexpr uint32_t P1_US = 208896;    // 4 KiB  forward-substitution scratch
@@ -151,9 +158,14 @@ constexpr uint32_t P1_GL = 215040;    // 5 x 256 B gates: g, beta, exp(g), exp(g
 constexpr uint32_t P1_SSP = 216320;   // 2 KiB  sums of squares per column quarter
 constexpr uint32_t P1_SC = 218368;    // 512 B  token scales
 constexpr uint32_t P1_BAR = 218880;   // mbarriers + TMEM address
-constexpr uint32_t kP1Smem = P1_BAR + 128 + 1024;  // barriers use 112 bytes
+constexpr uint32_t kP1Bars = 144;      // bytes of barriers
+constexpr uint32_t kP1Smem = P1_BAR + kP1Bars + 1024;
+static_assert(P1_VEC + 1024 <= P1_F1 && P1_F1 + 32768 <= P1_ES && P1_ES + 64 * kEsLd * 4 <= P1_VB,
+              "phase-1 shared-memory regions overlap");
 
-// Level d of the blocked inverse T = (I + A)^-1 (16x16 blocks, T row-major in Es,
+__device__ __forceinline__ uint32_t p1_fbuf(int s) { return (s & 1) ? P1_F1 : P1_F; }  // slice s's features
+
+// Level d of the blocked inverse T = (I + A)^-1 (16x16 blocks, T row-major in Es with rows kEsLd apart,
 // A in the float4-swizzled layout of sx()): for the blocks I - J = d,
 //   P = sum_{K=J}^{I-1} A_IK T_KJ  (into US),  then  T_IJ = -T_II P.
 template <int D>
@@ -167,17 +179,17 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
     for (int q = 0; q < 4 * D; ++q) {
       const int k = 16 * J + 4 * q;
       const float4 a4 = *reinterpret_cast<const float4*>(Am + row * 64 + ((((k >> 2) ^ row) & 15) << 2));
-      acc[0] = fmaf(a4.x, Es[k * 64 + 16 * J + cc], acc[0]);
-      acc[1] = fmaf(a4.y, Es[(k + 1) * 64 + 16 * J + cc], acc[1]);
-      acc[2] = fmaf(a4.z, Es[(k + 2) * 64 + 16 * J + cc], acc[2]);
-      acc[3] = fmaf(a4.w, Es[(k + 3) * 64 + 16 * J + cc], acc[3]);
+      acc[0] = fmaf(a4.x, Es[k * kEsLd + 16 * J + cc], acc[0]);
+      acc[1] = fmaf(a4.y, Es[(k + 1) * kEsLd + 16 * J + cc], acc[1]);
+      acc[2] = fmaf(a4.z, Es[(k + 2) * kEsLd + 16 * J + cc], acc[2]);
+      acc[3] = fmaf(a4.w, Es[(k + 3) * kEsLd + 16 * J + cc], acc[3]);
     }
     US[e] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
   tc::named_bar_sync(1, kP1Threads);
   for (int e = tid; e < kElems; e += kP1Threads) {
     const int J = e >> 8, I = J + D, r = (e >> 4) & 15, cc = e & 15;
-    const float* trow_ = Es + (16 * I + r) * 64 + 16 * I;
+    const float* trow_ = Es + (16 * I + r) * kEsLd + 16 * I;
     const float* pcol = US + (J << 8) + cc;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -187,7 +199,7 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
       acc[2] = fmaf(trow_[k + 2], pcol[(k + 2) << 4], acc[2]);
       acc[3] = fmaf(trow_[k + 3], pcol[(k + 3) << 4], acc[3]);
     }
-    Es[(16 * I + r) * 64 + 16 * J + cc] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
+    Es[(16 * I + r) * kEsLd + 16 * J + cc] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
   }
   tc::named_bar_sync(1, kP1Threads);
 }
@@ -200,7 +212,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   const TcArgs& a = sa.a;
   const uint32_t sbase = tc::smem_u32(sm);
   float* Am = reinterpret_cast<float*>(sm + P1_F);
-  float* Es = reinterpret_cast<float*>(sm + P1_F + 16384);
+  float* Es = reinterpret_cast<float*>(sm + P1_ES);
   float* US = reinterpret_cast<float*>(sm + P1_US);
   float* ph = reinterpret_cast<float*>(sm + P1_PH);
   float* gl = reinterpret_cast<float*>(sm + P1_GL);
@@ -214,12 +226,14 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + P1_BAR + 8);
   uint64_t* bar_xin = reinterpret_cast<uint64_t*>(sm + P1_BAR + 16);
   uint64_t* bar_zfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 96);  // [2] slot s & 1 read by all warps
-  uint64_t* bar_fready = reinterpret_cast<uint64_t*>(sm + P1_BAR + 32);
+  uint64_t* bar_fready = reinterpret_cast<uint64_t*>(sm + P1_BAR + 112);  // [2] features of a slice written to
+                                                                          //     buffer s & 1 (16 warps)
   uint64_t* bar_ops = reinterpret_cast<uint64_t*>(sm + P1_BAR + 40);
   uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);   // U staged
   uint64_t* bar_stfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 64);  // staged tiles copied out
-  uint64_t* bar_fdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 24);   // slice's Gram product done and its
-                                                                          // features copied out (2 arrivals)
+  uint64_t* bar_fdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 128);  // [2] the Gram product of the slice
+                                                                          //     in buffer s & 1 done and its
+                                                                          //     features copied out (2 arrivals)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cq = (warp >> 2) & 3;
@@ -237,11 +251,13 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
     tc::mbar_init(bar_xin, kP1Warps);
     tc::mbar_init(&bar_zfree[0], kP1Warps);
     tc::mbar_init(&bar_zfree[1], kP1Warps);
-    tc::mbar_init(bar_fready, kP1Warps);
+    tc::mbar_init(&bar_fready[0], kP1Warps);
+    tc::mbar_init(&bar_fready[1], kP1Warps);
     tc::mbar_init(bar_ops, kP1Warps);
     tc::mbar_init(bar_wdone, kP1Warps);
     tc::mbar_init(bar_stfree, 1);
-    tc::mbar_init(bar_fdone, 2);
+    tc::mbar_init(&bar_fdone[0], 2);
+    tc::mbar_init(&bar_fdone[1], 2);
     tc::fence_mbar_init();
   }
   build_omega(sm + P1_OMG, P, warp, lane, kP1Thr / 32);
@@ -259,7 +275,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
       const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
       const uint32_t id_n64 = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0;
+      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0;  // p_zfree, p_fready: phase bits per slot
       auto lift = [&](int s) {  // Z slot s & 1 = [k; q] Omega_s^T
 #pragma unroll
         for (int k0 = 0; k0 < 64; k0 += 16)
@@ -267,26 +283,32 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
                      tc::smem_desc_sw128(sbase + P1_OMG + s * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
         tc::mma_commit(&bar_lift[s & 1]);
       };
-      for (int64_t idx = cta; idx < total; idx += ncta) {
+      auto first_lifts = [&]() {  // slices 0 and 1 of the chunk whose inputs the compute warps announce
         ok &= split_wait(bar_xin, p_xin, sa.abort);
         p_xin ^= 1;
         tc::fence_after_sync();
         lift(0);
         lift(1);
+      };
+      if (cta < total) first_lifts();
+      for (int64_t idx = cta; idx < total; idx += ncta) {
         for (int s = 0; s < kSlices; ++s) {
           ok &= split_wait_bit(&bar_zfree[s & 1], p_zfree, s & 1, sa.abort);  // slot s & 1 read by all
           tc::fence_after_sync();
           if (s + 2 < kSlices) lift(s + 2);
-          ok &= split_wait(bar_fready, p_fready, sa.abort);
-          p_fready ^= 1;
+          ok &= split_wait_bit(&bar_fready[s & 1], p_fready, s & 1, sa.abort);
           tc::fence_after_sync();
+          const uint32_t fb = sbase + p1_fbuf(s);
 #pragma unroll
           for (int k0 = 0; k0 < 128; k0 += 16) {
-            const uint64_t fd = tc::smem_desc_sw128(sbase + P1_F + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
+            const uint64_t fd = tc::smem_desc_sw128(fb + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
             tc::mma_ss(tmem + P1_GP, fd, fd, id_gp, s > 0 || k0 > 0);
           }
-          tc::mma_commit(bar_fdone);  // F is rewritten once the publisher has copied it out too
+          tc::mma_commit(&bar_fdone[s & 1]);  // the buffer is rewritten once the publisher has copied it out too
         }
+        // every slot of this chunk has been read: the next chunk's first lifts run during this
+        // chunk's algebra (its inputs are announced by the compute warps mid-algebra)
+        if (idx + ncta < total) first_lifts();
         ok &= split_wait(bar_ops, p_ops, sa.abort);
         p_ops ^= 1;
         tc::fence_after_sync();
@@ -301,20 +323,20 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   } else if (warp == kP1Publisher) {
     // ================================================================ record copies, publication
     if (lane == 0) {
-      uint32_t p_fready = 0, p_wdone = 0;
+      uint32_t p_fready = 0, p_wdone = 0;  // p_fready: phase bits per buffer
       for (int64_t idx = cta; idx < total; idx += ncta) {
         uint8_t* rec = record(sa, idx / N, idx % N);
         for (int s = 0; s < kSlices; ++s) {
           // the slice's features: U_q (rows 64..127) as K-blocks 2s, 2s+1 and U_k (rows 0..63) as slice s
-          ok &= split_wait(bar_fready, p_fready, sa.abort);
-          p_fready ^= 1;
+          ok &= split_wait_bit(&bar_fready[s & 1], p_fready, s & 1, sa.abort);
+          const uint32_t fb = sbase + p1_fbuf(s);
           for (int kb = 0; kb < 2; ++kb) {
-            tc::bulk_store(rec + REC_Q + (2 * s + kb) * 8192, sbase + P1_F + kb * 16384 + 8192, 8192);
-            tc::bulk_store(rec + REC_UK + s * 16384 + kb * 8192, sbase + P1_F + kb * 16384, 8192);
+            tc::bulk_store(rec + REC_Q + (2 * s + kb) * 8192, fb + kb * 16384 + 8192, 8192);
+            tc::bulk_store(rec + REC_UK + s * 16384 + kb * 8192, fb + kb * 16384, 8192);
           }
           tc::bulk_commit();
           tc::bulk_wait_read();
-          tc::mbar_arrive(bar_fdone);
+          tc::mbar_arrive(&bar_fdone[s & 1]);
         }
         // T' (rows 0..63 of the U product's A operand), U, Aq and the factors
         ok &= split_wait(bar_wdone, p_wdone, sa.abort);
@@ -359,12 +381,15 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       const int64_t nidx = idx + ncta;
       const bool has_next = nidx < total;
       const int64_t nn = nidx % N, ncn = nidx / N;
-      // ---------------------------------------- chunk inputs -> lift of slice 0
-      tc::cp_async_wait_all();
-      if (!bf_in) load_kq_f32(a, n, int(c), sm + P1_XIN, tid);
-      tc::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(bar_xin);
+      // ---------------------------------------- chunk inputs -> lifts of slices 0, 1 (the first chunk;
+      // later chunks' inputs are announced during the previous chunk's algebra)
+      if (idx == cta) {
+        tc::cp_async_wait_all();
+        if (!bf_in) load_kq_f32(a, n, int(c), sm + P1_XIN, tid);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_xin);
+      }
       float vreg[8];  // v row tid/8, values 8 (tid%8) .. +7 (zero past the end)
       {
         const int row = tid >> 3, cc = tid & 7;
@@ -452,17 +477,16 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
           fp[j >> 1] = pack_f16(u0, u1);
           fp[(j >> 1) + 1] = pack_f16(u2, u3);
         }
-        if (s > 0) {
-          ok &= split_wait(bar_fdone, ph_fd, sa.abort);  // the previous slice's Gram product and copy-out
-          ph_fd ^= 1;                                      // are done with F
+        if (s >= 2) {  // slice s - 2's Gram product and copy-out are done with buffer s & 1
+          ok &= split_wait_bit(&bar_fdone[s & 1], ph_fd, s & 1, sa.abort);
           tc::fence_after_sync();
-        } else if (idx != cta) {  // the previous chunk's staged tiles have been copied out
+        } else if (s == 0 && idx != cta) {  // the previous chunk's staged tiles (buffer 0) have been copied out
           ok &= split_wait(bar_stfree, ph_st, sa.abort);
           ph_st ^= 1;
         }
         {
           const int kb = cq >> 1, e0 = 32 * (cq & 1);
-          uint8_t* fb = sm + P1_F + kb * 16384;
+          uint8_t* fb = sm + p1_fbuf(s) + kb * 16384;
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
             const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
@@ -473,14 +497,19 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         tc::fence_proxy_async_smem();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(bar_fready);
+        if (lane == 0) tc::mbar_arrive(&bar_fready[s & 1]);
       }
       ssp[cq * 128 + trow] = ss;
-      // every lift of this chunk has completed: the input tile takes the next chunk
-      if (has_next && bf_in) prefetch_kq(a, nn, int(ncn), sbase + P1_XIN, tid);
+      // every lift of this chunk has completed: the input tile takes the next chunk (announced to the
+      // issuer during the algebra below)
+      if (has_next) {
+        if (bf_in) prefetch_kq(a, nn, int(ncn), sbase + P1_XIN, tid);
+        else load_kq_f32(a, nn, int(ncn), sm + P1_XIN, tid);
+      }
       tc::cp_async_commit();
-      ok &= split_wait(bar_fdone, ph_fd, sa.abort);  // Gram product (and copy-out) of the last slice
-      ph_fd ^= 1;
+      // Gram products (and copy-outs) of the last two slices: buffer 0 takes the algebra's A next
+      ok &= split_wait_bit(&bar_fdone[0], ph_fd, 0, sa.abort);
+      ok &= split_wait_bit(&bar_fdone[1], ph_fd, 1, sa.abort);
       tc::fence_after_sync();
 
       // ---------------------------------------- chunk matrices
@@ -549,24 +578,30 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
           tcol[r] = (r >= j) ? sacc : 0.f;
         }
 #pragma unroll
-        for (int r = 0; r < 16; ++r) Es[(16 * I + r) * 64 + 16 * I + j] = tcol[r];
+        for (int r = 0; r < 16; ++r) Es[(16 * I + r) * kEsLd + 16 * I + j] = tcol[r];
       }
       for (int e = tid; e < 64 * 64; e += kP1Threads) {  // zeros off the diagonal blocks (lower ones are
         const int r = e >> 6, cc = e & 63;               // overwritten below)
-        if ((r >> 4) != (cc >> 4)) Es[e] = 0.f;
+        if ((r >> 4) != (cc >> 4)) Es[r * kEsLd + cc] = 0.f;
       }
       tc::named_bar_sync(1, kP1Threads);
       // (b) off-diagonal blocks level by level (d = I - J = 1, 2, 3), all threads
       t_level<1>(Am, Es, US, tid);
       t_level<2>(Am, Es, US, tid);
       t_level<3>(Am, Es, US, tid);
+      if (has_next) {  // the next chunk's inputs are in place: its first lifts may start
+        tc::cp_async_wait_all();
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_xin);
+      }
       // A operand [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major, 128 x 64)
       {
         const int r = tid >> 2, jq = tid & 3, i = r & 63;
         float w[16];
 #pragma unroll
         for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(Es + i * 64 + 16 * jq + 4 * j4);
+          const float4 t4 = *reinterpret_cast<const float4*>(Es + i * kEsLd + 16 * jq + 4 * j4);
           const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
           for (int qx = 0; qx < 4; ++qx) {
@@ -937,9 +972,10 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
 // and one small item (Aq, E).  The accumulators are double-buffered in TMEM so the
 // epilogue of one chunk overlaps the products of the next.
 constexpr int kP3Thr = 128;  // warp 0 issues, warp 1 loads, warps 2 and 3 (the q-row lanes) write y
+constexpr int kP3Ring = 4;   // 32 KiB ring stages
 
 // shared memory (phase 3)
-constexpr uint32_t P3_RING = 8192;     // 5 x 32 KiB; [U_q kb 2s | U_q kb 2s+1 | S half 0 | S half 1], 8 KiB each
+constexpr uint32_t P3_RING = 8192;     // 4 x 32 KiB; [U_q kb 2s | U_q kb 2s+1 | S half 0 | S half 1], 8 KiB each
 constexpr uint32_t P3_SMALL = 172032;  // 2 x 17 KiB: [Aq 8 KiB | E half 0 | E half 1 | yqs]
 constexpr uint32_t P3_SMALL_BYTES = 17408;
 constexpr uint32_t P3_BAR = 206848;
@@ -963,7 +999,7 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
   const int64_t N = sa.N;
   const int64_t total = N * a.NC;
   if (tid == 0) {
-    for (int b = 0; b < kRing; ++b) {
+    for (int b = 0; b < kP3Ring; ++b) {
       tc::mbar_init(&ring_full[b], 1);
       tc::mbar_init(&ring_empty[b], 1);
     }
@@ -993,8 +1029,8 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
           tc::fence_proxy_async_global();
         }
         for (int s = 0; s < kSlices; ++s, ++g) {
-          const int b = int(g % kRing);
-          if (g >= kRing) {
+          const int b = int(g % kP3Ring);
+          if (g >= kP3Ring) {
             ok &= split_wait_bit(&ring_empty[b], pe, b, sa.abort);
           }
           const uint32_t dst = sbase + P3_RING + b * 32768;
@@ -1030,7 +1066,7 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
         tc::fence_after_sync();
         const uint32_t dq = tmem + 128 * u, de = dq + 64;
         for (int s = 0; s < kSlices; ++s, ++g) {
-          const int b = int(g % kRing);
+          const int b = int(g % kP3Ring);
           ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
           tc::fence_after_sync();
           const uint32_t st = sbase + P3_RING + b * 32768;
@@ -1110,7 +1146,7 @@ constexpr uint32_t kSplitTslot = 225536;
 constexpr uint32_t kSplitSmem = kSplitTslot + 16 + 1024;
 static_assert(kP1Smem <= kSplitSmem && kP2Smem <= kSplitSmem && kP3Smem <= kSplitSmem,
               "a role's shared memory exceeds the launch's");
-static_assert(kSplitTslot >= P2_BAR + 8 * kP2Bars && kSplitTslot >= P1_BAR + 112 && kSplitTslot >= P3_BAR + 8 * 18,
+static_assert(kSplitTslot >= P2_BAR + 8 * kP2Bars && kSplitTslot >= P1_BAR + kP1Bars && kSplitTslot >= P3_BAR + 8 * 18,
               "TMEM slot overlaps a role's barriers");
 
 __device__ __forceinline__ uint8_t* split_smem() {

@@ -423,14 +423,16 @@ def test_tc_prefill_long_sequence_vs_oracle(kdn, proj, consts, tc_path):
     assert fro_rel(S.cpu().numpy(), Sr) < BF16_S_TOL
 
 
-def test_tc_resume_is_bit_exact(kdn, proj, tc_path):
+@pytest.mark.parametrize("cut", [128, 192])
+def test_tc_resume_is_bit_exact(kdn, proj, tc_path, cut):
+    """Prefill in two calls, the state carried in fp32, equals one call bit for bit (any chunk-aligned cut)."""
     q, k, v, beta, decay, _ = make_inputs(112, 3, 512, 64, True, False)
     dq, dk, dvv = (to_dev(a, torch.bfloat16) for a in (q, k, v))
     db, dd = to_dev(beta), to_dev(decay)
     Y, S = kdn.fused_chunked_deltanet_forward(dq, dk, dvv, db, dd, proj, 64, mode="bf16")
-    Y1, S1 = kdn.fused_chunked_deltanet_forward(dq[:, :192], dk[:, :192], dvv[:, :192], db[:, :192], dd[:, :192],
+    Y1, S1 = kdn.fused_chunked_deltanet_forward(dq[:, :cut], dk[:, :cut], dvv[:, :cut], db[:, :cut], dd[:, :cut],
                                                 proj, 64, mode="bf16")
-    Y2, S2 = kdn.fused_chunked_deltanet_forward(dq[:, 192:], dk[:, 192:], dvv[:, 192:], db[:, 192:], dd[:, 192:],
+    Y2, S2 = kdn.fused_chunked_deltanet_forward(dq[:, cut:], dk[:, cut:], dvv[:, cut:], db[:, cut:], dd[:, cut:],
                                                 proj, 64, S1, mode="bf16")
     assert torch.equal(torch.cat([Y1, Y2], 1), Y)
     assert torch.equal(S2, S)
