@@ -178,6 +178,19 @@ int kdn_tp_out_proj(const void* y, const void* w, void* out, int out_dtype, floa
                     int32_t K, void* stream);
 
 /*
+ * Dense projection of one GPU, out = x w^T: the hybrid LM's q|k|v|beta, anchor q|k|v, output,
+ * SwiGLU and head projections (the bias-free nn.Linear layers of layers/kernel_deltanet_layer.py:
+ * 46-49, layers/hybrid_kernel_deltanet_block.py:43-45 and models/kernel_deltanet_lm.py:65).  x: [M, K] bf16, w: [N, K] bf16, both
+ * row-major and 16-byte aligned; fp32 accumulation; out: [M, ldo] (ldo = 0 means N; ldo >= N,
+ * ldo * element size a multiple of 16 bytes), columns [0, N) written, out_dtype KDN_DTYPE_F32 or
+ * KDN_DTYPE_BF16.  K % 64 == 0, any N >= 1.  M <= 64 streams the weight through a GEMV kernel
+ * (16 rows per pass); larger M runs the TMA-fed tcgen05 GEMM of kdn_tp_out_proj (128 x 256 tiles,
+ * partial tiles at the M and N edges).  No reference entry point.
+ */
+int kdn_linear(const void* x, const void* w, void* out, int out_dtype, int64_t M, int32_t N, int32_t K, int64_t ldo,
+               void* stream);
+
+/*
  * The two-phase (bandwidth-optimal) form of kdn_tp_out_proj for the same sum over ranks.
  * Every rank stores its tiles of y w^T into its own copy `out` of the symmetric [M, N] buffer
  * (out_dtype KDN_DTYPE_F32, or KDN_DTYPE_BF16: the switch sums the bf16 copies in fp32 and the
@@ -271,7 +284,8 @@ int kdn_decode_attention(const void* q, const void* k_cache, const void* v_cache
  *     may be x; with a residual, out must not alias x, residual or h_out.
  *   kdn_swiglu: out[r, j] = silu(gate_up[r, j]) * gate_up[r, d_ff + j]  (SwiGLU, :45-46);
  *     gate_up [n, 2 d_ff], out [n, d_ff].
- *   kdn_mixer_inputs: z [n, 3 H 64 + H] (the fused q|k|v|beta projection) -> q, k [n, H, 64]
+ *   kdn_mixer_inputs: z [n, 3 H 64 + H] (the fused q|k|v|beta projection; rows z_ld elements
+ *     apart, z_ld = 0 meaning contiguous, z_ld even for 2-element loads) -> q, k [n, H, 64]
  *     L2-normalised per head (layers/kernel_deltanet_layer.py:98-99), v [n, H, 64], and fp32
  *     beta = sigmoid(z_beta) [n, H] (serving/tensor_parallel_runner.py:62) and decay =
  *     sigmoid(logit_decay[h]) [n, H] (kernel_deltanet_layer.py:71-73).  d_head must be 64.
@@ -282,8 +296,38 @@ int kdn_rmsnorm(const void* x, int dtype, const void* weight, int weight_dtype, 
 int kdn_add_rmsnorm(const void* x, const void* residual, int dtype, const void* weight, int weight_dtype, void* h_out,
                     void* out, int64_t n, int32_t d, float eps, void* stream);
 int kdn_swiglu(const void* gate_up, void* out, int dtype, int64_t n, int32_t d_ff, void* stream);
-int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, const void* logit_decay,
-                     int logit_dtype, void* q, void* k, void* v, float* beta, float* decay, void* stream);
+int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, int64_t z_ld,
+                     const void* logit_decay, int logit_dtype, void* q, void* k, void* v, float* beta, float* decay,
+                     void* stream);
+
+/*
+ * The softmax anchors of the hybrid LM (models/upcycling_llama_bridge.py:138-140, 240-249: causal
+ * multi-head attention with rotate-half rotary positions; the reference calls torch SDPA), bf16,
+ * d_head 64.  Sequences are packed back to back: sequence i holds tokens [cu[i], cu[i + 1]) of the
+ * batch (cu_seqlens: device int64 [num_seqs + 1]); its keys and values live in row cache_rows[i]
+ * (device int64 [num_seqs], NULL = row i) of the caches [cache_batch, H, max_len, 64].
+ *   kdn_anchor_qkv: qkv [total_tokens, 3, H, 64] (the fused q|k|v projection) -> q and k rotated
+ *     at position t - cu[i] + start_pos[i] (start_pos: device int64 [num_seqs], NULL = 0) with
+ *     inv_freq = rope_theta^(-2j/64), angle = position * inv_freq in fp32; k and v are stored at
+ *     that position of the cache row, q into q_out: [H, total_tokens, 64] (q_head_major = 1, the
+ *     layout kdn_varlen_causal_attention reads) or [total_tokens, H, 64] (0, the layout of
+ *     kdn_decode_attention).  A position or row outside the cache is skipped and recorded for
+ *     kdn_device_error (code 1).
+ *   kdn_varlen_causal_attention: out[t, h] = softmax(q_t K^T / 8 over positions <= t) V for every
+ *     token t of every sequence, q head-major [H, total_tokens, 64], the keys/values read from the
+ *     cache rows (positions [0, T_i)); out [total_tokens, H, 64].  max_seqlen (host) bounds every
+ *     T_i and is at most max_len; a longer sequence is recorded for kdn_device_error (code 1).
+ *     fp32 accumulation of both products, P rounded to bf16, 2^x via ex2.approx.
+ * No reference entry points.
+ */
+int kdn_anchor_qkv(const void* qkv, int dtype, const int64_t* cu_seqlens, const int64_t* start_pos,
+                   const int64_t* cache_rows, int64_t num_seqs, int64_t total_tokens, int32_t H, int32_t d_head,
+                   float rope_theta, void* q_out, int q_head_major, void* k_cache, void* v_cache, int64_t cache_batch,
+                   int64_t max_len, void* stream);
+int kdn_varlen_causal_attention(const void* q, const void* k_cache, const void* v_cache, int dtype,
+                                const int64_t* cu_seqlens, const int64_t* cache_rows, int64_t num_seqs,
+                                int64_t total_tokens, int32_t H, int32_t d_head, int64_t cache_batch, int64_t max_len,
+                                int64_t max_seqlen, void* out, void* stream);
 
 /*
  * Layout change of a ragged serving batch (no reference counterpart; the reference packs
@@ -385,7 +429,8 @@ int kdn_fork_state(void* states, int64_t num_slots, int64_t bytes_per_slot,
  * kernels whose bounds checks skipped a bad index, or whose bounded waits gave up).
  * Synchronises `stream`.  *code_out = 0 when nothing was recorded; otherwise 1 = a slot,
  * length or offset out of range, 2 = fused tensor-core prefill wait, 3 = two-phase prefill
- * wait, 4 = decode wait, 5 = tensor-parallel projection wait, 6 = tensor-core lift wait.
+ * wait, 4 = decode wait, 5 = tensor-parallel projection wait, 6 = tensor-core lift wait,
+ * 7 = anchor attention wait.
  */
 int kdn_device_error(void* stream, int* code_out);
 

@@ -38,6 +38,10 @@ thread_local std::string g_last_error;
 thread_local kdn::LaunchMarks g_marks;       // armed by kdn_set_prefill_events for the next prefill
 thread_local int g_last_prefill_launches = 0;
 
+// kdn_linear: row counts up to this stream the weight through the GEMV kernel (in groups of 16 rows);
+// above it the tcgen05 GEMM's 128-row tiles are the better use of the weight bytes
+constexpr int64_t kLinearGemvRows = 64;
+
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -389,6 +393,28 @@ int kdn_tp_out_proj(const void* y, const void* w, void* out, int out_dtype, floa
   return ok();
 }
 
+int kdn_linear(const void* x, const void* w, void* out, int out_dtype, int64_t M, int32_t N, int32_t K, int64_t ldo,
+               void* stream) {
+  if (M < 0 || M > int64_t(0x7fffff00)) return fail(KDN_ERR_INVALID, "M=%lld outside [0, 2^31 - 256]", (long long)M);
+  if (N < 1 || K < 1) return fail(KDN_ERR_INVALID, "N=%d K=%d", N, K);
+  if (M == 0) return ok();
+  if (K % 64 != 0) return fail(KDN_ERR_UNSUPPORTED, "K=%d: a positive multiple of 64", K);
+  if (!x || !w || !out) return fail(KDN_ERR_INVALID, "x/w/out is NULL");
+  if (out_dtype != KDN_DTYPE_F32 && out_dtype != KDN_DTYPE_BF16) return fail(KDN_ERR_INVALID, "bad output dtype");
+  const int64_t es = out_dtype == KDN_DTYPE_BF16 ? 2 : 4;
+  if (ldo == 0) ldo = N;
+  if (ldo < N || (ldo * es) % 16 != 0)
+    return fail(KDN_ERR_INVALID, "ldo=%lld: at least N and a multiple of 16 bytes", (long long)ldo);
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16)) return fail(KDN_ERR_INVALID, "x/w/out must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = M <= kLinearGemvRows
+                      ? kdn::launch_gemv(x, w, out, out_dtype == KDN_DTYPE_BF16, M, N, K, ldo, st)
+                      : kdn::launch_linear(x, w, out, out_dtype == KDN_DTYPE_BF16, M, N, K, ldo, st);
+  if (e == cudaErrorNotSupported) return fail(KDN_ERR_UNSUPPORTED, "no tensor-map encoder in this driver");
+  if (e != cudaSuccess) return cuda_fail(e, "linear launch");
+  return ok();
+}
+
 int64_t kdn_tp_out_proj_tiles(int64_t M, int32_t N) {
   if (M < 0 || N < 256 || N % 256 != 0) return 0;
   return kdn::tp_proj_tiles(M, N);
@@ -501,18 +527,71 @@ int kdn_swiglu(const void* gate_up, void* out, int dtype, int64_t n, int32_t d_f
   return ok();
 }
 
-int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, const void* logit_decay,
-                     int logit_dtype, void* q, void* k, void* v, float* beta, float* decay, void* stream) {
+int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, int64_t z_ld,
+                     const void* logit_decay, int logit_dtype, void* q, void* k, void* v, float* beta, float* decay,
+                     void* stream) {
   if (n < 0 || H < 1) return fail(KDN_ERR_INVALID, "n=%lld H=%d", (long long)n, H);
   if (d_head != 64) return fail(KDN_ERR_UNSUPPORTED, "d_head=%d (the lift takes 64)", d_head);
+  const int64_t row = int64_t(3) * H * d_head + H;
+  if (z_ld == 0) z_ld = row;
+  if (z_ld < row) return fail(KDN_ERR_INVALID, "z_ld=%lld below the row length %lld", (long long)z_ld, (long long)row);
   if (n == 0) return ok();
   if (!z || !logit_decay || !q || !k || !v || !beta || !decay) return fail(KDN_ERR_INVALID, "a pointer is NULL");
   if (!float_dtype(dtype) || !float_dtype(logit_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
   if (!aligned(z, 4) || !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
     return fail(KDN_ERR_INVALID, "z must be 4-byte, q/k/v 16-byte aligned");
-  cudaError_t e = kdn::launch_mixer_inputs(z, dtype, n, H, logit_decay, logit_dtype, q, k, v, beta, decay,
+  cudaError_t e = kdn::launch_mixer_inputs(z, dtype, n, H, z_ld, logit_decay, logit_dtype, q, k, v, beta, decay,
                                            static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "mixer-input launch");
+  return ok();
+}
+
+int kdn_anchor_qkv(const void* qkv, int dtype, const int64_t* cu_seqlens, const int64_t* start_pos,
+                   const int64_t* cache_rows, int64_t num_seqs, int64_t total_tokens, int32_t H, int32_t d_head,
+                   float rope_theta, void* q_out, int q_head_major, void* k_cache, void* v_cache, int64_t cache_batch,
+                   int64_t max_len, void* stream) {
+  if (num_seqs < 1 || total_tokens < 0 || H < 1 || cache_batch < 1 || max_len < 1)
+    return fail(KDN_ERR_INVALID, "num_seqs=%lld total=%lld H=%d cache_batch=%lld max_len=%lld", (long long)num_seqs,
+                (long long)total_tokens, H, (long long)cache_batch, (long long)max_len);
+  if (d_head != 64) return fail(KDN_ERR_UNSUPPORTED, "d_head=%d (64 only)", d_head);
+  if (dtype != KDN_DTYPE_BF16) return fail(KDN_ERR_UNSUPPORTED, "bf16 only");
+  if (!(rope_theta > 0.f)) return fail(KDN_ERR_INVALID, "rope_theta must be positive");
+  if (total_tokens == 0) return ok();
+  if (!qkv || !cu_seqlens || !q_out || !k_cache || !v_cache) return fail(KDN_ERR_INVALID, "a pointer is NULL");
+  if (!aligned(qkv, 4) || !aligned(q_out, 4) || !aligned(k_cache, 4) || !aligned(v_cache, 4))
+    return fail(KDN_ERR_INVALID, "qkv/q_out/caches must be 4-byte aligned");
+  cudaError_t e = kdn::launch_anchor_qkv(qkv, cu_seqlens, start_pos, cache_rows, num_seqs, total_tokens, H, rope_theta,
+                                         q_out, q_head_major != 0, k_cache, v_cache, cache_batch, max_len,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "anchor q/k/v launch");
+  return ok();
+}
+
+int kdn_varlen_causal_attention(const void* q, const void* k_cache, const void* v_cache, int dtype,
+                                const int64_t* cu_seqlens, const int64_t* cache_rows, int64_t num_seqs,
+                                int64_t total_tokens, int32_t H, int32_t d_head, int64_t cache_batch, int64_t max_len,
+                                int64_t max_seqlen, void* out, void* stream) {
+  if (num_seqs < 1 || total_tokens < 0 || H < 1 || cache_batch < 1 || max_len < 1 || max_seqlen < 0)
+    return fail(KDN_ERR_INVALID, "num_seqs=%lld total=%lld H=%d cache_batch=%lld max_len=%lld max_seqlen=%lld",
+                (long long)num_seqs, (long long)total_tokens, H, (long long)cache_batch, (long long)max_len,
+                (long long)max_seqlen);
+  if (d_head != 64) return fail(KDN_ERR_UNSUPPORTED, "d_head=%d (64 only)", d_head);
+  if (dtype != KDN_DTYPE_BF16) return fail(KDN_ERR_UNSUPPORTED, "bf16 only");
+  if (max_seqlen > max_len) return fail(KDN_ERR_INVALID, "max_seqlen=%lld exceeds the cache (%lld)",
+                                        (long long)max_seqlen, (long long)max_len);
+  const int64_t lim = (int64_t(1) << 31) - 1024;  // tensor-map row coordinates are 32-bit
+  if (int64_t(H) * total_tokens > lim || cache_batch * H * max_len > lim)
+    return fail(KDN_ERR_UNSUPPORTED, "more than 2^31 - 1024 rows of 64 in q or the cache");
+  if (num_seqs * H > int64_t(0x7fffffff) || (max_seqlen + 255) / 256 > 65535)
+    return fail(KDN_ERR_UNSUPPORTED, "grid too large");
+  if (total_tokens == 0 || max_seqlen == 0) return ok();
+  if (!q || !k_cache || !v_cache || !cu_seqlens || !out) return fail(KDN_ERR_INVALID, "a pointer is NULL");
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 16))
+    return fail(KDN_ERR_INVALID, "q/caches/out must be 16-byte aligned");
+  cudaError_t e = kdn::launch_anchor_attention(q, k_cache, v_cache, cu_seqlens, cache_rows, num_seqs, total_tokens, H,
+                                               cache_batch, max_len, max_seqlen, out, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported) return fail(KDN_ERR_UNSUPPORTED, "no tensor-map encoder in this driver");
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return ok();
 }
 
@@ -735,7 +814,12 @@ int kdn_device_error(void* stream, int* code_out) {
   int code_lift = 0;
   e = kdn::lift_read_error(static_cast<cudaStream_t>(stream), &code_lift);
   if (e != cudaSuccess) return cuda_fail(e, "device error read");
-  *code_out = code ? code : (code_tc ? code_tc : (code_split ? code_split : (code_proj ? code_proj : code_lift)));
+  int code_attn = 0;
+  e = kdn::attn_read_error(static_cast<cudaStream_t>(stream), &code_attn);
+  if (e != cudaSuccess) return cuda_fail(e, "device error read");
+  *code_out = code ? code
+                   : (code_tc ? code_tc
+                              : (code_split ? code_split : (code_proj ? code_proj : (code_lift ? code_lift : code_attn))));
   return ok();
 }
 

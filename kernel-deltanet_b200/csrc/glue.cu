@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T* __restrict__ gu, T
 
 // one warp per (token, head): z row = [q (H*64) | k (H*64) | v (H*64) | beta logits (H)]
 __global__ void __launch_bounds__(256) mixer_inputs_kernel(const void* __restrict__ z, int dt, int64_t n, int H,
-                                                           const void* __restrict__ logit_decay, int lddt,
+                                                           int64_t ld, const void* __restrict__ logit_decay, int lddt,
                                                            void* __restrict__ q, void* __restrict__ k,
                                                            void* __restrict__ v, float* __restrict__ beta,
                                                            float* __restrict__ decay) {
@@ -172,8 +172,7 @@ __global__ void __launch_bounds__(256) mixer_inputs_kernel(const void* __restric
   if (item >= n * H) return;
   const int64_t r = item / H;
   const int h = int(item - r * H);
-  const int64_t ld = int64_t(3) * H * kDk + H;
-  const int64_t zr = r * ld;
+  const int64_t zr = r * ld;  // z row stride (elements)
   const int64_t o = item * kDk + 2 * lane;  // [n, H, 64] outputs
   float2 qv, kv, vv;
   if ((ld & 1) == 0) {
@@ -234,9 +233,10 @@ cudaError_t launch_swiglu(const void* gu, void* out, int dt, int64_t n, int f, c
   return cudaGetLastError();
 }
 
-cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, const void* logit_decay, int lddt, void* q,
-                                void* k, void* v, float* beta, float* decay, cudaStream_t stream) {
-  mixer_inputs_kernel<<<grid_for(n * H, 8), 256, 0, stream>>>(z, dt, n, H, logit_decay, lddt, q, k, v, beta, decay);
+cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, int64_t z_ld, const void* logit_decay,
+                                int lddt, void* q, void* k, void* v, float* beta, float* decay, cudaStream_t stream) {
+  mixer_inputs_kernel<<<grid_for(n * H, 8), 256, 0, stream>>>(z, dt, n, H, z_ld, logit_decay, lddt, q, k, v, beta,
+                                                              decay);
   return cudaGetLastError();
 }
 

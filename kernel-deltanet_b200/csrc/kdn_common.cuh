@@ -119,5 +119,6 @@ constexpr int kErrSplitWaitTimeout = 3;  // two-phase prefill: a bounded wait ga
 constexpr int kErrDecodeWaitTimeout = 4; // decode: a bounded wait gave up
 constexpr int kErrProjWaitTimeout = 5;   // tensor-parallel projection: a bounded wait gave up
 constexpr int kErrLiftWaitTimeout = 6;   // tensor-core lift: a bounded wait gave up
+constexpr int kErrAttnWaitTimeout = 7;   // anchor attention: a bounded wait gave up
 
 }  // namespace kdn

@@ -138,15 +138,36 @@ cudaError_t launch_tp_proj_reduce_peer(const void* Y, const void* W, void* const
                                        int K, cudaStream_t stream);
 int tp_proj_max_world();
 int64_t tp_proj_tiles(int64_t M, int N);
+// y = x w^T of one rank (store form, any N >= 1, output row stride ldo): the TMA-fed tcgen05 GEMM
+cudaError_t launch_linear(const void* x, const void* w, void* out, bool out_bf16, int64_t M, int N, int K, int64_t ldo,
+                          cudaStream_t stream);
 cudaError_t tp_proj_read_error(cudaStream_t stream, int* code);
+
+// ---------------------------------------------------------------- gemv.cu
+// y = x w^T for a few rows (bf16 in, fp32 accumulation, output row stride ldo); rows are taken in
+// groups of gemv_max_rows(), the weight streamed once per group
+int gemv_max_rows();
+cudaError_t launch_gemv(const void* x, const void* w, void* y, bool y_bf16, int64_t M, int N, int K, int64_t ldo,
+                        cudaStream_t stream);
 
 // ---------------------------------------------------------------- glue.cu
 // element-wise steps of the hybrid block: RMSNorm, SwiGLU, the mixer-input split
 cudaError_t launch_rmsnorm(const void* x, const void* res, const void* w, int wdt, void* h_out, void* out, int dt,
                            int64_t n, int d, float eps, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* gu, void* out, int dt, int64_t n, int f, cudaStream_t stream);
-cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, const void* logit_decay, int lddt, void* q,
-                                void* k, void* v, float* beta, float* decay, cudaStream_t stream);
+cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, int64_t z_ld, const void* logit_decay,
+                                int lddt, void* q, void* k, void* v, float* beta, float* decay, cudaStream_t stream);
+
+// ---------------------------------------------------------------- anchor_attn.cu
+// rotary q/k of the anchors' fused q|k|v rows, k/v into the KV cache, q head-major [H, n, 64] or [n, H, 64]
+cudaError_t launch_anchor_qkv(const void* qkv, const int64_t* cu, const int64_t* start, const int64_t* rows, int64_t B,
+                              int64_t n, int H, float theta, void* q_out, bool q_head_major, void* k_cache,
+                              void* v_cache, int64_t cache_batch, int64_t L, cudaStream_t stream);
+// varlen causal softmax attention (d = 64, bf16) of head-major q against the KV cache rows
+cudaError_t launch_anchor_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* cu,
+                                    const int64_t* rows, int64_t B, int64_t n, int H, int64_t cache_batch, int64_t L,
+                                    int64_t max_seqlen, void* out, cudaStream_t stream);
+cudaError_t attn_read_error(cudaStream_t stream, int* code);
 
 // ---------------------------------------------------------------- decode_attn.cu
 // one query per (sequence, head) against its cached keys [0, lengths[b]] (d = 64), split-K

@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const
   unsigned int* claim = reinterpret_cast<unsigned int*>(sm + T_CLAIM);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KT = a.K / kBK;
-  const int tiles_n = a.N / kBN;
+  const int tiles_n = (a.N + kBN - 1) / kBN;  // the last tile column may be partial (store form only)
   const int64_t tiles = ((a.M + kBM - 1) / kBM) * tiles_n;
   bool ok = true;
 
@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const
       const int n0 = int(t % tiles_n) * kBN;
       const int m0 = int((t / tiles_n) * kBM);
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += cols, ++sc) {
+      for (int c0 = 0; c0 < kBN && n0 + c0 < a.N; c0 += cols, ++sc) {  // blocks past N hold no output
         const uint32_t buf = sbase + T_STG + (sc & 1u) * kStgBytes;
         if (tid == 0 && sc >= 2) bulk_wait_read_le1();  // the store that last read this buffer is done
         tc::named_bar_sync(1, 32 * kEpiWarps);
@@ -634,7 +634,7 @@ __global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const
         tc::fence_proxy_async_smem();  // the block is visible to the TMA engine
         tc::named_bar_sync(1, 32 * kEpiWarps);
         if (tid == 0) {
-          tma_store_2d(&mapO, buf, n0 + c0, m0);  // rows past M are not written
+          tma_store_2d(&mapO, buf, n0 + c0, m0);  // rows past M and columns past N are not written
           tc::bulk_commit();
         }
       }
@@ -673,13 +673,14 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// the [M, N] output (fp32 or bf16), boxes of 128 bytes x 128 rows, 128-byte swizzle (the staged blocks)
-bool encode_output(CUtensorMap* map, void* base, int64_t M, int N, bool bf16) {
+// the [M, N] output (fp32 or bf16, rows ld elements apart), boxes of 128 bytes x 128 rows, 128-byte
+// swizzle (the staged blocks)
+bool encode_output(CUtensorMap* map, void* base, int64_t M, int N, bool bf16, int64_t ld) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return false;
   const cuuint64_t es = bf16 ? 2 : 4;
   const cuuint64_t dims[2] = {cuuint64_t(N), cuuint64_t(M)};
-  const cuuint64_t strides[1] = {cuuint64_t(N) * es};
+  const cuuint64_t strides[1] = {cuuint64_t(ld) * es};
   const cuuint32_t box[2] = {cuuint32_t(128 / es), cuuint32_t(kBM)};
   const cuuint32_t estr[2] = {1, 1};
   return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides,
@@ -707,7 +708,7 @@ cudaError_t launch(const ProjArgs& a, cudaStream_t stream) {
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
   CUtensorMap mapA, mapB, mapO;
   if (a.mode != kMulticastAdd && encode_operand(&mapA, a.Y, a.M, a.K, kBM) &&
-      encode_operand(&mapB, a.W, a.N, a.K, kBN) && encode_output(&mapO, a.out, a.M, a.N, a.out_bf16 != 0)) {
+      encode_operand(&mapB, a.W, a.N, a.K, kBN) && encode_output(&mapO, a.out, a.M, a.N, a.out_bf16 != 0, a.N)) {
     cudaError_t e =
         cudaFuncSetAttribute(tp_proj_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmemT));
     if (e != cudaSuccess) return e;
@@ -724,6 +725,32 @@ cudaError_t launch(const ProjArgs& a, cudaStream_t stream) {
 }  // namespace
 
 int64_t tp_proj_tiles(int64_t M, int N) { return ((M + kBM - 1) / kBM) * (N / kBN); }
+
+cudaError_t launch_linear(const void* x, const void* w, void* out, bool out_bf16, int64_t M, int N, int K, int64_t ldo,
+                          cudaStream_t stream) {
+  ProjArgs a{};
+  a.Y = static_cast<const __nv_bfloat16*>(x);
+  a.W = static_cast<const __nv_bfloat16*>(w);
+  a.out = static_cast<float*>(out);
+  a.out_bf16 = out_bf16 ? 1 : 0;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = kStore;
+  a.world = 1;
+  CUtensorMap mapA, mapB, mapO;
+  // operand rows past M / N read as zero; output rows and columns past them are clipped by the store
+  if (!encode_operand(&mapA, x, M, K, kBM) || !encode_operand(&mapB, w, N, K, kBN) ||
+      !encode_output(&mapO, out, M, N, out_bf16, ldo))
+    return cudaErrorNotSupported;
+  cudaError_t e =
+      cudaFuncSetAttribute(tp_proj_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmemT));
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((int64_t(N) + kBN - 1) / kBN);
+  const int64_t grid = tiles < sm_count() ? tiles : sm_count();
+  tp_proj_tma_kernel<<<unsigned(grid), kThrT, kProjSmemT, stream>>>(a, mapA, mapB, mapO);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_tp_proj(const void* Y, const void* W, void* out, bool out_bf16, float* out_mc, int64_t M, int N,
                            int K, cudaStream_t stream) {

@@ -69,6 +69,11 @@ SIGNATURES = {
     "kdn_prefill_launch_count": (_INT, []),
     "kdn_tp_out_proj": (_INT, [_P, _P, _P, _INT, _P, _I64, _I32, _I32, _P]),
     "kdn_tp_out_proj_tiles": (_I64, [_I64, _I32]),
+    "kdn_linear": (_INT, [_P, _P, _P, _INT, _I64, _I32, _I32, _I64, _P]),
+    "kdn_anchor_qkv": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I32, _I32, ctypes.c_float, _P, _INT, _P, _P, _I64,
+                              _I64, _P]),
+    "kdn_varlen_causal_attention": (_INT, [_P, _P, _P, _INT, _P, _P, _I64, _I64, _I32, _I32, _I64, _I64, _I64, _P,
+                                           _P]),
     "kdn_tp_out_proj_allreduce": (_INT, [_P, _P, _P, _P, _INT, _P, _P, _U32, _I32, _I32, _I64, _I32, _I32, _P]),
     "kdn_tp_out_proj_allreduce_peer": (_INT, [_P, _P, ctypes.POINTER(_P), _INT, ctypes.POINTER(_P), _U32, _I32, _I32,
                                               _I64, _I32, _I32, _P]),
@@ -78,7 +83,7 @@ SIGNATURES = {
     "kdn_rmsnorm": (_INT, [_P, _INT, _P, _INT, _P, _I64, _I32, ctypes.c_float, _P]),
     "kdn_add_rmsnorm": (_INT, [_P, _P, _INT, _P, _INT, _P, _P, _I64, _I32, ctypes.c_float, _P]),
     "kdn_swiglu": (_INT, [_P, _P, _INT, _I64, _I32, _P]),
-    "kdn_mixer_inputs": (_INT, [_P, _INT, _I64, _I32, _I32, _P, _INT, _P, _P, _P, _P, _P, _P]),
+    "kdn_mixer_inputs": (_INT, [_P, _INT, _I64, _I32, _I32, _I64, _P, _INT, _P, _P, _P, _P, _P, _P]),
     "kdn_copy_rows": (_INT, [_P, ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _P]),
     "kdn_affine_compose": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "kdn_affine_prefix_states": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _P]),

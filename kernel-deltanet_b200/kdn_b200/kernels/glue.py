@@ -1,10 +1,12 @@
 """Element-wise steps of the hybrid block on libkdn (one pass each; CUDA tensors only).
 
-``rms_norm`` (layers/hybrid_kernel_deltanet_block.py:23-25), ``swiglu_product`` (silu(gate) * up,
+``linear`` (the block's bias-free projections, kdn_linear), ``rms_norm``
+(layers/hybrid_kernel_deltanet_block.py:23-25), ``swiglu_product`` (silu(gate) * up,
 :45-46) and ``mixer_inputs`` (split of the fused q|k|v|beta projection: unit-norm q, k per head,
 v, beta = sigmoid, decay = sigmoid(logit_decay) per head) -- the C entries kdn_rmsnorm,
-kdn_swiglu and kdn_mixer_inputs -- and ``decode_attention`` (the anchors' one-token attention over
-their KV cache, kdn_decode_attention).  Errors raise RuntimeError; there is no CPU path.
+kdn_swiglu and kdn_mixer_inputs -- and the anchors' attention: ``anchor_qkv`` (rotary q/k and the KV-cache
+fill, kdn_anchor_qkv), ``varlen_causal_attention`` (packed causal prefill, kdn_varlen_causal_attention) and
+``decode_attention`` (one token over the cache, kdn_decode_attention).  Errors raise RuntimeError; there is no CPU path.
 """
 
 from __future__ import annotations
@@ -63,9 +65,10 @@ def swiglu_product(gate_up: torch.Tensor) -> torch.Tensor:
 
 
 def mixer_inputs(z: torch.Tensor, num_heads: int, logit_decay: torch.Tensor, d_head: int = 64):
-    """z [n, 3 H d_head + H] -> q, k (unit norm), v [n, H, d_head] in z's dtype; beta, decay [n, H] fp32."""
+    """z [n, 3 H d_head + H] (rows may be strided, as a padded projection output leaves them) ->
+    q, k (unit norm), v [n, H, d_head] in z's dtype; beta, decay [n, H] fp32."""
     _cuda(z, logit_decay)
-    zc = z.contiguous()
+    zc = z if (z.dim() == 2 and z.stride(1) == 1) else z.contiguous()
     n, H = zc.shape[0], num_heads
     if zc.shape[1] != 3 * H * d_head + H:
         raise RuntimeError(f"z has {zc.shape[1]} columns, expected {3 * H * d_head + H}")
@@ -74,11 +77,84 @@ def mixer_inputs(z: torch.Tensor, num_heads: int, logit_decay: torch.Tensor, d_h
     beta = torch.empty(n, H, device=z.device, dtype=torch.float32)
     decay = torch.empty_like(beta)
     ld = logit_decay.contiguous()
-    _lib.check(_lib.load().kdn_mixer_inputs(zc.data_ptr(), _lib.dtype_code(zc), n, H, d_head, ld.data_ptr(),
+    _lib.check(_lib.load().kdn_mixer_inputs(zc.data_ptr(), _lib.dtype_code(zc), n, H, d_head,
+                                            zc.stride(0) if n > 1 else 0, ld.data_ptr(),
                                             _lib.dtype_code(ld), q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                             beta.data_ptr(), decay.data_ptr(), _lib.stream_handle(z.device)),
                "kdn_mixer_inputs")
     return q, k, v, beta, decay
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """x [..., K] @ weight[N, K]^T on libkdn (kdn_linear: GEMV up to 64 rows, tcgen05 GEMM above), bf16
+    operands, fp32 accumulation, output in out_dtype (x's dtype by default; bf16 or fp32).  When N is not
+    a multiple of 16 bytes of output the rows are padded and the result is a strided view."""
+    _cuda(x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise RuntimeError("kdn linear takes bf16 operands")
+    out_dtype = out_dtype or x.dtype
+    K = x.shape[-1]
+    N = weight.shape[0]
+    if weight.shape[1] != K:
+        raise RuntimeError(f"weight is {tuple(weight.shape)}, x has {K} columns")
+    xc = x.reshape(-1, K)
+    if not xc.is_contiguous() or xc.data_ptr() % 16:
+        xc = xc.contiguous()
+    wc = weight if weight.is_contiguous() else weight.contiguous()
+    M = xc.shape[0]
+    per16 = 16 // torch.empty((), dtype=out_dtype).element_size()
+    ldo = (N + per16 - 1) // per16 * per16
+    buf = torch.empty(M, ldo, device=x.device, dtype=out_dtype)
+    _lib.check(_lib.load().kdn_linear(xc.data_ptr(), wc.data_ptr(), buf.data_ptr(), _lib.dtype_code(buf), M, N, K,
+                                      ldo, _lib.stream_handle(x.device)), "kdn_linear")
+    out = buf if ldo == N else buf[:, :N]
+    return out if x.dim() == 2 else out.reshape(*x.shape[:-1], N)
+
+
+def anchor_qkv(qkv: torch.Tensor, cu_seqlens: torch.Tensor, num_heads: int, rope_theta: float,
+               k_cache: torch.Tensor, v_cache: torch.Tensor, cache_rows: Optional[torch.Tensor] = None,
+               start_pos: Optional[torch.Tensor] = None, q_head_major: bool = True) -> torch.Tensor:
+    """qkv [n, 3 H 64] (bf16, q | k | v) of sequences packed by cu_seqlens (device int64 [B + 1]) -> rotated
+    q ([H, n, 64] head-major, or [n, H, 64]); rotated k and v are stored into the caches [rows, H, L, 64] at
+    position (t - cu[i] + start_pos[i]) of row cache_rows[i] (kdn_anchor_qkv)."""
+    _cuda(qkv, cu_seqlens, k_cache, v_cache)
+    n, H = qkv.shape[0], num_heads
+    if qkv.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise RuntimeError("anchor_qkv takes bf16 tensors")
+    if qkv.numel() != n * 3 * H * 64 or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise RuntimeError("qkv must be [n, 3 H 64]; caches contiguous [rows, H, L, 64]")
+    qc = qkv.contiguous()
+    cu = cu_seqlens.to(torch.int64).contiguous()
+    rows = cache_rows.to(torch.int64).contiguous() if cache_rows is not None else None
+    start = start_pos.to(torch.int64).contiguous() if start_pos is not None else None
+    q = torch.empty((H, n, 64) if q_head_major else (n, H, 64), device=qkv.device, dtype=qkv.dtype)
+    _lib.check(_lib.load().kdn_anchor_qkv(qc.data_ptr(), _lib.dtype_code(qc), cu.data_ptr(),
+                                          start.data_ptr() if start is not None else None,
+                                          rows.data_ptr() if rows is not None else None, cu.numel() - 1, n, H, 64,
+                                          float(rope_theta), q.data_ptr(), int(q_head_major), k_cache.data_ptr(),
+                                          v_cache.data_ptr(), k_cache.shape[0], k_cache.shape[2],
+                                          _lib.stream_handle(qkv.device)), "kdn_anchor_qkv")
+    return q
+
+
+def varlen_causal_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cu_seqlens: torch.Tensor,
+                            max_seqlen: int, cache_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Head-major q [H, n, 64] of packed sequences (cu_seqlens device int64 [B + 1], every length <= max_seqlen)
+    against their cache rows -> causal softmax(q K^T / 8) V, [n, H, 64] bf16 (kdn_varlen_causal_attention)."""
+    _cuda(q, k_cache, v_cache, cu_seqlens)
+    H, n, dh = q.shape
+    if not (q.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise RuntimeError("q and the caches must be contiguous")
+    cu = cu_seqlens.to(torch.int64).contiguous()
+    rows = cache_rows.to(torch.int64).contiguous() if cache_rows is not None else None
+    out = torch.empty(n, H, dh, device=q.device, dtype=q.dtype)
+    _lib.check(_lib.load().kdn_varlen_causal_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                                       _lib.dtype_code(q), cu.data_ptr(),
+                                                       rows.data_ptr() if rows is not None else None, cu.numel() - 1,
+                                                       n, H, dh, k_cache.shape[0], k_cache.shape[2], int(max_seqlen),
+                                                       out.data_ptr(), _lib.stream_handle(q.device)),
+               "kdn_varlen_causal_attention")
+    return out
 
 
 def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lengths: torch.Tensor,

@@ -24,8 +24,10 @@ Mixers:
   its hybrid models (models/upcycling_llama_bridge.py:240-249, anchors at [10, 21]):
   multi-head causal softmax attention with rotary positions (the retained Llama attention,
   rotate-half convention, models/upcycling_llama_bridge.py:138-140) and a KV cache for decode.
-  The prefill is library attention (torch SDPA); the one-token decode is libkdn's split-K
-  kdn_decode_attention, which reads only each sequence's live keys.
+  With bf16 weights the rotary q/k and the KV-cache fill are one libkdn kernel (kdn_anchor_qkv), the
+  packed causal prefill is libkdn's tcgen05 varlen attention (kdn_varlen_causal_attention) and the
+  one-token decode its split-K kdn_decode_attention, which reads only each sequence's live keys; the
+  fp32 verification mode runs torch's rotary and SDPA.
 """
 
 from __future__ import annotations
@@ -42,6 +44,21 @@ from ..kernels import glue
 from ..kernels.fwht import FastWalshHadamardProjection
 from ..serving.ragged import ragged_prefill
 from ..serving.vllm_kernel_deltanet_op import hybrid_recurrent_forward
+
+
+class Linear(nn.Linear):
+    """Bias-free projection (the nn.Linear(bias=False) layers of layers/kernel_deltanet_layer.py:46-49 and
+    layers/hybrid_kernel_deltanet_block.py:43-45).  bf16 weights run on libkdn's kdn_linear (a GEMV
+    kernel for decode-size batches, the TMA-fed tcgen05 GEMM for prefill), with no other path; fp32
+    weights -- the exact-arithmetic verification mode -- use torch's fp32 matmul."""
+
+    def __init__(self, in_features: int, out_features: int):
+        super().__init__(in_features, out_features, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.weight.dtype == torch.bfloat16:
+            return glue.linear(x, self.weight)
+        return F.linear(x, self.weight)
 
 
 class RMSNorm(nn.Module):
@@ -72,8 +89,8 @@ class SwiGLUFFN(nn.Module):
             d_ff = (int(d_model * 8 / 3) + 63) // 64 * 64
         self.d_ff = d_ff
         self.chunk_tokens = chunk_tokens
-        self.w_gate_up = nn.Linear(d_model, 2 * d_ff, bias=False)
-        self.w_down = nn.Linear(d_ff, d_model, bias=False)
+        self.w_gate_up = Linear(d_model, 2 * d_ff)
+        self.w_down = Linear(d_ff, d_model)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.shape[0] <= self.chunk_tokens:
@@ -92,10 +109,10 @@ class KernelDeltaNetMixer(nn.Module):
         super().__init__()
         self.num_heads, self.d_head, self.chunk_size, self.mode = num_heads, d_head, chunk_size, mode
         hd = num_heads * d_head
-        self.w_qkvb = nn.Linear(d_model, 3 * hd + num_heads, bias=False)  # q | k | v | beta rows
+        self.w_qkvb = Linear(d_model, 3 * hd + num_heads)  # q | k | v | beta rows
         init_logit = math.log(initial_decay / (1.0 - initial_decay + 1e-7))
         self.logit_decay = nn.Parameter(torch.full((num_heads,), float(init_logit)))
-        self.w_out = nn.Linear(hd, d_model, bias=False)
+        self.w_out = Linear(hd, d_model)
         self.fwht = FastWalshHadamardProjection(d_head, rkhs_dim, seed)
 
     def project(self, x: torch.Tensor):
@@ -145,18 +162,34 @@ class SoftmaxAnchor(nn.Module):
     def __init__(self, d_model: int, num_heads: int, d_head: int = 64, rope_theta: float = 10000.0):
         super().__init__()
         self.num_heads, self.d_head, self.rope_theta = num_heads, d_head, rope_theta
-        self.w_qkv = nn.Linear(d_model, 3 * num_heads * d_head, bias=False)
-        self.w_out = nn.Linear(num_heads * d_head, d_model, bias=False)
+        self.w_qkv = Linear(d_model, 3 * num_heads * d_head)
+        self.w_out = Linear(num_heads * d_head, d_model)
 
     def _qkv(self, x: torch.Tensor, pos: torch.Tensor):
         n, H, dh = x.shape[0], self.num_heads, self.d_head
         q, k, v = self.w_qkv(x).view(n, 3, H, dh).unbind(1)
         return rotary(q, pos, self.rope_theta), rotary(k, pos, self.rope_theta), v
 
+    def _native(self, x: torch.Tensor, k_cache: torch.Tensor) -> bool:
+        """bf16 activations and caches with 64-wide heads run on libkdn's anchor kernels."""
+        return x.dtype == torch.bfloat16 and k_cache.dtype == torch.bfloat16 and self.d_head == 64
+
     def prefill(self, x: torch.Tensor, cu: list, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                rows: list) -> torch.Tensor:
-        """cu: host list of sequence offsets; sequence i is written to cache row rows[i] from position 0."""
+                rows: list, cu_dev: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """cu: host list of sequence offsets (cu_dev: the same on the device, if the caller has it);
+        sequence i is written to cache row rows[i] from position 0."""
         n = x.shape[0]
+        if self._native(x, k_cache):
+            if n == 0:
+                return self.w_out(x.new_empty(0, self.num_heads * self.d_head))
+            B = len(cu) - 1
+            cu_t = cu_dev if cu_dev is not None else torch.tensor(cu, device=x.device, dtype=torch.int64)
+            rows_t = None if list(rows) == list(range(B)) else torch.tensor(rows, device=x.device, dtype=torch.int64)
+            q = glue.anchor_qkv(self.w_qkv(x), cu_t, self.num_heads, self.rope_theta, k_cache, v_cache, rows_t)
+            max_len = max(cu[i + 1] - cu[i] for i in range(B))
+            o = glue.varlen_causal_attention(q, k_cache, v_cache, cu_t, max_len, rows_t)
+            return self.w_out(o.view(n, -1))
+        # fp32 verification mode: torch rotary and SDPA per sequence
         pos = torch.cat([torch.arange(cu[i + 1] - cu[i], device=x.device) for i in range(len(cu) - 1)]) \
             if n else torch.zeros(0, dtype=torch.int64, device=x.device)
         q, k, v = self._qkv(x, pos)
@@ -178,6 +211,11 @@ class SoftmaxAnchor(nn.Module):
         positions [0, lengths[b]]; `span` is a host bound on max(lengths) + 1 (the key range read).  No
         host synchronisation: the step can be captured in a CUDA graph."""
         B = x.shape[0]
+        if self._native(x, k_cache) and k_cache.shape[0] == B:
+            cu = torch.arange(B + 1, device=x.device, dtype=torch.int64)  # one token per sequence
+            q = glue.anchor_qkv(self.w_qkv(x), cu, self.num_heads, self.rope_theta, k_cache, v_cache,
+                                start_pos=lengths, q_head_major=False)
+            return self.w_out(glue.decode_attention(q, k_cache, v_cache, lengths).reshape(B, -1))
         q, k, v = self._qkv(x, lengths)
         rows = torch.arange(B, device=x.device)
         k_cache[rows, :, lengths] = k

@@ -34,7 +34,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from ..layers.hybrid_kernel_deltanet_block import HybridKernelDeltaNetBlock, RMSNorm
+from ..layers.hybrid_kernel_deltanet_block import HybridKernelDeltaNetBlock, Linear, RMSNorm
 
 
 @dataclass
@@ -75,7 +75,7 @@ class KernelDeltaNetLM(nn.Module):
                                       mode=mode, rope_theta=rope_theta)
             for i in range(num_layers)])
         self.final_norm = RMSNorm(d_model)
-        self.lm_head = nn.Linear(d_model, vocab_size, bias=False)
+        self.lm_head = Linear(d_model, vocab_size)
         if tie_weights:
             self.lm_head.weight = self.embed.weight
         self.apply(self._init_weights)
@@ -127,7 +127,7 @@ class KernelDeltaNetLM(nn.Module):
         for li, layer in enumerate(self.layers):
             h = layer.norm1(x)
             if layer.anchor:
-                mixed = layer.mixer.prefill(h, cu, cache.k_cache[li], cache.v_cache[li], list(range(B)))
+                mixed = layer.mixer.prefill(h, cu, cache.k_cache[li], cache.v_cache[li], list(range(B)), cu_dev)
             else:
                 mixed = layer.mixer.prefill(h, cu_dev, cache.states[li], rows, fresh)
             x = layer.finish(x, mixed)
@@ -192,7 +192,7 @@ class KernelDeltaNetLM(nn.Module):
             for li, layer in enumerate(self.layers):
                 h = layer.norm1(x)
                 if layer.anchor:
-                    mixed = layer.mixer.prefill(h, cu, cache.k_cache[li], cache.v_cache[li], list(range(B)))
+                    mixed = layer.mixer.prefill(h, cu, cache.k_cache[li], cache.v_cache[li], list(range(B)), cu_dev)
                 else:
                     mixed = layer.mixer.prefill(h, cu_dev, cache.states[li], rows, fresh)
                 x = layer.finish(x, mixed)

@@ -1,4 +1,5 @@
-"""Element-wise kernels of the hybrid block (kdn_rmsnorm, kdn_add_rmsnorm, kdn_swiglu, kdn_mixer_inputs).
+"""Element-wise kernels of the hybrid block (kdn_rmsnorm, kdn_add_rmsnorm, kdn_swiglu, kdn_mixer_inputs) and
+its dense projection (kdn_linear).
 
 CPU: argument checks of the C entries (no device work).  GPU: each kernel against the same
 formula in torch fp32 -- fp32 storage within 1e-6 relative, bf16 storage within one bf16
@@ -23,9 +24,18 @@ def test_glue_argument_checks(lib):
     assert lib.kdn_add_rmsnorm(P, Q, 1, R, 0, P, O, 0, 2048, 1e-6, None) == 0      # nothing to do
     assert lib.kdn_swiglu(P, P, 0, 4, 6, None) == 2                        # d_ff not a multiple of 4 (fp32)
     assert lib.kdn_swiglu(None, P, 0, 4, 8, None) == 1
-    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 32, P, 0, P, P, P, P, P, None) == 2   # d_head must be 64
-    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, None, 0, P, P, P, P, P, None) == 1
-    assert lib.kdn_mixer_inputs(P, 1, 0, 2, 64, P, 0, P, P, P, P, P, None) == 0
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 32, 0, P, 0, P, P, P, P, P, None) == 2   # d_head must be 64
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, 0, None, 0, P, P, P, P, P, None) == 1
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, 385, P, 0, P, P, P, P, P, None) == 1  # z_ld below the row (386)
+    assert lib.kdn_mixer_inputs(P, 1, 0, 2, 64, 0, P, 0, P, P, P, P, P, None) == 0
+    assert lib.kdn_linear(P, P, P, 1, 4, 100, 96, 0, None) == 2      # K not a multiple of 64
+    assert lib.kdn_linear(P, P, P, 1, 4, 100, 128, 99, None) == 1    # ldo below N
+    assert lib.kdn_linear(P, P, P, 1, 4, 100, 128, 100, None) == 1   # ldo not a multiple of 16 bytes (bf16)
+    assert lib.kdn_linear(P, P, P, 0, 4, 100, 128, 102, None) == 1   # ... nor (fp32)
+    assert lib.kdn_linear(P + 2, P, P, 1, 4, 100, 128, 0, None) == 1  # misaligned x
+    assert lib.kdn_linear(P, P, None, 1, 4, 96, 128, 0, None) == 1   # no output
+    assert lib.kdn_linear(P, P, P, 5, 4, 96, 128, 0, None) == 1      # bad dtype
+    assert lib.kdn_linear(P, P, P, 1, 0, 96, 128, 0, None) == 0      # nothing to do
     assert lib.kdn_decode_attention(P, P, P, P, P, 1, 2, 4, 100, 32, P, 1 << 20, None) == 2   # d_head 64 only
     assert lib.kdn_decode_attention(P, None, P, P, P, 1, 2, 4, 100, 64, P, 1 << 20, None) == 1
     assert lib.kdn_decode_attention(P, P, P, P, P, 1, 2, 4, 100, 64, P, 8, None) == 4        # workspace too small
@@ -96,6 +106,64 @@ def test_mixer_inputs(dtype, H):
     assert torch.equal(v, z[:, 2 * H * 64:3 * H * 64].reshape(n, H, 64))
     assert _close(beta, torch.sigmoid(zf[:, 3 * H * 64:]), torch.float32)
     assert _close(decay, torch.sigmoid(ld).expand(n, H), torch.float32)
+
+
+@pytest.mark.gpu
+def test_mixer_inputs_strided_rows():
+    """A padded projection output (rows wider than 3 H 64 + H) splits like its contiguous copy."""
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(2)
+    n, H = 70, 2
+    wide = torch.randn(n, 3 * H * 64 + H + 6, generator=g, device="cuda").to(torch.bfloat16)
+    z = wide[:, :3 * H * 64 + H]
+    ld = torch.randn(H, generator=g, device="cuda")
+    for a, b in zip(glue.mixer_inputs(z, H, ld), glue.mixer_inputs(z.contiguous(), H, ld)):
+        assert torch.equal(a, b)
+
+
+# (M, N, K): decode-size rows (GEMV, 4/8/16-row buckets and a second pass), the GEMM's partial tiles at the
+# M and N edges (N below one 256-column tile, odd N, the LM's 6176 / 32000), and K of one and many steps
+_LINEAR_SHAPES = [(1, 263, 128), (3, 2048, 2048), (8, 6176, 2048), (13, 386, 128), (16, 2048, 8192), (40, 7, 64),
+                  (64, 512, 256), (65, 128, 256), (200, 386, 128), (300, 263, 128), (1000, 6176, 2048),
+                  (777, 32000, 2048), (2048, 2048, 8192)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", _LINEAR_SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_linear_vs_fp32_matmul(M, N, K, out_dtype):
+    """kdn_linear against torch's fp32 product of the same bf16 operands: fp32 output within 1e-5 of the
+    largest |x||w| row-column product scale (accumulation order only), bf16 output within one bf16 rounding."""
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") / K ** 0.5).to(torch.bfloat16)
+    y = glue.linear(x, w, out_dtype=out_dtype)
+    ref = x.double() @ w.double().t()
+    assert y.shape == (M, N) and y.dtype == out_dtype
+    scale = float((x.double().norm(dim=1).max() * w.double().norm(dim=1).max()))
+    err = (y.double() - ref).abs()
+    if out_dtype == torch.float32:
+        assert float(err.max()) <= 1e-5 * scale
+    else:
+        assert bool((err <= 2.0 ** -8 * ref.abs() + 1e-5 * scale).all())
+
+
+@pytest.mark.gpu
+def test_linear_batched_input_and_launch_forms():
+    """A [B, T, K] input gives the [B, T, N] product; the GEMV (M <= 64) and GEMM forms agree on the
+    same rows."""
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(2, 70, 256, generator=g, device="cuda").to(torch.bfloat16)
+    w = torch.randn(384, 256, generator=g, device="cuda").to(torch.bfloat16)
+    y = glue.linear(x, w, out_dtype=torch.float32)
+    assert y.shape == (2, 70, 384)
+    rows = glue.linear(x.reshape(140, 256)[:50].contiguous(), w, out_dtype=torch.float32)
+    assert float((y.reshape(140, 384)[:50] - rows).abs().max()) <= 1e-5 * float(rows.abs().max())
 
 
 @pytest.mark.gpu
