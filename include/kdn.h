@@ -191,6 +191,18 @@ int kdn_linear(const void* x, const void* w, void* out, int out_dtype, int64_t M
                void* stream);
 
 /*
+ * SwiGLU's gate and up projections with the product fused into the GEMM epilogue
+ * (layers/hybrid_kernel_deltanet_block.py:43-46: silu(x W_gate^T) * (x W_up^T)): out[m, j] =
+ * silu(g) * u with g = x[m] . W_gate[j], u = x[m] . W_up[j] accumulated in fp32, stored as bf16
+ * [M, ldo] (ldo = 0 means d_ff).  w_interleaved [2 d_ff, K] bf16 holds the two weights in row
+ * blocks of 128: rows [256 t, 256 t + 128) are W_gate rows [128 t, 128 t + 128) and the next 128
+ * the same W_up rows.  d_ff % 128 == 0, K % 64 == 0, pointers 16-byte aligned.  The gate/up product
+ * never reaches memory.  No reference entry point.
+ */
+int kdn_linear_swiglu(const void* x, const void* w_interleaved, void* out, int64_t M, int32_t d_ff, int32_t K,
+                      int64_t ldo, void* stream);
+
+/*
  * The two-phase (bandwidth-optimal) form of kdn_tp_out_proj for the same sum over ranks.
  * Every rank stores its tiles of y w^T into its own copy `out` of the symmetric [M, N] buffer
  * (out_dtype KDN_DTYPE_F32, or KDN_DTYPE_BF16: the switch sums the bf16 copies in fp32 and the

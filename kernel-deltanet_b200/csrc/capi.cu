@@ -415,6 +415,25 @@ int kdn_linear(const void* x, const void* w, void* out, int out_dtype, int64_t M
   return ok();
 }
 
+int kdn_linear_swiglu(const void* x, const void* w_interleaved, void* out, int64_t M, int32_t d_ff, int32_t K,
+                      int64_t ldo, void* stream) {
+  if (M < 0 || M > int64_t(0x7fffff00)) return fail(KDN_ERR_INVALID, "M=%lld outside [0, 2^31 - 256]", (long long)M);
+  if (d_ff < 128 || d_ff % 128 != 0) return fail(KDN_ERR_UNSUPPORTED, "d_ff=%d: a positive multiple of 128", d_ff);
+  if (K < 64 || K % 64 != 0) return fail(KDN_ERR_UNSUPPORTED, "K=%d: a positive multiple of 64", K);
+  if (M == 0) return ok();
+  if (!x || !w_interleaved || !out) return fail(KDN_ERR_INVALID, "x/w/out is NULL");
+  if (ldo == 0) ldo = d_ff;
+  if (ldo < d_ff || (ldo * 2) % 16 != 0)
+    return fail(KDN_ERR_INVALID, "ldo=%lld: at least d_ff and a multiple of 16 bytes", (long long)ldo);
+  if (!aligned(x, 16) || !aligned(w_interleaved, 16) || !aligned(out, 16))
+    return fail(KDN_ERR_INVALID, "x/w/out must be 16-byte aligned");
+  cudaError_t e = kdn::launch_linear(x, w_interleaved, out, true, M, 2 * d_ff, K, ldo, static_cast<cudaStream_t>(stream),
+                                     true);
+  if (e == cudaErrorNotSupported) return fail(KDN_ERR_UNSUPPORTED, "no tensor-map encoder in this driver");
+  if (e != cudaSuccess) return cuda_fail(e, "linear-swiglu launch");
+  return ok();
+}
+
 int64_t kdn_tp_out_proj_tiles(int64_t M, int32_t N) {
   if (M < 0 || N < 256 || N % 256 != 0) return 0;
   return kdn::tp_proj_tiles(M, N);

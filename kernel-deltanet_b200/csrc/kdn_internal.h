@@ -138,9 +138,11 @@ cudaError_t launch_tp_proj_reduce_peer(const void* Y, const void* W, void* const
                                        int K, cudaStream_t stream);
 int tp_proj_max_world();
 int64_t tp_proj_tiles(int64_t M, int N);
-// y = x w^T of one rank (store form, any N >= 1, output row stride ldo): the TMA-fed tcgen05 GEMM
+// y = x w^T of one rank (store form, any N >= 1, output row stride ldo): the TMA-fed tcgen05 GEMM.
+// swiglu: w holds gate/up row blocks of 128 interleaved (N = 2 d_ff, d_ff % 128 == 0) and the epilogue
+// stores silu(gate) * up, [M, d_ff] bf16 (ldo elements apart)
 cudaError_t launch_linear(const void* x, const void* w, void* out, bool out_bf16, int64_t M, int N, int K, int64_t ldo,
-                          cudaStream_t stream);
+                          cudaStream_t stream, bool swiglu = false);
 cudaError_t tp_proj_read_error(cudaStream_t stream, int* code);
 
 // ---------------------------------------------------------------- gemv.cu

@@ -74,6 +74,7 @@ struct ProjArgs {
   int N, K;
   int mode, rank, world;
   int out_bf16;  // modes 0 and 3: the output copies hold bf16 (the sum is still formed in fp32)
+  int swiglu;    // store form: tile columns [0, 128) are gate and [128, 256) up; out = silu(gate) * up
   uint32_t target;  // counter value meaning "every rank has announced this tile" in this call
   float* peer_out[kMaxWorld];        // mode 3: every rank's copy of the output (this rank's included)
   uint32_t* peer_flags[kMaxWorld];   // mode 3: every rank's copy of the tile counters
@@ -593,19 +594,37 @@ __global__ void __launch_bounds__(kThrT, 1) tp_proj_tma_kernel(ProjArgs a, const
     uint32_t tcount = 0, sc = 0;
     const int r = 32 * warp + lane;
     const int cols = a.out_bf16 ? 64 : 32;  // columns per staged block (128 bytes a row)
+    const int tile_cols = a.swiglu ? kBN / 2 : kBN;  // output columns of a tile
+    const int n_lim = a.swiglu ? a.N / 2 : a.N;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++tcount) {
       const uint32_t ab = tcount & 1u;
       ok &= proj_wait(&accf[ab], (tcount >> 1) & 1u);
       tc::fence_after_sync();
-      const int n0 = int(t % tiles_n) * kBN;
+      const int n0 = int(t % tiles_n) * tile_cols;  // first output column of the tile
       const int m0 = int((t / tiles_n) * kBM);
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN && n0 + c0 < a.N; c0 += cols, ++sc) {  // blocks past N hold no output
+      for (int c0 = 0; c0 < tile_cols && n0 + c0 < n_lim; c0 += cols, ++sc) {  // blocks past N hold no output
         const uint32_t buf = sbase + T_STG + (sc & 1u) * kStgBytes;
         if (tid == 0 && sc >= 2) bulk_wait_read_le1();  // the store that last read this buffer is done
         tc::named_bar_sync(1, 32 * kEpiWarps);
         uint32_t w[32];  // the row's 128 bytes
-        if (a.out_bf16) {
+        if (a.swiglu) {  // bf16 out: silu(gate) * up, gate in accumulator column c, up in c + 128
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float gv[32], uv[32];
+            const uint32_t col = tmem + (uint32_t(32 * warp) << 16) + kBN * ab + c0 + 32 * h;
+            tc::tmem_ld32(col, gv);
+            tc::tmem_ld32(col + kBN / 2, uv);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = gv[2 * e] / (1.f + expf(-gv[2 * e])) * uv[2 * e];
+              const float p1 = gv[2 * e + 1] / (1.f + expf(-gv[2 * e + 1])) * uv[2 * e + 1];
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+              w[16 * h + e] = *reinterpret_cast<const uint32_t*>(&b2);
+            }
+          }
+        } else if (a.out_bf16) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float v[32];
@@ -727,8 +746,9 @@ cudaError_t launch(const ProjArgs& a, cudaStream_t stream) {
 int64_t tp_proj_tiles(int64_t M, int N) { return ((M + kBM - 1) / kBM) * (N / kBN); }
 
 cudaError_t launch_linear(const void* x, const void* w, void* out, bool out_bf16, int64_t M, int N, int K, int64_t ldo,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, bool swiglu) {
   ProjArgs a{};
+  a.swiglu = swiglu ? 1 : 0;
   a.Y = static_cast<const __nv_bfloat16*>(x);
   a.W = static_cast<const __nv_bfloat16*>(w);
   a.out = static_cast<float*>(out);
@@ -741,7 +761,7 @@ cudaError_t launch_linear(const void* x, const void* w, void* out, bool out_bf16
   CUtensorMap mapA, mapB, mapO;
   // operand rows past M / N read as zero; output rows and columns past them are clipped by the store
   if (!encode_operand(&mapA, x, M, K, kBM) || !encode_operand(&mapB, w, N, K, kBN) ||
-      !encode_output(&mapO, out, M, N, out_bf16, ldo))
+      !encode_output(&mapO, out, M, swiglu ? N / 2 : N, out_bf16, ldo))
     return cudaErrorNotSupported;
   cudaError_t e =
       cudaFuncSetAttribute(tp_proj_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kProjSmemT));

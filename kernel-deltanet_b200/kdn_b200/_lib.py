@@ -70,6 +70,7 @@ SIGNATURES = {
     "kdn_tp_out_proj": (_INT, [_P, _P, _P, _INT, _P, _I64, _I32, _I32, _P]),
     "kdn_tp_out_proj_tiles": (_I64, [_I64, _I32]),
     "kdn_linear": (_INT, [_P, _P, _P, _INT, _I64, _I32, _I32, _I64, _P]),
+    "kdn_linear_swiglu": (_INT, [_P, _P, _P, _I64, _I32, _I32, _I64, _P]),
     "kdn_anchor_qkv": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I32, _I32, ctypes.c_float, _P, _INT, _P, _P, _I64,
                               _I64, _P]),
     "kdn_varlen_causal_attention": (_INT, [_P, _P, _P, _INT, _P, _P, _I64, _I64, _I32, _I32, _I64, _I64, _I64, _P,

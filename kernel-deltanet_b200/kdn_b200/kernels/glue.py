@@ -85,10 +85,12 @@ def mixer_inputs(z: torch.Tensor, num_heads: int, logit_decay: torch.Tensor, d_h
     return q, k, v, beta, decay
 
 
-def linear(x: torch.Tensor, weight: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+def linear(x: torch.Tensor, weight: torch.Tensor, out_dtype: Optional[torch.dtype] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x [..., K] @ weight[N, K]^T on libkdn (kdn_linear: GEMV up to 64 rows, tcgen05 GEMM above), bf16
     operands, fp32 accumulation, output in out_dtype (x's dtype by default; bf16 or fp32).  When N is not
-    a multiple of 16 bytes of output the rows are padded and the result is a strided view."""
+    a multiple of 16 bytes of output the rows are padded and the result is a strided view.  `out`: a
+    contiguous [M, N] tensor (rows 16-byte aligned) to write into instead."""
     _cuda(x, weight)
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
         raise RuntimeError("kdn linear takes bf16 operands")
@@ -102,13 +104,46 @@ def linear(x: torch.Tensor, weight: torch.Tensor, out_dtype: Optional[torch.dtyp
         xc = xc.contiguous()
     wc = weight if weight.is_contiguous() else weight.contiguous()
     M = xc.shape[0]
-    per16 = 16 // torch.empty((), dtype=out_dtype).element_size()
-    ldo = (N + per16 - 1) // per16 * per16
-    buf = torch.empty(M, ldo, device=x.device, dtype=out_dtype)
+    if out is not None:
+        if out.shape != (M, N) or not out.is_contiguous() or out.dtype != out_dtype:
+            raise RuntimeError(f"out must be a contiguous [{M}, {N}] {out_dtype} tensor")
+        buf, ldo = out, N
+    else:
+        per16 = 16 // torch.empty((), dtype=out_dtype).element_size()
+        ldo = (N + per16 - 1) // per16 * per16
+        buf = torch.empty(M, ldo, device=x.device, dtype=out_dtype)
     _lib.check(_lib.load().kdn_linear(xc.data_ptr(), wc.data_ptr(), buf.data_ptr(), _lib.dtype_code(buf), M, N, K,
                                       ldo, _lib.stream_handle(x.device)), "kdn_linear")
     out = buf if ldo == N else buf[:, :N]
     return out if x.dim() == 2 else out.reshape(*x.shape[:-1], N)
+
+
+def swiglu_interleave(w_gate_up: torch.Tensor) -> torch.Tensor:
+    """[2 d_ff, K] (gate rows, then up rows) -> the row-block interleaved layout kdn_linear_swiglu reads
+    (128 gate rows, the same 128 up rows, ...)."""
+    f2, K = w_gate_up.shape
+    f = f2 // 2
+    if f2 % 256:
+        raise RuntimeError("d_ff must be a multiple of 128")
+    return w_gate_up.view(2, f // 128, 128, K).transpose(0, 1).reshape(f2, K).contiguous()
+
+
+def linear_swiglu(x: torch.Tensor, w_interleaved: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(x W_gate^T) * (x W_up^T), [M, d_ff] bf16, from the interleaved weight (kdn_linear_swiglu: the
+    product is formed in the GEMM epilogue)."""
+    _cuda(x, w_interleaved)
+    if x.dtype != torch.bfloat16 or w_interleaved.dtype != torch.bfloat16:
+        raise RuntimeError("kdn linear_swiglu takes bf16 operands")
+    xc = x if (x.is_contiguous() and x.data_ptr() % 16 == 0) else x.contiguous()
+    M, K = xc.shape
+    f = w_interleaved.shape[0] // 2
+    if out is None:
+        out = torch.empty(M, f, device=x.device, dtype=torch.bfloat16)
+    elif out.shape != (M, f) or not out.is_contiguous() or out.dtype != torch.bfloat16:
+        raise RuntimeError(f"out must be a contiguous [{M}, {f}] bf16 tensor")
+    _lib.check(_lib.load().kdn_linear_swiglu(xc.data_ptr(), w_interleaved.data_ptr(), out.data_ptr(), M, f, K, f,
+                                             _lib.stream_handle(x.device)), "kdn_linear_swiglu")
+    return out
 
 
 def anchor_qkv(qkv: torch.Tensor, cu_seqlens: torch.Tensor, num_heads: int, rope_theta: float,

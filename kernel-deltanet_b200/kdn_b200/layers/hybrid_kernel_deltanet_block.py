@@ -92,11 +92,31 @@ class SwiGLUFFN(nn.Module):
         self.w_gate_up = Linear(d_model, 2 * d_ff)
         self.w_down = Linear(d_ff, d_model)
 
+    def _interleaved(self) -> torch.Tensor:
+        """The gate/up weight in the row-block interleaved layout of kdn_linear_swiglu (rebuilt when the
+        parameter changes)."""
+        w = self.w_gate_up.weight
+        key = (w.data_ptr(), w._version, w.dtype)
+        if getattr(self, "_il_key", None) != key:
+            self._il = glue.swiglu_interleave(w.detach())
+            self._il_key = key
+        return self._il
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if x.shape[0] <= self.chunk_tokens:
+        n = x.shape[0]
+        if self.w_gate_up.weight.dtype == torch.bfloat16 and x.dim() == 2 and n > 64 and self.d_ff % 128 == 0:
+            # prefill: silu(gate) * up formed in the gate/up GEMM's epilogue, the down projection written
+            # straight into its rows of the output
+            w_il = self._interleaved()
+            out = torch.empty(n, self.w_down.out_features, device=x.device, dtype=x.dtype)
+            for s in range(0, n, self.chunk_tokens):
+                glue.linear(glue.linear_swiglu(x[s:s + self.chunk_tokens], w_il), self.w_down.weight,
+                            out=out[s:s + self.chunk_tokens])
+            return out
+        if n <= self.chunk_tokens:
             return self.w_down(glue.swiglu_product(self.w_gate_up(x)))
         out = torch.empty_like(x)
-        for s in range(0, x.shape[0], self.chunk_tokens):
+        for s in range(0, n, self.chunk_tokens):
             out[s:s + self.chunk_tokens] = self.w_down(glue.swiglu_product(self.w_gate_up(x[s:s + self.chunk_tokens])))
         return out
 

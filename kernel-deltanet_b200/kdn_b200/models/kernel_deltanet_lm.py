@@ -123,18 +123,32 @@ class KernelDeltaNetLM(nn.Module):
         cu_dev = torch.tensor(cu, device=dev, dtype=torch.int64)
         rows = torch.arange(B, device=dev)
         fresh = torch.ones(B, dtype=torch.bool)
-        x = self.embed(ids)
+        x, delta = self._prefill_body(self.embed(ids), cu, cu_dev, cache, rows, fresh)
+        cache.lengths = lens
+        cache.lengths_dev = torch.tensor(lens, device=dev, dtype=torch.int64)
+        last = cu_dev[1:] - 1
+        if delta is None:  # no blocks
+            return self.lm_head(self.final_norm(x[last]))
+        return self.lm_head(self.final_norm.add_forward(x[last], delta[last])[1])
+
+    def _prefill_body(self, x: torch.Tensor, cu: list, cu_dev: torch.Tensor, cache: HybridCache,
+                      rows: torch.Tensor, fresh: torch.Tensor):
+        """The blocks over a packed batch; returns (x, delta) with the last FFN output `delta` not yet
+        added to the residual stream x (each residual add runs fused with the RMSNorm after it)."""
+        B = len(cu) - 1
+        delta = None
         for li, layer in enumerate(self.layers):
-            h = layer.norm1(x)
+            if delta is None:
+                h = layer.norm1(x)
+            else:
+                x, h = layer.norm1.add_forward(x, delta)
             if layer.anchor:
                 mixed = layer.mixer.prefill(h, cu, cache.k_cache[li], cache.v_cache[li], list(range(B)), cu_dev)
             else:
                 mixed = layer.mixer.prefill(h, cu_dev, cache.states[li], rows, fresh)
-            x = layer.finish(x, mixed)
-        cache.lengths = lens
-        cache.lengths_dev = torch.tensor(lens, device=dev, dtype=torch.int64)
-        last = cu_dev[1:] - 1
-        return self.lm_head(self.final_norm(x[last]))
+            x, h = layer.norm2.add_forward(x, mixed)
+            delta = layer.ffn(h)
+        return x, delta
 
     def _decode_body(self, tokens: torch.Tensor, cache: HybridCache, span: int) -> torch.Tensor:
         """Device work of one decode step (no host synchronisation; capturable in a CUDA graph)."""
@@ -188,15 +202,9 @@ class KernelDeltaNetLM(nn.Module):
         rows = torch.arange(B, device=dev)
         fresh = torch.ones(B, dtype=torch.bool)
         with torch.no_grad():
-            x = self.embed(input_ids.to(dev).reshape(-1))
-            for li, layer in enumerate(self.layers):
-                h = layer.norm1(x)
-                if layer.anchor:
-                    mixed = layer.mixer.prefill(h, cu, cache.k_cache[li], cache.v_cache[li], list(range(B)), cu_dev)
-                else:
-                    mixed = layer.mixer.prefill(h, cu_dev, cache.states[li], rows, fresh)
-                x = layer.finish(x, mixed)
-            logits = self.lm_head(self.final_norm(x)).view(B, T, -1)
+            x, delta = self._prefill_body(self.embed(input_ids.to(dev).reshape(-1)), cu, cu_dev, cache, rows, fresh)
+            h = self.final_norm(x) if delta is None else self.final_norm.add_forward(x, delta)[1]
+            logits = self.lm_head(h).view(B, T, -1)
         loss = None
         if targets is not None:
             loss = F.cross_entropy(logits.float().view(-1, self.vocab_size), targets.to(dev).view(-1))

@@ -36,6 +36,11 @@ def test_glue_argument_checks(lib):
     assert lib.kdn_linear(P, P, None, 1, 4, 96, 128, 0, None) == 1   # no output
     assert lib.kdn_linear(P, P, P, 5, 4, 96, 128, 0, None) == 1      # bad dtype
     assert lib.kdn_linear(P, P, P, 1, 0, 96, 128, 0, None) == 0      # nothing to do
+    assert lib.kdn_linear_swiglu(P, P, P, 4, 192, 128, 0, None) == 2   # d_ff not a multiple of 128
+    assert lib.kdn_linear_swiglu(P, P, P, 4, 256, 96, 0, None) == 2    # K not a multiple of 64
+    assert lib.kdn_linear_swiglu(P, P, None, 4, 256, 128, 0, None) == 1
+    assert lib.kdn_linear_swiglu(P, P, P, 4, 256, 128, 255, None) == 1  # ldo below d_ff
+    assert lib.kdn_linear_swiglu(P, P, P, 0, 256, 128, 0, None) == 0
     assert lib.kdn_decode_attention(P, P, P, P, P, 1, 2, 4, 100, 32, P, 1 << 20, None) == 2   # d_head 64 only
     assert lib.kdn_decode_attention(P, None, P, P, P, 1, 2, 4, 100, 64, P, 1 << 20, None) == 1
     assert lib.kdn_decode_attention(P, P, P, P, P, 1, 2, 4, 100, 64, P, 8, None) == 4        # workspace too small
@@ -149,6 +154,23 @@ def test_linear_vs_fp32_matmul(M, N, K, out_dtype):
         assert float(err.max()) <= 1e-5 * scale
     else:
         assert bool((err <= 2.0 ** -8 * ref.abs() + 1e-5 * scale).all())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,F,K", [(65, 128, 64), (300, 384, 256), (1000, 8192, 2048), (129, 256, 8192)])
+def test_linear_swiglu_vs_fp32(M, F, K):
+    """The fused gate/up GEMM + SwiGLU epilogue against silu(g) * u from the float64 products of the same
+    bf16 operands: within one bf16 rounding plus 1e-5 of the output scale."""
+    from kdn_b200.kernels import glue
+
+    g = torch.Generator(device="cuda").manual_seed(M + F)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(2 * F, K, generator=g, device="cuda") / K ** 0.5).to(torch.bfloat16)
+    y = glue.linear_swiglu(x, glue.swiglu_interleave(w))
+    gu = x.double() @ w.double().t()
+    ref = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+    assert y.shape == (M, F) and y.dtype == torch.bfloat16
+    assert bool(((y.double() - ref).abs() <= 2.0 ** -8 * ref.abs() + 1e-5 * float(ref.abs().max())).all())
 
 
 @pytest.mark.gpu
