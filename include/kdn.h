@@ -300,7 +300,10 @@ int kdn_decode_attention(const void* q, const void* k_cache, const void* v_cache
  *     apart, z_ld = 0 meaning contiguous, z_ld even for 2-element loads) -> q, k [n, H, 64]
  *     L2-normalised per head (layers/kernel_deltanet_layer.py:98-99), v [n, H, 64], and fp32
  *     beta = sigmoid(z_beta) [n, H] (serving/tensor_parallel_runner.py:62) and decay =
- *     sigmoid(logit_decay[h]) [n, H] (kernel_deltanet_layer.py:71-73).  d_head must be 64.
+ *     sigmoid(logit_decay[h]) [n, H] (kernel_deltanet_layer.py:71-73).  d_head must be 64.  With
+ *     cu_seqlens (device int64 [num_seqs + 1], the packing of kdn_ragged_transpose) the outputs are
+ *     written in the head-major per-sequence layout instead (row cu[i] H + h T_i + t), the layout
+ *     kdn_chunked_prefill_varlen reads, so no separate transpose is needed; NULL keeps [n, H].
  * No reference entry points (the reference runs these as separate torch ops).
  */
 int kdn_rmsnorm(const void* x, int dtype, const void* weight, int weight_dtype, void* out, int64_t n, int32_t d,
@@ -309,8 +312,8 @@ int kdn_add_rmsnorm(const void* x, const void* residual, int dtype, const void* 
                     void* out, int64_t n, int32_t d, float eps, void* stream);
 int kdn_swiglu(const void* gate_up, void* out, int dtype, int64_t n, int32_t d_ff, void* stream);
 int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, int64_t z_ld,
-                     const void* logit_decay, int logit_dtype, void* q, void* k, void* v, float* beta, float* decay,
-                     void* stream);
+                     const void* logit_decay, int logit_dtype, const int64_t* cu_seqlens, int64_t num_seqs, void* q,
+                     void* k, void* v, float* beta, float* decay, void* stream);
 
 /*
  * The softmax anchors of the hybrid LM (models/upcycling_llama_bridge.py:138-140, 240-249: causal

@@ -547,8 +547,8 @@ int kdn_swiglu(const void* gate_up, void* out, int dtype, int64_t n, int32_t d_f
 }
 
 int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_head, int64_t z_ld,
-                     const void* logit_decay, int logit_dtype, void* q, void* k, void* v, float* beta, float* decay,
-                     void* stream) {
+                     const void* logit_decay, int logit_dtype, const int64_t* cu_seqlens, int64_t num_seqs, void* q,
+                     void* k, void* v, float* beta, float* decay, void* stream) {
   if (n < 0 || H < 1) return fail(KDN_ERR_INVALID, "n=%lld H=%d", (long long)n, H);
   if (d_head != 64) return fail(KDN_ERR_UNSUPPORTED, "d_head=%d (the lift takes 64)", d_head);
   const int64_t row = int64_t(3) * H * d_head + H;
@@ -559,7 +559,9 @@ int kdn_mixer_inputs(const void* z, int dtype, int64_t n, int32_t H, int32_t d_h
   if (!float_dtype(dtype) || !float_dtype(logit_dtype)) return fail(KDN_ERR_INVALID, "bad dtype");
   if (!aligned(z, 4) || !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
     return fail(KDN_ERR_INVALID, "z must be 4-byte, q/k/v 16-byte aligned");
-  cudaError_t e = kdn::launch_mixer_inputs(z, dtype, n, H, z_ld, logit_decay, logit_dtype, q, k, v, beta, decay,
+  if (cu_seqlens && num_seqs < 1) return fail(KDN_ERR_INVALID, "num_seqs=%lld with cu_seqlens", (long long)num_seqs);
+  cudaError_t e = kdn::launch_mixer_inputs(z, dtype, n, H, z_ld, logit_decay, logit_dtype, cu_seqlens, num_seqs, q, k,
+                                           v, beta, decay,
                                            static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "mixer-input launch");
   return ok();

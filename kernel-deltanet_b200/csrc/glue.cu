@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T* __restrict__ gu, T
 // one warp per (token, head): z row = [q (H*64) | k (H*64) | v (H*64) | beta logits (H)]
 __global__ void __launch_bounds__(256) mixer_inputs_kernel(const void* __restrict__ z, int dt, int64_t n, int H,
                                                            int64_t ld, const void* __restrict__ logit_decay, int lddt,
+                                                           const int64_t* __restrict__ cu, int64_t num_seqs,
                                                            void* __restrict__ q, void* __restrict__ k,
                                                            void* __restrict__ v, float* __restrict__ beta,
                                                            float* __restrict__ decay) {
@@ -173,7 +174,18 @@ __global__ void __launch_bounds__(256) mixer_inputs_kernel(const void* __restric
   const int64_t r = item / H;
   const int h = int(item - r * H);
   const int64_t zr = r * ld;  // z row stride (elements)
-  const int64_t o = item * kDk + 2 * lane;  // [n, H, 64] outputs
+  int64_t dst = item;         // output row: [n, H] token-major, or head-major per sequence
+  if (cu) {
+    int64_t lo = 0, hi = num_seqs - 1;  // the sequence holding token r: the last b with cu[b] <= r
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (cu[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int64_t c0 = cu[lo];
+    dst = c0 * H + int64_t(h) * (cu[lo + 1] - c0) + (r - c0);
+  }
+  const int64_t o = dst * kDk + 2 * lane;
   float2 qv, kv, vv;
   if ((ld & 1) == 0) {
     qv = ld2_as_f32(z, dt, zr + int64_t(h) * kDk + 2 * lane);
@@ -195,8 +207,8 @@ __global__ void __launch_bounds__(256) mixer_inputs_kernel(const void* __restric
   st2_from_f32(v, dt, o, vv.x, vv.y);
   if (lane == 0) {
     const float bl = ld_as_f32(z, dt, zr + int64_t(3) * H * kDk + h);
-    beta[item] = 1.f / (1.f + expf(-bl));
-    decay[item] = 1.f / (1.f + expf(-ld_as_f32(logit_decay, lddt, h)));
+    beta[dst] = 1.f / (1.f + expf(-bl));
+    decay[dst] = 1.f / (1.f + expf(-ld_as_f32(logit_decay, lddt, h)));
   }
 }
 
@@ -234,9 +246,10 @@ cudaError_t launch_swiglu(const void* gu, void* out, int dt, int64_t n, int f, c
 }
 
 cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, int64_t z_ld, const void* logit_decay,
-                                int lddt, void* q, void* k, void* v, float* beta, float* decay, cudaStream_t stream) {
-  mixer_inputs_kernel<<<grid_for(n * H, 8), 256, 0, stream>>>(z, dt, n, H, z_ld, logit_decay, lddt, q, k, v, beta,
-                                                              decay);
+                                int lddt, const int64_t* cu, int64_t num_seqs, void* q, void* k, void* v, float* beta,
+                                float* decay, cudaStream_t stream) {
+  mixer_inputs_kernel<<<grid_for(n * H, 8), 256, 0, stream>>>(z, dt, n, H, z_ld, logit_decay, lddt, cu, num_seqs, q,
+                                                              k, v, beta, decay);
   return cudaGetLastError();
 }
 

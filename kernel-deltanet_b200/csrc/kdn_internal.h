@@ -158,7 +158,8 @@ cudaError_t launch_rmsnorm(const void* x, const void* res, const void* w, int wd
                            int64_t n, int d, float eps, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* gu, void* out, int dt, int64_t n, int f, cudaStream_t stream);
 cudaError_t launch_mixer_inputs(const void* z, int dt, int64_t n, int H, int64_t z_ld, const void* logit_decay,
-                                int lddt, void* q, void* k, void* v, float* beta, float* decay, cudaStream_t stream);
+                                int lddt, const int64_t* cu, int64_t num_seqs, void* q, void* k, void* v, float* beta,
+                                float* decay, cudaStream_t stream);
 
 // ---------------------------------------------------------------- anchor_attn.cu
 // rotary q/k of the anchors' fused q|k|v rows, k/v into the KV cache, q head-major [H, n, 64] or [n, H, 64]

@@ -84,7 +84,7 @@ SIGNATURES = {
     "kdn_rmsnorm": (_INT, [_P, _INT, _P, _INT, _P, _I64, _I32, ctypes.c_float, _P]),
     "kdn_add_rmsnorm": (_INT, [_P, _P, _INT, _P, _INT, _P, _P, _I64, _I32, ctypes.c_float, _P]),
     "kdn_swiglu": (_INT, [_P, _P, _INT, _I64, _I32, _P]),
-    "kdn_mixer_inputs": (_INT, [_P, _INT, _I64, _I32, _I32, _I64, _P, _INT, _P, _P, _P, _P, _P, _P]),
+    "kdn_mixer_inputs": (_INT, [_P, _INT, _I64, _I32, _I32, _I64, _P, _INT, _P, _I64, _P, _P, _P, _P, _P, _P]),
     "kdn_copy_rows": (_INT, [_P, ctypes.c_size_t, _P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _P]),
     "kdn_affine_compose": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "kdn_affine_prefix_states": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _P]),

@@ -64,9 +64,12 @@ def swiglu_product(gate_up: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def mixer_inputs(z: torch.Tensor, num_heads: int, logit_decay: torch.Tensor, d_head: int = 64):
+def mixer_inputs(z: torch.Tensor, num_heads: int, logit_decay: torch.Tensor, d_head: int = 64,
+                 cu_seqlens: Optional[torch.Tensor] = None):
     """z [n, 3 H d_head + H] (rows may be strided, as a padded projection output leaves them) ->
-    q, k (unit norm), v [n, H, d_head] in z's dtype; beta, decay [n, H] fp32."""
+    q, k (unit norm), v [n, H, d_head] in z's dtype; beta, decay [n, H] fp32.  With cu_seqlens (device
+    int64 [B + 1]) the same-shaped outputs hold the head-major per-sequence layout (sequence i's head h
+    at rows cu[i] H + h T_i ...), the layout the ragged prefill consumes."""
     _cuda(z, logit_decay)
     zc = z if (z.dim() == 2 and z.stride(1) == 1) else z.contiguous()
     n, H = zc.shape[0], num_heads
@@ -77,9 +80,11 @@ def mixer_inputs(z: torch.Tensor, num_heads: int, logit_decay: torch.Tensor, d_h
     beta = torch.empty(n, H, device=z.device, dtype=torch.float32)
     decay = torch.empty_like(beta)
     ld = logit_decay.contiguous()
+    cu = cu_seqlens.to(torch.int64).contiguous() if cu_seqlens is not None else None
     _lib.check(_lib.load().kdn_mixer_inputs(zc.data_ptr(), _lib.dtype_code(zc), n, H, d_head,
-                                            zc.stride(0) if n > 1 else 0, ld.data_ptr(),
-                                            _lib.dtype_code(ld), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                            zc.stride(0) if n > 1 else 0, ld.data_ptr(), _lib.dtype_code(ld),
+                                            cu.data_ptr() if cu is not None else None,
+                                            cu.numel() - 1 if cu is not None else 0, q.data_ptr(), k.data_ptr(), v.data_ptr(),
                                             beta.data_ptr(), decay.data_ptr(), _lib.stream_handle(z.device)),
                "kdn_mixer_inputs")
     return q, k, v, beta, decay

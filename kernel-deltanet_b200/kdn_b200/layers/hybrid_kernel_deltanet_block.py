@@ -143,10 +143,12 @@ class KernelDeltaNetMixer(nn.Module):
                 fresh: torch.Tensor) -> torch.Tensor:
         """Packed prefill: every sequence starts from a zero state where `fresh` (else from its slot)
         and leaves its final state in `states[slots[i]]`."""
-        q, k, v, beta, decay = self.project(x)
+        # q, k, v, beta, decay come out in the head-major per-sequence layout the prefill reads
+        q, k, v, beta, decay = glue.mixer_inputs(self.w_qkvb(x), self.num_heads, self.logit_decay, self.d_head,
+                                                 cu_seqlens=cu_seqlens)
         y = torch.empty_like(v)
         ragged_prefill(q, k, v, beta, decay, cu_seqlens, states, slots, y, self.fwht, self.chunk_size,
-                       mode=self.mode, initial_state_mask=~fresh)
+                       mode=self.mode, initial_state_mask=~fresh, head_major_inputs=True)
         return self.w_out(y.view(x.shape[0], -1))
 
     def decode(self, x: torch.Tensor, states: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:

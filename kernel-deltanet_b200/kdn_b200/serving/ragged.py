@@ -7,7 +7,7 @@ keeps one recurrent state per stream.  Here:
 
     ragged_prefill(query, key, value, beta, decay, cu_seqlens, recurrent_states,
                    slot_mapping, output, fwht_proj=None, chunk_size=64, mode=None,
-                   initial_state_mask=None)
+                   initial_state_mask=None, head_major_inputs=False)
 
 * ``query``/``key`` [total_tokens, H, d_k], ``value``/``output`` [total_tokens, H, d_v],
   ``beta``/``decay`` [total_tokens, H] (``decay`` may be None: 1), packed back to back;
@@ -17,6 +17,9 @@ keeps one recurrent state per stream.  Here:
   place.  ``initial_state_mask[i] = False`` starts sequence i from zeros instead (a new
   request whose slot holds a stale state).  Slots must be distinct.
 * ``output`` is written in place; everything runs on the current CUDA stream.
+* ``head_major_inputs=True``: query/key/value/beta/decay (same shapes) already hold the
+  per-sequence head-major layout below (as ``kdn_mixer_inputs`` writes it given
+  ``cu_seqlens``), so their transposes are skipped; ``output`` stays packed.
 
 The packed tensors are moved to per-sequence head-major blocks ([H, T_i, .], no padding)
 by ``kdn_ragged_transpose``.  In bf16 mode a batch with at least as many (sequence, head)
@@ -102,7 +105,8 @@ def ragged_prefill(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, 
                    decay: Optional[torch.Tensor], cu_seqlens: torch.Tensor, recurrent_states: torch.Tensor,
                    slot_mapping: torch.Tensor, output: torch.Tensor,
                    fwht_proj: Optional[FastWalshHadamardProjection] = None, chunk_size: int = 64,
-                   mode: Optional[str] = None, initial_state_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+                   mode: Optional[str] = None, initial_state_mask: Optional[torch.Tensor] = None,
+                   head_major_inputs: bool = False) -> torch.Tensor:
     # ---------------------------------------------------------------- host-side checks
     if query.dim() != 3 or key.shape != query.shape:
         raise RuntimeError(f"query/key must be [total_tokens, H, d_k]; got {tuple(query.shape)}, {tuple(key.shape)}")
@@ -150,11 +154,17 @@ def ragged_prefill(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, 
     cu_dev = cu.to(dev)
     in_dtype = query.dtype if query.dtype in (torch.float32, torch.bfloat16) else torch.float32
     gate_dtype = beta.dtype if beta.dtype in (torch.float32, torch.bfloat16) else torch.float32
-    qh = _to_head_major(lib, query.to(in_dtype).contiguous(), cu_dev, num_seqs, H, dev)
-    kh = _to_head_major(lib, key.to(in_dtype).contiguous(), cu_dev, num_seqs, H, dev)
-    vh = _to_head_major(lib, value.to(in_dtype).contiguous(), cu_dev, num_seqs, H, dev)
-    bh = _to_head_major(lib, beta.to(gate_dtype).contiguous(), cu_dev, num_seqs, H, dev)
-    dh = _to_head_major(lib, decay.to(gate_dtype).contiguous(), cu_dev, num_seqs, H, dev) if decay is not None else None
+    if head_major_inputs:  # already laid out per sequence and head (kdn_mixer_inputs with cu_seqlens)
+        qh, kh, vh = (t.to(in_dtype).contiguous() for t in (query, key, value))
+        bh = beta.to(gate_dtype).contiguous()
+        dh = decay.to(gate_dtype).contiguous() if decay is not None else None
+    else:
+        qh = _to_head_major(lib, query.to(in_dtype).contiguous(), cu_dev, num_seqs, H, dev)
+        kh = _to_head_major(lib, key.to(in_dtype).contiguous(), cu_dev, num_seqs, H, dev)
+        vh = _to_head_major(lib, value.to(in_dtype).contiguous(), cu_dev, num_seqs, H, dev)
+        bh = _to_head_major(lib, beta.to(gate_dtype).contiguous(), cu_dev, num_seqs, H, dev)
+        dh = (_to_head_major(lib, decay.to(gate_dtype).contiguous(), cu_dev, num_seqs, H, dev)
+              if decay is not None else None)
     yh = torch.empty(total * H * dv, device=dev, dtype=output.dtype if output.dtype in (torch.float32, torch.bfloat16)
                      else in_dtype)
 

@@ -24,10 +24,10 @@ def test_glue_argument_checks(lib):
     assert lib.kdn_add_rmsnorm(P, Q, 1, R, 0, P, O, 0, 2048, 1e-6, None) == 0      # nothing to do
     assert lib.kdn_swiglu(P, P, 0, 4, 6, None) == 2                        # d_ff not a multiple of 4 (fp32)
     assert lib.kdn_swiglu(None, P, 0, 4, 8, None) == 1
-    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 32, 0, P, 0, P, P, P, P, P, None) == 2   # d_head must be 64
-    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, 0, None, 0, P, P, P, P, P, None) == 1
-    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, 385, P, 0, P, P, P, P, P, None) == 1  # z_ld below the row (386)
-    assert lib.kdn_mixer_inputs(P, 1, 0, 2, 64, 0, P, 0, P, P, P, P, P, None) == 0
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 32, 0, P, 0, None, 0, P, P, P, P, P, None) == 2   # d_head must be 64
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, 0, None, 0, None, 0, P, P, P, P, P, None) == 1
+    assert lib.kdn_mixer_inputs(P, 1, 4, 2, 64, 385, P, 0, None, 0, P, P, P, P, P, None) == 1  # z_ld below the row (386)
+    assert lib.kdn_mixer_inputs(P, 1, 0, 2, 64, 0, P, 0, None, 0, P, P, P, P, P, None) == 0
     assert lib.kdn_linear(P, P, P, 1, 4, 100, 96, 0, None) == 2      # K not a multiple of 64
     assert lib.kdn_linear(P, P, P, 1, 4, 100, 128, 99, None) == 1    # ldo below N
     assert lib.kdn_linear(P, P, P, 1, 4, 100, 128, 100, None) == 1   # ldo not a multiple of 16 bytes (bf16)
@@ -111,6 +111,28 @@ def test_mixer_inputs(dtype, H):
     assert torch.equal(v, z[:, 2 * H * 64:3 * H * 64].reshape(n, H, 64))
     assert _close(beta, torch.sigmoid(zf[:, 3 * H * 64:]), torch.float32)
     assert _close(decay, torch.sigmoid(ld).expand(n, H), torch.float32)
+
+
+@pytest.mark.gpu
+def test_mixer_inputs_head_major_layout():
+    """With cu_seqlens the split writes the ragged head-major layout: the same values as the packed split
+    moved by kdn_ragged_transpose."""
+    from kdn_b200.kernels import glue
+    from kdn_b200.serving.ragged import _to_head_major
+    from kdn_b200 import _lib
+
+    g = torch.Generator(device="cuda").manual_seed(4)
+    H, lens = 3, [5, 1, 40, 17]
+    n = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), device="cuda", dtype=torch.int64)
+    z = torch.randn(n, 3 * H * 64 + H, generator=g, device="cuda").to(torch.bfloat16)
+    ld = torch.randn(H, generator=g, device="cuda")
+    packed = glue.mixer_inputs(z, H, ld)
+    hm = glue.mixer_inputs(z, H, ld, cu_seqlens=cu)
+    lib = _lib.load()
+    for a, b in zip(packed, hm):
+        moved = _to_head_major(lib, a.contiguous(), cu, len(lens), H, torch.device("cuda"))
+        assert torch.equal(moved.view(-1), b.reshape(-1))
 
 
 @pytest.mark.gpu
