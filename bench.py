@@ -833,7 +833,10 @@ def run_case(name: str):
       tp_proj      the TMA-fed projection kernel, one rank: Y [32768, 512] x W [2048, 512]^T, bf16 -> fp32
       decode_attn  split-K decode attention, bf16 caches [8, 32, 16384, 64], live lengths 4096..16383
       backward     the prefill backward (exact fp32), 16 heads x 4096 tokens, decay 1
-      lift         the standalone feature lift, 4 x 65536 unit vectors, bf16 in and out"""
+      lift         the standalone feature lift, 4 x 65536 unit vectors, bf16 in and out
+      anchor_attn  the anchors' varlen causal attention, 4 sequences x 8192 tokens x 32 heads (bf16)
+      lm           the config-4 LM (22 blocks, random init): a prefill of 2 sequences (4096 + 8192 tokens)
+                   and 2 eager decode steps (every LM kernel, for a launch list)"""
     import torch
 
     import kdn_b200
@@ -859,6 +862,31 @@ def run_case(name: str):
         x = torch.nn.functional.normalize(torch.randn(4, 65536, 64, generator=g, device=dev), dim=-1).bfloat16()
         p = kdn_b200.FastWalshHadamardProjection().to(dev)
         call = lambda: p(x)
+    elif name == "anchor_attn":
+        from kdn_b200.kernels.glue import varlen_causal_attention
+
+        Ha, La, Ba = 32, 8192, 4
+        n = Ba * La
+        q = torch.randn(Ha, n, 64, generator=g, device=dev).bfloat16()
+        kc = torch.randn(Ba, Ha, La, 64, generator=g, device=dev).bfloat16()
+        vc = torch.randn(Ba, Ha, La, 64, generator=g, device=dev).bfloat16()
+        cu = torch.arange(0, n + 1, La, device=dev, dtype=torch.int64)
+        call = lambda: varlen_causal_attention(q, kc, vc, cu, La)
+    elif name == "lm":
+        from kdn_b200.models import KernelDeltaNetLM
+
+        torch.manual_seed(0)
+        with torch.device(dev):
+            model = KernelDeltaNetLM(mode="bf16")
+        model = model.to(dev, torch.bfloat16).eval()
+        lens = [4096, 8192]
+        ids = torch.randint(0, model.vocab_size, (sum(lens),), generator=g, device=dev)
+        cache = model.new_cache(len(lens), max(lens) + 8)
+
+        def call():
+            model.prefill(ids, [0, lens[0], sum(lens)], cache)
+            for _ in range(2):
+                model.decode_step(torch.zeros(len(lens), dtype=torch.int64, device=dev), cache)
     elif name == "backward":
         Nb, Tb = 16, 4096
         q = torch.nn.functional.normalize(torch.randn(Nb, Tb, 64, generator=g, device=dev), dim=-1)
@@ -896,7 +924,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-only", type=int, nargs=2, metavar=("N", "T"),
                     help="only run two prefill calls of N sequences x T tokens (for profiler captures)")
-    ap.add_argument("--case", choices=["tp_proj", "decode_attn", "backward", "lift"],
+    ap.add_argument("--case", choices=["tp_proj", "decode_attn", "backward", "lift", "anchor_attn", "lm"],
                     help="only run one fixed single-kernel invocation three times (for profiler captures)")
     ap.add_argument("--decode-only", type=int, metavar="STEPS",
                     help="only run the decode workload for STEPS steps (for profiler captures)")
