@@ -34,8 +34,6 @@
 #include <stdlib.h>
 #include <string.h>
 
-#include <atomic>
-
 #include "kdn_internal.h"
 #include "tc_chunk.cuh"
 
@@ -64,13 +62,6 @@ constexpr uint32_t REC_S0 = 164864;   // 64 KiB  state entering the chunk, S^T f
                                       //          32 KiB h, each MN-major SW64 [512 features x 32]
 constexpr uint32_t REC_E = 230400;    // 8 KiB   E fp16, halves at 4 KiB h, MN-major SW64 [64 tokens x 32]
 constexpr uint32_t REC_BYTES = 238592;
-// Pair path (chunks 2p, 2p+1 share one step of the state pass): the record of the first chunk
-// keeps the state entering the pair at REC_S0 as two row halves (features 256h..256h+255 at
-// 32 KiB h, fp16 MN-major SW128 [256 x 64]); the second chunk's REC_S0 holds the cross terms
-//   REC_H  = T'_1 U_k1 U_k0^T                                    (fp16 K-major SW128 [64 x 64])
-//   REC_PX = diag(yqs_1) U_q1 U_k0^T diag(ew_0)                  (fp16 K-major SW128 [64 x 64])
-constexpr uint32_t REC_H = REC_S0;
-constexpr uint32_t REC_PX = REC_S0 + 8192;
 
 struct SplitArgs {
   TcArgs a;
@@ -95,18 +86,6 @@ __device__ __forceinline__ void set_abort(uint32_t* abort) {
 __device__ __forceinline__ bool split_wait(uint64_t* bar, uint32_t parity, uint32_t* abort) {
   uint32_t n = 0;
   while (!tc::mbar_try_wait(bar, parity)) {
-    if ((++n & 1023u) == 0 && (n >= kWaitLimit || aborted(abort))) {
-      set_abort(abort);
-      return false;
-    }
-  }
-  return true;
-}
-
-// the same for a barrier that threads of the other CTA of the cluster arrive on
-__device__ __forceinline__ bool split_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* abort) {
-  uint32_t n = 0;
-  while (!tc::mbar_try_wait_cluster(bar, parity)) {
     if ((++n & 1023u) == 0 && (n >= kWaitLimit || aborted(abort))) {
       set_abort(abort);
       return false;
@@ -178,43 +157,13 @@ constexpr uint32_t P1_PH = 212992;    // 2 KiB  phase b[512]
 constexpr uint32_t P1_GL = 215040;    // 5 x 256 B gates: g, beta, exp(g), exp(g_{i-1}), exp(g_{C-1} - g)
 constexpr uint32_t P1_SSP = 216320;   // 2 KiB  sums of squares per column quarter
 constexpr uint32_t P1_SC = 218368;    // 512 B  token scales
-constexpr uint32_t P1_EW0 = 218880;   // 256 B  (pairs) ew of the pair's first chunk, for the second
-constexpr uint32_t P1_BAR = 219136;   // mbarriers + TMEM address
-constexpr uint32_t kP1Bars = 160;      // bytes of barriers
+constexpr uint32_t P1_BAR = 218880;   // mbarriers + TMEM address
+constexpr uint32_t kP1Bars = 144;      // bytes of barriers
 constexpr uint32_t kP1Smem = P1_BAR + kP1Bars + 1024;
 static_assert(P1_VEC + 1024 <= P1_F1 && P1_F1 + 32768 <= P1_ES && P1_ES + 64 * kEsLd * 4 <= P1_VB,
               "phase-1 shared-memory regions overlap");
-// Pairs (the second chunk of a pair also forms the products with the first chunk's features):
-//   P1_ES during the slice loop: the first chunk's U_k slice, reloaded from its record (16 KiB);
-//   P1_F1 during the algebra: G10 = U_k1 U_k0^T (fp16, MN-major SW128 [64 x 64], B operand of H),
-//   then the staged H = T'_1 G10 and P' = diag(yqs_1) U_q1 U_k0^T diag(ew_0) (fp16 K-major SW128).
-constexpr uint32_t P1_G10 = P1_F1;
-constexpr uint32_t P1_HST = P1_F1 + 8192;
-constexpr uint32_t P1_PXST = P1_F1 + 16384;
-constexpr uint32_t P1_GP2 = 384;  // TMEM: [U_k1; U_q1] U_k0^T, 64 cols
-constexpr uint32_t P1_H = 448;    // TMEM: [T'_1; T_1 diag(beta)] G10, 64 cols (rows 0..63 = H)
 
 __device__ __forceinline__ uint32_t p1_fbuf(int s) { return (s & 1) ? P1_F1 : P1_F; }  // slice s's features
-
-// The j-th chunk the preparation CTA `cta` of `ncta` takes (false past its last one).  Single
-// chunks go chunk-major (record c N + n at cta + j ncta); pairs go pair-major, the two chunks of
-// a pair back to back on one CTA (chunk 2p + (j & 1) of sequence n for unit p N + n).
-template <bool kPair>
-__device__ __forceinline__ bool prep_item(const SplitArgs& sa, int64_t cta, int64_t ncta, int64_t j, int64_t& n,
-                                          int64_t& c) {
-  if (kPair) {
-    const int64_t u = cta + (j >> 1) * ncta;
-    if (u >= sa.N * (sa.a.NC >> 1)) return false;
-    n = u % sa.N;
-    c = 2 * (u / sa.N) + (j & 1);
-    return true;
-  }
-  const int64_t idx = cta + j * ncta;
-  if (idx >= sa.N * sa.a.NC) return false;
-  n = idx % sa.N;
-  c = idx / sa.N;
-  return true;
-}
 
 // Level d of the blocked inverse T = (I + A)^-1 (16x16 blocks, T row-major in Es with rows kEsLd apart,
 // A in the float4-swizzled layout of sx()): for the blocks I - J = d,
@@ -258,7 +207,6 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
 // Phase 1 on CTAs cta = 0..ncta-1 (576 threads: 16 compute warps, an MMA issuer and a record
 // publisher; `tmem` = 512 allocated columns).  With rec_ready, each finished record is
 // published there (1) for the state pass.
-template <bool kPair>
 __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams& P, uint8_t* sm, uint32_t tmem,
                                           int64_t cta, int64_t ncta, uint32_t* rec_ready, bool& ok) {
   const TcArgs& a = sa.a;
@@ -286,8 +234,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   uint64_t* bar_fdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 128);  // [2] the Gram product of the slice
                                                                           //     in buffer s & 1 done and its
                                                                           //     features copied out (2 arrivals)
-  uint64_t* bar_xload = reinterpret_cast<uint64_t*>(sm + P1_BAR + 144);  // (pairs) first chunk's slice reloaded
-  uint64_t* bar_xfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 152);  // (pairs) cross products read it
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cq = (warp >> 2) & 3;
@@ -296,12 +242,9 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   const bool bf_in = a.in_dtype == KDN_DTYPE_BF16;
   const bool decayed = a.decay != nullptr;
   const int64_t N = sa.N;
-  int64_t n_first = 0, c_first = 0;
-  const bool any = prep_item<kPair>(sa, cta, ncta, 0, n_first, c_first);
+  const int64_t total = N * a.NC;
 
   if (tid == 0) {
-    tc::mbar_init(bar_xload, 1);
-    tc::mbar_init(bar_xfree, 1);
     tc::mbar_init(&bar_lift[0], 1);
     tc::mbar_init(&bar_lift[1], 1);
     tc::mbar_init(bar_mma, 1);
@@ -319,7 +262,8 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   }
   build_omega(sm + P1_OMG, P, warp, lane, kP1Thr / 32);
   for (int i = tid; i < kD; i += kP1Thr) ph[i] = P.phase[i];
-  if (warp < kP1Warps && bf_in && any) prefetch_kq(a, n_first, int(c_first), sbase + P1_XIN, tid);
+  if (warp < kP1Warps && bf_in && cta < total)
+    prefetch_kq(a, int64_t(cta) % N, int(int64_t(cta) / N), sbase + P1_XIN, tid);
   tc::cp_async_commit();
   tc::fence_before_sync();
   __syncthreads();
@@ -346,11 +290,8 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         lift(0);
         lift(1);
       };
-      if (any) first_lifts();
-      uint32_t p_xload = 0;
-      int64_t n = 0, c = 0;
-      for (int64_t j = 0; prep_item<kPair>(sa, cta, ncta, j, n, c); ++j) {
-        const bool second = kPair && (c & 1);  // second chunk of a pair: cross products with the first
+      if (cta < total) first_lifts();
+      for (int64_t idx = cta; idx < total; idx += ncta) {
         for (int s = 0; s < kSlices; ++s) {
           ok &= split_wait_bit(&bar_zfree[s & 1], p_zfree, s & 1, sa.abort);  // slot s & 1 read by all
           tc::fence_after_sync();
@@ -363,23 +304,11 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
             const uint64_t fd = tc::smem_desc_sw128(fb + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
             tc::mma_ss(tmem + P1_GP, fd, fd, id_gp, s > 0 || k0 > 0);
           }
-          if (second) {  // [U_k1; U_q1] U_k0^T over this slice's features (U_k0 slice reloaded into P1_ES)
-            ok &= split_wait(bar_xload, p_xload, sa.abort);
-            p_xload ^= 1;
-            tc::fence_after_sync();
-#pragma unroll
-            for (int k0 = 0; k0 < 128; k0 += 16)
-              tc::mma_ss(tmem + P1_GP2, tc::smem_desc_sw128(fb + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024),
-                         tc::smem_desc_sw128(sbase + P1_ES + (k0 >> 6) * 8192 + 2 * (k0 & 63), 16, 1024), id_gp,
-                         s > 0 || k0 > 0);
-            if (s + 1 < kSlices) tc::mma_commit(bar_xfree);  // the last one is covered by bar_fdone
-          }
           tc::mma_commit(&bar_fdone[s & 1]);  // the buffer is rewritten once the publisher has copied it out too
         }
         // every slot of this chunk has been read: the next chunk's first lifts run during this
         // chunk's algebra (its inputs are announced by the compute warps mid-algebra)
-        int64_t nn = 0, nc = 0;
-        if (prep_item<kPair>(sa, cta, ncta, j + 1, nn, nc)) first_lifts();
+        if (idx + ncta < total) first_lifts();
         ok &= split_wait(bar_ops, p_ops, sa.abort);
         p_ops ^= 1;
         tc::fence_after_sync();
@@ -387,12 +316,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         for (int k0 = 0; k0 < 64; k0 += 16)  // U = T diag(beta) V in lanes 64..127
           tc::mma_ss(tmem + P1_U, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
                      tc::smem_desc_sw128(sbase + P1_VB + 128 * k0, 8192, 1024), id_n64, k0 > 0);
-        if (second) {
-#pragma unroll
-          for (int k0 = 0; k0 < 64; k0 += 16)  // H = T' G10 in lanes 0..63
-            tc::mma_ss(tmem + P1_H, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
-                       tc::smem_desc_sw128(sbase + P1_G10 + 128 * k0, 8192, 1024), id_n64, k0 > 0);
-        }
         tc::mma_commit(bar_mma);
       }
     }
@@ -400,22 +323,10 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   } else if (warp == kP1Publisher) {
     // ================================================================ record copies, publication
     if (lane == 0) {
-      uint32_t p_fready = 0, p_wdone = 0, p_xfree = 0;  // p_fready: phase bits per buffer
-      int64_t n = 0, c = 0;
-      for (int64_t j = 0; prep_item<kPair>(sa, cta, ncta, j, n, c); ++j) {
-        uint8_t* rec = record(sa, c, n);
-        const bool second = kPair && (c & 1);
-        const uint8_t* rec0 = second ? record(sa, c - 1, n) : nullptr;
-        if (second) tc::bulk_wait_all();  // the first chunk's features are in its record
+      uint32_t p_fready = 0, p_wdone = 0;  // p_fready: phase bits per buffer
+      for (int64_t idx = cta; idx < total; idx += ncta) {
+        uint8_t* rec = record(sa, idx / N, idx % N);
         for (int s = 0; s < kSlices; ++s) {
-          if (second) {  // reload the first chunk's U_k slice s for the cross products
-            if (s > 0) {
-              ok &= split_wait(bar_xfree, p_xfree, sa.abort);
-              p_xfree ^= 1;
-            }
-            tc::mbar_arrive_expect_tx(bar_xload, 16384);
-            tc::bulk_load(sbase + P1_ES, rec0 + REC_UK + s * 16384, 16384, bar_xload);
-          }
           // the slice's features: U_q (rows 64..127) as K-blocks 2s, 2s+1 and U_k (rows 0..63) as slice s
           ok &= split_wait_bit(&bar_fready[s & 1], p_fready, s & 1, sa.abort);
           const uint32_t fb = sbase + p1_fbuf(s);
@@ -434,16 +345,12 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         tc::bulk_store(rec + REC_U, sbase + P1_F, 16384);
         tc::bulk_store(rec + REC_AQ, sbase + P1_AQ, 8192);
         tc::bulk_store(rec + REC_VEC, sbase + P1_VEC, 1024);
-        if (second) {
-          tc::bulk_store(rec + REC_H, sbase + P1_HST, 8192);
-          tc::bulk_store(rec + REC_PX, sbase + P1_PXST, 8192);
-        }
         tc::bulk_commit();
         tc::bulk_wait_read();
         tc::mbar_arrive(bar_stfree);  // the staging tiles take the next chunk
         if (rec_ready) {              // every byte of the record came through this thread's copies
           tc::bulk_wait_all();
-          publish_store(rec_ready + c * N + n, 1u);
+          publish_store(rec_ready + idx, 1u);
         }
       }
       tc::bulk_wait_all();
@@ -457,10 +364,9 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       ph_mma ^= 1;
       tc::fence_after_sync();
     };
-    float* ew0 = reinterpret_cast<float*>(sm + P1_EW0);
     float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};  // gates of the coming chunk (warp 0)
-    if (warp == 0 && any) {
-      const int64_t n0 = n_first, t00 = c_first * kC;
+    if (warp == 0 && cta < total) {
+      const int64_t n0 = int64_t(cta) % N, t00 = (int64_t(cta) / N) * kC;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int64_t tt = t00 + 2 * lane + e;
@@ -470,15 +376,14 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         }
       }
     }
-    int64_t n = 0, c = 0;
-    for (int64_t jj = 0; prep_item<kPair>(sa, cta, ncta, jj, n, c); ++jj) {
-      const int64_t t0 = c * kC;
-      int64_t nn = 0, ncn = 0;
-      const bool has_next = prep_item<kPair>(sa, cta, ncta, jj + 1, nn, ncn);
-      const bool second = kPair && (c & 1);
+    for (int64_t idx = cta; idx < total; idx += ncta) {
+      const int64_t n = idx % N, c = idx / N, t0 = c * kC;
+      const int64_t nidx = idx + ncta;
+      const bool has_next = nidx < total;
+      const int64_t nn = nidx % N, ncn = nidx / N;
       // ---------------------------------------- chunk inputs -> lifts of slices 0, 1 (the first chunk;
       // later chunks' inputs are announced during the previous chunk's algebra)
-      if (jj == 0) {
+      if (idx == cta) {
         tc::cp_async_wait_all();
         if (!bf_in) load_kq_f32(a, n, int(c), sm + P1_XIN, tid);
         tc::fence_proxy_async_smem();
@@ -575,7 +480,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         if (s >= 2) {  // slice s - 2's Gram product and copy-out are done with buffer s & 1
           ok &= split_wait_bit(&bar_fdone[s & 1], ph_fd, s & 1, sa.abort);
           tc::fence_after_sync();
-        } else if (s == 0 && jj != 0) {  // the previous chunk's staged tiles (buffer 0) have been copied out
+        } else if (s == 0 && idx != cta) {  // the previous chunk's staged tiles (buffer 0) have been copied out
           ok &= split_wait(bar_stfree, ph_st, sa.abort);
           ph_st ^= 1;
         }
@@ -648,35 +553,10 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
                 pack_f16_sat(aq[8 * h + 4], aq[8 * h + 5]), pack_f16_sat(aq[8 * h + 6], aq[8 * h + 7]));
         }
       }
-      if (second) {  // cross terms with the pair's first chunk (columns: its tokens l)
-        float gx[16];
-        tc::tmem_ld16(tmem + lane_off + P1_GP2 + 16 * cq, gx);
-        tc::tmem_ld_wait();
-        if (trow < 64) {  // G10 row trow as the MN-major B operand of H = T' G10 (raw, fp16)
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-            *reinterpret_cast<uint4*>(sm + P1_G10 + tc::sw128_offset(trow, 16 * cq + 8 * h)) =
-                make_uint4(pack_f16_sat(gx[8 * h], gx[8 * h + 1]), pack_f16_sat(gx[8 * h + 2], gx[8 * h + 3]),
-                           pack_f16_sat(gx[8 * h + 4], gx[8 * h + 5]), pack_f16_sat(gx[8 * h + 6], gx[8 * h + 7]));
-        } else {  // P'_il = yqs_i P10_il ew0_l: the first chunk's E, seen by this chunk's queries
-          const int i = trow - 64;
-          const float yq = sc[trow] * egp[i];
-          float px[16];
-#pragma unroll
-          for (int jx = 0; jx < 16; ++jx) px[jx] = yq * gx[jx] * ew0[16 * cq + jx];
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-            *reinterpret_cast<uint4*>(sm + P1_PXST + tc::sw128_offset(i, 16 * cq + 8 * h)) =
-                make_uint4(pack_f16_sat(px[8 * h], px[8 * h + 1]), pack_f16_sat(px[8 * h + 2], px[8 * h + 3]),
-                           pack_f16_sat(px[8 * h + 4], px[8 * h + 5]), pack_f16_sat(px[8 * h + 6], px[8 * h + 7]));
-        }
-      }
       {  // per-token factors of the state pass, and V (fp16) as the B operand of U
         float* vec = reinterpret_cast<float*>(sm + P1_VEC);
-        if (tid < 64) {
-          vec[tid] = wdec[tid] * sc[tid];
-          if (kPair && !second) ew0[tid] = vec[tid];
-        } else if (tid < 128) vec[tid] = sc[tid] * egp[tid - 64];
+        if (tid < 64) vec[tid] = wdec[tid] * sc[tid];
+        else if (tid < 128) vec[tid] = sc[tid] * egp[tid - 64];
         else if (tid == 128) vec[128] = eg[63];
         const int row = tid >> 3, cc = tid & 7;
         *reinterpret_cast<uint4*>(sm + P1_VB + tc::sw128_offset(row, 8 * cc)) =
@@ -750,15 +630,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
             reinterpret_cast<float4*>(sm + P1_F + (cq >> 1) * 8192 + ((trow - 64) * 32 + 16 * (cq & 1)) * 4);
 #pragma unroll
         for (int m = 0; m < 4; ++m) dst[m] = make_float4(u[4 * m], u[4 * m + 1], u[4 * m + 2], u[4 * m + 3]);
-      } else if (second) {  // H = T' G10 (lanes 0..63) -> fp16 K-major staging tile
-        float hv[16];
-        tc::tmem_ld16(tmem + lane_off + P1_H + 16 * cq, hv);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          *reinterpret_cast<uint4*>(sm + P1_HST + tc::sw128_offset(trow, 16 * cq + 8 * h)) =
-              make_uint4(pack_f16_sat(hv[8 * h], hv[8 * h + 1]), pack_f16_sat(hv[8 * h + 2], hv[8 * h + 3]),
-                         pack_f16_sat(hv[8 * h + 4], hv[8 * h + 5]), pack_f16_sat(hv[8 * h + 6], hv[8 * h + 7]));
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
@@ -1268,580 +1139,6 @@ __device__ __forceinline__ void output_role(const SplitArgs& sa, uint8_t* sm, ui
 }
 
 
-// ================================================================ pair path, state pass
-// One step of the serial chain takes a pair of chunks (c0 = 2p, c1 = 2p + 1: 128 tokens), on a
-// cluster of two CTAs per sequence that split the state by feature rows: CTA h keeps S^T rows
-// 256h..256h+255 (all 64 value columns, fp32 in TMEM).  With S the state entering the pair and
-// H = T'_1 U_k1 U_k0^T from the preparation:
-//   Y0  = [U_k0; U_k1] S^T             M = 128; each CTA over its 256 features, the partial sums
-//                                      exchanged through distributed shared memory
-//   X0  = T'_0 Y0[c0],                 E0 = U0 - X0,  E0'' = diag(ew0) E0
-//   X1  = T'_1 (eC0 Y0[c1]) + H E0'',  E1 = U1 - X1,  E1'' = diag(ew1) E1
-//   S^T <- eC0 eC1 S^T + U_k0^T (eC1 E0'') + U_k1^T E1''
-// since S entering c1 is eC0 S + U_k0^T E0'' (the single-chunk step of the state pass applied
-// twice).  From Y0 to E1 the work is column-wise, so CTA h takes value columns 32h..32h+31 and
-// hands the other CTA its half of the update operand by a bulk copy between the two CTAs'
-// shared memories.  Against two single-chunk steps this halves the products that contract over
-// the features (M = 128 tiles instead of 64-row ones) and splits them over two SMs.
-constexpr int kQW = 8;             // compute warps: TMEM lane quarter w & 3, column half w >> 2
-constexpr int kQProducer = kQW;    // bulk loads (lane 0)
-constexpr int kQIssuer = kQW + 1;  // tensor-core products (lane 0)
-constexpr int kQStore = kQW + 2;   // record copies and progress words (lane 0)
-constexpr int kQRing = 6;          // 16 KiB slots: one 64-feature block of both chunks' U_k
-
-// TMEM columns (pair state pass)
-constexpr uint32_t PQ_S = 0;    // S^T master, row tile j (128 features) at 64 j
-constexpr uint32_t PQ_Y = 128;  // Y0 partial, lanes = the pair's 128 tokens
-constexpr uint32_t PQ_X = 192;  // lanes 0..63 cols 0..31: X0; lanes 64..127 cols 32..63: X1
-
-// shared memory (pair state pass)
-constexpr uint32_t PQ_RING = 0;       // 6 x 16 KiB [U_k0 block | U_k1 block], K-major SW128 [128 x 64]
-constexpr uint32_t PQ_SOP = 98304;    // 32 KiB S^T operand (fp16 MN-major SW128 [256 x 64])
-constexpr uint32_t PQ_TP = 131072;    // 24 KiB [T'_0 | T'_1 | H] (fp16 K-major SW128 [64 x 64] each)
-constexpr uint32_t PQ_YB = 155648;    // 8 KiB  [Y0[c0] | eC0 Y0[c1]], own columns (fp16 MN-major SW128 [64 x 64])
-constexpr uint32_t PQ_EC = 163840;    // 4 KiB  E0'' own columns (fp16 MN-major SW64 [64 x 32])
-constexpr uint32_t PQ_EU = 167936;    // 16 KiB update operand [eC1 E0''; E1''], column half hh at 8 KiB hh
-                                      //        (fp16 MN-major SW64 [128 x 32]); the other CTA writes its half
-constexpr uint32_t PQ_RECV = 184320;  // 16 KiB the other CTA's Y0 partial of this CTA's columns (fp32 [128][32])
-constexpr uint32_t PQ_EST = 200704;   // 8 KiB  E0, E1 own columns for the records (fp16 MN-major SW64 [64 x 32])
-constexpr uint32_t PQ_BAR = 208896;
-constexpr int kQBars = 27;
-constexpr uint32_t kQSmem = PQ_BAR + 8 * kQBars;
-
-// 32 values of row r into an MN-major SW64 [rows x 32] fp16 tile, scaled by w
-__device__ __forceinline__ void store_row32_sw64(uint8_t* tile, int r, const float (&v)[32], float w) {
-#pragma unroll
-  for (int m = 0; m < 4; ++m)
-    *reinterpret_cast<uint4*>(tile + tc::sw64_offset(r, 8 * m)) =
-        make_uint4(pack_f16_sat(w * v[8 * m], w * v[8 * m + 1]), pack_f16_sat(w * v[8 * m + 2], w * v[8 * m + 3]),
-                   pack_f16_sat(w * v[8 * m + 4], w * v[8 * m + 5]), pack_f16_sat(w * v[8 * m + 6], w * v[8 * m + 7]));
-}
-// 32 values of row r into columns e0..e0+31 of an MN-major SW128 [rows x 64] fp16 tile, scaled by w
-__device__ __forceinline__ void store_row32_sw128(uint8_t* tile, int r, int e0, const float (&v)[32], float w) {
-#pragma unroll
-  for (int m = 0; m < 4; ++m)
-    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(r, e0 + 8 * m)) =
-        make_uint4(pack_f16_sat(w * v[8 * m], w * v[8 * m + 1]), pack_f16_sat(w * v[8 * m + 2], w * v[8 * m + 3]),
-                   pack_f16_sat(w * v[8 * m + 4], w * v[8 * m + 5]), pack_f16_sat(w * v[8 * m + 6], w * v[8 * m + 7]));
-}
-
-// State pass of sequence cta / 2 on the CTA of cluster rank h = cta % 2 (warps 0..10 work; the
-// others idle).  Waits for each pair's records (rec_ready) and publishes per (sequence, h) how
-// many pairs have their entering state and E in the records (out_prog).
-__device__ __forceinline__ void state_pair_role(const SplitArgs& sa, uint8_t* sm, uint32_t tmem, int64_t cta,
-                                                const uint32_t* rec_ready, uint32_t* out_prog, bool& ok) {
-  const TcArgs& a = sa.a;
-  const uint32_t sbase = tc::smem_u32(sm);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + PQ_BAR);
-  uint64_t* ring_full = bars;        // [6] slot loaded (bytes)
-  uint64_t* ring_empty = bars + 6;   // [6] slot read by the update (MMA commit)
-  uint64_t* sop_full = bars + 12;    // [2] S operand row tile written (8 compute warps)
-  uint64_t* tp_full = bars + 14;     // T'_0, T'_1, H loaded (bytes)
-  uint64_t* tp_empty = bars + 15;    // ... read (MMA commit)
-  uint64_t* bar_y = bars + 16;       // Y0 partial done (MMA commit)
-  uint64_t* bar_yb = bars + 17;      // Y0 operand written (the 4 warps of this CTA's columns)
-  uint64_t* bar_x = bars + 18;       // X done (MMA commit)
-  uint64_t* bar_ec = bars + 19;      // E0'' operand written (2 warps)
-  uint64_t* bar_h = bars + 20;       // H E0'' added into X1 (MMA commit)
-  uint64_t* bar_eu = bars + 21;      // update operand complete: 4 warps here, 2 arrivals (+ bytes) from the other CTA
-  uint64_t* bar_recv = bars + 22;    // the other CTA's Y0 partial arrived (128 of its threads)
-  uint64_t* bar_s = bars + 23;       // [2] update of row tile j done (MMA commit)
-  uint64_t* bar_est = bars + 25;     // E staging written (4 warps)
-  uint64_t* bar_stfree = bars + 26;  // S operand and E staging copied out (store warp)
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t n = cta >> 1;
-  const int h = int(cta & 1);  // cluster rank: feature rows 256h.., value columns 32h.. of the column-wise steps
-  const uint32_t peer = uint32_t(h ^ 1);
-  const int NP = a.NC >> 1;
-  const bool decayed = a.decay != nullptr;
-
-  if (tid == 0) {
-    for (int b = 0; b < kQRing; ++b) {
-      tc::mbar_init(&ring_full[b], 1);
-      tc::mbar_init(&ring_empty[b], 1);
-    }
-    tc::mbar_init(&sop_full[0], kQW);
-    tc::mbar_init(&sop_full[1], kQW);
-    tc::mbar_init(tp_full, 1);
-    tc::mbar_init(tp_empty, 1);
-    tc::mbar_init(bar_y, 1);
-    tc::mbar_init(bar_yb, 4);
-    tc::mbar_init(bar_x, 1);
-    tc::mbar_init(bar_ec, 2);
-    tc::mbar_init(bar_h, 1);
-    tc::mbar_init(bar_eu, 6);
-    tc::mbar_init(bar_recv, 128);
-    tc::mbar_init(&bar_s[0], 1);
-    tc::mbar_init(&bar_s[1], 1);
-    tc::mbar_init(bar_est, 4);
-    tc::mbar_init(bar_stfree, 1);
-    tc::fence_mbar_init();
-  }
-  // both CTAs' barriers are initialised before either touches the other's shared memory
-  tc::fence_before_sync();
-  tc::cluster_sync();
-  tc::fence_after_sync();
-
-  if (warp == kQProducer) {
-    // ================================================================ bulk loads
-    if (lane == 0) {
-      uint32_t pe = 0, pt = 0;  // pe: phase bits per slot
-      for (int p = 0; p < NP; ++p) {
-        const uint8_t* r0 = record(sa, 2 * p, n);
-        const uint8_t* r1 = record(sa, 2 * p + 1, n);
-        if (rec_ready) {  // both records published by the preparation
-          ok &= wait_flag(rec_ready + int64_t(2 * p) * sa.N + n, 1u, sa.abort);
-          ok &= wait_flag(rec_ready + int64_t(2 * p + 1) * sa.N + n, 1u, sa.abort);
-          tc::fence_proxy_async_global();
-        }
-        for (int i = 0; i < 4; ++i) {  // features 256h + 64i .. +63 of both chunks
-          const int g = 4 * p + i, b = g % kQRing;
-          if (g >= kQRing) ok &= split_wait_bit(&ring_empty[b], pe, b, sa.abort);
-          const uint32_t fo = REC_UK + uint32_t(4 * h + i) * 8192;
-          tc::mbar_arrive_expect_tx(&ring_full[b], 16384);
-          tc::bulk_load(sbase + PQ_RING + b * 16384, r0 + fo, 8192, &ring_full[b]);
-          tc::bulk_load(sbase + PQ_RING + b * 16384 + 8192, r1 + fo, 8192, &ring_full[b]);
-        }
-        if (p > 0) {
-          ok &= split_wait(tp_empty, pt, sa.abort);
-          pt ^= 1;
-        }
-        tc::mbar_arrive_expect_tx(tp_full, 24576);
-        tc::bulk_load(sbase + PQ_TP, r0 + REC_TP, 8192, tp_full);
-        tc::bulk_load(sbase + PQ_TP + 8192, r1 + REC_TP, 8192, tp_full);
-        tc::bulk_load(sbase + PQ_TP + 16384, r1 + REC_H, 8192, tp_full);
-      }
-    }
-    __syncwarp();
-  } else if (warp == kQIssuer) {
-    // ================================================================ tensor-core products
-    if (lane == 0) {
-      const uint32_t id_y = tc::idesc_f16_f32(128, 64, false, true);  // A K-major, B MN-major
-      const uint32_t id_h = tc::idesc_f16_f32(128, 32, false, true);
-      const uint32_t id_u = tc::idesc_f16_f32(128, 64, true, true);   // A MN-major: U_k^T
-      uint32_t pf = 0, ps = 0, pt = 0, pyb = 0, pec = 0, peu = 0;    // pf: bits per slot, ps: per tile
-      for (int p = 0; p < NP; ++p) {
-        // Y0 partial = [U_k0; U_k1] S^T over this CTA's features
-        for (int i = 0; i < 4; ++i) {
-          const int b = (4 * p + i) % kQRing;
-          if ((i & 1) == 0) ok &= split_wait_bit(&sop_full[i >> 1], ps, i >> 1, sa.abort);
-          ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
-          tc::fence_after_sync();
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc::mma_ss(tmem + PQ_Y, tc::smem_desc_sw128(sbase + PQ_RING + b * 16384 + 32 * kk, 16, 1024),
-                       tc::smem_desc_sw128(sbase + PQ_SOP + (64 * i + 16 * kk) * 128, 8192, 1024), id_y,
-                       i > 0 || kk > 0);
-        }
-        tc::mma_commit(bar_y);
-        // X = [T'_0; T'_1] [Y0[c0] | eC0 Y0[c1]]: the diagonal blocks are X0 and T'_1 eC0 Y0[c1]
-        ok &= split_wait(tp_full, pt, sa.abort);
-        pt ^= 1;
-        ok &= split_wait(bar_yb, pyb, sa.abort);
-        pyb ^= 1;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_ss(tmem + PQ_X, tc::smem_desc_sw128(sbase + PQ_TP + 32 * kk, 16, 1024),
-                     tc::smem_desc_sw128(sbase + PQ_YB + 2048 * kk, 8192, 1024), id_y, kk > 0);
-        tc::mma_commit(bar_x);
-        // X1 += H E0'' (A rows 0..63 are T'_1: they land in lanes nobody reads)
-        ok &= split_wait(bar_ec, pec, sa.abort);
-        pec ^= 1;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_ss(tmem + PQ_X + 32, tc::smem_desc_sw128(sbase + PQ_TP + 8192 + 32 * kk, 16, 1024),
-                     tc::smem_desc_sw64(sbase + PQ_EC + 1024 * kk, 8192, 512), id_h, true);
-        tc::mma_commit(bar_h);
-        tc::mma_commit(tp_empty);
-        // S^T += U_k^T [eC1 E0''; E1''] per 128-feature row tile
-        ok &= split_wait_cluster(bar_eu, peu, sa.abort);
-        peu ^= 1;
-        tc::fence_after_sync();
-#pragma unroll 1
-        for (int j = 0; j < 2; ++j) {
-          const int b0 = (4 * p + 2 * j) % kQRing;  // even: its pair of slots is adjacent
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            tc::mma_ss(tmem + PQ_S + 64 * j, tc::smem_desc_sw128(sbase + PQ_RING + b0 * 16384 + 2048 * kk, 16384, 1024),
-                       tc::smem_desc_sw64(sbase + PQ_EU + 1024 * kk, 8192, 512), id_u, true);
-          tc::mma_commit(&ring_empty[b0]);
-          tc::mma_commit(&ring_empty[b0 + 1]);
-          tc::mma_commit(&bar_s[j]);
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == kQStore) {
-    // ================================================================ record copies, progress
-    if (lane == 0) {
-      uint32_t ps = 0, pe = 0;  // ps: bits per tile
-      for (int p = 0; p < NP; ++p) {
-        uint8_t* r0 = record(sa, 2 * p, n);
-        uint8_t* r1 = record(sa, 2 * p + 1, n);
-        ok &= split_wait_bit(&sop_full[0], ps, 0, sa.abort);
-        ok &= split_wait_bit(&sop_full[1], ps, 1, sa.abort);
-        tc::bulk_store(r0 + REC_S0 + h * 32768, sbase + PQ_SOP, 32768);  // the state entering the pair
-        tc::bulk_commit();
-        ok &= split_wait(bar_est, pe, sa.abort);
-        pe ^= 1;
-        tc::bulk_store(r0 + REC_E + h * 4096, sbase + PQ_EST, 4096);
-        tc::bulk_store(r1 + REC_E + h * 4096, sbase + PQ_EST + 4096, 4096);
-        tc::bulk_commit();
-        tc::bulk_wait_read();
-        tc::mbar_arrive(bar_stfree);
-        if (out_prog) {  // pairs 0..p of this half are in the records
-          tc::bulk_wait_all();
-          publish_store(out_prog + 2 * n + h, uint32_t(p + 1));
-        }
-      }
-      tc::bulk_wait_all();
-    }
-    __syncwarp();
-  } else if (warp < kQW) {
-    // ================================================================ compute warps
-    const int quarter = warp & 3, ch = warp >> 2;  // TMEM lane quarter, 32-column half
-    const int t = quarter * 32 + lane;             // TMEM lane: feature of a row tile, token of the pair
-    const int ti = t & 63;
-    const bool first = t < 64;                     // token of c0 (else c1)
-    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-    const bool own = ch == h;                      // this warp's columns are this CTA's in the column-wise steps
-    const uint32_t recv_remote = tc::mapa(sbase + PQ_RECV, peer);
-    const uint32_t bar_recv_remote = tc::mapa(tc::smem_u32(bar_recv), peer);
-    const uint32_t bar_eu_remote = tc::mapa(tc::smem_u32(bar_eu), peer);
-    const uint32_t eu_rows = PQ_EU + uint32_t(h) * 8192 + (first ? 0u : 4096u);  // this thread's rows of the half
-#pragma unroll 1
-    for (int j = 0; j < 2; ++j) {  // state master from the initial state
-      float v[32];
-      const int64_t f = 256 * h + 128 * j + t;
-#pragma unroll
-      for (int q = 0; q < 32; ++q) v[q] = a.S0 ? a.S0[(n * kDV + 32 * ch + q) * kD + f] : 0.f;
-      tc::tmem_st32(tmem + lane_off + PQ_S + 64 * j + 32 * ch, v);
-    }
-    tc::tmem_st_wait();
-    auto signal = [&](uint64_t* bar) {  // this warp's shared-memory tiles -> tensor core / bulk copies
-      tc::fence_proxy_async_smem();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(bar);
-    };
-    uint32_t ps = 0, py = 0, prv = 0, px = 0, ph = 0, pst = 0;  // ps: bits per tile
-#pragma unroll 1
-    for (int p = 0; p < NP; ++p) {
-      // the pair's records are complete once its first ring slot has been loaded (its next
-      // phase needs this pair's update, so the parity of use g / 6 is the one to wait for)
-      {
-        const int g = 4 * p;
-        ok &= split_wait(&ring_full[g % kQRing], uint32_t((g / kQRing) & 1), sa.abort);
-      }
-      const uint8_t* rc = record(sa, 2 * p + (first ? 0 : 1), n);
-      float uu[32], ew = 0.f;
-      if (own) {  // U (fp32) of this token, this CTA's columns; the token's E'' factor
-        const float4* u4 = reinterpret_cast<const float4*>(rc + REC_U + h * 8192 + ti * 128);
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const float4 x = __ldcg(u4 + m);
-          uu[4 * m] = x.x, uu[4 * m + 1] = x.y, uu[4 * m + 2] = x.z, uu[4 * m + 3] = x.w;
-        }
-        ew = __ldcg(reinterpret_cast<const float*>(rc + REC_VEC) + ti);
-      }
-      const float eC0 = decayed ? __ldcg(reinterpret_cast<const float*>(record(sa, 2 * p, n) + REC_VEC) + 128) : 1.f;
-      const float eC1 =
-          decayed ? __ldcg(reinterpret_cast<const float*>(record(sa, 2 * p + 1, n) + REC_VEC) + 128) : 1.f;
-      // ---------------------------------------- S operand (fp16) of this pair; master decayed for its update
-      if (p > 0) {
-        ok &= split_wait(bar_stfree, pst, sa.abort);  // the previous pair's operand and E copied out
-        pst ^= 1;
-      }
-#pragma unroll 1
-      for (int j = 0; j < 2; ++j) {
-        if (p > 0) {
-          ok &= split_wait_bit(&bar_s[j], ps, j, sa.abort);
-          tc::fence_after_sync();
-        }
-        float v[32];
-        tc::tmem_ld32(tmem + lane_off + PQ_S + 64 * j + 32 * ch, v);
-        tc::tmem_ld_wait();
-        store_row32_sw128(sm + PQ_SOP, 128 * j + t, 32 * ch, v, 1.f);
-        if (decayed) {
-          const float w = eC0 * eC1;
-#pragma unroll
-          for (int q = 0; q < 32; ++q) v[q] *= w;
-          tc::tmem_st32(tmem + lane_off + PQ_S + 64 * j + 32 * ch, v);
-          tc::tmem_st_wait();
-        }
-        signal(&sop_full[j]);
-      }
-      // ---------------------------------------- Y0: partial sums of the other CTA's columns go there
-      ok &= split_wait(bar_y, py, sa.abort);
-      py ^= 1;
-      tc::fence_after_sync();
-      float yv[32];
-      tc::tmem_ld32(tmem + lane_off + PQ_Y + 32 * ch, yv);
-      tc::tmem_ld_wait();
-      if (!own) {
-        const uint32_t dst = recv_remote + uint32_t(t) * 128;
-#pragma unroll
-        for (int m = 0; m < 8; ++m)
-          tc::st_cluster_v4(dst + 16 * m, yv[4 * m], yv[4 * m + 1], yv[4 * m + 2], yv[4 * m + 3]);
-        tc::mbar_arrive_remote(bar_recv_remote);
-        tc::fence_before_sync();
-        __syncwarp();
-        continue;  // the column-wise steps are the other CTA's
-      }
-      ok &= split_wait_cluster(bar_recv, prv, sa.abort);
-      prv ^= 1;
-      {
-        const float4* r4 = reinterpret_cast<const float4*>(sm + PQ_RECV + t * 128);
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const float4 x = r4[m];
-          yv[4 * m] += x.x, yv[4 * m + 1] += x.y, yv[4 * m + 2] += x.z, yv[4 * m + 3] += x.w;
-        }
-      }
-      store_row32_sw128(sm + PQ_YB, ti, first ? 0 : 32, yv, first ? 1.f : eC0);
-      signal(bar_yb);
-      // ---------------------------------------- E0 (lanes 0..63) / E1 (lanes 64..127)
-      float xv[32];
-      if (first) {
-        ok &= split_wait(bar_x, px, sa.abort);
-        px ^= 1;
-        tc::fence_after_sync();
-        tc::tmem_ld32(tmem + lane_off + PQ_X, xv);
-      } else {
-        ok &= split_wait(bar_h, ph, sa.abort);
-        ph ^= 1;
-        tc::fence_after_sync();
-        tc::tmem_ld32(tmem + lane_off + PQ_X + 32, xv);
-      }
-      tc::tmem_ld_wait();
-#pragma unroll
-      for (int q = 0; q < 32; ++q) xv[q] = uu[q] - xv[q];  // E
-      store_row32_sw64(sm + PQ_EST + (first ? 0 : 4096), ti, xv, 1.f);
-      store_row32_sw64(sm + PQ_EU + h * 8192, t, xv, first ? ew * eC1 : ew);
-      if (first) store_row32_sw64(sm + PQ_EC, ti, xv, ew);
-      tc::fence_proxy_async_smem();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) {
-        if (first) tc::mbar_arrive(bar_ec);
-        tc::mbar_arrive(bar_eu);
-        tc::mbar_arrive(bar_est);
-      }
-      // this CTA's rows of its half of the update operand -> the other CTA (both warps of the rows)
-      tc::named_bar_sync(first ? 2 : 3, 64);
-      if ((quarter & 1) == 0 && lane == 0) {
-        tc::mbar_arrive_expect_tx_remote(bar_eu_remote, 4096);
-        tc::bulk_copy_to_cluster(tc::mapa(sbase + eu_rows, peer), sbase + eu_rows, 4096, bar_eu_remote);
-      }
-    }
-    // ---------------------------------------- final state
-#pragma unroll 1
-    for (int j = 0; j < 2; ++j) {
-      if (NP > 0) {
-        ok &= split_wait_bit(&bar_s[j], ps, j, sa.abort);
-        tc::fence_after_sync();
-      }
-      float v[32];
-      tc::tmem_ld32(tmem + lane_off + PQ_S + 64 * j + 32 * ch, v);
-      tc::tmem_ld_wait();
-      const int64_t f = 256 * h + 128 * j + t;
-#pragma unroll
-      for (int q = 0; q < 32; ++q) a.S_out[(n * kDV + 32 * ch + q) * kD + f] = v[q];
-    }
-  }
-  // no CTA of the cluster leaves while the other may still write into its shared memory
-  tc::fence_before_sync();
-  tc::cluster_sync();
-  tc::fence_after_sync();
-}
-
-// ================================================================ pair path, outputs
-// y of both chunks of a pair from the state entering it (from the two state CTAs' records):
-//   acc1 = [U_q0; U_q1] S^T                        (M = 128)
-//   acc2 = [Aq_0, 0; P', Aq_1] [E0; E1]            (P' = diag(yqs_1) U_q1 U_k0^T diag(ew0))
-//   y_c0 = yqs_0 acc1 + acc2,  y_c1 = eC0 yqs_1 acc1 + acc2
-// since the state entering c1 is eC0 S + U_k0^T E0''.  Persistent CTAs: warp 5 loads, warp 4
-// issues, warps 0..3 (all four TMEM lane quarters) write y; accumulators double-buffered.
-constexpr int kPORing = 3;
-constexpr uint32_t PO_RING = 0;      // 3 x 48 KiB; slice s: [U_q0 kb 2s | U_q1 kb 2s | U_q0 kb 2s+1 | U_q1 kb 2s+1 |
-                                     //                       S^T rows 128s..128s+127 (MN-major SW128)]
-constexpr uint32_t PO_A0 = 147456;   // 16 KiB [Aq_0; P'] (K-major SW128, 128 rows)
-constexpr uint32_t PO_ZERO = 163840; // 8 KiB zeros: [zeros; Aq_1] is the A operand of the second chunk's E
-constexpr uint32_t PO_AQ1 = 172032;  // 8 KiB Aq_1
-constexpr uint32_t PO_E = 180224;    // 16 KiB E0 (MN-major SW64 column halves 4 KiB apart), then E1
-constexpr uint32_t PO_FAC = 196608;  // 2 KiB the two chunks' factor vectors
-constexpr uint32_t PO_BAR = 198656;
-constexpr uint32_t kPOSmem = PO_BAR + 8 * 12;
-
-__device__ __forceinline__ void output_pair_role(const SplitArgs& sa, uint8_t* sm, uint32_t tmem, int64_t cta,
-                                                 int64_t ncta, const uint32_t* out_prog, bool& ok) {
-  const TcArgs& a = sa.a;
-  const uint32_t sbase = tc::smem_u32(sm);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + PO_BAR);
-  uint64_t* ring_full = bars;        // [3]
-  uint64_t* ring_empty = bars + 3;   // [3]
-  uint64_t* small_full = bars + 6;   // Aq, P', E and factors loaded
-  uint64_t* small_empty = bars + 7;  // ... read by the products (commit) and the epilogue (4 warps)
-  uint64_t* acc_full = bars + 8;     // [2]
-  uint64_t* acc_free = bars + 10;    // [2] accumulator buffer read (4 epilogue warps)
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t N = sa.N;
-  const int64_t units = N * (a.NC >> 1);
-  const bool decayed = a.decay != nullptr;
-  if (tid == 0) {
-    for (int b = 0; b < kPORing; ++b) {
-      tc::mbar_init(&ring_full[b], 1);
-      tc::mbar_init(&ring_empty[b], 1);
-    }
-    tc::mbar_init(small_full, 1);
-    tc::mbar_init(small_empty, 5);
-    for (int u = 0; u < 2; ++u) {
-      tc::mbar_init(&acc_full[u], 1);
-      tc::mbar_init(&acc_free[u], 4);
-    }
-    tc::fence_mbar_init();
-  }
-  for (int i = tid; i < 512; i += blockDim.x) reinterpret_cast<uint4*>(sm + PO_ZERO)[i] = make_uint4(0, 0, 0, 0);
-  tc::fence_proxy_async_smem();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-
-  if (warp == 5) {
-    // ================================================================ bulk loads
-    if (lane == 0) {
-      uint32_t pe = 0, pse = 0;  // pe: bits per slot
-      int64_t g = 0, j = 0;
-      for (int64_t w = cta; w < units; w += ncta, ++j) {
-        const int64_t n = w % N, p = w / N;
-        const uint8_t* r0 = record(sa, 2 * p, n);
-        const uint8_t* r1 = record(sa, 2 * p + 1, n);
-        if (out_prog) {  // both state CTAs are past this pair
-          ok &= wait_flag(out_prog + 2 * n, uint32_t(p + 1), sa.abort);
-          ok &= wait_flag(out_prog + 2 * n + 1, uint32_t(p + 1), sa.abort);
-          tc::fence_proxy_async_global();
-        }
-        for (int s = 0; s < kSlices; ++s, ++g) {
-          const int b = int(g % kPORing);
-          if (g >= kPORing) ok &= split_wait_bit(&ring_empty[b], pe, b, sa.abort);
-          const uint32_t dst = sbase + PO_RING + b * 49152;
-          tc::mbar_arrive_expect_tx(&ring_full[b], 49152);
-          for (int kb = 0; kb < 2; ++kb) {
-            tc::bulk_load(dst + 16384 * kb, r0 + REC_Q + (2 * s + kb) * 8192, 8192, &ring_full[b]);
-            tc::bulk_load(dst + 16384 * kb + 8192, r1 + REC_Q + (2 * s + kb) * 8192, 8192, &ring_full[b]);
-          }
-          tc::bulk_load(dst + 32768, r0 + REC_S0 + 16384 * s, 16384, &ring_full[b]);
-        }
-        if (j > 0) {
-          ok &= split_wait(small_empty, pse, sa.abort);
-          pse ^= 1;
-        }
-        tc::mbar_arrive_expect_tx(small_full, 8192 * 5 + 2048);
-        tc::bulk_load(sbase + PO_A0, r0 + REC_AQ, 8192, small_full);
-        tc::bulk_load(sbase + PO_A0 + 8192, r1 + REC_PX, 8192, small_full);
-        tc::bulk_load(sbase + PO_AQ1, r1 + REC_AQ, 8192, small_full);
-        tc::bulk_load(sbase + PO_E, r0 + REC_E, 8192, small_full);
-        tc::bulk_load(sbase + PO_E + 8192, r1 + REC_E, 8192, small_full);
-        tc::bulk_load(sbase + PO_FAC, r0 + REC_VEC, 1024, small_full);
-        tc::bulk_load(sbase + PO_FAC + 1024, r1 + REC_VEC, 1024, small_full);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 4) {
-    // ================================================================ MMA issuer
-    if (lane == 0) {
-      const uint32_t id = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t pf = 0, psf = 0, pfree = 0;  // pf, pfree: bits per slot
-      int64_t g = 0, j = 0;
-      for (int64_t w = cta; w < units; w += ncta, ++j) {
-        const int u = int(j & 1);
-        if (j >= 2) ok &= split_wait_bit(&acc_free[u], pfree, u, sa.abort);
-        tc::fence_after_sync();
-        const uint32_t d1 = tmem + 128 * u, d2 = d1 + 64;
-        for (int s = 0; s < kSlices; ++s, ++g) {
-          const int b = int(g % kPORing);
-          ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
-          tc::fence_after_sync();
-          const uint32_t st = sbase + PO_RING + b * 49152;
-#pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc::mma_ss(d1, tc::smem_desc_sw128(st + 16384 * kb + 32 * kk, 16, 1024),
-                         tc::smem_desc_sw128(st + 32768 + (64 * kb + 16 * kk) * 128, 8192, 1024), id,
-                         s > 0 || kb > 0 || kk > 0);
-          tc::mma_commit(&ring_empty[b]);
-        }
-        ok &= split_wait(small_full, psf, sa.abort);
-        psf ^= 1;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_ss(d2, tc::smem_desc_sw128(sbase + PO_A0 + 32 * kk, 16, 1024),
-                     tc::smem_desc_sw64(sbase + PO_E + 1024 * kk, 4096, 512), id, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_ss(d2, tc::smem_desc_sw128(sbase + PO_ZERO + 32 * kk, 16, 1024),
-                     tc::smem_desc_sw64(sbase + PO_E + 8192 + 1024 * kk, 4096, 512), id, true);
-        tc::mma_commit(small_empty);
-        tc::mma_commit(&acc_full[u]);
-      }
-    }
-    __syncwarp();
-  } else if (warp < 4) {
-    // ================================================================ epilogue (all 128 lanes)
-    const uint32_t lane_off = uint32_t(warp * 32) << 16;
-    const int t = warp * 32 + lane, ti = t & 63;
-    const bool first = t < 64;
-    uint32_t pa = 0;  // bits per buffer
-    int64_t j = 0;
-    for (int64_t w = cta; w < units; w += ncta, ++j) {
-      const int64_t n = w % N, p = w / N;
-      const int u = int(j & 1);
-      ok &= split_wait_bit(&acc_full[u], pa, u, sa.abort);
-      tc::fence_after_sync();
-      const float* f0 = reinterpret_cast<const float*>(sm + PO_FAC);
-      const float yqs = first ? f0[64 + ti] : f0[256 + 64 + ti] * (decayed ? f0[128] : 1.f);
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(small_empty);
-      const int64_t tok = (2 * p + (first ? 0 : 1)) * kC + ti;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float y1[32], y2[32];
-        tc::tmem_ld32(tmem + lane_off + 128 * u + 32 * hh, y1);
-        tc::tmem_ld32(tmem + lane_off + 128 * u + 64 + 32 * hh, y2);
-        tc::tmem_ld_wait();
-        if (tok < a.T) {
-          const int64_t o = (n * a.T + tok) * kDV + 32 * hh;
-#pragma unroll
-          for (int q = 0; q < 32; ++q) y1[q] = fmaf(yqs, y1[q], y2[q]);
-          if (a.y_dtype == KDN_DTYPE_BF16) {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + o);
-#pragma unroll
-            for (int m = 0; m < 4; ++m)
-              dst[m] = make_uint4(pack_bf16(y1[8 * m], y1[8 * m + 1]), pack_bf16(y1[8 * m + 2], y1[8 * m + 3]),
-                                  pack_bf16(y1[8 * m + 4], y1[8 * m + 5]), pack_bf16(y1[8 * m + 6], y1[8 * m + 7]));
-          } else {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o);
-#pragma unroll
-            for (int m = 0; m < 8; ++m) dst[m] = make_float4(y1[4 * m], y1[4 * m + 1], y1[4 * m + 2], y1[4 * m + 3]);
-          }
-        }
-      }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&acc_free[u]);
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-}
-
 // ================================================================ kernels
 // One shared-memory size for all launches of this path (the largest role); the TMEM
 // address slot sits above every role's layout.
@@ -1851,7 +1148,6 @@ static_assert(kP1Smem <= kSplitSmem && kP2Smem <= kSplitSmem && kP3Smem <= kSpli
               "a role's shared memory exceeds the launch's");
 static_assert(kSplitTslot >= P2_BAR + 8 * kP2Bars && kSplitTslot >= P1_BAR + kP1Bars && kSplitTslot >= P3_BAR + 8 * 18,
               "TMEM slot overlaps a role's barriers");
-static_assert(kSplitTslot >= kQSmem && kSplitTslot >= kPOSmem, "TMEM slot overlaps a pair role's barriers");
 
 __device__ __forceinline__ uint8_t* split_smem() {
   extern __shared__ uint8_t smem_raw[];
@@ -1882,7 +1178,7 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
   uint8_t* sm = split_smem();
   const uint32_t tmem = split_tmem_alloc(sm, 512);
   bool ok = true;
-  prep_role<false>(sa, P, sm, tmem, blockIdx.x, gridDim.x, nullptr, ok);
+  prep_role(sa, P, sm, tmem, blockIdx.x, gridDim.x, nullptr, ok);
   split_finish(tmem, 512, ok);
 }
 
@@ -1915,64 +1211,18 @@ __global__ void __launch_bounds__(kP1Thr, 1) split_persistent_kernel(SplitArgs s
     state_role(sa, sm, tmem, blockIdx.x, rec_ready, out_prog, ok);
   } else {
     const int64_t cta = int64_t(blockIdx.x) - n_state, ncta = int64_t(gridDim.x) - n_state;
-    prep_role<false>(sa, P, sm, tmem, cta, ncta, rec_ready, ok);
+    prep_role(sa, P, sm, tmem, cta, ncta, rec_ready, ok);
     output_role(sa, sm, tmem, cta, ncta, out_prog, ok);
   }
   split_finish(tmem, 512, ok);
 }
 
-// The pair path in one launch: clusters of two CTAs, one CTA per SM, all resident.  CTAs
-// 0..n_state-1 (clusters of one sequence each) run the pair state pass; the others prepare
-// the records chunk pair by chunk pair and then write the outputs of the pairs the state pass
-// has finished.
-__global__ void __launch_bounds__(kP1Thr, 1) pair_persistent_kernel(SplitArgs sa, ProjParams P, uint32_t* rec_ready,
-                                                                     uint32_t* out_prog, int n_state) {
-  uint8_t* sm = split_smem();
-  const uint32_t tmem = split_tmem_alloc(sm, 512);
-  bool ok = true;
-  if (int(blockIdx.x) < n_state) {
-    state_pair_role(sa, sm, tmem, blockIdx.x, rec_ready, out_prog, ok);
-  } else {
-    const int64_t cta = int64_t(blockIdx.x) - n_state, ncta = int64_t(gridDim.x) - n_state;
-    prep_role<true>(sa, P, sm, tmem, cta, ncta, rec_ready, ok);
-    output_pair_role(sa, sm, tmem, cta, ncta, out_prog, ok);
-  }
-  split_finish(tmem, 512, ok);
-}
-
-// whether the pair launch fits on this device: every cluster of two co-resident (cached per device)
-bool pair_launch_fits(int dev, int grid) {
-  static std::atomic<int> fits[64];  // 0 unknown, 1 yes, 2 no
-  if (dev < 0 || dev >= 64) return false;
-  int f = fits[dev].load(std::memory_order_relaxed);
-  if (f == 0) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(grid));
-    cfg.blockDim = dim3(kP1Thr);
-    cfg.dynamicSmemBytes = kSplitSmem;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, pair_persistent_kernel, &cfg);
-    if (e != cudaSuccess) (void)cudaGetLastError();
-    f = (e == cudaSuccess && clusters >= grid / 2) ? 1 : 2;
-    fits[dev].store(f, std::memory_order_relaxed);
-  }
-  return f == 1;
-}
-
 }  // namespace
 
-// records (whole chunk pairs: a sequence of an odd number of chunks gets an empty last chunk),
-// then the hand-over words of the persistent launch: one per record, two per sequence, the
-// abort word
+// records, then the hand-over words of the persistent launch: one per record, two per
+// sequence, the abort word
 size_t split_prefill_workspace(int64_t N, int64_t T) {
-  const int64_t NC = ((T + kC - 1) / kC + 1) & ~int64_t(1);
+  const int64_t NC = (T + kC - 1) / kC;
   return size_t(N) * size_t(NC) * REC_BYTES + ((size_t(N) * (size_t(NC) + 2) * 4 + 4 + 255) & ~size_t(255));
 }
 
@@ -2003,46 +1253,9 @@ cudaError_t launch_split_prefill(const PrefillProblem& p, const ProjParams& P, v
   if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess) return e;
   const int64_t total = p.N * int64_t(sa.a.NC);
   for (const void* f : {(const void*)chunk_prep_kernel, (const void*)state_pass_kernel, (const void*)output_pass_kernel,
-                        (const void*)split_persistent_kernel, (const void*)pair_persistent_kernel})
+                        (const void*)split_persistent_kernel})
     if ((e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSplitSmem))) != cudaSuccess)
       return e;
-  // Pair path (KDN_SPLIT_PAIR=0 or KDN_SPLIT_PERSISTENT=0 turns it off): the state pass takes
-  // chunk pairs on clusters of two CTAs per sequence, and leaves at least half of the SMs to the
-  // preparation and the outputs.
-  {
-    const char* env_pair = getenv("KDN_SPLIT_PAIR");
-    const char* env_pers = getenv("KDN_SPLIT_PERSISTENT");
-    const bool off = (env_pair && strcmp(env_pair, "0") == 0) || (env_pers && strcmp(env_pers, "0") == 0);
-    const int grid = sms & ~1;
-    const int n_state = int(2 * p.N);
-    if (coop && 2 * n_state <= grid && !off && pair_launch_fits(dev, grid)) {
-      sa.a.NC = int(((p.T + kC - 1) / kC + 1) & ~int64_t(1));
-      const int64_t records = p.N * int64_t(sa.a.NC);
-      uint32_t* rec_ready = reinterpret_cast<uint32_t*>(sa.ws + size_t(records) * REC_BYTES);
-      uint32_t* out_prog = rec_ready + records;
-      sa.abort = out_prog + 2 * p.N;
-      if ((e = cudaMemsetAsync(rec_ready, 0, (size_t(records) + 2 * p.N + 1) * 4, stream)) != cudaSuccess) return e;
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(unsigned(grid));
-      cfg.blockDim = dim3(kP1Thr);
-      cfg.dynamicSmemBytes = kSplitSmem;
-      cfg.stream = stream;
-      cudaLaunchAttribute at[2];
-      at[0].id = cudaLaunchAttributeClusterDimension;
-      at[0].val.clusterDim.x = 2;
-      at[0].val.clusterDim.y = 1;
-      at[0].val.clusterDim.z = 1;
-      at[1].id = cudaLaunchAttributeCooperative;
-      at[1].val.cooperative = 1;
-      cfg.attrs = at;
-      cfg.numAttrs = 2;
-      marks.begin(stream);
-      if ((e = cudaLaunchKernelEx(&cfg, pair_persistent_kernel, sa, P, rec_ready, out_prog, n_state)) != cudaSuccess)
-        return e;
-      marks.after(stream);
-      return cudaSuccess;
-    }
-  }
   // one launch for all phases when every CTA fits at once and the state pass leaves at least half
   // of the SMs for the other two (KDN_SPLIT_PERSISTENT=0 forces the three launches); measured at
   // T = 16384: 32 sequences 1.66 ms in one launch vs 1.73 ms in three, 48 sequences 3.9 vs 2.2 ms

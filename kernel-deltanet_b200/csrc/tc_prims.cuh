@@ -286,39 +286,6 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t caddr, float a, float b, 
 __device__ __forceinline__ void st_cluster_f32(uint32_t caddr, float a) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(caddr), "f"(a) : "memory");
 }
-// wait on a barrier of this CTA that threads of other CTAs of the cluster arrive on
-// (acquire at cluster scope: their prior shared::cluster writes are visible after it)
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// arrive on a barrier of another CTA of the cluster (`caddr` from mapa); release at cluster
-// scope orders this thread's earlier shared::cluster writes before the arrival
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
-}
-// arrive on a barrier of another CTA of the cluster and add `bytes` to the transaction
-// count of its current phase (the bytes of a bulk copy this thread issues next)
-__device__ __forceinline__ void mbar_arrive_expect_tx_remote(uint32_t caddr, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(caddr), "r"(bytes)
-               : "memory");
-}
-// shared memory of this CTA -> shared memory of a CTA of the cluster (`dst`, `bar` from mapa),
-// completion counted in bytes on that CTA's barrier; both addresses 16-byte aligned, bytes a
-// multiple of 16.  The source is read by the async proxy: fence generic writes to it first.
-__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   dst),
-               "r"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
 
 }  // namespace tc
 }  // namespace kdn
