@@ -16,18 +16,21 @@
 // inputs are loaded before the current group is computed.  Cosines: the argument is reduced by the
 // nearest multiple of 2 pi (Cody and Waite's method, 2 pi split in two floats), then __cosf.
 //
-// Tensor-core kernel (lift_tc_kernel; bf16 inputs, D = 512, Omega exact in bf16): the three transforms
-// of a block are one dense product x Omega^T.  Omega = H D3 H D2 H D1 / 8 has entries that are integers / 8;
-// when those are exact in bf16 (checked on the host per sign pattern) a bf16 x bf16 product with fp32
-// accumulation is exact up to the accumulation order.  A persistent CTA per SM builds Omega once
-// (64 KiB, the B operand), then per tile of 128 vectors one thread issues 16 tcgen05 MMAs into 512 TMEM
-// columns (lanes = vectors, columns = features).  Eight epilogue warps (two per TMEM lane quarter, one
-// column half each) take the cosines with the sum of squares (pass 1) and exchange the two halves' sums
-// through shared memory, then scale each row and write it as coalesced 16-byte stores (pass 2).  For bf16
-// outputs pass 1 stages the cosines in shared memory as fp16, so TMEM goes back to the issuer before pass 2
-// and the next tile's products overlap the write-back; for fp32 outputs the cosines stay in TMEM (written
-// back in place) and pass 2 goes through a per-warp staging buffer.  The next tile's inputs are loaded
-// during the epilogue.  KDN_LIFT_PATH=pair forces the CUDA-core kernel.
+// Tensor-core kernels (bf16 inputs, D = 512, Omega exact in bf16): the three transforms of a block are one
+// dense product x Omega^T.  Omega = H D3 H D2 H D1 / 8 has entries that are integers / 8; when those are
+// exact in bf16 (checked on the host per sign pattern) a bf16 x bf16 product with fp32 accumulation is
+// exact up to the accumulation order.  A persistent CTA per SM builds Omega once (64 KiB, the B operand),
+// then per tile of 128 vectors one thread issues 16 tcgen05 MMAs into 512 TMEM columns (lanes = vectors,
+// columns = features).
+//  - lift_tc_bf16_kernel (bf16 outputs): the features are two halves of 256 columns with their own
+//    products, handed back to the issuer half by half, so the next tile's products overlap this tile's
+//    epilogue.  Sixteen epilogue warps take the cosines and sums of squares (pass 1, cosines staged as
+//    fp16), then scale whole rows and write them as 512-byte stores (pass 2).
+//  - lift_tc_kernel (fp32 outputs): eight epilogue warps (two per TMEM lane quarter, one column half each)
+//    write the cosines back in place in TMEM with the sums of squares, then scale each row and write it
+//    through a per-warp staging buffer as coalesced 16-byte stores; the next tile's inputs load during
+//    the epilogue.
+// KDN_LIFT_PATH=pair forces the CUDA-core kernel.
 //
 // Fallback (lift_kernel): one warp per vector, for inputs or outputs that are not 16-byte aligned.
 #include <cuda_fp16.h>
@@ -301,9 +304,8 @@ constexpr uint32_t OFF_BAR = 216064;  // 2 mbarriers + TMEM address
 constexpr uint32_t kSmem = OFF_BAR + 64 + 1024;  // + alignment slack
 }  // namespace tcl
 
-template <typename TO>
 __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                    TO* __restrict__ out, int64_t n, ProjParams P) {
+                                                                   float* __restrict__ out, int64_t n, ProjParams P) {
   using namespace tcl;
   extern __shared__ uint8_t lift_tc_raw[];
   uint8_t* sm;
@@ -384,15 +386,194 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
       tc::fence_after_sync();
       const int64_t next = t + gridDim.x;
       if (next < tiles) load_tile(next);  // the products of this tile have read the input tile
-      if constexpr (sizeof(TO) == 2) {
-        // bf16 outputs. Pass 1: cos(tau^-1 z + b) and the sum of squares over this half's 256 features, the
-        // cosines staged as fp16 (2^-12 rounding, inside the output's 2^-9) so that TMEM can go back to the
-        // issuer before the write-back: the next tile's products overlap pass 2.
-        uint8_t* cs = sm + OFF_STG;
-        float ss = 0.f;
+      // fp32 outputs. Pass 1: cos(tau^-1 z + b) in place in TMEM, sum of squares over this half's 256 features
+      float ss = 0.f;
 #pragma unroll 1
-        for (int cc = 0; cc < 8; ++cc) {
-          const uint32_t col = 256 * ch + 32 * cc;
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint32_t col = 256 * ch + 32 * cc;
+        float z[32];
+        tc::tmem_ld32(tmem + lane_off + col, z);
+        tc::tmem_ld_wait();
+        const float4* b4 = reinterpret_cast<const float4*>(ph + col);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 b = b4[j >> 2];
+          z[j] = cos_reduced(fmaf(z[j], P.tau_inv, b.x));
+          z[j + 1] = cos_reduced(fmaf(z[j + 1], P.tau_inv, b.y));
+          z[j + 2] = cos_reduced(fmaf(z[j + 2], P.tau_inv, b.z));
+          z[j + 3] = cos_reduced(fmaf(z[j + 3], P.tau_inv, b.w));
+          ss = fmaf(z[j], z[j], fmaf(z[j + 1], z[j + 1], fmaf(z[j + 2], z[j + 2], fmaf(z[j + 3], z[j + 3], ss))));
+        }
+        tc::tmem_st32(tmem + lane_off + col, z);
+      }
+      tc::tmem_st_wait();
+      ssx[128 * ch + row] = ss;
+      tc::named_bar_sync(1, 32 * kEpiWarps);
+      // phi = amp cos / (amp ||cos|| + 1e-8)
+      const float scale = P.amp / fmaf(P.amp, sqrtf(ssx[row] + ssx[128 + row]), 1e-8f);
+      // pass 2: 128 output bytes (32 fp32 columns) of each row at a time, scaled and transposed through the
+      // staging (row r's 16-byte chunk c at c ^ (r & 7)) into whole-row 128-byte stores
+      const int64_t grow0 = t * kTile + 32 * q;  // output row of lane 0 of this warp
+#pragma unroll 1
+      for (int blk = 0; blk < 8; ++blk) {
+        const uint32_t col = 256 * ch + 32 * blk;
+        float a[32];
+        tc::tmem_ld32(tmem + lane_off + col, a);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+              make_float4(a[4 * c] * scale, a[4 * c + 1] * scale, a[4 * c + 2] * scale, a[4 * c + 3] * scale);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int jj = lane + 32 * k, r = jj >> 3, c = jj & 7;
+          const uint4 u = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+          if (grow0 + r < n)
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (grow0 + r) * 512 + col) + 16 * c) = u;
+        }
+        __syncwarp();  // the staging is rewritten by the next block
+      }
+      if (next < tiles) {  // TMEM read out and the next tile in shared memory: hand both to the issuer
+        tc::cp_async_wait_all();
+        tc::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_ready);
+      }
+    }
+  }
+  if (!ok) record_device_error(&g_lift_error, kErrLiftWaitTimeout);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 512);
+}
+
+// Tensor-core lift for bf16 outputs.  The 512 features of a tile are two halves of 256 TMEM columns,
+// produced by separate groups of products: the issuer gives half hh of the next tile its products as
+// soon as the epilogue has read half hh of this tile, so the tensor core never waits for a whole
+// epilogue and the epilogue never waits for the tensor core.  Sixteen epilogue warps (four per TMEM
+// lane quarter; warp w takes columns 64 (w >> 2) .. +63 of each half) take the cosines (plain __cosf:
+// its error, about 2e-6 for the arguments here, is far inside the bf16 output's 2^-9) and the
+// per-row sums of squares, staging the cosines as fp16 (2^-12 rounding); then each warp scales eight
+// whole rows and writes each as two coalesced 512-byte stores.
+namespace tcl2 {
+constexpr int kTile = 128;
+constexpr int kEpiWarps = 16;
+constexpr int kIssuerWarp = kEpiWarps;  // warp 16 issues the MMAs
+constexpr int kThreads = 32 * (kEpiWarps + 1);
+constexpr uint32_t kWaitLimit = 1u << 24;
+constexpr uint32_t OFF_OMG = 0;       // 64 KiB Omega (bf16, K-major SW128), slice s at 16 KiB s
+constexpr uint32_t OFF_X = 65536;     // 16 KiB input tile (bf16, K-major SW128, 128 rows x 64)
+constexpr uint32_t OFF_STG = 81920;   // 128 KiB fp16 cosines: row r at 1 KiB r, its 16-byte chunk c at c ^ (r & 7)
+constexpr uint32_t OFF_PH = 212992;   // 2 KiB phase b[512]
+constexpr uint32_t OFF_SS = 215040;   // 2 KiB partial sums of squares [column quarter][row]
+constexpr uint32_t OFF_BAR = 217088;  // 5 mbarriers + TMEM address
+constexpr uint32_t kSmem = OFF_BAR + 64 + 1024;  // + alignment slack
+}  // namespace tcl2
+
+__global__ void __launch_bounds__(tcl2::kThreads, 1) lift_tc_bf16_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                         __nv_bfloat16* __restrict__ out,
+                                                                         int64_t n, ProjParams P) {
+  using namespace tcl2;
+  extern __shared__ uint8_t lift_tc2_raw[];
+  uint8_t* sm;
+  {
+    const uint32_t a = tc::smem_u32(lift_tc2_raw);
+    sm = lift_tc2_raw + ((1024u - (a & 1023u)) & 1023u);
+  }
+  const uint32_t sbase = tc::smem_u32(sm);
+  float* ph = reinterpret_cast<float*>(sm + OFF_PH);
+  float* ssx = reinterpret_cast<float*>(sm + OFF_SS);
+  uint64_t* bar_half = reinterpret_cast<uint64_t*>(sm + OFF_BAR);       // [2] products of half hh done
+  uint64_t* bar_free = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 16);  // [2] half hh read out (16 warps)
+  uint64_t* bar_in = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 32);    // next input tile loaded (16 warps)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 40);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t tiles = (n + kTile - 1) / kTile;
+  bool ok = true;
+
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, 512);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int hh = 0; hh < 2; ++hh) {
+      tc::mbar_init(&bar_half[hh], 1);
+      tc::mbar_init(&bar_free[hh], kEpiWarps);
+    }
+    tc::mbar_init(bar_in, kEpiWarps);
+    tc::fence_mbar_init();
+  }
+  tcc::build_omega(sm + OFF_OMG, P, warp, lane, kThreads / 32);
+  for (int i = tid; i < 64 * kMaxBlocks; i += kThreads) ph[i] = P.phase[i];
+  // the 128 x 64 input tile of tile t, swizzled for the A operand (epilogue threads; rows past n read as 0)
+  auto load_tile = [&](int64_t t) {
+    const int64_t row0 = t * kTile;
+    for (int j = tid; j < kTile * 8; j += 32 * kEpiWarps) {
+      const int r = j >> 3, c = j & 7;
+      const bool in = row0 + r < n;
+      tc::cp_async16(sbase + OFF_X + tc::sw128_offset(r, 8 * c), x + (in ? (row0 + r) * kDk + 8 * c : 0),
+                     in ? 16 : 0);
+    }
+    tc::cp_async_commit();
+  };
+  if (warp < kEpiWarps && int64_t(blockIdx.x) < tiles) load_tile(blockIdx.x);
+  if (warp < kEpiWarps) tc::cp_async_wait_all();
+  tc::fence_proxy_async_smem();  // Omega (generic stores) and the first tile, for the tensor core
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot;
+
+  if (warp == kIssuerWarp) {
+    if (lane == 0) {
+      const uint32_t id = tc::idesc_bf16_f32(128, 128, false, false);
+      uint32_t pf = 0, pin = 0;  // pf: bits per half
+      int64_t i = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+        if (i > 0) {  // this tile's inputs are in shared memory
+          ok &= tc::mbar_wait_bounded(bar_in, pin, kWaitLimit);
+          pin ^= 1;
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          if (i > 0) {  // the epilogue has read half hh of the previous tile
+            ok &= tc::mbar_wait_bounded(&bar_free[hh], (pf >> hh) & 1u, kWaitLimit);
+            pf ^= 1u << hh;
+          }
+          tc::fence_after_sync();
+#pragma unroll
+          for (int s = 2 * hh; s < 2 * hh + 2; ++s)
+#pragma unroll
+            for (int k0 = 0; k0 < 64; k0 += 16)
+              tc::mma_ss(tmem + 128 * s, tc::smem_desc_sw128(sbase + OFF_X + 2 * k0, 16, 1024),
+                         tc::smem_desc_sw128(sbase + OFF_OMG + s * 16384 + 2 * k0, 16, 1024), id, k0 > 0);
+          tc::mma_commit(&bar_half[hh]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < kEpiWarps) {
+    const int q = warp & 3, cq = warp >> 2;  // TMEM lane quarter, column quarter of each half
+    const uint32_t lane_off = uint32_t(32 * q) << 16;
+    const int row = 32 * q + lane;           // this thread's row of the tile in pass 1
+    uint8_t* cs = sm + OFF_STG;
+    uint32_t ph_half = 0;  // bits per half
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int64_t next = t + gridDim.x;
+      // pass 1: cos(tau^-1 z + b) of this thread's row over 2 x 64 features, the sum of their squares,
+      // the cosines staged as fp16; each half of TMEM goes back to the issuer once read
+      float ss = 0.f;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        ok &= tc::mbar_wait_bounded(&bar_half[hh], (ph_half >> hh) & 1u, kWaitLimit);
+        ph_half ^= 1u << hh;
+        tc::fence_after_sync();
+        if (hh == 1 && next < tiles) load_tile(next);  // every product of this tile has read the input tile
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const uint32_t col = 256 * hh + 64 * cq + 32 * cc;
           float z[32];
           tc::tmem_ld32(tmem + lane_off + col, z);
           tc::tmem_ld_wait();
@@ -400,14 +581,14 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
             const float4 b = b4[j >> 2];
-            z[j] = cos_reduced(fmaf(z[j], P.tau_inv, b.x));
-            z[j + 1] = cos_reduced(fmaf(z[j + 1], P.tau_inv, b.y));
-            z[j + 2] = cos_reduced(fmaf(z[j + 2], P.tau_inv, b.z));
-            z[j + 3] = cos_reduced(fmaf(z[j + 3], P.tau_inv, b.w));
+            z[j] = __cosf(fmaf(z[j], P.tau_inv, b.x));
+            z[j + 1] = __cosf(fmaf(z[j + 1], P.tau_inv, b.y));
+            z[j + 2] = __cosf(fmaf(z[j + 2], P.tau_inv, b.z));
+            z[j + 3] = __cosf(fmaf(z[j + 3], P.tau_inv, b.w));
             ss = fmaf(z[j], z[j], fmaf(z[j + 1], z[j + 1], fmaf(z[j + 2], z[j + 2], fmaf(z[j + 3], z[j + 3], ss))));
           }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {  // chunk (col / 8 + k) of this thread's row: features col + 8k ..
+          for (int k = 0; k < 4; ++k) {  // chunk col / 8 + k of this thread's row
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -418,23 +599,27 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
             *reinterpret_cast<uint4*>(cs + row * 1024 + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-        ssx[128 * ch + row] = ss;
-        tc::named_bar_sync(1, 32 * kEpiWarps);
-        // phi = amp cos / (amp ||cos|| + 1e-8)
-        const float scale = P.amp / fmaf(P.amp, sqrtf(ssx[row] + ssx[128 + row]), 1e-8f);
-        if (next < tiles) {  // every warp has read TMEM and its scale; the next tile is in shared memory
-          tc::cp_async_wait_all();
-          tc::fence_proxy_async_smem();
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(bar_ready);
-        }
-        // pass 2: per row of this warp's quarter, its half's 512 output bytes as one coalesced store
-        const int64_t grow0 = t * kTile + 32 * q;
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bar_free[hh]);
+      }
+      ssx[128 * cq + row] = ss;
+      if (next < tiles) {  // the next tile's inputs are in place: its products may start
+        tc::cp_async_wait_all();
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_in);
+      }
+      tc::named_bar_sync(1, 32 * kEpiWarps);  // every row's cosines and partial sums are in shared memory
+      // pass 2: rows 8 warp .. 8 warp + 7, each as two 512-byte stores; phi = amp cos / (amp ||cos|| + 1e-8)
 #pragma unroll 1
-        for (int k = 0; k < 32; ++k) {
-          const float sc = __shfl_sync(0xffffffffu, scale, k);
-          const int r = 32 * q + k, c = 32 * ch + lane;
+      for (int k = 0; k < 8; ++k) {
+        const int r = 8 * warp + k;
+        const float sc = P.amp / fmaf(P.amp, sqrtf(ssx[r] + ssx[128 + r] + ssx[256 + r] + ssx[384 + r]), 1e-8f);
+        const int64_t grow = t * kTile + r;
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          const int c = 32 * hb + lane;
           const uint4 u = *reinterpret_cast<const uint4*>(cs + r * 1024 + ((c ^ (r & 7)) << 4));
           const uint32_t w[4] = {u.x, u.y, u.z, u.w};
           uint32_t o[4];
@@ -444,66 +629,10 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
             const __nv_bfloat162 b2 = __floats2bfloat162_rn(f.x * sc, f.y * sc);
             o[e] = *reinterpret_cast<const uint32_t*>(&b2);
           }
-          if (grow0 + k < n) *reinterpret_cast<uint4*>(out + (grow0 + k) * 512 + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        __syncwarp();  // this warp's staging rows are rewritten by its next tile
-      } else {
-        // fp32 outputs. Pass 1: cos(tau^-1 z + b) in place in TMEM, sum of squares over this half's 256 features
-        float ss = 0.f;
-#pragma unroll 1
-        for (int cc = 0; cc < 8; ++cc) {
-          const uint32_t col = 256 * ch + 32 * cc;
-          float z[32];
-          tc::tmem_ld32(tmem + lane_off + col, z);
-          tc::tmem_ld_wait();
-          const float4* b4 = reinterpret_cast<const float4*>(ph + col);
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 b = b4[j >> 2];
-            z[j] = cos_reduced(fmaf(z[j], P.tau_inv, b.x));
-            z[j + 1] = cos_reduced(fmaf(z[j + 1], P.tau_inv, b.y));
-            z[j + 2] = cos_reduced(fmaf(z[j + 2], P.tau_inv, b.z));
-            z[j + 3] = cos_reduced(fmaf(z[j + 3], P.tau_inv, b.w));
-            ss = fmaf(z[j], z[j], fmaf(z[j + 1], z[j + 1], fmaf(z[j + 2], z[j + 2], fmaf(z[j + 3], z[j + 3], ss))));
-          }
-          tc::tmem_st32(tmem + lane_off + col, z);
-        }
-        tc::tmem_st_wait();
-        ssx[128 * ch + row] = ss;
-        tc::named_bar_sync(1, 32 * kEpiWarps);
-        // phi = amp cos / (amp ||cos|| + 1e-8)
-        const float scale = P.amp / fmaf(P.amp, sqrtf(ssx[row] + ssx[128 + row]), 1e-8f);
-        // pass 2: 128 output bytes (32 fp32 columns) of each row at a time, scaled and transposed through the
-        // staging (row r's 16-byte chunk c at c ^ (r & 7)) into whole-row 128-byte stores
-        const int64_t grow0 = t * kTile + 32 * q;  // output row of lane 0 of this warp
-#pragma unroll 1
-        for (int blk = 0; blk < 8; ++blk) {
-          const uint32_t col = 256 * ch + 32 * blk;
-          float a[32];
-          tc::tmem_ld32(tmem + lane_off + col, a);
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<float4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-                make_float4(a[4 * c] * scale, a[4 * c + 1] * scale, a[4 * c + 2] * scale, a[4 * c + 3] * scale);
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int jj = lane + 32 * k, r = jj >> 3, c = jj & 7;
-            const uint4 u = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
-            if (grow0 + r < n)
-              *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + (grow0 + r) * 512 + col) + 16 * c) = u;
-          }
-          __syncwarp();  // the staging is rewritten by the next block
-        }
-        if (next < tiles) {  // TMEM read out and the next tile in shared memory: hand both to the issuer
-          tc::cp_async_wait_all();
-          tc::fence_proxy_async_smem();
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(bar_ready);
+          if (grow < n) *reinterpret_cast<uint4*>(out + grow * 512 + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
+      tc::named_bar_sync(1, 32 * kEpiWarps);  // the staging and the partial sums take the next tile
     }
   }
   if (!ok) record_device_error(&g_lift_error, kErrLiftWaitTimeout);
@@ -512,18 +641,31 @@ __global__ void __launch_bounds__(tcl::kThreads, 1) lift_tc_kernel(const __nv_bf
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
 }
 
-template <typename TO>
 cudaError_t launch_tc(const void* x, void* out, int64_t n, const ProjParams& P, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if ((e = allow_smem<lift_tc_kernel<TO>>(int(tcl::kSmem), dev)) != cudaSuccess) return e;
+  if ((e = allow_smem<lift_tc_kernel>(int(tcl::kSmem), dev)) != cudaSuccess) return e;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t tiles = (n + tcl::kTile - 1) / tcl::kTile;
   const int64_t blocks = tiles < sms ? tiles : sms;  // persistent: one CTA per SM
-  lift_tc_kernel<TO><<<dim3(unsigned(blocks)), tcl::kThreads, tcl::kSmem, stream>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<TO*>(out), n, P);
+  lift_tc_kernel<<<dim3(unsigned(blocks)), tcl::kThreads, tcl::kSmem, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<float*>(out), n, P);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tc_bf16(const void* x, void* out, int64_t n, const ProjParams& P, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if ((e = allow_smem<lift_tc_bf16_kernel>(int(tcl2::kSmem), dev)) != cudaSuccess) return e;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = (n + tcl2::kTile - 1) / tcl2::kTile;
+  const int64_t blocks = tiles < sms ? tiles : sms;  // persistent: one CTA per SM
+  lift_tc_bf16_kernel<<<dim3(unsigned(blocks)), tcl2::kThreads, tcl2::kSmem, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), n, P);
   return cudaGetLastError();
 }
 
@@ -555,8 +697,7 @@ cudaError_t launch_lift(const void* x, int x_dtype, void* out, int out_dtype, in
   const char* path = getenv("KDN_LIFT_PATH");
   const bool force_pair = path && strcmp(path, "pair") == 0;
   if (a16 && omega_bf16_exact && P.M == kMaxBlocks && x_dtype == KDN_DTYPE_BF16 && !force_pair)
-    return out_dtype == KDN_DTYPE_BF16 ? launch_tc<__nv_bfloat16>(x, out, n, P, stream)
-                                       : launch_tc<float>(x, out, n, P, stream);
+    return out_dtype == KDN_DTYPE_BF16 ? launch_tc_bf16(x, out, n, P, stream) : launch_tc(x, out, n, P, stream);
   if (a16 && P.M >= 1 && P.M <= kMaxBlocks) {
     const bool ib = x_dtype == KDN_DTYPE_BF16, ob = out_dtype == KDN_DTYPE_BF16;
     if (ib && ob) return launch_pair<__nv_bfloat16, __nv_bfloat16>(x, out, n, P, stream);
