@@ -21,6 +21,7 @@
 
 #include "kdn_internal.h"
 #include "lift.cuh"
+#include "tc_prims.cuh"
 
 namespace kdn {
 namespace {
@@ -379,6 +380,220 @@ size_t chain_smem_bytes(int D) {
   return sizeof(float) * (size_t(RT) * (D + 1) + 2 * C * 65 + 2 * C * (C + 1) + 4 * C + 2 * C * RT);
 }
 
+// (3) for chunk 64 and D = 512: the same serial pass with its loads off the chain.  The K and Q
+// features of a chunk stream through a 3-stage cp.async ring of 64-feature slices ([64 tokens x 64]
+// fp32, rows padded to 68 floats so that a 16-byte row read and the S reads are conflict-free),
+// the chunk's T, Aq and gates load into one of two buffers with its first slice, and the
+// products read 16 bytes at a time.  The state update reads the chunk's K rows from global memory
+// (L2) as float4 with eight loads in flight per thread and a 4 x (RT/2) register block per thread.
+// The arithmetic is the kernel above's (exact fp32), in another summation order.
+template <int RT>
+__global__ void __launch_bounds__(kThreads) simt_chain64_kernel(PrefillProblem p, Workspace w) {
+  constexpr int C = 64;
+  constexpr int TPR = kThreads / C;  // threads per chunk row
+  constexpr int VPT = RT / TPR;      // state rows per thread in the products
+  constexpr int LD = 68;             // padded row of the staged tiles (floats)
+  constexpr int kStages = 3;
+  constexpr int kSlice = C * LD;     // floats of one staged 64-feature slice
+  constexpr int D = 512, SD = D + 4, kNsl = D / 64;
+  constexpr int RPT = RT / 2;        // state rows per thread in the update (two row groups)
+  extern __shared__ __align__(16) float sm[];
+  float* S = sm;                              // [RT][SD]
+  float* ring = S + RT * SD;                  // [kStages][K | Q][C][LD]
+  float* Tb = ring + kStages * 2 * kSlice;    // [2][T | Aq][C][LD]
+  float* gb = Tb + 4 * C * LD;                // [2][C][4]
+  float* Rs = gb + 2 * C * 4;                 // [C][RT]
+  float* Es = Rs + C * RT;                    // [C][RT]
+
+  const int vt = blockIdx.x;
+  const int64_t n = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int i = tid / TPR;
+  const int v0 = (tid % TPR) * VPT;
+  const bool a_tile = vt * RT < p.a_rows;
+  const int row0 = a_tile ? vt * RT : vt * RT - p.a_rows;
+  const bool readout = !a_tile && p.y != nullptr;  // uniform per CTA
+  const int NC = w.NC;
+  const int64_t items = int64_t(NC) * kNsl;
+
+  for (int e = tid; e < RT * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    float s0 = 0.f;
+    if (a_tile)
+      s0 = (row0 + r == d) ? 1.f : 0.f;
+    else if (p.S0)
+      s0 = p.S0[(n * p.dv + row0 + r) * int64_t(D) + d];
+    S[r * SD + d] = s0;
+  }
+  // item g: slice g % 8 of chunk g / 8 into stage g % 3 (and, for the first slice, the chunk's
+  // T, Aq and gates into buffer c & 1); every call commits one group, possibly empty
+  auto issue = [&](int64_t g) {
+    if (g < items) {
+      const int c = int(g / kNsl), s = int(g % kNsl);
+      const int64_t rowbase = (n * w.Tp + int64_t(c) * C) * D + 64 * s;
+      float* st = ring + int(g % kStages) * 2 * kSlice;
+      for (int e = tid; e < C * 16; e += kThreads) {
+        const int r = e >> 4, q = e & 15;
+        tc::cp_async16(tc::smem_u32(st + r * LD + 4 * q), w.phik + rowbase + int64_t(r) * D + 4 * q, 16);
+        if (readout)
+          tc::cp_async16(tc::smem_u32(st + kSlice + r * LD + 4 * q), w.phiq + rowbase + int64_t(r) * D + 4 * q, 16);
+      }
+      if (s == 0) {
+        const int64_t cm = (n * NC + c) * int64_t(C) * C;
+        float* tb = Tb + (c & 1) * 2 * C * LD;
+        for (int e = tid; e < C * 16; e += kThreads) {
+          const int r = e >> 4, q = e & 15;
+          tc::cp_async16(tc::smem_u32(tb + r * LD + 4 * q), w.Tinv + cm + r * C + 4 * q, 16);
+          if (readout) tc::cp_async16(tc::smem_u32(tb + C * LD + r * LD + 4 * q), w.Aq + cm + r * C + 4 * q, 16);
+        }
+        const float* Gg = w.gates + (n * NC + c) * int64_t(C) * 4;
+        for (int e = tid; e < C; e += kThreads) tc::cp_async16(tc::smem_u32(gb + (c & 1) * C * 4 + 4 * e), Gg + 4 * e, 16);
+      }
+    }
+    tc::cp_async_commit();
+  };
+  for (int g = 0; g < kStages - 1; ++g) issue(g);
+  __syncthreads();
+
+  const int fb = tid % (D / 4);   // update: features 4 fb .. 4 fb + 3
+  const int rb = tid / (D / 4);   //         rows RPT rb .. RPT rb + RPT - 1
+  for (int c = 0; c < NC; ++c) {
+    if (p.S_chunks && !a_tile) {  // checkpoint: the state entering chunk c
+      float* Sc = p.S_chunks + ((n * NC + c) * p.dv + row0) * int64_t(D);
+      for (int e = tid; e < RT * D; e += kThreads) Sc[e] = S[(e / D) * SD + e % D];
+    }
+    // X = K S^T, Yq = Q S^T (C x RT), slice by slice from the ring
+    float x[VPT], yq[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) x[u] = yq[u] = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < kNsl; ++s) {
+      const int64_t g = int64_t(c) * kNsl + s;
+      tc::cp_async_wait_group<kStages - 2>();  // item g has landed (this thread's copies) ...
+      __syncthreads();                         // ... everyone's; item g - 1's stage is free
+      issue(g + kStages - 1);
+      const float* Ks = ring + int(g % kStages) * 2 * kSlice;
+      const float* Qs = Ks + kSlice;
+      const float* Sd = S + 64 * s;
+      if (readout) {
+#pragma unroll 4
+        for (int dd = 0; dd < 64; dd += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * LD + dd);
+          const float4 q4 = *reinterpret_cast<const float4*>(Qs + i * LD + dd);
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) {
+            const float4 s4 = *reinterpret_cast<const float4*>(Sd + (v0 + u) * SD + dd);
+            x[u] = fmaf(k4.w, s4.w, fmaf(k4.z, s4.z, fmaf(k4.y, s4.y, fmaf(k4.x, s4.x, x[u]))));
+            yq[u] = fmaf(q4.w, s4.w, fmaf(q4.z, s4.z, fmaf(q4.y, s4.y, fmaf(q4.x, s4.x, yq[u]))));
+          }
+        }
+      } else {
+#pragma unroll 4
+        for (int dd = 0; dd < 64; dd += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * LD + dd);
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) {
+            const float4 s4 = *reinterpret_cast<const float4*>(Sd + (v0 + u) * SD + dd);
+            x[u] = fmaf(k4.w, s4.w, fmaf(k4.z, s4.z, fmaf(k4.y, s4.y, fmaf(k4.x, s4.x, x[u]))));
+          }
+        }
+      }
+    }
+    const float* Tm = Tb + (c & 1) * 2 * C * LD;
+    const float* Am = Tm + C * LD;
+    const float* gt = gb + (c & 1) * C * 4;
+    // R_i = beta_i (v_i - exp(g_i) x_i)
+    const int64_t t = int64_t(c) * C + i;
+    const float beta_i = gt[4 * i + 3], gi = gt[4 * i + 1], gprev = gt[4 * i + 0], wi = gt[4 * i + 2];
+    const float gC = gt[4 * (C - 1) + 1];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+      float vv = 0.f;
+      if (!a_tile && t < p.T) vv = ld_as_f32(p.v, p.in_dtype, (n * p.T + t) * p.dv + row0 + v0 + u);
+      Rs[i * RT + v0 + u] = beta_i * (vv - gi * x[u]);
+    }
+    __syncthreads();
+    // E = T R  (T unit lower triangular)
+    float e_[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) e_[u] = Rs[i * RT + v0 + u];
+    for (int j = 0; j < i; ++j) {
+      const float tij = Tm[i * LD + j];
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) e_[u] = fmaf(tij, Rs[j * RT + v0 + u], e_[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) Es[i * RT + v0 + u] = e_[u];
+    if (p.E_rows && !a_tile) {
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) p.E_rows[(n * w.Tp + t) * p.dv + row0 + v0 + u] = e_[u];
+    }
+    __syncthreads();
+    // y_i = exp(g_{i-1}) yq_i + sum_{j<i} Aq_ij e_j ;  then E''_i = exp(g_{C-1} - g_i) e_i into Rs
+    if (readout) {
+      float yv[VPT];
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) yv[u] = gprev * yq[u];
+      for (int j = 0; j < i; ++j) {
+        const float aij = Am[i * LD + j];
+#pragma unroll
+        for (int u = 0; u < VPT; ++u) yv[u] = fmaf(aij, Es[j * RT + v0 + u], yv[u]);
+      }
+      if (t < p.T) {
+#pragma unroll
+        for (int u = 0; u < VPT; ++u) st_from_f32(p.y, p.y_dtype, (n * p.T + t) * p.dv + row0 + v0 + u, yv[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) Rs[i * RT + v0 + u] = wi * e_[u];
+    __syncthreads();
+    // S <- exp(g_{C-1}) S + E''^T K: features 4 fb .. + 3, rows RPT rb .. + RPT - 1
+    {
+      const float* Kg = w.phik + (n * w.Tp + int64_t(c) * C) * D + 4 * fb;
+      float acc[RPT][4];
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        const float4 s4 = *reinterpret_cast<const float4*>(S + (RPT * rb + r) * SD + 4 * fb);
+        acc[r][0] = gC * s4.x, acc[r][1] = gC * s4.y, acc[r][2] = gC * s4.z, acc[r][3] = gC * s4.w;
+      }
+#pragma unroll 1
+      for (int j0 = 0; j0 < C; j0 += 8) {
+        float4 kv[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) kv[jj] = __ldcg(reinterpret_cast<const float4*>(Kg + int64_t(j0 + jj) * D));
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+          for (int r = 0; r < RPT; ++r) {
+            const float ev = Rs[(j0 + jj) * RT + RPT * rb + r];
+            acc[r][0] = fmaf(ev, kv[jj].x, acc[r][0]);
+            acc[r][1] = fmaf(ev, kv[jj].y, acc[r][1]);
+            acc[r][2] = fmaf(ev, kv[jj].z, acc[r][2]);
+            acc[r][3] = fmaf(ev, kv[jj].w, acc[r][3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RPT; ++r)
+        *reinterpret_cast<float4*>(S + (RPT * rb + r) * SD + 4 * fb) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    }
+    __syncthreads();
+  }
+  tc::cp_async_wait_all();
+
+  float* dst = a_tile ? p.A_out + (n * p.a_rows + row0) * int64_t(D) : p.S_out + (n * p.dv + row0) * int64_t(D);
+  for (int e = tid; e < RT * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    dst[int64_t(r) * D + d] = S[r * SD + d];
+  }
+}
+
+template <int RT>
+size_t chain64_smem_bytes() {
+  return sizeof(float) * (size_t(RT) * (512 + 4) + 3 * 2 * 64 * 68 + 4 * 64 * 68 + 2 * 64 * 4 + 2 * 64 * RT);
+}
+
 // rows of S per chain CTA: 16, or 8 when 16-row tiles would leave SMs idle (few sequences), or 4
 // (chunk 64) when 8-row tiles would too; the chains are latency-bound, so more CTAs -- on more SMs,
 // then two per SM -- shorten them
@@ -410,7 +625,17 @@ cudaError_t launch_c(const PrefillProblem& p, const Workspace& w, const ProjPara
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     marks.after(stream);
   }
-  {
+  if (C == 64 && p.D == 512) {  // pipelined pass: 16-row tiles when they fill the SMs, else 8
+    const int rows = p.a_rows + p.dv;
+    const bool r16 = (rows / 16) * p.N >= current_sm_count();
+    const size_t smem = r16 ? chain64_smem_bytes<16>() : chain64_smem_bytes<8>();
+    auto chain = r16 ? simt_chain64_kernel<16> : simt_chain64_kernel<8>;
+    err = cudaFuncSetAttribute(chain, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return err;
+    chain<<<dim3(rows / (r16 ? 16 : 8), unsigned(p.N)), kThreads, smem, stream>>>(p, w);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    marks.after(stream);
+  } else {
     const int rt = chain_rows(p.a_rows + p.dv, p.N, C);
     const size_t smem = rt == 4   ? chain_smem_bytes<C, (C == 64 ? 4 : 8)>(p.D)
                         : rt == 8 ? chain_smem_bytes<C, 8>(p.D)
