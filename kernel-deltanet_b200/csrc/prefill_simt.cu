@@ -184,16 +184,28 @@ __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, W
     Tm[i * LD + j] = (i == j) ? 1.f : 0.f;
   }
   __syncthreads();
-  // forward substitution, row by row: T_ij = -sum_{l=j}^{i-1} A_il T_lj  (j < i)
-  for (int i = 1; i < C; ++i) {
-    if (tid < i) {
-      const int j = tid;
-      float s = 0.f;
-      for (int l = j; l < i; ++l) s = fmaf(G[i * LD + l], Tm[l * LD + j], s);
-      Tm[i * LD + j] = -s;
+  // forward substitution T_ij = -sum_{l=j}^{i-1} A_il T_lj (j < i): the columns of T are independent,
+  // so thread j takes column j down the rows with the column so far in registers (A_il read by all
+  // column threads at once: a broadcast)
+  if (tid < C) {
+    const int j = tid;
+    float col[C];
+#pragma unroll
+    for (int l = 0; l < C; ++l) col[l] = (l == j) ? 1.f : 0.f;
+#pragma unroll
+    for (int i = 1; i < C; ++i) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int l = 0; l < i; l += 2) {
+        s0 = fmaf(G[i * LD + l], col[l], s0);
+        if (l + 1 < i) s1 = fmaf(G[i * LD + l + 1], col[l + 1], s1);
+      }
+      if (i > j) col[i] = -(s0 + s1);
     }
-    __syncthreads();
+#pragma unroll
+    for (int l = 0; l < C; ++l) Tm[l * LD + j] = col[l];
   }
+  __syncthreads();
 
   float* To = w.Tinv + (n * w.NC + c) * int64_t(C) * C;
   float* Ao = w.Aq + (n * w.NC + c) * int64_t(C) * C;
@@ -385,10 +397,10 @@ size_t chain_smem_bytes(int D) {
 // fp32, rows padded to 68 floats so that a 16-byte row read and the S reads are conflict-free),
 // the chunk's T, Aq and gates load into one of two buffers with its first slice, and the
 // products read 16 bytes at a time.  The state update reads the chunk's K rows from global memory
-// (L2) as float4 with eight loads in flight per thread and a 4 x (RT/2) register block per thread.
+// (L2) as float4 with sixteen loads in flight per thread and a 4 x (RT/2) register block per thread.
 // The arithmetic is the kernel above's (exact fp32), in another summation order.
 template <int RT>
-__global__ void __launch_bounds__(kThreads) simt_chain64_kernel(PrefillProblem p, Workspace w) {
+__global__ void __launch_bounds__(kThreads, 1) simt_chain64_kernel(PrefillProblem p, Workspace w) {
   constexpr int C = 64;
   constexpr int TPR = kThreads / C;  // threads per chunk row
   constexpr int VPT = RT / TPR;      // state rows per thread in the products
@@ -513,14 +525,25 @@ __global__ void __launch_bounds__(kThreads) simt_chain64_kernel(PrefillProblem p
       Rs[i * RT + v0 + u] = beta_i * (vv - gi * x[u]);
     }
     __syncthreads();
-    // E = T R  (T unit lower triangular)
+    // E = T R over all 64 j (T is stored whole: unit diagonal, zeros above), four partial sums
     float e_[VPT];
+    {
+      float ep[4][VPT];
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) e_[u] = Rs[i * RT + v0 + u];
-    for (int j = 0; j < i; ++j) {
-      const float tij = Tm[i * LD + j];
+      for (int a = 0; a < 4; ++a)
 #pragma unroll
-      for (int u = 0; u < VPT; ++u) e_[u] = fmaf(tij, Rs[j * RT + v0 + u], e_[u]);
+        for (int u = 0; u < VPT; ++u) ep[a][u] = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < C; j += 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(Tm + i * LD + j);
+        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) ep[a][u] = fmaf(tv[a], Rs[(j + a) * RT + v0 + u], ep[a][u]);
+      }
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) e_[u] = (ep[0][u] + ep[1][u]) + (ep[2][u] + ep[3][u]);
     }
 #pragma unroll
     for (int u = 0; u < VPT; ++u) Es[i * RT + v0 + u] = e_[u];
@@ -530,15 +553,24 @@ __global__ void __launch_bounds__(kThreads) simt_chain64_kernel(PrefillProblem p
     }
     __syncthreads();
     // y_i = exp(g_{i-1}) yq_i + sum_{j<i} Aq_ij e_j ;  then E''_i = exp(g_{C-1} - g_i) e_i into Rs
-    if (readout) {
+    if (readout) {  // Aq is strictly lower triangular as stored: all 64 j, four partial sums
       float yv[VPT];
+      float yp[4][VPT];
 #pragma unroll
-      for (int u = 0; u < VPT; ++u) yv[u] = gprev * yq[u];
-      for (int j = 0; j < i; ++j) {
-        const float aij = Am[i * LD + j];
+      for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int u = 0; u < VPT; ++u) yv[u] = fmaf(aij, Es[j * RT + v0 + u], yv[u]);
+        for (int u = 0; u < VPT; ++u) yp[a][u] = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < C; j += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(Am + i * LD + j);
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) yp[a][u] = fmaf(av[a], Es[(j + a) * RT + v0 + u], yp[a][u]);
       }
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) yv[u] = fmaf(gprev, yq[u], (yp[0][u] + yp[1][u]) + (yp[2][u] + yp[3][u]));
       if (t < p.T) {
 #pragma unroll
         for (int u = 0; u < VPT; ++u) st_from_f32(p.y, p.y_dtype, (n * p.T + t) * p.dv + row0 + v0 + u, yv[u]);
@@ -557,12 +589,12 @@ __global__ void __launch_bounds__(kThreads) simt_chain64_kernel(PrefillProblem p
         acc[r][0] = gC * s4.x, acc[r][1] = gC * s4.y, acc[r][2] = gC * s4.z, acc[r][3] = gC * s4.w;
       }
 #pragma unroll 1
-      for (int j0 = 0; j0 < C; j0 += 8) {
-        float4 kv[8];
+      for (int j0 = 0; j0 < C; j0 += 16) {
+        float4 kv[16];
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) kv[jj] = __ldcg(reinterpret_cast<const float4*>(Kg + int64_t(j0 + jj) * D));
+        for (int jj = 0; jj < 16; ++jj) kv[jj] = __ldcg(reinterpret_cast<const float4*>(Kg + int64_t(j0 + jj) * D));
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
+        for (int jj = 0; jj < 16; ++jj) {
 #pragma unroll
           for (int r = 0; r < RPT; ++r) {
             const float ev = Rs[(j0 + jj) * RT + RPT * rb + r];
