@@ -809,8 +809,9 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
-def run_prefill_only(n_seq: int, seq: int):
-    """Two prefill calls on seeded inputs of [n_seq, seq] (the case `ncu` captures use)."""
+def run_prefill_only(n_seq: int, seq: int, mode: str = "bf16"):
+    """Two prefill calls on seeded inputs of [n_seq, seq] (the case `ncu` captures use); mode "fp32" runs
+    the exact CUDA-core path on fp32 copies of the inputs."""
     import torch
 
     import kdn_b200
@@ -818,10 +819,12 @@ def run_prefill_only(n_seq: int, seq: int):
     dev = torch.device("cuda", 0)
     proj = kdn_b200.FastWalshHadamardProjection().to(dev)
     q, k, v, beta = prefill_inputs(dev, 7, n_heads=n_seq, seq=seq)
-    y = torch.empty(n_seq, seq, DV, device=dev, dtype=torch.bfloat16)
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    q, k, v = (t.to(dt) for t in (q, k, v))
+    y = torch.empty(n_seq, seq, DV, device=dev, dtype=dt)
     S = torch.empty(n_seq, DV, D, device=dev, dtype=torch.float32)
     for _ in range(2):
-        kdn_b200.fused_chunked_deltanet_forward(q, k, v, beta, None, proj, C, mode="bf16", out=y, final_state=S)
+        kdn_b200.fused_chunked_deltanet_forward(q, k, v, beta, None, proj, C, mode=mode, out=y, final_state=S)
     torch.cuda.synchronize()
     print(json.dumps({"prefill_only": [n_seq, seq], "launches_per_call": int(kdn_b200.load().kdn_prefill_launch_count()),
                       "path": os.environ.get("KDN_PREFILL_PATH", "auto")}))
@@ -924,6 +927,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-only", type=int, nargs=2, metavar=("N", "T"),
                     help="only run two prefill calls of N sequences x T tokens (for profiler captures)")
+    ap.add_argument("--prefill-mode", default="bf16", choices=["bf16", "fp32"],
+                    help="arithmetic mode of --prefill-only")
     ap.add_argument("--case", choices=["tp_proj", "decode_attn", "backward", "lift", "anchor_attn", "lm"],
                     help="only run one fixed single-kernel invocation three times (for profiler captures)")
     ap.add_argument("--decode-only", type=int, metavar="STEPS",
@@ -955,7 +960,7 @@ def main():
         run_decode_only(args.decode_only)
         return
     if args.prefill_only:
-        run_prefill_only(*args.prefill_only)
+        run_prefill_only(*args.prefill_only, mode=args.prefill_mode)
         return
     if args.impl == "reference":
         run_reference(args)
