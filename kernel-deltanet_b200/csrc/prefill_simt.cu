@@ -831,6 +831,213 @@ __global__ void __launch_bounds__(kThreads) simt_adjoint_kernel(BackwardProblem 
   }
 }
 
+// (B1) for chunk 64 and D = 512: the same reverse pass with the loads of `simt_chain64_kernel`: the
+// chunk's K slices through a 3-stage cp.async ring for x = K dS^T, its T, Aq and gates into one of two
+// buffers with its first slice, the triangular products over all 64 rows with four partial sums
+// (T and Aq are stored whole, zeros where the sums skip), and the update reading K and Q rows from L2
+// as float4, eight rows of each in flight, into a 4 features x RT/2 rows block per thread.
+template <int RT>
+__global__ void __launch_bounds__(kThreads, 1) simt_adjoint64_kernel(BackwardProblem b, Workspace w,
+                                                                     float* __restrict__ dS_chunks,
+                                                                     float* __restrict__ dR_rows) {
+  constexpr int C = 64;
+  constexpr int TPR = kThreads / C;
+  constexpr int VPT = RT / TPR;
+  constexpr int LD = 68;
+  constexpr int kStages = 3;
+  constexpr int kSlice = C * LD;
+  constexpr int D = 512, SD = D + 4, kNsl = D / 64;
+  constexpr int RPT = RT / 2;
+  const PrefillProblem& p = b.fwd;
+  extern __shared__ __align__(16) float sm[];
+  float* dS = sm;                          // [RT][SD]
+  float* ring = dS + RT * SD;              // [kStages][C][LD] K slices
+  float* Tb = ring + kStages * kSlice;     // [2][T | Aq][C][LD]
+  float* gb = Tb + 4 * C * LD;             // [2][C][4]
+  float* Ys = gb + 2 * C * 4;              // [C][RT]: dY, then Gs_i dY_i
+  float* Ws = Ys + C * RT;                 // [C][RT]: dE, then beta_i G_i dR_i
+
+  const int64_t n = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int i = tid / TPR;
+  const int v0 = (tid % TPR) * VPT;
+  const int row0 = blockIdx.x * RT;
+  const int NC = w.NC;
+  const int64_t items = int64_t(NC) * kNsl;
+
+  for (int e = tid; e < RT * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    dS[r * SD + d] = b.dS_final ? b.dS_final[(n * p.dv + row0 + r) * int64_t(D) + d] : 0.f;
+  }
+  // item g: slice g % 8 of chunk NC - 1 - g / 8 (chunks in reverse) into stage g % 3; the first slice
+  // also brings the chunk's T, Aq and gates into buffer (g / 8) & 1
+  auto issue = [&](int64_t g) {
+    if (g < items) {
+      const int ci = int(g / kNsl), s = int(g % kNsl), c = NC - 1 - ci;
+      const int64_t rowbase = (n * w.Tp + int64_t(c) * C) * D + 64 * s;
+      float* st = ring + int(g % kStages) * kSlice;
+      for (int e = tid; e < C * 16; e += kThreads) {
+        const int r = e >> 4, q = e & 15;
+        tc::cp_async16(tc::smem_u32(st + r * LD + 4 * q), w.phik + rowbase + int64_t(r) * D + 4 * q, 16);
+      }
+      if (s == 0) {
+        const int64_t cm = (n * NC + c) * int64_t(C) * C;
+        float* tb = Tb + (ci & 1) * 2 * C * LD;
+        for (int e = tid; e < C * 16; e += kThreads) {
+          const int r = e >> 4, q = e & 15;
+          tc::cp_async16(tc::smem_u32(tb + r * LD + 4 * q), w.Tinv + cm + r * C + 4 * q, 16);
+          tc::cp_async16(tc::smem_u32(tb + C * LD + r * LD + 4 * q), w.Aq + cm + r * C + 4 * q, 16);
+        }
+        const float* Gg = w.gates + (n * NC + c) * int64_t(C) * 4;
+        for (int e = tid; e < C; e += kThreads) tc::cp_async16(tc::smem_u32(gb + (ci & 1) * C * 4 + 4 * e), Gg + 4 * e, 16);
+      }
+    }
+    tc::cp_async_commit();
+  };
+  for (int g = 0; g < kStages - 1; ++g) issue(g);
+  __syncthreads();
+
+  const int fb = tid % (D / 4);
+  const int rb = tid / (D / 4);
+  for (int ci = 0; ci < NC; ++ci) {
+    const int c = NC - 1 - ci;
+    float* dSc = dS_chunks + ((n * NC + c) * p.dv + row0) * int64_t(D);
+    for (int e = tid; e < RT * D; e += kThreads) dSc[e] = dS[(e / D) * SD + e % D];
+    // x_i = k_i . dS_v  (C x RT), slice by slice from the ring
+    float x[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) x[u] = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < kNsl; ++s) {
+      const int64_t g = int64_t(ci) * kNsl + s;
+      tc::cp_async_wait_group<kStages - 2>();
+      __syncthreads();
+      issue(g + kStages - 1);
+      const float* Ks = ring + int(g % kStages) * kSlice;
+      const float* Sd = dS + 64 * s;
+#pragma unroll 4
+      for (int dd = 0; dd < 64; dd += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * LD + dd);
+#pragma unroll
+        for (int u = 0; u < VPT; ++u) {
+          const float4 s4 = *reinterpret_cast<const float4*>(Sd + (v0 + u) * SD + dd);
+          x[u] = fmaf(k4.w, s4.w, fmaf(k4.z, s4.z, fmaf(k4.y, s4.y, fmaf(k4.x, s4.x, x[u]))));
+        }
+      }
+    }
+    const float* Tm = Tb + (ci & 1) * 2 * C * LD;
+    const float* Am = Tm + C * LD;
+    const float* gt = gb + (ci & 1) * C * 4;
+    const int64_t t = int64_t(c) * C + i;
+#pragma unroll
+    for (int u = 0; u < VPT; ++u)
+      Ys[i * RT + v0 + u] = t < p.T ? ld_as_f32(b.dy, b.dy_dtype, (n * p.T + t) * p.dv + row0 + v0 + u) : 0.f;
+    __syncthreads();
+    // dE_i = Rg_i x_i + sum_j Aq_ji dY_j  (Aq_ji = 0 for j <= i)
+    const float rg = gt[4 * i + 2];
+    float de[VPT];
+    {
+      float dp[4][VPT];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int u = 0; u < VPT; ++u) dp[a][u] = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < C; j += 4) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const float aq = Am[(j + a) * LD + i];
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) dp[a][u] = fmaf(aq, Ys[(j + a) * RT + v0 + u], dp[a][u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) de[u] = fmaf(rg, x[u], (dp[0][u] + dp[1][u]) + (dp[2][u] + dp[3][u]));
+    }
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) Ws[i * RT + v0 + u] = de[u];
+    __syncthreads();
+    // dR_i = sum_j T_ji dE_j  (T_ii = 1, T_ji = 0 for j < i)
+    float dr[VPT];
+    {
+      float dp[4][VPT];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int u = 0; u < VPT; ++u) dp[a][u] = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < C; j += 4) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const float tv = Tm[(j + a) * LD + i];
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) dp[a][u] = fmaf(tv, Ws[(j + a) * RT + v0 + u], dp[a][u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) dr[u] = (dp[0][u] + dp[1][u]) + (dp[2][u] + dp[3][u]);
+    }
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) dR_rows[(n * w.Tp + t) * p.dv + row0 + v0 + u] = dr[u];
+    const float gprev = gt[4 * i + 0], gi = gt[4 * i + 1], beta_i = gt[4 * i + 3];
+    const float gC = gt[4 * (C - 1) + 1];
+    __syncthreads();  // every read of dE and dY is done
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+      Ws[i * RT + v0 + u] = beta_i * gi * dr[u];
+      Ys[i * RT + v0 + u] *= gprev;
+    }
+    __syncthreads();
+    // dS <- G_{C-1} dS + sum_j (Gs_j dY_j q_j^T - beta_j G_j dR_j k_j^T): features 4 fb.., rows RPT rb..
+    {
+      const int64_t base = (n * w.Tp + int64_t(c) * C) * D + 4 * fb;
+      float acc[RPT][4];
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        const float4 s4 = *reinterpret_cast<const float4*>(dS + (RPT * rb + r) * SD + 4 * fb);
+        acc[r][0] = gC * s4.x, acc[r][1] = gC * s4.y, acc[r][2] = gC * s4.z, acc[r][3] = gC * s4.w;
+      }
+#pragma unroll 1
+      for (int j0 = 0; j0 < C; j0 += 8) {
+        float4 kv[8], qv[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          kv[jj] = __ldcg(reinterpret_cast<const float4*>(w.phik + base + int64_t(j0 + jj) * D));
+          qv[jj] = __ldcg(reinterpret_cast<const float4*>(w.phiq + base + int64_t(j0 + jj) * D));
+        }
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+          for (int r = 0; r < RPT; ++r) {
+            const float yv = Ys[(j0 + jj) * RT + RPT * rb + r], wv = -Ws[(j0 + jj) * RT + RPT * rb + r];
+            acc[r][0] = fmaf(yv, qv[jj].x, fmaf(wv, kv[jj].x, acc[r][0]));
+            acc[r][1] = fmaf(yv, qv[jj].y, fmaf(wv, kv[jj].y, acc[r][1]));
+            acc[r][2] = fmaf(yv, qv[jj].z, fmaf(wv, kv[jj].z, acc[r][2]));
+            acc[r][3] = fmaf(yv, qv[jj].w, fmaf(wv, kv[jj].w, acc[r][3]));
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RPT; ++r)
+        *reinterpret_cast<float4*>(dS + (RPT * rb + r) * SD + 4 * fb) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    }
+    __syncthreads();
+  }
+  tc::cp_async_wait_all();
+  if (b.dS0) {
+    for (int e = tid; e < RT * D; e += kThreads) {
+      const int r = e / D, d = e % D;
+      b.dS0[(n * p.dv + row0 + r) * int64_t(D) + d] = dS[r * SD + d];
+    }
+  }
+}
+
+template <int RT>
+size_t adjoint64_smem_bytes() {
+  return sizeof(float) * (size_t(RT) * (512 + 4) + 3 * 64 * 68 + 4 * 64 * 68 + 2 * 64 * 4 + 2 * 64 * RT);
+}
+
 // (B2) per (chunk, sequence): the gradients of the chunk's tokens.  The feature gradients
 // overwrite the chunk's lifted features in the workspace (dq -> phiq rows, dk -> phik rows).
 constexpr int kSlab = 32;
@@ -1239,7 +1446,16 @@ cudaError_t launch_backward_c(BackwardProblem b, const Workspace& w, const Backw
   b.fwd.A_out = nullptr;
   cudaError_t err = launch_c<C>(b.fwd, w, P, stream, none);  // lift, prep, chain with checkpoints
   if (err != cudaSuccess) return err;
-  {
+  if (C == 64 && b.fwd.D == 512) {  // pipelined reverse pass
+    const bool r16 = chain_rows(b.fwd.dv, b.fwd.N, C) == 16;
+    const size_t smem = r16 ? adjoint64_smem_bytes<16>() : adjoint64_smem_bytes<8>();
+    auto adjoint = r16 ? simt_adjoint64_kernel<16> : simt_adjoint64_kernel<8>;
+    err = cudaFuncSetAttribute(adjoint, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return err;
+    adjoint<<<dim3(b.fwd.dv / (r16 ? 16 : 8), unsigned(b.fwd.N)), kThreads, smem, stream>>>(b, w, x.dS_chunks,
+                                                                                            x.dR_rows);
+    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  } else {
     // tiles of at least 8 rows here: the adjoint loads K and Q per chunk, and 4-row tiles measured slower
     const int rt = chain_rows(b.fwd.dv, b.fwd.N, C) == 16 ? 16 : 8;
     const size_t smem = rt == 8 ? adjoint_smem_bytes<C, 8>(b.fwd.D) : adjoint_smem_bytes<C, 16>(b.fwd.D);
