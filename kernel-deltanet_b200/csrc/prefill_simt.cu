@@ -1042,10 +1042,13 @@ size_t adjoint64_smem_bytes() {
 // overwrite the chunk's lifted features in the workspace (dq -> phiq rows, dk -> phik rows).
 constexpr int kSlab = 32;
 
+constexpr int kSlabLd = kSlab + 4;  // staged slab rows: 16-byte aligned for cp.async
+
 template <int C>
 size_t grad_smem_bytes(int dv) {
-  return sizeof(float) * (size_t(3) * C * (dv + 1) + 2 * C * (C + 1) + 2 * C * (kSlab + 1) +
-                          2 * size_t(dv) * (kSlab + 1) + 9 * C + 8);
+  // rows, the two C x C matrices, two stages of [K | Q | S_0 | dS_C] slabs, the per-token vectors
+  return sizeof(float) * (size_t(3) * C * (dv + 1) + 2 * C * (C + 1) + 2 * (2 * C + 2 * size_t(dv)) * kSlabLd +
+                          9 * C + 8);
 }
 
 template <int C>
@@ -1065,11 +1068,10 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
   float* Ym = Xm + C * LV;         // [C][LV] dY rows
   float* M1 = Ym + C * LV;         // [C][LD] Gram k.k, then Ab + Ab^T
   float* M2 = M1 + C * LD;         // [C][LD] Mq
-  float* Ks = M2 + C * LD;         // [C][SL]
-  float* Qs = Ks + C * SL;         // [C][SL]
-  float* S0s = Qs + C * SL;        // [dv][SL]
-  float* dSs = S0s + dv * SL;      // [dv][SL]
-  float* gl = dSs + dv * SL;       // [C] g_i
+  float* ring = M2 + C * LD;       // 2 stages of [K | Q | S_0 | dS_C] slabs, rows kSlabLd floats apart
+  const int kStage = (2 * C + 2 * dv) * kSlabLd;
+  float* Ks = ring;                // sweep 1: the K slab in stage 0, [C][SL]
+  float* gl = ring + 2 * kStage;   // [C] g_i
   float* bt = gl + C;              // [C] beta_i
   float* lm = bt + C;              // [C] decay as given (1 past T)
   float* dg = lm + C;              // [C] d g_i
@@ -1134,10 +1136,6 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
       const int r = e / kSlab, cc = e % kSlab;
       Ks[r * SL + cc] = Kg[int64_t(r) * D + d0 + cc];
     }
-    for (int e = tid; e < dv * kSlab; e += kThreads) {
-      const int r = e / kSlab, cc = e % kSlab;
-      dss = fmaf(S0g[int64_t(r) * D + d0 + cc], dSg[int64_t(r) * D + d0 + cc], dss);
-    }
     __syncthreads();
 #pragma unroll 4
     for (int dd = 0; dd < kSlab; ++dd) {
@@ -1154,8 +1152,27 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
     }
     __syncthreads();
   }
-  dss = warp_sum(dss);
-  if (lane == 0) red[warp] = dss;
+
+  // the slabs of sweep 2 through a 2-stage cp.async ring (slab m + 1 loads while slab m is used);
+  // <dS_C, S_0> is taken from the staged slabs too
+  const int nslab = D / kSlab;
+  auto issue = [&](int m) {
+    if (m < nslab) {
+      float* st = ring + (m & 1) * kStage;
+      const int dm = m * kSlab;
+      constexpr int kq = kSlab / 4;  // 16-byte pieces per slab row
+      for (int e = tid; e < (2 * C + 2 * dv) * kq; e += kThreads) {
+        const int r = e / kq, q4 = e % kq;
+        const float* src = r < C       ? Kg + int64_t(r) * D
+                           : r < 2 * C ? Qg + int64_t(r - C) * D
+                           : r < 2 * C + dv ? S0g + int64_t(r - 2 * C) * D
+                                            : dSg + int64_t(r - 2 * C - dv) * D;
+        tc::cp_async16(tc::smem_u32(st + r * kSlabLd + 4 * q4), src + dm + 4 * q4, 16);
+      }
+    }
+    tc::cp_async_commit();
+  };
+  issue(0);  // sweep 1 is over with stage 0 (its last barrier); slab 0 lands during the C x C phase
 
   // ---- C x C phase: dA, dY.E, the exp(g) factors, d g and d beta contributions
   float dA[R][R], dP[R][R];
@@ -1228,52 +1245,81 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
   const float Rg_i = expf(gl[C - 1] - gl[i]);
   const float bG = bt[i] * G_i;
   float p1 = 0.f, p2 = 0.f, p3 = 0.f;
-  for (int d0 = 0; d0 < D; d0 += kSlab) {
-    __syncthreads();
-    for (int e = tid; e < C * kSlab; e += kThreads) {
-      const int r = e / kSlab, cc = e % kSlab;
-      Ks[r * SL + cc] = Kg[int64_t(r) * D + d0 + cc];
-      Qs[r * SL + cc] = Qg[int64_t(r) * D + d0 + cc];
-    }
+  for (int m = 0; m < nslab; ++m) {
+    const int d0 = m * kSlab;
+    tc::cp_async_wait_group<0>();
+    __syncthreads();  // slab m has landed everywhere; the stage of slab m - 1 is free
+    issue(m + 1);
+    const float* st = ring + (m & 1) * kStage;
+    const float* Kst = st;
+    const float* Qst = st + C * kSlabLd;
+    const float* S0s = st + 2 * C * kSlabLd;
+    const float* dSs = S0s + dv * kSlabLd;
     for (int e = tid; e < dv * kSlab; e += kThreads) {
       const int r = e / kSlab, cc = e % kSlab;
-      S0s[r * SL + cc] = S0g[int64_t(r) * D + d0 + cc];
-      dSs[r * SL + cc] = dSg[int64_t(r) * D + d0 + cc];
+      dss = fmaf(S0s[r * kSlabLd + cc], dSs[r * kSlabLd + cc], dss);
     }
-    __syncthreads();
     float yS[CPT], xS[CPT], wS[CPT], mK[CPT], mQ[CPT], aK[CPT];
 #pragma unroll
     for (int q = 0; q < CPT; ++q) yS[q] = xS[q] = wS[q] = mK[q] = mQ[q] = aK[q] = 0.f;
+    // the staged rows are read 16 bytes at a time (cb is a multiple of 4, rows are 16-byte aligned)
+    auto row4 = [&](const float* rowp, float (&o)[CPT]) {
+#pragma unroll
+      for (int q = 0; q < CPT; q += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(rowp + cb + q);
+        o[q] = f.x;
+        o[q + 1] = f.y;
+        o[q + 2] = f.z;
+        o[q + 3] = f.w;
+      }
+    };
     for (int v = 0; v < dv; ++v) {
       const float yi = Ym[i * LV + v], xi = Xm[i * LV + v], ei = Em[i * LV + v];
+      float s0[CPT], ds[CPT];
+      row4(S0s + v * kSlabLd, s0);
+      row4(dSs + v * kSlabLd, ds);
 #pragma unroll
       for (int q = 0; q < CPT; ++q) {
-        const float s0 = S0s[v * SL + cb + q], ds = dSs[v * SL + cb + q];
-        yS[q] = fmaf(yi, s0, yS[q]);
-        xS[q] = fmaf(xi, s0, xS[q]);
-        wS[q] = fmaf(ei, ds, wS[q]);
+        yS[q] = fmaf(yi, s0[q], yS[q]);
+        xS[q] = fmaf(xi, s0[q], xS[q]);
+        wS[q] = fmaf(ei, ds[q], wS[q]);
       }
     }
     for (int j = 0; j < C; ++j) {
       const float m_ij = M2[i * LD + j], m_ji = M2[j * LD + i], a_ij = M1[i * LD + j];
+      float kj[CPT], qj[CPT];
+      row4(Kst + j * kSlabLd, kj);
+      row4(Qst + j * kSlabLd, qj);
 #pragma unroll
       for (int q = 0; q < CPT; ++q) {
-        const float kj = Ks[j * SL + cb + q], qj = Qs[j * SL + cb + q];
-        mK[q] = fmaf(m_ij, kj, mK[q]);
-        aK[q] = fmaf(a_ij, kj, aK[q]);
-        mQ[q] = fmaf(m_ji, qj, mQ[q]);
+        mK[q] = fmaf(m_ij, kj[q], mK[q]);
+        aK[q] = fmaf(a_ij, kj[q], aK[q]);
+        mQ[q] = fmaf(m_ji, qj[q], mQ[q]);
       }
     }
+    float oq[CPT], ok_[CPT], kr[CPT], qr[CPT];
+    row4(Kst + i * kSlabLd, kr);
+    row4(Qst + i * kSlabLd, qr);
 #pragma unroll
     for (int q = 0; q < CPT; ++q) {
-      const float ki = Ks[i * SL + cb + q], qi = Qs[i * SL + cb + q];
+      const float ki = kr[q], qi = qr[q];
       p1 = fmaf(ki, xS[q], p1);
       p2 = fmaf(qi, yS[q], p2);
       p3 = fmaf(ki, wS[q], p3);
-      Qg[int64_t(i) * D + d0 + cb + q] = fmaf(Gs_i, yS[q], mK[q]);
-      Kg[int64_t(i) * D + d0 + cb + q] = mQ[q] - bG * xS[q] + Rg_i * wS[q] + aK[q];
+      oq[q] = fmaf(Gs_i, yS[q], mK[q]);
+      ok_[q] = mQ[q] - bG * xS[q] + Rg_i * wS[q] + aK[q];
+    }
+    // the gradients overwrite this chunk's features (its slab is staged already), 16 bytes at a time
+#pragma unroll
+    for (int q = 0; q < CPT; q += 4) {
+      *reinterpret_cast<float4*>(Qg + int64_t(i) * D + d0 + cb + q) = make_float4(oq[q], oq[q + 1], oq[q + 2], oq[q + 3]);
+      *reinterpret_cast<float4*>(Kg + int64_t(i) * D + d0 + cb + q) =
+          make_float4(ok_[q], ok_[q + 1], ok_[q + 2], ok_[q + 3]);
     }
   }
+  tc::cp_async_wait_all();
+  dss = warp_sum(dss);
+  if (lane == 0) red[warp] = dss;
 #pragma unroll
   for (int o = TPR2 / 2; o > 0; o >>= 1) {
     p1 += __shfl_xor_sync(0xffffffffu, p1, o);
