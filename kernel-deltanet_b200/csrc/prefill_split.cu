@@ -105,6 +105,19 @@ __device__ __forceinline__ bool split_wait_bit(uint64_t* bar, uint32_t& bits, in
   return r;
 }
 
+// Element i of a gate array (bf16 or fp32) as raw bits: the bf16 bits in the low half, else the fp32
+// bits.  The two loads are predicated into one register, so nothing consumes the value at the load
+// and the issuing warp does not wait for it until the bits are converted.
+__device__ __forceinline__ uint32_t ld_gate_bits(const void* p, bool bf16, int64_t i) {
+  uint32_t r;
+  const char* b = reinterpret_cast<const char*>(p);
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %1, 0;\n\t@q ld.global.u16 %0, [%2];\n\t@!q ld.global.b32 %0, [%3];\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(bf16)), "l"(b + 2 * i), "l"(b + 4 * i));
+  return r;
+}
+
 // ---- hand-over flags between the phases of the persistent launch (global memory)
 constexpr uint32_t kFlagSpins = 1u << 24;  // bounded: ~10 s of polling at most
 // wait until *flag >= target (acquire at GPU scope)
@@ -159,7 +172,8 @@ constexpr uint32_t P1_SSP = 216320;   // 2 KiB  sums of squares per column quart
 constexpr uint32_t P1_SC = 218368;    // 512 B  token scales
 constexpr uint32_t P1_BAR = 218880;   // mbarriers + TMEM address
 constexpr uint32_t kP1Bars = 144;      // bytes of barriers
-constexpr uint32_t kP1Smem = P1_BAR + kP1Bars + 1024;
+constexpr uint32_t P1_FK = 219136;    // 256 B  beta exp(g) s_k per token: the column factors of T'
+constexpr uint32_t kP1Smem = P1_FK + 256 + 1024;
 static_assert(P1_VEC + 1024 <= P1_F1 && P1_F1 + 32768 <= P1_ES && P1_ES + 64 * kEsLd * 4 <= P1_VB,
               "phase-1 shared-memory regions overlap");
 
@@ -222,6 +236,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   float* wdec = gl + 256;
   float* ssp = reinterpret_cast<float*>(sm + P1_SSP);
   float* sc = reinterpret_cast<float*>(sm + P1_SC);
+  float* fk = reinterpret_cast<float*>(sm + P1_FK);
   uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + P1_BAR + 80);  // [2] lift into slot s & 1 done
   uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + P1_BAR + 8);
   uint64_t* bar_xin = reinterpret_cast<uint64_t*>(sm + P1_BAR + 16);
@@ -234,6 +249,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   uint64_t* bar_fdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 128);  // [2] the Gram product of the slice
                                                                           //     in buffer s & 1 done and its
                                                                           //     features copied out (2 arrivals)
+  uint64_t* bar_gram = reinterpret_cast<uint64_t*>(sm + P1_BAR + 24);    // the last slice's Gram product done
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cq = (warp >> 2) & 3;
@@ -258,6 +274,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
     tc::mbar_init(bar_stfree, 1);
     tc::mbar_init(&bar_fdone[0], 2);
     tc::mbar_init(&bar_fdone[1], 2);
+    tc::mbar_init(bar_gram, 1);
     tc::fence_mbar_init();
   }
   build_omega(sm + P1_OMG, P, warp, lane, kP1Thr / 32);
@@ -305,6 +322,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
             tc::mma_ss(tmem + P1_GP, fd, fd, id_gp, s > 0 || k0 > 0);
           }
           tc::mma_commit(&bar_fdone[s & 1]);  // the buffer is rewritten once the publisher has copied it out too
+          if (s == kSlices - 1) tc::mma_commit(bar_gram);
         }
         // every slot of this chunk has been read: the next chunk's first lifts run during this
         // chunk's algebra (its inputs are announced by the compute warps mid-algebra)
@@ -358,26 +376,74 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
     __syncwarp();
   } else if (warp < kP1Warps) {
     // ================================================================ compute warps
-    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0, ph_fd = 0;
+    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0, ph_fd = 0, ph_gram = 0;
     auto wait_mma = [&]() {
       ok &= split_wait(bar_mma, ph_mma, sa.abort);
       ph_mma ^= 1;
       tc::fence_after_sync();
     };
-    float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};  // gates of the coming chunk (warp 0)
-    if (warp == 0 && cta < total) {
-      const int64_t n0 = int64_t(cta) % N, t00 = (int64_t(cta) / N) * kC;
+    // gates of the coming chunk (warp 0), as raw bits: converting at the load would make the warp wait
+    // for it there; the next chunk's gates are only used a chunk later
+    const bool gate_bf = a.gate_dtype == KDN_DTYPE_BF16;
+    uint32_t nb[2] = {0u, 0u}, nd[2] = {0x3f800000u, 0x3f800000u};
+    auto load_gates = [&](int64_t n_, int64_t c_) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int64_t tt = t00 + 2 * lane + e;
+        const int64_t tt = c_ * kC + 2 * lane + e;
+        nb[e] = 0u;
+        nd[e] = 0x3f800000u;  // 1.0f
         if (tt < a.T) {
-          nb[e] = ld_as_f32(a.beta, a.gate_dtype, n0 * a.T + tt);
-          if (decayed) nd[e] = ld_as_f32(a.decay, a.gate_dtype, n0 * a.T + tt);
+          nb[e] = ld_gate_bits(a.beta, gate_bf, n_ * a.T + tt);
+          if (decayed) nd[e] = ld_gate_bits(a.decay, gate_bf, n_ * a.T + tt);
         }
       }
-    }
+    };
+    auto gate_f32 = [&](uint32_t bits) { return __uint_as_float(gate_bf ? bits << 16 : bits); };
+    // warp 0: the gates of the chunk whose raw gates nb, nd hold: beta, the inclusive scan of
+    // log clamp(decay, 1e-5, 1) and the derived factors
+    auto compute_gates = [&]() {
+      const float lg0 = decayed ? logf(fminf(fmaxf(gate_f32(nd[0]), 1e-5f), 1.0f)) : 0.f;
+      const float lg1 = decayed ? logf(fminf(fmaxf(gate_f32(nd[1]), 1e-5f), 1.0f)) : 0.f;
+      float s = lg0 + lg1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      const float g0 = s - lg1, g1 = s;
+      const float gend = __shfl_sync(0xffffffffu, s, 31);
+      const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
+      gl[2 * lane] = g0;
+      gl[2 * lane + 1] = g1;
+      bt[2 * lane] = gate_f32(nb[0]);
+      bt[2 * lane + 1] = gate_f32(nb[1]);
+      eg[2 * lane] = __expf(g0);
+      eg[2 * lane + 1] = __expf(g1);
+      egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
+      egp[2 * lane + 1] = __expf(g0);
+      wdec[2 * lane] = __expf(gend - g0);
+      wdec[2 * lane + 1] = __expf(gend - g1);
+    };
+    if (warp == 0 && cta < total) load_gates(int64_t(cta) % N, int64_t(cta) / N);
+    // v of chunk (n_, c_) into the T staging area Es (free from the end of one chunk's algebra to the
+    // next chunk's T): thread tid copies row tid / 8, values 8 (tid % 8) .. +7 (zeros past the end), and
+    // later reads back only what it copied itself
+    auto prefetch_v = [&](int64_t n_, int64_t c_) {
+      const int row = tid >> 3, cc = tid & 7;
+      const int64_t t = c_ * kC + row;
+      const bool in = t < a.T;
+      if (bf_in) {
+        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.v) + (in ? (n_ * a.T + t) * kDV + 8 * cc : 0);
+        tc::cp_async16(sbase + P1_ES + row * 128 + 16 * cc, src, in ? 16 : 0);
+      } else {
+        const float* src = reinterpret_cast<const float*>(a.v) + (in ? (n_ * a.T + t) * kDV + 8 * cc : 0);
+        tc::cp_async16(sbase + P1_ES + row * 256 + 32 * cc, src, in ? 16 : 0);
+        tc::cp_async16(sbase + P1_ES + row * 256 + 32 * cc + 16, src + 4, in ? 16 : 0);
+      }
+      tc::cp_async_commit();
+    };
     for (int64_t idx = cta; idx < total; idx += ncta) {
-      const int64_t n = idx % N, c = idx / N, t0 = c * kC;
+      const int64_t n = idx % N, c = idx / N;
       const int64_t nidx = idx + ncta;
       const bool has_next = nidx < total;
       const int64_t nn = nidx % N, ncn = nidx / N;
@@ -389,65 +455,11 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(bar_xin);
+        prefetch_v(n, c);  // later chunks' v is fetched during the previous chunk's products
       }
-      float vreg[8];  // v row tid/8, values 8 (tid%8) .. +7 (zero past the end)
-      {
-        const int row = tid >> 3, cc = tid & 7;
-        const int64_t t = t0 + row;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) vreg[j] = 0.f;
-        if (t < a.T) {
-          if (bf_in) {
-            const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.v) +
-                                                           (n * a.T + t) * kDV + 8 * cc);
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(h[j]);
-              vreg[2 * j] = f.x;
-              vreg[2 * j + 1] = f.y;
-            }
-          } else {
-            const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.v) +
-                                                                (n * a.T + t) * kDV + 8 * cc);
-            const float4 x0 = src[0], x1 = src[1];
-            vreg[0] = x0.x, vreg[1] = x0.y, vreg[2] = x0.z, vreg[3] = x0.w;
-            vreg[4] = x1.x, vreg[5] = x1.y, vreg[6] = x1.z, vreg[7] = x1.w;
-          }
-        }
-      }
-      if (warp == 0) {  // gates: beta, inclusive scan of log clamp(decay, 1e-5, 1), derived factors
-        const float lg0 = decayed ? logf(fminf(fmaxf(nd[0], 1e-5f), 1.0f)) : 0.f;
-        const float lg1 = decayed ? logf(fminf(fmaxf(nd[1], 1e-5f), 1.0f)) : 0.f;
-        float s = lg0 + lg1;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float y = __shfl_up_sync(0xffffffffu, s, o);
-          if (lane >= o) s += y;
-        }
-        const float g0 = s - lg1, g1 = s;
-        const float gend = __shfl_sync(0xffffffffu, s, 31);
-        const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
-        gl[2 * lane] = g0;
-        gl[2 * lane + 1] = g1;
-        bt[2 * lane] = nb[0];
-        bt[2 * lane + 1] = nb[1];
-        eg[2 * lane] = __expf(g0);
-        eg[2 * lane + 1] = __expf(g1);
-        egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
-        egp[2 * lane + 1] = __expf(g0);
-        wdec[2 * lane] = __expf(gend - g0);
-        wdec[2 * lane + 1] = __expf(gend - g1);
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int64_t tt = ncn * kC + 2 * lane + e;
-          nb[e] = 0.f;
-          nd[e] = 1.f;
-          if (has_next && tt < a.T) {
-            nb[e] = ld_as_f32(a.beta, a.gate_dtype, nn * a.T + tt);
-            if (decayed) nd[e] = ld_as_f32(a.decay, a.gate_dtype, nn * a.T + tt);
-          }
-        }
+      if (warp == 0 && idx == cta) {  // later chunks' gates are formed during the previous chunk's U product
+        compute_gates();
+        if (has_next) load_gates(nn, ncn);
       }
 
       // ---------------------------------------- slice loop: features, Gram products
@@ -483,6 +495,9 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         } else if (s == 0 && idx != cta) {  // the previous chunk's staged tiles (buffer 0) have been copied out
           ok &= split_wait(bar_stfree, ph_st, sa.abort);
           ph_st ^= 1;
+        } else if (s == 1 && idx != cta) {  // the previous chunk's last slice (buffer 1) has been copied out
+          ok &= split_wait_bit(&bar_fdone[1], ph_fd, 1, sa.abort);
+          tc::fence_after_sync();
         }
         {
           const int kb = cq >> 1, e0 = 32 * (cq & 1);
@@ -507,9 +522,11 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         else load_kq_f32(a, nn, int(ncn), sm + P1_XIN, tid);
       }
       tc::cp_async_commit();
-      // Gram products (and copy-outs) of the last two slices: buffer 0 takes the algebra's A next
+      // the Gram products of the last two slices, and the copy-out of slice kSlices - 2 (buffer 0 takes
+      // the algebra's A next); the last slice's copy-out is awaited before the next chunk rewrites buffer 1
       ok &= split_wait_bit(&bar_fdone[0], ph_fd, 0, sa.abort);
-      ok &= split_wait_bit(&bar_fdone[1], ph_fd, 1, sa.abort);
+      ok &= split_wait(bar_gram, ph_gram, sa.abort);
+      ph_gram ^= 1;
       tc::fence_after_sync();
 
       // ---------------------------------------- chunk matrices
@@ -558,7 +575,26 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         if (tid < 64) vec[tid] = wdec[tid] * sc[tid];
         else if (tid < 128) vec[tid] = sc[tid] * egp[tid - 64];
         else if (tid == 128) vec[128] = eg[63];
+        else if (tid >= 256 && tid < 320) fk[tid - 256] = bt[tid - 256] * eg[tid - 256] * sc[tid - 256];
         const int row = tid >> 3, cc = tid & 7;
+        // this thread's v values (the group committed after them is the next chunk's k, q prefetch)
+        tc::cp_async_wait_group<1>();
+        float vreg[8];
+        if (bf_in) {
+          const uint4 w = *reinterpret_cast<const uint4*>(sm + P1_ES + row * 128 + 16 * cc);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            vreg[2 * j] = f.x;
+            vreg[2 * j + 1] = f.y;
+          }
+        } else {
+          const float4 x0 = *reinterpret_cast<const float4*>(sm + P1_ES + row * 256 + 32 * cc);
+          const float4 x1 = *reinterpret_cast<const float4*>(sm + P1_ES + row * 256 + 32 * cc + 16);
+          vreg[0] = x0.x, vreg[1] = x0.y, vreg[2] = x0.z, vreg[3] = x0.w;
+          vreg[4] = x1.x, vreg[5] = x1.y, vreg[6] = x1.z, vreg[7] = x1.w;
+        }
         *reinterpret_cast<uint4*>(sm + P1_VB + tc::sw128_offset(row, 8 * cc)) =
             make_uint4(pack_f16_sat(vreg[0], vreg[1]), pack_f16_sat(vreg[2], vreg[3]), pack_f16_sat(vreg[4], vreg[5]),
                        pack_f16_sat(vreg[6], vreg[7]));
@@ -598,16 +634,16 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       // A operand [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major, 128 x 64)
       {
         const int r = tid >> 2, jq = tid & 3, i = r & 63;
+        const float* colf = r < 64 ? fk : bt;
         float w[16];
 #pragma unroll
         for (int j4 = 0; j4 < 4; ++j4) {
           const float4 t4 = *reinterpret_cast<const float4*>(Es + i * kEsLd + 16 * jq + 4 * j4);
-          const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
-#pragma unroll
-          for (int qx = 0; qx < 4; ++qx) {
-            const int j = 16 * jq + 4 * j4 + qx;
-            w[4 * j4 + qx] = tv[qx] * (r < 64 ? bt[j] * eg[j] * sc[j] : bt[j]);
-          }
+          const float4 f4 = *reinterpret_cast<const float4*>(colf + 16 * jq + 4 * j4);
+          w[4 * j4] = t4.x * f4.x;
+          w[4 * j4 + 1] = t4.y * f4.y;
+          w[4 * j4 + 2] = t4.z * f4.z;
+          w[4 * j4 + 3] = t4.w * f4.w;
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h)
@@ -617,8 +653,16 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      tc::named_bar_sync(1, kP1Threads);  // also: gates and scales of this chunk no longer read
+      tc::named_bar_sync(1, kP1Threads);  // also: gates, scales and Es of this chunk no longer read
       if (lane == 0) tc::mbar_arrive(bar_ops);
+      if (has_next) {
+        prefetch_v(nn, ncn);
+        if (warp == 0) {  // this chunk's gates are no longer read: the next chunk's take their place
+          compute_gates();
+          const int64_t n2 = nidx + ncta;
+          if (n2 < total) load_gates(n2 % N, n2 / N);
+        }
+      }
       wait_mma();  // U
 
       // ---------------------------------------- U -> staging tile (F), copied out by the issuer
@@ -1146,7 +1190,7 @@ constexpr uint32_t kSplitTslot = 225536;
 constexpr uint32_t kSplitSmem = kSplitTslot + 16 + 1024;
 static_assert(kP1Smem <= kSplitSmem && kP2Smem <= kSplitSmem && kP3Smem <= kSplitSmem,
               "a role's shared memory exceeds the launch's");
-static_assert(kSplitTslot >= P2_BAR + 8 * kP2Bars && kSplitTslot >= P1_BAR + kP1Bars && kSplitTslot >= P3_BAR + 8 * 18,
+static_assert(kSplitTslot >= P2_BAR + 8 * kP2Bars && kSplitTslot >= P1_FK + 256 && P1_FK >= P1_BAR + kP1Bars && kSplitTslot >= P3_BAR + 8 * 18,
               "TMEM slot overlaps a role's barriers");
 
 __device__ __forceinline__ uint8_t* split_smem() {
