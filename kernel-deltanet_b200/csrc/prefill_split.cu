@@ -105,19 +105,6 @@ __device__ __forceinline__ bool split_wait_bit(uint64_t* bar, uint32_t& bits, in
   return r;
 }
 
-// Element i of a gate array (bf16 or fp32) as raw bits: the bf16 bits in the low half, else the fp32
-// bits.  The two loads are predicated into one register, so nothing consumes the value at the load
-// and the issuing warp does not wait for it until the bits are converted.
-__device__ __forceinline__ uint32_t ld_gate_bits(const void* p, bool bf16, int64_t i) {
-  uint32_t r;
-  const char* b = reinterpret_cast<const char*>(p);
-  asm volatile(
-      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %1, 0;\n\t@q ld.global.u16 %0, [%2];\n\t@!q ld.global.b32 %0, [%3];\n\t}"
-      : "=r"(r)
-      : "r"(uint32_t(bf16)), "l"(b + 2 * i), "l"(b + 4 * i));
-  return r;
-}
-
 // ---- hand-over flags between the phases of the persistent launch (global memory)
 constexpr uint32_t kFlagSpins = 1u << 24;  // bounded: ~10 s of polling at most
 // wait until *flag >= target (acquire at GPU scope)

@@ -225,17 +225,24 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a_in, ProjPa
   } else {
     // ============================================================ compute warps
     uint32_t ph_lift = 0, ph_mma = 0;
-    float nb[2] = {0.f, 0.f}, nd[2] = {1.f, 1.f};  // gates of the coming chunk (warp 0)
-    if (warp == 0) {
+    // gates of the coming chunk (warp 0), as raw bits: converting at the load would make the warp wait
+    // for it there, and the next chunk's gates are only used a chunk later
+    const bool gate_bf = a.gate_dtype == KDN_DTYPE_BF16;
+    uint32_t nb[2] = {0u, 0u}, nd[2] = {0x3f800000u, 0x3f800000u};
+    auto load_gates = [&](int64_t t_first) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int64_t tt = 2 * lane + e;
+        const int64_t tt = t_first + 2 * lane + e;
+        nb[e] = 0u;
+        nd[e] = 0x3f800000u;  // 1.0f
         if (tt < a.T) {
-          nb[e] = ld_as_f32(a.beta, a.gate_dtype, n * a.T + tt);
-          if (decayed) nd[e] = ld_as_f32(a.decay, a.gate_dtype, n * a.T + tt);
+          nb[e] = ld_gate_bits(a.beta, gate_bf, n * a.T + tt);
+          if (decayed) nd[e] = ld_gate_bits(a.decay, gate_bf, n * a.T + tt);
         }
       }
-    }
+    };
+    auto gate_f32 = [&](uint32_t bits) { return __uint_as_float(gate_bf ? bits << 16 : bits); };
+    if (warp == 0) load_gates(0);
     for (int c = 0; c < a.NC; ++c) {
       const int64_t t0 = int64_t(c) * kC;
       const bool has_next = c + 1 < a.NC;
@@ -247,8 +254,8 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a_in, ProjPa
       if (lane == 0) tc::mbar_arrive(bar_xin);
       tc::named_bar_sync(1, kComputeThreads);  // v rows copied by other threads are visible
       if (warp == 0) {  // gates: beta, inclusive scan of log clamp(decay, 1e-5, 1), derived factors
-        const float lg0 = decayed ? logf(fminf(fmaxf(nd[0], 1e-5f), 1.0f)) : 0.f;
-        const float lg1 = decayed ? logf(fminf(fmaxf(nd[1], 1e-5f), 1.0f)) : 0.f;
+        const float lg0 = decayed ? logf(fminf(fmaxf(gate_f32(nd[0]), 1e-5f), 1.0f)) : 0.f;
+        const float lg1 = decayed ? logf(fminf(fmaxf(gate_f32(nd[1]), 1e-5f), 1.0f)) : 0.f;
         float s = lg0 + lg1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -260,24 +267,15 @@ __global__ void __launch_bounds__(kThr, 1) prefill_tc_kernel(TcArgs a_in, ProjPa
         const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
         gl[2 * lane] = g0;
         gl[2 * lane + 1] = g1;
-        bt[2 * lane] = nb[0];
-        bt[2 * lane + 1] = nb[1];
+        bt[2 * lane] = gate_f32(nb[0]);
+        bt[2 * lane + 1] = gate_f32(nb[1]);
         eg[2 * lane] = __expf(g0);
         eg[2 * lane + 1] = __expf(g1);
         egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
         egp[2 * lane + 1] = __expf(g0);
         wdec[2 * lane] = __expf(gend - g0);
         wdec[2 * lane + 1] = __expf(gend - g1);
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int64_t tt = t0 + kC + 2 * lane + e;
-          nb[e] = 0.f;
-          nd[e] = 1.f;
-          if (has_next && tt < a.T) {
-            nb[e] = ld_as_f32(a.beta, a.gate_dtype, n * a.T + tt);
-            if (decayed) nd[e] = ld_as_f32(a.decay, a.gate_dtype, n * a.T + tt);
-          }
-        }
+        if (has_next) load_gates(t0 + kC);
       }
 
       // -------------------------------------------- slice loop
