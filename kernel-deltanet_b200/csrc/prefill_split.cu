@@ -126,42 +126,53 @@ __device__ __forceinline__ void publish_store(uint32_t* flag, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
 }
 // ================================================================ phase 1
-constexpr int kP1Warps = 16;  // compute warps, 4 per TMEM lane quarter
-constexpr int kP1Threads = 32 * kP1Warps;
-constexpr int kP1Issuer = kP1Warps;         // issues every MMA (lane 0)
-constexpr int kP1Publisher = kP1Warps + 1;  // copies the record out and publishes it (lane 0)
+// The preparation runs two chunks at once on every CTA: 8 lift warps take the features of chunk
+// r + 1 (TMEM -> cosines -> fp16 tiles, MUFU-bound) while 8 algebra warps finish chunk r (scales,
+// A, Aq, T = (I + A)^-1, the operand of U and U's copy-out: latency-bound CUDA-core work), so the two
+// kinds of work overlap instead of taking turns.  One thread issues every MMA and one copies the
+// record out; both poll their barriers and serve whichever side is ready.
+constexpr int kP1Warps = 16;                  // compute warps
+constexpr int kP1Lift = 8;                    // warps 0..7: lift warps, 2 per TMEM lane quarter
+constexpr int kP1Alg = 8;                     // warps 8..15: algebra warps, 2 per TMEM lane quarter
+constexpr int kP1AlgThreads = 32 * kP1Alg;
+constexpr int kP1Issuer = kP1Warps;           // issues every MMA (lane 0)
+constexpr int kP1Publisher = kP1Warps + 1;    // copies the record out and publishes it (lane 0)
 constexpr int kP1Thr = 32 * (kP1Warps + 2);
+constexpr uint32_t kPollLimit = 1u << 28;     // polls of the issuer / publisher without progress
 
 // TMEM columns (phase 1)
 constexpr uint32_t P1_Z = 0;     // lift results, 2 x 128 cols (slices s at 128 (s & 1))
-constexpr uint32_t P1_GP = 256;  // [G; P], 64 cols
-constexpr uint32_t P1_U = 320;   // U in lanes 64..127, 64 cols (apart from the lift slots, so that the
-                                 // next chunk's first lifts can run during this chunk's algebra)
+constexpr uint32_t P1_GP = 256;  // [G; P] of chunk r at 64 (r & 1), 2 x 64 cols
+constexpr uint32_t P1_U = 384;   // U in lanes 64..127, 64 cols
 
 // shared memory (phase 1)
 constexpr uint32_t P1_OMG = 0;        // 64 KiB Omega (bf16)
 constexpr uint32_t P1_XIN = 65536;    // 16 KiB [k; q] (bf16, K-major)
-constexpr uint32_t P1_F = 81920;      // 32 KiB slice features [U_k; U_q] of even slices | algebra: A (f32),
-                                      //        then the U staging tile
+constexpr uint32_t P1_F = 81920;      // 32 KiB slice features [U_k; U_q] of even slices
 constexpr uint32_t P1_AQ = 114688;    // 8 KiB  Aq (fp16, K-major SW128), copied to the record
 constexpr uint32_t P1_VEC = 122880;   // 1 KiB  per-token factors of the state pass, copied to the record
 constexpr uint32_t P1_F1 = 124928;    // 32 KiB slice features of odd slices (two buffers: a slice's
                                       //        features are written while the previous slice's Gram
                                       //        product and copy-out still read the other buffer)
-constexpr uint32_t P1_ES = 157696;    // 17 KiB T = (I + A)^-1 (fp32), rows kEsLd floats apart
+constexpr uint32_t P1_ES = 157696;    // 17 KiB T = (I + A)^-1 (fp32), rows kEsLd floats apart; between
+                                      //        chunks, the next chunk's v rows
 constexpr int kEsLd = 68;             // padded row: the row-wise float4 reads of 8 rows hit distinct banks
-constexpr uint32_t P1_VB = 180224;    // 8 KiB  V (fp16, MN-major), B operand of U
-constexpr uint32_t P1_TOP = 188416;   // 16 KiB [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major)
+constexpr uint32_t P1_VB = 180224;    // 8 KiB  V (fp16, MN-major), B operand of U; then U's value
+                                      //        columns 0..31 (fp32 [64][32]), copied to the record
+constexpr uint32_t P1_TOP = 188416;   // 16 KiB A (fp32, sx layout) during the inverse; then the A operand
+                                      //        [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major),
+                                      //        whose second half then takes U's value columns 32..63
 constexpr uint32_t P1_US = 208896;    // 4 KiB  forward-substitution scratch
 constexpr uint32_t P1_PH = 212992;    // 2 KiB  phase b[512]
 constexpr uint32_t P1_GL = 215040;    // 5 x 256 B gates: g, beta, exp(g), exp(g_{i-1}), exp(g_{C-1} - g)
 constexpr uint32_t P1_SSP = 216320;   // 2 KiB  sums of squares per column quarter
 constexpr uint32_t P1_SC = 218368;    // 512 B  token scales
-constexpr uint32_t P1_BAR = 218880;   // mbarriers + TMEM address
-constexpr uint32_t kP1Bars = 144;      // bytes of barriers
+constexpr uint32_t P1_BAR = 218880;   // mbarriers
+constexpr uint32_t kP1Bars = 256;     // bytes of barriers
 constexpr uint32_t P1_FK = 219136;    // 256 B  beta exp(g) s_k per token: the column factors of T'
 constexpr uint32_t kP1Smem = P1_FK + 256 + 1024;
-static_assert(P1_VEC + 1024 <= P1_F1 && P1_F1 + 32768 <= P1_ES && P1_ES + 64 * kEsLd * 4 <= P1_VB,
+static_assert(P1_VEC + 1024 <= P1_F1 && P1_F1 + 32768 <= P1_ES && P1_ES + 64 * kEsLd * 4 <= P1_VB &&
+                  P1_BAR + kP1Bars <= P1_FK,
               "phase-1 shared-memory regions overlap");
 
 __device__ __forceinline__ uint32_t p1_fbuf(int s) { return (s & 1) ? P1_F1 : P1_F; }  // slice s's features
@@ -169,10 +180,11 @@ __device__ __forceinline__ uint32_t p1_fbuf(int s) { return (s & 1) ? P1_F1 : P1
 // Level d of the blocked inverse T = (I + A)^-1 (16x16 blocks, T row-major in Es with rows kEsLd apart,
 // A in the float4-swizzled layout of sx()): for the blocks I - J = d,
 //   P = sum_{K=J}^{I-1} A_IK T_KJ  (into US),  then  T_IJ = -T_II P.
+// gtid = 0..255, the algebra warps' thread index.
 template <int D>
-__device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, int tid) {
+__device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, int gtid) {
   constexpr int kElems = (4 - D) * 256;
-  for (int e = tid; e < kElems; e += kP1Threads) {
+  for (int e = gtid; e < kElems; e += kP1AlgThreads) {
     const int J = e >> 8, I = J + D, r = (e >> 4) & 15, cc = e & 15;
     const int row = 16 * I + r;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -187,8 +199,8 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
     }
     US[e] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
-  tc::named_bar_sync(1, kP1Threads);
-  for (int e = tid; e < kElems; e += kP1Threads) {
+  tc::named_bar_sync(1, kP1AlgThreads);
+  for (int e = gtid; e < kElems; e += kP1AlgThreads) {
     const int J = e >> 8, I = J + D, r = (e >> 4) & 15, cc = e & 15;
     const float* trow_ = Es + (16 * I + r) * kEsLd + 16 * I;
     const float* pcol = US + (J << 8) + cc;
@@ -202,17 +214,31 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
     }
     Es[(16 * I + r) * kEsLd + 16 * J + cc] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
   }
-  tc::named_bar_sync(1, kP1Threads);
+  tc::named_bar_sync(1, kP1AlgThreads);
 }
 
-// Phase 1 on CTAs cta = 0..ncta-1 (576 threads: 16 compute warps, an MMA issuer and a record
-// publisher; `tmem` = 512 allocated columns).  With rec_ready, each finished record is
-// published there (1) for the state pass.
+// Polling loops of the issuer and the publisher: `poll` counts rounds without progress and gives up
+// (setting the abort word) after kPollLimit of them, or at once when another wait has given up.
+__device__ __forceinline__ bool poll_on(uint32_t& poll, bool progressed, uint32_t* abort) {
+  if (progressed) {
+    poll = 0;
+    return true;
+  }
+  if ((++poll & 1023u) == 0 && (poll >= kPollLimit || aborted(abort))) {
+    set_abort(abort);
+    return false;
+  }
+  return true;
+}
+
+// Phase 1 on CTAs cta = 0..ncta-1 (576 threads: 8 lift warps, 8 algebra warps, an MMA issuer and a
+// record publisher; `tmem` = 512 allocated columns).  Chunk records idx = cta, cta + ncta, ...  With
+// rec_ready, each finished record is published there (1) for the state pass.
 __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams& P, uint8_t* sm, uint32_t tmem,
                                           int64_t cta, int64_t ncta, uint32_t* rec_ready, bool& ok) {
   const TcArgs& a = sa.a;
   const uint32_t sbase = tc::smem_u32(sm);
-  float* Am = reinterpret_cast<float*>(sm + P1_F);
+  float* Am = reinterpret_cast<float*>(sm + P1_TOP);
   float* Es = reinterpret_cast<float*>(sm + P1_ES);
   float* US = reinterpret_cast<float*>(sm + P1_US);
   float* ph = reinterpret_cast<float*>(sm + P1_PH);
@@ -224,156 +250,274 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   float* ssp = reinterpret_cast<float*>(sm + P1_SSP);
   float* sc = reinterpret_cast<float*>(sm + P1_SC);
   float* fk = reinterpret_cast<float*>(sm + P1_FK);
-  uint64_t* bar_lift = reinterpret_cast<uint64_t*>(sm + P1_BAR + 80);  // [2] lift into slot s & 1 done
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(sm + P1_BAR + 8);
-  uint64_t* bar_xin = reinterpret_cast<uint64_t*>(sm + P1_BAR + 16);
-  uint64_t* bar_zfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 96);  // [2] slot s & 1 read by all warps
-  uint64_t* bar_fready = reinterpret_cast<uint64_t*>(sm + P1_BAR + 112);  // [2] features of a slice written to
-                                                                          //     buffer s & 1 (16 warps)
-  uint64_t* bar_ops = reinterpret_cast<uint64_t*>(sm + P1_BAR + 40);
-  uint64_t* bar_wdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 48);   // U staged
-  uint64_t* bar_stfree = reinterpret_cast<uint64_t*>(sm + P1_BAR + 64);  // staged tiles copied out
-  uint64_t* bar_fdone = reinterpret_cast<uint64_t*>(sm + P1_BAR + 128);  // [2] the Gram product of the slice
-                                                                          //     in buffer s & 1 done and its
-                                                                          //     features copied out (2 arrivals)
-  uint64_t* bar_gram = reinterpret_cast<uint64_t*>(sm + P1_BAR + 24);    // the last slice's Gram product done
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P1_BAR);
+  uint64_t* bar_lift = bars;         // [2] lift into Z slot s & 1 done (MMA commit)
+  uint64_t* bar_zfree = bars + 2;    // [2] Z slot s & 1 read (8 lift warps)
+  uint64_t* bar_fready = bars + 4;   // [2] a slice's features written to buffer s & 1 (8 lift warps)
+  uint64_t* bar_fdone = bars + 6;    // [2] that slice's Gram product done and its features copied out
+                                     //     (MMA commit + publisher)
+  uint64_t* bar_gram = bars + 8;     // [2] chunk r's last Gram product into GP buffer r & 1 done
+  uint64_t* bar_xin = bars + 10;     // the next chunk's [k; q] tile in place (8 lift warps)
+  uint64_t* bar_ssp = bars + 11;     // a chunk's sums of squares written (8 lift warps)
+  uint64_t* bar_gpfree = bars + 12;  // a chunk's [G; P] and sums of squares read (8 algebra warps)
+  uint64_t* bar_ops = bars + 13;     // the operands of U in place (8 algebra warps)
+  uint64_t* bar_mma = bars + 14;     // U done (MMA commit)
+  uint64_t* bar_wdone = bars + 15;   // U staged for the copy-out (8 algebra warps)
+  uint64_t* bar_stfree = bars + 16;  // the chunk's staged tiles copied out (publisher)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, cq = (warp >> 2) & 3;
+  const int quarter = warp & 3, wh = (warp >> 2) & 1;  // TMEM lane quarter; which of the quarter's 2 warps
   const int trow = quarter * 32 + lane;
   const uint32_t lane_off = uint32_t(quarter * 32) << 16;
   const bool bf_in = a.in_dtype == KDN_DTYPE_BF16;
   const bool decayed = a.decay != nullptr;
   const int64_t N = sa.N;
   const int64_t total = N * a.NC;
+  const int64_t nrec = cta < total ? (total - 1 - cta) / ncta + 1 : 0;  // this CTA's chunk records
 
   if (tid == 0) {
-    tc::mbar_init(&bar_lift[0], 1);
-    tc::mbar_init(&bar_lift[1], 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&bar_lift[b], 1);
+      tc::mbar_init(&bar_zfree[b], kP1Lift);
+      tc::mbar_init(&bar_fready[b], kP1Lift);
+      tc::mbar_init(&bar_fdone[b], 2);
+      tc::mbar_init(&bar_gram[b], 1);
+    }
+    tc::mbar_init(bar_xin, kP1Lift);
+    tc::mbar_init(bar_ssp, kP1Lift);
+    tc::mbar_init(bar_gpfree, kP1Alg);
+    tc::mbar_init(bar_ops, kP1Alg);
     tc::mbar_init(bar_mma, 1);
-    tc::mbar_init(bar_xin, kP1Warps);
-    tc::mbar_init(&bar_zfree[0], kP1Warps);
-    tc::mbar_init(&bar_zfree[1], kP1Warps);
-    tc::mbar_init(&bar_fready[0], kP1Warps);
-    tc::mbar_init(&bar_fready[1], kP1Warps);
-    tc::mbar_init(bar_ops, kP1Warps);
-    tc::mbar_init(bar_wdone, kP1Warps);
+    tc::mbar_init(bar_wdone, kP1Alg);
     tc::mbar_init(bar_stfree, 1);
-    tc::mbar_init(&bar_fdone[0], 2);
-    tc::mbar_init(&bar_fdone[1], 2);
-    tc::mbar_init(bar_gram, 1);
     tc::fence_mbar_init();
   }
   build_omega(sm + P1_OMG, P, warp, lane, kP1Thr / 32);
   for (int i = tid; i < kD; i += kP1Thr) ph[i] = P.phase[i];
-  if (warp < kP1Warps && bf_in && cta < total)
-    prefetch_kq(a, int64_t(cta) % N, int(int64_t(cta) / N), sbase + P1_XIN, tid);
-  tc::cp_async_commit();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
   if (warp == kP1Issuer) {
     // ================================================================ MMA issuer
+    // Three in-order programs, served as their operands arrive: the lifts (chunk rl, slice sl), the
+    // Gram products (rg, sg) and the U products (ru).
     if (lane == 0) {
       const uint32_t id_lift = tc::idesc_bf16_f32(128, 128, false, false);
       const uint32_t id_gp = tc::idesc_f16_f32(128, 64, false, false);
       const uint32_t id_n64 = tc::idesc_f16_f32(128, 64, false, true);
-      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0;  // p_zfree, p_fready: phase bits per slot
-      auto lift = [&](int s) {  // Z slot s & 1 = [k; q] Omega_s^T
-#pragma unroll
-        for (int k0 = 0; k0 < 64; k0 += 16)
-          tc::mma_ss(tmem + P1_Z + 128 * (s & 1), tc::smem_desc_sw128(sbase + P1_XIN + 2 * k0, 16, 1024),
-                     tc::smem_desc_sw128(sbase + P1_OMG + s * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
-        tc::mma_commit(&bar_lift[s & 1]);
-      };
-      auto first_lifts = [&]() {  // slices 0 and 1 of the chunk whose inputs the compute warps announce
-        ok &= split_wait(bar_xin, p_xin, sa.abort);
-        p_xin ^= 1;
-        tc::fence_after_sync();
-        lift(0);
-        lift(1);
-      };
-      if (cta < total) first_lifts();
-      for (int64_t idx = cta; idx < total; idx += ncta) {
-        for (int s = 0; s < kSlices; ++s) {
-          ok &= split_wait_bit(&bar_zfree[s & 1], p_zfree, s & 1, sa.abort);  // slot s & 1 read by all
+      uint32_t p_xin = 0, p_zfree = 0, p_fready = 0, p_ops = 0;  // p_zfree, p_fready: bits per slot
+      int64_t kl = 0, kg = 0, ku = 0;                             // items issued of each program
+      const int64_t nl = 4 * nrec;
+      uint32_t poll = 0;
+      while (ok && (kl < nl || kg < nl || ku < nrec)) {
+        bool progressed = false;
+        if (ku < nrec && tc::mbar_test_wait(bar_ops, p_ops)) {  // U = T diag(beta) V in lanes 64..127
+          p_ops ^= 1;
           tc::fence_after_sync();
-          if (s + 2 < kSlices) lift(s + 2);
-          ok &= split_wait_bit(&bar_fready[s & 1], p_fready, s & 1, sa.abort);
-          tc::fence_after_sync();
-          const uint32_t fb = sbase + p1_fbuf(s);
 #pragma unroll
-          for (int k0 = 0; k0 < 128; k0 += 16) {
-            const uint64_t fd = tc::smem_desc_sw128(fb + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
-            tc::mma_ss(tmem + P1_GP, fd, fd, id_gp, s > 0 || k0 > 0);
-          }
-          tc::mma_commit(&bar_fdone[s & 1]);  // the buffer is rewritten once the publisher has copied it out too
-          if (s == kSlices - 1) tc::mma_commit(bar_gram);
+          for (int k0 = 0; k0 < 64; k0 += 16)
+            tc::mma_ss(tmem + P1_U, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
+                       tc::smem_desc_sw128(sbase + P1_VB + 128 * k0, 8192, 1024), id_n64, k0 > 0);
+          tc::mma_commit(bar_mma);
+          ++ku;
+          progressed = true;
         }
-        // every slot of this chunk has been read: the next chunk's first lifts run during this
-        // chunk's algebra (its inputs are announced by the compute warps mid-algebra)
-        if (idx + ncta < total) first_lifts();
-        ok &= split_wait(bar_ops, p_ops, sa.abort);
-        p_ops ^= 1;
-        tc::fence_after_sync();
+        if (kg < nl) {  // [G; P] += F_s F_s^T over the slice's features (rows 0..63 of F are U_k)
+          const int sg = int(kg & 3), b = sg & 1;
+          if (tc::mbar_test_wait(&bar_fready[b], (p_fready >> b) & 1u)) {
+            p_fready ^= 1u << b;
+            tc::fence_after_sync();
+            const uint32_t gp = tmem + P1_GP + 64 * uint32_t((kg >> 2) & 1);
+            const uint32_t fb = sbase + p1_fbuf(sg);
 #pragma unroll
-        for (int k0 = 0; k0 < 64; k0 += 16)  // U = T diag(beta) V in lanes 64..127
-          tc::mma_ss(tmem + P1_U, tc::smem_desc_sw128(sbase + P1_TOP + 2 * k0, 16, 1024),
-                     tc::smem_desc_sw128(sbase + P1_VB + 128 * k0, 8192, 1024), id_n64, k0 > 0);
-        tc::mma_commit(bar_mma);
+            for (int k0 = 0; k0 < 128; k0 += 16) {
+              const uint64_t fd = tc::smem_desc_sw128(fb + (k0 >> 6) * 16384 + 2 * (k0 & 63), 16, 1024);
+              tc::mma_ss(gp, fd, fd, id_gp, sg > 0 || k0 > 0);
+            }
+            tc::mma_commit(&bar_fdone[b]);  // the buffer is rewritten once the publisher has copied it out too
+            if (sg == 3) tc::mma_commit(&bar_gram[(kg >> 2) & 1]);
+            ++kg;
+            progressed = true;
+          }
+        }
+        if (kl < nl) {  // Z slot sl & 1 = [k; q] Omega_sl^T
+          const int sl = int(kl & 3), b = sl & 1;
+          // slices 0, 1 need the chunk's input tile; every use of a slot but its first needs the
+          // slot's previous contents read
+          bool ready = true;
+          if (sl == 0) ready = tc::mbar_test_wait(bar_xin, p_xin);
+          if (ready && kl >= 2) ready = tc::mbar_test_wait(&bar_zfree[b], (p_zfree >> b) & 1u);
+          if (ready) {
+            if (sl == 0) p_xin ^= 1;
+            if (kl >= 2) p_zfree ^= 1u << b;
+            tc::fence_after_sync();
+#pragma unroll
+            for (int k0 = 0; k0 < 64; k0 += 16)
+              tc::mma_ss(tmem + P1_Z + 128 * b, tc::smem_desc_sw128(sbase + P1_XIN + 2 * k0, 16, 1024),
+                         tc::smem_desc_sw128(sbase + P1_OMG + sl * 16384 + 2 * k0, 16, 1024), id_lift, k0 > 0);
+            tc::mma_commit(&bar_lift[b]);
+            ++kl;
+            progressed = true;
+          }
+        }
+        ok &= poll_on(poll, progressed, sa.abort);
       }
     }
     __syncwarp();
   } else if (warp == kP1Publisher) {
     // ================================================================ record copies, publication
+    // Two in-order programs: the slices' features (as soon as written) and each chunk's remaining
+    // tiles (once staged, and only after the chunk's feature copies were issued).
     if (lane == 0) {
-      uint32_t p_fready = 0, p_wdone = 0;  // p_fready: phase bits per buffer
-      for (int64_t idx = cta; idx < total; idx += ncta) {
-        uint8_t* rec = record(sa, idx / N, idx % N);
-        for (int s = 0; s < kSlices; ++s) {
-          // the slice's features: U_q (rows 64..127) as K-blocks 2s, 2s+1 and U_k (rows 0..63) as slice s
-          ok &= split_wait_bit(&bar_fready[s & 1], p_fready, s & 1, sa.abort);
-          const uint32_t fb = sbase + p1_fbuf(s);
-          for (int kb = 0; kb < 2; ++kb) {
-            tc::bulk_store(rec + REC_Q + (2 * s + kb) * 8192, fb + kb * 16384 + 8192, 8192);
-            tc::bulk_store(rec + REC_UK + s * 16384 + kb * 8192, fb + kb * 16384, 8192);
+      uint32_t p_fready = 0, p_wdone = 0;  // p_fready: bits per buffer
+      int64_t kf = 0, kt = 0;
+      const int64_t nf = 4 * nrec;
+      uint32_t poll = 0;
+      while (ok && (kf < nf || kt < nrec)) {
+        bool progressed = false;
+        if (kf < nf) {
+          const int s = int(kf & 3), b = s & 1;
+          if (tc::mbar_test_wait(&bar_fready[b], (p_fready >> b) & 1u)) {
+            p_fready ^= 1u << b;
+            const int64_t idx = cta + (kf >> 2) * ncta;
+            uint8_t* rec = record(sa, idx / N, idx % N);
+            // the slice's features: U_q (rows 64..127) as K-blocks 2s, 2s+1 and U_k (rows 0..63) as slice s
+            const uint32_t fb = sbase + p1_fbuf(s);
+            for (int kb = 0; kb < 2; ++kb) {
+              tc::bulk_store(rec + REC_Q + (2 * s + kb) * 8192, fb + kb * 16384 + 8192, 8192);
+              tc::bulk_store(rec + REC_UK + s * 16384 + kb * 8192, fb + kb * 16384, 8192);
+            }
+            tc::bulk_commit();
+            tc::bulk_wait_read();
+            tc::mbar_arrive(&bar_fdone[b]);
+            ++kf;
+            progressed = true;
           }
+        }
+        if (kt < nrec && kf >= 4 * (kt + 1) && tc::mbar_test_wait(bar_wdone, p_wdone)) {
+          p_wdone ^= 1;
+          const int64_t idx = cta + kt * ncta;
+          uint8_t* rec = record(sa, idx / N, idx % N);
+          // T' (rows 0..63 of the U product's A operand), U (two column halves), Aq and the factors
+          tc::bulk_store(rec + REC_TP, sbase + P1_TOP, 8192);
+          tc::bulk_store(rec + REC_U, sbase + P1_VB, 8192);
+          tc::bulk_store(rec + REC_U + 8192, sbase + P1_TOP + 8192, 8192);
+          tc::bulk_store(rec + REC_AQ, sbase + P1_AQ, 8192);
+          tc::bulk_store(rec + REC_VEC, sbase + P1_VEC, 1024);
           tc::bulk_commit();
           tc::bulk_wait_read();
-          tc::mbar_arrive(&bar_fdone[s & 1]);
+          tc::mbar_arrive(bar_stfree);  // the staging tiles take the next chunk
+          if (rec_ready) {              // every byte of the record came through this thread's copies
+            tc::bulk_wait_all();
+            publish_store(rec_ready + idx, 1u);
+          }
+          ++kt;
+          progressed = true;
         }
-        // T' (rows 0..63 of the U product's A operand), U, Aq and the factors
-        ok &= split_wait(bar_wdone, p_wdone, sa.abort);
-        p_wdone ^= 1;
-        tc::bulk_store(rec + REC_TP, sbase + P1_TOP, 8192);
-        tc::bulk_store(rec + REC_U, sbase + P1_F, 16384);
-        tc::bulk_store(rec + REC_AQ, sbase + P1_AQ, 8192);
-        tc::bulk_store(rec + REC_VEC, sbase + P1_VEC, 1024);
-        tc::bulk_commit();
-        tc::bulk_wait_read();
-        tc::mbar_arrive(bar_stfree);  // the staging tiles take the next chunk
-        if (rec_ready) {              // every byte of the record came through this thread's copies
-          tc::bulk_wait_all();
-          publish_store(rec_ready + idx, 1u);
-        }
+        ok &= poll_on(poll, progressed, sa.abort);
       }
       tc::bulk_wait_all();
     }
     __syncwarp();
-  } else if (warp < kP1Warps) {
-    // ================================================================ compute warps
-    uint32_t ph_lift = 0, ph_mma = 0, ph_st = 0, ph_fd = 0, ph_gram = 0;
-    auto wait_mma = [&]() {
-      ok &= split_wait(bar_mma, ph_mma, sa.abort);
-      ph_mma ^= 1;
-      tc::fence_after_sync();
+  } else if (warp < kP1Lift) {
+    // ================================================================ lift warps
+    // warp (quarter, wh): rows 32 quarter .. +31 of [k; q], columns 64 wh .. +63 of each slice, as two
+    // 32-column groups cc (column quarter 2 wh + cc of the slice)
+    uint32_t ph_lift = 0, ph_fd = 0, ph_gpf = 0;  // ph_lift, ph_fd: bits per slot / buffer
+    auto load_inputs = [&](int64_t idx) {  // the chunk's [k; q] tile (all 256 lift threads)
+      const int64_t n = idx % N, c = idx / N;
+      for (int t2 = tid; t2 < 512; t2 += 32 * kP1Lift) {
+        if (bf_in) prefetch_kq(a, n, int(c), sbase + P1_XIN, t2);
+        else load_kq_f32(a, n, int(c), sm + P1_XIN, t2);
+      }
+      tc::cp_async_commit();
     };
-    // gates of the coming chunk (warp 0), as raw bits: converting at the load would make the warp wait
-    // for it there; the next chunk's gates are only used a chunk later
+    auto announce_inputs = [&]() {
+      tc::cp_async_wait_all();
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_xin);
+    };
+    if (nrec > 0) {
+      load_inputs(cta);
+      announce_inputs();
+    }
+    for (int64_t r = 0; r < nrec; ++r) {
+      const int64_t idx = cta + r * ncta;
+      const bool has_next = r + 1 < nrec;
+      float ss0 = 0.f, ss1 = 0.f;  // sums of squares of column groups cc = 0, 1
+#pragma unroll 1
+      for (int s = 0; s < kSlices; ++s) {
+        ok &= split_wait_bit(&bar_lift[s & 1], ph_lift, s & 1, sa.abort);
+        tc::fence_after_sync();
+        if (s == kSlices - 1 && has_next) load_inputs(idx + ncta);  // every lift of the chunk is done
+        uint8_t* fb = sm + p1_fbuf(s) + wh * 16384;
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          float z[32];
+          tc::tmem_ld32(tmem + lane_off + P1_Z + 128 * (s & 1) + 64 * wh + 32 * cc, z);
+          tc::tmem_ld_wait();
+          if (cc == 1) {  // the slot is read: the issuer may lift slice s + 2 into it
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bar_zfree[s & 1]);
+          }
+          // u = cos(tau_inv z + b); the hardware cosine's ~1e-6 absolute error is far
+          // below the fp16 spacing of the stored features for the |arguments| <= 32 here
+          uint32_t fp[16];
+          const float4* phs = reinterpret_cast<const float4*>(ph + 128 * s + 64 * wh + 32 * cc);
+          float acc = cc ? ss1 : ss0;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 b4 = phs[j >> 2];
+            const float u0 = __cosf(fmaf(z[j], P.tau_inv, b4.x));
+            const float u1 = __cosf(fmaf(z[j + 1], P.tau_inv, b4.y));
+            const float u2 = __cosf(fmaf(z[j + 2], P.tau_inv, b4.z));
+            const float u3 = __cosf(fmaf(z[j + 3], P.tau_inv, b4.w));
+            acc = fmaf(u0, u0, fmaf(u1, u1, fmaf(u2, u2, fmaf(u3, u3, acc))));
+            fp[j >> 1] = pack_f16(u0, u1);
+            fp[(j >> 1) + 1] = pack_f16(u2, u3);
+          }
+          if (cc) ss1 = acc;
+          else ss0 = acc;
+          if (cc == 0 && (s >= 2 || r > 0)) {  // the buffer's previous slice: Gram product and copy-out done
+            ok &= split_wait_bit(&bar_fdone[s & 1], ph_fd, s & 1, sa.abort);
+            tc::fence_after_sync();
+          }
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
+            *reinterpret_cast<uint4*>(fb + tc::sw128_offset(trow, 32 * cc + 8 * c8)) = pk;
+          }
+        }
+        tc::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bar_fready[s & 1]);
+      }
+      if (has_next) announce_inputs();  // the next chunk's first lifts may start
+      // the sums of squares, once the algebra warps have read the previous chunk's
+      if (r > 0) {
+        ok &= split_wait(bar_gpfree, ph_gpf, sa.abort);
+        ph_gpf ^= 1;
+      }
+      ssp[(2 * wh) * 128 + trow] = ss0;
+      ssp[(2 * wh + 1) * 128 + trow] = ss1;
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_ssp);
+    }
+  } else if (warp < kP1Warps) {
+    // ================================================================ algebra warps
+    // warp (quarter, wh): row trow of [k; q], columns 32 wh .. +31 of the 64 x 64 chunk matrices
+    const int gtid = tid - 32 * kP1Lift;
+    uint32_t ph_ssp = 0, ph_gram = 0, ph_mma = 0, ph_st = 0;  // ph_gram: bits per GP buffer
+    // gates of the coming chunk (warp 8) as raw bits: converting at the load would make the warp wait
+    // for it there, and they are only used a chunk later
     const bool gate_bf = a.gate_dtype == KDN_DTYPE_BF16;
     uint32_t nb[2] = {0u, 0u}, nd[2] = {0x3f800000u, 0x3f800000u};
-    auto load_gates = [&](int64_t n_, int64_t c_) {
+    auto load_gates = [&](int64_t idx) {
+      const int64_t n_ = idx % N, c_ = idx / N;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int64_t tt = c_ * kC + 2 * lane + e;
@@ -386,281 +530,203 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       }
     };
     auto gate_f32 = [&](uint32_t bits) { return __uint_as_float(gate_bf ? bits << 16 : bits); };
-    // warp 0: the gates of the chunk whose raw gates nb, nd hold: beta, the inclusive scan of
-    // log clamp(decay, 1e-5, 1) and the derived factors
-    auto compute_gates = [&]() {
-      const float lg0 = decayed ? logf(fminf(fmaxf(gate_f32(nd[0]), 1e-5f), 1.0f)) : 0.f;
-      const float lg1 = decayed ? logf(fminf(fmaxf(gate_f32(nd[1]), 1e-5f), 1.0f)) : 0.f;
-      float s = lg0 + lg1;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, s, o);
-        if (lane >= o) s += y;
-      }
-      const float g0 = s - lg1, g1 = s;
-      const float gend = __shfl_sync(0xffffffffu, s, 31);
-      const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
-      gl[2 * lane] = g0;
-      gl[2 * lane + 1] = g1;
-      bt[2 * lane] = gate_f32(nb[0]);
-      bt[2 * lane + 1] = gate_f32(nb[1]);
-      eg[2 * lane] = __expf(g0);
-      eg[2 * lane + 1] = __expf(g1);
-      egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
-      egp[2 * lane + 1] = __expf(g0);
-      wdec[2 * lane] = __expf(gend - g0);
-      wdec[2 * lane + 1] = __expf(gend - g1);
-    };
-    if (warp == 0 && cta < total) load_gates(int64_t(cta) % N, int64_t(cta) / N);
-    // v of chunk (n_, c_) into the T staging area Es (free from the end of one chunk's algebra to the
-    // next chunk's T): thread tid copies row tid / 8, values 8 (tid % 8) .. +7 (zeros past the end), and
+    // v of chunk idx into the staging area Es (free from one chunk's operand of U to the next chunk's
+    // inverse): thread gtid copies row gtid / 4, values 16 (gtid % 4) .. +15 (zeros past the end), and
     // later reads back only what it copied itself
-    auto prefetch_v = [&](int64_t n_, int64_t c_) {
-      const int row = tid >> 3, cc = tid & 7;
+    auto prefetch_v = [&](int64_t idx) {
+      const int64_t n_ = idx % N, c_ = idx / N;
+      const int row = gtid >> 2, cc = gtid & 3;
       const int64_t t = c_ * kC + row;
       const bool in = t < a.T;
-      if (bf_in) {
-        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.v) + (in ? (n_ * a.T + t) * kDV + 8 * cc : 0);
-        tc::cp_async16(sbase + P1_ES + row * 128 + 16 * cc, src, in ? 16 : 0);
-      } else {
-        const float* src = reinterpret_cast<const float*>(a.v) + (in ? (n_ * a.T + t) * kDV + 8 * cc : 0);
-        tc::cp_async16(sbase + P1_ES + row * 256 + 32 * cc, src, in ? 16 : 0);
-        tc::cp_async16(sbase + P1_ES + row * 256 + 32 * cc + 16, src + 4, in ? 16 : 0);
-      }
+      const int es = bf_in ? 2 : 4;
+      const char* src = reinterpret_cast<const char*>(a.v) + (in ? ((n_ * a.T + t) * kDV + 16 * cc) * es : 0);
+      const uint32_t dst = sbase + P1_ES + row * 64 * es + 16 * cc * es;
+      for (int o = 0; o < 16 * es; o += 16) tc::cp_async16(dst + o, src + (in ? o : 0), in ? 16 : 0);
       tc::cp_async_commit();
     };
-    for (int64_t idx = cta; idx < total; idx += ncta) {
-      const int64_t n = idx % N, c = idx / N;
-      const int64_t nidx = idx + ncta;
-      const bool has_next = nidx < total;
-      const int64_t nn = nidx % N, ncn = nidx / N;
-      // ---------------------------------------- chunk inputs -> lifts of slices 0, 1 (the first chunk;
-      // later chunks' inputs are announced during the previous chunk's algebra)
-      if (idx == cta) {
-        tc::cp_async_wait_all();
-        if (!bf_in) load_kq_f32(a, n, int(c), sm + P1_XIN, tid);
-        tc::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(bar_xin);
-        prefetch_v(n, c);  // later chunks' v is fetched during the previous chunk's products
-      }
-      if (warp == 0 && idx == cta) {  // later chunks' gates are formed during the previous chunk's U product
-        compute_gates();
-        if (has_next) load_gates(nn, ncn);
-      }
-
-      // ---------------------------------------- slice loop: features, Gram products
-      float ss = 0.f;
-#pragma unroll 1
-      for (int s = 0; s < kSlices; ++s) {
-        ok &= split_wait_bit(&bar_lift[s & 1], ph_lift, s & 1, sa.abort);
-        tc::fence_after_sync();
-        float z[32];
-        tc::tmem_ld32(tmem + lane_off + P1_Z + 128 * (s & 1) + 32 * cq, z);
-        tc::tmem_ld_wait();
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bar_zfree[s & 1]);
-        // u = cos(tau_inv z + b); the hardware cosine's ~1e-6 absolute error is far
-        // below the fp16 spacing of the stored features for the |arguments| <= 32 here
-        uint32_t fp[16];
-        const float4* phs = reinterpret_cast<const float4*>(ph + 128 * s + 32 * cq);
+    if (nrec > 0) {
+      prefetch_v(cta);
+      if (warp == kP1Lift) load_gates(cta);
+    }
+    for (int64_t r = 0; r < nrec; ++r) {
+      const int64_t idx = cta + r * ncta;
+      const bool has_next = r + 1 < nrec;
+      if (warp == kP1Lift) {  // gates: beta, inclusive scan of log clamp(decay, 1e-5, 1), derived factors
+        const float lg0 = decayed ? logf(fminf(fmaxf(gate_f32(nd[0]), 1e-5f), 1.0f)) : 0.f;
+        const float lg1 = decayed ? logf(fminf(fmaxf(gate_f32(nd[1]), 1e-5f), 1.0f)) : 0.f;
+        float s = lg0 + lg1;
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 b4 = phs[j >> 2];
-          const float u0 = __cosf(fmaf(z[j], P.tau_inv, b4.x));
-          const float u1 = __cosf(fmaf(z[j + 1], P.tau_inv, b4.y));
-          const float u2 = __cosf(fmaf(z[j + 2], P.tau_inv, b4.z));
-          const float u3 = __cosf(fmaf(z[j + 3], P.tau_inv, b4.w));
-          ss = fmaf(u0, u0, fmaf(u1, u1, fmaf(u2, u2, fmaf(u3, u3, ss))));
-          fp[j >> 1] = pack_f16(u0, u1);
-          fp[(j >> 1) + 1] = pack_f16(u2, u3);
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, s, o);
+          if (lane >= o) s += y;
         }
-        if (s >= 2) {  // slice s - 2's Gram product and copy-out are done with buffer s & 1
-          ok &= split_wait_bit(&bar_fdone[s & 1], ph_fd, s & 1, sa.abort);
-          tc::fence_after_sync();
-        } else if (s == 0 && idx != cta) {  // the previous chunk's staged tiles (buffer 0) have been copied out
-          ok &= split_wait(bar_stfree, ph_st, sa.abort);
-          ph_st ^= 1;
-        } else if (s == 1 && idx != cta) {  // the previous chunk's last slice (buffer 1) has been copied out
-          ok &= split_wait_bit(&bar_fdone[1], ph_fd, 1, sa.abort);
-          tc::fence_after_sync();
-        }
-        {
-          const int kb = cq >> 1, e0 = 32 * (cq & 1);
-          uint8_t* fb = sm + p1_fbuf(s) + kb * 16384;
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            const uint4 pk = make_uint4(fp[4 * c8], fp[4 * c8 + 1], fp[4 * c8 + 2], fp[4 * c8 + 3]);
-            const uint32_t off = tc::sw128_offset(trow, e0 + 8 * c8);
-            *reinterpret_cast<uint4*>(fb + off) = pk;
-          }
-        }
-        tc::fence_proxy_async_smem();
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bar_fready[s & 1]);
+        const float g0 = s - lg1, g1 = s;
+        const float gend = __shfl_sync(0xffffffffu, s, 31);
+        const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
+        gl[2 * lane] = g0;
+        gl[2 * lane + 1] = g1;
+        bt[2 * lane] = gate_f32(nb[0]);
+        bt[2 * lane + 1] = gate_f32(nb[1]);
+        eg[2 * lane] = __expf(g0);
+        eg[2 * lane + 1] = __expf(g1);
+        egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
+        egp[2 * lane + 1] = __expf(g0);
+        wdec[2 * lane] = __expf(gend - g0);
+        wdec[2 * lane + 1] = __expf(gend - g1);
+        if (has_next) load_gates(idx + ncta);
       }
-      ssp[cq * 128 + trow] = ss;
-      // every lift of this chunk has completed: the input tile takes the next chunk (announced to the
-      // issuer during the algebra below)
-      if (has_next) {
-        if (bf_in) prefetch_kq(a, nn, int(ncn), sbase + P1_XIN, tid);
-        else load_kq_f32(a, nn, int(ncn), sm + P1_XIN, tid);
-      }
-      tc::cp_async_commit();
-      // the Gram products of the last two slices, and the copy-out of slice kSlices - 2 (buffer 0 takes
-      // the algebra's A next); the last slice's copy-out is awaited before the next chunk rewrites buffer 1
-      ok &= split_wait_bit(&bar_fdone[0], ph_fd, 0, sa.abort);
-      ok &= split_wait(bar_gram, ph_gram, sa.abort);
-      ph_gram ^= 1;
+      // ---------------------------------------- the chunk's sums of squares and [G; P]
+      ok &= split_wait(bar_ssp, ph_ssp, sa.abort);
+      ph_ssp ^= 1;
+      ok &= split_wait_bit(&bar_gram[r & 1], ph_gram, int(r & 1), sa.abort);
       tc::fence_after_sync();
-
-      // ---------------------------------------- chunk matrices
-      float gp[16];
-      tc::tmem_ld16(tmem + lane_off + P1_GP + 16 * cq, gp);
+      float gp[32];
+      tc::tmem_ld32(tmem + lane_off + P1_GP + 64 * uint32_t(r & 1) + 32 * wh, gp);
       tc::tmem_ld_wait();
-      tc::named_bar_sync(1, kP1Threads);  // sums of squares and gates visible
-      if (tid < 128)
-        sc[tid] = P.amp / (P.amp * sqrtf(ssp[tid] + ssp[128 + tid] + ssp[256 + tid] + ssp[384 + tid]) + 1e-8f);
-      tc::named_bar_sync(1, kP1Threads);
+      if (gtid < 128)
+        sc[gtid] =
+            P.amp / (P.amp * sqrtf(ssp[gtid] + ssp[128 + gtid] + ssp[256 + gtid] + ssp[384 + gtid]) + 1e-8f);
+      tc::fence_before_sync();
+      tc::named_bar_sync(1, kP1AlgThreads);  // scales and gates visible; sums of squares read
+      if (lane == 0) tc::mbar_arrive(bar_gpfree);
+      if (r > 0) {  // the previous chunk's staged tiles (Aq, factors, V / U, A operand) have been copied out
+        ok &= split_wait(bar_stfree, ph_st, sa.abort);
+        ph_st ^= 1;
+      }
       {
         const int i = trow & 63;
         const float si = sc[trow];
         if (trow < 64) {  // k row: A_ij = beta_i exp(g_i - g_j) s_i s_j G_ij, j < i
           const float bi = bt[i], gi = gl[i];
 #pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4) {
+          for (int j4 = 0; j4 < 8; ++j4) {
             float4 av;
             float* ap = &av.x;
 #pragma unroll
             for (int qx = 0; qx < 4; ++qx) {
-              const int jj = 4 * j4 + qx, j = 16 * cq + jj;
+              const int jj = 4 * j4 + qx, j = 32 * wh + jj;
               const float dec = decayed ? __expf(gi - gl[j]) : 1.f;
               ap[qx] = (j < i) ? bi * dec * gp[jj] * si * sc[j] : 0.f;
             }
-            *reinterpret_cast<float4*>(Am + sx(i, 16 * cq + 4 * j4)) = av;
+            *reinterpret_cast<float4*>(Am + sx(i, 32 * wh + 4 * j4)) = av;
           }
         } else {  // q row: Aq_ij = exp(g_{i-1} - g_j) s_qi s_kj P_ij, j < i (fp16 into the record)
           const float gp_i = i > 0 ? gl[i - 1] : 0.f;
-          float aq[16];
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = 16 * cq + jj;
-            const float dec = decayed ? __expf(gp_i - gl[j]) : 1.f;
-            aq[jj] = (j < i) ? dec * gp[jj] * si * sc[j] : 0.f;
+          for (int h = 0; h < 4; ++h) {
+            float aq[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              const int j = 32 * wh + 8 * h + jj;
+              const float dec = decayed ? __expf(gp_i - gl[j]) : 1.f;
+              aq[jj] = (j < i) ? dec * gp[8 * h + jj] * si * sc[j] : 0.f;
+            }
+            *reinterpret_cast<uint4*>(sm + P1_AQ + tc::sw128_offset(i, 32 * wh + 8 * h)) =
+                make_uint4(pack_f16_sat(aq[0], aq[1]), pack_f16_sat(aq[2], aq[3]), pack_f16_sat(aq[4], aq[5]),
+                           pack_f16_sat(aq[6], aq[7]));
           }
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-            *reinterpret_cast<uint4*>(sm + P1_AQ + tc::sw128_offset(i, 16 * cq + 8 * h)) = make_uint4(
-                pack_f16_sat(aq[8 * h], aq[8 * h + 1]), pack_f16_sat(aq[8 * h + 2], aq[8 * h + 3]),
-                pack_f16_sat(aq[8 * h + 4], aq[8 * h + 5]), pack_f16_sat(aq[8 * h + 6], aq[8 * h + 7]));
         }
       }
-      {  // per-token factors of the state pass, and V (fp16) as the B operand of U
+      {  // per-token factors of the state pass, the column factors of T', and V (fp16) as the B operand of U
         float* vec = reinterpret_cast<float*>(sm + P1_VEC);
-        if (tid < 64) vec[tid] = wdec[tid] * sc[tid];
-        else if (tid < 128) vec[tid] = sc[tid] * egp[tid - 64];
-        else if (tid == 128) vec[128] = eg[63];
-        else if (tid >= 256 && tid < 320) fk[tid - 256] = bt[tid - 256] * eg[tid - 256] * sc[tid - 256];
-        const int row = tid >> 3, cc = tid & 7;
-        // this thread's v values (the group committed after them is the next chunk's k, q prefetch)
-        tc::cp_async_wait_group<1>();
-        float vreg[8];
+        if (gtid < 64) vec[gtid] = wdec[gtid] * sc[gtid];
+        else if (gtid < 128) vec[gtid] = sc[gtid] * egp[gtid - 64];
+        else if (gtid == 128) vec[128] = eg[63];
+        else if (gtid >= 192) fk[gtid - 192] = bt[gtid - 192] * eg[gtid - 192] * sc[gtid - 192];
+        const int row = gtid >> 2, cc = gtid & 3;
+        tc::cp_async_wait_all();  // this thread's v values
+        float vreg[16];
         if (bf_in) {
-          const uint4 w = *reinterpret_cast<const uint4*>(sm + P1_ES + row * 128 + 16 * cc);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(h[j]);
-            vreg[2 * j] = f.x;
-            vreg[2 * j + 1] = f.y;
+          for (int h = 0; h < 2; ++h) {
+            const uint4 w = *reinterpret_cast<const uint4*>(sm + P1_ES + row * 128 + 32 * cc + 16 * h);
+            const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(hp[j]);
+              vreg[8 * h + 2 * j] = f.x;
+              vreg[8 * h + 2 * j + 1] = f.y;
+            }
           }
         } else {
-          const float4 x0 = *reinterpret_cast<const float4*>(sm + P1_ES + row * 256 + 32 * cc);
-          const float4 x1 = *reinterpret_cast<const float4*>(sm + P1_ES + row * 256 + 32 * cc + 16);
-          vreg[0] = x0.x, vreg[1] = x0.y, vreg[2] = x0.z, vreg[3] = x0.w;
-          vreg[4] = x1.x, vreg[5] = x1.y, vreg[6] = x1.z, vreg[7] = x1.w;
-        }
-        *reinterpret_cast<uint4*>(sm + P1_VB + tc::sw128_offset(row, 8 * cc)) =
-            make_uint4(pack_f16_sat(vreg[0], vreg[1]), pack_f16_sat(vreg[2], vreg[3]), pack_f16_sat(vreg[4], vreg[5]),
-                       pack_f16_sat(vreg[6], vreg[7]));
-      }
-      tc::named_bar_sync(1, kP1Threads);
-      // T = (I + A)^-1 (fp32, row-major in Es), with 16x16 blocks T_IJ:
-      // (a) diagonal blocks by forward substitution, one thread per column (warps 0..3,
-      //     lanes 0..15), everything above the diagonal zero;
-      if (warp < 4 && lane < 16) {
-        const int I = warp, j = lane;
-        float tcol[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          float sacc = (r == j) ? 1.f : 0.f;
-#pragma unroll
-          for (int kk = 0; kk < r; ++kk) sacc = fmaf(-Am[sx(16 * I + r, 16 * I + kk)], tcol[kk], sacc);
-          tcol[r] = (r >= j) ? sacc : 0.f;
-        }
-#pragma unroll
-        for (int r = 0; r < 16; ++r) Es[(16 * I + r) * kEsLd + 16 * I + j] = tcol[r];
-      }
-      for (int e = tid; e < 64 * 64; e += kP1Threads) {  // zeros off the diagonal blocks (lower ones are
-        const int r = e >> 6, cc = e & 63;               // overwritten below)
-        if ((r >> 4) != (cc >> 4)) Es[r * kEsLd + cc] = 0.f;
-      }
-      tc::named_bar_sync(1, kP1Threads);
-      // (b) off-diagonal blocks level by level (d = I - J = 1, 2, 3), all threads
-      t_level<1>(Am, Es, US, tid);
-      t_level<2>(Am, Es, US, tid);
-      t_level<3>(Am, Es, US, tid);
-      if (has_next) {  // the next chunk's inputs are in place: its first lifts may start
-        tc::cp_async_wait_all();
-        tc::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(bar_xin);
-      }
-      // A operand [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major, 128 x 64)
-      {
-        const int r = tid >> 2, jq = tid & 3, i = r & 63;
-        const float* colf = r < 64 ? fk : bt;
-        float w[16];
-#pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(Es + i * kEsLd + 16 * jq + 4 * j4);
-          const float4 f4 = *reinterpret_cast<const float4*>(colf + 16 * jq + 4 * j4);
-          w[4 * j4] = t4.x * f4.x;
-          w[4 * j4 + 1] = t4.y * f4.y;
-          w[4 * j4 + 2] = t4.z * f4.z;
-          w[4 * j4 + 3] = t4.w * f4.w;
+          for (int m = 0; m < 4; ++m) {
+            const float4 x = *reinterpret_cast<const float4*>(sm + P1_ES + row * 256 + 64 * cc + 16 * m);
+            vreg[4 * m] = x.x, vreg[4 * m + 1] = x.y, vreg[4 * m + 2] = x.z, vreg[4 * m + 3] = x.w;
+          }
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          *reinterpret_cast<uint4*>(sm + P1_TOP + tc::sw128_offset(r, 16 * jq + 8 * h)) =
-              make_uint4(pack_f16_sat(w[8 * h], w[8 * h + 1]), pack_f16_sat(w[8 * h + 2], w[8 * h + 3]),
-                         pack_f16_sat(w[8 * h + 4], w[8 * h + 5]), pack_f16_sat(w[8 * h + 6], w[8 * h + 7]));
+          *reinterpret_cast<uint4*>(sm + P1_VB + tc::sw128_offset(row, 16 * cc + 8 * h)) =
+              make_uint4(pack_f16_sat(vreg[8 * h], vreg[8 * h + 1]), pack_f16_sat(vreg[8 * h + 2], vreg[8 * h + 3]),
+                         pack_f16_sat(vreg[8 * h + 4], vreg[8 * h + 5]),
+                         pack_f16_sat(vreg[8 * h + 6], vreg[8 * h + 7]));
+      }
+      tc::named_bar_sync(1, kP1AlgThreads);
+      // T = (I + A)^-1 (fp32, row-major in Es), with 16x16 blocks T_IJ:
+      // (a) diagonal blocks by forward substitution, one thread per column (the first 4 algebra warps,
+      //     lanes 0..15), everything above the diagonal zero;
+      if (warp < kP1Lift + 4 && lane < 16) {
+        const int I = warp - kP1Lift, j = lane;
+        float tcol[16];
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+          float sacc = (rr == j) ? 1.f : 0.f;
+#pragma unroll
+          for (int kk = 0; kk < rr; ++kk) sacc = fmaf(-Am[sx(16 * I + rr, 16 * I + kk)], tcol[kk], sacc);
+          tcol[rr] = (rr >= j) ? sacc : 0.f;
+        }
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) Es[(16 * I + rr) * kEsLd + 16 * I + j] = tcol[rr];
+      }
+      for (int e = gtid; e < 64 * 64; e += kP1AlgThreads) {  // zeros off the diagonal blocks (lower ones are
+        const int rr = e >> 6, cc = e & 63;                  // overwritten below)
+        if ((rr >> 4) != (cc >> 4)) Es[rr * kEsLd + cc] = 0.f;
+      }
+      tc::named_bar_sync(1, kP1AlgThreads);
+      // (b) off-diagonal blocks level by level (d = I - J = 1, 2, 3)
+      t_level<1>(Am, Es, US, gtid);
+      t_level<2>(Am, Es, US, gtid);
+      t_level<3>(Am, Es, US, gtid);
+      // A operand [T diag(beta exp(g) s_k); T diag(beta)] (fp16, K-major, 128 x 64) over A, which is no
+      // longer read
+      {
+        const int rr = gtid >> 1, jh = gtid & 1, i = rr & 63;
+        const float* colf = rr < 64 ? fk : bt;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float w[8];
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const float4 t4 = *reinterpret_cast<const float4*>(Es + i * kEsLd + 32 * jh + 8 * h + 4 * m);
+            const float4 f4 = *reinterpret_cast<const float4*>(colf + 32 * jh + 8 * h + 4 * m);
+            w[4 * m] = t4.x * f4.x;
+            w[4 * m + 1] = t4.y * f4.y;
+            w[4 * m + 2] = t4.z * f4.z;
+            w[4 * m + 3] = t4.w * f4.w;
+          }
+          *reinterpret_cast<uint4*>(sm + P1_TOP + tc::sw128_offset(rr, 32 * jh + 8 * h)) =
+              make_uint4(pack_f16_sat(w[0], w[1]), pack_f16_sat(w[2], w[3]), pack_f16_sat(w[4], w[5]),
+                         pack_f16_sat(w[6], w[7]));
+        }
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      tc::named_bar_sync(1, kP1Threads);  // also: gates, scales and Es of this chunk no longer read
+      tc::named_bar_sync(1, kP1AlgThreads);  // also: gates, scales and Es of this chunk no longer read
       if (lane == 0) tc::mbar_arrive(bar_ops);
-      if (has_next) {
-        prefetch_v(nn, ncn);
-        if (warp == 0) {  // this chunk's gates are no longer read: the next chunk's take their place
-          compute_gates();
-          const int64_t n2 = nidx + ncta;
-          if (n2 < total) load_gates(n2 % N, n2 / N);
-        }
-      }
-      wait_mma();  // U
-
-      // ---------------------------------------- U -> staging tile (F), copied out by the issuer
+      if (has_next) prefetch_v(idx + ncta);
+      ok &= split_wait(bar_mma, ph_mma, sa.abort);  // U
+      ph_mma ^= 1;
+      tc::fence_after_sync();
+      // ---------------------------------------- U -> staging tiles (value columns 32 wh .. +31: VB for
+      // the first half, the A operand's second half for the other), copied out by the publisher
       if (trow >= 64) {
-        float u[16];
-        tc::tmem_ld16(tmem + lane_off + P1_U + 16 * cq, u);
+        float u[32];
+        tc::tmem_ld32(tmem + lane_off + P1_U + 32 * wh, u);
         tc::tmem_ld_wait();
-        float4* dst =
-            reinterpret_cast<float4*>(sm + P1_F + (cq >> 1) * 8192 + ((trow - 64) * 32 + 16 * (cq & 1)) * 4);
+        float4* dst = reinterpret_cast<float4*>(sm + (wh ? P1_TOP + 8192 : P1_VB) + (trow - 64) * 128);
 #pragma unroll
-        for (int m = 0; m < 4; ++m) dst[m] = make_float4(u[4 * m], u[4 * m + 1], u[4 * m + 2], u[4 * m + 3]);
+        for (int m = 0; m < 8; ++m) dst[m] = make_float4(u[4 * m], u[4 * m + 1], u[4 * m + 2], u[4 * m + 3]);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
