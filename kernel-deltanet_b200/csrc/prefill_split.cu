@@ -157,6 +157,8 @@ constexpr uint32_t P1_F1 = 124928;    // 32 KiB slice features of odd slices (tw
 constexpr uint32_t P1_ES = 157696;    // 17 KiB T = (I + A)^-1 (fp32), rows kEsLd floats apart; between
                                       //        chunks, the next chunk's v rows
 constexpr int kEsLd = 68;             // padded row: the row-wise float4 reads of 8 rows hit distinct banks
+constexpr uint32_t P1_GL = 175104;    // 3 x 1280 B gates of chunk r at 1280 (r % 3): g, beta, exp(g),
+                                      //        exp(g_{i-1}), exp(g_{C-1} - g), 256 B each
 constexpr uint32_t P1_VB = 180224;    // 8 KiB  V (fp16, MN-major), B operand of U; then U's value
                                       //        columns 0..31 (fp32 [64][32]), copied to the record
 constexpr uint32_t P1_TOP = 188416;   // 16 KiB A (fp32, sx layout) during the inverse; then the A operand
@@ -164,14 +166,14 @@ constexpr uint32_t P1_TOP = 188416;   // 16 KiB A (fp32, sx layout) during the i
                                       //        whose second half then takes U's value columns 32..63
 constexpr uint32_t P1_US = 208896;    // 4 KiB  forward-substitution scratch
 constexpr uint32_t P1_PH = 212992;    // 2 KiB  phase b[512]
-constexpr uint32_t P1_GL = 215040;    // 5 x 256 B gates: g, beta, exp(g), exp(g_{i-1}), exp(g_{C-1} - g)
 constexpr uint32_t P1_SSP = 216320;   // 2 KiB  sums of squares per column quarter
 constexpr uint32_t P1_SC = 218368;    // 512 B  token scales
 constexpr uint32_t P1_BAR = 218880;   // mbarriers
 constexpr uint32_t kP1Bars = 256;     // bytes of barriers
 constexpr uint32_t P1_FK = 219136;    // 256 B  beta exp(g) s_k per token: the column factors of T'
 constexpr uint32_t kP1Smem = P1_FK + 256 + 1024;
-static_assert(P1_VEC + 1024 <= P1_F1 && P1_F1 + 32768 <= P1_ES && P1_ES + 64 * kEsLd * 4 <= P1_VB &&
+static_assert(P1_VEC + 1024 <= P1_F1 && P1_F1 + 32768 <= P1_ES && P1_ES + 64 * kEsLd * 4 <= P1_GL &&
+                  P1_GL + 3 * 1280 <= P1_VB &&
                   P1_BAR + kP1Bars <= P1_FK,
               "phase-1 shared-memory regions overlap");
 
@@ -183,8 +185,11 @@ __device__ __forceinline__ uint32_t p1_fbuf(int s) { return (s & 1) ? P1_F1 : P1
 // gtid = 0..255, the algebra warps' thread index.
 template <int D>
 __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, int gtid) {
-  constexpr int kElems = (4 - D) * 256;
-  for (int e = gtid; e < kElems; e += kP1AlgThreads) {
+  constexpr int kIters = 4 - D;  // (4 - D) * 256 block elements over 256 threads
+  static_assert(kP1AlgThreads == 256, "one block element per thread and block");
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int e = gtid + 256 * it;
     const int J = e >> 8, I = J + D, r = (e >> 4) & 15, cc = e & 15;
     const int row = 16 * I + r;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -200,7 +205,9 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
     US[e] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
   tc::named_bar_sync(1, kP1AlgThreads);
-  for (int e = gtid; e < kElems; e += kP1AlgThreads) {
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int e = gtid + 256 * it;
     const int J = e >> 8, I = J + D, r = (e >> 4) & 15, cc = e & 15;
     const float* trow_ = Es + (16 * I + r) * kEsLd + 16 * I;
     const float* pcol = US + (J << 8) + cc;
@@ -242,11 +249,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   float* Es = reinterpret_cast<float*>(sm + P1_ES);
   float* US = reinterpret_cast<float*>(sm + P1_US);
   float* ph = reinterpret_cast<float*>(sm + P1_PH);
-  float* gl = reinterpret_cast<float*>(sm + P1_GL);
-  float* bt = gl + 64;
-  float* eg = gl + 128;
-  float* egp = gl + 192;
-  float* wdec = gl + 256;
+  float* gates = reinterpret_cast<float*>(sm + P1_GL);  // chunk r's at 320 (r % 3) floats
   float* ssp = reinterpret_cast<float*>(sm + P1_SSP);
   float* sc = reinterpret_cast<float*>(sm + P1_SC);
   float* fk = reinterpret_cast<float*>(sm + P1_FK);
@@ -368,10 +371,17 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
   } else if (warp == kP1Publisher) {
     // ================================================================ record copies, publication
     // Two in-order programs: the slices' features (as soon as written) and each chunk's remaining
-    // tiles (once staged, and only after the chunk's feature copies were issued).
+    // tiles (once staged, and only after the chunk's feature copies were issued).  A slice's buffer is
+    // handed back once its copy has read it, which is checked when the next copy is issued (the lift
+    // warps rewrite it two slices later), so that this thread seldom waits on a copy.
     if (lane == 0) {
       uint32_t p_fready = 0, p_wdone = 0;  // p_fready: bits per buffer
       int64_t kf = 0, kt = 0;
+      int pend = -1;  // buffer of the last feature copy, not yet handed back
+      auto hand_back = [&]() {  // every copy issued so far has read its source
+        if (pend >= 0) tc::mbar_arrive(&bar_fdone[pend]);
+        pend = -1;
+      };
       const int64_t nf = 4 * nrec;
       uint32_t poll = 0;
       while (ok && (kf < nf || kt < nrec)) {
@@ -389,8 +399,9 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
               tc::bulk_store(rec + REC_UK + s * 16384 + kb * 8192, fb + kb * 16384, 8192);
             }
             tc::bulk_commit();
-            tc::bulk_wait_read();
-            tc::mbar_arrive(&bar_fdone[b]);
+            tc::bulk_wait_read_but1();  // the copies before this one have read their buffers
+            if (pend >= 0) tc::mbar_arrive(&bar_fdone[pend]);
+            pend = b;
             ++kf;
             progressed = true;
           }
@@ -407,6 +418,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
           tc::bulk_store(rec + REC_VEC, sbase + P1_VEC, 1024);
           tc::bulk_commit();
           tc::bulk_wait_read();
+          hand_back();
           tc::mbar_arrive(bar_stfree);  // the staging tiles take the next chunk
           if (rec_ready) {              // every byte of the record came through this thread's copies
             tc::bulk_wait_all();
@@ -418,6 +430,7 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
         ok &= poll_on(poll, progressed, sa.abort);
       }
       tc::bulk_wait_all();
+      hand_back();
     }
     __syncwarp();
   } else if (warp < kP1Lift) {
@@ -439,13 +452,59 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_xin);
     };
+    // gates of the coming chunk (warp 0) as raw bits: converting at the load would make the warp wait
+    // for it there, and they are only used a chunk later
+    const bool gate_bf = a.gate_dtype == KDN_DTYPE_BF16;
+    uint32_t nb[2] = {0u, 0u}, nd[2] = {0x3f800000u, 0x3f800000u};
+    auto load_gates = [&](int64_t idx) {
+      const int64_t n_ = idx % N, c_ = idx / N;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int64_t tt = c_ * kC + 2 * lane + e;
+        nb[e] = 0u;
+        nd[e] = 0x3f800000u;  // 1.0f
+        if (tt < a.T) {
+          nb[e] = ld_gate_bits(a.beta, gate_bf, n_ * a.T + tt);
+          if (decayed) nd[e] = ld_gate_bits(a.decay, gate_bf, n_ * a.T + tt);
+        }
+      }
+    };
+    auto gate_f32 = [&](uint32_t bits) { return __uint_as_float(gate_bf ? bits << 16 : bits); };
     if (nrec > 0) {
+      if (warp == 0) load_gates(cta);
       load_inputs(cta);
       announce_inputs();
     }
     for (int64_t r = 0; r < nrec; ++r) {
       const int64_t idx = cta + r * ncta;
       const bool has_next = r + 1 < nrec;
+      if (warp == 0) {  // the chunk's gates: beta, inclusive scan of log clamp(decay, 1e-5, 1), derived
+        // factors.  Buffer r % 3: the algebra warps are on chunk r - 1 at the latest (the sums of
+        // squares of chunk r - 1 were written after they had read chunk r - 2's)
+        float* gl = gates + 320 * int(r % 3);
+        const float lg0 = decayed ? logf(fminf(fmaxf(gate_f32(nd[0]), 1e-5f), 1.0f)) : 0.f;
+        const float lg1 = decayed ? logf(fminf(fmaxf(gate_f32(nd[1]), 1e-5f), 1.0f)) : 0.f;
+        float sg = lg0 + lg1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, sg, o);
+          if (lane >= o) sg += y;
+        }
+        const float g0 = sg - lg1, g1 = sg;
+        const float gend = __shfl_sync(0xffffffffu, sg, 31);
+        const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
+        gl[2 * lane] = g0;
+        gl[2 * lane + 1] = g1;
+        gl[64 + 2 * lane] = gate_f32(nb[0]);
+        gl[64 + 2 * lane + 1] = gate_f32(nb[1]);
+        gl[128 + 2 * lane] = __expf(g0);
+        gl[128 + 2 * lane + 1] = __expf(g1);
+        gl[192 + 2 * lane] = lane == 0 ? 1.f : __expf(gprev);
+        gl[192 + 2 * lane + 1] = __expf(g0);
+        gl[256 + 2 * lane] = __expf(gend - g0);
+        gl[256 + 2 * lane + 1] = __expf(gend - g1);
+        if (has_next) load_gates(idx + ncta);
+      }
       float ss0 = 0.f, ss1 = 0.f;  // sums of squares of column groups cc = 0, 1
 #pragma unroll 1
       for (int s = 0; s < kSlices; ++s) {
@@ -512,24 +571,6 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
     // warp (quarter, wh): row trow of [k; q], columns 32 wh .. +31 of the 64 x 64 chunk matrices
     const int gtid = tid - 32 * kP1Lift;
     uint32_t ph_ssp = 0, ph_gram = 0, ph_mma = 0, ph_st = 0;  // ph_gram: bits per GP buffer
-    // gates of the coming chunk (warp 8) as raw bits: converting at the load would make the warp wait
-    // for it there, and they are only used a chunk later
-    const bool gate_bf = a.gate_dtype == KDN_DTYPE_BF16;
-    uint32_t nb[2] = {0u, 0u}, nd[2] = {0x3f800000u, 0x3f800000u};
-    auto load_gates = [&](int64_t idx) {
-      const int64_t n_ = idx % N, c_ = idx / N;
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int64_t tt = c_ * kC + 2 * lane + e;
-        nb[e] = 0u;
-        nd[e] = 0x3f800000u;  // 1.0f
-        if (tt < a.T) {
-          nb[e] = ld_gate_bits(a.beta, gate_bf, n_ * a.T + tt);
-          if (decayed) nd[e] = ld_gate_bits(a.decay, gate_bf, n_ * a.T + tt);
-        }
-      }
-    };
-    auto gate_f32 = [&](uint32_t bits) { return __uint_as_float(gate_bf ? bits << 16 : bits); };
     // v of chunk idx into the staging area Es (free from one chunk's operand of U to the next chunk's
     // inverse): thread gtid copies row gtid / 4, values 16 (gtid % 4) .. +15 (zeros past the end), and
     // later reads back only what it copied itself
@@ -544,37 +585,15 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       for (int o = 0; o < 16 * es; o += 16) tc::cp_async16(dst + o, src + (in ? o : 0), in ? 16 : 0);
       tc::cp_async_commit();
     };
-    if (nrec > 0) {
-      prefetch_v(cta);
-      if (warp == kP1Lift) load_gates(cta);
-    }
+    if (nrec > 0) prefetch_v(cta);
     for (int64_t r = 0; r < nrec; ++r) {
       const int64_t idx = cta + r * ncta;
       const bool has_next = r + 1 < nrec;
-      if (warp == kP1Lift) {  // gates: beta, inclusive scan of log clamp(decay, 1e-5, 1), derived factors
-        const float lg0 = decayed ? logf(fminf(fmaxf(gate_f32(nd[0]), 1e-5f), 1.0f)) : 0.f;
-        const float lg1 = decayed ? logf(fminf(fmaxf(gate_f32(nd[1]), 1e-5f), 1.0f)) : 0.f;
-        float s = lg0 + lg1;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float y = __shfl_up_sync(0xffffffffu, s, o);
-          if (lane >= o) s += y;
-        }
-        const float g0 = s - lg1, g1 = s;
-        const float gend = __shfl_sync(0xffffffffu, s, 31);
-        const float gprev = __shfl_up_sync(0xffffffffu, g1, 1);
-        gl[2 * lane] = g0;
-        gl[2 * lane + 1] = g1;
-        bt[2 * lane] = gate_f32(nb[0]);
-        bt[2 * lane + 1] = gate_f32(nb[1]);
-        eg[2 * lane] = __expf(g0);
-        eg[2 * lane + 1] = __expf(g1);
-        egp[2 * lane] = lane == 0 ? 1.f : __expf(gprev);
-        egp[2 * lane + 1] = __expf(g0);
-        wdec[2 * lane] = __expf(gend - g0);
-        wdec[2 * lane + 1] = __expf(gend - g1);
-        if (has_next) load_gates(idx + ncta);
-      }
+      const float* gl = gates + 320 * int(r % 3);
+      const float* bt = gl + 64;
+      const float* eg = gl + 128;
+      const float* egp = gl + 192;
+      const float* wdec = gl + 256;
       // ---------------------------------------- the chunk's sums of squares and [G; P]
       ok &= split_wait(bar_ssp, ph_ssp, sa.abort);
       ph_ssp ^= 1;
@@ -589,53 +608,33 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
       tc::fence_before_sync();
       tc::named_bar_sync(1, kP1AlgThreads);  // scales and gates visible; sums of squares read
       if (lane == 0) tc::mbar_arrive(bar_gpfree);
-      if (r > 0) {  // the previous chunk's staged tiles (Aq, factors, V / U, A operand) have been copied out
-        ok &= split_wait(bar_stfree, ph_st, sa.abort);
-        ph_st ^= 1;
-      }
+      // A and Aq in registers (in place of [G; P]) and this thread's v values, then, once the previous
+      // chunk's staged tiles have been copied out, everything into shared memory
+      const int i = trow & 63;
       {
-        const int i = trow & 63;
         const float si = sc[trow];
         if (trow < 64) {  // k row: A_ij = beta_i exp(g_i - g_j) s_i s_j G_ij, j < i
           const float bi = bt[i], gi = gl[i];
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            float4 av;
-            float* ap = &av.x;
-#pragma unroll
-            for (int qx = 0; qx < 4; ++qx) {
-              const int jj = 4 * j4 + qx, j = 32 * wh + jj;
-              const float dec = decayed ? __expf(gi - gl[j]) : 1.f;
-              ap[qx] = (j < i) ? bi * dec * gp[jj] * si * sc[j] : 0.f;
-            }
-            *reinterpret_cast<float4*>(Am + sx(i, 32 * wh + 4 * j4)) = av;
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = 32 * wh + jj;
+            const float dec = decayed ? __expf(gi - gl[j]) : 1.f;
+            gp[jj] = (j < i) ? bi * dec * gp[jj] * si * sc[j] : 0.f;
           }
         } else {  // q row: Aq_ij = exp(g_{i-1} - g_j) s_qi s_kj P_ij, j < i (fp16 into the record)
           const float gp_i = i > 0 ? gl[i - 1] : 0.f;
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            float aq[8];
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-              const int j = 32 * wh + 8 * h + jj;
-              const float dec = decayed ? __expf(gp_i - gl[j]) : 1.f;
-              aq[jj] = (j < i) ? dec * gp[8 * h + jj] * si * sc[j] : 0.f;
-            }
-            *reinterpret_cast<uint4*>(sm + P1_AQ + tc::sw128_offset(i, 32 * wh + 8 * h)) =
-                make_uint4(pack_f16_sat(aq[0], aq[1]), pack_f16_sat(aq[2], aq[3]), pack_f16_sat(aq[4], aq[5]),
-                           pack_f16_sat(aq[6], aq[7]));
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = 32 * wh + jj;
+            const float dec = decayed ? __expf(gp_i - gl[j]) : 1.f;
+            gp[jj] = (j < i) ? dec * gp[jj] * si * sc[j] : 0.f;
           }
         }
       }
-      {  // per-token factors of the state pass, the column factors of T', and V (fp16) as the B operand of U
-        float* vec = reinterpret_cast<float*>(sm + P1_VEC);
-        if (gtid < 64) vec[gtid] = wdec[gtid] * sc[gtid];
-        else if (gtid < 128) vec[gtid] = sc[gtid] * egp[gtid - 64];
-        else if (gtid == 128) vec[128] = eg[63];
-        else if (gtid >= 192) fk[gtid - 192] = bt[gtid - 192] * eg[gtid - 192] * sc[gtid - 192];
-        const int row = gtid >> 2, cc = gtid & 3;
+      const int row = gtid >> 2, cc = gtid & 3;
+      float vreg[16];
+      {
         tc::cp_async_wait_all();  // this thread's v values
-        float vreg[16];
         if (bf_in) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -655,6 +654,29 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
             vreg[4 * m] = x.x, vreg[4 * m + 1] = x.y, vreg[4 * m + 2] = x.z, vreg[4 * m + 3] = x.w;
           }
         }
+      }
+      if (r > 0) {  // the previous chunk's staged tiles (Aq, factors, V / U, A operand) have been copied out
+        ok &= split_wait(bar_stfree, ph_st, sa.abort);
+        ph_st ^= 1;
+      }
+      if (trow < 64) {
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+          *reinterpret_cast<float4*>(Am + sx(i, 32 * wh + 4 * j4)) =
+              make_float4(gp[4 * j4], gp[4 * j4 + 1], gp[4 * j4 + 2], gp[4 * j4 + 3]);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          *reinterpret_cast<uint4*>(sm + P1_AQ + tc::sw128_offset(i, 32 * wh + 8 * h)) =
+              make_uint4(pack_f16_sat(gp[8 * h], gp[8 * h + 1]), pack_f16_sat(gp[8 * h + 2], gp[8 * h + 3]),
+                         pack_f16_sat(gp[8 * h + 4], gp[8 * h + 5]), pack_f16_sat(gp[8 * h + 6], gp[8 * h + 7]));
+      }
+      {  // per-token factors of the state pass, the column factors of T', and V (fp16) as the B operand of U
+        float* vec = reinterpret_cast<float*>(sm + P1_VEC);
+        if (gtid < 64) vec[gtid] = wdec[gtid] * sc[gtid];
+        else if (gtid < 128) vec[gtid] = sc[gtid] * egp[gtid - 64];
+        else if (gtid == 128) vec[128] = eg[63];
+        else if (gtid >= 192) fk[gtid - 192] = bt[gtid - 192] * eg[gtid - 192] * sc[gtid - 192];
 #pragma unroll
         for (int h = 0; h < 2; ++h)
           *reinterpret_cast<uint4*>(sm + P1_VB + tc::sw128_offset(row, 16 * cc + 8 * h)) =

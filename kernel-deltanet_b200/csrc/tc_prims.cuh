@@ -261,6 +261,8 @@ __device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t byt
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // the shared-memory sources of this thread's committed bulk stores have been read
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// the source reads of every bulk group but the most recent one are done
+__device__ __forceinline__ void bulk_wait_read_but1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // this thread's committed bulk stores are complete
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // all but the two most recently committed bulk groups of this thread are complete
