@@ -138,7 +138,7 @@ constexpr int kP1AlgThreads = 32 * kP1Alg;
 constexpr int kP1Issuer = kP1Warps;           // issues every MMA (lane 0)
 constexpr int kP1Publisher = kP1Warps + 1;    // copies the record out and publishes it (lane 0)
 constexpr int kP1Thr = 32 * (kP1Warps + 2);
-constexpr uint32_t kPollLimit = 1u << 28;     // polls of the issuer / publisher without progress
+constexpr uint32_t kPollLimit = 1u << 26;     // idle rounds of the issuer / publisher (~64 ns each)
 
 // TMEM columns (phase 1)
 constexpr uint32_t P1_Z = 0;     // lift results, 2 x 128 cols (slices s at 128 (s & 1))
@@ -225,12 +225,15 @@ __device__ __forceinline__ void t_level(const float* Am, float* Es, float* US, i
 }
 
 // Polling loops of the issuer and the publisher: `poll` counts rounds without progress and gives up
-// (setting the abort word) after kPollLimit of them, or at once when another wait has given up.
+// (setting the abort word) after kPollLimit of them, or at once when another wait has given up.  An
+// idle round sleeps briefly, so that the polling thread takes few issue slots from the compute warps
+// of its sub-partition.
 __device__ __forceinline__ bool poll_on(uint32_t& poll, bool progressed, uint32_t* abort) {
   if (progressed) {
     poll = 0;
     return true;
   }
+  __nanosleep(64);
   if ((++poll & 1023u) == 0 && (poll >= kPollLimit || aborted(abort))) {
     set_abort(abort);
     return false;
