@@ -159,13 +159,33 @@ def _copy_rows(lib, dst, src, stream):
     _lib.check(rc, "kdn_copy_rows")
 
 
+def _segment_plan(T: int, seg: int, chunk: int):
+    """Token ranges [(t0, t1)] of the streamed segments, whole chunks except the ragged end of the
+    sequence.  The middle segments are `seg` tokens long (few calls, small per-call overhead); the
+    sequence starts and ends with ramps of seg/8, seg/4 and seg/2 tokens, because the copy-in of the
+    first segment and the compute and copy-out of the last one overlap nothing."""
+    seg_c = max(1, seg // chunk)
+    n_c = (T + chunk - 1) // chunk
+    ramp = sorted({r for r in (seg_c // 8, seg_c // 4, seg_c // 2) if 1 <= r < seg_c})
+    if n_c <= 2 * sum(ramp) + seg_c:
+        sizes = [seg_c] * (n_c // seg_c) + ([n_c % seg_c] if n_c % seg_c else [])
+    else:
+        mid = n_c - 2 * sum(ramp)
+        sizes = ramp + [seg_c] * (mid // seg_c) + ([mid % seg_c] if mid % seg_c else []) + ramp[::-1]
+    plan, c0 = [], 0
+    for sz in sizes:
+        plan.append((c0 * chunk, min(T, (c0 + sz) * chunk)))
+        c0 += sz
+    return plan
+
+
 def _streamed_forward(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state, mode, dev, out, final_state,
                       segment_tokens):
     """Host tensors in, host tensors out, the work on `dev`: the sequence is cut into segments of whole
-    chunks; while segment i runs, the inputs of segment i+1 are copied in and the outputs of segment
-    i-1 are copied out (two copy streams, double-buffered device segments).  The fp32 state is
-    carried from segment to segment on the device, so the result equals one call over the whole
-    sequence (the chunks and their arithmetic are the same)."""
+    chunks (`_segment_plan`); while segment i runs, the inputs of segment i+1 are copied in and the
+    outputs of segment i-1 are copied out (two copy streams, three device segment buffers).  The fp32
+    state is carried from segment to segment on the device, so the result equals one call over the
+    whole sequence (the chunks and their arithmetic are the same)."""
     if dev.type != "cuda":
         raise RuntimeError(f"device must be a CUDA device, got {dev}")
     for t in (k, v, beta, decay, initial_state, out, final_state):
@@ -190,15 +210,19 @@ def _streamed_forward(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state
     if S_host.shape != (B, dv, D) or S_host.dtype != torch.float32 or not S_host.is_contiguous():
         raise RuntimeError("final_state must be a contiguous host float32 tensor [B, d_v, D]")
     seg = max(chunk_size, (int(segment_tokens) // chunk_size) * chunk_size)
+    plan = _segment_plan(T, seg, chunk_size)
+    seg = max([t1 - t0 for t0, t1 in plan], default=chunk_size)  # the longest segment sizes the buffers
     proj = fwht_proj  # its device constants are built per device on demand
     compute = torch.cuda.current_stream(dev)
     copy_in = torch.cuda.Stream(dev)
     copy_out = torch.cuda.Stream(dev)
+    # a segment of n tokens views the first B*n rows of its flat buffers as contiguous [B, n, ...] tensors
+    view = lambda flat, n, *tail: flat[:B * n * (tail[0] if tail else 1)].view(B, n, *tail)
     with torch.cuda.device(dev):
-        nb = 2
-        dsrc = [[torch.empty(B, seg, t.shape[-1], dtype=t.dtype, device=dev) for t in src] for _ in range(nb)]
-        dgate = [[torch.empty(B, seg, dtype=g.dtype, device=dev) for g in gates] for _ in range(nb)]
-        dy = [torch.empty(B, seg, dv, dtype=in_dtype, device=dev) for _ in range(nb)]
+        nb = 3  # three segment buffers: a short segment's copy-in never waits for the copy-out two back
+        dsrc = [[torch.empty(B * seg * t.shape[-1], dtype=t.dtype, device=dev) for t in src] for _ in range(nb)]
+        dgate = [[torch.empty(B * seg, dtype=g.dtype, device=dev) for g in gates] for _ in range(nb)]
+        dy = [torch.empty(B * seg * dv, dtype=in_dtype, device=dev) for _ in range(nb)]
         dS = [torch.empty(B, dv, D, dtype=torch.float32, device=dev) for _ in range(2)]
         if initial_state is not None:
             if initial_state.shape != (B, dv, D):
@@ -212,30 +236,25 @@ def _streamed_forward(q, k, v, beta, decay, fwht_proj, chunk_size, initial_state
         freed = [torch.cuda.Event() for _ in range(nb)]   # segment buffer i % nb may be refilled
         loaded = [torch.cuda.Event() for _ in range(nb)]
         done = [torch.cuda.Event() for _ in range(nb)]
-        nseg = (T + seg - 1) // seg
+        nseg = len(plan)
         S_prev = dS[1] if initial_state is not None else None
-        for i in range(nseg):
-            t0, t1 = i * seg, min(T, (i + 1) * seg)
+        for i, (t0, t1) in enumerate(plan):
             n = t1 - t0
             b = i % nb
+            qq, kk, vv = (view(x, n, t.shape[-1]) for x, t in zip(dsrc[b], src))
+            gg = [view(x, n) for x in dgate[b]]
+            yy = view(dy[b], n, dv)
             with torch.cuda.stream(copy_in):
                 if i >= nb:
                     copy_in.wait_event(freed[b])
-                for hs, ds in zip(src + gates, dsrc[b] + dgate[b]):  # one strided copy per tensor
+                for hs, ds in zip(src + gates, [qq, kk, vv] + gg):  # one strided copy per tensor
                     _copy_rows(lib, ds, hs[:, t0:t1], copy_in)
                 loaded[b].record(copy_in)
             compute.wait_event(loaded[b])
             S_next = dS[i % 2]
-            qq, kk, vv = (x[:, :n].contiguous() if n < seg else x for x in dsrc[b])
-            gg = [x[:, :n].contiguous() if n < seg else x for x in dgate[b]]
             dd = gg[1] if decay is not None else None
-            if n == seg:
-                yy = dy[b]
-                fused_chunked_deltanet_forward(qq, kk, vv, gg[0], dd, proj, chunk_size, S_prev, mode=mode,
-                                               workspace=ws, out=yy, final_state=S_next)
-            else:  # the last, shorter segment
-                yy, _ = fused_chunked_deltanet_forward(qq, kk, vv, gg[0], dd, proj, chunk_size, S_prev, mode=mode,
-                                                       workspace=ws, final_state=S_next)
+            fused_chunked_deltanet_forward(qq, kk, vv, gg[0], dd, proj, chunk_size, S_prev, mode=mode,
+                                           workspace=ws, out=yy, final_state=S_next)
             done[b].record(compute)
             with torch.cuda.stream(copy_out):
                 copy_out.wait_event(done[b])
