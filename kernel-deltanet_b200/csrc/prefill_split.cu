@@ -895,7 +895,9 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
   } else if (warp == kP2Issuer) {
     // ================================================================ tensor-core products
     if (lane == 0) {
-      const uint32_t id_k = tc::idesc_f16_f32(128, kHalf, false, true);  // A K-major, B MN-major
+      // Y = U_k S^T and X = T' Y have the chunk's 64 tokens as rows: M = 64 products, whose accumulator
+      // rows 16 q .. 16 q + 15 sit in TMEM lanes 32 q .. 32 q + 15
+      const uint32_t id_k = tc::idesc_f16_f32(64, kHalf, false, true);  // A K-major, B MN-major
       const uint32_t id_s = tc::idesc_f16_f32(128, kHalf, true, true);   // A MN-major (U_k^T)
       // descriptor bases; the products only add constant offsets
       const uint64_t d_ring = tc::smem_desc_sw128(sbase + P2_RING, 16, 1024);     // U_k as A (K-major)
@@ -919,8 +921,6 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
             const uint64_t b0 = tc::desc_add(db, uint32_t(j) * 4096);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              // M = 128: rows 0..63 are the chunk's tokens; rows 64..127 (the next 8 KiB) give
-              // lanes nobody reads
               tc::mma_ss(tmem + P2_Y, tc::desc_add(a0, 32 * kk), tc::desc_add(b0, 1024 * kk), id_k,
                          p > 0 || j > 0 || kk > 0);
           }
@@ -932,7 +932,7 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         tc::fence_after_sync();
         const uint64_t dt = tc::desc_add(d_tp, uint32_t(u) * 8192);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)  // K = the 64 tokens; rows 64..127 of A: unread lanes
+        for (int kk = 0; kk < 4; ++kk)  // K = the 64 tokens
           tc::mma_ss(tmem + P2_X, tc::desc_add(dt, 32 * kk), tc::desc_add(d_yb, 16 * kk * 64), id_k, kk > 0);
         tc::mma_commit(&tp_empty[u]);
         tc::mma_commit(bar_x);
@@ -984,7 +984,9 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
   } else if (warp < kP2Warps) {
     // ================================================================ compute warps
     const int quarter = warp & 3, ch = warp >> 2;  // TMEM lane quarter, 16-column half of the CTA's 32
-    const int trow = quarter * 32 + lane;
+    const int trow = quarter * 32 + lane;          // feature row of the state slices (TMEM lane)
+    const int yrow = quarter * 16 + lane;          // token row of the M = 64 products (lanes 0..15)
+    const bool ylane = lane < 16;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const int cbase = col0 + 16 * ch;  // first value column of this thread
     const bool decayed = a.decay != nullptr;
@@ -997,10 +999,10 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
     }
     tc::tmem_st_wait();
     uint32_t py = 0, px = 0, ps[2] = {0, 0}, pff = 0, pst = 0;  // pff: phase bits per slot
-    auto store_tile = [&](uint32_t off, const float* v, float w) {  // 16 values of row trow, fp16 SW64
+    auto store_tile = [&](uint32_t off, int row, const float* v, float w) {  // 16 values of a row, fp16 SW64
 #pragma unroll
       for (int m = 0; m < 2; ++m)
-        *reinterpret_cast<uint4*>(sm + off + tc::sw64_offset(trow, 16 * ch + 8 * m)) =
+        *reinterpret_cast<uint4*>(sm + off + tc::sw64_offset(row, 16 * ch + 8 * m)) =
             make_uint4(pack_f16_sat(w * v[8 * m], w * v[8 * m + 1]), pack_f16_sat(w * v[8 * m + 2], w * v[8 * m + 3]),
                        pack_f16_sat(w * v[8 * m + 4], w * v[8 * m + 5]),
                        pack_f16_sat(w * v[8 * m + 6], w * v[8 * m + 7]));
@@ -1018,14 +1020,14 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         const int u = c & 1;
         ok &= split_wait_bit(&fac_full[u], pff, u, sa.abort);
         const float* fac = reinterpret_cast<const float*>(sm + P2_FAC + u * P2_FAC_BYTES);
-        if (trow < 64) {
-          const float4* u4 = reinterpret_cast<const float4*>(fac + trow * 32 + 16 * ch);
+        if (ylane) {
+          const float4* u4 = reinterpret_cast<const float4*>(fac + yrow * 32 + 16 * ch);
 #pragma unroll
           for (int m = 0; m < 4; ++m) {
             const float4 x = u4[m];
             cu[4 * m] = x.x, cu[4 * m + 1] = x.y, cu[4 * m + 2] = x.z, cu[4 * m + 3] = x.w;
           }
-          cew = fac[2048 + trow];
+          cew = fac[2048 + yrow];
         }
         ceC = fac[2048 + 128];
         __syncwarp();
@@ -1041,7 +1043,7 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
           float v[16];
           tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p + h) + 16 * ch, v);
           tc::tmem_ld_wait();
-          store_tile(P2_SOP + (2 * p + h) * 8192, v, 1.f);
+          store_tile(P2_SOP + (2 * p + h) * 8192, trow, v, 1.f);
           if (decayed) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] *= ceC;
@@ -1053,23 +1055,25 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
       }
       // ---------------------------------------- Y (fp16) for X = T' Y
       wait_bar(bar_y, py);
-      if (trow < 64) {
+      {
         float y[16];
         tc::tmem_ld16(tmem + lane_off + P2_Y + 16 * ch, y);
         tc::tmem_ld_wait();
-        store_tile(P2_YB, y, 1.f);
+        if (ylane) store_tile(P2_YB, yrow, y, 1.f);
       }
       signal(&tp_full[c & 1]);
       // ---------------------------------------- E = U - X and E'' for the update
       wait_bar(bar_x, px);
-      if (trow < 64) {
+      {
         float x[16];
         tc::tmem_ld16(tmem + lane_off + P2_X + 16 * ch, x);
         tc::tmem_ld_wait();
+        if (ylane) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) x[j] = cu[j] - x[j];
-        store_tile(P2_ET, x, 1.f);
-        store_tile(P2_EB, x, cew);
+          for (int j = 0; j < 16; ++j) x[j] = cu[j] - x[j];
+          store_tile(P2_ET, yrow, x, 1.f);
+          store_tile(P2_EB, yrow, x, cew);
+        }
       }
       signal(bar_e);
     }
