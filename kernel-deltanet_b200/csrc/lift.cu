@@ -611,14 +611,19 @@ __global__ void __launch_bounds__(tcl2::kThreads, 1) lift_tc_bf16_kernel(const _
         if (lane == 0) tc::mbar_arrive(bar_in);
       }
       tc::named_bar_sync(1, 32 * kEpiWarps);  // every row's cosines and partial sums are in shared memory
-      // pass 2: rows 8 warp .. 8 warp + 7, each as two 512-byte stores; phi = amp cos / (amp ||cos|| + 1e-8)
+      // pass 2: rows 8 warp .. 8 warp + 7, each as two 512-byte stores; phi = amp cos / (amp ||cos|| + 1e-8).
+      // Lane k forms row 8 warp + k's scale (the norm and the quotient by the hardware reciprocal square
+      // root and reciprocal: about 1e-7 relative, far inside bf16's 2^-9) and passes it to the warp.
+      float sc_own;
+      {
+        const int r = 8 * warp + (lane & 7);
+        const float ssr = ssx[r] + ssx[128 + r] + ssx[256 + r] + ssx[384 + r];
+        sc_own = __fdividef(P.amp, fmaf(P.amp, ssr * rsqrtf(ssr), 1e-8f));
+      }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int r = 8 * warp + k;  // r & 7 == k: the swizzle below folds to constants
-        // the norm and the quotient by the hardware reciprocal square root and reciprocal (about 1e-7
-        // relative, far inside bf16's 2^-9); every lane forms the same scale
-        const float ssr = ssx[r] + ssx[128 + r] + ssx[256 + r] + ssx[384 + r];
-        const float sc = __fdividef(P.amp, fmaf(P.amp, ssr * rsqrtf(ssr), 1e-8f));
+        const float sc = __shfl_sync(0xffffffffu, sc_own, k);
         const int64_t grow = t * kTile + r;
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
