@@ -779,15 +779,16 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
 constexpr int kHalf = 32;    // value columns per CTA
 constexpr int kP2Warps = 8;  // compute warps: 2 per TMEM lane quarter, 16 columns each
 constexpr int kP2Producer = kP2Warps;      // bulk loads (lane 0)
-constexpr int kP2Issuer = kP2Warps + 1;    // tensor-core products (lane 0)
+constexpr int kP2Issuer = kP2Warps + 1;    // tensor-core products of the even slices, and X (lane 0)
 constexpr int kP2Store = kP2Warps + 2;     // record copies and progress words (lane 0)
-constexpr int kP2Thr = 32 * (kP2Warps + 3);
+constexpr int kP2Issuer2 = kP2Warps + 3;   // tensor-core products of the odd slices (lane 0)
+constexpr int kP2Thr = 32 * (kP2Warps + 4);
 constexpr int kP2Bars = 22;
 
 // TMEM columns (phase 2)
 constexpr uint32_t P2_S = 0;    // S^T master, slice s at 32 s (lanes = features), fp32
-constexpr uint32_t P2_Y = 128;  // Y = U_k S^T (lanes 0..63 = k tokens), 32 cols
-constexpr uint32_t P2_X = 160;  // X = T' Y, 32 cols
+constexpr uint32_t P2_Y = 128;  // Y = U_k S^T as 4 partial sums, feature slice s at 32 s (32 cols each)
+constexpr uint32_t P2_X = 256;  // X = T' Y, 32 cols
 
 // shared memory (phase 2)
 constexpr int kRing = 4;              // 32 KiB stages; items: U_k slices (0,1), (2,3) of each chunk
@@ -803,8 +804,8 @@ constexpr uint32_t P2_BAR = 210944;
 constexpr uint32_t kP2Smem = P2_BAR + 256 + 1024;
 static_assert(8 * kP2Bars <= 256, "phase-2 barriers overflow their slot");
 
-// Phase 2 on CTA cta (sequence cta / 2, value columns 32 (cta % 2)..+31; warps 0..10 work,
-// others idle; `tmem` >= 256 allocated columns).  With rec_ready it waits for each record
+// Phase 2 on CTA cta (sequence cta / 2, value columns 32 (cta % 2)..+31; warps 0..11 work,
+// others idle; `tmem` = 512 allocated columns).  With rec_ready it waits for each record
 // to be published; with out_prog it publishes, per sequence and column half, how many
 // chunks have their entering state and E in the records.
 __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uint32_t tmem, int64_t cta,
@@ -834,16 +835,16 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
   if (tid == 0) {
     for (int b = 0; b < kRing; ++b) {
       tc::mbar_init(&ring_full[b], 1 + kP2Warps);
-      tc::mbar_init(&ring_empty[b], 1);
+      tc::mbar_init(&ring_empty[b], 2);  // both issuers' update products of the item
     }
     for (int u = 0; u < 2; ++u) {
       tc::mbar_init(&tp_full[u], 1 + kP2Warps);
       tc::mbar_init(&tp_empty[u], 1);
-      tc::mbar_init(&bar_s[u], 1);
+      tc::mbar_init(&bar_s[u], 2);
       tc::mbar_init(&fac_full[u], 1);
       tc::mbar_init(&fac_empty[u], kP2Warps);
     }
-    tc::mbar_init(bar_y, 1);
+    tc::mbar_init(bar_y, 2);
     tc::mbar_init(bar_x, 1);
     tc::mbar_init(bar_e, kP2Warps);
     tc::mbar_init(bar_stfree, 1);
@@ -892,9 +893,13 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
       }
     }
     __syncwarp();
-  } else if (warp == kP2Issuer) {
+  } else if (warp == kP2Issuer || warp == kP2Issuer2) {
     // ================================================================ tensor-core products
+    // Two issuing threads: one issue costs the issuing thread about 45 cycles, more than the tensor core
+    // needs for these small products, so the even and the odd feature slices are issued by different
+    // warps (their accumulators are independent: Y as one partial sum per slice, the state by slice).
     if (lane == 0) {
+      const int sl = warp == kP2Issuer2 ? 1 : 0;  // this thread's slice of each slice pair: 2p + sl
       // Y = U_k S^T and X = T' Y have the chunk's 64 tokens as rows: M = 64 products, whose accumulator
       // rows 16 q .. 16 q + 15 sit in TMEM lanes 32 q .. 32 q + 15
       const uint32_t id_k = tc::idesc_f16_f32(64, kHalf, false, true);  // A K-major, B MN-major
@@ -909,47 +914,43 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
       uint32_t pf = 0, pt = 0, pe = 0;  // pf, pt: phase bits per slot
       for (int c = 0; c < NC; ++c) {
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {  // Y += U_k S^T over the features of slices 2p, 2p+1
+        for (int p = 0; p < 2; ++p) {  // Y_s = U_k,s S_s^T for slice s = 2p + sl
           const int b = (2 * c + p) & (kRing - 1);  // item 2c + p: its U_k slices and state operand
           ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
           tc::fence_after_sync();
-          const uint64_t da = tc::desc_add(d_ring, uint32_t(b) * 32768);
-          const uint64_t db = tc::desc_add(d_sop, uint32_t(p) * 16384);
-#pragma unroll 1
-          for (int j = 0; j < 4; ++j) {  // slice 2p + (j >> 1), its 64-feature half j & 1
-            const uint64_t a0 = tc::desc_add(da, uint32_t(j) * 8192);
-            const uint64_t b0 = tc::desc_add(db, uint32_t(j) * 4096);
+          // item block j = 2 sl + hh: slice 2p + sl, its 64-feature half hh
+          const uint64_t da = tc::desc_add(d_ring, uint32_t(b) * 32768 + uint32_t(2 * sl) * 8192);
+          const uint64_t db = tc::desc_add(d_sop, uint32_t(p) * 16384 + uint32_t(2 * sl) * 4096);
+          const uint32_t dy = tmem + P2_Y + 32 * (2 * p + sl);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              tc::mma_ss(tmem + P2_Y, tc::desc_add(a0, 32 * kk), tc::desc_add(b0, 1024 * kk), id_k,
-                         p > 0 || j > 0 || kk > 0);
-          }
+              tc::mma_ss(dy, tc::desc_add(da, hh * 8192 + 32 * kk), tc::desc_add(db, hh * 4096 + 1024 * kk), id_k,
+                         hh > 0 || kk > 0);
         }
         tc::mma_commit(bar_y);
-        // X = T' Y
-        const int u = c & 1;
-        ok &= split_wait_bit(&tp_full[u], pt, u, sa.abort);  // T' and the Y operand
-        tc::fence_after_sync();
-        const uint64_t dt = tc::desc_add(d_tp, uint32_t(u) * 8192);
+        if (sl == 0) {  // X = T' Y
+          const int u = c & 1;
+          ok &= split_wait_bit(&tp_full[u], pt, u, sa.abort);  // T' and the Y operand
+          tc::fence_after_sync();
+          const uint64_t dt = tc::desc_add(d_tp, uint32_t(u) * 8192);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)  // K = the 64 tokens
-          tc::mma_ss(tmem + P2_X, tc::desc_add(dt, 32 * kk), tc::desc_add(d_yb, 16 * kk * 64), id_k, kk > 0);
-        tc::mma_commit(&tp_empty[u]);
-        tc::mma_commit(bar_x);
-        // S_s^T += U_k,s^T E'' for s = 2p, 2p+1
+          for (int kk = 0; kk < 4; ++kk)  // K = the 64 tokens
+            tc::mma_ss(tmem + P2_X, tc::desc_add(dt, 32 * kk), tc::desc_add(d_yb, 16 * kk * 64), id_k, kk > 0);
+          tc::mma_commit(&tp_empty[u]);
+          tc::mma_commit(bar_x);
+        }
+        // S_s^T += U_k,s^T E'' for s = 2p + sl
         wait_bar(bar_e, pe);
-#pragma unroll 1
+#pragma unroll
         for (int p = 0; p < 2; ++p) {
           const int b = (2 * c + p) & (kRing - 1);
-          const uint64_t da = tc::desc_add(d_ringT, uint32_t(b) * 32768);
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            const uint64_t a0 = tc::desc_add(da, uint32_t(h) * 16384);
-            const uint32_t dcol = tmem + P2_S + kHalf * (2 * p + h);
+          const uint64_t a0 = tc::desc_add(d_ringT, uint32_t(b) * 32768 + uint32_t(sl) * 16384);
+          const uint32_t dcol = tmem + P2_S + kHalf * (2 * p + sl);
 #pragma unroll
-            for (int k0 = 0; k0 < 64; k0 += 16)
-              tc::mma_ss(dcol, tc::desc_add(a0, 128 * k0), tc::desc_add(d_eb, 64 * k0), id_s, true);
-          }
+          for (int k0 = 0; k0 < 64; k0 += 16)
+            tc::mma_ss(dcol, tc::desc_add(a0, 128 * k0), tc::desc_add(d_eb, 64 * k0), id_s, true);
           tc::mma_commit(&ring_empty[b]);
           tc::mma_commit(&bar_s[p]);
         }
@@ -1055,10 +1056,20 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
       }
       // ---------------------------------------- Y (fp16) for X = T' Y
       wait_bar(bar_y, py);
-      {
-        float y[16];
+      {  // Y = the sum of the 4 slices' partial products
+        float y[16], y2[16];
         tc::tmem_ld16(tmem + lane_off + P2_Y + 16 * ch, y);
+        tc::tmem_ld16(tmem + lane_off + P2_Y + 32 + 16 * ch, y2);
         tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] += y2[j];
+#pragma unroll
+        for (int s2 = 2; s2 < kSlices; ++s2) {
+          tc::tmem_ld16(tmem + lane_off + P2_Y + 32 * s2 + 16 * ch, y2);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) y[j] += y2[j];
+        }
         if (ylane) store_tile(P2_YB, yrow, y, 1.f);
       }
       signal(&tp_full[c & 1]);
@@ -1310,10 +1321,10 @@ __global__ void __launch_bounds__(kP1Thr, 1) chunk_prep_kernel(SplitArgs sa, Pro
 
 __global__ void __launch_bounds__(kP2Thr, 1) state_pass_kernel(SplitArgs sa) {
   uint8_t* sm = split_smem();
-  const uint32_t tmem = split_tmem_alloc(sm, 256);
+  const uint32_t tmem = split_tmem_alloc(sm, 512);
   bool ok = true;
   state_role(sa, sm, tmem, blockIdx.x, nullptr, nullptr, ok);
-  split_finish(tmem, 256, ok);
+  split_finish(tmem, 512, ok);
 }
 
 __global__ void __launch_bounds__(kP3Thr, 1) output_pass_kernel(SplitArgs sa) {
