@@ -787,7 +787,7 @@ constexpr int kP2Bars = 22;
 
 // TMEM columns (phase 2)
 constexpr uint32_t P2_S = 0;    // S^T master, slice s at 32 s (lanes = features), fp32
-constexpr uint32_t P2_Y = 128;  // Y = U_k S^T as 4 partial sums, feature slice s at 32 s (32 cols each)
+constexpr uint32_t P2_Y = 128;  // Y = U_k S^T as 2 partial sums: the even slices' at 128, the odd slices' at 160
 constexpr uint32_t P2_X = 256;  // X = T' Y, 32 cols
 
 // shared memory (phase 2)
@@ -897,7 +897,7 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
     // ================================================================ tensor-core products
     // Two issuing threads: one issue costs the issuing thread about 45 cycles, more than the tensor core
     // needs for these small products, so the even and the odd feature slices are issued by different
-    // warps (their accumulators are independent: Y as one partial sum per slice, the state by slice).
+    // warps (their accumulators are independent: Y as one partial sum per issuer, the state by slice).
     if (lane == 0) {
       const int sl = warp == kP2Issuer2 ? 1 : 0;  // this thread's slice of each slice pair: 2p + sl
       // Y = U_k S^T and X = T' Y have the chunk's 64 tokens as rows: M = 64 products, whose accumulator
@@ -921,13 +921,13 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
           // item block j = 2 sl + hh: slice 2p + sl, its 64-feature half hh
           const uint64_t da = tc::desc_add(d_ring, uint32_t(b) * 32768 + uint32_t(2 * sl) * 8192);
           const uint64_t db = tc::desc_add(d_sop, uint32_t(p) * 16384 + uint32_t(2 * sl) * 4096);
-          const uint32_t dy = tmem + P2_Y + 32 * (2 * p + sl);
+          const uint32_t dy = tmem + P2_Y + 32 * sl;
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               tc::mma_ss(dy, tc::desc_add(da, hh * 8192 + 32 * kk), tc::desc_add(db, hh * 4096 + 1024 * kk), id_k,
-                         hh > 0 || kk > 0);
+                         p > 0 || hh > 0 || kk > 0);
         }
         tc::mma_commit(bar_y);
         if (sl == 0) {  // X = T' Y
@@ -1056,20 +1056,13 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
       }
       // ---------------------------------------- Y (fp16) for X = T' Y
       wait_bar(bar_y, py);
-      {  // Y = the sum of the 4 slices' partial products
+      {  // Y = the sum of the two issuers' partial products
         float y[16], y2[16];
         tc::tmem_ld16(tmem + lane_off + P2_Y + 16 * ch, y);
         tc::tmem_ld16(tmem + lane_off + P2_Y + 32 + 16 * ch, y2);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] += y2[j];
-#pragma unroll
-        for (int s2 = 2; s2 < kSlices; ++s2) {
-          tc::tmem_ld16(tmem + lane_off + P2_Y + 32 * s2 + 16 * ch, y2);
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) y[j] += y2[j];
-        }
         if (ylane) store_tile(P2_YB, yrow, y, 1.f);
       }
       signal(&tp_full[c & 1]);
