@@ -783,7 +783,7 @@ constexpr int kP2Issuer = kP2Warps + 1;    // tensor-core products of the even s
 constexpr int kP2Store = kP2Warps + 2;     // record copies and progress words (lane 0)
 constexpr int kP2Issuer2 = kP2Warps + 3;   // tensor-core products of the odd slices (lane 0)
 constexpr int kP2Thr = 32 * (kP2Warps + 4);
-constexpr int kP2Bars = 22;
+constexpr int kP2Bars = 25;
 
 // TMEM columns (phase 2)
 constexpr uint32_t P2_S = 0;    // S^T master, slice s at 32 s (lanes = features), fp32
@@ -799,8 +799,9 @@ constexpr uint32_t P2_FAC_BYTES = 9216;  //   then ew[64], yqs[64], eC
 constexpr uint32_t P2_SOP = 165888;   // 32 KiB S^T operand (fp16, MN-major SW64 [512 x 32]), slice s at 8 KiB s
 constexpr uint32_t P2_YB = 198656;    // 4 KiB  Y (fp16, MN-major SW64 [64 x 32])
 constexpr uint32_t P2_EB = 202752;    // 4 KiB  E'' (fp16, MN-major SW64)
-constexpr uint32_t P2_ET = 206848;    // 4 KiB  E (fp16, MN-major SW64), copied to the record
-constexpr uint32_t P2_BAR = 210944;
+constexpr uint32_t P2_ET = 206848;    // 2 x 4 KiB E of chunk c at 4 KiB (c & 1) (fp16, MN-major SW64), copied
+                                      //        to the record
+constexpr uint32_t P2_BAR = 215040;
 constexpr uint32_t kP2Smem = P2_BAR + 256 + 1024;
 static_assert(8 * kP2Bars <= 256, "phase-2 barriers overflow their slot");
 
@@ -824,7 +825,8 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
   uint64_t* fac_full = bars + 16;    // [2] factors of the chunk loaded (bytes)
   uint64_t* fac_empty = bars + 18;   // [2] factors copied to registers (8 compute warps)
   uint64_t* bar_e = bars + 20;       // E'' operand and E tile written (8 compute warps)
-  uint64_t* bar_stfree = bars + 21;  // the record copies have read the state operand and E (store warp)
+  uint64_t* bar_stfree = bars + 21;  // [2] the record copy has read slice pair p of the state operand (store warp)
+  uint64_t* bar_ed = bars + 23;      // [2] E tile of chunk c in buffer c & 1 written (8 compute warps)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n = cta >> 1;
@@ -847,7 +849,10 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
     tc::mbar_init(bar_y, 2);
     tc::mbar_init(bar_x, 1);
     tc::mbar_init(bar_e, kP2Warps);
-    tc::mbar_init(bar_stfree, 1);
+    tc::mbar_init(&bar_stfree[0], 1);
+    tc::mbar_init(&bar_stfree[1], 1);
+    tc::mbar_init(&bar_ed[0], kP2Warps);
+    tc::mbar_init(&bar_ed[1], kP2Warps);
     tc::fence_mbar_init();
   }
   tc::fence_before_sync();
@@ -959,22 +964,29 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
     __syncwarp();
   } else if (warp == kP2Store) {
     // ================================================================ record copies, progress
+    // Each slice pair of the state operand is copied as soon as it is written and handed back once the
+    // copy has read it, well before the next chunk rewrites it (the copies read shared memory at only
+    // about 10 bytes per cycle); E is double-buffered, so that its copy never holds up the chain either.
     if (lane == 0) {
-      uint32_t pf = 0, pe = 0;  // pf: phase bits per ring slot
+      uint32_t pf = 0, ped = 0;  // phase bits per ring slot / E buffer
       for (int c = 0; c < NC; ++c) {
         uint8_t* rec = record(sa, c, n);
-        for (int p = 0; p < 2; ++p) {  // both state-operand pairs written (their ring items loaded)
+        for (int p = 0; p < 2; ++p) {  // slice pair p of the state entering the chunk (its ring item loaded)
           const int b = (2 * c + p) & (kRing - 1);
           ok &= split_wait_bit(&ring_full[b], pf, b, sa.abort);
+          tc::bulk_store(rec + REC_S0 + half * 32768 + p * 16384, sbase + P2_SOP + p * 16384, 16384);
+          tc::bulk_commit();
+          if (p == 1) {
+            tc::bulk_wait_read_but1();       // pair 0 (and the previous chunk's E) read
+            tc::mbar_arrive(&bar_stfree[0]);
+          }
         }
-        tc::bulk_store(rec + REC_S0 + half * 32768, sbase + P2_SOP, 32768);  // the state entering the chunk
+        ok &= split_wait_bit(&bar_ed[c & 1], ped, c & 1, sa.abort);
+        tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET + 4096 * (c & 1), 4096);
         tc::bulk_commit();
-        wait_bar(bar_e, pe);
-        tc::bulk_store(rec + REC_E + half * 4096, sbase + P2_ET, 4096);
-        tc::bulk_commit();
-        tc::bulk_wait_read();
-        tc::mbar_arrive(bar_stfree);  // the state operand and E may be rewritten
-        if (out_prog) {               // chunks 0..c of this half are in the record
+        tc::bulk_wait_read_but1();  // pair 1 read
+        tc::mbar_arrive(&bar_stfree[1]);
+        if (out_prog) {  // chunks 0..c of this half are in the record
           tc::bulk_wait_all();
           publish_store(out_prog + 2 * n + half, uint32_t(c + 1));
         }
@@ -1034,11 +1046,16 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&fac_empty[u]);
       }
-      if (c > 0) wait_bar(bar_stfree, pst);  // the previous chunk's state operand and E have been copied
       // ---------------------------------------- per slice pair: state operand (fp16), decay
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (c > 0) wait_bar(&bar_s[p], ps[p]);  // the previous chunk's update of slices 2p, 2p+1
+        if (c > 0) {
+          wait_bar(&bar_s[p], ps[p]);  // the previous chunk's update of slices 2p, 2p+1
+          // ... and the record copy of the previous chunk's state operand pair p (E of chunk c - 2, in this
+          // chunk's E buffer, was read before that)
+          ok &= split_wait_bit(&bar_stfree[p], pst, p, sa.abort);
+          tc::fence_after_sync();
+        }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {  // slice 2p + h
           float v[16];
@@ -1075,11 +1092,17 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         if (ylane) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) x[j] = cu[j] - x[j];
-          store_tile(P2_ET, yrow, x, 1.f);
+          store_tile(P2_ET + 4096 * (c & 1), yrow, x, 1.f);
           store_tile(P2_EB, yrow, x, cew);
         }
       }
-      signal(bar_e);
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(&bar_ed[c & 1]);
+        tc::mbar_arrive(bar_e);
+      }
     }
     wait_bar(&bar_s[0], ps[0]);
     wait_bar(&bar_s[1], ps[1]);
