@@ -773,9 +773,10 @@ __device__ __forceinline__ void prep_role(const SplitArgs& sa, const ProjParams&
 // has read them) and T' (8 KiB) are streamed; the outputs are left to phase 3.
 // The chain is serial (state -> Y -> X -> E -> state).  Every role has its own warp so
 // that no step waits behind another's work: 8 compute warps move tiles between TMEM
-// and shared memory, one thread issues the tensor-core products as soon as a tile's
-// warps have arrived, one keeps the bulk loads ahead, and one copies the entering state
-// and E into the record (and publishes the progress) off the chain.
+// and shared memory, two threads issue the tensor-core products as soon as a tile's
+// warps have arrived (the even and the odd feature slices), one keeps the bulk loads
+// ahead, and one copies the entering state and E into the record (and publishes the
+// progress) off the chain.
 constexpr int kHalf = 32;    // value columns per CTA
 constexpr int kP2Warps = 8;  // compute warps: 2 per TMEM lane quarter, 16 columns each
 constexpr int kP2Producer = kP2Warps;      // bulk loads (lane 0)
