@@ -1044,21 +1044,30 @@ constexpr int kSlab = 32;
 
 constexpr int kSlabLd = kSlab + 4;  // staged slab rows: 16-byte aligned for cp.async
 
+// threads of the gradient kernel: 16 warps at C = 64 (the kernel is one CTA per SM, so the extra warps
+// hide the shared-memory latency of its loops), 8 at C = 32
+template <int C>
+__host__ __device__ constexpr int grad_threads() {
+  return C == 64 ? 512 : 256;
+}
+
 template <int C>
 size_t grad_smem_bytes(int dv) {
   // rows, the two C x C matrices, two stages of [K | Q | S_0 | dS_C] slabs, the per-token vectors
   return sizeof(float) * (size_t(3) * C * (dv + 1) + 2 * C * (C + 1) + 2 * (2 * C + 2 * size_t(dv)) * kSlabLd +
-                          9 * C + 8);
+                          9 * C + grad_threads<C>() / 32);
 }
 
 template <int C>
-__global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, Workspace w,
+__global__ void __launch_bounds__(grad_threads<C>()) simt_grad_kernel(BackwardProblem b, Workspace w,
                                                              const float* __restrict__ dS_chunks,
                                                              const float* __restrict__ dR_rows) {
-  constexpr int R = C / 16;             // C x C tile per thread: R x R
+  constexpr int kGT = grad_threads<C>();
+  constexpr int TJ = kGT / 16;          // the C x C products: 16 x TJ threads, each an RI x RJ tile
+  constexpr int RI = C / 16, RJ = C / TJ;
   constexpr int LD = C + 1;
   constexpr int SL = kSlab + 1;
-  constexpr int TPR2 = kThreads / C;    // threads per token row in the slab phase
+  constexpr int TPR2 = kGT / C;         // threads per token row in the slab phase
   constexpr int CPT = kSlab / TPR2;     // slab columns per thread
   const PrefillProblem& p = b.fwd;
   const int D = p.D, dv = p.dv, LV = dv + 1;
@@ -1080,7 +1089,7 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
   float* s2 = s1 + C;              // [C] dY_i . (S_0 q_i)
   float* s3 = s2 + C;              // [C] E_i . (dS_C k_i)
   float* xv = s3 + C;              // [C] dR_i . v_i
-  float* red = xv + C;             // [8] <dS_C, S_0> partials
+  float* red = xv + C;             // [warps] <dS_C, S_0> partials
 
   const int c = blockIdx.x;
   const int64_t n = blockIdx.y;
@@ -1113,42 +1122,41 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
       lm[ii] = dec;
     }
   }
-  for (int e = tid; e < C * dv; e += kThreads) {
+  for (int e = tid; e < C * dv; e += kGT) {
     const int ii = e / dv, v = e % dv;
     const int64_t t = t0 + ii;
     Em[ii * LV + v] = p.E_rows[(n * w.Tp + t) * dv + v];
     Xm[ii * LV + v] = dR_rows[(n * w.Tp + t) * dv + v];
     Ym[ii * LV + v] = t < p.T ? ld_as_f32(b.dy, b.dy_dtype, (n * p.T + t) * dv + v) : 0.f;
   }
-  for (int e = tid; e < C; e += kThreads) dg[e] = dbA[e] = s1[e] = s2[e] = s3[e] = 0.f;
+  for (int e = tid; e < C; e += kGT) dg[e] = dbA[e] = s1[e] = s2[e] = s3[e] = 0.f;
   __syncthreads();
 
   // ---- sweep 1: Gram k.k and <dS_C, S_0>
-  const int ti = tid / 16, tj = tid % 16;
-  float gk[R][R];
+  const int ti = tid / TJ, tj = tid % TJ;
+  float gk[RI][RJ];
 #pragma unroll
-  for (int a = 0; a < R; ++a)
+  for (int a = 0; a < RI; ++a)
 #pragma unroll
-    for (int q = 0; q < R; ++q) gk[a][q] = 0.f;
+    for (int q = 0; q < RJ; ++q) gk[a][q] = 0.f;
   float dss = 0.f;
   for (int d0 = 0; d0 < D; d0 += kSlab) {
-    for (int e = tid; e < C * kSlab; e += kThreads) {
+    for (int e = tid; e < C * kSlab; e += kGT) {
       const int r = e / kSlab, cc = e % kSlab;
       Ks[r * SL + cc] = Kg[int64_t(r) * D + d0 + cc];
     }
     __syncthreads();
 #pragma unroll 4
     for (int dd = 0; dd < kSlab; ++dd) {
-      float ka[R], kb[R];
+      float ka[RI], kb[RJ];
 #pragma unroll
-      for (int a = 0; a < R; ++a) {
-        ka[a] = Ks[(R * ti + a) * SL + dd];
-        kb[a] = Ks[(R * tj + a) * SL + dd];
-      }
+      for (int a = 0; a < RI; ++a) ka[a] = Ks[(RI * ti + a) * SL + dd];
 #pragma unroll
-      for (int a = 0; a < R; ++a)
+      for (int q = 0; q < RJ; ++q) kb[q] = Ks[(RJ * tj + q) * SL + dd];
 #pragma unroll
-        for (int q = 0; q < R; ++q) gk[a][q] = fmaf(ka[a], kb[q], gk[a][q]);
+      for (int a = 0; a < RI; ++a)
+#pragma unroll
+        for (int q = 0; q < RJ; ++q) gk[a][q] = fmaf(ka[a], kb[q], gk[a][q]);
     }
     __syncthreads();
   }
@@ -1161,7 +1169,7 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
       float* st = ring + (m & 1) * kStage;
       const int dm = m * kSlab;
       constexpr int kq = kSlab / 4;  // 16-byte pieces per slab row
-      for (int e = tid; e < (2 * C + 2 * dv) * kq; e += kThreads) {
+      for (int e = tid; e < (2 * C + 2 * dv) * kq; e += kGT) {
         const int r = e / kq, q4 = e % kq;
         const float* src = r < C       ? Kg + int64_t(r) * D
                            : r < 2 * C ? Qg + int64_t(r - C) * D
@@ -1175,67 +1183,82 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
   issue(0);  // sweep 1 is over with stage 0 (its last barrier); slab 0 lands during the C x C phase
 
   // ---- C x C phase: dA, dY.E, the exp(g) factors, d g and d beta contributions
-  float dA[R][R], dP[R][R];
+  float dA[RI][RJ], dP[RI][RJ];
 #pragma unroll
-  for (int a = 0; a < R; ++a)
+  for (int a = 0; a < RI; ++a)
 #pragma unroll
-    for (int q = 0; q < R; ++q) dA[a][q] = dP[a][q] = 0.f;
+    for (int q = 0; q < RJ; ++q) dA[a][q] = dP[a][q] = 0.f;
   for (int v = 0; v < dv; ++v) {
-    float xa[R], ya[R], eb[R];
+    float xa[RI], ya[RI], eb[RJ];
 #pragma unroll
-    for (int a = 0; a < R; ++a) {
-      xa[a] = Xm[(R * ti + a) * LV + v];
-      ya[a] = Ym[(R * ti + a) * LV + v];
-      eb[a] = Em[(R * tj + a) * LV + v];
+    for (int a = 0; a < RI; ++a) {
+      xa[a] = Xm[(RI * ti + a) * LV + v];
+      ya[a] = Ym[(RI * ti + a) * LV + v];
     }
 #pragma unroll
-    for (int a = 0; a < R; ++a)
+    for (int q = 0; q < RJ; ++q) eb[q] = Em[(RJ * tj + q) * LV + v];
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
+    for (int a = 0; a < RI; ++a)
+#pragma unroll
+      for (int q = 0; q < RJ; ++q) {
         dA[a][q] = fmaf(-xa[a], eb[q], dA[a][q]);
         dP[a][q] = fmaf(ya[a], eb[q], dP[a][q]);
       }
   }
   const float* Pg = w.Aq + (n * w.NC + c) * int64_t(C) * C;
-  float ab[R][R], mq[R][R];
+  float ab[RI][RJ], mq[RI][RJ];
 #pragma unroll
-  for (int a = 0; a < R; ++a)
+  for (int a = 0; a < RI; ++a) {
+    const int ii = RI * ti + a;
+    float sg = 0.f, sb = 0.f, sp = 0.f;  // this row's d g_i, d beta_i and d g_{i-1} terms
 #pragma unroll
-    for (int q = 0; q < R; ++q) {
-      const int ii = R * ti + a, jj = R * tj + q;
+    for (int q = 0; q < RJ; ++q) {
+      const int jj = RJ * tj + q;
       ab[a][q] = mq[a][q] = 0.f;
       if (jj < ii) {
         const float eij = expf(gl[ii] - gl[jj]);
         const float aij = bt[ii] * eij * gk[a][q];
-        const float ca = dA[a][q] * aij;  // d g through A
-        atomicAdd(&dg[ii], ca);
-        atomicAdd(&dg[jj], -ca);
-        atomicAdd(&dbA[ii], dA[a][q] * eij * gk[a][q]);
+        const float ca = dA[a][q] * aij;              // d g through A
         const float cp = dP[a][q] * Pg[ii * C + jj];  // d g through P
-        atomicAdd(&dg[ii - 1], cp);
-        atomicAdd(&dg[jj], -cp);
+        sg += ca;
+        sb += dA[a][q] * eij * gk[a][q];
+        sp += cp;
+        atomicAdd(&dg[jj], -(ca + cp));
         mq[a][q] = dP[a][q] * expf(gl[ii - 1] - gl[jj]);
         ab[a][q] = dA[a][q] * bt[ii] * eij;
       }
     }
+    // the TJ threads of a row group share row ii: one atomic each per group
 #pragma unroll
-  for (int a = 0; a < R; ++a)
+    for (int o = TJ / 2; o > 0; o >>= 1) {
+      sg += __shfl_xor_sync(0xffffffffu, sg, o);
+      sb += __shfl_xor_sync(0xffffffffu, sb, o);
+      sp += __shfl_xor_sync(0xffffffffu, sp, o);
+    }
+    if (tj == 0 && ii > 0) {
+      atomicAdd(&dg[ii], sg);
+      atomicAdd(&dbA[ii], sb);
+      atomicAdd(&dg[ii - 1], sp);
+    }
+  }
 #pragma unroll
-    for (int q = 0; q < R; ++q) {
-      M1[(R * ti + a) * LD + R * tj + q] = ab[a][q];
-      M2[(R * ti + a) * LD + R * tj + q] = mq[a][q];
+  for (int a = 0; a < RI; ++a)
+#pragma unroll
+    for (int q = 0; q < RJ; ++q) {
+      M1[(RI * ti + a) * LD + RJ * tj + q] = ab[a][q];
+      M2[(RI * ti + a) * LD + RJ * tj + q] = mq[a][q];
     }
   __syncthreads();
-  float sym[R][R];
+  float sym[RI][RJ];
 #pragma unroll
-  for (int a = 0; a < R; ++a)
+  for (int a = 0; a < RI; ++a)
 #pragma unroll
-    for (int q = 0; q < R; ++q) sym[a][q] = ab[a][q] + M1[(R * tj + q) * LD + R * ti + a];
+    for (int q = 0; q < RJ; ++q) sym[a][q] = ab[a][q] + M1[(RJ * tj + q) * LD + RI * ti + a];
   __syncthreads();
 #pragma unroll
-  for (int a = 0; a < R; ++a)
+  for (int a = 0; a < RI; ++a)
 #pragma unroll
-    for (int q = 0; q < R; ++q) M1[(R * ti + a) * LD + R * tj + q] = sym[a][q];
+    for (int q = 0; q < RJ; ++q) M1[(RI * ti + a) * LD + RJ * tj + q] = sym[a][q];
 
   // ---- sweep 2: feature gradients, 32 columns at a time
   const int i = tid / TPR2;
@@ -1255,7 +1278,7 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
     const float* Qst = st + C * kSlabLd;
     const float* S0s = st + 2 * C * kSlabLd;
     const float* dSs = S0s + dv * kSlabLd;
-    for (int e = tid; e < dv * kSlab; e += kThreads) {
+    for (int e = tid; e < dv * kSlab; e += kGT) {
       const int r = e / kSlab, cc = e % kSlab;
       dss = fmaf(S0s[r * kSlabLd + cc], dSs[r * kSlabLd + cc], dss);
     }
@@ -1349,7 +1372,7 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
     if (ii > 0) atomicAdd(&dg[ii - 1], expf(gl[ii - 1]) * s2[ii]);
     if (ii == C - 1) {
       float tot = 0.f;
-      for (int q = 0; q < kThreads / 32; ++q) tot += red[q];
+      for (int q = 0; q < kGT / 32; ++q) tot += red[q];
       atomicAdd(&dg[C - 1], expf(gl[C - 1]) * tot);
     }
   }
@@ -1367,7 +1390,7 @@ __global__ void __launch_bounds__(kThreads) simt_grad_kernel(BackwardProblem b, 
       }
     }
   }
-  for (int e = tid; e < C * dv; e += kThreads) {
+  for (int e = tid; e < C * dv; e += kGT) {
     const int ii = e / dv, v = e % dv;
     const int64_t t = t0 + ii;
     if (t < p.T) b.dv_out[(n * p.T + t) * dv + v] = bt[ii] * Xm[ii * LV + v];
@@ -1515,7 +1538,8 @@ cudaError_t launch_backward_c(BackwardProblem b, const Workspace& w, const Backw
     const size_t smem = grad_smem_bytes<C>(b.fwd.dv);
     err = cudaFuncSetAttribute(simt_grad_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return err;
-    simt_grad_kernel<C><<<dim3(w.NC, unsigned(b.fwd.N)), kThreads, smem, stream>>>(b, w, x.dS_chunks, x.dR_rows);
+    simt_grad_kernel<C><<<dim3(w.NC, unsigned(b.fwd.N)), grad_threads<C>(), smem, stream>>>(b, w, x.dS_chunks,
+                                                                                          x.dR_rows);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
   }
   {
