@@ -1057,19 +1057,22 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
           ok &= split_wait_bit(&bar_stfree[p], pst, p, sa.abort);
           tc::fence_after_sync();
         }
+        float v0[16], v1[16];  // slices 2p and 2p + 1, loaded together (one wait)
+        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p) + 16 * ch, v0);
+        tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p + 1) + 16 * ch, v1);
+        tc::tmem_ld_wait();
+        store_tile(P2_SOP + (2 * p) * 8192, trow, v0, 1.f);
+        store_tile(P2_SOP + (2 * p + 1) * 8192, trow, v1, 1.f);
+        if (decayed) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // slice 2p + h
-          float v[16];
-          tc::tmem_ld16(tmem + lane_off + P2_S + kHalf * (2 * p + h) + 16 * ch, v);
-          tc::tmem_ld_wait();
-          store_tile(P2_SOP + (2 * p + h) * 8192, trow, v, 1.f);
-          if (decayed) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] *= ceC;
-            tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p + h) + 16 * ch, v);
+          for (int j = 0; j < 16; ++j) {
+            v0[j] *= ceC;
+            v1[j] *= ceC;
           }
+          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p) + 16 * ch, v0);
+          tc::tmem_st16(tmem + lane_off + P2_S + kHalf * (2 * p + 1) + 16 * ch, v1);
+          tc::tmem_st_wait();
         }
-        if (decayed) tc::tmem_st_wait();
         signal(&ring_full[(2 * c + p) & (kRing - 1)]);
       }
       // ---------------------------------------- Y (fp16) for X = T' Y
