@@ -27,6 +27,9 @@ namespace kdn {
 namespace {
 
 constexpr int kThreads = 256;
+// padded rows (floats) of the chunk-64 chain's shared tiles: T and Aq (16-byte row reads), the feature
+// slices and the state (8-byte fragment reads: a row stride of 8 mod 32 words keeps them conflict-free)
+constexpr int kChainLd = 68, kChainRingLd = 72, kChainSd = 520;
 
 struct Workspace {
   float* phik;   // [N, Tp, D]
@@ -39,6 +42,30 @@ struct Workspace {
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---- exact-fp32 products on the tensor cores: x = hi + lo with hi = x truncated to tf32 and lo the
+// exact remainder (which the tensor core reads at tf32 precision, within 2^-20 |x|), and
+// a b ~ hi_a hi_b + hi_a lo_b + lo_a hi_b (the split-tf32 scheme of Markidis et al., 2018): each tf32
+// product is exact in the fp32 accumulator and the dropped terms are about 2^-20 |a b|, near the
+// accuracy of an fp32 dot product.
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = __float_as_uint(x) & 0xffffe000u;        // tf32 by truncation: the top 19 bits
+  lo = __float_as_uint(x - __uint_as_float(hi));  // the exact remainder, below 2^-10 |x|, read as tf32
+}
+// c += a b for a 16 x 8 tile of a (row-major fragment a[4]) and an 8 x 8 tile of b (b0, b1)
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_3xtf32(float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                           const uint32_t (&bh)[2], const uint32_t (&bl)[2]) {
+  mma_tf32(c, al, bh[0], bh[1]);  // the small terms first
+  mma_tf32(c, ah, bl[0], bl[1]);
+  mma_tf32(c, ah, bh[0], bh[1]);
+}
 
 Workspace carve(void* base, int64_t N, int64_t T, int dv, int C, int D, size_t* total) {
   (void)dv;
@@ -404,14 +431,17 @@ __global__ void __launch_bounds__(kThreads, 1) simt_chain64_kernel(PrefillProble
   constexpr int C = 64;
   constexpr int TPR = kThreads / C;  // threads per chunk row
   constexpr int VPT = RT / TPR;      // state rows per thread in the products
-  constexpr int LD = 68;             // padded row of the staged tiles (floats)
+  constexpr int LD = kChainLd;       // padded row of the staged T and Aq (floats)
+  constexpr int LDK = kChainRingLd;  // padded row of the staged feature slices
   constexpr int kStages = 3;
-  constexpr int kSlice = C * LD;     // floats of one staged 64-feature slice
-  constexpr int D = 512, SD = D + 4, kNsl = D / 64;
+  constexpr int kSlice = C * LDK;    // floats of one staged 64-feature slice
+  constexpr int D = 512, SD = kChainSd, kNsl = D / 64;
   constexpr int RPT = RT / 2;        // state rows per thread in the update (two row groups)
+  constexpr int NT = RT / 8;         // 8-row tiles of the state in the tensor-core products
+  static_assert(kThreads == 256 && RT % 8 == 0, "the products take 8 warps: 4 token tiles x 2 feature halves");
   extern __shared__ __align__(16) float sm[];
   float* S = sm;                              // [RT][SD]
-  float* ring = S + RT * SD;                  // [kStages][K | Q][C][LD]
+  float* ring = S + RT * SD;                  // [kStages][K | Q][C][LDK]
   float* Tb = ring + kStages * 2 * kSlice;    // [2][T | Aq][C][LD]
   float* gb = Tb + 4 * C * LD;                // [2][C][4]
   float* Rs = gb + 2 * C * 4;                 // [C][RT]
@@ -446,9 +476,9 @@ __global__ void __launch_bounds__(kThreads, 1) simt_chain64_kernel(PrefillProble
       float* st = ring + int(g % kStages) * 2 * kSlice;
       for (int e = tid; e < C * 16; e += kThreads) {
         const int r = e >> 4, q = e & 15;
-        tc::cp_async16(tc::smem_u32(st + r * LD + 4 * q), w.phik + rowbase + int64_t(r) * D + 4 * q, 16);
+        tc::cp_async16(tc::smem_u32(st + r * LDK + 4 * q), w.phik + rowbase + int64_t(r) * D + 4 * q, 16);
         if (readout)
-          tc::cp_async16(tc::smem_u32(st + kSlice + r * LD + 4 * q), w.phiq + rowbase + int64_t(r) * D + 4 * q, 16);
+          tc::cp_async16(tc::smem_u32(st + kSlice + r * LDK + 4 * q), w.phiq + rowbase + int64_t(r) * D + 4 * q, 16);
       }
       if (s == 0) {
         const int64_t cm = (n * NC + c) * int64_t(C) * C;
@@ -474,42 +504,100 @@ __global__ void __launch_bounds__(kThreads, 1) simt_chain64_kernel(PrefillProble
       float* Sc = p.S_chunks + ((n * NC + c) * p.dv + row0) * int64_t(D);
       for (int e = tid; e < RT * D; e += kThreads) Sc[e] = S[(e / D) * SD + e % D];
     }
-    // X = K S^T, Yq = Q S^T (C x RT), slice by slice from the ring
-    float x[VPT], yq[VPT];
+    // X = K S^T, Yq = Q S^T (C x RT), slice by slice from the ring, on the tensor cores in split tf32:
+    // warp w takes token rows 16 (w & 3) .. + 15 and the k-steps 4 (w >> 2) .. + 3 (8 features each) of
+    // every slice; the two halves of the features meet in shared memory (Rs, Es are free until R and E).
+    // A k-step's fragment slots t and t + 4 take the adjacent features 2t and 2t + 1 (the same order in
+    // A and B, so the sum is unchanged): one 8-byte shared load per row, conflict-free with the padded
+    // rows.  Two accumulators per product (even and odd k-steps) halve the dependent chain.
+    {
+      const int wq = tid >> 5, g8 = (tid & 31) >> 2, t4 = tid & 3;
+      const int mrow = 16 * (wq & 3) + g8, kh = wq >> 2;
+      float xa[2][NT][4], ya[2][NT][4];
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) x[u] = yq[u] = 0.f;
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xa[h][nt][e] = ya[h][nt][e] = 0.f;
 #pragma unroll 1
-    for (int s = 0; s < kNsl; ++s) {
-      const int64_t g = int64_t(c) * kNsl + s;
-      tc::cp_async_wait_group<kStages - 2>();  // item g has landed (this thread's copies) ...
-      __syncthreads();                         // ... everyone's; item g - 1's stage is free
-      issue(g + kStages - 1);
-      const float* Ks = ring + int(g % kStages) * 2 * kSlice;
-      const float* Qs = Ks + kSlice;
-      const float* Sd = S + 64 * s;
-      if (readout) {
-#pragma unroll 4
-        for (int dd = 0; dd < 64; dd += 4) {
-          const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * LD + dd);
-          const float4 q4 = *reinterpret_cast<const float4*>(Qs + i * LD + dd);
+      for (int s = 0; s < kNsl; ++s) {
+        const int64_t g = int64_t(c) * kNsl + s;
+        tc::cp_async_wait_group<kStages - 2>();  // item g has landed (this thread's copies) ...
+        __syncthreads();                         // ... everyone's; item g - 1's stage is free
+        issue(g + kStages - 1);
+        const float* Ks = ring + int(g % kStages) * 2 * kSlice;
+        const float* Qs = Ks + kSlice;
+        const float* Sd = S + 64 * s;
 #pragma unroll
-          for (int u = 0; u < VPT; ++u) {
-            const float4 s4 = *reinterpret_cast<const float4*>(Sd + (v0 + u) * SD + dd);
-            x[u] = fmaf(k4.w, s4.w, fmaf(k4.z, s4.z, fmaf(k4.y, s4.y, fmaf(k4.x, s4.x, x[u]))));
-            yq[u] = fmaf(q4.w, s4.w, fmaf(q4.z, s4.z, fmaf(q4.y, s4.y, fmaf(q4.x, s4.x, yq[u]))));
+        for (int kk = 0; kk < 4; ++kk) {
+          const int kb = 8 * (4 * kh + kk) + 2 * t4;  // this lane's features kb, kb + 1 of the slice
+          uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {  // B = S^T: state row 8 nt + g8
+            const float2 s2 = *reinterpret_cast<const float2*>(Sd + (8 * nt + g8) * SD + kb);
+            split_tf32(s2.x, bh[nt][0], bl[nt][0]);
+            split_tf32(s2.y, bh[nt][1], bl[nt][1]);
           }
-        }
-      } else {
-#pragma unroll 4
-        for (int dd = 0; dd < 64; dd += 4) {
-          const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * LD + dd);
+          uint32_t ah[4], al[4];
+          {
+            const float2 r0 = *reinterpret_cast<const float2*>(Ks + mrow * LDK + kb);
+            const float2 r1 = *reinterpret_cast<const float2*>(Ks + (mrow + 8) * LDK + kb);
+            split_tf32(r0.x, ah[0], al[0]);
+            split_tf32(r1.x, ah[1], al[1]);
+            split_tf32(r0.y, ah[2], al[2]);
+            split_tf32(r1.y, ah[3], al[3]);
+          }
 #pragma unroll
-          for (int u = 0; u < VPT; ++u) {
-            const float4 s4 = *reinterpret_cast<const float4*>(Sd + (v0 + u) * SD + dd);
-            x[u] = fmaf(k4.w, s4.w, fmaf(k4.z, s4.z, fmaf(k4.y, s4.y, fmaf(k4.x, s4.x, x[u]))));
+          for (int nt = 0; nt < NT; ++nt) mma_3xtf32(xa[kk & 1][nt], ah, al, bh[nt], bl[nt]);
+          if (readout) {
+            const float2 r0 = *reinterpret_cast<const float2*>(Qs + mrow * LDK + kb);
+            const float2 r1 = *reinterpret_cast<const float2*>(Qs + (mrow + 8) * LDK + kb);
+            split_tf32(r0.x, ah[0], al[0]);
+            split_tf32(r1.x, ah[1], al[1]);
+            split_tf32(r0.y, ah[2], al[2]);
+            split_tf32(r1.y, ah[3], al[3]);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) mma_3xtf32(ya[kk & 1][nt], ah, al, bh[nt], bl[nt]);
           }
         }
       }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          xa[0][nt][e] += xa[1][nt][e];
+          ya[0][nt][e] += ya[1][nt][e];
+        }
+      // fragment element e of n-tile nt: token mrow + 8 (e >> 1), state row 8 nt + 2 t4 + (e & 1)
+      if (kh == 1) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int o = (mrow + 8 * (e >> 1)) * RT + 8 * nt + 2 * t4 + (e & 1);
+            Rs[o] = xa[0][nt][e];
+            Es[o] = ya[0][nt][e];
+          }
+      }
+      __syncthreads();
+      if (kh == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int o = (mrow + 8 * (e >> 1)) * RT + 8 * nt + 2 * t4 + (e & 1);
+            Rs[o] += xa[0][nt][e];
+            Es[o] += ya[0][nt][e];
+          }
+      }
+      __syncthreads();
+    }
+    float x[VPT], yq[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+      x[u] = Rs[i * RT + v0 + u];
+      yq[u] = Es[i * RT + v0 + u];
     }
     const float* Tm = Tb + (c & 1) * 2 * C * LD;
     const float* Am = Tm + C * LD;
@@ -623,7 +711,8 @@ __global__ void __launch_bounds__(kThreads, 1) simt_chain64_kernel(PrefillProble
 
 template <int RT>
 size_t chain64_smem_bytes() {
-  return sizeof(float) * (size_t(RT) * (512 + 4) + 3 * 2 * 64 * 68 + 4 * 64 * 68 + 2 * 64 * 4 + 2 * 64 * RT);
+  return sizeof(float) *
+         (size_t(RT) * kChainSd + 3 * 2 * 64 * kChainRingLd + 4 * 64 * kChainLd + 2 * 64 * 4 + 2 * 64 * RT);
 }
 
 // rows of S per chain CTA: 16, or 8 when 16-row tiles would leave SMs idle (few sequences), or 4
@@ -843,15 +932,18 @@ __global__ void __launch_bounds__(kThreads, 1) simt_adjoint64_kernel(BackwardPro
   constexpr int C = 64;
   constexpr int TPR = kThreads / C;
   constexpr int VPT = RT / TPR;
-  constexpr int LD = 68;
+  constexpr int LD = kChainLd;
+  constexpr int LDK = kChainRingLd;
   constexpr int kStages = 3;
-  constexpr int kSlice = C * LD;
-  constexpr int D = 512, SD = D + 4, kNsl = D / 64;
+  constexpr int kSlice = C * LDK;
+  constexpr int D = 512, SD = kChainSd, kNsl = D / 64;
   constexpr int RPT = RT / 2;
+  constexpr int NT = RT / 8;
+  static_assert(kThreads == 256 && RT % 8 == 0, "the products take 8 warps: 4 token tiles x 2 feature halves");
   const PrefillProblem& p = b.fwd;
   extern __shared__ __align__(16) float sm[];
   float* dS = sm;                          // [RT][SD]
-  float* ring = dS + RT * SD;              // [kStages][C][LD] K slices
+  float* ring = dS + RT * SD;              // [kStages][C][LDK] K slices
   float* Tb = ring + kStages * kSlice;     // [2][T | Aq][C][LD]
   float* gb = Tb + 4 * C * LD;             // [2][C][4]
   float* Ys = gb + 2 * C * 4;              // [C][RT]: dY, then Gs_i dY_i
@@ -878,7 +970,7 @@ __global__ void __launch_bounds__(kThreads, 1) simt_adjoint64_kernel(BackwardPro
       float* st = ring + int(g % kStages) * kSlice;
       for (int e = tid; e < C * 16; e += kThreads) {
         const int r = e >> 4, q = e & 15;
-        tc::cp_async16(tc::smem_u32(st + r * LD + 4 * q), w.phik + rowbase + int64_t(r) * D + 4 * q, 16);
+        tc::cp_async16(tc::smem_u32(st + r * LDK + 4 * q), w.phik + rowbase + int64_t(r) * D + 4 * q, 16);
       }
       if (s == 0) {
         const int64_t cm = (n * NC + c) * int64_t(C) * C;
@@ -903,28 +995,67 @@ __global__ void __launch_bounds__(kThreads, 1) simt_adjoint64_kernel(BackwardPro
     const int c = NC - 1 - ci;
     float* dSc = dS_chunks + ((n * NC + c) * p.dv + row0) * int64_t(D);
     for (int e = tid; e < RT * D; e += kThreads) dSc[e] = dS[(e / D) * SD + e % D];
-    // x_i = k_i . dS_v  (C x RT), slice by slice from the ring
-    float x[VPT];
+    // x_i = k_i . dS_v  (C x RT), slice by slice from the ring, on the tensor cores in split tf32 with
+    // the warp layout of simt_chain64_kernel's X; the two feature halves meet in Ws (free until dE)
+    {
+      const int wq = tid >> 5, g8 = (tid & 31) >> 2, t4 = tid & 3;
+      const int mrow = 16 * (wq & 3) + g8, kh = wq >> 2;
+      float xa[2][NT][4];
 #pragma unroll
-    for (int u = 0; u < VPT; ++u) x[u] = 0.f;
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xa[h][nt][e] = 0.f;
 #pragma unroll 1
-    for (int s = 0; s < kNsl; ++s) {
-      const int64_t g = int64_t(ci) * kNsl + s;
-      tc::cp_async_wait_group<kStages - 2>();
-      __syncthreads();
-      issue(g + kStages - 1);
-      const float* Ks = ring + int(g % kStages) * kSlice;
-      const float* Sd = dS + 64 * s;
-#pragma unroll 4
-      for (int dd = 0; dd < 64; dd += 4) {
-        const float4 k4 = *reinterpret_cast<const float4*>(Ks + i * LD + dd);
+      for (int s = 0; s < kNsl; ++s) {
+        const int64_t g = int64_t(ci) * kNsl + s;
+        tc::cp_async_wait_group<kStages - 2>();
+        __syncthreads();
+        issue(g + kStages - 1);
+        const float* Ks = ring + int(g % kStages) * kSlice;
+        const float* Sd = dS + 64 * s;
 #pragma unroll
-        for (int u = 0; u < VPT; ++u) {
-          const float4 s4 = *reinterpret_cast<const float4*>(Sd + (v0 + u) * SD + dd);
-          x[u] = fmaf(k4.w, s4.w, fmaf(k4.z, s4.z, fmaf(k4.y, s4.y, fmaf(k4.x, s4.x, x[u]))));
+        for (int kk = 0; kk < 4; ++kk) {
+          const int kb = 8 * (4 * kh + kk) + 2 * t4;
+          uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const float2 s2 = *reinterpret_cast<const float2*>(Sd + (8 * nt + g8) * SD + kb);
+            split_tf32(s2.x, bh[nt][0], bl[nt][0]);
+            split_tf32(s2.y, bh[nt][1], bl[nt][1]);
+          }
+          const float2 r0 = *reinterpret_cast<const float2*>(Ks + mrow * LDK + kb);
+          const float2 r1 = *reinterpret_cast<const float2*>(Ks + (mrow + 8) * LDK + kb);
+          uint32_t ah[4], al[4];
+          split_tf32(r0.x, ah[0], al[0]);
+          split_tf32(r1.x, ah[1], al[1]);
+          split_tf32(r0.y, ah[2], al[2]);
+          split_tf32(r1.y, ah[3], al[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_3xtf32(xa[kk & 1][nt], ah, al, bh[nt], bl[nt]);
         }
       }
+      if (kh == 1) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            Ws[(mrow + 8 * (e >> 1)) * RT + 8 * nt + 2 * t4 + (e & 1)] = xa[0][nt][e] + xa[1][nt][e];
+      }
+      __syncthreads();
+      if (kh == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            Ws[(mrow + 8 * (e >> 1)) * RT + 8 * nt + 2 * t4 + (e & 1)] += xa[0][nt][e] + xa[1][nt][e];
+      }
+      __syncthreads();
     }
+    float x[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) x[u] = Ws[i * RT + v0 + u];
     const float* Tm = Tb + (ci & 1) * 2 * C * LD;
     const float* Am = Tm + C * LD;
     const float* gt = gb + (ci & 1) * C * 4;
@@ -1035,7 +1166,7 @@ __global__ void __launch_bounds__(kThreads, 1) simt_adjoint64_kernel(BackwardPro
 
 template <int RT>
 size_t adjoint64_smem_bytes() {
-  return sizeof(float) * (size_t(RT) * (512 + 4) + 3 * 64 * 68 + 4 * 64 * 68 + 2 * 64 * 4 + 2 * 64 * RT);
+  return sizeof(float) * (size_t(RT) * kChainSd + 3 * 64 * kChainRingLd + 4 * 64 * kChainLd + 2 * 64 * 4 + 2 * 64 * RT);
 }
 
 // (B2) per (chunk, sequence): the gradients of the chunk's tokens.  The feature gradients
