@@ -876,6 +876,10 @@ __device__ __forceinline__ void state_role(const SplitArgs& sa, uint8_t* sm, uin
         if (rec_ready) {  // the record has been published by the preparation pass
           ok &= wait_flag(rec_ready + int64_t(c) * sa.N + n, 1u, sa.abort);
           tc::fence_proxy_async_global();
+        } else if (c + 2 < NC) {  // every record is in place: the one two chunks ahead into L2 meanwhile
+          const uint8_t* ahead = record(sa, c + 2, n);
+          tc::bulk_prefetch_l2(ahead + REC_UK, REC_AQ - REC_UK);  // U_k, T', U
+          tc::bulk_prefetch_l2(ahead + REC_VEC, 1024);
         }
         for (int p = 0; p < 2; ++p, ++g) {  // U_k slices 2p, 2p+1
           const int b = int(g % kRing);
