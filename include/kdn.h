@@ -44,7 +44,9 @@ extern "C" {
 #define KDN_INDEX_I64 1
 
 /* prefill arithmetic modes */
-#define KDN_MODE_F32 0  /* exact fp32 arithmetic (CUDA cores) */
+#define KDN_MODE_F32 0  /* fp32 arithmetic: CUDA cores, and split-tf32 tensor-core products
+                           (three tf32 products per term, fp32 accumulation) for K S^T and
+                           Q S^T at chunk 64 / D 512 */
 #define KDN_MODE_BF16 1 /* bf16 tensor-core products, fp32 accumulation, fp32 state */
 
 /* decode readout order */
@@ -141,7 +143,7 @@ int kdn_prefill_launch_count(void);
  * allocate device memory when they run a prefill (an engine that reserved
  * nearly all device memory for its own pool up front, a step loop that cannot
  * take cudaFree's implicit device synchronisation).  It always runs the exact
- * fp32 CUDA-core path (KDN_MODE_F32); its scratch is the fixed
+ * fp32 path (KDN_MODE_F32); its scratch is the fixed
  * KDN_STATIC_SCRATCH_BYTES array above, so nothing is allocated per call.
  *   - Sizes whose scratch need exceeds KDN_STATIC_SCRATCH_BYTES are rejected
  *     with KDN_ERR_WORKSPACE before any work is enqueued.
@@ -258,7 +260,7 @@ int kdn_chunked_prefill_varlen(const void* q, const void* k, const void* v, int 
  * state) [N, dv, D] fp32, it writes fp32 gradients: dq, dk [N, T, d_k], dv_out [N, T, dv],
  * dbeta [N, T], ddecay [N, T] (when decay is given; zero where the decay is clamped, i.e.
  * outside [1e-5, 1]) and, if d_initial_state is not NULL, dL/d(initial state) [N, dv, D].
- * Exact fp32 on CUDA cores: the forward is recomputed with checkpoints (the state entering
+ * fp32 arithmetic (KDN_MODE_F32's kernels): the forward is recomputed with checkpoints (the state entering
  * every chunk), then one reverse pass over chunks carries the state's adjoint, one parallel
  * pass forms every chunk's gradients, and the lift is differentiated through its butterfly.
  * dv a multiple of 16 up to 128; chunk 32 or 64; workspace from

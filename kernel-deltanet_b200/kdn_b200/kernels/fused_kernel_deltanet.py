@@ -12,7 +12,8 @@ with q, k [B, T, d_k], v [B, T, d_v], beta/decay [B, T], state [B, d_v, D]
 Y is returned in q's dtype; the state is always returned in float32 (the
 reference keeps it in the input dtype -- fp32 state is this build's contract).
 
-Arithmetic modes: ``"fp32"`` (exact fp32, CUDA cores) and ``"bf16"`` (bf16
+Arithmetic modes: ``"fp32"`` (fp32: CUDA cores and split-tf32 tensor-core products, 1e-4 of the
+fp32 reference) and ``"bf16"`` (bf16
 tensor-core products with fp32 accumulation and fp32 state); default: "bf16"
 for bfloat16 inputs, "fp32" otherwise.  The work runs in libkdn on the
 tensors' CUDA device and current stream; there is no CPU path.  Host
