@@ -676,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1) simt_chain64_kernel(PrefillProble
         const float4 s4 = *reinterpret_cast<const float4*>(S + (RPT * rb + r) * SD + 4 * fb);
         acc[r][0] = gC * s4.x, acc[r][1] = gC * s4.y, acc[r][2] = gC * s4.z, acc[r][3] = gC * s4.w;
       }
-#pragma unroll 1
+#pragma unroll
       for (int j0 = 0; j0 < C; j0 += 16) {
         float4 kv[16];
 #pragma unroll
@@ -1128,7 +1128,7 @@ __global__ void __launch_bounds__(kThreads, 1) simt_adjoint64_kernel(BackwardPro
         const float4 s4 = *reinterpret_cast<const float4*>(dS + (RPT * rb + r) * SD + 4 * fb);
         acc[r][0] = gC * s4.x, acc[r][1] = gC * s4.y, acc[r][2] = gC * s4.z, acc[r][3] = gC * s4.w;
       }
-#pragma unroll 1
+#pragma unroll
       for (int j0 = 0; j0 < C; j0 += 8) {
         float4 kv[8], qv[8];
 #pragma unroll
