@@ -115,16 +115,24 @@ __global__ void __launch_bounds__(kThreads) simt_lift_kernel(PrefillProblem p, W
   }
 }
 
+// floats of one staged 64-feature slice in the preparation: feature-major rows of 68 (16-byte reads of
+// a thread's 4 token rows) for chunk 64, token-major rows of 65 otherwise
+template <int C>
+constexpr int prep_stage_floats() {
+  return C == 64 ? 64 * 68 : C * 65;
+}
+
 // (2) per (chunk c, sequence n): G = K K^T, P = Q K^T, gates, T = (I + A)^-1, Aq.
 // kQ = false (no readout): P and Aq are skipped (Aq is written as zeros).
 template <int C, bool kQ>
 __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, Workspace w) {
   constexpr int R = C / 16;  // each thread owns an R x R tile of G and of P
   constexpr int LD = C + 1;
+  constexpr int SL = prep_stage_floats<C>();  // floats of one staged slice
   extern __shared__ float sm[];
-  float* Ks = sm;            // [C][65]
-  float* Qs = Ks + C * 65;   // [C][65]
-  float* G = Qs + C * 65;    // [C][LD], becomes A
+  float* Ks = sm;            // chunk 64: [64 features][68] (feature-major); else [C][65]
+  float* Qs = Ks + SL;
+  float* G = Qs + SL;        // [C][LD], becomes A
   float* Pm = G + C * LD;    // [C][LD], becomes Aq
   float* Tm = Pm + C * LD;   // [C][LD]
   float* gl = Tm + C * LD;   // [C]
@@ -147,18 +155,36 @@ __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, W
   for (int d0 = 0; d0 < D; d0 += 64) {
     for (int e = tid; e < C * 64; e += kThreads) {
       const int r = e >> 6, cc = e & 63;
-      Ks[r * 65 + cc] = Kg[int64_t(r) * D + d0 + cc];
-      if (kQ) Qs[r * 65 + cc] = Qg[int64_t(r) * D + d0 + cc];
+      if constexpr (C == 64) {  // feature-major: a thread's 4 rows at one feature are one 16-byte read
+        Ks[cc * 68 + r] = Kg[int64_t(r) * D + d0 + cc];
+        if (kQ) Qs[cc * 68 + r] = Qg[int64_t(r) * D + d0 + cc];
+      } else {
+        Ks[r * 65 + cc] = Kg[int64_t(r) * D + d0 + cc];
+        if (kQ) Qs[r * 65 + cc] = Qg[int64_t(r) * D + d0 + cc];
+      }
     }
     __syncthreads();
 #pragma unroll 4
     for (int dd = 0; dd < 64; ++dd) {
       float a[R], qq[R], b[R];
+      if constexpr (C == 64) {
+        const float4 a4 = *reinterpret_cast<const float4*>(Ks + dd * 68 + ti * R);
+        const float4 b4 = *reinterpret_cast<const float4*>(Ks + dd * 68 + tj * R);
+        a[0] = a4.x, a[1] = a4.y, a[2] = a4.z, a[3] = a4.w;
+        b[0] = b4.x, b[1] = b4.y, b[2] = b4.z, b[3] = b4.w;
+        if (kQ) {
+          const float4 q4 = *reinterpret_cast<const float4*>(Qs + dd * 68 + ti * R);
+          qq[0] = q4.x, qq[1] = q4.y, qq[2] = q4.z, qq[3] = q4.w;
+        } else {
+          qq[0] = qq[1] = qq[2] = qq[3] = 0.f;
+        }
+      } else {
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        a[r] = Ks[(ti * R + r) * 65 + dd];
-        qq[r] = kQ ? Qs[(ti * R + r) * 65 + dd] : 0.f;
-        b[r] = Ks[(tj * R + r) * 65 + dd];
+        for (int r = 0; r < R; ++r) {
+          a[r] = Ks[(ti * R + r) * 65 + dd];
+          qq[r] = kQ ? Qs[(ti * R + r) * 65 + dd] : 0.f;
+          b[r] = Ks[(tj * R + r) * 65 + dd];
+        }
       }
 #pragma unroll
       for (int r = 0; r < R; ++r)
@@ -254,7 +280,7 @@ __global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrefillProblem p, W
 
 template <int C>
 constexpr size_t prep_smem_bytes() {
-  return sizeof(float) * (2 * C * 65 + 3 * C * (C + 1) + 2 * C);
+  return sizeof(float) * (2 * prep_stage_floats<C>() + 3 * C * (C + 1) + 2 * C);
 }
 
 // (3) per (tile of RT rows of S, sequence n): the serial pass over chunks (RT = 16, or 8 when the
