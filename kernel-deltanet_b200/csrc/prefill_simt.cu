@@ -1583,20 +1583,21 @@ __global__ void __launch_bounds__(kThreads) lift_backward_kernel(BackwardProblem
     const int64_t n = row / p.T, t = row % p.T;
     const float2 xv = ld2_as_f32(isq ? p.q : p.k, p.in_dtype, row * kDk + 2 * lane);
     const float* g = (isq ? w.phiq : w.phik) + (n * w.Tp + t) * D;
-    float z[kMaxBlocks][2], u[kMaxBlocks][2], gg[kMaxBlocks][2];
+    float sn[kMaxBlocks][2], u[kMaxBlocks][2], gg[kMaxBlocks][2];  // sin z, amp cos z, the incoming gradient
     float ss = 0.f, ug = 0.f;
 #pragma unroll
     for (int m = 0; m < kMaxBlocks; ++m) {
-      z[m][0] = z[m][1] = u[m][0] = u[m][1] = gg[m][0] = gg[m][1] = 0.f;
+      sn[m][0] = sn[m][1] = u[m][0] = u[m][1] = gg[m][0] = gg[m][1] = 0.f;
       if (m < P.M) {
         float a0, a1;
         structured_block(xv.x, xv.y, P.sign_bits[m], lane, a0, a1);
         const int f = 64 * m + 2 * lane;
         const float2 ph = *reinterpret_cast<const float2*>(P.phase + f);
-        z[m][0] = fmaf(a0, P.tau_inv, ph.x);
-        z[m][1] = fmaf(a1, P.tau_inv, ph.y);
-        u[m][0] = P.amp * cosf(z[m][0]);
-        u[m][1] = P.amp * cosf(z[m][1]);
+        float c0, c1;  // one range reduction for the sine and the cosine of each argument
+        sincosf(fmaf(a0, P.tau_inv, ph.x), &sn[m][0], &c0);
+        sincosf(fmaf(a1, P.tau_inv, ph.y), &sn[m][1], &c1);
+        u[m][0] = P.amp * c0;
+        u[m][1] = P.amp * c1;
         const float2 gv = *reinterpret_cast<const float2*>(g + f);
         gg[m][0] = gv.x;
         gg[m][1] = gv.y;
@@ -1613,8 +1614,8 @@ __global__ void __launch_bounds__(kThreads) lift_backward_kernel(BackwardProblem
 #pragma unroll
     for (int m = 0; m < kMaxBlocks; ++m) {
       if (m < P.M) {
-        const float dz0 = -(gg[m][0] * c1 - u[m][0] * c2) * P.amp * sinf(z[m][0]);
-        const float dz1 = -(gg[m][1] * c1 - u[m][1] * c2) * P.amp * sinf(z[m][1]);
+        const float dz0 = -(gg[m][0] * c1 - u[m][0] * c2) * P.amp * sn[m][0];
+        const float dz1 = -(gg[m][1] * c1 - u[m][1] * c2) * P.amp * sn[m][1];
         float a0, a1;
         structured_block_t(dz0, dz1, P.sign_bits[m], lane, a0, a1);
         dx0 += a0;
